@@ -1,0 +1,252 @@
+/*
+ * glm5x_moe.h -- C ABI of the B200 routed-expert MoE sublayer.
+ *
+ * Drop-in for the expert-sublayer boundary of rsb1813/project-glm5x. Every
+ * entry point names the reference interface it replaces (paths inside the
+ * reference project). Plain pointers and sizes only; `stream` arguments are
+ * cudaStream_t handles passed as void* (NULL = the engine's own stream).
+ *
+ * Conventions (runtime/include/k3x/backend.hpp:170-298):
+ *  - Every function returns a glm5x_status; codes 0..19 keep the values of
+ *    k3x::ErrorCode (runtime/include/k3x/status.hpp:9-30). The message of the
+ *    last failure is available from glm5x_moe_error_message() (per engine) or
+ *    glm5x_last_error_message() (per thread, for calls without an engine).
+ *  - Bad inputs are rejected before any device work.
+ *  - One engine = one device, one stream; not thread-safe, like CudaBackend.
+ *  - Weights are NVFP4 ([out, in] packed two E2M1 per byte, low nibble first,
+ *    E4M3 block-16 scales in the 128x4 blocked layout, one FP32 global
+ *    scale) exactly as the reference's packer and .pn4 sidecars store them
+ *    (reference/glm5x_ref/nvfp4.py:58-198, packed_cache.py:277-309), or
+ *    MXFP4 (E8M0 group-32 scales, row-major, mxfp4.py:31-107).
+ */
+#ifndef GLM5X_MOE_H_
+#define GLM5X_MOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* k3x::ErrorCode values (status.hpp:9-30) plus engine-specific codes. */
+typedef enum glm5x_status {
+  GLM5X_OK = 0,
+  GLM5X_IO_ERROR = 1,
+  GLM5X_BAD_MAGIC = 2,
+  GLM5X_UNSUPPORTED_VERSION = 3,
+  GLM5X_TRUNCATED_FILE = 7,
+  GLM5X_INVALID_EXTENT = 9,
+  GLM5X_DATA_CRC_MISMATCH = 10,
+  GLM5X_AUXILIARY_CRC_MISMATCH = 11,
+  GLM5X_TENSOR_NOT_FOUND = 14,
+  GLM5X_INVALID_MXFP4 = 15,
+  GLM5X_INVALID_STATE = 16,
+  GLM5X_BACKEND_UNAVAILABLE = 17,
+  GLM5X_UNSUPPORTED_ARCHITECTURE = 19,
+  GLM5X_DEVICE_ERROR = 100,    /* CUDA error or a device-side error word */
+  GLM5X_OUT_OF_MEMORY = 101,
+  GLM5X_WAIT_TIMEOUT = 102     /* a bounded device wait gave up */
+} glm5x_status;
+
+typedef enum glm5x_precision {
+  GLM5X_PRECISION_NVFP4 = 0,   /* E2M1 + E4M3/16 + FP32 global */
+  GLM5X_PRECISION_MXFP4 = 1    /* E2M1 + E8M0/32 */
+} glm5x_precision;
+
+typedef enum glm5x_scale_mode {
+  GLM5X_SCALE_MAX_ABS = 0,     /* nvfp4.py:164-170, mxfp4.py:70-79 */
+  GLM5X_SCALE_MSE = 1          /* nvfp4.py:139-163, mxfp4.py:80-97 */
+} glm5x_scale_mode;
+
+/* Layer shape and policy. Replaces the constructor arguments of
+ * GLM5XLayer10MoEReference (reference/glm5x_ref/layer10_moe.py:352-374) and
+ * the fixed constants of build_learned_routes
+ * (runtime/src/cuda_glm5x_real_expert_bench.cpp:291-293). */
+typedef struct glm5x_moe_config {
+  int32_t hidden;            /* 6144 */
+  int32_t intermediate;      /* 2048 */
+  int32_t num_experts;       /* 256 routed experts (global count) */
+  int32_t top_k;             /* 8 */
+  int32_t has_shared;        /* 1: one always-on shared expert */
+  float routed_scaling;      /* 2.5 */
+  int32_t precision;         /* glm5x_precision */
+  int32_t max_tokens;        /* largest T per forward on this engine */
+  int32_t expert_begin;      /* first expert held here (expert parallel) */
+  int32_t expert_count;      /* experts held here; num_experts on one GPU */
+} glm5x_moe_config;
+
+/* One NVFP4 matrix [rows, cols] (GLM5XNVFP4Weight, nvfp4.py:58-98). */
+typedef struct glm5x_nvfp4_matrix {
+  const uint8_t* packed;     /* rows * cols / 2 bytes */
+  const uint8_t* scales;     /* blocked E4M3, ceil(rows/128)*ceil(cols/64)*512 bytes */
+  float global_scale;
+  int64_t rows;
+  int64_t cols;
+} glm5x_nvfp4_matrix;
+
+/* One MXFP4 matrix (Mxfp4WeightView, runtime/include/k3x/backend.hpp:114-121). */
+typedef struct glm5x_mxfp4_matrix {
+  const uint8_t* packed;     /* rows * cols / 2 bytes */
+  const uint8_t* scales;     /* row-major E8M0, rows * cols / group bytes */
+  int64_t rows;
+  int64_t cols;
+  int64_t group_size;        /* 32 */
+} glm5x_mxfp4_matrix;
+
+typedef struct glm5x_moe_stats {
+  /* subset of k3x::BackendRuntimeStats (backend.hpp:55-105) */
+  uint64_t forward_calls;
+  uint64_t kernel_launches;
+  uint64_t resident_weight_bytes;
+  uint64_t activation_h2d_bytes;
+  uint64_t device_to_host_bytes;
+  uint64_t stream_synchronization_count;
+  uint64_t workspace_bytes;
+  uint64_t loaded_experts;
+} glm5x_moe_stats;
+
+typedef struct glm5x_moe glm5x_moe;
+
+/* ---------------------------------------------------------------- engine */
+
+/* make_cuda_backend (backend.hpp:296-298; backend_cuda.cu:5091-5168).
+ * Fails with GLM5X_UNSUPPORTED_ARCHITECTURE on anything but sm_100. */
+glm5x_status glm5x_moe_create(const glm5x_moe_config* config, int device, glm5x_moe** out);
+void glm5x_moe_destroy(glm5x_moe* moe);
+const char* glm5x_moe_error_message(const glm5x_moe* moe);
+const char* glm5x_last_error_message(void);
+
+/* Router weight [num_experts, hidden] BF16 and correction bias [num_experts]
+ * FP32, host memory (GLM5XLayer10MoEReference router_weight /
+ * correction_bias, layer10_moe.py:375-380, 411-413). */
+glm5x_status glm5x_moe_set_router(glm5x_moe* moe, const uint16_t* weight_bf16,
+                                  const float* bias);
+
+/* Admit one expert's gate/up [I, H] and down [H, I] NVFP4 matrices.
+ * expert = global expert id, or -1 for the shared expert. Host pointers
+ * (load_glm5x_bf16_expert, runtime/include/k3x/glm5x_bundle.hpp:21-26;
+ * GLM5XPackedExpertCache.get, packed_cache.py:506-617). */
+glm5x_status glm5x_moe_load_expert_nvfp4(glm5x_moe* moe, int32_t expert,
+                                         const glm5x_nvfp4_matrix* gate,
+                                         const glm5x_nvfp4_matrix* up,
+                                         const glm5x_nvfp4_matrix* down);
+/* Same, with the matrices already in device memory (no host staging). */
+glm5x_status glm5x_moe_load_expert_nvfp4_device(glm5x_moe* moe, int32_t expert,
+                                                const glm5x_nvfp4_matrix* gate,
+                                                const glm5x_nvfp4_matrix* up,
+                                                const glm5x_nvfp4_matrix* down);
+/* MXFP4 expert (Mxfp4MlpView, backend.hpp:154-158), host pointers. */
+glm5x_status glm5x_moe_load_expert_mxfp4(glm5x_moe* moe, int32_t expert,
+                                         const glm5x_mxfp4_matrix* gate,
+                                         const glm5x_mxfp4_matrix* up,
+                                         const glm5x_mxfp4_matrix* down);
+/* Parse and admit a .pn4 / .pm4 packed sidecar
+ * (GLM5XPackedExpertCache._decode_role, packed_cache.py:407-504): header
+ * "<8sII" ("GLM5XPI4", 1, json_len), sorted compact JSON, payload; CRC32C of
+ * every section is verified. */
+glm5x_status glm5x_moe_load_sidecar(glm5x_moe* moe, int32_t expert, const char* path);
+
+/* Full sublayer on device buffers: hidden [T, hidden] BF16 -> out [T, hidden]
+ * FP32 = sum over top-k of weight * expert(x) + shared(x). Asynchronous on
+ * `stream`. (GLM5XLayer10MoEReference.__call__, layer10_moe.py:942-968;
+ * CudaBackend::raw_bf16_situ_mlp_expert_major_with_shared,
+ * backend_cuda.cu:1545-1867.) */
+glm5x_status glm5x_moe_forward(glm5x_moe* moe, const void* hidden_bf16, int64_t tokens,
+                               float* out, void* stream);
+/* Same with host buffers (H2D, forward, D2H, synchronize): the reference's
+ * ComputeBackend convention of host spans in and host vectors out. */
+glm5x_status glm5x_moe_forward_host(glm5x_moe* moe, const uint16_t* hidden_bf16,
+                                    int64_t tokens, float* out);
+/* Expert path only, with caller-supplied routing (device buffers): ids
+ * [T, top_k] int32 global expert ids, weights [T, top_k] FP32 (the
+ * contribution of each slot, already scaled). Replaces
+ * mxfp4_situ_mlp_grid / raw_bf16_situ_mlp_expert_major
+ * (backend.hpp:220-252) for callers that route themselves. */
+glm5x_status glm5x_moe_forward_routed(glm5x_moe* moe, const void* hidden_bf16, int64_t tokens,
+                                      const int32_t* ids, const float* weights, float* out,
+                                      void* stream);
+/* Routing of the last forward (synchronizes): ids/weights [T, top_k] in
+ * descending choice order, logits [T, num_experts] (may be NULL). */
+glm5x_status glm5x_moe_last_routing(glm5x_moe* moe, int32_t* ids, float* weights,
+                                    float* logits, int64_t tokens);
+/* Synchronizes and turns the device error word into a status. */
+glm5x_status glm5x_moe_check(glm5x_moe* moe);
+glm5x_status glm5x_moe_get_stats(const glm5x_moe* moe, glm5x_moe_stats* out);
+/* Device pointer and size of an internal buffer of the last forward, for
+ * parity tests: 0 act packed, 1 act scales (blocked), 2 act global [nseg],
+ * 3 h BF16 [rows, I], 4 h packed, 5 h scales, 6 h global, 7 y BF16 [rows, H],
+ * 8 segment starts [nseg+1] int32, 9 segment counts [nseg], 10 row_token,
+ * 11 pos [T, k+1], 12 row_weight. */
+glm5x_status glm5x_moe_debug_buffer(glm5x_moe* moe, int32_t which, void** ptr, size_t* bytes);
+/* Phase timing with CUDA events on the forward's stream (the per-projection
+ * device times the reference records, backend_cuda.cu:2034-2040, 2151-2168).
+ * Phases: 0 row amax, 1 router logits, 2 top-k, 3 permutation, 4 activation
+ * quantize, 5 gate/up GEMM, 6 h quantize, 7 down GEMM, 8 combine. */
+#define GLM5X_NUM_PHASES 9
+glm5x_status glm5x_moe_set_profiling(glm5x_moe* moe, int32_t enable);
+/* Synchronizes; writes the milliseconds accumulated per phase since the last
+ * call (ms[GLM5X_NUM_PHASES]) and the number of profiled forwards, then resets. */
+glm5x_status glm5x_moe_phase_times(glm5x_moe* moe, float* ms, int32_t* forwards);
+/* The engine's own stream (used by glm5x_moe_forward_host and by forwards
+ * given a NULL stream), as a cudaStream_t. */
+glm5x_status glm5x_moe_get_stream(glm5x_moe* moe, void** stream);
+/* Synchronizes, then copies the first `bytes` of debug buffer `which` to the
+ * device pointer `dst`. */
+glm5x_status glm5x_moe_debug_copy(glm5x_moe* moe, int32_t which, void* dst, size_t bytes);
+
+/* ---------------------------------------------------------------- kernels */
+/* Stand-alone device kernels. All pointers are device pointers. */
+
+/* Converter NVFP4 packing of one matrix (quantize_nvfp4_weight,
+ * nvfp4.py:180-198; scale_mode GLM5X_SCALE_MSE is the reference default).
+ * src FP32 or BF16 [rows, cols]; packed [rows, cols/2]; scales blocked;
+ * global_out one float (device). */
+glm5x_status glm5x_nvfp4_quantize_f32(const float* src, int64_t rows, int64_t cols,
+                                      int32_t scale_mode, uint8_t* packed, uint8_t* scales,
+                                      float* global_out, void* stream);
+glm5x_status glm5x_nvfp4_quantize_bf16(const uint16_t* src, int64_t rows, int64_t cols,
+                                       int32_t scale_mode, uint8_t* packed, uint8_t* scales,
+                                       float* global_out, void* stream);
+/* Activation quantization of expert-major slabs (layer10_moe.py:729 ->
+ * nvfp4.py:236-252): rows seg_start[s] .. + seg_count[s] of the output take
+ * src rows row_token[row]; each segment gets its own global scale
+ * (seg_global[s]). Scales are written in the blocked layout of the output
+ * row space. nseg <= 1024; cols a multiple of 512. */
+glm5x_status glm5x_nvfp4_quantize_slabs_bf16(const uint16_t* src, int64_t cols,
+                                             const int32_t* row_token, const int32_t* seg_start,
+                                             const int32_t* seg_count, int32_t nseg,
+                                             int64_t out_rows, uint8_t* packed,
+                                             uint8_t* scales, float* seg_global, void* stream);
+/* dequantize_nvfp4 (nvfp4.py:201-217). */
+glm5x_status glm5x_nvfp4_dequantize(const uint8_t* packed, const uint8_t* scales,
+                                    float global_scale, int64_t rows, int64_t cols, float* out,
+                                    void* stream);
+/* encode_mxfp4 (k3x_ref/mxfp4.py:31-107); synchronizes to report
+ * GLM5X_INVALID_MXFP4 for exponents above 126. */
+glm5x_status glm5x_mxfp4_encode_f32(const float* src, int64_t rows, int64_t cols,
+                                    int64_t group_size, int32_t scale_mode, uint8_t* packed,
+                                    uint8_t* scales, void* stream);
+/* decode_mxfp4 (mxfp4.py:110-144; runtime/src/ops.cpp:40-63); synchronizes
+ * to report GLM5X_INVALID_MXFP4 for the reserved scale 0xFF. */
+glm5x_status glm5x_mxfp4_decode(const uint8_t* packed, const uint8_t* scales, int64_t rows,
+                                int64_t cols, int64_t group_size, float* out, void* stream);
+/* select_routing natural mode over given sigmoid scores (routing_policy.cpp:
+ * 31-159) for T tokens at once: scores/bias -> ids [T,k], weights [T,k]
+ * multiplied by routed_scale (1.0 reproduces select_routing itself). */
+glm5x_status glm5x_select_routing(const float* scores, const float* bias, int64_t tokens,
+                                  int32_t num_experts, int32_t top_k, float routed_scale,
+                                  int32_t* ids, float* weights, void* stream);
+/* The device expert-major permutation (build_expert_major_plan,
+ * runtime/src/expert_major.cpp:12-98): ids [T,k] -> seg_count [E],
+ * seg_start [E+1] (128-aligned), pos [T,k], row_token [rows]. */
+glm5x_status glm5x_expert_major_plan(const int32_t* ids, int64_t tokens, int32_t top_k,
+                                     int32_t num_experts, int32_t* seg_count,
+                                     int32_t* seg_start, int32_t* pos, int32_t* row_token,
+                                     void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GLM5X_MOE_H_ */

@@ -1,0 +1,99 @@
+// ref_shim.cpp -- TEST INFRASTRUCTURE ONLY.
+//
+// A C-ABI shim over the reference's own C++ CPU implementation of the MoE
+// expert path. oracle/Makefile compiles this file together with the
+// reference's sources where they lie (runtime/src/{routing_policy,
+// expert_major,ops,backend_cpu,profile}.cpp) into oracle/_ref/libk3x_ref.so.
+// Used by tests (to pin the C restatement in glm5x_oracle.c) and by bench.py's
+// `--impl reference` / cpu_baseline legs (the reference's CPU expert path).
+#include "k3x/backend.hpp"
+#include "k3x/expert_major.hpp"
+#include "k3x/ops.hpp"
+#include "k3x/routing_policy.hpp"
+
+#include <cstddef>
+#include <cstdint>
+#include <cstring>
+#include <memory>
+#include <span>
+#include <vector>
+
+namespace {
+std::unique_ptr<k3x::ComputeBackend>& cpu() {
+  static thread_local std::unique_ptr<k3x::ComputeBackend> backend = k3x::make_cpu_backend();
+  return backend;
+}
+}  // namespace
+
+extern "C" {
+
+// k3x::select_routing natural mode (runtime/src/routing_policy.cpp:31-159).
+int ref_select_routing(const float* scores, const float* bias, int n, int k, int32_t* ids,
+                       float* weights) {
+  auto r = k3x::select_routing(std::span<const float>(scores, n), std::span<const float>(bias, n),
+                               static_cast<std::size_t>(k),
+                               k3x::RoutingPolicyConfig{.mode = k3x::RoutingMode::natural});
+  if (!r) return -1;
+  for (int s = 0; s < k; ++s) {
+    ids[s] = static_cast<int32_t>(r.value().expert_ids[s]);
+    weights[s] = r.value().normalized_weights[s];
+  }
+  return 0;
+}
+
+// k3x::decode_mxfp4 (runtime/src/ops.cpp:40-63).
+int ref_decode_mxfp4(const uint8_t* packed, const uint8_t* scales, int64_t rows, int64_t cols,
+                     int64_t group, float* out) {
+  auto r = k3x::decode_mxfp4(
+      std::span<const std::byte>(reinterpret_cast<const std::byte*>(packed), rows * cols / 2),
+      std::span<const std::byte>(reinterpret_cast<const std::byte*>(scales), rows * cols / group),
+      rows, cols, group);
+  if (!r) return -1;
+  std::memcpy(out, r.value().data(), sizeof(float) * r.value().size());
+  return 0;
+}
+
+// CpuBackend::dense_situ_mlp(..., MlpActivation::silu) (runtime/src/backend_cpu.cpp:107-128).
+int ref_dense_silu_mlp(const float* x, const float* gate, const float* up, const float* down,
+                       int64_t H, int64_t I, float* out) {
+  k3x::DenseMlpView view{
+      {1, std::span<const float>(gate, H * I), static_cast<std::size_t>(I), static_cast<std::size_t>(H)},
+      {2, std::span<const float>(up, H * I), static_cast<std::size_t>(I), static_cast<std::size_t>(H)},
+      {3, std::span<const float>(down, H * I), static_cast<std::size_t>(H), static_cast<std::size_t>(I)}};
+  auto r = cpu()->dense_situ_mlp(std::span<const float>(x, H), view, 1.0F, std::nullopt, 0,
+                                 k3x::ProfilePhase::decode, k3x::MlpActivation::silu);
+  if (!r) return -1;
+  std::memcpy(out, r.value().data(), sizeof(float) * H);
+  return 0;
+}
+
+// k3x::build_expert_major_plan (runtime/src/expert_major.cpp:12-56). Writes
+// groups in first-use order: group_expert[g], group_size[g]; and per
+// assignment (group-major) token, slot and contribution. Returns the number
+// of groups, or -1.
+int ref_expert_major_plan(const int32_t* ids, const float* contributions, int T, int k,
+                          int32_t* group_expert, int32_t* group_size, int32_t* a_token,
+                          int32_t* a_slot, float* a_contrib) {
+  std::vector<k3x::ExpertMajorTokenRoute> routes(T);
+  for (int t = 0; t < T; ++t)
+    for (int s = 0; s < k; ++s) {
+      routes[t].expert_ids.push_back(static_cast<uint32_t>(ids[t * k + s]));
+      routes[t].contributions.push_back(contributions[t * k + s]);
+    }
+  auto r = k3x::build_expert_major_plan(routes);
+  if (!r) return -1;
+  int a = 0;
+  const auto& groups = r.value().groups;
+  for (std::size_t g = 0; g < groups.size(); ++g) {
+    group_expert[g] = static_cast<int32_t>(groups[g].expert_id);
+    group_size[g] = static_cast<int32_t>(groups[g].assignments.size());
+    for (const auto& as : groups[g].assignments) {
+      a_token[a] = static_cast<int32_t>(as.token_index);
+      a_slot[a] = static_cast<int32_t>(as.router_slot);
+      a_contrib[a] = as.contribution;
+      ++a;
+    }
+  }
+  return static_cast<int>(groups.size());
+}
+}

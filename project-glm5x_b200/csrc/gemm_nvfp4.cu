@@ -1,0 +1,358 @@
+// gemm_nvfp4.cu -- persistent grouped NVFP4 GEMM on tcgen05 block-scaled MMA.
+//
+// Replaces the reference's expert projections: the cuBLASLt NVFP4
+// torch._scaled_mm calls (reference/glm5x_ref/nvfp4.py:220-233, 294-335;
+// grouped form reference/glm5x_ref/nvfp4_batched.py:64-151) and the SIMT
+// MXFP4 grid (runtime/cuda/mxfp4.cu:67-104), with SwiGLU
+// (runtime/cuda/situ.cu:51-75, layer10_moe.py:730) fused into the gate/up
+// epilogue and the routing weight (layer10_moe.py:843-846) fused into the
+// down epilogue.
+//
+// Structure (one CTA per SM, 192 threads):
+//   warp 0      TMA producer: weight tile (128 rows x 256 K) and activation
+//               tile (BN rows x 256 K), both 128B-swizzled, plus the four
+//               512-byte scale chunks of each operand by bulk copy.
+//   warp 1      TMEM owner and MMA issuer: tcgen05.cp moves the scale chunks
+//               into TMEM, then four kind::mxf4nvf4 block16 MMAs (K = 64
+//               each) per stage accumulate into TMEM.
+//   warps 2-5   epilogue: tcgen05.ld of the 128 x n accumulator, scale by the
+//               two global scales, fused activation, BF16 stores.
+// Weights are the M side (swap-AB): M = 128 weight rows per tile, N = the
+// expert's tokens (<= BN), so the decode regime (a few tokens per expert)
+// still uses full 128-row MMAs. Tiles are enumerated expert-major, then
+// weight tile, then token tile, so CTAs sharing a weight or token tile run at
+// the same time and hit L2.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cstdint>
+
+#include "glm5x_kernels.cuh"
+#include "glm5x_ptx.cuh"
+
+namespace glm5x {
+
+namespace {
+
+constexpr int kBM = 128;          // weight rows per tile
+constexpr int kBKBytes = 128;     // K bytes per stage (256 FP4 values)
+constexpr int kChunkBytes = 512;  // one 128-row x 4-scale chunk
+constexpr int kThreads = 192;
+constexpr int kMaxSeg = 260;      // segments (local experts + shared) per launch
+
+template <int BN>
+struct Cfg {
+  static constexpr int kSfbCh = BN > 128 ? 2 : 1;  // 128-row scale blocks per tile
+  static constexpr int kAcc = BN > 128 ? 1 : 2;    // TMEM accumulator buffers
+  static constexpr int kStages = BN > 128 ? 4 : (BN > 64 ? 5 : (BN > 32 ? 6 : 8));
+  static constexpr int kABytes = kBM * kBKBytes;
+  static constexpr int kBBytes = BN * kBKBytes;
+  static constexpr int kSfaBytes = 4 * kChunkBytes;
+  static constexpr int kSfbBytes = kSfbCh * 4 * kChunkBytes;
+  static constexpr int kStageBytes =
+      ((kABytes + kBBytes + kSfaBytes + kSfbBytes + 1023) / 1024) * 1024;
+  static constexpr int kSfaCols = 16;               // 4 MMAs x 4 columns
+  static constexpr int kSfbCols = 16 * kSfbCh;      // 4 MMAs x 4 * kSfbCh
+  static constexpr int kSfBase = kAcc * BN;
+  static constexpr int kStageSfCols = kSfaCols + kSfbCols;
+  static constexpr int kTmemCols = 512;
+  static_assert(kSfBase + kStages * kStageSfCols <= kTmemCols, "TMEM budget");
+  static constexpr size_t kSmem = (size_t)kStages * kStageBytes + 1024 + 256;
+  static_assert(kSmem + 3 * 4 * (kMaxSeg + 1) <= 232448, "shared memory budget");
+};
+
+struct TileInfo {
+  int seg, m_tile, row_start, n_valid;
+};
+
+__device__ __forceinline__ bool decode_tile(int tile, int m_tiles, int nseg, int bn,
+                                            const int32_t* __restrict__ ntp,
+                                            const int32_t* __restrict__ cnt,
+                                            const int32_t* __restrict__ start, TileInfo& ti) {
+  const int key = tile / m_tiles;
+  int lo = 0, hi = nseg;  // largest s with ntp[s] <= key
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (ntp[mid] <= key) lo = mid; else hi = mid;
+  }
+  const int s = lo;
+  const int nt = ntp[s + 1] - ntp[s];
+  if (nt <= 0) return false;
+  const int local = tile - m_tiles * ntp[s];
+  const int m = local / nt, n = local % nt;
+  ti.seg = s;
+  ti.m_tile = m;
+  ti.row_start = start[s] + n * bn;
+  const int left = cnt[s] - n * bn;
+  ti.n_valid = left < bn ? left : bn;
+  return true;
+}
+
+__device__ __forceinline__ uint16_t f2bf(float x) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(x));
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    nvfp4_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                              const __grid_constant__ CUtensorMap tmap_b, const GemmParams p) {
+  using C = Cfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
+  uint64_t* empty = full + C::kStages;
+  uint64_t* tfull = empty + C::kStages;
+  uint64_t* tempty = tfull + C::kAcc;
+  uint64_t* drained = tempty + C::kAcc;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drained + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int m_tiles = p.M_per / kBM;
+  const int ks_count = p.K / 256;
+  const int kc_per_rb = p.K / 64;  // scale chunks per 128-row block
+  __shared__ int32_t s_ntp[kMaxSeg + 1], s_cnt[kMaxSeg], s_start[kMaxSeg + 1];
+
+  for (int i = threadIdx.x; i <= p.nseg; i += blockDim.x) {
+    s_ntp[i] = p.ntile_prefix[i];
+    s_start[i] = p.seg_start[i];
+    if (i < p.nseg) s_cnt[i] = p.seg_count[i];
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < C::kAcc; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 128);
+    }
+    mbar_init(drained, 1);
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, C::kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  const int total_tiles = m_tiles * s_ntp[p.nseg];
+
+  if (warp == 0) {
+    // ------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+        TileInfo ti;
+        if (!decode_tile(tile, m_tiles, p.nseg, BN, s_ntp, s_cnt, s_start, ti)) continue;
+        const int a_row = ti.seg * p.M_per + ti.m_tile * kBM;
+        const int sfb_ch = ti.n_valid > 128 ? 2 : 1;
+        const uint8_t* sfa = p.sfa + (size_t)(a_row / 128) * kc_per_rb * kChunkBytes;
+        const uint8_t* sfb = p.sfb + (size_t)(ti.row_start / 128) * kc_per_rb * kChunkBytes;
+        const uint32_t bytes = C::kABytes + C::kBBytes + C::kSfaBytes + sfb_ch * 4 * kChunkBytes;
+        for (int ks = 0; ks < ks_count; ++ks) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, p.err)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + stage * C::kStageBytes;
+          uint8_t* sb = sa + C::kABytes;
+          uint8_t* ssfa = sb + C::kBBytes;
+          uint8_t* ssfb = ssfa + C::kSfaBytes;
+          mbar_arrive_expect_tx(&full[stage], bytes);
+          tma_load_2d(sa, &tmap_a, &full[stage], ks * kBKBytes, a_row);
+          tma_load_2d(sb, &tmap_b, &full[stage], ks * kBKBytes, ti.row_start);
+          bulk_load(ssfa, sfa + (size_t)ks * 4 * kChunkBytes, C::kSfaBytes, &full[stage]);
+          for (int h = 0; h < sfb_ch; ++h)
+            bulk_load(ssfb + h * 4 * kChunkBytes,
+                      sfb + ((size_t)h * kc_per_rb + ks * 4) * kChunkBytes, 4 * kChunkBytes,
+                      &full[stage]);
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+        TileInfo ti;
+        if (!decode_tile(tile, m_tiles, p.nseg, BN, s_ntp, s_cnt, s_start, ti)) continue;
+        const uint32_t n_mma = (uint32_t)((ti.n_valid + 7) / 8 * 8);
+        const int sfb_ch = ti.n_valid > 128 ? 2 : 1;
+        const uint32_t idesc = idesc_fp4(kBM, n_mma, 0, 0, 0);
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, p.err)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int ks = 0; ks < ks_count; ++ks) {
+          if (!mbar_wait(&full[stage], phase, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint8_t* sa = smem + stage * C::kStageBytes;
+          const uint8_t* sb = sa + C::kABytes;
+          const uint8_t* ssfa = sb + C::kBBytes;
+          const uint8_t* ssfb = ssfa + C::kSfaBytes;
+          const uint32_t sfa_col = tmem_base + C::kSfBase + stage * C::kStageSfCols;
+          const uint32_t sfb_col = sfa_col + C::kSfaCols;
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            tmem_cp_sf(sfa_col + 4 * c, desc_sf_chunk(smem_u32(ssfa + c * kChunkBytes)));
+          for (int h = 0; h < sfb_ch; ++h)
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+              tmem_cp_sf(sfb_col + 4 * C::kSfbCh * c + 4 * h,
+                         desc_sf_chunk(smem_u32(ssfb + h * 4 * kChunkBytes + c * kChunkBytes)));
+          const uint32_t a_addr = smem_u32(sa), b_addr = smem_u32(sb);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            mma_nvfp4(d_tmem, desc_kmajor_sw128(a_addr + 32 * c),
+                      desc_kmajor_sw128(b_addr + 32 * c), idesc, sfa_col + 4 * c,
+                      sfb_col + 4 * C::kSfbCh * c, (ks | c) != 0 ? 1u : 0u);
+          }
+          tc_commit(&empty[stage]);
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit(&tfull[acc]);
+        if (++acc == C::kAcc) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      // every MMA this thread issued has completed once `drained` flips
+      tc_commit(drained);
+      mbar_wait(drained, 0, p.err);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
+      TileInfo ti;
+      if (!decode_tile(tile, m_tiles, p.nseg, BN, s_ntp, s_cnt, s_start, ti)) continue;
+      if (!mbar_wait(&tfull[acc], acc_phase, p.err)) break;
+      tc_fence_after();
+      const uint32_t t_row = tmem_base + ((uint32_t)(32 * q) << 16) + acc * BN;
+      float bscale = p.b_global[ti.seg];
+      if (EPI == 0) {
+        const float wg = p.a_global[2 * ti.seg + (lane >= 16 ? 1 : 0)];
+        const float scale = bscale * wg;
+        const int j = ti.m_tile * (kBM / 2) + 16 * q + (lane & 15);
+        const int hcols = p.M_per / 2;
+        float amax = 0.0f;
+        for (int c0 = 0; c0 < ti.n_valid; c0 += 32) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(t_row + c0, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float mine = __uint_as_float(v[i]) * scale;
+            const float up = __shfl_down_sync(0xffffffffu, mine, 16);
+            if (lane < 16 && c0 + i < ti.n_valid) {
+              const float gate = mine;
+              const float h = gate / (1.0f + expf(-gate)) * up;
+              const uint16_t hb = f2bf(h);
+              amax = fmaxf(amax, fabsf(__uint_as_float((uint32_t)hb << 16)));
+              p.out[(size_t)(ti.row_start + c0 + i) * hcols + j] = hb;
+            }
+          }
+        }
+        for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        if (lane == 0 && ti.n_valid > 0)
+          atomicMax(reinterpret_cast<unsigned int*>(p.h_amax + ti.seg), __float_as_uint(amax));
+      } else {
+        const float scale = bscale * p.a_global[ti.seg];
+        const int o = ti.m_tile * kBM + 32 * q + lane;
+        for (int c0 = 0; c0 < ti.n_valid; c0 += 32) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(t_row + c0, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            if (c0 + i < ti.n_valid) {
+              const int row = ti.row_start + c0 + i;
+              const float y = __uint_as_float(v[i]) * scale * p.row_weight[row];
+              p.out[(size_t)row * p.M_per + o] = f2bf(y);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+      if (++acc == C::kAcc) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, C::kTmemCols);
+}
+
+template <int BN, int EPI>
+cudaError_t launch_impl(const CUtensorMap* ta, const CUtensorMap* tb, const GemmParams& p,
+                        int num_sms, cudaStream_t st) {
+  auto kern = nvfp4_grouped_gemm_kernel<BN, EPI>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)Cfg<BN>::kSmem);
+  if (e != cudaSuccess) return e;
+  kern<<<num_sms, kThreads, Cfg<BN>::kSmem, st>>>(*ta, *tb, p);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+size_t nvfp4_gemm_smem_bytes(int bn) {
+  switch (bn) {
+    case 32: return Cfg<32>::kSmem;
+    case 64: return Cfg<64>::kSmem;
+    case 128: return Cfg<128>::kSmem;
+    case 256: return Cfg<256>::kSmem;
+  }
+  return 0;
+}
+
+cudaError_t launch_nvfp4_grouped_gemm(int bn, int epi, const CUtensorMap* tmap_a,
+                                      const CUtensorMap* tmap_b, const GemmParams& p,
+                                      int num_sms, cudaStream_t st) {
+  if (p.nseg > kMaxSeg || p.K % 256 || p.M_per % kBM) return cudaErrorInvalidValue;
+#define G5_CASE(BN_)                                                              \
+  case BN_:                                                                       \
+    return epi == 0 ? launch_impl<BN_, 0>(tmap_a, tmap_b, p, num_sms, st)         \
+                    : launch_impl<BN_, 1>(tmap_a, tmap_b, p, num_sms, st);
+  switch (bn) {
+    G5_CASE(32)
+    G5_CASE(64)
+    G5_CASE(128)
+    G5_CASE(256)
+  }
+#undef G5_CASE
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace glm5x

@@ -1,0 +1,102 @@
+// glm5x_kernels.cuh -- launcher declarations shared by the kernels and the
+// host engine.
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace glm5x {
+
+// ------------------------------------------------------------ quant.cu
+cudaError_t launch_row_amax_bf16(const uint16_t* src, int64_t rows, int cols, float* out,
+                                 uint32_t* err, cudaStream_t st);
+template <typename T>
+cudaError_t launch_nvfp4_quantize_matrix(const T* src, int64_t rows, int64_t cols, int mse,
+                                         float* amax_scratch, uint8_t* packed,
+                                         uint8_t* scales_blocked, float* global_out,
+                                         uint32_t* err, cudaStream_t st);
+cudaError_t launch_nvfp4_quantize_segments(const uint16_t* src, int K, const int32_t* row_token,
+                                           const int32_t* seg_start, const int32_t* seg_count,
+                                           const int32_t* qprefix, int nseg,
+                                           const float* seg_amax, int64_t max_rows,
+                                           uint8_t* packed, uint8_t* scales_blocked,
+                                           float* seg_global, cudaStream_t st);
+cudaError_t launch_nvfp4_dequantize(const uint8_t* packed, const uint8_t* scales_blocked,
+                                    float g, int64_t rows, int64_t cols, float* out,
+                                    cudaStream_t st);
+cudaError_t launch_mxfp4_decode(const uint8_t* packed, const uint8_t* scales, int64_t n,
+                                int group, float* out, uint32_t* err, cudaStream_t st);
+template <typename T>
+cudaError_t launch_mxfp4_encode(const T* src, int64_t n, int group, int mse, uint8_t* packed,
+                                uint8_t* scales, uint32_t* err, cudaStream_t st);
+
+// ------------------------------------------------------------ route.cu
+struct PermuteBuffers {
+  int32_t* chunk_count;   // [ceil(T/256), E]
+  int32_t* rank;          // [T, k]
+  int32_t* seg_count;     // [nseg]
+  int32_t* seg_start;     // [nseg + 1], 128-aligned starts
+  int32_t* qprefix;       // [nseg + 1], prefix of counts rounded up to 8
+  int32_t* ntile_prefix;  // [nseg + 1], prefix of N-tile counts
+  float* seg_amax;        // [nseg], max |x| of each segment's input rows
+  float* h_amax;          // [nseg], max |h| of each segment's SwiGLU output
+  int32_t* pos;           // [T, k + has_shared], row of each (token, slot)
+  int32_t* row_token;     // [rows], token of each segment row
+  float* row_weight;      // [rows], routing weight of each segment row
+};
+
+cudaError_t launch_router_logits_simt(const uint16_t* x, const uint16_t* w, int T, int H, int E,
+                                      float* logits, cudaStream_t st);
+cudaError_t launch_topk(const float* in, int values_are_scores, const float* bias, int T, int E,
+                        int k, float routed_scale, int32_t* ids, float* weights, uint32_t* err,
+                        cudaStream_t st);
+cudaError_t launch_permute(const int32_t* ids, const float* weights, const float* token_amax,
+                           int T, int k, int E, int has_shared, int bn, PermuteBuffers b,
+                           uint32_t* err, cudaStream_t st);
+
+// ------------------------------------------------------------ gemm_nvfp4.cu
+// Grouped block-scaled FP4 GEMM over expert segments, weights as the M side:
+//   D[m, n] = sum_k W_e[m, k] * X[row_start + n, k]  (NVFP4: E4M3 per 16)
+// Epilogue 0 (gate/up): W rows interleave 16 gate and 16 up rows per 32, and
+//   h = silu(gate) * up is stored as BF16 into h_out[row, M_per / 2].
+// Epilogue 1 (down): y * row_weight[row] stored as BF16 into y_out[row, M_per].
+struct GemmParams {
+  const uint8_t* sfa;           // blocked scales of the stacked weights
+  const uint8_t* sfb;           // blocked scales of the activation rows
+  const int32_t* seg_count;     // [nseg]
+  const int32_t* seg_start;     // [nseg + 1]
+  const int32_t* ntile_prefix;  // [nseg + 1]
+  const float* a_global;        // epi 0: [2 * nseg] (gate, up); epi 1: [nseg]
+  const float* b_global;        // [nseg]
+  const float* row_weight;      // epi 1
+  uint16_t* out;                // epi 0: h [rows, M_per/2]; epi 1: y [rows, M_per]
+  float* h_amax;                // epi 0: [nseg]
+  uint32_t* err;
+  int K;                        // contraction length (elements)
+  int M_per;                    // weight rows per expert
+  int nseg;
+};
+
+cudaError_t launch_nvfp4_grouped_gemm(int bn, int epi, const CUtensorMap* tmap_a,
+                                      const CUtensorMap* tmap_b, const GemmParams& p,
+                                      int num_sms, cudaStream_t st);
+size_t nvfp4_gemm_smem_bytes(int bn);
+
+// ------------------------------------------------------------ combine.cu
+// out[t, :] = sum_{s < kk} y[pos[t, s], :] (FP32 accumulation of BF16 rows).
+cudaError_t launch_combine(const uint16_t* y, const int32_t* pos, int T, int kk, int H,
+                           float* out, cudaStream_t st);
+
+// ------------------------------------------------------------ weights.cu
+// Interleave gate [I, K] and up [I, K] (packed NVFP4 + blocked scales) into
+// the stacked gate/up weight slot: 16 gate rows then 16 up rows per 32.
+cudaError_t launch_interleave_gate_up(const uint8_t* gate_packed, const uint8_t* gate_sf,
+                                      const uint8_t* up_packed, const uint8_t* up_sf, int I,
+                                      int K, int group, uint8_t* dst_packed, uint8_t* dst_sf,
+                                      cudaStream_t st);
+// Row-major scale bytes [rows, K/group] -> blocked layout (zero padding).
+cudaError_t launch_scales_to_blocked(const uint8_t* rm, int64_t rows, int64_t sf_cols,
+                                     uint8_t* blocked, cudaStream_t st);
+
+}  // namespace glm5x

@@ -1,0 +1,930 @@
+// moe_engine.cu -- host engine behind the C ABI in include/glm5x_moe.h.
+//
+// Owns the resident expert weights (the role of ResidentWeightTable,
+// runtime/cuda/resident_weights.cuh:36-57, without eviction: every local
+// expert stays in HBM), the forward workspace, the TMA descriptors, and the
+// launch sequence of one MoE sublayer forward:
+//   row amax -> router logits -> top-k -> expert-major permutation ->
+//   activation NVFP4 slabs -> gate/up GEMM (+SwiGLU) -> h NVFP4 slabs ->
+//   down GEMM (+routing weight) -> combine.
+// Nothing in the forward synchronizes with the host; there is no CPU path.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/glm5x_moe.h"
+#include "fp4_codec.h"
+#include "glm5x_kernels.cuh"
+#include "glm5x_ptx.cuh"
+#include "sidecar.h"
+
+using namespace glm5x;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+glm5x_status fail_global(glm5x_status st, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  std::vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return st;
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point, so the
+// library does not link libcuda directly.
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2-D byte tensor [rows, row_bytes], box {128 bytes, box_rows}, 128B swizzle.
+bool make_tmap_u8(CUtensorMap* m, void* base, uint64_t row_bytes, uint64_t rows,
+                  uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {row_bytes, rows};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {128, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, base, dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <typename T>
+struct DevBuf {
+  T* p = nullptr;
+  size_t n = 0;
+};
+
+}  // namespace
+
+struct glm5x_moe {
+  glm5x_moe_config cfg{};
+  int device = 0;
+  int num_sms = 148;
+  cudaStream_t stream = nullptr;
+  std::string error;
+  glm5x_moe_stats stats{};
+  std::vector<void*> allocations;
+  int nseg = 0;      // local experts + shared
+  int E_loc = 0;
+  int64_t rows_cap = 0;
+  int last_T = 0;
+  int last_bn = 0;
+  bool routed_last = false;
+
+  // weights
+  uint8_t *w13_packed = nullptr, *w13_sf = nullptr, *w2_packed = nullptr, *w2_sf = nullptr;
+  float *w13_global = nullptr, *w2_global = nullptr;
+  std::vector<uint8_t> loaded;  // per slot
+  uint16_t* router_w = nullptr;
+  float* router_bias = nullptr;
+  bool router_set = false;
+
+  // workspace
+  uint32_t* err = nullptr;
+  float *token_amax = nullptr, *logits = nullptr, *topk_w = nullptr;
+  int32_t* topk_ids = nullptr;
+  PermuteBuffers pb{};
+  uint8_t *act_packed = nullptr, *act_sf = nullptr, *h_packed = nullptr, *h_sf = nullptr;
+  float *act_global = nullptr, *h_global = nullptr;
+  uint16_t *h_bf16 = nullptr, *y_bf16 = nullptr;
+  uint16_t* stage_in = nullptr;  // host-API staging
+  float* stage_out = nullptr;
+  uint8_t* stage_w = nullptr;    // weight admission staging
+  size_t stage_w_bytes = 0;
+  float* scratch_f = nullptr;
+
+  bool profiling = false;
+  int profiled = 0;
+  cudaEvent_t ev[GLM5X_NUM_PHASES + 1]{};
+  double phase_ms[GLM5X_NUM_PHASES]{};
+
+  CUtensorMap tm_w13{}, tm_w2{};
+  CUtensorMap tm_act[4]{}, tm_h[4]{};  // box rows 32, 64, 128, 256
+
+  glm5x_status fail(glm5x_status st, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    std::vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    error = buf;
+    g_last_error = buf;
+    return st;
+  }
+
+  template <typename T>
+  bool alloc(T** p, size_t count) {
+    void* q = nullptr;
+    if (cudaMalloc(&q, std::max<size_t>(count, 1) * sizeof(T)) != cudaSuccess) return false;
+    allocations.push_back(q);
+    stats.workspace_bytes += count * sizeof(T);
+    *p = static_cast<T*>(q);
+    return true;
+  }
+
+  int H() const { return cfg.hidden; }
+  int I() const { return cfg.intermediate; }
+  int K() const { return cfg.top_k; }
+  int kk() const { return cfg.top_k + (cfg.has_shared ? 1 : 0); }
+
+  size_t w13_packed_bytes() const { return (size_t)2 * I() * H() / 2; }
+  size_t w13_sf_bytes() const { return (size_t)(2 * I() / 128) * (H() / 64) * 512; }
+  size_t w2_packed_bytes() const { return (size_t)H() * I() / 2; }
+  size_t w2_sf_bytes() const { return (size_t)(H() / 128) * (I() / 64) * 512; }
+};
+
+namespace {
+
+glm5x_status cuda_fail(glm5x_moe* m, cudaError_t e, const char* what) {
+  return m->fail(GLM5X_DEVICE_ERROR, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define G5_CHECK(m, expr, what)                  \
+  do {                                           \
+    cudaError_t e_ = (expr);                     \
+    if (e_ != cudaSuccess) return cuda_fail(m, e_, what); \
+  } while (0)
+
+int bn_index(int bn) { return bn == 32 ? 0 : bn == 64 ? 1 : bn == 128 ? 2 : 3; }
+
+int pick_bn(const glm5x_moe* m, int64_t T) {
+  const double per_expert = (double)T * m->K() / std::max(1, m->cfg.num_experts);
+  if (per_expert <= 24) return 32;
+  if (per_expert <= 48) return 64;
+  if (per_expert <= 96) return 128;
+  return 256;
+}
+
+int slot_of(const glm5x_moe* m, int32_t expert) {
+  if (expert < 0) return m->cfg.has_shared ? m->E_loc : -1;
+  const int s = expert - m->cfg.expert_begin;
+  return (s >= 0 && s < m->E_loc) ? s : -1;
+}
+
+glm5x_status validate_nvfp4(glm5x_moe* m, const glm5x_nvfp4_matrix* w, int64_t rows,
+                            int64_t cols, const char* role) {
+  if (!w || !w->packed || !w->scales) return m->fail(GLM5X_INVALID_EXTENT, "%s: null matrix", role);
+  if (w->rows != rows || w->cols != cols)
+    return m->fail(GLM5X_INVALID_EXTENT, "%s: shape [%lld, %lld], expected [%lld, %lld]", role,
+                   (long long)w->rows, (long long)w->cols, (long long)rows, (long long)cols);
+  if (!(w->global_scale > 0.0f) || !std::isfinite(w->global_scale))
+    return m->fail(GLM5X_INVALID_EXTENT, "%s: global scale must be finite and positive", role);
+  return GLM5X_OK;
+}
+
+}  // namespace
+
+// ============================================================== engine API
+extern "C" {
+
+const char* glm5x_last_error_message(void) { return g_last_error.c_str(); }
+
+const char* glm5x_moe_error_message(const glm5x_moe* moe) {
+  return moe ? moe->error.c_str() : g_last_error.c_str();
+}
+
+glm5x_status glm5x_moe_create(const glm5x_moe_config* cfg, int device, glm5x_moe** out) {
+  if (!cfg || !out) return fail_global(GLM5X_INVALID_EXTENT, "null config or output");
+  *out = nullptr;
+  const glm5x_moe_config& c = *cfg;
+  if (c.hidden <= 0 || c.intermediate <= 0 || c.hidden % 512 || c.intermediate % 512 ||
+      c.intermediate % 64)
+    return fail_global(GLM5X_INVALID_EXTENT, "hidden and intermediate must be multiples of 512");
+  if (c.num_experts <= 0 || c.num_experts > 256 || c.top_k <= 0 || c.top_k > 16 ||
+      c.top_k > c.num_experts)
+    return fail_global(GLM5X_INVALID_EXTENT, "need 0 < top_k <= 16, top_k <= num_experts <= 256");
+  if (c.max_tokens <= 0 || c.max_tokens > (1 << 20))
+    return fail_global(GLM5X_INVALID_EXTENT, "max_tokens out of range");
+  if (!(c.routed_scaling > 0.0f)) return fail_global(GLM5X_INVALID_EXTENT, "routed_scaling <= 0");
+  if (c.precision != GLM5X_PRECISION_NVFP4 && c.precision != GLM5X_PRECISION_MXFP4)
+    return fail_global(GLM5X_INVALID_EXTENT, "unknown precision");
+  const int ecount = c.expert_count > 0 ? c.expert_count : c.num_experts;
+  if (c.expert_begin < 0 || c.expert_begin + ecount > c.num_experts)
+    return fail_global(GLM5X_INVALID_EXTENT, "expert range outside [0, num_experts)");
+
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0)
+    return fail_global(GLM5X_BACKEND_UNAVAILABLE, "no CUDA device");
+  if (device < 0 || device >= ndev) return fail_global(GLM5X_BACKEND_UNAVAILABLE, "bad device");
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess)
+    return fail_global(GLM5X_BACKEND_UNAVAILABLE, "cannot query device");
+  if (prop.major != 10 || prop.minor != 0)
+    return fail_global(GLM5X_UNSUPPORTED_ARCHITECTURE,
+                       "device compute capability %d.%d; this build needs sm_100 (B200)",
+                       prop.major, prop.minor);
+  if (!encode_fn()) return fail_global(GLM5X_BACKEND_UNAVAILABLE, "cuTensorMapEncodeTiled missing");
+
+  auto* m = new glm5x_moe();
+  m->cfg = c;
+  m->cfg.expert_count = ecount;
+  m->device = device;
+  m->num_sms = prop.multiProcessorCount;
+  m->E_loc = ecount;
+  m->nseg = ecount + (c.has_shared ? 1 : 0);
+  cudaSetDevice(device);
+  if (cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess) {
+    delete m;
+    return fail_global(GLM5X_BACKEND_UNAVAILABLE, "stream creation failed");
+  }
+  const int64_t T = c.max_tokens;
+  const int H = c.hidden, I = c.intermediate, E = c.num_experts, k = c.top_k;
+  const int nseg = m->nseg;
+  m->rows_cap = T * (int64_t)m->kk() + (int64_t)nseg * 128 + 256;
+  const int64_t R = m->rows_cap;
+  const int64_t rb = R / 128 + 2;
+  bool ok = true;
+  ok &= m->alloc(&m->w13_packed, (size_t)nseg * m->w13_packed_bytes());
+  ok &= m->alloc(&m->w13_sf, (size_t)nseg * m->w13_sf_bytes());
+  ok &= m->alloc(&m->w2_packed, (size_t)nseg * m->w2_packed_bytes());
+  ok &= m->alloc(&m->w2_sf, (size_t)nseg * m->w2_sf_bytes());
+  ok &= m->alloc(&m->w13_global, (size_t)2 * nseg);
+  ok &= m->alloc(&m->w2_global, (size_t)nseg);
+  ok &= m->alloc(&m->router_w, (size_t)E * H);
+  ok &= m->alloc(&m->router_bias, (size_t)E);
+  ok &= m->alloc(&m->err, 1);
+  ok &= m->alloc(&m->token_amax, (size_t)T);
+  ok &= m->alloc(&m->logits, (size_t)T * E);
+  ok &= m->alloc(&m->topk_w, (size_t)T * k);
+  ok &= m->alloc(&m->topk_ids, (size_t)T * k);
+  ok &= m->alloc(&m->pb.chunk_count, (size_t)((T + 255) / 256) * E);
+  ok &= m->alloc(&m->pb.rank, (size_t)T * k);
+  ok &= m->alloc(&m->pb.seg_count, (size_t)nseg + 1);
+  ok &= m->alloc(&m->pb.seg_start, (size_t)nseg + 1);
+  ok &= m->alloc(&m->pb.qprefix, (size_t)nseg + 1);
+  ok &= m->alloc(&m->pb.ntile_prefix, (size_t)nseg + 1);
+  ok &= m->alloc(&m->pb.seg_amax, (size_t)nseg);
+  ok &= m->alloc(&m->pb.h_amax, (size_t)nseg);
+  ok &= m->alloc(&m->pb.pos, (size_t)T * m->kk());
+  ok &= m->alloc(&m->pb.row_token, (size_t)R);
+  ok &= m->alloc(&m->pb.row_weight, (size_t)R);
+  ok &= m->alloc(&m->act_packed, (size_t)R * H / 2);
+  ok &= m->alloc(&m->act_sf, (size_t)rb * (H / 64) * 512);
+  ok &= m->alloc(&m->act_global, (size_t)nseg);
+  ok &= m->alloc(&m->h_bf16, (size_t)R * I);
+  ok &= m->alloc(&m->h_packed, (size_t)R * I / 2);
+  ok &= m->alloc(&m->h_sf, (size_t)rb * (I / 64) * 512);
+  ok &= m->alloc(&m->h_global, (size_t)nseg);
+  ok &= m->alloc(&m->y_bf16, (size_t)R * H);
+  ok &= m->alloc(&m->stage_in, (size_t)T * H);
+  ok &= m->alloc(&m->stage_out, (size_t)T * H);
+  ok &= m->alloc(&m->scratch_f, 16);
+  if (!ok) {
+    glm5x_moe_destroy(m);
+    return fail_global(GLM5X_OUT_OF_MEMORY, "device allocation failed (max_tokens=%lld)",
+                       (long long)T);
+  }
+  cudaMemset(m->err, 0, sizeof(uint32_t));
+  cudaMemset(m->w13_global, 0, sizeof(float) * 2 * nseg);
+  cudaMemset(m->w2_global, 0, sizeof(float) * nseg);
+  cudaMemset(m->act_packed, 0, (size_t)R * H / 2);
+  cudaMemset(m->h_packed, 0, (size_t)R * I / 2);
+  cudaMemset(m->act_sf, 0, (size_t)rb * (H / 64) * 512);
+  cudaMemset(m->h_sf, 0, (size_t)rb * (I / 64) * 512);
+  m->loaded.assign(nseg, 0);
+  ok = make_tmap_u8(&m->tm_w13, m->w13_packed, H / 2, (uint64_t)nseg * 2 * I, 128) &&
+       make_tmap_u8(&m->tm_w2, m->w2_packed, I / 2, (uint64_t)nseg * H, 128);
+  const int boxes[4] = {32, 64, 128, 256};
+  for (int i = 0; i < 4 && ok; ++i) {
+    ok = make_tmap_u8(&m->tm_act[i], m->act_packed, H / 2, R, boxes[i]) &&
+         make_tmap_u8(&m->tm_h[i], m->h_packed, I / 2, R, boxes[i]);
+  }
+  if (!ok) {
+    glm5x_moe_destroy(m);
+    return fail_global(GLM5X_BACKEND_UNAVAILABLE, "tensor map encoding failed");
+  }
+  if (cudaDeviceSynchronize() != cudaSuccess) {
+    glm5x_moe_destroy(m);
+    return fail_global(GLM5X_DEVICE_ERROR, "device initialization failed");
+  }
+  *out = m;
+  return GLM5X_OK;
+}
+
+void glm5x_moe_destroy(glm5x_moe* m) {
+  if (!m) return;
+  cudaSetDevice(m->device);
+  if (m->stream) cudaStreamSynchronize(m->stream);
+  for (void* p : m->allocations) cudaFree(p);
+  if (m->stage_w) cudaFree(m->stage_w);
+  if (m->stream) cudaStreamDestroy(m->stream);
+  for (auto& e : m->ev)
+    if (e) cudaEventDestroy(e);
+  delete m;
+}
+
+glm5x_status glm5x_moe_set_router(glm5x_moe* m, const uint16_t* w, const float* bias) {
+  if (!m || !w || !bias) return fail_global(GLM5X_INVALID_EXTENT, "null router argument");
+  const int E = m->cfg.num_experts, H = m->H();
+  for (int e = 0; e < E; ++e)
+    if (!std::isfinite(bias[e])) return m->fail(GLM5X_INVALID_STATE, "router bias not finite");
+  cudaSetDevice(m->device);
+  G5_CHECK(m, cudaMemcpyAsync(m->router_w, w, sizeof(uint16_t) * E * H, cudaMemcpyHostToDevice,
+                              m->stream), "router upload");
+  G5_CHECK(m, cudaMemcpyAsync(m->router_bias, bias, sizeof(float) * E, cudaMemcpyHostToDevice,
+                              m->stream), "bias upload");
+  G5_CHECK(m, cudaStreamSynchronize(m->stream), "router upload");
+  m->router_set = true;
+  return GLM5X_OK;
+}
+
+static glm5x_status admit_nvfp4(glm5x_moe* m, int slot, const glm5x_nvfp4_matrix* gate,
+                                const glm5x_nvfp4_matrix* up, const glm5x_nvfp4_matrix* down,
+                                bool device_ptrs) {
+  const int H = m->H(), I = m->I();
+  const size_t g_pb = (size_t)I * H / 2, g_sb = (size_t)(I / 128) * (H / 64) * 512;
+  const size_t d_pb = m->w2_packed_bytes(), d_sb = m->w2_sf_bytes();
+  const uint8_t *gp = gate->packed, *gs = gate->scales, *up_p = up->packed, *us = up->scales;
+  const uint8_t *dp = down->packed, *ds = down->scales;
+  cudaStream_t st = m->stream;
+  if (!device_ptrs) {
+    const size_t need = 2 * (g_pb + g_sb);
+    if (m->stage_w_bytes < need) {
+      if (m->stage_w) cudaFree(m->stage_w);
+      m->stage_w = nullptr;
+      m->stage_w_bytes = 0;
+      G5_CHECK(m, cudaMalloc(&m->stage_w, need), "weight staging");
+      m->stage_w_bytes = need;
+    }
+    uint8_t* s = m->stage_w;
+    G5_CHECK(m, cudaMemcpyAsync(s, gp, g_pb, cudaMemcpyHostToDevice, st), "gate upload");
+    G5_CHECK(m, cudaMemcpyAsync(s + g_pb, gs, g_sb, cudaMemcpyHostToDevice, st), "gate upload");
+    G5_CHECK(m, cudaMemcpyAsync(s + g_pb + g_sb, up_p, g_pb, cudaMemcpyHostToDevice, st), "up");
+    G5_CHECK(m, cudaMemcpyAsync(s + 2 * g_pb + g_sb, us, g_sb, cudaMemcpyHostToDevice, st), "up");
+    gp = s;
+    gs = s + g_pb;
+    up_p = s + g_pb + g_sb;
+    us = s + 2 * g_pb + g_sb;
+  }
+  G5_CHECK(m, launch_interleave_gate_up(gp, gs, up_p, us, I, H, 16,
+                                        m->w13_packed + (size_t)slot * m->w13_packed_bytes(),
+                                        m->w13_sf + (size_t)slot * m->w13_sf_bytes(), st),
+           "gate/up interleave");
+  const cudaMemcpyKind kind = device_ptrs ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+  G5_CHECK(m, cudaMemcpyAsync(m->w2_packed + (size_t)slot * d_pb, dp, d_pb, kind, st), "down");
+  G5_CHECK(m, cudaMemcpyAsync(m->w2_sf + (size_t)slot * d_sb, ds, d_sb, kind, st), "down scales");
+  const float g13[2] = {gate->global_scale, up->global_scale};
+  G5_CHECK(m, cudaMemcpyAsync(m->w13_global + 2 * slot, g13, sizeof g13, cudaMemcpyHostToDevice, st),
+           "globals");
+  G5_CHECK(m, cudaMemcpyAsync(m->w2_global + slot, &down->global_scale, sizeof(float),
+                              cudaMemcpyHostToDevice, st), "globals");
+  G5_CHECK(m, cudaStreamSynchronize(st), "expert admission");
+  if (!m->loaded[slot]) {
+    m->loaded[slot] = 1;
+    m->stats.loaded_experts++;
+    m->stats.resident_weight_bytes += m->w13_packed_bytes() + m->w13_sf_bytes() + d_pb + d_sb;
+  }
+  return GLM5X_OK;
+}
+
+static glm5x_status load_nvfp4_common(glm5x_moe* m, int32_t expert,
+                                      const glm5x_nvfp4_matrix* gate,
+                                      const glm5x_nvfp4_matrix* up,
+                                      const glm5x_nvfp4_matrix* down, bool dev) {
+  if (!m) return fail_global(GLM5X_INVALID_STATE, "null engine");
+  if (m->cfg.precision != GLM5X_PRECISION_NVFP4)
+    return m->fail(GLM5X_INVALID_STATE, "engine precision is not NVFP4");
+  const int slot = slot_of(m, expert);
+  if (slot < 0) return m->fail(GLM5X_INVALID_EXTENT, "expert %d is not held by this engine", expert);
+  glm5x_status s;
+  if ((s = validate_nvfp4(m, gate, m->I(), m->H(), "gate")) != GLM5X_OK) return s;
+  if ((s = validate_nvfp4(m, up, m->I(), m->H(), "up")) != GLM5X_OK) return s;
+  if ((s = validate_nvfp4(m, down, m->H(), m->I(), "down")) != GLM5X_OK) return s;
+  cudaSetDevice(m->device);
+  return admit_nvfp4(m, slot, gate, up, down, dev);
+}
+
+glm5x_status glm5x_moe_load_expert_nvfp4(glm5x_moe* m, int32_t expert,
+                                         const glm5x_nvfp4_matrix* gate,
+                                         const glm5x_nvfp4_matrix* up,
+                                         const glm5x_nvfp4_matrix* down) {
+  return load_nvfp4_common(m, expert, gate, up, down, false);
+}
+
+glm5x_status glm5x_moe_load_expert_nvfp4_device(glm5x_moe* m, int32_t expert,
+                                                const glm5x_nvfp4_matrix* gate,
+                                                const glm5x_nvfp4_matrix* up,
+                                                const glm5x_nvfp4_matrix* down) {
+  return load_nvfp4_common(m, expert, gate, up, down, true);
+}
+
+glm5x_status glm5x_moe_load_expert_mxfp4(glm5x_moe* m, int32_t expert,
+                                         const glm5x_mxfp4_matrix* gate,
+                                         const glm5x_mxfp4_matrix* up,
+                                         const glm5x_mxfp4_matrix* down) {
+  if (!m) return fail_global(GLM5X_INVALID_STATE, "null engine");
+  (void)expert;
+  (void)gate;
+  (void)up;
+  (void)down;
+  return m->fail(GLM5X_BACKEND_UNAVAILABLE, "MXFP4 experts are not admitted by this build yet");
+}
+
+glm5x_status glm5x_moe_load_sidecar(glm5x_moe* m, int32_t expert, const char* path) {
+  if (!m || !path) return fail_global(GLM5X_INVALID_STATE, "null argument");
+  Sidecar sc;
+  std::string msg;
+  const int rc = read_sidecar(path, &sc, &msg);
+  if (rc != 0) return m->fail(static_cast<glm5x_status>(rc), "%s", msg.c_str());
+  if (sc.precision == 0) {
+    glm5x_nvfp4_matrix mats[3];
+    for (int r = 0; r < 3; ++r) {
+      const SidecarRole& ro = sc.roles[r];
+      if (ro.group_size != 16) return m->fail(GLM5X_INVALID_EXTENT, "NVFP4 group size must be 16");
+      const int64_t expect = ((ro.rows + 127) / 128) * ((ro.cols / 16 + 3) / 4) * 512;
+      if (ro.scale_bytes != expect)
+        return m->fail(GLM5X_INVALID_EXTENT, "NVFP4 blocked scale size mismatch");
+      mats[r] = glm5x_nvfp4_matrix{sc.payload.data() + ro.packed_offset,
+                                   sc.payload.data() + ro.scale_offset, ro.global_scale, ro.rows,
+                                   ro.cols};
+    }
+    return glm5x_moe_load_expert_nvfp4(m, expert, &mats[0], &mats[1], &mats[2]);
+  }
+  glm5x_mxfp4_matrix mats[3];
+  for (int r = 0; r < 3; ++r) {
+    const SidecarRole& ro = sc.roles[r];
+    mats[r] = glm5x_mxfp4_matrix{sc.payload.data() + ro.packed_offset,
+                                 sc.payload.data() + ro.scale_offset, ro.rows, ro.cols,
+                                 ro.group_size};
+  }
+  return glm5x_moe_load_expert_mxfp4(m, expert, &mats[0], &mats[1], &mats[2]);
+}
+
+static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
+                                const int32_t* ids_in, const float* w_in, float* out,
+                                cudaStream_t st) {
+  if (T64 <= 0 || T64 > m->cfg.max_tokens)
+    return m->fail(GLM5X_INVALID_EXTENT, "tokens %lld outside [1, %d]", (long long)T64,
+                   m->cfg.max_tokens);
+  if (m->cfg.precision != GLM5X_PRECISION_NVFP4)
+    return m->fail(GLM5X_BACKEND_UNAVAILABLE, "MXFP4 forward is not built yet");
+  if (m->E_loc != m->cfg.num_experts)
+    return m->fail(GLM5X_INVALID_STATE, "expert-parallel engines forward through the EP API");
+  for (int s = 0; s < m->nseg; ++s)
+    if (!m->loaded[s]) return m->fail(GLM5X_INVALID_STATE, "expert slot %d not loaded", s);
+  if (!ids_in && !m->router_set) return m->fail(GLM5X_INVALID_STATE, "router not set");
+  const int T = static_cast<int>(T64);
+  const int H = m->H(), I = m->I(), E = m->cfg.num_experts, k = m->K();
+  const int hs = m->cfg.has_shared ? 1 : 0;
+  const int bn = pick_bn(m, T);
+  const int bi = bn_index(bn);
+  uint64_t launches = 0;
+  auto mark = [&](int phase) {
+    if (m->profiling) cudaEventRecord(m->ev[phase], st);
+  };
+  mark(0);
+  G5_CHECK(m, launch_row_amax_bf16(x, T, H, m->token_amax, m->err, st), "row amax");
+  mark(1);
+  ++launches;
+  const int32_t* ids = ids_in;
+  const float* wts = w_in;
+  if (!ids_in) {
+    G5_CHECK(m, launch_router_logits_simt(x, m->router_w, T, H, E, m->logits, st), "router");
+    mark(2);
+    G5_CHECK(m, launch_topk(m->logits, 0, m->router_bias, T, E, k, m->cfg.routed_scaling,
+                            m->topk_ids, m->topk_w, m->err, st), "topk");
+    launches += 2;
+    ids = m->topk_ids;
+    wts = m->topk_w;
+  } else {
+    mark(2);
+  }
+  mark(3);
+  G5_CHECK(m, launch_permute(ids, wts, m->token_amax, T, k, E, hs, bn, m->pb, m->err, st),
+           "permute");
+  launches += 3;
+  const int64_t max_rows = (int64_t)T * m->kk() + (int64_t)m->nseg * 8;
+  mark(4);
+  G5_CHECK(m, launch_nvfp4_quantize_segments(x, H, m->pb.row_token, m->pb.seg_start,
+                                             m->pb.seg_count, m->pb.qprefix, m->nseg,
+                                             m->pb.seg_amax, max_rows, m->act_packed, m->act_sf,
+                                             m->act_global, st), "activation quantize");
+  GemmParams g1{};
+  g1.sfa = m->w13_sf;
+  g1.sfb = m->act_sf;
+  g1.seg_count = m->pb.seg_count;
+  g1.seg_start = m->pb.seg_start;
+  g1.ntile_prefix = m->pb.ntile_prefix;
+  g1.a_global = m->w13_global;
+  g1.b_global = m->act_global;
+  g1.out = m->h_bf16;
+  g1.h_amax = m->pb.h_amax;
+  g1.err = m->err;
+  g1.K = H;
+  g1.M_per = 2 * I;
+  g1.nseg = m->nseg;
+  mark(5);
+  G5_CHECK(m, launch_nvfp4_grouped_gemm(bn, 0, &m->tm_w13, &m->tm_act[bi], g1, m->num_sms, st),
+           "gate/up GEMM");
+  mark(6);
+  G5_CHECK(m, launch_nvfp4_quantize_segments(m->h_bf16, I, nullptr, m->pb.seg_start,
+                                             m->pb.seg_count, m->pb.qprefix, m->nseg,
+                                             m->pb.h_amax, max_rows, m->h_packed, m->h_sf,
+                                             m->h_global, st), "h quantize");
+  GemmParams g2 = g1;
+  g2.sfa = m->w2_sf;
+  g2.sfb = m->h_sf;
+  g2.a_global = m->w2_global;
+  g2.b_global = m->h_global;
+  g2.row_weight = m->pb.row_weight;
+  g2.out = m->y_bf16;
+  g2.h_amax = nullptr;
+  g2.K = I;
+  g2.M_per = H;
+  mark(7);
+  G5_CHECK(m, launch_nvfp4_grouped_gemm(bn, 1, &m->tm_w2, &m->tm_h[bi], g2, m->num_sms, st),
+           "down GEMM");
+  mark(8);
+  G5_CHECK(m, launch_combine(m->y_bf16, m->pb.pos, T, m->kk(), H, out, st), "combine");
+  mark(9);
+  if (m->profiling) {
+    // accumulate this forward's phases (waits only on this forward's events)
+    G5_CHECK(m, cudaEventSynchronize(m->ev[9]), "profiling");
+    for (int i = 0; i < GLM5X_NUM_PHASES; ++i) {
+      float ms = 0.0f;
+      if (cudaEventElapsedTime(&ms, m->ev[i], m->ev[i + 1]) == cudaSuccess) m->phase_ms[i] += ms;
+    }
+    m->profiled++;
+  }
+  launches += 5;
+  m->stats.forward_calls++;
+  m->stats.kernel_launches += launches;
+  m->last_T = T;
+  m->last_bn = bn;
+  m->routed_last = ids_in == nullptr;
+  return GLM5X_OK;
+}
+
+glm5x_status glm5x_moe_forward(glm5x_moe* m, const void* hidden, int64_t T, float* out,
+                               void* stream) {
+  if (!m || !hidden || !out) return fail_global(GLM5X_INVALID_STATE, "null argument");
+  cudaSetDevice(m->device);
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : m->stream;
+  return run_forward(m, static_cast<const uint16_t*>(hidden), T, nullptr, nullptr, out, st);
+}
+
+glm5x_status glm5x_moe_forward_routed(glm5x_moe* m, const void* hidden, int64_t T,
+                                      const int32_t* ids, const float* weights, float* out,
+                                      void* stream) {
+  if (!m || !hidden || !out || !ids || !weights)
+    return fail_global(GLM5X_INVALID_STATE, "null argument");
+  cudaSetDevice(m->device);
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : m->stream;
+  return run_forward(m, static_cast<const uint16_t*>(hidden), T, ids, weights, out, st);
+}
+
+glm5x_status glm5x_moe_forward_host(glm5x_moe* m, const uint16_t* hidden, int64_t T,
+                                    float* out) {
+  if (!m || !hidden || !out) return fail_global(GLM5X_INVALID_STATE, "null argument");
+  if (T <= 0 || T > m->cfg.max_tokens)
+    return m->fail(GLM5X_INVALID_EXTENT, "tokens outside [1, max_tokens]");
+  cudaSetDevice(m->device);
+  const size_t in_bytes = sizeof(uint16_t) * T * m->H(), out_bytes = sizeof(float) * T * m->H();
+  G5_CHECK(m, cudaMemcpyAsync(m->stage_in, hidden, in_bytes, cudaMemcpyHostToDevice, m->stream),
+           "hidden upload");
+  glm5x_status s = run_forward(m, m->stage_in, T, nullptr, nullptr, m->stage_out, m->stream);
+  if (s != GLM5X_OK) return s;
+  G5_CHECK(m, cudaMemcpyAsync(out, m->stage_out, out_bytes, cudaMemcpyDeviceToHost, m->stream),
+           "output download");
+  G5_CHECK(m, cudaStreamSynchronize(m->stream), "forward");
+  m->stats.activation_h2d_bytes += in_bytes;
+  m->stats.device_to_host_bytes += out_bytes;
+  m->stats.stream_synchronization_count++;
+  return glm5x_moe_check(m);
+}
+
+glm5x_status glm5x_moe_check(glm5x_moe* m) {
+  if (!m) return fail_global(GLM5X_INVALID_STATE, "null engine");
+  cudaSetDevice(m->device);
+  G5_CHECK(m, cudaDeviceSynchronize(), "device synchronize");
+  uint32_t e = 0;
+  G5_CHECK(m, cudaMemcpy(&e, m->err, sizeof e, cudaMemcpyDeviceToHost), "error word");
+  if (e) {
+    cudaMemset(m->err, 0, sizeof(uint32_t));
+    if (e & kErrWaitTimeout) return m->fail(GLM5X_WAIT_TIMEOUT, "device wait timed out (0x%x)", e);
+    if (e & kErrNonFinite) return m->fail(GLM5X_INVALID_STATE, "non-finite input (0x%x)", e);
+    if (e & kErrBounds) return m->fail(GLM5X_INVALID_EXTENT, "routing ids invalid (0x%x)", e);
+    return m->fail(GLM5X_DEVICE_ERROR, "device error word 0x%x", e);
+  }
+  return GLM5X_OK;
+}
+
+glm5x_status glm5x_moe_last_routing(glm5x_moe* m, int32_t* ids, float* weights, float* logits,
+                                    int64_t T) {
+  if (!m) return fail_global(GLM5X_INVALID_STATE, "null engine");
+  if (!m->routed_last || T != m->last_T)
+    return m->fail(GLM5X_INVALID_STATE, "no routed forward with %lld tokens", (long long)T);
+  cudaSetDevice(m->device);
+  G5_CHECK(m, cudaStreamSynchronize(m->stream), "sync");
+  const int k = m->K();
+  if (ids) G5_CHECK(m, cudaMemcpy(ids, m->topk_ids, sizeof(int32_t) * T * k, cudaMemcpyDeviceToHost), "ids");
+  if (weights) G5_CHECK(m, cudaMemcpy(weights, m->topk_w, sizeof(float) * T * k, cudaMemcpyDeviceToHost), "w");
+  if (logits)
+    G5_CHECK(m, cudaMemcpy(logits, m->logits, sizeof(float) * T * m->cfg.num_experts,
+                           cudaMemcpyDeviceToHost), "logits");
+  return GLM5X_OK;
+}
+
+glm5x_status glm5x_moe_get_stats(const glm5x_moe* m, glm5x_moe_stats* out) {
+  if (!m || !out) return fail_global(GLM5X_INVALID_STATE, "null argument");
+  *out = m->stats;
+  return GLM5X_OK;
+}
+
+glm5x_status glm5x_moe_debug_buffer(glm5x_moe* m, int32_t which, void** ptr, size_t* bytes) {
+  if (!m || !ptr || !bytes) return fail_global(GLM5X_INVALID_STATE, "null argument");
+  const int64_t R = m->rows_cap, H = m->H(), I = m->I();
+  const int64_t rb = R / 128 + 2;
+  switch (which) {
+    case 0: *ptr = m->act_packed; *bytes = R * H / 2; break;
+    case 1: *ptr = m->act_sf; *bytes = rb * (H / 64) * 512; break;
+    case 2: *ptr = m->act_global; *bytes = sizeof(float) * m->nseg; break;
+    case 3: *ptr = m->h_bf16; *bytes = R * I * 2; break;
+    case 4: *ptr = m->h_packed; *bytes = R * I / 2; break;
+    case 5: *ptr = m->h_sf; *bytes = rb * (I / 64) * 512; break;
+    case 6: *ptr = m->h_global; *bytes = sizeof(float) * m->nseg; break;
+    case 7: *ptr = m->y_bf16; *bytes = R * H * 2; break;
+    case 8: *ptr = m->pb.seg_start; *bytes = sizeof(int32_t) * (m->nseg + 1); break;
+    case 9: *ptr = m->pb.seg_count; *bytes = sizeof(int32_t) * m->nseg; break;
+    case 10: *ptr = m->pb.row_token; *bytes = sizeof(int32_t) * R; break;
+    case 11: *ptr = m->pb.pos; *bytes = sizeof(int32_t) * m->cfg.max_tokens * m->kk(); break;
+    case 12: *ptr = m->pb.row_weight; *bytes = sizeof(float) * R; break;
+    default: return m->fail(GLM5X_INVALID_EXTENT, "unknown debug buffer %d", which);
+  }
+  return GLM5X_OK;
+}
+
+glm5x_status glm5x_moe_set_profiling(glm5x_moe* m, int32_t enable) {
+  if (!m) return fail_global(GLM5X_INVALID_STATE, "null engine");
+  cudaSetDevice(m->device);
+  if (enable && !m->ev[0]) {
+    for (auto& e : m->ev) G5_CHECK(m, cudaEventCreate(&e), "event create");
+  }
+  m->profiling = enable != 0;
+  return GLM5X_OK;
+}
+
+glm5x_status glm5x_moe_phase_times(glm5x_moe* m, float* ms, int32_t* forwards) {
+  if (!m || !ms) return fail_global(GLM5X_INVALID_STATE, "null argument");
+  cudaSetDevice(m->device);
+  G5_CHECK(m, cudaDeviceSynchronize(), "sync");
+  for (int i = 0; i < GLM5X_NUM_PHASES; ++i) {
+    ms[i] = static_cast<float>(m->phase_ms[i]);
+    m->phase_ms[i] = 0.0;
+  }
+  if (forwards) *forwards = m->profiled;
+  m->profiled = 0;
+  return GLM5X_OK;
+}
+
+glm5x_status glm5x_moe_get_stream(glm5x_moe* m, void** stream) {
+  if (!m || !stream) return fail_global(GLM5X_INVALID_STATE, "null argument");
+  *stream = m->stream;
+  return GLM5X_OK;
+}
+
+glm5x_status glm5x_moe_debug_copy(glm5x_moe* m, int32_t which, void* dst, size_t bytes) {
+  void* src = nullptr;
+  size_t size = 0;
+  glm5x_status st = glm5x_moe_debug_buffer(m, which, &src, &size);
+  if (st != GLM5X_OK) return st;
+  if (!dst || bytes > size) return m->fail(GLM5X_INVALID_EXTENT, "debug copy larger than buffer");
+  cudaSetDevice(m->device);
+  G5_CHECK(m, cudaStreamSynchronize(m->stream), "sync");
+  G5_CHECK(m, cudaMemcpy(dst, src, bytes, cudaMemcpyDeviceToDevice), "debug copy");
+  return GLM5X_OK;
+}
+
+// ============================================================== kernel API
+}  // extern "C"
+
+static cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+static glm5x_status sync_error(cudaStream_t st, uint32_t* err_dev, uint32_t mask_invalid,
+                               const char* what) {
+  cudaError_t e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return fail_global(GLM5X_DEVICE_ERROR, "%s: %s", what, cudaGetErrorString(e));
+  uint32_t w = 0;
+  cudaMemcpy(&w, err_dev, sizeof w, cudaMemcpyDeviceToHost);
+  cudaFree(err_dev);
+  if (w & mask_invalid) return fail_global(GLM5X_INVALID_MXFP4, "%s: invalid input (0x%x)", what, w);
+  if (w) return fail_global(GLM5X_INVALID_STATE, "%s: device error 0x%x", what, w);
+  return GLM5X_OK;
+}
+
+template <typename T>
+static glm5x_status nvfp4_quantize_any(const T* src, int64_t rows, int64_t cols, int32_t mode,
+                                       uint8_t* packed, uint8_t* scales, float* g, void* stream) {
+  if (!src || !packed || !scales || !g) return fail_global(GLM5X_INVALID_EXTENT, "null pointer");
+  if (rows <= 0 || cols <= 0 || cols % 16)
+    return fail_global(GLM5X_INVALID_EXTENT, "NVFP4 needs cols to be a positive multiple of 16");
+  uint32_t* err = nullptr;
+  float* amax = nullptr;
+  if (cudaMalloc(&err, 4) != cudaSuccess || cudaMalloc(&amax, 4) != cudaSuccess)
+    return fail_global(GLM5X_OUT_OF_MEMORY, "scratch allocation");
+  cudaStream_t st = as_stream(stream);
+  cudaMemsetAsync(err, 0, 4, st);
+  cudaError_t e = launch_nvfp4_quantize_matrix<T>(src, rows, cols, mode, amax, packed, scales, g,
+                                                  err, st);
+  if (e != cudaSuccess) return fail_global(GLM5X_DEVICE_ERROR, "quantize: %s", cudaGetErrorString(e));
+  glm5x_status s = sync_error(st, err, 0, "nvfp4 quantize");
+  cudaFree(amax);
+  return s;
+}
+
+extern "C" {
+glm5x_status glm5x_nvfp4_quantize_f32(const float* src, int64_t rows, int64_t cols,
+                                      int32_t mode, uint8_t* packed, uint8_t* scales,
+                                      float* g, void* stream) {
+  return nvfp4_quantize_any<float>(src, rows, cols, mode, packed, scales, g, stream);
+}
+
+glm5x_status glm5x_nvfp4_quantize_bf16(const uint16_t* src, int64_t rows, int64_t cols,
+                                       int32_t mode, uint8_t* packed, uint8_t* scales,
+                                       float* g, void* stream) {
+  return nvfp4_quantize_any<__nv_bfloat16>(reinterpret_cast<const __nv_bfloat16*>(src), rows,
+                                           cols, mode, packed, scales, g, stream);
+}
+
+glm5x_status glm5x_nvfp4_quantize_slabs_bf16(const uint16_t* src, int64_t cols,
+                                             const int32_t* row_token, const int32_t* seg_start,
+                                             const int32_t* seg_count, int32_t nseg,
+                                             int64_t out_rows, uint8_t* packed,
+                                             uint8_t* scales, float* seg_global, void* stream) {
+  if (!src || !row_token || !seg_start || !seg_count || !packed || !scales || !seg_global)
+    return fail_global(GLM5X_INVALID_EXTENT, "null pointer");
+  if (cols <= 0 || cols % 512 || nseg <= 0 || nseg > 1024 || out_rows <= 0)
+    return fail_global(GLM5X_INVALID_EXTENT, "slab quantize: bad extents");
+  cudaStream_t st = as_stream(stream);
+  // segment bookkeeping on the host: counts rounded to 8, amax per segment
+  std::vector<int32_t> cnt(nseg), start(nseg + 1);
+  cudaMemcpy(cnt.data(), seg_count, sizeof(int32_t) * nseg, cudaMemcpyDeviceToHost);
+  cudaMemcpy(start.data(), seg_start, sizeof(int32_t) * (nseg + 1), cudaMemcpyDeviceToHost);
+  std::vector<int32_t> q(nseg + 1, 0);
+  for (int s = 0; s < nseg; ++s) {
+    if (cnt[s] < 0 || start[s] % 128 || start[s] + (cnt[s] + 7) / 8 * 8 > out_rows)
+      return fail_global(GLM5X_INVALID_EXTENT, "segment %d out of range", s);
+    q[s + 1] = q[s] + (cnt[s] + 7) / 8 * 8;
+  }
+  std::vector<int32_t> tok(out_rows);
+  cudaMemcpy(tok.data(), row_token, sizeof(int32_t) * out_rows, cudaMemcpyDeviceToHost);
+  int32_t max_tok = 0;
+  for (int s = 0; s < nseg; ++s)
+    for (int r = 0; r < cnt[s]; ++r) max_tok = std::max(max_tok, tok[start[s] + r]);
+  // per-token amax, then per-segment max
+  float *tok_amax = nullptr, *seg_amax = nullptr;
+  int32_t* qp = nullptr;
+  uint32_t* err = nullptr;
+  cudaMalloc(&tok_amax, sizeof(float) * (max_tok + 1));
+  cudaMalloc(&seg_amax, sizeof(float) * nseg);
+  cudaMalloc(&qp, sizeof(int32_t) * (nseg + 1));
+  cudaMalloc(&err, 4);
+  cudaMemsetAsync(err, 0, 4, st);
+  launch_row_amax_bf16(src, max_tok + 1, (int)cols, tok_amax, err, st);
+  std::vector<float> ta(max_tok + 1), sa(nseg, 0.0f);
+  cudaMemcpyAsync(ta.data(), tok_amax, sizeof(float) * (max_tok + 1), cudaMemcpyDeviceToHost, st);
+  cudaStreamSynchronize(st);
+  for (int s = 0; s < nseg; ++s)
+    for (int r = 0; r < cnt[s]; ++r) sa[s] = std::max(sa[s], ta[tok[start[s] + r]]);
+  cudaMemcpyAsync(seg_amax, sa.data(), sizeof(float) * nseg, cudaMemcpyHostToDevice, st);
+  cudaMemcpyAsync(qp, q.data(), sizeof(int32_t) * (nseg + 1), cudaMemcpyHostToDevice, st);
+  cudaError_t e = launch_nvfp4_quantize_segments(src, (int)cols, row_token, seg_start, seg_count,
+                                                 qp, nseg, seg_amax, q[nseg], packed, scales,
+                                                 seg_global, st);
+  glm5x_status s = e == cudaSuccess ? sync_error(st, err, 0, "slab quantize")
+                                    : fail_global(GLM5X_DEVICE_ERROR, "slab quantize launch");
+  cudaFree(tok_amax);
+  cudaFree(seg_amax);
+  cudaFree(qp);
+  return s;
+}
+
+glm5x_status glm5x_nvfp4_dequantize(const uint8_t* packed, const uint8_t* scales, float g,
+                                    int64_t rows, int64_t cols, float* out, void* stream) {
+  if (!packed || !scales || !out || rows <= 0 || cols <= 0 || cols % 16)
+    return fail_global(GLM5X_INVALID_EXTENT, "dequantize: bad arguments");
+  cudaError_t e = launch_nvfp4_dequantize(packed, scales, g, rows, cols, out, as_stream(stream));
+  return e == cudaSuccess ? GLM5X_OK : fail_global(GLM5X_DEVICE_ERROR, "dequantize launch");
+}
+
+glm5x_status glm5x_mxfp4_encode_f32(const float* src, int64_t rows, int64_t cols,
+                                    int64_t group, int32_t mode, uint8_t* packed,
+                                    uint8_t* scales, void* stream) {
+  if (!src || !packed || !scales || rows <= 0 || cols <= 0 || group <= 0 || group > 64 ||
+      cols % group || cols % 2)
+    return fail_global(GLM5X_INVALID_MXFP4, "cols must align to group_size and nibble pairs");
+  uint32_t* err = nullptr;
+  if (cudaMalloc(&err, 4) != cudaSuccess) return fail_global(GLM5X_OUT_OF_MEMORY, "scratch");
+  cudaStream_t st = as_stream(stream);
+  cudaMemsetAsync(err, 0, 4, st);
+  launch_mxfp4_encode<float>(src, rows * cols, (int)group, mode, packed, scales, err, st);
+  return sync_error(st, err, kErrBadScale | kErrNonFinite, "mxfp4 encode");
+}
+
+glm5x_status glm5x_mxfp4_decode(const uint8_t* packed, const uint8_t* scales, int64_t rows,
+                                int64_t cols, int64_t group, float* out, void* stream) {
+  if (!packed || !scales || !out || rows <= 0 || cols <= 0 || group <= 0 || cols % group ||
+      cols % 2)
+    return fail_global(GLM5X_INVALID_MXFP4, "cols must align to group_size and nibble pairs");
+  uint32_t* err = nullptr;
+  if (cudaMalloc(&err, 4) != cudaSuccess) return fail_global(GLM5X_OUT_OF_MEMORY, "scratch");
+  cudaStream_t st = as_stream(stream);
+  cudaMemsetAsync(err, 0, 4, st);
+  launch_mxfp4_decode(packed, scales, rows * cols, (int)group, out, err, st);
+  return sync_error(st, err, kErrBadScale, "mxfp4 decode");
+}
+
+glm5x_status glm5x_select_routing(const float* scores, const float* bias, int64_t T, int32_t E,
+                                  int32_t k, float scale, int32_t* ids, float* weights,
+                                  void* stream) {
+  if (!scores || !bias || !ids || !weights || T <= 0 || E <= 0 || E > 512 || k <= 0 || k > 16 ||
+      k > E)
+    return fail_global(GLM5X_INVALID_STATE, "invalid routing dimensions");
+  uint32_t* err = nullptr;
+  if (cudaMalloc(&err, 4) != cudaSuccess) return fail_global(GLM5X_OUT_OF_MEMORY, "scratch");
+  cudaStream_t st = as_stream(stream);
+  cudaMemsetAsync(err, 0, 4, st);
+  launch_topk(scores, 1, bias, (int)T, E, k, scale, ids, weights, err, st);
+  return sync_error(st, err, 0, "select routing");
+}
+
+glm5x_status glm5x_expert_major_plan(const int32_t* ids, int64_t T, int32_t k, int32_t E,
+                                     int32_t* seg_count, int32_t* seg_start, int32_t* pos,
+                                     int32_t* row_token, void* stream) {
+  if (!ids || !seg_count || !seg_start || !pos || !row_token || T <= 0 || k <= 0 || k > 16 ||
+      E <= 0 || E > 256)
+    return fail_global(GLM5X_INVALID_EXTENT, "invalid plan dimensions");
+  cudaStream_t st = as_stream(stream);
+  PermuteBuffers b{};
+  const int nchunks = (int)((T + 255) / 256);
+  float* wts = nullptr;
+  float* amax = nullptr;
+  uint32_t* err = nullptr;
+  bool ok = cudaMalloc(&b.chunk_count, sizeof(int32_t) * nchunks * E) == cudaSuccess &&
+            cudaMalloc(&b.rank, sizeof(int32_t) * T * k) == cudaSuccess &&
+            cudaMalloc(&b.qprefix, sizeof(int32_t) * (E + 1)) == cudaSuccess &&
+            cudaMalloc(&b.ntile_prefix, sizeof(int32_t) * (E + 1)) == cudaSuccess &&
+            cudaMalloc(&b.seg_amax, sizeof(float) * E) == cudaSuccess &&
+            cudaMalloc(&b.h_amax, sizeof(float) * E) == cudaSuccess &&
+            cudaMalloc(&b.row_weight, sizeof(float) * (T * k + E * 128)) == cudaSuccess &&
+            cudaMalloc(&wts, sizeof(float) * T * k) == cudaSuccess &&
+            cudaMalloc(&amax, sizeof(float) * T) == cudaSuccess &&
+            cudaMalloc(&err, 4) == cudaSuccess;
+  glm5x_status s = GLM5X_OK;
+  if (!ok) {
+    s = fail_global(GLM5X_OUT_OF_MEMORY, "plan scratch");
+  } else {
+    b.seg_count = seg_count;
+    b.seg_start = seg_start;
+    b.pos = pos;
+    b.row_token = row_token;
+    cudaMemsetAsync(wts, 0, sizeof(float) * T * k, st);
+    cudaMemsetAsync(amax, 0, sizeof(float) * T, st);
+    cudaMemsetAsync(err, 0, 4, st);
+    launch_permute(ids, wts, amax, (int)T, k, E, 0, 256, b, err, st);
+    s = sync_error(st, err, 0, "expert-major plan");
+    err = nullptr;
+  }
+  cudaFree(b.chunk_count);
+  cudaFree(b.rank);
+  cudaFree(b.qprefix);
+  cudaFree(b.ntile_prefix);
+  cudaFree(b.seg_amax);
+  cudaFree(b.h_amax);
+  cudaFree(b.row_weight);
+  cudaFree(wts);
+  cudaFree(amax);
+  if (err) cudaFree(err);
+  return s;
+}
+
+}  // extern "C"

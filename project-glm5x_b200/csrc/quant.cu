@@ -1,0 +1,340 @@
+// quant.cu -- FP4 packing / unpacking kernels.
+//
+//  * nvfp4_quantize_matrix: the converter's NVFP4 packing of one matrix with
+//    one global scale (reference/glm5x_ref/nvfp4.py:180-198, both scale modes),
+//    writing scales straight into the 128x4 blocked layout (nvfp4.py:23-40).
+//  * nvfp4_quantize_segments: the runtime activation quantizer. Rows are
+//    gathered into expert-major segments and every segment gets its own global
+//    scale, as the reference quantizes each expert's token slab separately
+//    (reference/glm5x_ref/layer10_moe.py:729 -> nvfp4.py:236-252, max_abs).
+//  * nvfp4_dequantize / mxfp4_decode: bit-exact decoders (nvfp4.py:201-217,
+//    reference/k3x_ref/mxfp4.py:110-144, runtime/src/ops.cpp:40-63).
+//  * mxfp4_encode: encode_mxfp4 (mxfp4.py:31-107, both scale modes).
+#include <cuda_bf16.h>
+#include <cstdint>
+
+#include "fp4_codec.h"
+#include "glm5x_kernels.cuh"
+#include "glm5x_ptx.cuh"
+
+namespace glm5x {
+
+__device__ __forceinline__ float bf16_bits_to_float(uint16_t b) {
+  return __uint_as_float(static_cast<uint32_t>(b) << 16);
+}
+
+__device__ __forceinline__ void atomic_max_nonneg(float* addr, float v) {
+  // valid for v >= 0: the IEEE bit pattern of non-negative floats orders like
+  // unsigned integers
+  atomicMax(reinterpret_cast<unsigned int*>(addr), __float_as_uint(v));
+}
+
+// ------------------------------------------------------------------ amax
+// Max |x| over the whole matrix (row-major, `n` elements) into *out (which the
+// caller zeroes). Records kErrNonFinite on NaN/Inf.
+template <typename T>
+__global__ void amax_kernel(const T* __restrict__ src, int64_t n, float* out, uint32_t* err) {
+  float m = 0.0f;
+  bool bad = false;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float v;
+    if constexpr (sizeof(T) == 2)
+      v = bf16_bits_to_float(reinterpret_cast<const uint16_t*>(src)[i]);
+    else
+      v = static_cast<float>(src[i]);
+    bad |= !isfinite(v);
+    m = fmaxf(m, fabsf(v));
+  }
+  for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (bad) atomicOr(err, kErrNonFinite);
+  if (lane_id() == 0) atomic_max_nonneg(out, m);
+}
+
+// Per-row max |x| of a BF16 [rows, cols] matrix, one warp per row.
+__global__ void row_amax_bf16_kernel(const uint16_t* __restrict__ src, int64_t rows, int cols,
+                                     float* __restrict__ out, uint32_t* err) {
+  const int64_t row = blockIdx.x * (int64_t)(blockDim.x / 32) + threadIdx.x / 32;
+  if (row >= rows) return;
+  const uint4* p = reinterpret_cast<const uint4*>(src + row * cols);
+  float m = 0.0f;
+  bool bad = false;
+  for (int i = lane_id(); i < cols / 8; i += 32) {
+    const uint4 v = __ldg(p + i);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float a = __uint_as_float(w[j] << 16), b = __uint_as_float(w[j] & 0xffff0000u);
+      bad |= !isfinite(a) || !isfinite(b);
+      m = fmaxf(m, fmaxf(fabsf(a), fabsf(b)));
+    }
+  }
+  for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane_id() == 0) {
+    out[row] = m;
+    if (bad) atomicOr(err, kErrNonFinite);
+  }
+}
+
+// ------------------------------------------------------------------ NVFP4 matrix
+// One thread per 16-element block. `amax` holds max|x| over the matrix.
+template <typename T>
+__global__ void nvfp4_quantize_matrix_kernel(const T* __restrict__ src, int64_t rows, int64_t cols,
+                                             int mse, const float* __restrict__ amax,
+                                             uint8_t* __restrict__ packed,
+                                             uint8_t* __restrict__ scales_blocked,
+                                             float* __restrict__ global_out) {
+  const int64_t nb = cols / 16;
+  const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const float g = nvfp4_global_scale(*amax);
+  if (idx == 0) *global_out = g;
+  if (idx >= rows * nb) return;
+  const int64_t r = idx / nb, b = idx % nb;
+  float x[16];
+  const T* s = src + r * cols + b * 16;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    if constexpr (sizeof(T) == 2)
+      x[i] = bf16_bits_to_float(reinterpret_cast<const uint16_t*>(s)[i]);
+    else
+      x[i] = static_cast<float>(s[i]);
+  }
+  uint8_t p[8];
+  const uint32_t sb = nvfp4_quantize_block(x, g, mse != 0, p);
+  uint2 pk;
+  pk.x = p[0] | (p[1] << 8) | (p[2] << 16) | ((uint32_t)p[3] << 24);
+  pk.y = p[4] | (p[5] << 8) | (p[6] << 16) | ((uint32_t)p[7] << 24);
+  *reinterpret_cast<uint2*>(packed + r * (cols / 2) + b * 8) = pk;
+  scales_blocked[blocked_sf_offset(r, b, nb)] = static_cast<uint8_t>(sb);
+}
+
+// ------------------------------------------------------------------ NVFP4 segments
+// Expert-major activation quantization (max_abs). Flat row f in
+// [0, qprefix[nseg]) maps to segment s (qprefix is the prefix sum of each
+// segment's row count rounded up to 8) and row seg_start[s] + (f - qprefix[s])
+// of the output. Rows past count[s] are zero-filled so the MMA's N padding
+// reads zeros. Source rows are gathered by row_token (a token index into src).
+// seg_amax[s] = max |x| over the segment's gathered rows; seg_global[s] is
+// written here. One warp per row; K must be a multiple of 512.
+__global__ void nvfp4_quantize_segments_kernel(
+    const uint16_t* __restrict__ src, int K, const int32_t* __restrict__ row_token,
+    const int32_t* __restrict__ seg_start, const int32_t* __restrict__ seg_count,
+    const int32_t* __restrict__ qprefix, int nseg, const float* __restrict__ seg_amax,
+    uint8_t* __restrict__ packed, uint8_t* __restrict__ scales_blocked,
+    float* __restrict__ seg_global) {
+  const int warps = blockDim.x / 32;
+  const int64_t f = blockIdx.x * (int64_t)warps + threadIdx.x / 32;
+  const int total = qprefix[nseg];
+  if (f >= total) return;
+  // upper_bound over qprefix[0..nseg]
+  int lo = 0, hi = nseg;
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (qprefix[mid] <= f) lo = mid; else hi = mid;
+  }
+  const int s = lo;
+  const int r = static_cast<int>(f - qprefix[s]);
+  const int64_t row = seg_start[s] + r;
+  const float g = nvfp4_global_scale(seg_amax[s]);
+  if (r == 0 && lane_id() == 0) seg_global[s] = g;
+  const int nb = K / 16;
+  uint8_t* prow = packed + row * (K / 2);
+  if (r >= seg_count[s]) {
+    for (int b = lane_id(); b < nb; b += 32) {
+      *reinterpret_cast<uint2*>(prow + b * 8) = make_uint2(0, 0);
+      scales_blocked[blocked_sf_offset(row, b, nb)] = 0;
+    }
+    return;
+  }
+  const int64_t t = row_token ? row_token[row] : row;
+  const uint16_t* xrow = src + t * (int64_t)K;
+  const float six_g = f_mul(kFp4Max, g);
+  for (int b = lane_id(); b < nb; b += 32) {
+    const uint4* q = reinterpret_cast<const uint4*>(xrow + b * 16);
+    const uint4 v0 = __ldg(q), v1 = __ldg(q + 1);
+    const uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    float x[16];
+    float bmax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      x[2 * j] = __uint_as_float(w[j] << 16);
+      x[2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
+      bmax = fmaxf(bmax, fmaxf(fabsf(x[2 * j]), fabsf(x[2 * j + 1])));
+    }
+    float base = f_div(bmax, six_g);
+    base = fminf(fmaxf(base, kE4M3Tiny), kE4M3Max);
+    const uint32_t sb = e4m3_encode(base);
+    const float denom = f_mul(e4m3_decode(sb), g);
+    uint32_t lo32 = 0, hi32 = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) lo32 |= e2m1_encode(f_div(x[i], denom)) << (4 * i);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) hi32 |= e2m1_encode(f_div(x[8 + i], denom)) << (4 * i);
+    *reinterpret_cast<uint2*>(prow + b * 8) = make_uint2(lo32, hi32);
+    scales_blocked[blocked_sf_offset(row, b, nb)] = static_cast<uint8_t>(sb);
+  }
+}
+
+// ------------------------------------------------------------------ decoders
+__global__ void nvfp4_dequantize_kernel(const uint8_t* __restrict__ packed,
+                                        const uint8_t* __restrict__ scales_blocked, float g,
+                                        int64_t rows, int64_t cols, float* __restrict__ out) {
+  const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;  // one byte (2 values)
+  if (idx >= rows * cols / 2) return;
+  const int64_t r = idx / (cols / 2), c = (idx % (cols / 2)) * 2;
+  const uint8_t byte = packed[idx];
+  const float s = f_mul(e4m3_decode(scales_blocked[blocked_sf_offset(r, c / 16, cols / 16)]), g);
+  out[r * cols + c] = f_mul(e2m1_value(byte & 15u), s);
+  out[r * cols + c + 1] = f_mul(e2m1_value(byte >> 4), s);
+}
+
+__global__ void mxfp4_decode_kernel(const uint8_t* __restrict__ packed,
+                                    const uint8_t* __restrict__ scales, int64_t n, int group,
+                                    float* __restrict__ out, uint32_t* err) {
+  const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (idx >= n / 2) return;
+  const uint8_t byte = packed[idx];
+  const int64_t e0 = idx * 2;
+  const uint8_t sc = scales[e0 / group];
+  if (sc == 0xff) atomicOr(err, kErrBadScale);
+  const float s = pow2f(static_cast<int>(sc) - 127);
+  out[e0] = f_mul(e2m1_value(byte & 15u), s);
+  out[e0 + 1] = f_mul(e2m1_value(byte >> 4), s);
+}
+
+// One thread per group of `group` (<= 64) elements.
+template <typename T>
+__global__ void mxfp4_encode_kernel(const T* __restrict__ src, int64_t ngroups, int group,
+                                    int mse, uint8_t* __restrict__ packed,
+                                    uint8_t* __restrict__ scales, uint32_t* err) {
+  const int64_t gi = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (gi >= ngroups) return;
+  float x[64];
+  float m = 0.0f;
+  for (int i = 0; i < group; ++i) {
+    float v;
+    if constexpr (sizeof(T) == 2)
+      v = bf16_bits_to_float(reinterpret_cast<const uint16_t*>(src)[gi * group + i]);
+    else
+      v = static_cast<float>(src[gi * group + i]);
+    if (!isfinite(v)) atomicOr(err, kErrNonFinite);
+    x[i] = v;
+    m = fmaxf(m, fabsf(v));
+  }
+  bool overflow = false;
+  const int e = mxfp4_exponent(m, &overflow);
+  if (overflow) atomicOr(err, kErrBadScale);
+  int sel = e;
+  uint32_t codes[64];
+  if (!mse) {
+    const float sc = pow2f(e);
+    for (int i = 0; i < group; ++i) codes[i] = e2m1_encode(f_div(x[i], sc));
+  } else {
+    float best = 0.0f;
+    for (int c = 0; c < 7; ++c) {
+      int ce = e - 4 + c;
+      ce = ce < -127 ? -127 : (ce > 126 ? 126 : ce);
+      const float sc = pow2f(ce);
+      uint32_t cc[64];
+      float sum = 0.0f;
+      for (int i = 0; i < group; ++i) {
+        cc[i] = e2m1_encode(f_div(x[i], sc));
+        const float d = f_sub(f_mul(e2m1_value(cc[i]), sc), x[i]);
+        sum = f_add(sum, f_mul(d, d));
+      }
+      const float err_c = f_div(sum, static_cast<float>(group));
+      if (c == 0 || err_c < best) {
+        best = err_c;
+        sel = ce;
+        for (int i = 0; i < group; ++i) codes[i] = cc[i];
+      }
+    }
+  }
+  scales[gi] = static_cast<uint8_t>(sel + 127);
+  for (int i = 0; i < group / 2; ++i)
+    packed[gi * (group / 2) + i] = static_cast<uint8_t>(codes[2 * i] | (codes[2 * i + 1] << 4));
+}
+
+// ------------------------------------------------------------------ launchers
+cudaError_t launch_row_amax_bf16(const uint16_t* src, int64_t rows, int cols, float* out,
+                                 uint32_t* err, cudaStream_t st) {
+  if (rows == 0) return cudaSuccess;
+  const int warps = 8;
+  row_amax_bf16_kernel<<<(unsigned)((rows + warps - 1) / warps), warps * 32, 0, st>>>(
+      src, rows, cols, out, err);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_nvfp4_quantize_matrix(const T* src, int64_t rows, int64_t cols, int mse,
+                                         float* amax_scratch, uint8_t* packed,
+                                         uint8_t* scales_blocked, float* global_out,
+                                         uint32_t* err, cudaStream_t st) {
+  cudaMemsetAsync(amax_scratch, 0, sizeof(float), st);
+  const int64_t n = rows * cols;
+  const int amax_blocks = static_cast<int>(std::min<int64_t>((n + 255) / 256, 148 * 8));
+  amax_kernel<T><<<amax_blocks, 256, 0, st>>>(src, n, amax_scratch, err);
+  // padded scale entries of the blocked layout stay zero, as in _to_blocked
+  cudaMemsetAsync(scales_blocked, 0,
+                  ((rows + 127) / 128) * ((cols / 16 + 3) / 4) * 512, st);
+  const int64_t blocks = rows * (cols / 16);
+  nvfp4_quantize_matrix_kernel<T><<<(unsigned)((blocks + 127) / 128), 128, 0, st>>>(
+      src, rows, cols, mse, amax_scratch, packed, scales_blocked, global_out);
+  return cudaGetLastError();
+}
+template cudaError_t launch_nvfp4_quantize_matrix<float>(const float*, int64_t, int64_t, int,
+                                                         float*, uint8_t*, uint8_t*, float*,
+                                                         uint32_t*, cudaStream_t);
+template cudaError_t launch_nvfp4_quantize_matrix<__nv_bfloat16>(const __nv_bfloat16*, int64_t,
+                                                                 int64_t, int, float*, uint8_t*,
+                                                                 uint8_t*, float*, uint32_t*,
+                                                                 cudaStream_t);
+
+cudaError_t launch_nvfp4_quantize_segments(const uint16_t* src, int K, const int32_t* row_token,
+                                           const int32_t* seg_start, const int32_t* seg_count,
+                                           const int32_t* qprefix, int nseg,
+                                           const float* seg_amax, int64_t max_rows,
+                                           uint8_t* packed, uint8_t* scales_blocked,
+                                           float* seg_global, cudaStream_t st) {
+  if (max_rows <= 0) return cudaSuccess;
+  const int warps = 8;
+  nvfp4_quantize_segments_kernel<<<(unsigned)((max_rows + warps - 1) / warps), warps * 32, 0,
+                                   st>>>(src, K, row_token, seg_start, seg_count, qprefix, nseg,
+                                         seg_amax, packed, scales_blocked, seg_global);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_nvfp4_dequantize(const uint8_t* packed, const uint8_t* scales_blocked,
+                                    float g, int64_t rows, int64_t cols, float* out,
+                                    cudaStream_t st) {
+  const int64_t n = rows * cols / 2;
+  if (n == 0) return cudaSuccess;
+  nvfp4_dequantize_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(packed, scales_blocked,
+                                                                       g, rows, cols, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_mxfp4_decode(const uint8_t* packed, const uint8_t* scales, int64_t n,
+                                int group, float* out, uint32_t* err, cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
+  mxfp4_decode_kernel<<<(unsigned)((n / 2 + 255) / 256), 256, 0, st>>>(packed, scales, n, group,
+                                                                       out, err);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_mxfp4_encode(const T* src, int64_t n, int group, int mse, uint8_t* packed,
+                                uint8_t* scales, uint32_t* err, cudaStream_t st) {
+  const int64_t ng = n / group;
+  if (ng == 0) return cudaSuccess;
+  mxfp4_encode_kernel<T><<<(unsigned)((ng + 127) / 128), 128, 0, st>>>(src, ng, group, mse,
+                                                                       packed, scales, err);
+  return cudaGetLastError();
+}
+template cudaError_t launch_mxfp4_encode<float>(const float*, int64_t, int, int, uint8_t*,
+                                                uint8_t*, uint32_t*, cudaStream_t);
+template cudaError_t launch_mxfp4_encode<__nv_bfloat16>(const __nv_bfloat16*, int64_t, int, int,
+                                                        uint8_t*, uint8_t*, uint32_t*,
+                                                        cudaStream_t);
+
+}  // namespace glm5x

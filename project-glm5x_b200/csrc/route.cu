@@ -1,0 +1,332 @@
+// route.cu -- router top-k and the expert-major token permutation.
+//
+// Routing follows the reference's C++ natural-mode policy
+// (runtime/src/routing_policy.cpp:31-159, called from
+// runtime/src/cuda_glm5x_real_expert_bench.cpp:287-328) and the Python router
+// (reference/glm5x_ref/layer10_moe.py:760-789): score = sigmoid(logit),
+// choice = score + bias, top-k by choice with ties to the lower expert index
+// (std::stable_sort order), weight = score / sum(selected scores, summed in
+// slot order) * routed_scaling.
+//
+// The permutation replaces build_expert_major_plan / packed plan
+// (runtime/src/expert_major.cpp:12-98) with a device counting sort: segments
+// in ascending expert order, each segment's tokens in ascending token order,
+// every segment starting on a 128-row boundary (one 128-row block of the
+// block-scaled operand never spans two experts). The shared expert is segment
+// `num_experts` holding every token in order.
+#include <cstdint>
+
+#include "fp4_codec.h"
+#include "glm5x_kernels.cuh"
+#include "glm5x_ptx.cuh"
+
+namespace glm5x {
+
+// ------------------------------------------------------------------ logits
+// FP32 router logits [T, E] = x[T, H] . W[E, H]^T from BF16 inputs.
+// 64-token x 64-expert tile per block, 256 threads, 4x4 outputs per thread.
+__global__ void __launch_bounds__(256) router_logits_simt_kernel(
+    const uint16_t* __restrict__ x, const uint16_t* __restrict__ w, int T, int H, int E,
+    float* __restrict__ logits) {
+  __shared__ float xs[32][64 + 1];
+  __shared__ float ws[32][64 + 1];
+  const int t0 = blockIdx.x * 64, e0 = blockIdx.y * 64;
+  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < H; k0 += 32) {
+    for (int i = threadIdx.x; i < 64 * 32; i += 256) {
+      const int r = i / 32, c = i % 32;
+      const int t = t0 + r, e = e0 + r;
+      xs[c][r] = t < T ? __uint_as_float((uint32_t)x[(int64_t)t * H + k0 + c] << 16) : 0.0f;
+      ws[c][r] = e < E ? __uint_as_float((uint32_t)w[(int64_t)e * H + k0 + c] << 16) : 0.0f;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int c = 0; c < 32; ++c) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = xs[c][ty * 4 + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = ws[c][tx * 4 + j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int t = t0 + ty * 4 + i, e = e0 + tx * 4 + j;
+      if (t < T && e < E) logits[(int64_t)t * E + e] = acc[i][j];
+    }
+}
+
+// ------------------------------------------------------------------ top-k
+// One warp per token. Lane l owns experts l, l+32, ... (E <= 32 * 16).
+// `values_are_scores` = 1 means `in` already holds sigmoid scores (the
+// select_routing parity entry point), else logits.
+__global__ void topk_kernel(const float* __restrict__ in, int values_are_scores,
+                            const float* __restrict__ bias, int T, int E, int k,
+                            float routed_scale, int32_t* __restrict__ ids,
+                            float* __restrict__ weights, uint32_t* err) {
+  const int warps = blockDim.x / 32;
+  const int t = blockIdx.x * warps + threadIdx.x / 32;
+  if (t >= T) return;
+  const int lane = lane_id();
+  constexpr int kMaxPer = 16;
+  float score[kMaxPer], choice[kMaxPer];
+  const int per = (E + 31) / 32;
+  bool bad = false;
+#pragma unroll
+  for (int j = 0; j < kMaxPer; ++j) {
+    const int e = lane + 32 * j;
+    if (j < per && e < E) {
+      const float v = in[(int64_t)t * E + e];
+      float s;
+      if (values_are_scores) {
+        s = v;
+        bad |= !(s >= 0.0f && s <= 1.0f);
+      } else {
+        s = f_div(1.0f, f_add(1.0f, expf(-v)));
+      }
+      score[j] = s;
+      choice[j] = f_add(s, bias[e]);
+      bad |= !isfinite(choice[j]);
+    } else {
+      score[j] = 0.0f;
+      choice[j] = -INFINITY;
+    }
+  }
+  if (bad) atomicOr(err, kErrNonFinite);
+  uint32_t taken = 0;
+  float denom = 0.0f;
+  float sel_score[16];
+  int sel_id[16];
+  for (int s = 0; s < k; ++s) {
+    // local best: max choice, lowest expert id on ties
+    float best = -INFINITY;
+    int best_e = 0x7fffffff;
+#pragma unroll
+    for (int j = 0; j < kMaxPer; ++j) {
+      const int e = lane + 32 * j;
+      if (j < per && e < E && !((taken >> j) & 1u)) {
+        if (choice[j] > best || (choice[j] == best && e < best_e)) {
+          best = choice[j];
+          best_e = e;
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oe = __shfl_xor_sync(0xffffffffu, best_e, o);
+      if (ob > best || (ob == best && oe < best_e)) {
+        best = ob;
+        best_e = oe;
+      }
+    }
+    const int owner = best_e % 32, slot = best_e / 32;
+    float sc = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kMaxPer; ++j)
+      if (lane == owner && j == slot) {
+        taken |= 1u << j;
+        sc = score[j];
+      }
+    sc = __shfl_sync(0xffffffffu, sc, owner);
+    sel_score[s] = sc;
+    sel_id[s] = best_e;
+    denom = f_add(denom, sc);
+  }
+  if (lane == 0) {
+    for (int s = 0; s < k; ++s) {
+      ids[(int64_t)t * k + s] = sel_id[s];
+      weights[(int64_t)t * k + s] = f_mul(f_div(sel_score[s], denom), routed_scale);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ permutation
+constexpr int kChunk = 256;  // tokens per counting chunk
+
+// Per 256-token chunk: per-expert counts and each (token, slot)'s rank among
+// the chunk's tokens routed to the same expert (stable). E <= 256.
+__global__ void __launch_bounds__(kChunk) permute_count_kernel(
+    const int32_t* __restrict__ ids, int T, int k, int E, int32_t* __restrict__ chunk_count,
+    int32_t* __restrict__ rank, uint32_t* err) {
+  __shared__ uint32_t bits[256][kChunk / 32];
+  const int c = blockIdx.x;
+  for (int i = threadIdx.x; i < 256 * (kChunk / 32); i += blockDim.x) (&bits[0][0])[i] = 0;
+  __syncthreads();
+  const int t = c * kChunk + threadIdx.x;
+  const int word = threadIdx.x / 32, bit = threadIdx.x % 32;
+  int my[16];
+  if (t < T) {
+    for (int s = 0; s < k; ++s) {
+      int e = ids[(int64_t)t * k + s];
+      if (e < 0 || e >= E) {
+        atomicOr(err, kErrBounds);
+        e = 0;
+      }
+      my[s] = e;
+      const uint32_t prev = atomicOr(&bits[e][word], 1u << bit);
+      if (prev & (1u << bit)) atomicOr(err, kErrBounds);  // duplicate expert in one token
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < E) {
+    int n = 0;
+    for (int w = 0; w < kChunk / 32; ++w) n += __popc(bits[threadIdx.x][w]);
+    chunk_count[(int64_t)c * E + threadIdx.x] = n;
+  }
+  if (t < T) {
+    for (int s = 0; s < k; ++s) {
+      const int e = my[s];
+      int r = __popc(bits[e][word] & ((1u << bit) - 1u));
+      for (int w = 0; w < word; ++w) r += __popc(bits[e][w]);
+      rank[(int64_t)t * k + s] = r;
+    }
+  }
+}
+
+// Block-wide exclusive scan over n <= blockDim.x values (Hillis-Steele).
+__device__ int block_exclusive_scan(int v, int* buf, int* total) {
+  const int i = threadIdx.x;
+  buf[i] = v;
+  __syncthreads();
+  for (int off = 1; off < (int)blockDim.x; off <<= 1) {
+    const int add = i >= off ? buf[i - off] : 0;
+    __syncthreads();
+    buf[i] += add;
+    __syncthreads();
+  }
+  const int incl = buf[i];
+  if (total) *total = buf[blockDim.x - 1];
+  __syncthreads();
+  return incl - v;
+}
+
+// Single block, blockDim >= nseg = E + has_shared (<= 1024). Turns chunk
+// counts into per-chunk bases, builds segment starts (128-aligned), the
+// quantizer row prefix (counts rounded up to 8) and the GEMM N-tile prefix,
+// and clears the per-segment amax accumulators.
+__global__ void permute_scan_kernel(int32_t* __restrict__ chunk_count, int nchunks, int T, int E,
+                                    int has_shared, int bn, int32_t* __restrict__ seg_count,
+                                    int32_t* __restrict__ seg_start,
+                                    int32_t* __restrict__ qprefix,
+                                    int32_t* __restrict__ ntile_prefix,
+                                    float* __restrict__ seg_amax, float* __restrict__ h_amax) {
+  extern __shared__ int scan_buf[];
+  const int e = threadIdx.x;
+  const int nseg = E + has_shared;
+  int count = 0;
+  if (e < E) {
+    for (int c = 0; c < nchunks; ++c) {
+      const int v = chunk_count[(int64_t)c * E + e];
+      chunk_count[(int64_t)c * E + e] = count;
+      count += v;
+    }
+  } else if (e == E && has_shared) {
+    count = T;
+  }
+  const bool valid = e < nseg;
+  int tot;
+  const int start = block_exclusive_scan(valid ? (count + 127) / 128 * 128 : 0, scan_buf, &tot);
+  const int q = block_exclusive_scan(valid ? (count + 7) / 8 * 8 : 0, scan_buf, &tot);
+  const int qt = tot;
+  // N tiles: 128-row aligned chunks of at most bn rows
+  const int nt = valid ? (count + bn - 1) / bn : 0;
+  const int tp = block_exclusive_scan(nt, scan_buf, &tot);
+  if (valid) {
+    seg_count[e] = count;
+    seg_start[e] = start;
+    qprefix[e] = q;
+    ntile_prefix[e] = tp;
+    seg_amax[e] = 0.0f;
+    h_amax[e] = 0.0f;
+  }
+  if (e == 0) {
+    qprefix[nseg] = qt;
+    ntile_prefix[nseg] = tot;
+  }
+  __syncthreads();
+  if (e == nseg - 1) seg_start[nseg] = start + (count + 127) / 128 * 128;
+}
+
+// One thread per (token, slot) pair, plus one per token for the shared expert.
+__global__ void permute_scatter_kernel(const int32_t* __restrict__ ids,
+                                       const float* __restrict__ weights, int T, int k, int E,
+                                       int has_shared, const int32_t* __restrict__ chunk_base,
+                                       const int32_t* __restrict__ rank,
+                                       const int32_t* __restrict__ seg_start,
+                                       const float* __restrict__ token_amax,
+                                       int32_t* __restrict__ pos, int32_t* __restrict__ row_token,
+                                       float* __restrict__ row_weight,
+                                       float* __restrict__ seg_amax) {
+  const int kk = k + has_shared;
+  const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)T * kk) return;
+  const int t = static_cast<int>(idx / kk), s = static_cast<int>(idx % kk);
+  int p, e;
+  float w;
+  if (s < k) {
+    e = ids[(int64_t)t * k + s];
+    e = e < 0 || e >= E ? 0 : e;
+    p = seg_start[e] + chunk_base[(int64_t)(t / kChunk) * E + e] + rank[(int64_t)t * k + s];
+    w = weights[(int64_t)t * k + s];
+  } else {
+    e = E;
+    p = seg_start[E] + t;
+    w = 1.0f;
+  }
+  pos[idx] = p;
+  row_token[p] = t;
+  row_weight[p] = w;
+  atomicMax(reinterpret_cast<unsigned int*>(seg_amax + e), __float_as_uint(token_amax[t]));
+}
+
+// ------------------------------------------------------------------ launchers
+cudaError_t launch_router_logits_simt(const uint16_t* x, const uint16_t* w, int T, int H, int E,
+                                      float* logits, cudaStream_t st) {
+  if (T == 0) return cudaSuccess;
+  dim3 grid((T + 63) / 64, (E + 63) / 64);
+  router_logits_simt_kernel<<<grid, 256, 0, st>>>(x, w, T, H, E, logits);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_topk(const float* in, int values_are_scores, const float* bias, int T, int E,
+                        int k, float routed_scale, int32_t* ids, float* weights, uint32_t* err,
+                        cudaStream_t st) {
+  if (T == 0) return cudaSuccess;
+  const int warps = 8;
+  topk_kernel<<<(T + warps - 1) / warps, warps * 32, 0, st>>>(in, values_are_scores, bias, T, E,
+                                                               k, routed_scale, ids, weights, err);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_permute(const int32_t* ids, const float* weights, const float* token_amax,
+                           int T, int k, int E, int has_shared, int bn, PermuteBuffers b,
+                           uint32_t* err, cudaStream_t st) {
+  const int nchunks = (T + kChunk - 1) / kChunk;
+  if (T > 0) {
+    permute_count_kernel<<<nchunks, kChunk, 0, st>>>(ids, T, k, E, b.chunk_count, b.rank, err);
+  }
+  const int nseg = E + has_shared;
+  int threads = 32;
+  while (threads < nseg + 1) threads <<= 1;
+  permute_scan_kernel<<<1, threads, threads * sizeof(int), st>>>(
+      b.chunk_count, nchunks, T, E, has_shared, bn, b.seg_count, b.seg_start, b.qprefix,
+      b.ntile_prefix, b.seg_amax, b.h_amax);
+  const int64_t n = (int64_t)T * (k + has_shared);
+  if (n > 0) {
+    permute_scatter_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(
+        ids, weights, T, k, E, has_shared, b.chunk_count, b.rank, b.seg_start, token_amax, b.pos,
+        b.row_token, b.row_weight, b.seg_amax);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace glm5x

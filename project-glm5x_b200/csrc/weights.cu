@@ -1,0 +1,113 @@
+// weights.cu -- admission-time weight layout kernels and the combine kernel.
+//
+// Weight admission keeps the reference's NVFP4 sidecar layout (packed
+// [rows, K/2], low nibble first, scales in the 128x4 blocked layout of
+// reference/glm5x_ref/nvfp4.py:23-40 as stored by packed_cache.py:277-309);
+// the only change is the gate/up interleave that lets one 128-row MMA tile
+// hold 64 gate rows and the 64 matching up rows. MXFP4 row-major E8M0 scales
+// (reference/k3x_ref/mxfp4.py:98-101) are reordered into the same blocked
+// layout.
+//
+// combine replaces the reference's weighted scatter (index_add_,
+// reference/glm5x_ref/layer10_moe.py:843-846; ragged_expert_mix_kernel,
+// runtime/cuda/moe_layer.cu:25-44; shared add moe_layer.cu:64-70): every
+// token gathers its k routed rows plus its shared-expert row (already
+// weighted in the down-projection epilogue) in FP32.
+#include <cstdint>
+
+#include "fp4_codec.h"
+#include "glm5x_kernels.cuh"
+
+namespace glm5x {
+
+// Interleaved row R of the stacked gate/up matrix: group q = R / 32, rows
+// 0-15 of the group are gate rows 16q..16q+15 and rows 16-31 the same up rows.
+__device__ __forceinline__ void interleave_source(int R, int* which, int* j) {
+  *which = (R & 16) ? 1 : 0;
+  *j = (R >> 5) * 16 + (R & 15);
+}
+
+__global__ void interleave_rows_kernel(const uint8_t* __restrict__ gate,
+                                       const uint8_t* __restrict__ up, int I, int row_bytes,
+                                       uint8_t* __restrict__ dst) {
+  const int R = blockIdx.x;
+  int which, j;
+  interleave_source(R, &which, &j);
+  const uint4* s = reinterpret_cast<const uint4*>((which ? up : gate) + (size_t)j * row_bytes);
+  uint4* d = reinterpret_cast<uint4*>(dst + (size_t)R * row_bytes);
+  for (int i = threadIdx.x; i < row_bytes / 16; i += blockDim.x) d[i] = s[i];
+}
+
+__global__ void interleave_scales_kernel(const uint8_t* __restrict__ gate_sf,
+                                         const uint8_t* __restrict__ up_sf, int I, int sf_cols,
+                                         uint8_t* __restrict__ dst_sf) {
+  const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)2 * I * sf_cols) return;
+  const int R = static_cast<int>(idx / sf_cols), c = static_cast<int>(idx % sf_cols);
+  int which, j;
+  interleave_source(R, &which, &j);
+  dst_sf[blocked_sf_offset(R, c, sf_cols)] =
+      (which ? up_sf : gate_sf)[blocked_sf_offset(j, c, sf_cols)];
+}
+
+__global__ void scales_to_blocked_kernel(const uint8_t* __restrict__ rm, int64_t rows,
+                                         int64_t sf_cols, uint8_t* __restrict__ blocked) {
+  const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (idx >= rows * sf_cols) return;
+  const int64_t r = idx / sf_cols, c = idx % sf_cols;
+  blocked[blocked_sf_offset(r, c, sf_cols)] = rm[idx];
+}
+
+// One block per token; 8 BF16 (16 bytes) per vector.
+__global__ void combine_kernel(const uint16_t* __restrict__ y, const int32_t* __restrict__ pos,
+                               int kk, int H, float* __restrict__ out) {
+  const int t = blockIdx.x;
+  __shared__ int32_t rows[32];
+  if (threadIdx.x < kk) rows[threadIdx.x] = pos[(int64_t)t * kk + threadIdx.x];
+  __syncthreads();
+  for (int v = threadIdx.x; v < H / 8; v += blockDim.x) {
+    float acc[8] = {};
+    for (int s = 0; s < kk; ++s) {
+      const uint4 q = __ldg(reinterpret_cast<const uint4*>(y + (int64_t)rows[s] * H) + v);
+      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        acc[2 * i] += __uint_as_float(w[i] << 16);
+        acc[2 * i + 1] += __uint_as_float(w[i] & 0xffff0000u);
+      }
+    }
+    float4* o = reinterpret_cast<float4*>(out + (int64_t)t * H) + 2 * v;
+    o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+  }
+}
+
+cudaError_t launch_interleave_gate_up(const uint8_t* gate_packed, const uint8_t* gate_sf,
+                                      const uint8_t* up_packed, const uint8_t* up_sf, int I,
+                                      int K, int group, uint8_t* dst_packed, uint8_t* dst_sf,
+                                      cudaStream_t st) {
+  interleave_rows_kernel<<<2 * I, 128, 0, st>>>(gate_packed, up_packed, I, K / 2, dst_packed);
+  const int sf_cols = K / group;
+  const int64_t n = (int64_t)2 * I * sf_cols;
+  interleave_scales_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(gate_sf, up_sf, I,
+                                                                        sf_cols, dst_sf);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_scales_to_blocked(const uint8_t* rm, int64_t rows, int64_t sf_cols,
+                                     uint8_t* blocked, cudaStream_t st) {
+  const int64_t n = rows * sf_cols;
+  if (n == 0) return cudaSuccess;
+  scales_to_blocked_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(rm, rows, sf_cols,
+                                                                        blocked);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_combine(const uint16_t* y, const int32_t* pos, int T, int kk, int H,
+                           float* out, cudaStream_t st) {
+  if (T == 0) return cudaSuccess;
+  combine_kernel<<<T, 256, 0, st>>>(y, pos, kk, H, out);
+  return cudaGetLastError();
+}
+
+}  // namespace glm5x

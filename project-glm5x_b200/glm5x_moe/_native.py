@@ -1,0 +1,141 @@
+"""ctypes binding of libglm5x_moe.so (the C ABI declared in include/glm5x_moe.h).
+
+The library is required: importing this module raises if it is missing or
+lacks a symbol, so no caller can silently fall back to another code path.
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libglm5x_moe.so"
+
+STATUS_NAMES = {
+    0: "OK", 1: "IO_ERROR", 2: "BAD_MAGIC", 3: "UNSUPPORTED_VERSION", 7: "TRUNCATED_FILE",
+    9: "INVALID_EXTENT", 10: "DATA_CRC_MISMATCH", 11: "AUXILIARY_CRC_MISMATCH",
+    14: "TENSOR_NOT_FOUND", 15: "INVALID_MXFP4", 16: "INVALID_STATE",
+    17: "BACKEND_UNAVAILABLE", 19: "UNSUPPORTED_ARCHITECTURE", 100: "DEVICE_ERROR",
+    101: "OUT_OF_MEMORY", 102: "WAIT_TIMEOUT",
+}
+
+NUM_PHASES = 9
+PHASE_NAMES = ["row_amax", "router_logits", "topk", "permute", "act_quantize", "gate_up_gemm",
+               "h_quantize", "down_gemm", "combine"]
+
+PRECISION_NVFP4 = 0
+PRECISION_MXFP4 = 1
+SCALE_MAX_ABS = 0
+SCALE_MSE = 1
+
+
+class Glm5xError(RuntimeError):
+    """A non-OK glm5x_status; `.code` is the numeric status, `.name` its name."""
+
+    def __init__(self, code: int, message: str) -> None:
+        self.code = int(code)
+        self.name = STATUS_NAMES.get(self.code, f"STATUS_{self.code}")
+        super().__init__(f"{self.name}: {message}")
+
+
+class MoeConfig(ctypes.Structure):
+    _fields_ = [
+        ("hidden", ctypes.c_int32), ("intermediate", ctypes.c_int32),
+        ("num_experts", ctypes.c_int32), ("top_k", ctypes.c_int32),
+        ("has_shared", ctypes.c_int32), ("routed_scaling", ctypes.c_float),
+        ("precision", ctypes.c_int32), ("max_tokens", ctypes.c_int32),
+        ("expert_begin", ctypes.c_int32), ("expert_count", ctypes.c_int32),
+    ]
+
+
+class Nvfp4Matrix(ctypes.Structure):
+    _fields_ = [
+        ("packed", ctypes.c_void_p), ("scales", ctypes.c_void_p),
+        ("global_scale", ctypes.c_float), ("rows", ctypes.c_int64), ("cols", ctypes.c_int64),
+    ]
+
+
+class Mxfp4Matrix(ctypes.Structure):
+    _fields_ = [
+        ("packed", ctypes.c_void_p), ("scales", ctypes.c_void_p),
+        ("rows", ctypes.c_int64), ("cols", ctypes.c_int64), ("group_size", ctypes.c_int64),
+    ]
+
+
+class MoeStats(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_uint64) for n in (
+        "forward_calls", "kernel_launches", "resident_weight_bytes", "activation_h2d_bytes",
+        "device_to_host_bytes", "stream_synchronization_count", "workspace_bytes",
+        "loaded_experts")]
+
+
+_P = ctypes.c_void_p
+_I32 = ctypes.c_int32
+_I64 = ctypes.c_int64
+_F = ctypes.c_float
+
+# name -> argtypes (every function returns glm5x_status unless listed in _RESTYPE)
+SIGNATURES = {
+    "glm5x_moe_create": [ctypes.POINTER(MoeConfig), ctypes.c_int, ctypes.POINTER(_P)],
+    "glm5x_moe_destroy": [_P],
+    "glm5x_moe_error_message": [_P],
+    "glm5x_last_error_message": [],
+    "glm5x_moe_set_router": [_P, _P, _P],
+    "glm5x_moe_load_expert_nvfp4": [_P, _I32, ctypes.POINTER(Nvfp4Matrix),
+                                    ctypes.POINTER(Nvfp4Matrix), ctypes.POINTER(Nvfp4Matrix)],
+    "glm5x_moe_load_expert_nvfp4_device": [_P, _I32, ctypes.POINTER(Nvfp4Matrix),
+                                           ctypes.POINTER(Nvfp4Matrix),
+                                           ctypes.POINTER(Nvfp4Matrix)],
+    "glm5x_moe_load_expert_mxfp4": [_P, _I32, ctypes.POINTER(Mxfp4Matrix),
+                                    ctypes.POINTER(Mxfp4Matrix), ctypes.POINTER(Mxfp4Matrix)],
+    "glm5x_moe_load_sidecar": [_P, _I32, ctypes.c_char_p],
+    "glm5x_moe_forward": [_P, _P, _I64, _P, _P],
+    "glm5x_moe_forward_host": [_P, _P, _I64, _P],
+    "glm5x_moe_forward_routed": [_P, _P, _I64, _P, _P, _P, _P],
+    "glm5x_moe_last_routing": [_P, _P, _P, _P, _I64],
+    "glm5x_moe_check": [_P],
+    "glm5x_moe_get_stats": [_P, ctypes.POINTER(MoeStats)],
+    "glm5x_moe_debug_buffer": [_P, _I32, ctypes.POINTER(_P), ctypes.POINTER(ctypes.c_size_t)],
+    "glm5x_moe_debug_copy": [_P, _I32, _P, ctypes.c_size_t],
+    "glm5x_moe_set_profiling": [_P, _I32],
+    "glm5x_moe_phase_times": [_P, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(_I32)],
+    "glm5x_moe_get_stream": [_P, ctypes.POINTER(_P)],
+    "glm5x_nvfp4_quantize_f32": [_P, _I64, _I64, _I32, _P, _P, _P, _P],
+    "glm5x_nvfp4_quantize_bf16": [_P, _I64, _I64, _I32, _P, _P, _P, _P],
+    "glm5x_nvfp4_quantize_slabs_bf16": [_P, _I64, _P, _P, _P, _I32, _I64, _P, _P, _P, _P],
+    "glm5x_nvfp4_dequantize": [_P, _P, _F, _I64, _I64, _P, _P],
+    "glm5x_mxfp4_encode_f32": [_P, _I64, _I64, _I64, _I32, _P, _P, _P],
+    "glm5x_mxfp4_decode": [_P, _P, _I64, _I64, _I64, _P, _P],
+    "glm5x_select_routing": [_P, _P, _I64, _I32, _I32, _F, _P, _P, _P],
+    "glm5x_expert_major_plan": [_P, _I64, _I32, _I32, _P, _P, _P, _P, _P],
+}
+_RESTYPE = {
+    "glm5x_moe_destroy": None,
+    "glm5x_moe_error_message": ctypes.c_char_p,
+    "glm5x_last_error_message": ctypes.c_char_p,
+}
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """Load libglm5x_moe.so once; raise if it is absent or incomplete."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise ImportError(
+                f"{LIB_PATH} is missing: build it with `python -m glm5x_moe.build` "
+                "(there is no fallback implementation)")
+        handle = ctypes.CDLL(str(LIB_PATH))
+        for name, args in SIGNATURES.items():
+            fn = getattr(handle, name)  # AttributeError if the symbol is missing
+            fn.argtypes = args
+            fn.restype = _RESTYPE.get(name, ctypes.c_int)
+        _lib = handle
+    return _lib
+
+
+def check(status: int, engine=None) -> None:
+    if status != 0:
+        L = lib()
+        msg = (L.glm5x_moe_error_message(engine) if engine else L.glm5x_last_error_message())
+        raise Glm5xError(status, (msg or b"").decode(errors="replace"))

@@ -1,0 +1,197 @@
+"""The MoE sublayer engine, mirroring the reference's layer interface.
+
+``GLM5XMoELayer`` takes the arguments of ``GLM5XLayer10MoEReference``
+(reference/glm5x_ref/layer10_moe.py:349-374) that matter for the routed-expert
+path (router weight, correction bias, top_k, routed_scaling_factor, a shared
+expert, NVFP4 experts) and returns a ``GLM5XMoEForward``-shaped result
+(output, router_logits, topk_indices, topk_weights). All work runs in
+libglm5x_moe.so on one CUDA device.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import Mapping
+
+import torch
+
+from . import _native as N
+from .nvfp4 import GLM5XNVFP4Weight
+
+
+@dataclass(frozen=True)
+class GLM5XMoEForward:
+    """(reference/glm5x_ref/layer10_moe.py:93-101, minus loaded_experts)"""
+
+    output: torch.Tensor
+    router_logits: torch.Tensor | None
+    topk_indices: torch.Tensor | None
+    topk_weights: torch.Tensor | None
+
+
+@dataclass(frozen=True)
+class NVFP4Expert:
+    """gate/up [I, H] and down [H, I] NVFP4 projections of one expert."""
+
+    gate_proj: GLM5XNVFP4Weight
+    up_proj: GLM5XNVFP4Weight
+    down_proj: GLM5XNVFP4Weight
+
+
+def _stream() -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+class GLM5XMoELayer:
+    """Routed-expert MoE sublayer on a B200 (sm_100) through the C ABI."""
+
+    def __init__(self, *, hidden_size: int = 6144, intermediate_size: int = 2048,
+                 num_experts: int = 256, top_k: int = 8, routed_scaling_factor: float = 2.5,
+                 has_shared: bool = True, max_tokens: int = 8192, device: int = 0,
+                 precision: str = "nvfp4", expert_begin: int = 0,
+                 expert_count: int | None = None) -> None:
+        if precision not in {"nvfp4", "mxfp4"}:
+            raise ValueError("GLM5X_INVALID_EXPERT_PRECISION")
+        if not isinstance(top_k, int) or not 0 < top_k <= num_experts:
+            raise ValueError("GLM5X_INVALID_TOP_K")
+        if routed_scaling_factor <= 0:
+            raise ValueError("GLM5X_INVALID_ROUTED_SCALE")
+        cfg = N.MoeConfig(hidden_size, intermediate_size, num_experts, top_k,
+                          1 if has_shared else 0, float(routed_scaling_factor),
+                          N.PRECISION_NVFP4 if precision == "nvfp4" else N.PRECISION_MXFP4,
+                          max_tokens, expert_begin,
+                          expert_count if expert_count is not None else num_experts)
+        handle = ctypes.c_void_p()
+        N.check(N.lib().glm5x_moe_create(ctypes.byref(cfg), device, ctypes.byref(handle)))
+        self._h = handle
+        self.device = torch.device("cuda", device)
+        self.hidden_size = hidden_size
+        self.intermediate_size = intermediate_size
+        self.num_experts = num_experts
+        self.top_k = top_k
+        self.has_shared = has_shared
+        self.max_tokens = max_tokens
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            N.lib().glm5x_moe_destroy(self._h)
+            self._h = None
+
+    def __del__(self) -> None:  # pragma: no cover - interpreter shutdown order
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ------------------------------------------------------------ weights
+    def set_router(self, router_weight: torch.Tensor, correction_bias: torch.Tensor) -> None:
+        w = router_weight.detach().to(device="cpu", dtype=torch.bfloat16).contiguous()
+        b = correction_bias.detach().to(device="cpu", dtype=torch.float32).contiguous()
+        if tuple(w.shape) != (self.num_experts, self.hidden_size):
+            raise ValueError("GLM5X_ROUTER_WEIGHT_SHAPE")
+        if tuple(b.shape) != (self.num_experts,):
+            raise ValueError("GLM5X_ROUTER_BIAS_SHAPE")
+        N.check(N.lib().glm5x_moe_set_router(self._h, w.data_ptr(), b.data_ptr()), self._h)
+
+    def load_expert(self, expert_id: int, expert: NVFP4Expert) -> None:
+        """Admit one NVFP4 expert held in device tensors (expert_id -1 = shared)."""
+        g, u, d = expert.gate_proj.matrix(), expert.up_proj.matrix(), expert.down_proj.matrix()
+        with torch.cuda.device(self.device):
+            torch.cuda.current_stream().synchronize()
+            N.check(N.lib().glm5x_moe_load_expert_nvfp4_device(
+                self._h, expert_id, ctypes.byref(g), ctypes.byref(u), ctypes.byref(d)), self._h)
+
+    def load_sidecar(self, expert_id: int, path: str) -> None:
+        N.check(N.lib().glm5x_moe_load_sidecar(self._h, expert_id, str(path).encode()), self._h)
+
+    # ------------------------------------------------------------ forward
+    def __call__(self, hidden_states: torch.Tensor, *, want_routing: bool = True
+                 ) -> GLM5XMoEForward:
+        if hidden_states.ndim < 2 or hidden_states.shape[-1] != self.hidden_size:
+            raise ValueError("GLM5X_MOE_HIDDEN_SHAPE")
+        shape = hidden_states.shape
+        flat = hidden_states.reshape(-1, self.hidden_size).to(torch.bfloat16).contiguous()
+        if flat.device != self.device:
+            raise ValueError("GLM5X_MOE_DEVICE_MISMATCH")
+        T = flat.shape[0]
+        out = torch.empty((T, self.hidden_size), dtype=torch.float32, device=self.device)
+        with torch.cuda.device(self.device):
+            N.check(N.lib().glm5x_moe_forward(self._h, flat.data_ptr(), T, out.data_ptr(),
+                                              _stream()), self._h)
+            if not want_routing:
+                return GLM5XMoEForward(out.reshape(shape), None, None, None)
+            torch.cuda.current_stream().synchronize()
+            ids = torch.empty((T, self.top_k), dtype=torch.int32)
+            w = torch.empty((T, self.top_k), dtype=torch.float32)
+            logits = torch.empty((T, self.num_experts), dtype=torch.float32)
+            N.check(N.lib().glm5x_moe_last_routing(self._h, ids.data_ptr(), w.data_ptr(),
+                                                   logits.data_ptr(), T), self._h)
+            N.check(N.lib().glm5x_moe_check(self._h), self._h)
+        return GLM5XMoEForward(
+            output=out.reshape(shape),
+            router_logits=logits.reshape(*shape[:-1], self.num_experts),
+            topk_indices=ids.reshape(*shape[:-1], self.top_k),
+            topk_weights=w.reshape(*shape[:-1], self.top_k))
+
+    def forward_routed(self, hidden: torch.Tensor, ids: torch.Tensor,
+                       weights: torch.Tensor) -> torch.Tensor:
+        """Expert path with caller-supplied routing (ids [T,k] int32,
+        weights [T,k] fp32, device tensors)."""
+        flat = hidden.reshape(-1, self.hidden_size).to(torch.bfloat16).contiguous()
+        T = flat.shape[0]
+        ids = ids.to(device=self.device, dtype=torch.int32).contiguous()
+        weights = weights.to(device=self.device, dtype=torch.float32).contiguous()
+        if tuple(ids.shape) != (T, self.top_k) or tuple(weights.shape) != (T, self.top_k):
+            raise ValueError("GLM5X_ROUTING_SHAPE")
+        out = torch.empty((T, self.hidden_size), dtype=torch.float32, device=self.device)
+        with torch.cuda.device(self.device):
+            N.check(N.lib().glm5x_moe_forward_routed(self._h, flat.data_ptr(), T, ids.data_ptr(),
+                                                     weights.data_ptr(), out.data_ptr(),
+                                                     _stream()), self._h)
+        return out
+
+    def forward_host(self, hidden_bf16_host: torch.Tensor, out_host: torch.Tensor) -> None:
+        """Host buffers in/out: H2D copy, forward, D2H copy, synchronize."""
+        T = hidden_bf16_host.shape[0]
+        N.check(N.lib().glm5x_moe_forward_host(self._h, hidden_bf16_host.data_ptr(), T,
+                                               out_host.data_ptr()), self._h)
+
+    def check(self) -> None:
+        N.check(N.lib().glm5x_moe_check(self._h), self._h)
+
+    def debug_buffer(self, which: int) -> tuple[int, int]:
+        ptr = ctypes.c_void_p()
+        size = ctypes.c_size_t()
+        N.check(N.lib().glm5x_moe_debug_buffer(self._h, which, ctypes.byref(ptr),
+                                               ctypes.byref(size)), self._h)
+        return int(ptr.value or 0), int(size.value)
+
+    def debug_tensor(self, which: int, dtype: torch.dtype, count: int) -> torch.Tensor:
+        """Copy the first `count` elements of an internal device buffer."""
+        esz = torch.tensor([], dtype=dtype).element_size()
+        out = torch.empty(count, dtype=dtype, device=self.device)
+        with torch.cuda.device(self.device):
+            torch.cuda.current_stream().synchronize()
+            N.check(N.lib().glm5x_moe_debug_copy(self._h, which, out.data_ptr(), count * esz),
+                    self._h)
+        return out
+
+    def set_profiling(self, enable: bool) -> None:
+        N.check(N.lib().glm5x_moe_set_profiling(self._h, 1 if enable else 0), self._h)
+
+    def phase_times(self) -> tuple[dict, int]:
+        """(milliseconds per phase accumulated since the last call, forwards)."""
+        ms = (ctypes.c_float * N.NUM_PHASES)()
+        n = ctypes.c_int32()
+        N.check(N.lib().glm5x_moe_phase_times(self._h, ms, ctypes.byref(n)), self._h)
+        return {name: float(ms[i]) for i, name in enumerate(N.PHASE_NAMES)}, int(n.value)
+
+    def stream_handle(self) -> int:
+        s = ctypes.c_void_p()
+        N.check(N.lib().glm5x_moe_get_stream(self._h, ctypes.byref(s)), self._h)
+        return int(s.value or 0)
+
+    def stats(self) -> Mapping[str, int]:
+        s = N.MoeStats()
+        N.check(N.lib().glm5x_moe_get_stats(self._h, ctypes.byref(s)), self._h)
+        return {name: int(getattr(s, name)) for name, _ in N.MoeStats._fields_}
