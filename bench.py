@@ -131,16 +131,16 @@ def make_hidden(T: int, seed: int, device):
     return h.to(torch.bfloat16).to(device)
 
 
-def build_layer(T: int, device_index: int, seed: int = 0):
+def build_layer(T: int, device_index: int, seed: int = 0, experts: int = E):
     import torch
     from glm5x_moe.layer import GLM5XMoELayer, NVFP4Expert
     from glm5x_moe.nvfp4 import quantize_nvfp4_weight
     dev = torch.device("cuda", device_index)
-    layer = GLM5XMoELayer(hidden_size=H, intermediate_size=I, num_experts=E, top_k=K_TOP,
+    layer = GLM5XMoELayer(hidden_size=H, intermediate_size=I, num_experts=experts, top_k=K_TOP,
                           routed_scaling_factor=SCALE, has_shared=True, max_tokens=T,
                           device=device_index)
     g = torch.Generator(device=dev).manual_seed(seed)
-    for e in list(range(E)) + [-1]:
+    for e in list(range(experts)) + [-1]:
         mats = []
         for shape in ((I, H), (I, H), (H, I)):
             w = (torch.randn(shape, generator=g, device=dev) * 0.02).to(torch.bfloat16)
@@ -148,8 +148,8 @@ def build_layer(T: int, device_index: int, seed: int = 0):
         layer.load_expert(e, NVFP4Expert(*mats))
         del mats
     gc = torch.Generator(device="cpu").manual_seed(seed + 1)
-    router = (torch.randn(E, H, generator=gc) * 0.02).to(torch.bfloat16)
-    bias = torch.rand(E, generator=gc) * 0.2 - 0.1
+    router = (torch.randn(experts, H, generator=gc) * 0.02).to(torch.bfloat16)
+    bias = torch.rand(experts, generator=gc) * 0.2 - 0.1
     layer.set_router(router, bias)
     torch.cuda.synchronize(dev)
     return layer
@@ -247,11 +247,12 @@ def run_ours(args) -> None:
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
         pg = dist
-    T = workload_tokens(args.workload)
-    layer = build_layer(T, local, seed=0)
+    T = args.tokens or workload_tokens(args.workload)
+    experts = args.experts or E
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.set_stream(stream)
+    layer = build_layer(T, local, seed=0, experts=experts)
     hidden = make_hidden(T, seed=100 + rank, device=dev)
-    out = torch.empty((T, H), dtype=torch.float32, device=dev)
-    stream = torch.cuda.current_stream()
     # warm-up
     for _ in range(args.warmup):
         layer(hidden, want_routing=False)
@@ -263,11 +264,13 @@ def run_ours(args) -> None:
     torch.cuda.synchronize()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
+        torch.cuda.nvtx.range_push("bench_timed")
         start.record(stream)
         for _ in range(args.steps):
             layer(hidden, want_routing=False)
         stop.record(stream)
         torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
     layer.check()
     ms_total = start.elapsed_time(stop)
     launches = layer.stats()["kernel_launches"] - stats0["kernel_launches"]
@@ -309,6 +312,7 @@ def run_ours(args) -> None:
         pk = peaks()
         fp4_peak = 4.0 * pk["bf16_sustained"]  # dense FP4 : BF16 = 4 : 1 on B200
         assignments = T * (K_TOP + 1)
+        custom = bool(args.tokens or args.experts)
         gemm1_flop = 2.0 * assignments * (2 * I) * H
         gemm1_ms = phases["gate_up_gemm"]
         achieved = gemm1_flop / (gemm1_ms / 1000.0) / 1e12
@@ -327,8 +331,10 @@ def run_ours(args) -> None:
             "vs_baseline": None, "dtype": "nvfp4 (e2m1 x e4m3/16, fp32 accumulate)",
             "data": "synthetic (seeded; weights N(0,0.02) packed NVFP4 mse; hidden MTP-draft "
                     "pattern)",
-            "config": {"workload": f"{args.workload}: GLM-5 MoE layer, {T} tokens/rank, 256 "
-                                   "NVFP4 experts top-8 + 1 shared, 6144->2048->6144",
+            "config": {"workload": (f"custom profiling case: {T} tokens/rank, {experts} experts"
+                                    if custom else
+                                    f"{args.workload}: GLM-5 MoE layer, {T} tokens/rank, 256 "
+                                    "NVFP4 experts top-8 + 1 shared, 6144->2048->6144"),
                        "global_batch": world * T, "tokens_per_rank": T,
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                        "l2": "inputs larger than L2 (5.46 GB of expert weights per step)"},
@@ -362,6 +368,8 @@ def main() -> None:
     ap.add_argument("--workload", default="c5", choices=["c5", "c3"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tokens", type=int, default=0, help="override tokens (profiling only)")
+    ap.add_argument("--experts", type=int, default=0, help="override experts (profiling only)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -188,6 +188,9 @@ glm5x_status glm5x_moe_set_profiling(glm5x_moe* moe, int32_t enable);
 /* Synchronizes; writes the milliseconds accumulated per phase since the last
  * call (ms[GLM5X_NUM_PHASES]) and the number of profiled forwards, then resets. */
 glm5x_status glm5x_moe_phase_times(glm5x_moe* moe, float* ms, int32_t* forwards);
+/* Token-tile width of the expert GEMMs: 32, 64, 128 or 256 rows, or 0 to
+ * choose from the batch (the default). */
+glm5x_status glm5x_moe_set_tile_n(glm5x_moe* moe, int32_t bn);
 /* The engine's own stream (used by glm5x_moe_forward_host and by forwards
  * given a NULL stream), as a cudaStream_t. */
 glm5x_status glm5x_moe_get_stream(glm5x_moe* moe, void** stream);

@@ -220,11 +220,14 @@ __global__ void __launch_bounds__(kThreads, 1)
               tmem_cp_sf(sfb_col + 4 * C::kSfbCh * c + 4 * h,
                          desc_sf_chunk(smem_u32(ssfb + h * 4 * kChunkBytes + c * kChunkBytes)));
           const uint32_t a_addr = smem_u32(sa), b_addr = smem_u32(sb);
+          // A tile narrower than 128 rows starts at row 32j of its scale
+          // block; the 32x128b copy put rows 32j.. in column j of the chunk.
+          const uint32_t sfb_sub = (uint32_t)((ti.row_start & 127) >> 5);
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             mma_nvfp4(d_tmem, desc_kmajor_sw128(a_addr + 32 * c),
                       desc_kmajor_sw128(b_addr + 32 * c), idesc, sfa_col + 4 * c,
-                      sfb_col + 4 * C::kSfbCh * c, (ks | c) != 0 ? 1u : 0u);
+                      sfb_col + 4 * C::kSfbCh * c + sfb_sub, (ks | c) != 0 ? 1u : 0u);
           }
           tc_commit(&empty[stage]);
           if (++stage == C::kStages) {

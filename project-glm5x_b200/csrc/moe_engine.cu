@@ -122,6 +122,7 @@ struct glm5x_moe {
   size_t stage_w_bytes = 0;
   float* scratch_f = nullptr;
 
+  int force_bn = 0;  // 0 = choose the token tile from the batch
   bool profiling = false;
   int profiled = 0;
   cudaEvent_t ev[GLM5X_NUM_PHASES + 1]{};
@@ -177,6 +178,7 @@ glm5x_status cuda_fail(glm5x_moe* m, cudaError_t e, const char* what) {
 int bn_index(int bn) { return bn == 32 ? 0 : bn == 64 ? 1 : bn == 128 ? 2 : 3; }
 
 int pick_bn(const glm5x_moe* m, int64_t T) {
+  if (m->force_bn) return m->force_bn;
   const double per_expert = (double)T * m->K() / std::max(1, m->cfg.num_experts);
   if (per_expert <= 24) return 32;
   if (per_expert <= 48) return 64;
@@ -703,6 +705,14 @@ glm5x_status glm5x_moe_phase_times(glm5x_moe* m, float* ms, int32_t* forwards) {
   }
   if (forwards) *forwards = m->profiled;
   m->profiled = 0;
+  return GLM5X_OK;
+}
+
+glm5x_status glm5x_moe_set_tile_n(glm5x_moe* m, int32_t bn) {
+  if (!m) return fail_global(GLM5X_INVALID_STATE, "null engine");
+  if (bn != 0 && bn != 32 && bn != 64 && bn != 128 && bn != 256)
+    return m->fail(GLM5X_INVALID_EXTENT, "token tile must be 0, 32, 64, 128 or 256");
+  m->force_bn = bn;
   return GLM5X_OK;
 }
 

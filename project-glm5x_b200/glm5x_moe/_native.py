@@ -99,6 +99,7 @@ SIGNATURES = {
     "glm5x_moe_set_profiling": [_P, _I32],
     "glm5x_moe_phase_times": [_P, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(_I32)],
     "glm5x_moe_get_stream": [_P, ctypes.POINTER(_P)],
+    "glm5x_moe_set_tile_n": [_P, _I32],
     "glm5x_nvfp4_quantize_f32": [_P, _I64, _I64, _I32, _P, _P, _P, _P],
     "glm5x_nvfp4_quantize_bf16": [_P, _I64, _I64, _I32, _P, _P, _P, _P],
     "glm5x_nvfp4_quantize_slabs_bf16": [_P, _I64, _P, _P, _P, _I32, _I64, _P, _P, _P, _P],
@@ -132,6 +133,16 @@ def lib() -> ctypes.CDLL:
             fn.restype = _RESTYPE.get(name, ctypes.c_int)
         _lib = handle
     return _lib
+
+
+CUDA_STREAM_LEGACY = 1  # cudaStreamLegacy
+
+
+def stream_arg(handle: int) -> ctypes.c_void_p:
+    """A torch stream handle as the C ABI's `stream`: torch's default stream
+    has handle 0, which the C ABI would read as "the engine's own stream", so
+    it is passed as cudaStreamLegacy instead."""
+    return ctypes.c_void_p(handle if handle else CUDA_STREAM_LEGACY)
 
 
 def check(status: int, engine=None) -> None:

@@ -39,7 +39,7 @@ class NVFP4Expert:
 
 
 def _stream() -> ctypes.c_void_p:
-    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    return N.stream_arg(torch.cuda.current_stream().cuda_stream)
 
 
 class GLM5XMoELayer:
@@ -175,6 +175,10 @@ class GLM5XMoELayer:
             N.check(N.lib().glm5x_moe_debug_copy(self._h, which, out.data_ptr(), count * esz),
                     self._h)
         return out
+
+    def set_tile_n(self, bn: int) -> None:
+        """Force the expert GEMMs' token tile (32/64/128/256), 0 = automatic."""
+        N.check(N.lib().glm5x_moe_set_tile_n(self._h, bn), self._h)
 
     def set_profiling(self, enable: bool) -> None:
         N.check(N.lib().glm5x_moe_set_profiling(self._h, 1 if enable else 0), self._h)

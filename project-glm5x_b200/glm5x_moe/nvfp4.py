@@ -23,7 +23,7 @@ def _ceil_div(value: int, divisor: int) -> int:
 
 
 def _stream() -> ctypes.c_void_p:
-    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    return N.stream_arg(torch.cuda.current_stream().cuda_stream)
 
 
 def _require_cuda(t: torch.Tensor, what: str) -> None:

@@ -12,6 +12,7 @@ import pytest
 import torch
 
 import oracle as O
+from glm5x_moe import _native as N
 
 pytestmark = pytest.mark.gpu
 
@@ -21,7 +22,7 @@ MX_CASES = ["kat_codes", "kat_12", "kat_chunks", "kat_row", "seed31_max", "seed3
 
 
 def _s():
-    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    return N.stream_arg(torch.cuda.current_stream().cuda_stream)
 
 
 @pytest.mark.parametrize("name", NV_CASES)
@@ -151,8 +152,9 @@ def test_gpu_slab_quantize_matches_oracle():
     scales = torch.zeros(O.blocked_size(rows, K // 16), dtype=torch.uint8, device="cuda")
     gl = torch.zeros(E, dtype=torch.float32, device="cuda")
     rt = torch.from_numpy(np.where(tok >= 0, tok, 0).astype(np.int32)).cuda()
+    st_full = np.append(starts, rows).astype(np.int32)
     N.check(N.lib().glm5x_nvfp4_quantize_slabs_bf16(
-        hd.data_ptr(), K, rt.data_ptr(), torch.from_numpy(starts.astype(np.int32)).cuda().data_ptr(),
+        hd.data_ptr(), K, rt.data_ptr(), torch.from_numpy(st_full).cuda().data_ptr(),
         torch.from_numpy(counts.astype(np.int32)).cuda().data_ptr(), E, rows, packed.data_ptr(),
         scales.data_ptr(), gl.data_ptr(), _s()))
     p_h, s_h, g_h = packed.cpu().numpy(), scales.cpu().numpy(), gl.cpu().numpy()

@@ -31,10 +31,14 @@ def _assert_close(got, want, what):
     assert max_rel <= MAX_REL and cos >= MIN_COS, (what, max_rel, l2, cos)
 
 
-@pytest.mark.parametrize("T", [1, 5, 40, 300])
-def test_routed_expert_path_small_shapes(T):
+@pytest.mark.parametrize("T,bn", [(1, 0), (5, 0), (40, 0), (300, 0), (40, 32), (100, 64),
+                                  (300, 128), (300, 256), (520, 256), (130, 32)])
+def test_routed_expert_path_small_shapes(T, bn):
+    """Every token-tile width, including segments that span several tiles and
+    tiles that start inside a 128-row scale block."""
     H, I, E, k = 512, 512, 8, 2
-    layer = _layer(H, I, E, k, True, 512)
+    layer = _layer(H, I, E, k, True, 600)
+    layer.set_tile_n(bn)
     experts, deq = {}, {}
     for e in list(range(E)) + [-1]:
         ex, dq = make_expert(H, I, 1000 + e)
