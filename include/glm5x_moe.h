@@ -181,7 +181,7 @@ glm5x_status glm5x_moe_get_stats(const glm5x_moe* moe, glm5x_moe_stats* out);
 glm5x_status glm5x_moe_debug_buffer(glm5x_moe* moe, int32_t which, void** ptr, size_t* bytes);
 /* Phase timing with CUDA events on the forward's stream (the per-projection
  * device times the reference records, backend_cuda.cu:2034-2040, 2151-2168).
- * Phases: 0 row amax, 1 router logits, 2 top-k, 3 permutation, 4 activation
+ * Phases: 0 row amax, 1 router (tcgen05 logits + top-k), 2 (unused), 3 permutation, 4 activation
  * quantize, 5 gate/up GEMM, 6 h quantize, 7 down GEMM, 8 combine. */
 #define GLM5X_NUM_PHASES 9
 glm5x_status glm5x_moe_set_profiling(glm5x_moe* moe, int32_t enable);

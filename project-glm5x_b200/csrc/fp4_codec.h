@@ -81,16 +81,43 @@ G5_HD float e2m1_value(uint32_t code) {
 }
 
 // The reference picks argmin_i |v - codebook[i]| with the first index
-// winning ties. For the normalized values the encoders produce (|v| < 16)
-// every candidate difference near a midpoint is exact in FP32, so the
-// argmin equals: magnitude rounded to the nearest E2M1 value with ties
-// toward the smaller magnitude, and code 0 (+0) for anything rounding to 0.
+// winning ties. For |v| < 16 (every normalized value the encoders produce)
+// every candidate difference near a midpoint is exact in FP32, so the argmin
+// is: magnitude rounded to the nearest E2M1 value with ties toward the smaller
+// magnitude, and code 0 (+0) for anything rounding to 0. The seven decision
+// thresholds (0.25 0.75 1.25 1.75 2.5 3.5 5) have zero low 21 mantissa bits,
+// so the magnitude code is a table lookup on bits(|v| - 1 ulp) >> 21. Checked
+// against the reference's argmin for all 2.2e9 floats with |v| <= 16.
 G5_HD uint32_t e2m1_encode(float v) {
-  const float a = fabsf(v);
-  uint32_t m = (a > 0.25f) + (a > 0.75f) + (a > 1.25f) + (a > 1.75f) + (a > 2.5f) +
-               (a > 3.5f) + (a > 5.0f);
-  if (m != 0 && v < 0.0f) m |= 8u;
-  return m;
+  const uint32_t b = f_bits(v) & 0x7fffffffu;
+  if (b == 0) return 0;
+  int k = static_cast<int>((b - 1u) >> 21) - 500;  // 500 = bits(0.25) >> 21
+  if (k < 0) return 0;
+  if (k > 17) k = 17;
+  // magnitude code for k = 0..17: 1 x6, 2 x3, 3 x2, 4 x2, 5 x2, 6 x2, 7
+  constexpr uint64_t kLut = 0x3ed6c8da489249ull;
+  const uint32_t m = static_cast<uint32_t>((kLut >> (3 * k)) & 7u);
+  return (f_bits(v) >> 31) ? (m | 8u) : m;
+}
+
+// x / d for the encoders: RN(x * RN(1/d)) is within 2 ulps of the IEEE
+// quotient; the E2M1 code can differ only when the quotient sits within 2
+// ulps of a value with a 2-bit mantissa (all thresholds are such values), in
+// which case the IEEE quotient is computed. rcp = RN(1/d).
+G5_HD float ratio_for_code(float x, float d, float rcp) {
+  float q = f_mul(x, rcp);
+  const uint32_t qb = f_bits(q) & 0x7fffffffu;
+  if (qb != 0 && ((qb + 2u) & 0x1fffffu) <= 4u) q = f_div(x, d);
+  return q;
+}
+
+G5_HD float f_rcp(float d) {
+#if defined(__CUDA_ARCH__)
+  return __frcp_rn(d);
+#else
+  volatile float r = 1.0f / d;
+  return r;
+#endif
 }
 
 // float -> float8_e4m3fn, round to nearest even, saturating at 448.
@@ -169,7 +196,8 @@ G5_HD uint32_t nvfp4_quantize_block(const float* x, float g, bool mse, uint8_t* 
   if (!mse) {
     sel = e4m3_encode(base);
     const float denom = f_mul(e4m3_decode(sel), g);
-    for (int i = 0; i < 16; ++i) codes[i] = e2m1_encode(f_div(x[i], denom));
+    const float rcp = f_rcp(denom);
+    for (int i = 0; i < 16; ++i) codes[i] = e2m1_encode(ratio_for_code(x[i], denom, rcp));
   } else {
     const float factors[9] = {0.5f, 0.625f, 0.75f, 0.875f, 1.0f, 1.125f, 1.25f, 1.5f, 2.0f};
     float best_err = 0.0f;
@@ -180,10 +208,11 @@ G5_HD uint32_t nvfp4_quantize_block(const float* x, float g, bool mse, uint8_t* 
       if (cand > kE4M3Max) cand = kE4M3Max;
       const uint32_t cb = e4m3_encode(cand);
       const float denom = f_mul(e4m3_decode(cb), g);
+      const float rcp = f_rcp(denom);
       uint32_t cc[16];
       float lane[8];
       for (int i = 0; i < 16; ++i) {
-        cc[i] = e2m1_encode(f_div(x[i], denom));
+        cc[i] = e2m1_encode(ratio_for_code(x[i], denom, rcp));
         const float d = f_sub(f_mul(e2m1_value(cc[i]), denom), x[i]);
         const float sq = f_mul(d, d);
         if (i < 8)

@@ -8,15 +8,16 @@
 // epilogue and the routing weight (layer10_moe.py:843-846) fused into the
 // down epilogue.
 //
-// Structure (one CTA per SM, 192 threads):
+// Structure (one CTA per SM, 320 threads):
 //   warp 0      TMA producer: weight tile (128 rows x 256 K) and activation
 //               tile (BN rows x 256 K), both 128B-swizzled, plus the four
 //               512-byte scale chunks of each operand by bulk copy.
 //   warp 1      TMEM owner and MMA issuer: tcgen05.cp moves the scale chunks
 //               into TMEM, then four kind::mxf4nvf4 block16 MMAs (K = 64
 //               each) per stage accumulate into TMEM.
-//   warps 2-5   epilogue: tcgen05.ld of the 128 x n accumulator, scale by the
-//               two global scales, fused activation, BF16 stores.
+//   warps 2-9   epilogue: two warps per 32-lane TMEM quadrant, alternating
+//               32-column chunks of the 128 x n accumulator; scale by the two
+//               global scales, fused activation, BF16 stores.
 // Weights are the M side (swap-AB): M = 128 weight rows per tile, N = the
 // expert's tokens (<= BN), so the decode regime (a few tokens per expert)
 // still uses full 128-row MMAs. Tiles are enumerated expert-major, then
@@ -36,7 +37,8 @@ namespace {
 constexpr int kBM = 128;          // weight rows per tile
 constexpr int kBKBytes = 128;     // K bytes per stage (256 FP4 values)
 constexpr int kChunkBytes = 512;  // one 128-row x 4-scale chunk
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;      // two warps per TMEM lane quadrant
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kMaxSeg = 260;      // segments (local experts + shared) per launch
 
 template <int BN>
@@ -81,7 +83,8 @@ __device__ __forceinline__ bool decode_tile(int tile, int m_tiles, int nseg, int
   const int m = local / nt, n = local % nt;
   ti.seg = s;
   ti.m_tile = m;
-  ti.row_start = start[s] + n * bn;
+  // tiles narrower than 128 rows each own a 128-row block (tile_stride 128)
+  ti.row_start = start[s] + n * (bn < 128 ? 128 : bn);
   const int left = cnt[s] - n * bn;
   ti.n_valid = left < bn ? left : bn;
   return true;
@@ -125,7 +128,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < C::kAcc; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 128);
+      mbar_init(&tempty[a], 32 * kEpiWarps);
     }
     mbar_init(drained, 1);
     fence_barrier_init();
@@ -220,14 +223,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               tmem_cp_sf(sfb_col + 4 * C::kSfbCh * c + 4 * h,
                          desc_sf_chunk(smem_u32(ssfb + h * 4 * kChunkBytes + c * kChunkBytes)));
           const uint32_t a_addr = smem_u32(sa), b_addr = smem_u32(sb);
-          // A tile narrower than 128 rows starts at row 32j of its scale
-          // block; the 32x128b copy put rows 32j.. in column j of the chunk.
-          const uint32_t sfb_sub = (uint32_t)((ti.row_start & 127) >> 5);
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             mma_nvfp4(d_tmem, desc_kmajor_sw128(a_addr + 32 * c),
                       desc_kmajor_sw128(b_addr + 32 * c), idesc, sfa_col + 4 * c,
-                      sfb_col + 4 * C::kSfbCh * c + sfb_sub, (ks | c) != 0 ? 1u : 0u);
+                      sfb_col + 4 * C::kSfbCh * c, (ks | c) != 0 ? 1u : 0u);
           }
           tc_commit(&empty[stage]);
           if (++stage == C::kStages) {
@@ -249,7 +249,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------ epilogue
-    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int q = warp & 3;                // TMEM lane quadrant this warp may access
+    const int half = (warp - 2) >> 2;      // which alternate 32-column chunks
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
@@ -258,47 +259,53 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(&tfull[acc], acc_phase, p.err)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(32 * q) << 16) + acc * BN;
-      float bscale = p.b_global[ti.seg];
+      const float bscale = p.b_global[ti.seg];
       if (EPI == 0) {
-        const float wg = p.a_global[2 * ti.seg + (lane >= 16 ? 1 : 0)];
-        const float scale = bscale * wg;
+        // Rows 32q..32q+15 of the tile are gate rows, 32q+16..32q+31 the
+        // matching up rows. For columns (i, i+16) of a chunk, lanes l and
+        // l^16 swap one value so that every lane computes one h.
+        const float s_gate = bscale * p.a_global[2 * ti.seg];
+        const float s_up = bscale * p.a_global[2 * ti.seg + 1];
+        const bool lo = lane < 16;
         const int j = ti.m_tile * (kBM / 2) + 16 * q + (lane & 15);
         const int hcols = p.M_per / 2;
         float amax = 0.0f;
-        for (int c0 = 0; c0 < ti.n_valid; c0 += 32) {
+        for (int c0 = 32 * half; c0 < ti.n_valid; c0 += 64) {
           uint32_t v[32];
           tmem_ld_32x32b_x32(t_row + c0, v);
           tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float mine = __uint_as_float(v[i]) * scale;
-            const float up = __shfl_down_sync(0xffffffffu, mine, 16);
-            if (lane < 16 && c0 + i < ti.n_valid) {
-              const float gate = mine;
-              const float h = gate / (1.0f + expf(-gate)) * up;
+          for (int i = 0; i < 16; ++i) {
+            const float send = __uint_as_float(lo ? v[i + 16] : v[i]);
+            const float recv = __shfl_xor_sync(0xffffffffu, send, 16);
+            const float gate = lo ? __uint_as_float(v[i]) * s_gate : recv * s_gate;
+            const float up = lo ? recv * s_up : __uint_as_float(v[i + 16]) * s_up;
+            const int col = c0 + i + (lo ? 0 : 16);
+            if (col < ti.n_valid) {
+              const float h = __fdividef(gate, 1.0f + __expf(-gate)) * up;
               const uint16_t hb = f2bf(h);
               amax = fmaxf(amax, fabsf(__uint_as_float((uint32_t)hb << 16)));
-              p.out[(size_t)(ti.row_start + c0 + i) * hcols + j] = hb;
+              p.out[(size_t)(ti.row_start + col) * hcols + j] = hb;
             }
           }
         }
         for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-        if (lane == 0 && ti.n_valid > 0)
+        if (lane == 0 && amax > 0.0f)
           atomicMax(reinterpret_cast<unsigned int*>(p.h_amax + ti.seg), __float_as_uint(amax));
       } else {
         const float scale = bscale * p.a_global[ti.seg];
         const int o = ti.m_tile * kBM + 32 * q + lane;
-        for (int c0 = 0; c0 < ti.n_valid; c0 += 32) {
+        for (int c0 = 32 * half; c0 < ti.n_valid; c0 += 64) {
           uint32_t v[32];
           tmem_ld_32x32b_x32(t_row + c0, v);
+          const float wmine =
+              c0 + lane < ti.n_valid ? p.row_weight[ti.row_start + c0 + lane] * scale : 0.0f;
           tmem_ld_wait();
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            if (c0 + i < ti.n_valid) {
-              const int row = ti.row_start + c0 + i;
-              const float y = __uint_as_float(v[i]) * scale * p.row_weight[row];
-              p.out[(size_t)row * p.M_per + o] = f2bf(y);
-            }
+            const float w = __shfl_sync(0xffffffffu, wmine, i);
+            if (c0 + i < ti.n_valid)
+              p.out[(size_t)(ti.row_start + c0 + i) * p.M_per + o] = f2bf(__uint_as_float(v[i]) * w);
           }
         }
       }

@@ -8,6 +8,20 @@
 
 namespace glm5x {
 
+// ------------------------------------------------------------ segment layout
+// Expert segments start on 128-row boundaries. With a token tile bn >= 128,
+// logical row q of a segment is physical row q. With bn < 128 every bn-row
+// tile owns a whole 128-row block (rows past bn unused), so that each tile's
+// activation scales start a 128-row scale block, which is where the
+// block-scaled MMA reads them (its scale-factor TMEM address must stay
+// 4-column aligned, so a tile cannot start inside a block).
+__host__ __device__ __forceinline__ int segment_row(int q, int bn) {
+  return bn < 128 ? (q / bn) * 128 + q % bn : q;
+}
+__host__ __device__ __forceinline__ int segment_rows(int count, int bn) {
+  return bn < 128 ? (count + bn - 1) / bn * 128 : (count + 127) / 128 * 128;
+}
+
 // ------------------------------------------------------------ quant.cu
 cudaError_t launch_row_amax_bf16(const uint16_t* src, int64_t rows, int cols, float* out,
                                  uint32_t* err, cudaStream_t st);
@@ -18,7 +32,7 @@ cudaError_t launch_nvfp4_quantize_matrix(const T* src, int64_t rows, int64_t col
                                          uint32_t* err, cudaStream_t st);
 cudaError_t launch_nvfp4_quantize_segments(const uint16_t* src, int K, const int32_t* row_token,
                                            const int32_t* seg_start, const int32_t* seg_count,
-                                           const int32_t* qprefix, int nseg,
+                                           const int32_t* qprefix, int nseg, int bn,
                                            const float* seg_amax, int64_t max_rows,
                                            uint8_t* packed, uint8_t* scales_blocked,
                                            float* seg_global, cudaStream_t st);
@@ -46,14 +60,21 @@ struct PermuteBuffers {
   float* row_weight;      // [rows], routing weight of each segment row
 };
 
-cudaError_t launch_router_logits_simt(const uint16_t* x, const uint16_t* w, int T, int H, int E,
-                                      float* logits, cudaStream_t st);
 cudaError_t launch_topk(const float* in, int values_are_scores, const float* bias, int T, int E,
                         int k, float routed_scale, int32_t* ids, float* weights, uint32_t* err,
                         cudaStream_t st);
 cudaError_t launch_permute(const int32_t* ids, const float* weights, const float* token_amax,
                            int T, int k, int E, int has_shared, int bn, PermuteBuffers b,
                            uint32_t* err, cudaStream_t st);
+
+// ------------------------------------------------------------ router_tc.cu
+// BF16 router logits on tcgen05 + sigmoid/bias/top-k epilogue. tmap_x: hidden
+// [T, H] BF16, box {64, 128}; tmap_w: router weight [E, H] BF16, box {64, E}.
+bool router_tc_supported(int E, int H, int k);
+cudaError_t launch_router_tc(const CUtensorMap* tmap_x, const CUtensorMap* tmap_w,
+                             const float* bias, int T, int H, int E, int k, float routed_scale,
+                             float* logits, int32_t* ids, float* weights, uint32_t* err,
+                             cudaStream_t st);
 
 // ------------------------------------------------------------ gemm_nvfp4.cu
 // Grouped block-scaled FP4 GEMM over expert segments, weights as the M side:

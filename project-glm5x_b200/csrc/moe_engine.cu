@@ -62,6 +62,21 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
+// 2-D BF16 tensor [rows, cols], box {64 elements, box_rows}, 128B swizzle.
+bool make_tmap_bf16(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows,
+                    uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * 2};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // 2-D byte tensor [rows, row_bytes], box {128 bytes, box_rows}, 128B swizzle.
 bool make_tmap_u8(CUtensorMap* m, void* base, uint64_t row_bytes, uint64_t rows,
                   uint32_t box_rows) {
@@ -129,6 +144,7 @@ struct glm5x_moe {
   double phase_ms[GLM5X_NUM_PHASES]{};
 
   CUtensorMap tm_w13{}, tm_w2{};
+  CUtensorMap tm_router{};
   CUtensorMap tm_act[4]{}, tm_h[4]{};  // box rows 32, 64, 128, 256
 
   glm5x_status fail(glm5x_status st, const char* fmt, ...) {
@@ -224,6 +240,9 @@ glm5x_status glm5x_moe_create(const glm5x_moe_config* cfg, int device, glm5x_moe
   if (c.num_experts <= 0 || c.num_experts > 256 || c.top_k <= 0 || c.top_k > 16 ||
       c.top_k > c.num_experts)
     return fail_global(GLM5X_INVALID_EXTENT, "need 0 < top_k <= 16, top_k <= num_experts <= 256");
+  if (!router_tc_supported(c.num_experts, c.hidden, c.top_k) && c.num_experts % 16 != 0 &&
+      c.num_experts > 16)
+    return fail_global(GLM5X_INVALID_EXTENT, "num_experts must be a multiple of 16");
   if (c.max_tokens <= 0 || c.max_tokens > (1 << 20))
     return fail_global(GLM5X_INVALID_EXTENT, "max_tokens out of range");
   if (!(c.routed_scaling > 0.0f)) return fail_global(GLM5X_INVALID_EXTENT, "routed_scaling <= 0");
@@ -261,7 +280,12 @@ glm5x_status glm5x_moe_create(const glm5x_moe_config* cfg, int device, glm5x_moe
   const int64_t T = c.max_tokens;
   const int H = c.hidden, I = c.intermediate, E = c.num_experts, k = c.top_k;
   const int nseg = m->nseg;
-  m->rows_cap = T * (int64_t)m->kk() + (int64_t)nseg * 128 + 256;
+  // segment rows for the widest layout the automatic tile choice can use:
+  // 32-row tiles (4 x rows) up to 24 tokens per expert, 64-row tiles (2 x)
+  // up to 48, dense beyond
+  const int64_t per32 = std::min<int64_t>(T, 24LL * E / k), per64 = std::min<int64_t>(T, 48LL * E / k);
+  const int64_t logical = std::max({T * (int64_t)m->kk(), 4 * per32 * m->kk(), 2 * per64 * m->kk()});
+  m->rows_cap = logical + (int64_t)nseg * 128 + 256;
   const int64_t R = m->rows_cap;
   const int64_t rb = R / 128 + 2;
   bool ok = true;
@@ -355,6 +379,10 @@ glm5x_status glm5x_moe_set_router(glm5x_moe* m, const uint16_t* w, const float* 
   G5_CHECK(m, cudaMemcpyAsync(m->router_bias, bias, sizeof(float) * E, cudaMemcpyHostToDevice,
                               m->stream), "bias upload");
   G5_CHECK(m, cudaStreamSynchronize(m->stream), "router upload");
+  if (!router_tc_supported(E, H, m->K()))
+    return m->fail(GLM5X_INVALID_EXTENT, "router needs num_experts in [16, 256], a multiple of 16");
+  if (!make_tmap_bf16(&m->tm_router, m->router_w, H, E, E))
+    return m->fail(GLM5X_BACKEND_UNAVAILABLE, "router tensor map");
   m->router_set = true;
   return GLM5X_OK;
 }
@@ -497,7 +525,13 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
   const int T = static_cast<int>(T64);
   const int H = m->H(), I = m->I(), E = m->cfg.num_experts, k = m->K();
   const int hs = m->cfg.has_shared ? 1 : 0;
-  const int bn = pick_bn(m, T);
+  int bn = pick_bn(m, T);
+  // tiles narrower than 128 rows each take a 128-row block: make sure the
+  // worst case still fits the workspace, else use 128-row tiles
+  if (bn < 128 && (int64_t)(128 / bn) * T * m->kk() + (int64_t)m->nseg * 128 > m->rows_cap) {
+    if (m->force_bn) return m->fail(GLM5X_INVALID_EXTENT, "token tile %d too narrow for %d tokens", bn, T);
+    bn = 128;
+  }
   const int bi = bn_index(bn);
   uint64_t launches = 0;
   auto mark = [&](int phase) {
@@ -510,16 +544,19 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
   const int32_t* ids = ids_in;
   const float* wts = w_in;
   if (!ids_in) {
-    G5_CHECK(m, launch_router_logits_simt(x, m->router_w, T, H, E, m->logits, st), "router");
-    mark(2);
-    G5_CHECK(m, launch_topk(m->logits, 0, m->router_bias, T, E, k, m->cfg.routed_scaling,
-                            m->topk_ids, m->topk_w, m->err, st), "topk");
-    launches += 2;
+    if (reinterpret_cast<uintptr_t>(x) % 16)
+      return m->fail(GLM5X_INVALID_EXTENT, "hidden must be 16-byte aligned");
+    CUtensorMap tm_x;
+    if (!make_tmap_bf16(&tm_x, x, H, T, 128))
+      return m->fail(GLM5X_BACKEND_UNAVAILABLE, "hidden tensor map");
+    G5_CHECK(m, launch_router_tc(&tm_x, &m->tm_router, m->router_bias, T, H, E, k,
+                                 m->cfg.routed_scaling, m->logits, m->topk_ids, m->topk_w, m->err,
+                                 st), "router");
+    launches += 1;
     ids = m->topk_ids;
     wts = m->topk_w;
-  } else {
-    mark(2);
   }
+  mark(2);
   mark(3);
   G5_CHECK(m, launch_permute(ids, wts, m->token_amax, T, k, E, hs, bn, m->pb, m->err, st),
            "permute");
@@ -527,7 +564,7 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
   const int64_t max_rows = (int64_t)T * m->kk() + (int64_t)m->nseg * 8;
   mark(4);
   G5_CHECK(m, launch_nvfp4_quantize_segments(x, H, m->pb.row_token, m->pb.seg_start,
-                                             m->pb.seg_count, m->pb.qprefix, m->nseg,
+                                             m->pb.seg_count, m->pb.qprefix, m->nseg, bn,
                                              m->pb.seg_amax, max_rows, m->act_packed, m->act_sf,
                                              m->act_global, st), "activation quantize");
   GemmParams g1{};
@@ -549,7 +586,7 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
            "gate/up GEMM");
   mark(6);
   G5_CHECK(m, launch_nvfp4_quantize_segments(m->h_bf16, I, nullptr, m->pb.seg_start,
-                                             m->pb.seg_count, m->pb.qprefix, m->nseg,
+                                             m->pb.seg_count, m->pb.qprefix, m->nseg, bn,
                                              m->pb.h_amax, max_rows, m->h_packed, m->h_sf,
                                              m->h_global, st), "h quantize");
   GemmParams g2 = g1;
@@ -828,7 +865,7 @@ glm5x_status glm5x_nvfp4_quantize_slabs_bf16(const uint16_t* src, int64_t cols,
   cudaMemcpyAsync(seg_amax, sa.data(), sizeof(float) * nseg, cudaMemcpyHostToDevice, st);
   cudaMemcpyAsync(qp, q.data(), sizeof(int32_t) * (nseg + 1), cudaMemcpyHostToDevice, st);
   cudaError_t e = launch_nvfp4_quantize_segments(src, (int)cols, row_token, seg_start, seg_count,
-                                                 qp, nseg, seg_amax, q[nseg], packed, scales,
+                                                 qp, nseg, 256, seg_amax, q[nseg], packed, scales,
                                                  seg_global, st);
   glm5x_status s = e == cudaSuccess ? sync_error(st, err, 0, "slab quantize")
                                     : fail_global(GLM5X_DEVICE_ERROR, "slab quantize launch");

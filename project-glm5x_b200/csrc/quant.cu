@@ -119,7 +119,7 @@ __global__ void nvfp4_quantize_matrix_kernel(const T* __restrict__ src, int64_t 
 __global__ void nvfp4_quantize_segments_kernel(
     const uint16_t* __restrict__ src, int K, const int32_t* __restrict__ row_token,
     const int32_t* __restrict__ seg_start, const int32_t* __restrict__ seg_count,
-    const int32_t* __restrict__ qprefix, int nseg, const float* __restrict__ seg_amax,
+    const int32_t* __restrict__ qprefix, int nseg, int bn, const float* __restrict__ seg_amax,
     uint8_t* __restrict__ packed, uint8_t* __restrict__ scales_blocked,
     float* __restrict__ seg_global) {
   const int warps = blockDim.x / 32;
@@ -134,7 +134,7 @@ __global__ void nvfp4_quantize_segments_kernel(
   }
   const int s = lo;
   const int r = static_cast<int>(f - qprefix[s]);
-  const int64_t row = seg_start[s] + r;
+  const int64_t row = seg_start[s] + segment_row(r, bn);
   const float g = nvfp4_global_scale(seg_amax[s]);
   if (r == 0 && lane_id() == 0) seg_global[s] = g;
   const int nb = K / 16;
@@ -165,11 +165,13 @@ __global__ void nvfp4_quantize_segments_kernel(
     base = fminf(fmaxf(base, kE4M3Tiny), kE4M3Max);
     const uint32_t sb = e4m3_encode(base);
     const float denom = f_mul(e4m3_decode(sb), g);
+    const float rcp = f_rcp(denom);
     uint32_t lo32 = 0, hi32 = 0;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) lo32 |= e2m1_encode(f_div(x[i], denom)) << (4 * i);
+    for (int i = 0; i < 8; ++i) lo32 |= e2m1_encode(ratio_for_code(x[i], denom, rcp)) << (4 * i);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) hi32 |= e2m1_encode(f_div(x[8 + i], denom)) << (4 * i);
+    for (int i = 0; i < 8; ++i)
+      hi32 |= e2m1_encode(ratio_for_code(x[8 + i], denom, rcp)) << (4 * i);
     *reinterpret_cast<uint2*>(prow + b * 8) = make_uint2(lo32, hi32);
     scales_blocked[blocked_sf_offset(row, b, nb)] = static_cast<uint8_t>(sb);
   }
@@ -292,7 +294,7 @@ template cudaError_t launch_nvfp4_quantize_matrix<__nv_bfloat16>(const __nv_bflo
 
 cudaError_t launch_nvfp4_quantize_segments(const uint16_t* src, int K, const int32_t* row_token,
                                            const int32_t* seg_start, const int32_t* seg_count,
-                                           const int32_t* qprefix, int nseg,
+                                           const int32_t* qprefix, int nseg, int bn,
                                            const float* seg_amax, int64_t max_rows,
                                            uint8_t* packed, uint8_t* scales_blocked,
                                            float* seg_global, cudaStream_t st) {
@@ -300,7 +302,7 @@ cudaError_t launch_nvfp4_quantize_segments(const uint16_t* src, int K, const int
   const int warps = 8;
   nvfp4_quantize_segments_kernel<<<(unsigned)((max_rows + warps - 1) / warps), warps * 32, 0,
                                    st>>>(src, K, row_token, seg_start, seg_count, qprefix, nseg,
-                                         seg_amax, packed, scales_blocked, seg_global);
+                                         bn, seg_amax, packed, scales_blocked, seg_global);
   return cudaGetLastError();
 }
 

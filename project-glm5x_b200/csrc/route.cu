@@ -22,48 +22,6 @@
 
 namespace glm5x {
 
-// ------------------------------------------------------------------ logits
-// FP32 router logits [T, E] = x[T, H] . W[E, H]^T from BF16 inputs.
-// 64-token x 64-expert tile per block, 256 threads, 4x4 outputs per thread.
-__global__ void __launch_bounds__(256) router_logits_simt_kernel(
-    const uint16_t* __restrict__ x, const uint16_t* __restrict__ w, int T, int H, int E,
-    float* __restrict__ logits) {
-  __shared__ float xs[32][64 + 1];
-  __shared__ float ws[32][64 + 1];
-  const int t0 = blockIdx.x * 64, e0 = blockIdx.y * 64;
-  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
-  float acc[4][4] = {};
-  for (int k0 = 0; k0 < H; k0 += 32) {
-    for (int i = threadIdx.x; i < 64 * 32; i += 256) {
-      const int r = i / 32, c = i % 32;
-      const int t = t0 + r, e = e0 + r;
-      xs[c][r] = t < T ? __uint_as_float((uint32_t)x[(int64_t)t * H + k0 + c] << 16) : 0.0f;
-      ws[c][r] = e < E ? __uint_as_float((uint32_t)w[(int64_t)e * H + k0 + c] << 16) : 0.0f;
-    }
-    __syncthreads();
-#pragma unroll 8
-    for (int c = 0; c < 32; ++c) {
-      float a[4], b[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) a[i] = xs[c][ty * 4 + i];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) b[j] = ws[c][tx * 4 + j];
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
-    }
-    __syncthreads();
-  }
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int t = t0 + ty * 4 + i, e = e0 + tx * 4 + j;
-      if (t < T && e < E) logits[(int64_t)t * E + e] = acc[i][j];
-    }
-}
-
 // ------------------------------------------------------------------ top-k
 // One warp per token. Lane l owns experts l, l+32, ... (E <= 32 * 16).
 // `values_are_scores` = 1 means `in` already holds sigmoid scores (the
@@ -234,7 +192,7 @@ __global__ void permute_scan_kernel(int32_t* __restrict__ chunk_count, int nchun
   }
   const bool valid = e < nseg;
   int tot;
-  const int start = block_exclusive_scan(valid ? (count + 127) / 128 * 128 : 0, scan_buf, &tot);
+  const int start = block_exclusive_scan(valid ? segment_rows(count, bn) : 0, scan_buf, &tot);
   const int q = block_exclusive_scan(valid ? (count + 7) / 8 * 8 : 0, scan_buf, &tot);
   const int qt = tot;
   // N tiles: 128-row aligned chunks of at most bn rows
@@ -253,13 +211,14 @@ __global__ void permute_scan_kernel(int32_t* __restrict__ chunk_count, int nchun
     ntile_prefix[nseg] = tot;
   }
   __syncthreads();
-  if (e == nseg - 1) seg_start[nseg] = start + (count + 127) / 128 * 128;
+  if (e == nseg - 1) seg_start[nseg] = start + segment_rows(count, bn);
 }
 
 // One thread per (token, slot) pair, plus one per token for the shared expert.
 __global__ void permute_scatter_kernel(const int32_t* __restrict__ ids,
                                        const float* __restrict__ weights, int T, int k, int E,
-                                       int has_shared, const int32_t* __restrict__ chunk_base,
+                                       int has_shared, int bn,
+                                       const int32_t* __restrict__ chunk_base,
                                        const int32_t* __restrict__ rank,
                                        const int32_t* __restrict__ seg_start,
                                        const float* __restrict__ token_amax,
@@ -275,11 +234,12 @@ __global__ void permute_scatter_kernel(const int32_t* __restrict__ ids,
   if (s < k) {
     e = ids[(int64_t)t * k + s];
     e = e < 0 || e >= E ? 0 : e;
-    p = seg_start[e] + chunk_base[(int64_t)(t / kChunk) * E + e] + rank[(int64_t)t * k + s];
+    p = seg_start[e] +
+        segment_row(chunk_base[(int64_t)(t / kChunk) * E + e] + rank[(int64_t)t * k + s], bn);
     w = weights[(int64_t)t * k + s];
   } else {
     e = E;
-    p = seg_start[E] + t;
+    p = seg_start[E] + segment_row(t, bn);
     w = 1.0f;
   }
   pos[idx] = p;
@@ -289,14 +249,6 @@ __global__ void permute_scatter_kernel(const int32_t* __restrict__ ids,
 }
 
 // ------------------------------------------------------------------ launchers
-cudaError_t launch_router_logits_simt(const uint16_t* x, const uint16_t* w, int T, int H, int E,
-                                      float* logits, cudaStream_t st) {
-  if (T == 0) return cudaSuccess;
-  dim3 grid((T + 63) / 64, (E + 63) / 64);
-  router_logits_simt_kernel<<<grid, 256, 0, st>>>(x, w, T, H, E, logits);
-  return cudaGetLastError();
-}
-
 cudaError_t launch_topk(const float* in, int values_are_scores, const float* bias, int T, int E,
                         int k, float routed_scale, int32_t* ids, float* weights, uint32_t* err,
                         cudaStream_t st) {
@@ -323,7 +275,7 @@ cudaError_t launch_permute(const int32_t* ids, const float* weights, const float
   const int64_t n = (int64_t)T * (k + has_shared);
   if (n > 0) {
     permute_scatter_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(
-        ids, weights, T, k, E, has_shared, b.chunk_count, b.rank, b.seg_start, token_amax, b.pos,
+        ids, weights, T, k, E, has_shared, bn, b.chunk_count, b.rank, b.seg_start, token_amax, b.pos,
         b.row_token, b.row_weight, b.seg_amax);
   }
   return cudaGetLastError();

@@ -152,11 +152,12 @@ def test_gpu_slab_quantize_matches_oracle():
     scales = torch.zeros(O.blocked_size(rows, K // 16), dtype=torch.uint8, device="cuda")
     gl = torch.zeros(E, dtype=torch.float32, device="cuda")
     rt = torch.from_numpy(np.where(tok >= 0, tok, 0).astype(np.int32)).cuda()
-    st_full = np.append(starts, rows).astype(np.int32)
+    # keep every device tensor referenced until the call returns
+    st_d = torch.from_numpy(np.append(starts, rows).astype(np.int32)).cuda()
+    cnt_d = torch.from_numpy(counts.astype(np.int32)).cuda()
     N.check(N.lib().glm5x_nvfp4_quantize_slabs_bf16(
-        hd.data_ptr(), K, rt.data_ptr(), torch.from_numpy(st_full).cuda().data_ptr(),
-        torch.from_numpy(counts.astype(np.int32)).cuda().data_ptr(), E, rows, packed.data_ptr(),
-        scales.data_ptr(), gl.data_ptr(), _s()))
+        hd.data_ptr(), K, rt.data_ptr(), st_d.data_ptr(), cnt_d.data_ptr(), E, rows,
+        packed.data_ptr(), scales.data_ptr(), gl.data_ptr(), _s()))
     p_h, s_h, g_h = packed.cpu().numpy(), scales.cpu().numpy(), gl.cpu().numpy()
     x = hidden.to(torch.float32).numpy()
     sf_rm = O.from_blocked(s_h, rows, K // 16)
