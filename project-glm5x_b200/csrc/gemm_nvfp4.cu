@@ -97,7 +97,9 @@ __device__ __forceinline__ uint16_t f2bf(float x) {
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     nvfp4_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                              const __grid_constant__ CUtensorMap tmap_b, const GemmParams p) {
+                              const __grid_constant__ CUtensorMap tmap_b32,
+                              const __grid_constant__ CUtensorMap tmap_b64,
+                              const __grid_constant__ CUtensorMap tmap_b128, const GemmParams p) {
   using C = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -140,7 +142,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmap_a);
-    tma_prefetch_desc(&tmap_b);
+    tma_prefetch_desc(&tmap_b32);
+    tma_prefetch_desc(&tmap_b64);
+    tma_prefetch_desc(&tmap_b128);
   }
   tc_fence_before();
   __syncthreads();
@@ -154,14 +158,40 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      const size_t a_row_bytes = (size_t)p.K / 2;
+      // L2 prefetch of one tile's weight rows + scales and activation rows
+      auto prefetch_tile = [&](int tile) {
+        TileInfo tp;
+        if (tile >= total_tiles ||
+            !decode_tile(tile, m_tiles, p.nseg, BN, s_ntp, s_cnt, s_start, tp))
+          return;
+        const size_t a_row = (size_t)tp.seg * p.M_per + (size_t)tp.m_tile * kBM;
+        const uint8_t* a = p.a_packed + a_row * a_row_bytes;
+        const uint32_t a_bytes = (uint32_t)(kBM * a_row_bytes);
+        for (uint32_t off = 0; off < a_bytes; off += 65536u)
+          l2_prefetch(a + off, a_bytes - off < 65536u ? a_bytes - off : 65536u);
+        l2_prefetch(p.sfa + (a_row / 128) * kc_per_rb * kChunkBytes, kc_per_rb * kChunkBytes);
+        const uint32_t b_bytes = (uint32_t)(((tp.n_valid + 31) & ~31) * a_row_bytes);
+        l2_prefetch(p.b_packed + (size_t)tp.row_start * a_row_bytes, b_bytes);
+      };
       for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
         TileInfo ti;
         if (!decode_tile(tile, m_tiles, p.nseg, BN, s_ntp, s_cnt, s_start, ti)) continue;
+        prefetch_tile(tile + gridDim.x);
         const int a_row = ti.seg * p.M_per + ti.m_tile * kBM;
         const int sfb_ch = ti.n_valid > 128 ? 2 : 1;
         const uint8_t* sfa = p.sfa + (size_t)(a_row / 128) * kc_per_rb * kChunkBytes;
         const uint8_t* sfb = p.sfb + (size_t)(ti.row_start / 128) * kc_per_rb * kChunkBytes;
-        const uint32_t bytes = C::kABytes + C::kBBytes + C::kSfaBytes + sfb_ch * 4 * kChunkBytes;
+        // activation rows in pieces: rows [0, 128) and [128, n), each rounded
+        // up to 32 rows and loaded with the 32/64/128-row box that fits
+        const int rows0 = ti.n_valid < 128 ? ti.n_valid : 128;
+        const int rows1 = ti.n_valid - rows0;
+        const int box0 = rows0 <= 32 ? 32 : (rows0 <= 64 ? 64 : 128);
+        const int box1 = rows1 <= 0 ? 0 : (rows1 <= 32 ? 32 : (rows1 <= 64 ? 64 : 128));
+        const CUtensorMap* m0 = box0 == 32 ? &tmap_b32 : (box0 == 64 ? &tmap_b64 : &tmap_b128);
+        const CUtensorMap* m1 = box1 == 32 ? &tmap_b32 : (box1 == 64 ? &tmap_b64 : &tmap_b128);
+        const uint32_t bytes = C::kABytes + (box0 + box1) * kBKBytes + C::kSfaBytes +
+                               sfb_ch * 4 * kChunkBytes;
         for (int ks = 0; ks < ks_count; ++ks) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, p.err)) {
             ok = false;
@@ -173,7 +203,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* ssfb = ssfa + C::kSfaBytes;
           mbar_arrive_expect_tx(&full[stage], bytes);
           tma_load_2d(sa, &tmap_a, &full[stage], ks * kBKBytes, a_row);
-          tma_load_2d(sb, &tmap_b, &full[stage], ks * kBKBytes, ti.row_start);
+          tma_load_2d(sb, m0, &full[stage], ks * kBKBytes, ti.row_start);
+          if (box1) tma_load_2d(sb + 128 * kBKBytes, m1, &full[stage], ks * kBKBytes,
+                                ti.row_start + 128);
           bulk_load(ssfa, sfa + (size_t)ks * 4 * kChunkBytes, C::kSfaBytes, &full[stage]);
           for (int h = 0; h < sfb_ch; ++h)
             bulk_load(ssfb + h * 4 * kChunkBytes,
@@ -270,10 +302,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int j = ti.m_tile * (kBM / 2) + 16 * q + (lane & 15);
         const int hcols = p.M_per / 2;
         float amax = 0.0f;
+        uint32_t nxt[32];
+        if (32 * half < ti.n_valid) tmem_ld_32x32b_x32(t_row + 32 * half, nxt);
         for (int c0 = 32 * half; c0 < ti.n_valid; c0 += 64) {
+          tmem_ld_wait(nxt);
           uint32_t v[32];
-          tmem_ld_32x32b_x32(t_row + c0, v);
-          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = nxt[i];
+          if (c0 + 64 < ti.n_valid) tmem_ld_32x32b_x32(t_row + c0 + 64, nxt);
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const float send = __uint_as_float(lo ? v[i + 16] : v[i]);
@@ -295,12 +331,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else {
         const float scale = bscale * p.a_global[ti.seg];
         const int o = ti.m_tile * kBM + 32 * q + lane;
+        uint32_t nxt[32];
+        if (32 * half < ti.n_valid) tmem_ld_32x32b_x32(t_row + 32 * half, nxt);
         for (int c0 = 32 * half; c0 < ti.n_valid; c0 += 64) {
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(t_row + c0, v);
           const float wmine =
               c0 + lane < ti.n_valid ? p.row_weight[ti.row_start + c0 + lane] * scale : 0.0f;
-          tmem_ld_wait();
+          tmem_ld_wait(nxt);
+          uint32_t v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = nxt[i];
+          if (c0 + 64 < ti.n_valid) tmem_ld_32x32b_x32(t_row + c0 + 64, nxt);
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const float w = __shfl_sync(0xffffffffu, wmine, i);
@@ -331,7 +371,7 @@ cudaError_t launch_impl(const CUtensorMap* ta, const CUtensorMap* tb, const Gemm
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)Cfg<BN>::kSmem);
   if (e != cudaSuccess) return e;
-  kern<<<num_sms, kThreads, Cfg<BN>::kSmem, st>>>(*ta, *tb, p);
+  kern<<<num_sms, kThreads, Cfg<BN>::kSmem, st>>>(*ta, tb[0], tb[1], tb[2], p);
   return cudaGetLastError();
 }
 

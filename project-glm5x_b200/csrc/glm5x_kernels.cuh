@@ -83,6 +83,8 @@ cudaError_t launch_router_tc(const CUtensorMap* tmap_x, const CUtensorMap* tmap_
 //   h = silu(gate) * up is stored as BF16 into h_out[row, M_per / 2].
 // Epilogue 1 (down): y * row_weight[row] stored as BF16 into y_out[row, M_per].
 struct GemmParams {
+  const uint8_t* a_packed;      // stacked weights (for L2 prefetch)
+  const uint8_t* b_packed;      // activation rows (for L2 prefetch)
   const uint8_t* sfa;           // blocked scales of the stacked weights
   const uint8_t* sfb;           // blocked scales of the activation rows
   const int32_t* seg_count;     // [nseg]
@@ -99,6 +101,8 @@ struct GemmParams {
   int nseg;
 };
 
+// tmap_b[i]: the activation rows with a box of (32 << i) rows, i = 0..2
+// (32, 64, 128); a tile loads its rows in pieces of at most 128.
 cudaError_t launch_nvfp4_grouped_gemm(int bn, int epi, const CUtensorMap* tmap_a,
                                       const CUtensorMap* tmap_b, const GemmParams& p,
                                       int num_sms, cudaStream_t st);

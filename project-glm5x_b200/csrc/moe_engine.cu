@@ -532,7 +532,6 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
     if (m->force_bn) return m->fail(GLM5X_INVALID_EXTENT, "token tile %d too narrow for %d tokens", bn, T);
     bn = 128;
   }
-  const int bi = bn_index(bn);
   uint64_t launches = 0;
   auto mark = [&](int phase) {
     if (m->profiling) cudaEventRecord(m->ev[phase], st);
@@ -568,6 +567,8 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
                                              m->pb.seg_amax, max_rows, m->act_packed, m->act_sf,
                                              m->act_global, st), "activation quantize");
   GemmParams g1{};
+  g1.a_packed = m->w13_packed;
+  g1.b_packed = m->act_packed;
   g1.sfa = m->w13_sf;
   g1.sfb = m->act_sf;
   g1.seg_count = m->pb.seg_count;
@@ -582,7 +583,7 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
   g1.M_per = 2 * I;
   g1.nseg = m->nseg;
   mark(5);
-  G5_CHECK(m, launch_nvfp4_grouped_gemm(bn, 0, &m->tm_w13, &m->tm_act[bi], g1, m->num_sms, st),
+  G5_CHECK(m, launch_nvfp4_grouped_gemm(bn, 0, &m->tm_w13, m->tm_act, g1, m->num_sms, st),
            "gate/up GEMM");
   mark(6);
   G5_CHECK(m, launch_nvfp4_quantize_segments(m->h_bf16, I, nullptr, m->pb.seg_start,
@@ -590,6 +591,8 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
                                              m->pb.h_amax, max_rows, m->h_packed, m->h_sf,
                                              m->h_global, st), "h quantize");
   GemmParams g2 = g1;
+  g2.a_packed = m->w2_packed;
+  g2.b_packed = m->h_packed;
   g2.sfa = m->w2_sf;
   g2.sfb = m->h_sf;
   g2.a_global = m->w2_global;
@@ -600,7 +603,7 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
   g2.K = I;
   g2.M_per = H;
   mark(7);
-  G5_CHECK(m, launch_nvfp4_grouped_gemm(bn, 1, &m->tm_w2, &m->tm_h[bi], g2, m->num_sms, st),
+  G5_CHECK(m, launch_nvfp4_grouped_gemm(bn, 1, &m->tm_w2, m->tm_h, g2, m->num_sms, st),
            "down GEMM");
   mark(8);
   G5_CHECK(m, launch_combine(m->y_bf16, m->pb.pos, T, m->kk(), H, out, st), "combine");

@@ -133,7 +133,7 @@ __global__ void __launch_bounds__(192, 1)
       for (int c0 = 0; c0 < E; c0 += 32) {
         uint32_t v[32];
         tmem_ld_32x32b_x32(tmem + ((uint32_t)(32 * q) << 16) + c0, v);
-        tmem_ld_wait();
+        tmem_ld_wait(v);
         if (t < T) {
           if (logits) {
             float* dst = logits + (int64_t)t * E + c0;
