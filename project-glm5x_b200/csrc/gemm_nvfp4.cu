@@ -30,6 +30,16 @@
 #include "glm5x_kernels.cuh"
 #include "glm5x_ptx.cuh"
 
+// Build-time tuning: L2 prefetch of the next tile's operands (measured to
+// raise DRAM traffic without speeding the GEMM up, so off) and loading only
+// the activation rows a tile needs (in 32/64/128-row pieces).
+#ifndef G5_GEMM_L2_PREFETCH
+#define G5_GEMM_L2_PREFETCH 0
+#endif
+#ifndef G5_GEMM_B_PIECES
+#define G5_GEMM_B_PIECES 1
+#endif
+
 namespace glm5x {
 
 namespace {
@@ -177,15 +187,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
         TileInfo ti;
         if (!decode_tile(tile, m_tiles, p.nseg, BN, s_ntp, s_cnt, s_start, ti)) continue;
-        prefetch_tile(tile + gridDim.x);
+        if (G5_GEMM_L2_PREFETCH) prefetch_tile(tile + gridDim.x);
         const int a_row = ti.seg * p.M_per + ti.m_tile * kBM;
         const int sfb_ch = ti.n_valid > 128 ? 2 : 1;
         const uint8_t* sfa = p.sfa + (size_t)(a_row / 128) * kc_per_rb * kChunkBytes;
         const uint8_t* sfb = p.sfb + (size_t)(ti.row_start / 128) * kc_per_rb * kChunkBytes;
         // activation rows in pieces: rows [0, 128) and [128, n), each rounded
         // up to 32 rows and loaded with the 32/64/128-row box that fits
-        const int rows0 = ti.n_valid < 128 ? ti.n_valid : 128;
-        const int rows1 = ti.n_valid - rows0;
+        const int rows0 = G5_GEMM_B_PIECES ? (ti.n_valid < 128 ? ti.n_valid : 128) : (BN < 128 ? BN : 128);
+        const int rows1 = G5_GEMM_B_PIECES ? ti.n_valid - rows0 : (BN > 128 ? BN - 128 : 0);
         const int box0 = rows0 <= 32 ? 32 : (rows0 <= 64 ? 64 : 128);
         const int box1 = rows1 <= 0 ? 0 : (rows1 <= 32 ? 32 : (rows1 <= 64 ? 64 : 128));
         const CUtensorMap* m0 = box0 == 32 ? &tmap_b32 : (box0 == 64 ? &tmap_b64 : &tmap_b128);

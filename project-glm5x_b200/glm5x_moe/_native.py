@@ -6,9 +6,13 @@ lacks a symbol, so no caller can silently fall back to another code path.
 from __future__ import annotations
 
 import ctypes
+import os
 from pathlib import Path
 
-LIB_PATH = Path(__file__).resolve().parent / "libglm5x_moe.so"
+# GLM5X_LIBRARY may point at another build of the same C ABI (e.g. a tuning
+# variant); the default is the in-tree build next to this file.
+LIB_PATH = Path(os.environ.get("GLM5X_LIBRARY") or
+                Path(__file__).resolve().parent / "libglm5x_moe.so")
 
 STATUS_NAMES = {
     0: "OK", 1: "IO_ERROR", 2: "BAD_MAGIC", 3: "UNSUPPORTED_VERSION", 7: "TRUNCATED_FILE",
