@@ -312,14 +312,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int j = ti.m_tile * (kBM / 2) + 16 * q + (lane & 15);
         const int hcols = p.M_per / 2;
         float amax = 0.0f;
-        uint32_t nxt[32];
-        if (32 * half < ti.n_valid) tmem_ld_32x32b_x32(t_row + 32 * half, nxt);
         for (int c0 = 32 * half; c0 < ti.n_valid; c0 += 64) {
-          tmem_ld_wait(nxt);
           uint32_t v[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = nxt[i];
-          if (c0 + 64 < ti.n_valid) tmem_ld_32x32b_x32(t_row + c0 + 64, nxt);
+          tmem_ld_32x32b_x32(t_row + c0, v);
+          tmem_ld_wait(v);
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const float send = __uint_as_float(lo ? v[i + 16] : v[i]);
@@ -341,16 +337,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else {
         const float scale = bscale * p.a_global[ti.seg];
         const int o = ti.m_tile * kBM + 32 * q + lane;
-        uint32_t nxt[32];
-        if (32 * half < ti.n_valid) tmem_ld_32x32b_x32(t_row + 32 * half, nxt);
         for (int c0 = 32 * half; c0 < ti.n_valid; c0 += 64) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(t_row + c0, v);
           const float wmine =
               c0 + lane < ti.n_valid ? p.row_weight[ti.row_start + c0 + lane] * scale : 0.0f;
-          tmem_ld_wait(nxt);
-          uint32_t v[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = nxt[i];
-          if (c0 + 64 < ti.n_valid) tmem_ld_32x32b_x32(t_row + c0 + 64, nxt);
+          tmem_ld_wait(v);
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const float w = __shfl_sync(0xffffffffu, wmine, i);
