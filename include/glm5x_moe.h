@@ -248,6 +248,20 @@ glm5x_status glm5x_expert_major_plan(const int32_t* ids, int64_t tokens, int32_t
                                      int32_t* seg_start, int32_t* pos, int32_t* row_token,
                                      void* stream);
 
+/* Same plan as glm5x_expert_major_plan, for callers that cannot allocate
+ * device memory (an allocator-owning host framework, a process at its memory
+ * cap, or a serving loop that cannot take cudaFree's device-wide
+ * synchronization). No counterpart in the reference: its planner runs on
+ * the host. Scratch is a fixed __device__ array (about 1 MB per GPU, held
+ * until exit); tokens <= 8192 and tokens * top_k <= 65536, else
+ * GLM5X_INVALID_EXTENT. The first call on a device looks the array up
+ * (make it before capturing a stream there); calls whose GPU work overlaps
+ * share the array and race. Synchronizes `stream` to report errors. */
+glm5x_status glm5x_expert_major_plan_noalloc(const int32_t* ids, int64_t tokens, int32_t top_k,
+                                             int32_t num_experts, int32_t* seg_count,
+                                             int32_t* seg_start, int32_t* pos,
+                                             int32_t* row_token, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -8,6 +8,9 @@
 
 namespace glm5x {
 
+// Sets the message glm5x_last_error_message() returns on this thread.
+void set_last_error(const char* msg);
+
 // ------------------------------------------------------------ segment layout
 // Expert segments start on 128-row boundaries. With a token tile bn >= 128,
 // logical row q of a segment is physical row q. With bn < 128 every bn-row

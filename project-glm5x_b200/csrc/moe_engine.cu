@@ -100,6 +100,11 @@ struct DevBuf {
 
 }  // namespace
 
+namespace glm5x {
+// Records the per-thread message returned by glm5x_last_error_message().
+void set_last_error(const char* msg) { g_last_error = msg; }
+}  // namespace glm5x
+
 struct glm5x_moe {
   glm5x_moe_config cfg{};
   int device = 0;

@@ -112,6 +112,7 @@ SIGNATURES = {
     "glm5x_mxfp4_decode": [_P, _P, _I64, _I64, _I64, _P, _P],
     "glm5x_select_routing": [_P, _P, _I64, _I32, _I32, _F, _P, _P, _P],
     "glm5x_expert_major_plan": [_P, _I64, _I32, _I32, _P, _P, _P, _P, _P],
+    "glm5x_expert_major_plan_noalloc": [_P, _I64, _I32, _I32, _P, _P, _P, _P, _P],
 }
 _RESTYPE = {
     "glm5x_moe_destroy": None,
