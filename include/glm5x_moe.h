@@ -191,6 +191,10 @@ glm5x_status glm5x_moe_phase_times(glm5x_moe* moe, float* ms, int32_t* forwards)
 /* Token-tile width of the expert GEMMs: 32, 64, 128 or 256 rows, or 0 to
  * choose from the batch (the default). */
 glm5x_status glm5x_moe_set_tile_n(glm5x_moe* moe, int32_t bn);
+/* 256-row token tiles run on CTA pairs (tcgen05 cta_group::2, the default)
+ * or on single CTAs (enable = 0); both give the same results to within
+ * accumulation order. */
+glm5x_status glm5x_moe_set_pair_mma(glm5x_moe* moe, int32_t enable);
 /* The engine's own stream (used by glm5x_moe_forward_host and by forwards
  * given a NULL stream), as a cudaStream_t. */
 glm5x_status glm5x_moe_get_stream(glm5x_moe* moe, void** stream);

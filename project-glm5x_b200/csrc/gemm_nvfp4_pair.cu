@@ -1,0 +1,363 @@
+// gemm_nvfp4_pair.cu -- grouped NVFP4 GEMM on CTA pairs (tcgen05 cta_group::2).
+//
+// Same contract and epilogues as gemm_nvfp4.cu (the reference's NVFP4
+// projections, reference/glm5x_ref/nvfp4.py:220-233 / nvfp4_batched.py:64-151,
+// with SwiGLU and the routing weight fused), for token tiles up to 256 rows.
+// A cluster of two CTAs on neighbouring SMs computes a 256-weight-row x
+// N-token tile with M = 256 MMAs: each CTA loads its own 128 weight rows and
+// half of the N token rows, so per FLOP each SM moves two thirds of the bytes
+// a single-CTA 128 x 256 tile moves. Each CTA also loads its weight rows'
+// scale chunks and all N rows' scale chunks (the MMA reads every column's
+// scales from each CTA's own TMEM).
+//
+// Roles (per CTA, 320 threads): warp 0 issues this CTA's TMA loads, all
+// counted on the leader CTA's full barrier; warp 1 of the leader copies the
+// scale chunks into both TMEMs and issues the pair MMAs (the peer's warp 1
+// only shares the TMEM allocation); warps 2-9 of both CTAs drain their own
+// TMEM and signal the leader when done. The leader's commits arrive on both
+// CTAs' barriers.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cstdint>
+
+#include "glm5x_kernels.cuh"
+#include "glm5x_ptx.cuh"
+
+namespace glm5x {
+namespace {
+
+constexpr int kPM = 256;           // weight rows per pair tile (128 per CTA)
+constexpr int kBN = 256;           // token rows per pair tile (up to 128 per CTA)
+constexpr int kBK = 128;           // K bytes per stage (256 FP4)
+constexpr int kChunk = 512;        // one 128-row x 4-scale chunk
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kStages = 5;
+constexpr int kABytes = 128 * kBK;           // this CTA's weight rows
+constexpr int kBBytes = 128 * kBK;           // this CTA's token rows
+constexpr int kSfaBytes = 4 * kChunk;
+constexpr int kSfbBytes = 2 * 4 * kChunk;    // both 128-row scale blocks of the tile
+constexpr int kStageBytes = ((kABytes + kBBytes + kSfaBytes + kSfbBytes + 1023) / 1024) * 1024;
+constexpr int kSfaCols = 16, kSfbCols = 32;
+constexpr int kSfBase = kBN;                 // one accumulator of kBN columns
+constexpr int kTmemCols = 512;
+static_assert(kSfBase + kStages * (kSfaCols + kSfbCols) <= kTmemCols, "TMEM budget");
+constexpr int kMaxSeg = 260;
+constexpr size_t kSmem = (size_t)kStages * kStageBytes + 1024 + 256;
+static_assert(kSmem + 3 * 4 * (kMaxSeg + 1) <= 232448, "shared memory budget");
+
+struct PairTile {
+  int seg, m2, row_start, n_valid;
+};
+
+__device__ __forceinline__ bool decode_pair_tile(int tile, int m2_tiles, int nseg,
+                                                 const int32_t* __restrict__ ntp,
+                                                 const int32_t* __restrict__ cnt,
+                                                 const int32_t* __restrict__ start,
+                                                 PairTile& ti) {
+  const int key = tile / m2_tiles;
+  int lo = 0, hi = nseg;
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (ntp[mid] <= key) lo = mid; else hi = mid;
+  }
+  const int nt = ntp[lo + 1] - ntp[lo];
+  if (nt <= 0) return false;
+  const int local = tile - m2_tiles * ntp[lo];
+  ti.seg = lo;
+  ti.m2 = local / nt;
+  const int n = local % nt;
+  ti.row_start = start[lo] + n * kBN;
+  const int left = cnt[lo] - n * kBN;
+  ti.n_valid = left < kBN ? left : kBN;
+  return true;
+}
+
+__device__ __forceinline__ uint16_t f2bf(float x) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(x));
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    nvfp4_pair_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                           const __grid_constant__ CUtensorMap tmap_b32,
+                           const __grid_constant__ CUtensorMap tmap_b64,
+                           const __grid_constant__ CUtensorMap tmap_b128,
+                           const __grid_constant__ CUtensorMap tmap_sfa,
+                           const __grid_constant__ CUtensorMap tmap_sfb, const GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  uint64_t* empty = full + kStages;
+  uint64_t* tfull = empty + kStages;
+  uint64_t* tempty = tfull + 1;
+  uint64_t* drained = tempty + 1;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drained + 1);
+  __shared__ int32_t s_ntp[kMaxSeg + 1], s_cnt[kMaxSeg], s_start[kMaxSeg + 1];
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int m2_tiles = p.M_per / kPM;
+  const int ks_count = p.K / 256;
+  const int kc_per_rb = p.K / 64;
+
+  for (int i = threadIdx.x; i <= p.nseg; i += blockDim.x) {
+    s_ntp[i] = p.ntile_prefix[i];
+    s_start[i] = p.seg_start[i];
+    if (i < p.nseg) s_cnt[i] = p.seg_count[i];
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(tfull, 1);
+    mbar_init(tempty, 2 * 32 * kEpiWarps);
+    mbar_init(drained, 1);
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_holder, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // the peer's barriers exist before anyone signals them
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  const int total_tiles = m2_tiles * s_ntp[p.nseg];
+
+  if (warp == 0) {
+    // ------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmap_a);
+      tma_prefetch_desc(&tmap_sfa);
+      tma_prefetch_desc(&tmap_sfb);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = pair; tile < total_tiles && ok; tile += npairs) {
+        PairTile ti;
+        if (!decode_pair_tile(tile, m2_tiles, p.nseg, s_ntp, s_cnt, s_start, ti)) continue;
+        const int n_mma = (ti.n_valid + 15) & ~15;
+        const int half = n_mma / 2;  // token rows held by each CTA (multiple of 8)
+        const int box = half <= 32 ? 32 : (half <= 64 ? 64 : 128);
+        const CUtensorMap* mb = box == 32 ? &tmap_b32 : (box == 64 ? &tmap_b64 : &tmap_b128);
+        const int sfb_ch = n_mma > 128 ? 2 : 1;
+        const int a_row = ti.seg * p.M_per + ti.m2 * kPM + (int)rank * 128;
+        const int sfa_y = 2 * (a_row / 128) * kc_per_rb;          // 256-byte rows of the map
+        const int sfb_y = 2 * (ti.row_start / 128) * kc_per_rb;
+        const uint32_t cta_bytes = kABytes + box * kBK + kSfaBytes + sfb_ch * 4 * kChunk;
+        for (int ks = 0; ks < ks_count; ++ks) {
+          if (!mbar_wait_cluster(&empty[stage], phase ^ 1u, p.err)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + stage * kStageBytes;
+          uint8_t* sb = sa + kABytes;
+          uint8_t* ssfa = sb + kBBytes;
+          uint8_t* ssfb = ssfa + kSfaBytes;
+          const uint32_t lead_full = mapa_shared(smem_u32(&full[stage]), 0);
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * cta_bytes);
+          tma_load_2d_pair(sa, &tmap_a, lead_full, ks * kBK, a_row);
+          tma_load_2d_pair(sb, mb, lead_full, ks * kBK, ti.row_start + (int)rank * half);
+          tma_load_2d_pair(ssfa, &tmap_sfa, lead_full, 0, sfa_y + 8 * ks);
+          for (int h = 0; h < sfb_ch; ++h)
+            tma_load_2d_pair(ssfb + h * 4 * kChunk, &tmap_sfb, lead_full, 0,
+                             sfb_y + 2 * h * kc_per_rb + 8 * ks);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------ MMA (leader)
+    if (leader && lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int tile = pair; tile < total_tiles && ok; tile += npairs) {
+        PairTile ti;
+        if (!decode_pair_tile(tile, m2_tiles, p.nseg, s_ntp, s_cnt, s_start, ti)) continue;
+        const uint32_t n_mma = (uint32_t)((ti.n_valid + 15) & ~15);
+        const int sfb_ch = n_mma > 128 ? 2 : 1;
+        const uint32_t idesc = idesc_fp4(kPM, n_mma, 0, 0, 0);
+        if (!mbar_wait_cluster(tempty, acc_phase ^ 1u, p.err)) break;
+        tc_fence_after();
+        for (int ks = 0; ks < ks_count; ++ks) {
+          if (!mbar_wait_cluster(&full[stage], phase, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint8_t* sa = smem + stage * kStageBytes;
+          const uint8_t* sb = sa + kABytes;
+          const uint8_t* ssfa = sb + kBBytes;
+          const uint8_t* ssfb = ssfa + kSfaBytes;
+          const uint32_t sfa_col = tmem_base + kSfBase + stage * (kSfaCols + kSfbCols);
+          const uint32_t sfb_col = sfa_col + kSfaCols;
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            tmem_cp_sf_pair(sfa_col + 4 * c, desc_sf_chunk(smem_u32(ssfa + c * kChunk)));
+          for (int h = 0; h < sfb_ch; ++h)
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+              tmem_cp_sf_pair(sfb_col + 8 * c + 4 * h,
+                              desc_sf_chunk(smem_u32(ssfb + h * 4 * kChunk + c * kChunk)));
+          const uint32_t a_addr = smem_u32(sa), b_addr = smem_u32(sb);
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            mma_nvfp4_pair(tmem_base, desc_kmajor_sw128(a_addr + 32 * c),
+                           desc_kmajor_sw128(b_addr + 32 * c), idesc, sfa_col + 4 * c,
+                           sfb_col + 8 * c, (ks | c) != 0 ? 1u : 0u);
+          tc_commit_pair(&empty[stage], 0x3);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit_pair(tfull, 0x3);
+        acc_phase ^= 1u;
+      }
+      tc_commit_pair(drained, 0x1);
+      mbar_wait(drained, 0, p.err);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------ epilogue (both CTAs)
+    const int q = warp & 3;
+    const int half_cols = (warp - 2) >> 2;
+    const uint32_t lead_tempty = mapa_shared(smem_u32(tempty), 0);
+    uint32_t acc_phase = 0;
+    for (int tile = pair; tile < total_tiles; tile += npairs) {
+      PairTile ti;
+      if (!decode_pair_tile(tile, m2_tiles, p.nseg, s_ntp, s_cnt, s_start, ti)) continue;
+      if (!mbar_wait_cluster(tfull, acc_phase, p.err)) break;
+      tc_fence_after();
+      const uint32_t t_row = tmem_base + ((uint32_t)(32 * q) << 16);
+      const int m_tile = 2 * ti.m2 + (int)rank;  // this CTA's 128-row weight tile
+      const float bscale = p.b_global[ti.seg];
+      if (EPI == 0) {
+        const float s_gate = bscale * p.a_global[2 * ti.seg];
+        const float s_up = bscale * p.a_global[2 * ti.seg + 1];
+        const bool lo = lane < 16;
+        const int j = m_tile * 64 + 16 * q + (lane & 15);
+        const int hcols = p.M_per / 2;
+        float amax = 0.0f;
+        for (int c0 = 32 * half_cols; c0 < ti.n_valid; c0 += 64) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(t_row + c0, v);
+          tmem_ld_wait(v);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float send = __uint_as_float(lo ? v[i + 16] : v[i]);
+            const float recv = __shfl_xor_sync(0xffffffffu, send, 16);
+            const float gate = lo ? __uint_as_float(v[i]) * s_gate : recv * s_gate;
+            const float up = lo ? recv * s_up : __uint_as_float(v[i + 16]) * s_up;
+            const int col = c0 + i + (lo ? 0 : 16);
+            if (col < ti.n_valid) {
+              const float h = __fdividef(gate, 1.0f + __expf(-gate)) * up;
+              const uint16_t hb = f2bf(h);
+              amax = fmaxf(amax, fabsf(__uint_as_float((uint32_t)hb << 16)));
+              p.out[(size_t)(ti.row_start + col) * hcols + j] = hb;
+            }
+          }
+        }
+        for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        if (lane == 0 && amax > 0.0f)
+          atomicMax(reinterpret_cast<unsigned int*>(p.h_amax + ti.seg), __float_as_uint(amax));
+      } else {
+        const float scale = bscale * p.a_global[ti.seg];
+        const int o = m_tile * 128 + 32 * q + lane;
+        for (int c0 = 32 * half_cols; c0 < ti.n_valid; c0 += 64) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(t_row + c0, v);
+          const float wmine =
+              c0 + lane < ti.n_valid ? p.row_weight[ti.row_start + c0 + lane] * scale : 0.0f;
+          tmem_ld_wait(v);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float w = __shfl_sync(0xffffffffu, wmine, i);
+            if (c0 + i < ti.n_valid)
+              p.out[(size_t)(ti.row_start + c0 + i) * p.M_per + o] = f2bf(__uint_as_float(v[i]) * w);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive_cluster(lead_tempty);
+      acc_phase ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no CTA frees TMEM or exits while its peer may still signal it
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem_base, kTmemCols);
+}
+
+template <int EPI>
+cudaError_t launch_pair(const CUtensorMap* ta, const CUtensorMap* tb, const CUtensorMap* tsfa,
+                        const CUtensorMap* tsfb, const GemmParams& p, int grid,
+                        cudaStream_t st) {
+  auto kern = nvfp4_pair_gemm_kernel<EPI>;
+  cudaError_t e =
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, *ta, tb[0], tb[1], tb[2], *tsfa, *tsfb, p);
+}
+
+}  // namespace
+
+int nvfp4_pair_gemm_grid(int num_sms) {
+  // as many CTA pairs as can be resident at once (clusters of two SMs)
+  auto kern = nvfp4_pair_gemm_kernel<0>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem) !=
+      cudaSuccess)
+    return 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)num_sms);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess) return 0;
+  return 2 * clusters;
+}
+
+cudaError_t launch_nvfp4_pair_gemm(int epi, const CUtensorMap* tmap_a, const CUtensorMap* tmap_b,
+                                   const CUtensorMap* tmap_sfa, const CUtensorMap* tmap_sfb,
+                                   const GemmParams& p, int grid, cudaStream_t st) {
+  if (p.nseg > kMaxSeg || p.K % 256 || p.M_per % kPM || grid < 2 || grid % 2)
+    return cudaErrorInvalidValue;
+  return epi == 0 ? launch_pair<0>(tmap_a, tmap_b, tmap_sfa, tmap_sfb, p, grid, st)
+                  : launch_pair<1>(tmap_a, tmap_b, tmap_sfa, tmap_sfb, p, grid, st);
+}
+
+}  // namespace glm5x

@@ -111,6 +111,16 @@ cudaError_t launch_nvfp4_grouped_gemm(int bn, int epi, const CUtensorMap* tmap_a
                                       int num_sms, cudaStream_t st);
 size_t nvfp4_gemm_smem_bytes(int bn);
 
+// ------------------------------------------------------------ gemm_nvfp4_pair.cu
+// Same GEMM on CTA pairs (cta_group::2, M = 256) for token tiles of up to 256
+// rows. tmap_sfa / tmap_sfb: the blocked scale arrays as [bytes/256, 256]
+// uint8 tensors with a {256, 8} box (four 512-byte chunks). grid = an even
+// CTA count, at most nvfp4_pair_gemm_grid().
+int nvfp4_pair_gemm_grid(int num_sms);
+cudaError_t launch_nvfp4_pair_gemm(int epi, const CUtensorMap* tmap_a, const CUtensorMap* tmap_b,
+                                   const CUtensorMap* tmap_sfa, const CUtensorMap* tmap_sfb,
+                                   const GemmParams& p, int grid, cudaStream_t st);
+
 // ------------------------------------------------------------ combine.cu
 // out[t, :] = sum_{s < kk} y[pos[t, s], :] (FP32 accumulation of BF16 rows).
 cudaError_t launch_combine(const uint16_t* y, const int32_t* pos, int T, int kk, int H,

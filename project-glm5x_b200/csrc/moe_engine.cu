@@ -77,6 +77,21 @@ bool make_tmap_bf16(CUtensorMap* m, const void* base, uint64_t cols, uint64_t ro
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// A blocked scale array as a [bytes/256, 256] byte tensor, box {256, 8}: one
+// TMA copy moves four consecutive 512-byte scale chunks.
+bool make_tmap_sf(CUtensorMap* m, void* base, uint64_t bytes) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn || bytes % 256) return false;
+  cuuint64_t dims[2] = {256, bytes / 256};
+  cuuint64_t strides[1] = {256};
+  cuuint32_t box[2] = {256, 8};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, base, dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // 2-D byte tensor [rows, row_bytes], box {128 bytes, box_rows}, 128B swizzle.
 bool make_tmap_u8(CUtensorMap* m, void* base, uint64_t row_bytes, uint64_t rows,
                   uint32_t box_rows) {
@@ -150,6 +165,9 @@ struct glm5x_moe {
 
   CUtensorMap tm_w13{}, tm_w2{};
   CUtensorMap tm_router{};
+  CUtensorMap tm_w13_sf{}, tm_w2_sf{}, tm_act_sf{}, tm_h_sf{};
+  int pair_grid = 0;       // CTAs for the pair GEMM (0 = unavailable)
+  bool use_pair = true;    // 256-row token tiles on CTA pairs
   CUtensorMap tm_act[4]{}, tm_h[4]{};  // box rows 32, 64, 128, 256
 
   glm5x_status fail(glm5x_status st, const char* fmt, ...) {
@@ -349,10 +367,16 @@ glm5x_status glm5x_moe_create(const glm5x_moe_config* cfg, int device, glm5x_moe
     ok = make_tmap_u8(&m->tm_act[i], m->act_packed, H / 2, R, boxes[i]) &&
          make_tmap_u8(&m->tm_h[i], m->h_packed, I / 2, R, boxes[i]);
   }
+  ok = ok && make_tmap_sf(&m->tm_w13_sf, m->w13_sf, (uint64_t)nseg * m->w13_sf_bytes()) &&
+       make_tmap_sf(&m->tm_w2_sf, m->w2_sf, (uint64_t)nseg * m->w2_sf_bytes()) &&
+       make_tmap_sf(&m->tm_act_sf, m->act_sf, (uint64_t)rb * (H / 64) * 512) &&
+       make_tmap_sf(&m->tm_h_sf, m->h_sf, (uint64_t)rb * (I / 64) * 512);
   if (!ok) {
     glm5x_moe_destroy(m);
     return fail_global(GLM5X_BACKEND_UNAVAILABLE, "tensor map encoding failed");
   }
+  m->pair_grid = nvfp4_pair_gemm_grid(m->num_sms);
+  cudaGetLastError();
   if (cudaDeviceSynchronize() != cudaSuccess) {
     glm5x_moe_destroy(m);
     return fail_global(GLM5X_DEVICE_ERROR, "device initialization failed");
@@ -588,7 +612,11 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
   g1.M_per = 2 * I;
   g1.nseg = m->nseg;
   mark(5);
-  G5_CHECK(m, launch_nvfp4_grouped_gemm(bn, 0, &m->tm_w13, m->tm_act, g1, m->num_sms, st),
+  const bool pair = bn == 256 && m->use_pair && m->pair_grid >= 2;
+  G5_CHECK(m,
+           pair ? launch_nvfp4_pair_gemm(0, &m->tm_w13, m->tm_act, &m->tm_w13_sf, &m->tm_act_sf,
+                                         g1, m->pair_grid, st)
+                : launch_nvfp4_grouped_gemm(bn, 0, &m->tm_w13, m->tm_act, g1, m->num_sms, st),
            "gate/up GEMM");
   mark(6);
   G5_CHECK(m, launch_nvfp4_quantize_segments(m->h_bf16, I, nullptr, m->pb.seg_start,
@@ -608,7 +636,10 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
   g2.K = I;
   g2.M_per = H;
   mark(7);
-  G5_CHECK(m, launch_nvfp4_grouped_gemm(bn, 1, &m->tm_w2, m->tm_h, g2, m->num_sms, st),
+  G5_CHECK(m,
+           pair ? launch_nvfp4_pair_gemm(1, &m->tm_w2, m->tm_h, &m->tm_w2_sf, &m->tm_h_sf, g2,
+                                         m->pair_grid, st)
+                : launch_nvfp4_grouped_gemm(bn, 1, &m->tm_w2, m->tm_h, g2, m->num_sms, st),
            "down GEMM");
   mark(8);
   G5_CHECK(m, launch_combine(m->y_bf16, m->pb.pos, T, m->kk(), H, out, st), "combine");
@@ -758,6 +789,12 @@ glm5x_status glm5x_moe_set_tile_n(glm5x_moe* m, int32_t bn) {
   if (bn != 0 && bn != 32 && bn != 64 && bn != 128 && bn != 256)
     return m->fail(GLM5X_INVALID_EXTENT, "token tile must be 0, 32, 64, 128 or 256");
   m->force_bn = bn;
+  return GLM5X_OK;
+}
+
+glm5x_status glm5x_moe_set_pair_mma(glm5x_moe* m, int32_t enable) {
+  if (!m) return fail_global(GLM5X_INVALID_STATE, "null engine");
+  m->use_pair = enable != 0;
   return GLM5X_OK;
 }
 

@@ -180,6 +180,10 @@ class GLM5XMoELayer:
         """Force the expert GEMMs' token tile (32/64/128/256), 0 = automatic."""
         N.check(N.lib().glm5x_moe_set_tile_n(self._h, bn), self._h)
 
+    def set_pair_mma(self, enable: bool) -> None:
+        """256-row token tiles on CTA pairs (default) or single CTAs."""
+        N.check(N.lib().glm5x_moe_set_pair_mma(self._h, 1 if enable else 0), self._h)
+
     def set_profiling(self, enable: bool) -> None:
         N.check(N.lib().glm5x_moe_set_profiling(self._h, 1 if enable else 0), self._h)
 

@@ -31,14 +31,17 @@ def _assert_close(got, want, what):
     assert max_rel <= MAX_REL and cos >= MIN_COS, (what, max_rel, l2, cos)
 
 
-@pytest.mark.parametrize("T,bn", [(1, 0), (5, 0), (40, 0), (300, 0), (40, 32), (100, 64),
-                                  (300, 128), (300, 256), (520, 256), (130, 32)])
-def test_routed_expert_path_small_shapes(T, bn):
-    """Every token-tile width, including segments that span several tiles and
-    tiles that start inside a 128-row scale block."""
+@pytest.mark.parametrize("T,bn,pair", [(1, 0, True), (5, 0, True), (40, 0, True), (300, 0, True),
+                                       (40, 32, True), (100, 64, True), (300, 128, True),
+                                       (300, 256, True), (520, 256, True), (130, 32, True),
+                                       (300, 256, False), (520, 256, False), (7, 256, True)])
+def test_routed_expert_path_small_shapes(T, bn, pair):
+    """Every token-tile width (256-row tiles on CTA pairs and on single CTAs),
+    including segments that span several tiles and narrow tiles."""
     H, I, E, k = 512, 512, 8, 2
     layer = _layer(H, I, E, k, True, 600)
     layer.set_tile_n(bn)
+    layer.set_pair_mma(pair)
     experts, deq = {}, {}
     for e in list(range(E)) + [-1]:
         ex, dq = make_expert(H, I, 1000 + e)
@@ -52,7 +55,32 @@ def test_routed_expert_path_small_shapes(T, bn):
     layer.check()
     shared = deq.pop(-1)
     want, _ = oracle_forward(bf16_to_np(hidden), ids, w, deq, shared)
-    _assert_close(out.cpu().numpy(), want, f"T={T}")
+    _assert_close(out.cpu().numpy(), want, f"T={T} bn={bn} pair={pair}")
+    layer.close()
+
+
+@pytest.mark.parametrize("pair", [True, False])
+def test_glm_shape_256_tiles(pair):
+    """GLM-shaped experts with 256-row token tiles (the prefill path), on CTA
+    pairs and on single CTAs."""
+    H, I, E, k, T = 6144, 2048, 4, 4, 300
+    layer = _layer(H, I, E, k, True, T)
+    layer.set_tile_n(256)
+    layer.set_pair_mma(pair)
+    deq = {}
+    for e in list(range(E)) + [-1]:
+        ex, dq = make_expert(H, I, 900 + e)
+        layer.load_expert(e, ex)
+        deq[e] = dq
+    rng = np.random.default_rng(9)
+    ids = np.stack([rng.permutation(E)[:k] for _ in range(T)]).astype(np.int32)
+    w = rng.random((T, k)).astype(np.float32)
+    hidden = torch.randn(T, H, generator=torch.Generator().manual_seed(3)).to(torch.bfloat16)
+    out = layer.forward_routed(hidden.cuda(), torch.from_numpy(ids), torch.from_numpy(w))
+    layer.check()
+    shared = deq.pop(-1)
+    want, _ = oracle_forward(bf16_to_np(hidden), ids, w, deq, shared)
+    _assert_close(out.cpu().numpy(), want, f"pair={pair}")
     layer.close()
 
 
