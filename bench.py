@@ -254,8 +254,8 @@ def run_ours(args) -> None:
     layer = build_layer(T, local, seed=0, experts=experts)
     if args.tile_n:
         layer.set_tile_n(args.tile_n)
-    if args.single_cta:
-        layer.set_pair_mma(False)
+    if args.pair_cta:
+        layer.set_pair_mma(True)
     hidden = make_hidden(T, seed=100 + rank, device=dev)
     # warm-up
     for _ in range(args.warmup):
@@ -374,7 +374,7 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tokens", type=int, default=0, help="override tokens (profiling only)")
     ap.add_argument("--tile-n", type=int, default=0, help="force the GEMM token tile (tuning)")
-    ap.add_argument("--single-cta", action="store_true", help="256-row tiles on single CTAs")
+    ap.add_argument("--pair-cta", action="store_true", help="256-row tiles on CTA pairs (tuning)")
     ap.add_argument("--experts", type=int, default=0, help="override experts (profiling only)")
     args = ap.parse_args()
     if args.warmup < 3:

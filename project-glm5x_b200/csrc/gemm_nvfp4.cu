@@ -8,16 +8,26 @@
 // epilogue and the routing weight (layer10_moe.py:843-846) fused into the
 // down epilogue.
 //
-// Structure (one CTA per SM, 320 threads):
+// Structure (one CTA per SM, 512 threads = four warpgroups):
 //   warp 0      TMA producer: weight tile (128 rows x 256 K) and activation
 //               tile (BN rows x 256 K), both 128B-swizzled, plus the four
 //               512-byte scale chunks of each operand by bulk copy.
-//   warp 1      TMEM owner and MMA issuer: tcgen05.cp moves the scale chunks
-//               into TMEM, then four kind::mxf4nvf4 block16 MMAs (K = 64
-//               each) per stage accumulate into TMEM.
-//   warps 2-9   epilogue: two warps per 32-lane TMEM quadrant, alternating
-//               32-column chunks of the 128 x n accumulator; scale by the two
-//               global scales, fused activation, BF16 stores.
+//   warp 1      TMEM owner and MMA issuer: four kind::mxf4nvf4 block16 MMAs
+//               (K = 64 each) per stage accumulate into TMEM.
+//   warps 2-5   scale staging, one per 32-lane TMEM quadrant: each stage's
+//               scale chunks go from shared memory through registers into
+//               that stage's TMEM scale columns with tcgen05.st (the layout a
+//               32x128b.warpx4 tcgen05.cp would write). Done by tcgen05.cp
+//               from the MMA thread, the copies execute in the tensor pipe
+//               between the MMAs and cost about a third of its time; from
+//               these warps they overlap the MMAs.
+//   warps 8-15  epilogue: two warps per 32-lane TMEM quadrant, alternating
+//               32-column chunks of the 128 x n accumulator. Each warp drains
+//               its columns to registers, hands the TMEM buffer back, then
+//               scales by the two global scales, applies the fused
+//               activation and stores BF16.
+//   warps 6, 7  idle. The first two warpgroups give registers to the two
+//               epilogue warpgroups (setmaxnreg).
 // Weights are the M side (swap-AB): M = 128 weight rows per tile, N = the
 // expert's tokens (<= BN), so the decode regime (a few tokens per expert)
 // still uses full 128-row MMAs. Tiles are enumerated expert-major, then
@@ -48,7 +58,13 @@ constexpr int kBM = 128;          // weight rows per tile
 constexpr int kBKBytes = 128;     // K bytes per stage (256 FP4 values)
 constexpr int kChunkBytes = 512;  // one 128-row x 4-scale chunk
 constexpr int kEpiWarps = 8;      // two warps per TMEM lane quadrant
-constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kEpiWarp0 = 8;      // first epilogue warp (warpgroups 2 and 3)
+constexpr int kSfWarp0 = 2;       // scale-staging warps 2..5
+constexpr int kThreads = 512;
+// setmaxnreg split of the 64K registers: 256 x 80 + 256 x 176 = 65536
+constexpr uint32_t kRegsLow = 80;
+constexpr uint32_t kRegsEpi = 176;
+static_assert(256 * kRegsLow + 256 * kRegsEpi <= 65536, "register split");
 constexpr int kMaxSeg = 260;      // segments (local experts + shared) per launch
 
 template <int BN>
@@ -69,6 +85,7 @@ struct Cfg {
   static constexpr int kTmemCols = 512;
   static_assert(kSfBase + kStages * kStageSfCols <= kTmemCols, "TMEM budget");
   static constexpr size_t kSmem = (size_t)kStages * kStageBytes + 1024 + 256;
+  static_assert((3 * kStages + 2 * kAcc + 1) * 8 + 4 <= 256, "barrier area");
   static_assert(kSmem + 3 * 4 * (kMaxSeg + 1) <= 232448, "shared memory budget");
 };
 
@@ -116,7 +133,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                                              ~static_cast<uintptr_t>(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
   uint64_t* empty = full + C::kStages;
-  uint64_t* tfull = empty + C::kStages;
+  uint64_t* sf_ready = empty + C::kStages;
+  uint64_t* tfull = sf_ready + C::kStages;
   uint64_t* tempty = tfull + C::kAcc;
   uint64_t* drained = tempty + C::kAcc;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drained + 1);
@@ -137,6 +155,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
+      mbar_init(&sf_ready[s], 4);
     }
     for (int a = 0; a < C::kAcc; ++a) {
       mbar_init(&tfull[a], 1);
@@ -161,7 +180,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   const int total_tiles = m_tiles * s_ntp[p.nseg];
-
+  if (warp < kEpiWarp0) {
+  // the producer, MMA and staging warpgroups give registers back together
+  regs_dealloc<kRegsLow>();
   if (warp == 0) {
     // ------------------------------------------------------ TMA producer
     if (lane == 0) {
@@ -239,31 +260,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         TileInfo ti;
         if (!decode_tile(tile, m_tiles, p.nseg, BN, s_ntp, s_cnt, s_start, ti)) continue;
         const uint32_t n_mma = (uint32_t)((ti.n_valid + 7) / 8 * 8);
-        const int sfb_ch = ti.n_valid > 128 ? 2 : 1;
         const uint32_t idesc = idesc_fp4(kBM, n_mma, 0, 0, 0);
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, p.err)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int ks = 0; ks < ks_count; ++ks) {
-          if (!mbar_wait(&full[stage], phase, p.err)) {
+          // operands landed (full) and this stage's scales are in TMEM
+          if (!mbar_wait(&full[stage], phase, p.err) ||
+              !mbar_wait(&sf_ready[stage], phase, p.err)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint8_t* sa = smem + stage * C::kStageBytes;
           const uint8_t* sb = sa + C::kABytes;
-          const uint8_t* ssfa = sb + C::kBBytes;
-          const uint8_t* ssfb = ssfa + C::kSfaBytes;
           const uint32_t sfa_col = tmem_base + C::kSfBase + stage * C::kStageSfCols;
           const uint32_t sfb_col = sfa_col + C::kSfaCols;
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-            tmem_cp_sf(sfa_col + 4 * c, desc_sf_chunk(smem_u32(ssfa + c * kChunkBytes)));
-          for (int h = 0; h < sfb_ch; ++h)
-#pragma unroll
-            for (int c = 0; c < 4; ++c)
-              tmem_cp_sf(sfb_col + 4 * C::kSfbCh * c + 4 * h,
-                         desc_sf_chunk(smem_u32(ssfb + h * 4 * kChunkBytes + c * kChunkBytes)));
           const uint32_t a_addr = smem_u32(sa), b_addr = smem_u32(sb);
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
@@ -289,10 +301,68 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(drained, 0, p.err);
     }
     __syncwarp();
+  } else if (warp < kSfWarp0 + 4) {
+    // ------------------------------------------------------ scale staging
+    // Lane l of the warp owning quadrant q writes, for every scale chunk of
+    // the stage, the chunk's 16 bytes at l * 16 into four consecutive TMEM
+    // columns of lane 32q + l: the layout tcgen05.cp.32x128b.warpx4 writes
+    // (every quadrant gets the same 32 x 16 bytes).
+    const int q = warp & 3;
+    const uint32_t t_lane = tmem_base + ((uint32_t)(32 * q) << 16);
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+      TileInfo ti;
+      if (!decode_tile(tile, m_tiles, p.nseg, BN, s_ntp, s_cnt, s_start, ti)) continue;
+      const bool two_blocks = ti.n_valid > 128;
+      for (int ks = 0; ks < ks_count; ++ks) {
+        if (!mbar_wait(&full[stage], phase, p.err)) {
+          ok = false;
+          break;
+        }
+        const uint8_t* ssfa = smem + stage * C::kStageBytes + C::kABytes + C::kBBytes;
+        const uint8_t* ssfb = ssfa + C::kSfaBytes;
+        const uint32_t sfa_col = C::kSfBase + stage * C::kStageSfCols;
+        const uint32_t sfb_col = sfa_col + C::kSfaCols;
+        uint32_t r[16];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const uint4 v = *reinterpret_cast<const uint4*>(ssfa + c * kChunkBytes + lane * 16);
+          r[4 * c] = v.x; r[4 * c + 1] = v.y; r[4 * c + 2] = v.z; r[4 * c + 3] = v.w;
+        }
+        tmem_st_32x32b_x16(t_lane + sfa_col, r);
+        // SFB column 4 * kSfbCh * c + 4 * h holds chunk (128-row block h, K chunk c)
+#pragma unroll
+        for (int part = 0; part < C::kSfbCh; ++part) {
+          uint32_t rb[16];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int col = 4 * j + 16 * part;  // first column of this group
+            const int c = col / (4 * C::kSfbCh), h = (col / 4) % C::kSfbCh;
+            uint4 v = make_uint4(0u, 0u, 0u, 0u);
+            if (h == 0 || two_blocks)
+              v = *reinterpret_cast<const uint4*>(ssfb + (h * 4 + c) * kChunkBytes + lane * 16);
+            rb[4 * j] = v.x; rb[4 * j + 1] = v.y; rb[4 * j + 2] = v.z; rb[4 * j + 3] = v.w;
+          }
+          tmem_st_32x32b_x16(t_lane + sfb_col + 16 * part, rb);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sf_ready[stage]);
+        if (++stage == C::kStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  }
   } else {
     // ------------------------------------------------------ epilogue
-    const int q = warp & 3;                // TMEM lane quadrant this warp may access
-    const int half = (warp - 2) >> 2;      // which alternate 32-column chunks
+    regs_alloc<kRegsEpi>();
+    const int q = warp & 3;                         // TMEM lane quadrant this warp may access
+    const int half = (warp - kEpiWarp0) >> 2;       // which alternate 32-column chunks
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
@@ -301,6 +371,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(&tfull[acc], acc_phase, p.err)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(32 * q) << 16) + acc * BN;
+      // Drain this warp's columns of the accumulator into registers and hand
+      // the TMEM buffer back before any math or store, so the next tile's
+      // MMAs overlap this tile's epilogue even with a single buffer.
+      constexpr int kChunks = (BN + 63) / 64;
+      uint32_t v[kChunks][32];
+#pragma unroll
+      for (int i = 0; i < kChunks; ++i)
+        if (32 * half + 64 * i < ti.n_valid) tmem_ld_32x32b_x32(t_row + 32 * half + 64 * i, v[i]);
+      tmem_ld_wait();
+#pragma unroll
+      for (int i = 0; i < kChunks; ++i) reg_fence(v[i]);
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
       const float bscale = p.b_global[ti.seg];
       if (EPI == 0) {
         // Rows 32q..32q+15 of the tile are gate rows, 32q+16..32q+31 the
@@ -312,16 +395,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int j = ti.m_tile * (kBM / 2) + 16 * q + (lane & 15);
         const int hcols = p.M_per / 2;
         float amax = 0.0f;
-        for (int c0 = 32 * half; c0 < ti.n_valid; c0 += 64) {
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(t_row + c0, v);
-          tmem_ld_wait(v);
+#pragma unroll
+        for (int ch = 0; ch < kChunks; ++ch) {
+          const int c0 = 32 * half + 64 * ch;
+          if (c0 >= ti.n_valid) break;
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const float send = __uint_as_float(lo ? v[i + 16] : v[i]);
+            const float send = __uint_as_float(lo ? v[ch][i + 16] : v[ch][i]);
             const float recv = __shfl_xor_sync(0xffffffffu, send, 16);
-            const float gate = lo ? __uint_as_float(v[i]) * s_gate : recv * s_gate;
-            const float up = lo ? recv * s_up : __uint_as_float(v[i + 16]) * s_up;
+            const float gate = lo ? __uint_as_float(v[ch][i]) * s_gate : recv * s_gate;
+            const float up = lo ? recv * s_up : __uint_as_float(v[ch][i + 16]) * s_up;
             const int col = c0 + i + (lo ? 0 : 16);
             if (col < ti.n_valid) {
               const float h = __fdividef(gate, 1.0f + __expf(-gate)) * up;
@@ -337,22 +420,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else {
         const float scale = bscale * p.a_global[ti.seg];
         const int o = ti.m_tile * kBM + 32 * q + lane;
-        for (int c0 = 32 * half; c0 < ti.n_valid; c0 += 64) {
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(t_row + c0, v);
+#pragma unroll
+        for (int ch = 0; ch < kChunks; ++ch) {
+          const int c0 = 32 * half + 64 * ch;
+          if (c0 >= ti.n_valid) break;
           const float wmine =
               c0 + lane < ti.n_valid ? p.row_weight[ti.row_start + c0 + lane] * scale : 0.0f;
-          tmem_ld_wait(v);
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const float w = __shfl_sync(0xffffffffu, wmine, i);
             if (c0 + i < ti.n_valid)
-              p.out[(size_t)(ti.row_start + c0 + i) * p.M_per + o] = f2bf(__uint_as_float(v[i]) * w);
+              p.out[(size_t)(ti.row_start + c0 + i) * p.M_per + o] =
+                  f2bf(__uint_as_float(v[ch][i]) * w);
           }
         }
       }
-      tc_fence_before();
-      mbar_arrive(&tempty[acc]);
       if (++acc == C::kAcc) {
         acc = 0;
         acc_phase ^= 1u;
@@ -373,6 +455,12 @@ cudaError_t launch_impl(const CUtensorMap* ta, const CUtensorMap* tb, const Gemm
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)Cfg<BN>::kSmem);
   if (e != cudaSuccess) return e;
+  // setmaxnreg.inc waits until the block's launch registers cover the split;
+  // refuse a build whose launch register count could not.
+  cudaFuncAttributes fa{};
+  e = cudaFuncGetAttributes(&fa, kern);
+  if (e != cudaSuccess) return e;
+  if ((size_t)fa.numRegs * kThreads < 256u * (kRegsLow + kRegsEpi)) return cudaErrorInvalidConfiguration;
   kern<<<num_sms, kThreads, Cfg<BN>::kSmem, st>>>(*ta, tb[0], tb[1], tb[2], p);
   return cudaGetLastError();
 }

@@ -167,7 +167,7 @@ struct glm5x_moe {
   CUtensorMap tm_router{};
   CUtensorMap tm_w13_sf{}, tm_w2_sf{}, tm_act_sf{}, tm_h_sf{};
   int pair_grid = 0;       // CTAs for the pair GEMM (0 = unavailable)
-  bool use_pair = true;    // 256-row token tiles on CTA pairs
+  bool use_pair = false;   // 256-row token tiles on CTA pairs (opt-in: slower than single CTAs)
   CUtensorMap tm_act[4]{}, tm_h[4]{};  // box rows 32, 64, 128, 256
 
   glm5x_status fail(glm5x_status st, const char* fmt, ...) {
