@@ -917,6 +917,7 @@ glm5x_status glm5x_nvfp4_quantize_slabs_bf16(const uint16_t* src, int64_t cols,
   cudaFree(tok_amax);
   cudaFree(seg_amax);
   cudaFree(qp);
+  cudaFree(err);
   return s;
 }
 

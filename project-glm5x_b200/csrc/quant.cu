@@ -116,6 +116,103 @@ __global__ void nvfp4_quantize_matrix_kernel(const T* __restrict__ src, int64_t 
 // reads zeros. Source rows are gathered by row_token (a token index into src).
 // seg_amax[s] = max |x| over the segment's gathered rows; seg_global[s] is
 // written here. One warp per row; K must be a multiple of 512.
+// E2M1 codes of eight values (already divided by the block's scale), packed
+// two per byte with the first value in the low nibble, by the hardware
+// converter (round to nearest even, saturating at 6).
+__device__ __forceinline__ uint32_t e2m1x8_rn(const float* q) {
+  uint32_t r;
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n\t"
+      "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
+      : "=r"(r)
+      : "f"(q[0]), "f"(q[1]), "f"(q[2]), "f"(q[3]), "f"(q[4]), "f"(q[5]), "f"(q[6]), "f"(q[7]));
+  return r;
+}
+
+// Nibbles equal to 0x8 (negative zero) become 0x0 (the reference's argmin
+// picks +0, code 0, for anything that rounds to zero).
+__device__ __forceinline__ uint32_t clear_negative_zero(uint32_t w) {
+  const uint32_t t = w ^ 0x88888888u;                              // 0 where w == 8
+  const uint32_t nz = ((t & 0x77777777u) + 0x77777777u) | t;       // bit 3: t != 0
+  return w & ~(~nz & 0x88888888u);
+}
+
+// max that returns NaN when either input is NaN (fmaxf drops NaNs)
+__device__ __forceinline__ float fmax_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+__device__ __forceinline__ float rcp_approx(float d) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(d));
+  return r;
+}
+
+// One 16-element NVFP4 block with max_abs scaling against global scale g
+// (six_g = 6 * g, rcp_six_g = rcp.approx(six_g)): writes the 8 packed bytes
+// as two words and returns the E4M3 scale byte. Bit-identical to
+// nvfp4_quantize_block(..., mse = false), i.e. to the reference's
+// scale = E4M3(clamp(bmax / (6 g))), code = argmin |RN(x / (scale * g)) - c|.
+//
+// Every quotient is first taken as RN(x * rcp.approx(divisor)), within 3 ulps
+// of the IEEE quotient. A rounding decision can only differ between the two
+// when the quotient lies within a few ulps of a decision boundary, and every
+// boundary has a run of zero low mantissa bits: E4M3 rounding midpoints (low
+// 20 bits 0x80000) for the scale, and for the codes the thresholds 0.25,
+// 0.75, 1.25, 1.75, 2.5, 3.5 and 5 (low 21 bits zero). Quotients within 8 bit
+// steps of such a pattern are recomputed with IEEE division; BF16 data puts
+// about 0.5% of the codes there (exact ties are common). The other codes come
+// from the hardware E2M1 converter (nearest, saturating at 6), which agrees
+// with the argmin away from ties; its -0 is mapped to +0 (code 0) like the
+// argmin. Exact zeros and non-finite values also take the IEEE path (the
+// caller's bmax must propagate NaN).
+__device__ __forceinline__ uint32_t quantize_block16(const float (&x)[16], float bmax, float g,
+                                                     float six_g, float rcp_six_g,
+                                                     uint32_t& lo32, uint32_t& hi32) {
+  float base = __fmul_rn(bmax, rcp_six_g);
+  if (((f_bits(base) + 8u - 0x80000u) & 0xfffffu) <= 16u || !(base <= 3.0e38f))
+    base = f_div(bmax, six_g);
+  base = fminf(fmaxf(base, kE4M3Tiny), kE4M3Max);
+  const uint32_t sb = e4m3_encode(base);
+  const float denom = f_mul(e4m3_decode(sb), g);
+  const float ra = rcp_approx(denom);
+  float q[16];
+  bool any_near = !(bmax <= 3.0e38f);  // bmax is NaN-propagating: NaN / Inf input
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    q[i] = __fmul_rn(x[i], ra);
+    any_near |= ((f_bits(q[i]) + 8u) & 0x1fffffu) <= 16u;  // the sign bit does not matter
+  }
+  lo32 = clear_negative_zero(e2m1x8_rn(q));
+  hi32 = clear_negative_zero(e2m1x8_rn(q + 8));
+  if (!any_near) return sb;
+  uint32_t near = 0;
+  if (!(bmax <= 3.0e38f)) {
+    near = 0xffffu;
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) near |= (((f_bits(q[i]) + 8u) & 0x1fffffu) <= 16u ? 1u : 0u) << i;
+  }
+  while (near) {
+    const int i = __ffs(near) - 1;
+    near &= near - 1;
+    float xi = x[0];  // x[i] without dynamic indexing (keeps x in registers)
+#pragma unroll
+    for (int k = 1; k < 16; ++k) xi = k == i ? x[k] : xi;
+    const uint32_t code = e2m1_encode(f_div(xi, denom));
+    if (i < 8)
+      lo32 = (lo32 & ~(0xfu << (4 * i))) | (code << (4 * i));
+    else
+      hi32 = (hi32 & ~(0xfu << (4 * (i - 8)))) | (code << (4 * (i - 8)));
+  }
+  return sb;
+}
+
 __global__ void nvfp4_quantize_segments_kernel(
     const uint16_t* __restrict__ src, int K, const int32_t* __restrict__ row_token,
     const int32_t* __restrict__ seg_start, const int32_t* __restrict__ seg_count,
@@ -149,6 +246,11 @@ __global__ void nvfp4_quantize_segments_kernel(
   const int64_t t = row_token ? row_token[row] : row;
   const uint16_t* xrow = src + t * (int64_t)K;
   const float six_g = f_mul(kFp4Max, g);
+  const float rcp_six_g = rcp_approx(six_g);
+  // nb a multiple of 32: every lane runs every iteration, and lanes 4j..4j+3
+  // hold the four scales of one 32-bit word of the blocked layout
+  const bool word_scales =
+      (nb & 31) == 0 && (reinterpret_cast<uintptr_t>(scales_blocked) & 3) == 0;
   for (int b = lane_id(); b < nb; b += 32) {
     const uint4* q = reinterpret_cast<const uint4*>(xrow + b * 16);
     const uint4 v0 = __ldg(q), v1 = __ldg(q + 1);
@@ -159,21 +261,108 @@ __global__ void nvfp4_quantize_segments_kernel(
     for (int j = 0; j < 8; ++j) {
       x[2 * j] = __uint_as_float(w[j] << 16);
       x[2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
-      bmax = fmaxf(bmax, fmaxf(fabsf(x[2 * j]), fabsf(x[2 * j + 1])));
+      bmax = fmax_nan(bmax, fmax_nan(fabsf(x[2 * j]), fabsf(x[2 * j + 1])));
     }
-    float base = f_div(bmax, six_g);
-    base = fminf(fmaxf(base, kE4M3Tiny), kE4M3Max);
-    const uint32_t sb = e4m3_encode(base);
-    const float denom = f_mul(e4m3_decode(sb), g);
-    const float rcp = f_rcp(denom);
-    uint32_t lo32 = 0, hi32 = 0;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) lo32 |= e2m1_encode(ratio_for_code(x[i], denom, rcp)) << (4 * i);
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-      hi32 |= e2m1_encode(ratio_for_code(x[8 + i], denom, rcp)) << (4 * i);
+    uint32_t lo32, hi32;
+    const uint32_t sb = quantize_block16(x, bmax, g, six_g, rcp_six_g, lo32, hi32);
     *reinterpret_cast<uint2*>(prow + b * 8) = make_uint2(lo32, hi32);
-    scales_blocked[blocked_sf_offset(row, b, nb)] = static_cast<uint8_t>(sb);
+    if (word_scales) {
+      uint32_t sw = sb << (8 * (b & 3));
+      sw |= __shfl_xor_sync(0xffffffffu, sw, 1);
+      sw |= __shfl_xor_sync(0xffffffffu, sw, 2);
+      if ((b & 3) == 0)
+        *reinterpret_cast<uint32_t*>(scales_blocked + blocked_sf_offset(row, b, nb)) = sw;
+    } else {
+      scales_blocked[blocked_sf_offset(row, b, nb)] = static_cast<uint8_t>(sb);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ MXFP4 terms
+// Four-term MXFP4 expansion of expert-major rows for the MXFP4 expert path.
+// The reference runs MXFP4 experts on decoded weights with BF16/FP32
+// activations (reference/glm5x_ref/layer10_moe.py:572-593, runtime/src/
+// backend_cpu.cpp:197-270); the FP4 tensor cores need FP4 on both sides, so
+// every activation row x becomes four MXFP4 rows q_0..q_3 with
+// q_j = MXFP4(x - q_0 - ... - q_{j-1}) (E2M1 codes, one E8M0 scale per 32,
+// scale = the smallest power of two with max|residual| <= 6 * scale).
+// sum_j q_j matches x to about 4e-5 relative, so the GEMM reproduces the
+// reference's FP32-activation products within its tolerance.
+// Segments hold 4 rows per token (row 4q + j of the segment is term j of its
+// q-th token, placed with segment_row); token slot f of qprefix maps to one
+// token, slots past the segment's tokens are zero-filled. Source rows are
+// row_token[term-0 row], or the term-0 row itself when row_token is null.
+// One warp per token; K must be a multiple of 1024.
+__global__ void mxfp4_terms_segments_kernel(
+    const uint16_t* __restrict__ src, int K, const int32_t* __restrict__ row_token,
+    const int32_t* __restrict__ seg_start, const int32_t* __restrict__ seg_count,
+    const int32_t* __restrict__ qprefix, int nseg, int bn, uint8_t* __restrict__ packed,
+    uint8_t* __restrict__ scales_blocked) {
+  const int warps = blockDim.x / 32;
+  const int64_t f = blockIdx.x * (int64_t)warps + threadIdx.x / 32;
+  if (f >= qprefix[nseg]) return;
+  int lo = 0, hi = nseg;
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (qprefix[mid] <= f) lo = mid; else hi = mid;
+  }
+  const int s = lo;
+  const int r = static_cast<int>(f - qprefix[s]);  // token slot in the segment
+  const int ng = K / 32;
+  int64_t rows[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) rows[j] = seg_start[s] + segment_row(4 * r + j, bn);
+  if (4 * r >= seg_count[s]) {
+    for (int g = lane_id(); g < ng; g += 32)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        *reinterpret_cast<uint4*>(packed + rows[j] * (K / 2) + g * 16) = make_uint4(0, 0, 0, 0);
+        scales_blocked[blocked_sf_offset(rows[j], g, ng)] = 0;
+      }
+    return;
+  }
+  const int64_t t = row_token ? row_token[rows[0]] : rows[0];
+  const uint16_t* xrow = src + t * (int64_t)K;
+  for (int g = lane_id(); g < ng; g += 32) {
+    const uint4* qv = reinterpret_cast<const uint4*>(xrow + g * 32);
+    float res[32];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const uint4 v = __ldg(qv + u);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        res[8 * u + 2 * i] = __uint_as_float(w[i] << 16);
+        res[8 * u + 2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float m = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) m = fmaxf(m, fabsf(res[i]));
+      // smallest e with m <= 6 * 2^e: e = ceil(log2(m / 6)) from the bits
+      int e = -127;
+      if (m > 0.0f) {
+        const uint32_t qb = __float_as_uint(m / 6.0f);
+        const int ex = (int)(qb >> 23) - 127;
+        e = ex + ((qb & 0x7fffffu) != 0u ? 1 : 0);
+        if (ex == -127) e = -126;  // subnormal quotient
+        e = e < -127 ? -127 : (e > 127 ? 127 : e);
+      }
+      const float scale = pow2f(e);
+      const float inv = e == -127 ? 0.0f : pow2f(-e);
+      uint32_t word[4] = {0, 0, 0, 0};
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const uint32_t c = e == -127 ? 0u : e2m1_encode(res[i] * inv);
+        word[i / 8] |= c << (4 * (i % 8));
+        res[i] -= e2m1_value(c) * scale;
+      }
+      *reinterpret_cast<uint4*>(packed + rows[j] * (K / 2) + g * 16) =
+          make_uint4(word[0], word[1], word[2], word[3]);
+      scales_blocked[blocked_sf_offset(rows[j], g, ng)] = static_cast<uint8_t>(e + 127);
+    }
   }
 }
 
@@ -303,6 +492,18 @@ cudaError_t launch_nvfp4_quantize_segments(const uint16_t* src, int K, const int
   nvfp4_quantize_segments_kernel<<<(unsigned)((max_rows + warps - 1) / warps), warps * 32, 0,
                                    st>>>(src, K, row_token, seg_start, seg_count, qprefix, nseg,
                                          bn, seg_amax, packed, scales_blocked, seg_global);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_mxfp4_terms_segments(const uint16_t* src, int K, const int32_t* row_token,
+                                        const int32_t* seg_start, const int32_t* seg_count,
+                                        const int32_t* qprefix, int nseg, int bn,
+                                        int64_t max_slots, uint8_t* packed,
+                                        uint8_t* scales_blocked, cudaStream_t st) {
+  if (max_slots <= 0) return cudaSuccess;
+  const int warps = 8;
+  mxfp4_terms_segments_kernel<<<(unsigned)((max_slots + warps - 1) / warps), warps * 32, 0, st>>>(
+      src, K, row_token, seg_start, seg_count, qprefix, nseg, bn, packed, scales_blocked);
   return cudaGetLastError();
 }
 

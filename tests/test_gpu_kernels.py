@@ -138,18 +138,44 @@ def test_gpu_expert_major_plan(T, E, k):
     assert np.array_equal(rt_h[valid], tok[valid])
 
 
-def test_gpu_slab_quantize_matches_oracle():
+def _tie_hidden(T, K, rng):
+    """BF16 rows whose slab amax is 2688 (global scale exactly 1) and whose
+    16-blocks have dyadic maxima, so values divided by their block scale land
+    exactly on the E2M1 decision thresholds (0.25, 0.75, ..., 5) where the
+    reference's argmin (ties to the lower code) and round-to-nearest-even
+    differ, plus signed zeros and saturating values."""
+    vals = np.array([0.0, -0.0, 0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0, 6.0, 0.5, 1.0, 3.0,
+                     0.125, 0.7, 1.8, 4.5, 5.5], dtype=np.float32)
+    x = rng.choice(vals, size=(T, K // 16, 16)) * rng.choice([-1.0, 1.0], size=(T, K // 16, 16))
+    x[:, :, 0] = 6.0  # block max 6 * 2^j below: the E4M3 block scale is 2^j exactly
+    x *= (2.0 ** rng.integers(-3, 4, size=(T, K // 16, 1))).astype(np.float32)
+    x = x.reshape(T, K)
+    x[:, 7] = 2688.0  # every token (so every slab) has amax 2688
+    return torch.from_numpy(x.astype(np.float32)).to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("kind,K,misalign", [("random", 6144, 0), ("ties", 512, 0),
+                                             ("ties", 2048, 1)])
+def test_gpu_slab_quantize_matches_oracle(kind, K, misalign):
+    """Expert-major slab quantization (the activation / intermediate quantizer
+    of the forward path) is bit-exact against the oracle, on random data and
+    on data built to hit every E2M1 tie; misalign=1 offsets the scale buffer
+    by one byte (byte-wise scale stores)."""
     from glm5x_moe import _native as N
     rng = np.random.default_rng(8)
-    T, E, k, K = 96, 16, 4, 6144
-    hidden = torch.randn(T, K, generator=torch.Generator().manual_seed(8)).to(torch.bfloat16)
-    hidden[3] *= 40  # one loud token changes its slabs' global scales
+    T, E, k = 96, 16, 4
+    if kind == "random":
+        hidden = torch.randn(T, K, generator=torch.Generator().manual_seed(8)).to(torch.bfloat16)
+        hidden[3] *= 40  # one loud token changes its slabs' global scales
+    else:
+        hidden = _tie_hidden(T, K, rng)
     ids = np.stack([rng.permutation(E)[:k] for _ in range(T)]).astype(np.int32)
     counts, starts, tok, slot, pos = O.expert_major_layout(ids, E, align=128)
     rows = int(starts[-1] + (counts[-1] + 127) // 128 * 128)
     hd = hidden.cuda()
     packed = torch.zeros((rows, K // 2), dtype=torch.uint8, device="cuda")
-    scales = torch.zeros(O.blocked_size(rows, K // 16), dtype=torch.uint8, device="cuda")
+    scales_buf = torch.zeros(O.blocked_size(rows, K // 16) + 16, dtype=torch.uint8, device="cuda")
+    scales = scales_buf[misalign:misalign + O.blocked_size(rows, K // 16)]
     gl = torch.zeros(E, dtype=torch.float32, device="cuda")
     rt = torch.from_numpy(np.where(tok >= 0, tok, 0).astype(np.int32)).cuda()
     # keep every device tensor referenced until the call returns
