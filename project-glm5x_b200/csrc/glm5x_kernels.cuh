@@ -39,6 +39,12 @@ cudaError_t launch_nvfp4_quantize_segments(const uint16_t* src, int K, const int
                                            const float* seg_amax, int64_t max_rows,
                                            uint8_t* packed, uint8_t* scales_blocked,
                                            float* seg_global, cudaStream_t st);
+// Four-term MXFP4 expansion of expert-major rows (4 operand rows per token).
+cudaError_t launch_mxfp4_terms_segments(const uint16_t* src, int K, const int32_t* row_token,
+                                        const int32_t* seg_start, const int32_t* seg_count,
+                                        const int32_t* qprefix, int nseg, int bn,
+                                        int64_t max_slots, uint8_t* packed,
+                                        uint8_t* scales_blocked, cudaStream_t st);
 cudaError_t launch_nvfp4_dequantize(const uint8_t* packed, const uint8_t* scales_blocked,
                                     float g, int64_t rows, int64_t cols, float* out,
                                     cudaStream_t st);
@@ -66,9 +72,11 @@ struct PermuteBuffers {
 cudaError_t launch_topk(const float* in, int values_are_scores, const float* bias, int T, int E,
                         int k, float routed_scale, int32_t* ids, float* weights, uint32_t* err,
                         cudaStream_t st);
+// rows_per: operand rows per (token, slot) -- 1 for NVFP4, 4 for the MXFP4
+// four-term activation expansion (pos and row_token refer to the first).
 cudaError_t launch_permute(const int32_t* ids, const float* weights, const float* token_amax,
                            int T, int k, int E, int has_shared, int bn, PermuteBuffers b,
-                           uint32_t* err, cudaStream_t st);
+                           uint32_t* err, cudaStream_t st, int rows_per = 1);
 
 // ------------------------------------------------------------ router_tc.cu
 // BF16 router logits on tcgen05 + sigmoid/bias/top-k epilogue. tmap_x: hidden

@@ -172,7 +172,8 @@ __device__ int block_exclusive_scan(int v, int* buf, int* total) {
 // quantizer row prefix (counts rounded up to 8) and the GEMM N-tile prefix,
 // and clears the per-segment amax accumulators.
 __global__ void permute_scan_kernel(int32_t* __restrict__ chunk_count, int nchunks, int T, int E,
-                                    int has_shared, int bn, int32_t* __restrict__ seg_count,
+                                    int has_shared, int bn, int rows_per,
+                                    int32_t* __restrict__ seg_count,
                                     int32_t* __restrict__ seg_start,
                                     int32_t* __restrict__ qprefix,
                                     int32_t* __restrict__ ntile_prefix,
@@ -191,15 +192,19 @@ __global__ void permute_scan_kernel(int32_t* __restrict__ chunk_count, int nchun
     count = T;
   }
   const bool valid = e < nseg;
+  // every (token, slot) takes rows_per operand rows (4 for the MXFP4 term
+  // expansion); segment counts, starts and tiles are in rows, the quantizer
+  // prefix in groups of rows_per rows (the rows rounded up to 8)
+  const int rows = count * rows_per;
   int tot;
-  const int start = block_exclusive_scan(valid ? segment_rows(count, bn) : 0, scan_buf, &tot);
-  const int q = block_exclusive_scan(valid ? (count + 7) / 8 * 8 : 0, scan_buf, &tot);
+  const int start = block_exclusive_scan(valid ? segment_rows(rows, bn) : 0, scan_buf, &tot);
+  const int q = block_exclusive_scan(valid ? (rows + 7) / 8 * 8 / rows_per : 0, scan_buf, &tot);
   const int qt = tot;
-  // N tiles: 128-row aligned chunks of at most bn rows
-  const int nt = valid ? (count + bn - 1) / bn : 0;
+  // N tiles of at most bn rows
+  const int nt = valid ? (rows + bn - 1) / bn : 0;
   const int tp = block_exclusive_scan(nt, scan_buf, &tot);
   if (valid) {
-    seg_count[e] = count;
+    seg_count[e] = rows;
     seg_start[e] = start;
     qprefix[e] = q;
     ntile_prefix[e] = tp;
@@ -211,13 +216,13 @@ __global__ void permute_scan_kernel(int32_t* __restrict__ chunk_count, int nchun
     ntile_prefix[nseg] = tot;
   }
   __syncthreads();
-  if (e == nseg - 1) seg_start[nseg] = start + segment_rows(count, bn);
+  if (e == nseg - 1) seg_start[nseg] = start + segment_rows(rows, bn);
 }
 
 // One thread per (token, slot) pair, plus one per token for the shared expert.
 __global__ void permute_scatter_kernel(const int32_t* __restrict__ ids,
                                        const float* __restrict__ weights, int T, int k, int E,
-                                       int has_shared, int bn,
+                                       int has_shared, int bn, int rows_per,
                                        const int32_t* __restrict__ chunk_base,
                                        const int32_t* __restrict__ rank,
                                        const int32_t* __restrict__ seg_start,
@@ -234,12 +239,13 @@ __global__ void permute_scatter_kernel(const int32_t* __restrict__ ids,
   if (s < k) {
     e = ids[(int64_t)t * k + s];
     e = e < 0 || e >= E ? 0 : e;
-    p = seg_start[e] +
-        segment_row(chunk_base[(int64_t)(t / kChunk) * E + e] + rank[(int64_t)t * k + s], bn);
+    p = seg_start[e] + segment_row(rows_per * (chunk_base[(int64_t)(t / kChunk) * E + e] +
+                                               rank[(int64_t)t * k + s]),
+                                   bn);
     w = weights[(int64_t)t * k + s];
   } else {
     e = E;
-    p = seg_start[E] + segment_row(t, bn);
+    p = seg_start[E] + segment_row(rows_per * t, bn);
     w = 1.0f;
   }
   pos[idx] = p;
@@ -261,7 +267,7 @@ cudaError_t launch_topk(const float* in, int values_are_scores, const float* bia
 
 cudaError_t launch_permute(const int32_t* ids, const float* weights, const float* token_amax,
                            int T, int k, int E, int has_shared, int bn, PermuteBuffers b,
-                           uint32_t* err, cudaStream_t st) {
+                           uint32_t* err, cudaStream_t st, int rows_per) {
   const int nchunks = (T + kChunk - 1) / kChunk;
   if (T > 0) {
     permute_count_kernel<<<nchunks, kChunk, 0, st>>>(ids, T, k, E, b.chunk_count, b.rank, err);
@@ -270,12 +276,13 @@ cudaError_t launch_permute(const int32_t* ids, const float* weights, const float
   int threads = 32;
   while (threads < nseg + 1) threads <<= 1;
   permute_scan_kernel<<<1, threads, threads * sizeof(int), st>>>(
-      b.chunk_count, nchunks, T, E, has_shared, bn, b.seg_count, b.seg_start, b.qprefix,
+      b.chunk_count, nchunks, T, E, has_shared, bn, rows_per, b.seg_count, b.seg_start, b.qprefix,
       b.ntile_prefix, b.seg_amax, b.h_amax);
   const int64_t n = (int64_t)T * (k + has_shared);
   if (n > 0) {
     permute_scatter_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(
-        ids, weights, T, k, E, has_shared, bn, b.chunk_count, b.rank, b.seg_start, token_amax, b.pos,
+        ids, weights, T, k, E, has_shared, bn, rows_per, b.chunk_count, b.rank, b.seg_start,
+        token_amax, b.pos,
         b.row_token, b.row_weight, b.seg_amax);
   }
   return cudaGetLastError();
