@@ -63,20 +63,74 @@ def peaks() -> dict:
     return {"hbm_gbs": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "source": "fallback"}
 
 
+def library_nvfp4_tflops(m: int, n: int, k: int, device, iters: int = 10) -> float | None:
+    """Dense cuBLASLt NVFP4 GEMM (torch._scaled_mm, block-16 E4M3 scales) of
+    shape m x n x k on random codes: the library's rate for the same FLOPs as
+    the grouped gate/up GEMM, a measured tensor-core denominator."""
+    import torch
+    try:
+        a = torch.randint(0, 256, (m, k // 2), dtype=torch.uint8, device=device)
+        b = torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, device=device)
+        rup = lambda x, r: (x + r - 1) // r * r
+        sa = torch.randint(0x30, 0x40, (rup(m, 128) * rup(k // 16, 4),), dtype=torch.uint8,
+                           device=device).view(torch.float8_e4m3fn)
+        sb = torch.randint(0x30, 0x40, (rup(n, 128) * rup(k // 16, 4),), dtype=torch.uint8,
+                           device=device).view(torch.float8_e4m3fn)
+        fa, fb = a.view(torch.float4_e2m1fn_x2), b.view(torch.float4_e2m1fn_x2).t()
+        run = lambda: torch._scaled_mm(fa, fb, scale_a=sa, scale_b=sb, out_dtype=torch.bfloat16)
+        for _ in range(3):
+            run()
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(iters):
+            run()
+        e1.record()
+        torch.cuda.synchronize(device)
+        ms = e0.elapsed_time(e1) / iters
+        del a, b, sa, sb
+        torch.cuda.empty_cache()
+        return 2.0 * m * n * k / (ms / 1000.0) / 1e12
+    except Exception:
+        return None
+
+
 # ---------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi clocks/throttle sampling during the timed region."""
+    """SM clock and clock-event (throttle) reasons sampled during the timed
+    region: NVML polled every 5 ms from a thread (reads only), else
+    nvidia-smi at its 200 ms minimum interval."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clock-event reason bits
+    REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+               "hw_thermal_slowdown": 0x40}
 
     def __init__(self, index: int) -> None:
         self.index = index
         self.proc = None
         self.lines: list[str] = []
+        self.samples: list[tuple[float, int]] = []
+        self.max_mhz = None
+        self.nvml = None
+        self._stop = threading.Event()
 
     def __enter__(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            get_reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+            self.nvml = (pynvml, h, get_reasons)
+            self._t = threading.Thread(target=self._poll, daemon=True)
+            self._t.start()
+            return self
+        except Exception:
+            self.nvml = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
@@ -88,11 +142,24 @@ class ClockSampler:
             self.proc = None
         return self
 
+    def _poll(self):
+        pynvml, h, get_reasons = self.nvml
+        while not self._stop.is_set():
+            try:
+                self.samples.append((float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)),
+                                     int(get_reasons(h))))
+            except Exception:
+                return
+            time.sleep(0.005)
+
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
     def __exit__(self, *exc):
+        self._stop.set()
+        if self.nvml:
+            self._t.join(timeout=1)
         if self.proc:
             self.proc.terminate()
             try:
@@ -101,22 +168,29 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self) -> dict:
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            f = [x.strip() for x in ln.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            for i, n in enumerate(names):
-                if f[5 + i].lower() == "active":
-                    reasons.add(n)
+        sm, mx, reasons = [], self.max_mhz, set()
+        if self.nvml:
+            for mhz, bits in self.samples:
+                sm.append(mhz)
+                reasons.update(n for n, b in self.REASONS.items() if bits & b)
+            src = "nvml 5 ms"
+        else:
+            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+            for ln in self.lines:
+                f = [x.strip() for x in ln.split(",")]
+                if len(f) < 9:
+                    continue
+                try:
+                    sm.append(float(f[1]))
+                    mx = float(f[2])
+                except ValueError:
+                    continue
+                for i, n in enumerate(names):
+                    if f[5 + i].lower() == "active":
+                        reasons.add(n)
+            src = "nvidia-smi 200 ms"
         return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "source": src}
 
 
 # ---------------------------------------------------------------- inputs
@@ -262,7 +336,10 @@ def run_ours(args) -> None:
         layer(hidden, want_routing=False)
     torch.cuda.synchronize()
     stats0 = layer.stats()
-    layer.set_profiling(False)
+    # phase events (CUDA events on the forward's own stream between its
+    # kernels) are recorded during the timed steps themselves
+    layer.set_profiling(True)
+    layer.phase_times()  # drop warm-up samples
     if pg:
         pg.barrier()
     torch.cuda.synchronize()
@@ -278,20 +355,15 @@ def run_ours(args) -> None:
     layer.check()
     ms_total = start.elapsed_time(stop)
     launches = layer.stats()["kernel_launches"] - stats0["kernel_launches"]
+    phases, nprof = layer.phase_times()
+    layer.set_profiling(False)
+    phases = {k: v / max(nprof, 1) for k, v in phases.items()}
     if pg:
         t = torch.tensor([ms_total], device=dev)
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
         ms_total = float(t.item())
     ms_step = ms_total / args.steps
     value = world * T * args.steps / (ms_total / 1000.0)
-
-    # per-phase device times (CUDA events on the forward's stream)
-    layer.set_profiling(True)
-    for _ in range(args.steps):
-        layer(hidden, want_routing=False)
-    phases, nprof = layer.phase_times()
-    layer.set_profiling(False)
-    phases = {k: v / max(nprof, 1) for k, v in phases.items()}
 
     # end to end through the C ABI with host buffers (pinned): H2D + forward + D2H
     hid_host = hidden.cpu().pin_memory()
@@ -328,6 +400,7 @@ def run_ours(args) -> None:
             except Exception:
                 traffic = None
         layer_flop = T * (9 * FLOP_PER_TOKEN_EXPERT + ROUTER_FLOP_PER_TOKEN)
+        lib_tf = None if args.no_library_gemm else library_nvfp4_tflops(assignments, 2 * I, H, dev)
         line = {
             "metric": "NVFP4 MoE-layer tokens/s", "value": value, "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -349,7 +422,11 @@ def run_ours(args) -> None:
                          "frac": achieved / fp4_peak, "traffic": traffic,
                          "peak_source": f"4 x bf16_tflops_sustained of {pk['source']} "
                                         "MEASURED_PEAKS.json (dense FP4:BF16 rate 4:1)",
-                         "frac_of_nominal_9pf": achieved / 9000.0},
+                         "frac_of_nominal_9pf": achieved / 9000.0,
+                         "library": {"kernel": f"cuBLASLt NVFP4 dense {assignments}x{2 * I}x{H} "
+                                               "(torch._scaled_mm), same FLOPs, measured here",
+                                     "tflops": lib_tf,
+                                     "frac": (achieved / lib_tf) if lib_tf else None}},
             "gpu_launches": int(launches),
             "clocks": clocks.summary(),
             "e2e": {"value": e2e_value, "unit": "tokens/s",
@@ -372,6 +449,8 @@ def main() -> None:
     ap.add_argument("--workload", default="c5", choices=["c5", "c3"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-library-gemm", action="store_true",
+                    help="skip the cuBLASLt NVFP4 reference GEMM of the roofline")
     ap.add_argument("--tokens", type=int, default=0, help="override tokens (profiling only)")
     ap.add_argument("--tile-n", type=int, default=0, help="force the GEMM token tile (tuning)")
     ap.add_argument("--pair-cta", action="store_true", help="256-row tiles on CTA pairs (tuning)")

@@ -160,8 +160,25 @@ struct glm5x_moe {
   int force_bn = 0;  // 0 = choose the token tile from the batch
   bool profiling = false;
   int profiled = 0;
-  cudaEvent_t ev[GLM5X_NUM_PHASES + 1]{};
+  // Phase events of the last kProfRing forwards: accumulated lazily (when a
+  // slot is reused or phase times are read), so profiled forwards do not wait
+  // on the device.
+  static constexpr int kProfRing = 64;
+  cudaEvent_t ev[kProfRing][GLM5X_NUM_PHASES + 1]{};
+  bool prof_pending[kProfRing]{};
+  int prof_slot = 0;
   double phase_ms[GLM5X_NUM_PHASES]{};
+  void accumulate_slot(int slot) {
+    if (!prof_pending[slot]) return;
+    cudaEventSynchronize(ev[slot][GLM5X_NUM_PHASES]);
+    for (int i = 0; i < GLM5X_NUM_PHASES; ++i) {
+      float ms = 0.0f;
+      if (cudaEventElapsedTime(&ms, ev[slot][i], ev[slot][i + 1]) == cudaSuccess)
+        phase_ms[i] += ms;
+    }
+    prof_pending[slot] = false;
+    profiled++;
+  }
 
   CUtensorMap tm_w13{}, tm_w2{};
   CUtensorMap tm_router{};
@@ -392,8 +409,9 @@ void glm5x_moe_destroy(glm5x_moe* m) {
   for (void* p : m->allocations) cudaFree(p);
   if (m->stage_w) cudaFree(m->stage_w);
   if (m->stream) cudaStreamDestroy(m->stream);
-  for (auto& e : m->ev)
-    if (e) cudaEventDestroy(e);
+  for (auto& row : m->ev)
+    for (auto& e : row)
+      if (e) cudaEventDestroy(e);
   delete m;
 }
 
@@ -562,8 +580,10 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
     bn = 128;
   }
   uint64_t launches = 0;
+  const int pslot = m->prof_slot;
+  if (m->profiling) m->accumulate_slot(pslot);  // the ring wrapped onto an unread slot
   auto mark = [&](int phase) {
-    if (m->profiling) cudaEventRecord(m->ev[phase], st);
+    if (m->profiling) cudaEventRecord(m->ev[pslot][phase], st);
   };
   mark(0);
   G5_CHECK(m, launch_row_amax_bf16(x, T, H, m->token_amax, m->err, st), "row amax");
@@ -645,13 +665,8 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
   G5_CHECK(m, launch_combine(m->y_bf16, m->pb.pos, T, m->kk(), H, out, st), "combine");
   mark(9);
   if (m->profiling) {
-    // accumulate this forward's phases (waits only on this forward's events)
-    G5_CHECK(m, cudaEventSynchronize(m->ev[9]), "profiling");
-    for (int i = 0; i < GLM5X_NUM_PHASES; ++i) {
-      float ms = 0.0f;
-      if (cudaEventElapsedTime(&ms, m->ev[i], m->ev[i + 1]) == cudaSuccess) m->phase_ms[i] += ms;
-    }
-    m->profiled++;
+    m->prof_pending[pslot] = true;
+    m->prof_slot = (pslot + 1) % glm5x_moe::kProfRing;
   }
   launches += 5;
   m->stats.forward_calls++;
@@ -764,8 +779,9 @@ glm5x_status glm5x_moe_debug_buffer(glm5x_moe* m, int32_t which, void** ptr, siz
 glm5x_status glm5x_moe_set_profiling(glm5x_moe* m, int32_t enable) {
   if (!m) return fail_global(GLM5X_INVALID_STATE, "null engine");
   cudaSetDevice(m->device);
-  if (enable && !m->ev[0]) {
-    for (auto& e : m->ev) G5_CHECK(m, cudaEventCreate(&e), "event create");
+  if (enable && !m->ev[0][0]) {
+    for (auto& row : m->ev)
+      for (auto& e : row) G5_CHECK(m, cudaEventCreate(&e), "event create");
   }
   m->profiling = enable != 0;
   return GLM5X_OK;
@@ -775,6 +791,7 @@ glm5x_status glm5x_moe_phase_times(glm5x_moe* m, float* ms, int32_t* forwards) {
   if (!m || !ms) return fail_global(GLM5X_INVALID_STATE, "null argument");
   cudaSetDevice(m->device);
   G5_CHECK(m, cudaDeviceSynchronize(), "sync");
+  for (int k = 0; k < glm5x_moe::kProfRing; ++k) m->accumulate_slot((m->prof_slot + k) % glm5x_moe::kProfRing);
   for (int i = 0; i < GLM5X_NUM_PHASES; ++i) {
     ms[i] = static_cast<float>(m->phase_ms[i]);
     m->phase_ms[i] = 0.0;
