@@ -136,11 +136,23 @@ glm5x_status glm5x_moe_load_expert_nvfp4_device(glm5x_moe* moe, int32_t expert,
                                                 const glm5x_nvfp4_matrix* gate,
                                                 const glm5x_nvfp4_matrix* up,
                                                 const glm5x_nvfp4_matrix* down);
-/* MXFP4 expert (Mxfp4MlpView, backend.hpp:154-158), host pointers. */
+/* MXFP4 expert (Mxfp4MlpView, backend.hpp:154-158), host pointers: packed
+ * [rows, cols/2] low nibble first and row-major E8M0 scales [rows, cols/32]
+ * (encode_mxfp4, k3x_ref/mxfp4.py:31-107). group_size must be 32. A 0xFF
+ * scale is rejected with GLM5X_INVALID_MXFP4 (decode_mxfp4,
+ * runtime/src/ops.cpp:40-63). The engine must be created with
+ * GLM5X_PRECISION_MXFP4; its forward feeds the experts four MXFP4 residual
+ * terms per activation row (the reference's MXFP4 path keeps activations in
+ * full precision, backend_cuda.cu:1878-2171). */
 glm5x_status glm5x_moe_load_expert_mxfp4(glm5x_moe* moe, int32_t expert,
                                          const glm5x_mxfp4_matrix* gate,
                                          const glm5x_mxfp4_matrix* up,
                                          const glm5x_mxfp4_matrix* down);
+/* Same, with the matrices already in device memory (no host staging). */
+glm5x_status glm5x_moe_load_expert_mxfp4_device(glm5x_moe* moe, int32_t expert,
+                                                const glm5x_mxfp4_matrix* gate,
+                                                const glm5x_mxfp4_matrix* up,
+                                                const glm5x_mxfp4_matrix* down);
 /* Parse and admit a .pn4 / .pm4 packed sidecar
  * (GLM5XPackedExpertCache._decode_role, packed_cache.py:407-504): header
  * "<8sII" ("GLM5XPI4", 1, json_len), sorted compact JSON, payload; CRC32C of

@@ -291,6 +291,24 @@ def nvfp4_expert_dequant_oracle(slab_bf16: np.ndarray, w13, w2) -> np.ndarray:
     return (h_deq.astype(np.float64) @ w2.astype(np.float64).T).astype(np.float32)
 
 
+def mxfp4_expert_oracle(x: np.ndarray, w13, w2) -> np.ndarray:
+    """One MXFP4 expert over token rows x [n, H] (BF16 values as FP32): the
+    reference's MXFP4 expert path restated (layer10_moe.py:571-593 decodes
+    the E2M1/E8M0 weights, mxfp4.py:110-144, and runs the expert MLP on the
+    decoded weights with unquantized activations, :711-738; the C++ MXFP4
+    grid likewise keeps activations in FP32, backend_cuda.cu:1878-2171).
+    gate/up/down products accumulate in double, h = silu(gate) * up is rounded
+    to BF16 (the reference's linear outputs are BF16).
+
+    w13: (gate_deq [I,H], up_deq [I,H]) FP32; w2: down_deq [H,I] FP32."""
+    gate_deq, up_deq = w13
+    a = np.asarray(x, dtype=np.float64)
+    gate = (a @ gate_deq.astype(np.float64).T).astype(np.float32)
+    up = (a @ up_deq.astype(np.float64).T).astype(np.float32)
+    h = bf16_round(silu(gate) * up)
+    return (h.astype(np.float64) @ w2.astype(np.float64).T).astype(np.float32)
+
+
 def relative_error(actual: np.ndarray, expected: np.ndarray) -> tuple[float, float, float]:
     """(max |a-e| / max |e|, ||a-e|| / ||e||, cosine similarity)."""
     a = np.asarray(actual, dtype=np.float64).reshape(-1)

@@ -67,19 +67,24 @@ constexpr uint32_t kRegsEpi = 176;
 static_assert(256 * kRegsLow + 256 * kRegsEpi <= 65536, "register split");
 constexpr int kMaxSeg = 260;      // segments (local experts + shared) per launch
 
-template <int BN>
+// MX = 0: NVFP4 (E4M3 scale per 16, kind::mxf4nvf4 block16, one 4-scale
+// chunk per K = 64 MMA). MX = 1: MXFP4 (E8M0 scale per 32, kind::mxf4 block32,
+// one chunk per two MMAs, which pick its scale bytes 0-1 or 2-3 by the scale
+// id) with four B rows per token (the residual terms of the activation).
+template <int BN, int MX>
 struct Cfg {
   static constexpr int kSfbCh = BN > 128 ? 2 : 1;  // 128-row scale blocks per tile
   static constexpr int kAcc = BN > 128 ? 1 : 2;    // TMEM accumulator buffers
   static constexpr int kStages = BN > 128 ? 4 : (BN > 64 ? 5 : (BN > 32 ? 6 : 8));
+  static constexpr int kCh = MX ? 2 : 4;           // scale chunks per 128 rows per stage
   static constexpr int kABytes = kBM * kBKBytes;
   static constexpr int kBBytes = BN * kBKBytes;
-  static constexpr int kSfaBytes = 4 * kChunkBytes;
-  static constexpr int kSfbBytes = kSfbCh * 4 * kChunkBytes;
+  static constexpr int kSfaBytes = kCh * kChunkBytes;
+  static constexpr int kSfbBytes = kSfbCh * kCh * kChunkBytes;
   static constexpr int kStageBytes =
       ((kABytes + kBBytes + kSfaBytes + kSfbBytes + 1023) / 1024) * 1024;
-  static constexpr int kSfaCols = 16;               // 4 MMAs x 4 columns
-  static constexpr int kSfbCols = 16 * kSfbCh;      // 4 MMAs x 4 * kSfbCh
+  static constexpr int kSfaCols = 4 * kCh;            // 4 columns per chunk
+  static constexpr int kSfbCols = 4 * kCh * kSfbCh;   // chunk c of block h at 4 * kSfbCh * c + 4 * h
   static constexpr int kSfBase = kAcc * BN;
   static constexpr int kStageSfCols = kSfaCols + kSfbCols;
   static constexpr int kTmemCols = 512;
@@ -121,13 +126,13 @@ __device__ __forceinline__ uint16_t f2bf(float x) {
   return __bfloat16_as_ushort(__float2bfloat16_rn(x));
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, int MX>
 __global__ void __launch_bounds__(kThreads, 1)
     nvfp4_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                               const __grid_constant__ CUtensorMap tmap_b32,
                               const __grid_constant__ CUtensorMap tmap_b64,
                               const __grid_constant__ CUtensorMap tmap_b128, const GemmParams p) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, MX>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -143,7 +148,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x % 32;
   const int m_tiles = p.M_per / kBM;
   const int ks_count = p.K / 256;
-  const int kc_per_rb = p.K / 64;  // scale chunks per 128-row block
+  const int kc_per_rb = p.K / (MX ? 128 : 64);  // scale chunks per 128-row block
   __shared__ int32_t s_ntp[kMaxSeg + 1], s_cnt[kMaxSeg], s_start[kMaxSeg + 1];
 
   for (int i = threadIdx.x; i <= p.nseg; i += blockDim.x) {
@@ -222,7 +227,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const CUtensorMap* m0 = box0 == 32 ? &tmap_b32 : (box0 == 64 ? &tmap_b64 : &tmap_b128);
         const CUtensorMap* m1 = box1 == 32 ? &tmap_b32 : (box1 == 64 ? &tmap_b64 : &tmap_b128);
         const uint32_t bytes = C::kABytes + (box0 + box1) * kBKBytes + C::kSfaBytes +
-                               sfb_ch * 4 * kChunkBytes;
+                               sfb_ch * C::kCh * kChunkBytes;
         for (int ks = 0; ks < ks_count; ++ks) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, p.err)) {
             ok = false;
@@ -237,11 +242,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_2d(sb, m0, &full[stage], ks * kBKBytes, ti.row_start);
           if (box1) tma_load_2d(sb + 128 * kBKBytes, m1, &full[stage], ks * kBKBytes,
                                 ti.row_start + 128);
-          bulk_load(ssfa, sfa + (size_t)ks * 4 * kChunkBytes, C::kSfaBytes, &full[stage]);
+          bulk_load(ssfa, sfa + (size_t)ks * C::kCh * kChunkBytes, C::kSfaBytes, &full[stage]);
           for (int h = 0; h < sfb_ch; ++h)
-            bulk_load(ssfb + h * 4 * kChunkBytes,
-                      sfb + ((size_t)h * kc_per_rb + ks * 4) * kChunkBytes, 4 * kChunkBytes,
-                      &full[stage]);
+            bulk_load(ssfb + h * C::kCh * kChunkBytes,
+                      sfb + ((size_t)h * kc_per_rb + ks * C::kCh) * kChunkBytes,
+                      C::kCh * kChunkBytes, &full[stage]);
           if (++stage == C::kStages) {
             stage = 0;
             phase ^= 1u;
@@ -279,9 +284,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t a_addr = smem_u32(sa), b_addr = smem_u32(sb);
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
-            mma_nvfp4(d_tmem, desc_kmajor_sw128(a_addr + 32 * c),
-                      desc_kmajor_sw128(b_addr + 32 * c), idesc, sfa_col + 4 * c,
-                      sfb_col + 4 * C::kSfbCh * c, (ks | c) != 0 ? 1u : 0u);
+            if (MX) {
+              // chunk c / 2; scale bytes 0-1 (id 0) or 2-3 (id 2) of each column,
+              // given in the address's top bits and in the descriptor
+              const uint32_t id = (uint32_t)(c & 1) * 2u;
+              mma_mxfp4(d_tmem, desc_kmajor_sw128(a_addr + 32 * c),
+                        desc_kmajor_sw128(b_addr + 32 * c), idesc_fp4(kBM, n_mma, 1, id, id),
+                        (sfa_col + 4 * (c >> 1)) | (id << 30),
+                        (sfb_col + 4 * C::kSfbCh * (c >> 1)) | (id << 30),
+                        (ks | c) != 0 ? 1u : 0u);
+            } else {
+              mma_nvfp4(d_tmem, desc_kmajor_sw128(a_addr + 32 * c),
+                        desc_kmajor_sw128(b_addr + 32 * c), idesc, sfa_col + 4 * c,
+                        sfb_col + 4 * C::kSfbCh * c, (ks | c) != 0 ? 1u : 0u);
+            }
           }
           tc_commit(&empty[stage]);
           if (++stage == C::kStages) {
@@ -325,28 +341,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint8_t* ssfb = ssfa + C::kSfaBytes;
         const uint32_t sfa_col = C::kSfBase + stage * C::kStageSfCols;
         const uint32_t sfb_col = sfa_col + C::kSfaCols;
-        uint32_t r[16];
+        // SFA: chunk c -> columns 4c..4c+3
+        uint32_t r[C::kSfaCols];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < C::kCh; ++c) {
           const uint4 v = *reinterpret_cast<const uint4*>(ssfa + c * kChunkBytes + lane * 16);
           r[4 * c] = v.x; r[4 * c + 1] = v.y; r[4 * c + 2] = v.z; r[4 * c + 3] = v.w;
         }
-        tmem_st_32x32b_x16(t_lane + sfa_col, r);
-        // SFB column 4 * kSfbCh * c + 4 * h holds chunk (128-row block h, K chunk c)
 #pragma unroll
-        for (int part = 0; part < C::kSfbCh; ++part) {
-          uint32_t rb[16];
+        for (int o = 0; o < C::kSfaCols; o += 8) tmem_st_32x32b_x8(t_lane + sfa_col + o, r + o);
+        // SFB: chunk c of 128-row block h -> columns 4 * kSfbCh * c + 4h
+        uint32_t rb[C::kSfbCols];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int col = 4 * j + 16 * part;  // first column of this group
-            const int c = col / (4 * C::kSfbCh), h = (col / 4) % C::kSfbCh;
-            uint4 v = make_uint4(0u, 0u, 0u, 0u);
-            if (h == 0 || two_blocks)
-              v = *reinterpret_cast<const uint4*>(ssfb + (h * 4 + c) * kChunkBytes + lane * 16);
-            rb[4 * j] = v.x; rb[4 * j + 1] = v.y; rb[4 * j + 2] = v.z; rb[4 * j + 3] = v.w;
-          }
-          tmem_st_32x32b_x16(t_lane + sfb_col + 16 * part, rb);
+        for (int g = 0; g < C::kSfbCols / 4; ++g) {
+          const int c = g / C::kSfbCh, h = g % C::kSfbCh;
+          uint4 v = make_uint4(0u, 0u, 0u, 0u);
+          if (h == 0 || two_blocks)
+            v = *reinterpret_cast<const uint4*>(ssfb + (h * C::kCh + c) * kChunkBytes + lane * 16);
+          rb[4 * g] = v.x; rb[4 * g + 1] = v.y; rb[4 * g + 2] = v.z; rb[4 * g + 3] = v.w;
         }
+#pragma unroll
+        for (int o = 0; o < C::kSfbCols; o += 8) tmem_st_32x32b_x8(t_lane + sfb_col + o, rb + o);
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
@@ -385,7 +400,58 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
       const float bscale = p.b_global[ti.seg];
-      if (EPI == 0) {
+      if (MX && EPI == 0) {
+        // Columns 4r..4r+3 of a chunk are the four terms of the chunk's token
+        // r (r = 0..7): their sum is the token's product. Lanes l < 16 hold
+        // gate rows and compute h for tokens 0-3, lanes l + 16 the matching up
+        // rows and tokens 4-7; one swap per token pair. h goes to the token's
+        // term-0 row.
+        const float s_gate = bscale * p.a_global[2 * ti.seg];
+        const float s_up = bscale * p.a_global[2 * ti.seg + 1];
+        const bool lo = lane < 16;
+        const int j = ti.m_tile * (kBM / 2) + 16 * q + (lane & 15);
+        const int hcols = p.M_per / 2;
+#pragma unroll
+        for (int ch = 0; ch < kChunks; ++ch) {
+          const int c0 = 32 * half + 64 * ch;
+          if (c0 >= ti.n_valid) break;
+          float t[8];
+#pragma unroll
+          for (int r = 0; r < 8; ++r)
+            t[r] = (__uint_as_float(v[ch][4 * r]) + __uint_as_float(v[ch][4 * r + 1])) +
+                   (__uint_as_float(v[ch][4 * r + 2]) + __uint_as_float(v[ch][4 * r + 3]));
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const float recv = __shfl_xor_sync(0xffffffffu, lo ? t[r + 4] : t[r], 16);
+            const float gate = (lo ? t[r] : recv) * s_gate;
+            const float up = (lo ? recv : t[r + 4]) * s_up;
+            const int col = c0 + 4 * (r + (lo ? 0 : 4));
+            if (col < ti.n_valid)
+              p.out[(size_t)(ti.row_start + col) * hcols + j] =
+                  f2bf(__fdividef(gate, 1.0f + __expf(-gate)) * up);
+          }
+        }
+      } else if (MX) {
+        // four term columns per token; routing weight of the term-0 row
+        const float scale = bscale * p.a_global[ti.seg];
+        const int o = ti.m_tile * kBM + 32 * q + lane;
+#pragma unroll
+        for (int ch = 0; ch < kChunks; ++ch) {
+          const int c0 = 32 * half + 64 * ch;
+          if (c0 >= ti.n_valid) break;
+          const float wmine = lane < 8 && c0 + 4 * lane < ti.n_valid
+                                  ? p.row_weight[ti.row_start + c0 + 4 * lane] * scale
+                                  : 0.0f;
+#pragma unroll
+          for (int r = 0; r < 8; ++r) {
+            const float w = __shfl_sync(0xffffffffu, wmine, r);
+            const float t = (__uint_as_float(v[ch][4 * r]) + __uint_as_float(v[ch][4 * r + 1])) +
+                            (__uint_as_float(v[ch][4 * r + 2]) + __uint_as_float(v[ch][4 * r + 3]));
+            if (c0 + 4 * r < ti.n_valid)
+              p.out[(size_t)(ti.row_start + c0 + 4 * r) * p.M_per + o] = f2bf(t * w);
+          }
+        }
+      } else if (EPI == 0) {
         // Rows 32q..32q+15 of the tile are gate rows, 32q+16..32q+31 the
         // matching up rows. For columns (i, i+16) of a chunk, lanes l and
         // l^16 swap one value so that every lane computes one h.
@@ -448,12 +514,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) tmem_dealloc(tmem_base, C::kTmemCols);
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, int MX>
 cudaError_t launch_impl(const CUtensorMap* ta, const CUtensorMap* tb, const GemmParams& p,
                         int num_sms, cudaStream_t st) {
-  auto kern = nvfp4_grouped_gemm_kernel<BN, EPI>;
+  auto kern = nvfp4_grouped_gemm_kernel<BN, EPI, MX>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)Cfg<BN>::kSmem);
+                                       (int)Cfg<BN, MX>::kSmem);
   if (e != cudaSuccess) return e;
   // setmaxnreg.inc waits until the block's launch registers cover the split;
   // refuse a build whose launch register count could not.
@@ -461,7 +527,7 @@ cudaError_t launch_impl(const CUtensorMap* ta, const CUtensorMap* tb, const Gemm
   e = cudaFuncGetAttributes(&fa, kern);
   if (e != cudaSuccess) return e;
   if ((size_t)fa.numRegs * kThreads < 256u * (kRegsLow + kRegsEpi)) return cudaErrorInvalidConfiguration;
-  kern<<<num_sms, kThreads, Cfg<BN>::kSmem, st>>>(*ta, tb[0], tb[1], tb[2], p);
+  kern<<<num_sms, kThreads, Cfg<BN, MX>::kSmem, st>>>(*ta, tb[0], tb[1], tb[2], p);
   return cudaGetLastError();
 }
 
@@ -469,22 +535,25 @@ cudaError_t launch_impl(const CUtensorMap* ta, const CUtensorMap* tb, const Gemm
 
 size_t nvfp4_gemm_smem_bytes(int bn) {
   switch (bn) {
-    case 32: return Cfg<32>::kSmem;
-    case 64: return Cfg<64>::kSmem;
-    case 128: return Cfg<128>::kSmem;
-    case 256: return Cfg<256>::kSmem;
+    case 32: return Cfg<32, 0>::kSmem;
+    case 64: return Cfg<64, 0>::kSmem;
+    case 128: return Cfg<128, 0>::kSmem;
+    case 256: return Cfg<256, 0>::kSmem;
   }
   return 0;
 }
 
 cudaError_t launch_nvfp4_grouped_gemm(int bn, int epi, const CUtensorMap* tmap_a,
                                       const CUtensorMap* tmap_b, const GemmParams& p,
-                                      int num_sms, cudaStream_t st) {
+                                      int num_sms, cudaStream_t st, int mxfp4) {
   if (p.nseg > kMaxSeg || p.K % 256 || p.M_per % kBM) return cudaErrorInvalidValue;
-#define G5_CASE(BN_)                                                              \
-  case BN_:                                                                       \
-    return epi == 0 ? launch_impl<BN_, 0>(tmap_a, tmap_b, p, num_sms, st)         \
-                    : launch_impl<BN_, 1>(tmap_a, tmap_b, p, num_sms, st);
+#define G5_CASE(BN_)                                                                     \
+  case BN_:                                                                              \
+    if (mxfp4)                                                                           \
+      return epi == 0 ? launch_impl<BN_, 0, 1>(tmap_a, tmap_b, p, num_sms, st)           \
+                      : launch_impl<BN_, 1, 1>(tmap_a, tmap_b, p, num_sms, st);          \
+    return epi == 0 ? launch_impl<BN_, 0, 0>(tmap_a, tmap_b, p, num_sms, st)             \
+                    : launch_impl<BN_, 1, 0>(tmap_a, tmap_b, p, num_sms, st);
   switch (bn) {
     G5_CASE(32)
     G5_CASE(64)

@@ -114,9 +114,12 @@ struct GemmParams {
 
 // tmap_b[i]: the activation rows with a box of (32 << i) rows, i = 0..2
 // (32, 64, 128); a tile loads its rows in pieces of at most 128.
+// mxfp4 = 1: MXFP4 operands (E8M0 scale per 32 in the blocked layout) and
+// four B rows per token (residual terms), summed in the epilogue; outputs and
+// routing weights live on each token's term-0 row.
 cudaError_t launch_nvfp4_grouped_gemm(int bn, int epi, const CUtensorMap* tmap_a,
                                       const CUtensorMap* tmap_b, const GemmParams& p,
-                                      int num_sms, cudaStream_t st);
+                                      int num_sms, cudaStream_t st, int mxfp4 = 0);
 size_t nvfp4_gemm_smem_bytes(int bn);
 
 // ------------------------------------------------------------ gemm_nvfp4_pair.cu
@@ -142,6 +145,9 @@ cudaError_t launch_interleave_gate_up(const uint8_t* gate_packed, const uint8_t*
                                       int K, int group, uint8_t* dst_packed, uint8_t* dst_sf,
                                       cudaStream_t st);
 // Row-major scale bytes [rows, K/group] -> blocked layout (zero padding).
+// Sets *found to 1 if any of the n bytes equals value (*found not cleared).
+cudaError_t launch_find_byte(const uint8_t* p, int64_t n, uint32_t value, uint32_t* found,
+                             cudaStream_t st);
 cudaError_t launch_scales_to_blocked(const uint8_t* rm, int64_t rows, int64_t sf_cols,
                                      uint8_t* blocked, cudaStream_t st);
 

@@ -150,6 +150,7 @@ struct glm5x_moe {
   PermuteBuffers pb{};
   uint8_t *act_packed = nullptr, *act_sf = nullptr, *h_packed = nullptr, *h_sf = nullptr;
   float *act_global = nullptr, *h_global = nullptr;
+  float* ones = nullptr;  // unit global scales (MXFP4 has none)
   uint16_t *h_bf16 = nullptr, *y_bf16 = nullptr;
   uint16_t* stage_in = nullptr;  // host-API staging
   float* stage_out = nullptr;
@@ -213,10 +214,15 @@ struct glm5x_moe {
   int K() const { return cfg.top_k; }
   int kk() const { return cfg.top_k + (cfg.has_shared ? 1 : 0); }
 
+  bool mx() const { return cfg.precision == GLM5X_PRECISION_MXFP4; }
+  int grp() const { return mx() ? 32 : 16; }   // values per scale
+  int terms() const { return mx() ? 4 : 1; }   // B rows per token (MXFP4 residual terms)
+  // bytes of blocked scales for `rows` rows of length K (128-row x 4-scale chunks of 512 B)
+  size_t sf_bytes(int64_t rows, int64_t K) const { return (size_t)(rows / 128) * (K / grp() / 4) * 512; }
   size_t w13_packed_bytes() const { return (size_t)2 * I() * H() / 2; }
-  size_t w13_sf_bytes() const { return (size_t)(2 * I() / 128) * (H() / 64) * 512; }
+  size_t w13_sf_bytes() const { return sf_bytes(2 * I(), H()); }
   size_t w2_packed_bytes() const { return (size_t)H() * I() / 2; }
-  size_t w2_sf_bytes() const { return (size_t)(H() / 128) * (I() / 64) * 512; }
+  size_t w2_sf_bytes() const { return sf_bytes(H(), I()); }
 };
 
 namespace {
@@ -235,7 +241,8 @@ int bn_index(int bn) { return bn == 32 ? 0 : bn == 64 ? 1 : bn == 128 ? 2 : 3; }
 
 int pick_bn(const glm5x_moe* m, int64_t T) {
   if (m->force_bn) return m->force_bn;
-  const double per_expert = (double)T * m->K() / std::max(1, m->cfg.num_experts);
+  // B rows per expert (4 per token for MXFP4 terms)
+  const double per_expert = (double)T * m->K() * m->terms() / std::max(1, m->cfg.num_experts);
   if (per_expert <= 24) return 32;
   if (per_expert <= 48) return 64;
   if (per_expert <= 96) return 128;
@@ -321,10 +328,13 @@ glm5x_status glm5x_moe_create(const glm5x_moe_config* cfg, int device, glm5x_moe
   const int H = c.hidden, I = c.intermediate, E = c.num_experts, k = c.top_k;
   const int nseg = m->nseg;
   // segment rows for the widest layout the automatic tile choice can use:
-  // 32-row tiles (4 x rows) up to 24 tokens per expert, 64-row tiles (2 x)
-  // up to 48, dense beyond
-  const int64_t per32 = std::min<int64_t>(T, 24LL * E / k), per64 = std::min<int64_t>(T, 48LL * E / k);
-  const int64_t logical = std::max({T * (int64_t)m->kk(), 4 * per32 * m->kk(), 2 * per64 * m->kk()});
+  // 32-row tiles (4 x rows) up to 24 rows per expert, 64-row tiles (2 x) up
+  // to 48, dense beyond; MXFP4 has 4 rows (terms) per token
+  const int tr = m->terms();
+  const int64_t per32 = std::min<int64_t>(T, 24LL * E / (k * tr)),
+                per64 = std::min<int64_t>(T, 48LL * E / (k * tr));
+  const int64_t logical =
+      tr * std::max({T * (int64_t)m->kk(), 4 * per32 * m->kk(), 2 * per64 * m->kk()});
   m->rows_cap = logical + (int64_t)nseg * 128 + 256;
   const int64_t R = m->rows_cap;
   const int64_t rb = R / 128 + 2;
@@ -354,11 +364,12 @@ glm5x_status glm5x_moe_create(const glm5x_moe_config* cfg, int device, glm5x_moe
   ok &= m->alloc(&m->pb.row_token, (size_t)R);
   ok &= m->alloc(&m->pb.row_weight, (size_t)R);
   ok &= m->alloc(&m->act_packed, (size_t)R * H / 2);
-  ok &= m->alloc(&m->act_sf, (size_t)rb * (H / 64) * 512);
+  ok &= m->alloc(&m->act_sf, m->sf_bytes(rb * 128, H));
   ok &= m->alloc(&m->act_global, (size_t)nseg);
   ok &= m->alloc(&m->h_bf16, (size_t)R * I);
   ok &= m->alloc(&m->h_packed, (size_t)R * I / 2);
-  ok &= m->alloc(&m->h_sf, (size_t)rb * (I / 64) * 512);
+  ok &= m->alloc(&m->h_sf, m->sf_bytes(rb * 128, I));
+  ok &= m->alloc(&m->ones, (size_t)2 * nseg);
   ok &= m->alloc(&m->h_global, (size_t)nseg);
   ok &= m->alloc(&m->y_bf16, (size_t)R * H);
   ok &= m->alloc(&m->stage_in, (size_t)T * H);
@@ -374,8 +385,12 @@ glm5x_status glm5x_moe_create(const glm5x_moe_config* cfg, int device, glm5x_moe
   cudaMemset(m->w2_global, 0, sizeof(float) * nseg);
   cudaMemset(m->act_packed, 0, (size_t)R * H / 2);
   cudaMemset(m->h_packed, 0, (size_t)R * I / 2);
-  cudaMemset(m->act_sf, 0, (size_t)rb * (H / 64) * 512);
-  cudaMemset(m->h_sf, 0, (size_t)rb * (I / 64) * 512);
+  cudaMemset(m->act_sf, 0, m->sf_bytes(rb * 128, H));
+  cudaMemset(m->h_sf, 0, m->sf_bytes(rb * 128, I));
+  if (m->ones) {
+    std::vector<float> one(2 * nseg, 1.0f);
+    cudaMemcpy(m->ones, one.data(), sizeof(float) * one.size(), cudaMemcpyHostToDevice);
+  }
   m->loaded.assign(nseg, 0);
   ok = make_tmap_u8(&m->tm_w13, m->w13_packed, H / 2, (uint64_t)nseg * 2 * I, 128) &&
        make_tmap_u8(&m->tm_w2, m->w2_packed, I / 2, (uint64_t)nseg * H, 128);
@@ -386,8 +401,8 @@ glm5x_status glm5x_moe_create(const glm5x_moe_config* cfg, int device, glm5x_moe
   }
   ok = ok && make_tmap_sf(&m->tm_w13_sf, m->w13_sf, (uint64_t)nseg * m->w13_sf_bytes()) &&
        make_tmap_sf(&m->tm_w2_sf, m->w2_sf, (uint64_t)nseg * m->w2_sf_bytes()) &&
-       make_tmap_sf(&m->tm_act_sf, m->act_sf, (uint64_t)rb * (H / 64) * 512) &&
-       make_tmap_sf(&m->tm_h_sf, m->h_sf, (uint64_t)rb * (I / 64) * 512);
+       make_tmap_sf(&m->tm_act_sf, m->act_sf, m->sf_bytes(rb * 128, H)) &&
+       make_tmap_sf(&m->tm_h_sf, m->h_sf, m->sf_bytes(rb * 128, I));
   if (!ok) {
     glm5x_moe_destroy(m);
     return fail_global(GLM5X_BACKEND_UNAVAILABLE, "tensor map encoding failed");
@@ -514,16 +529,107 @@ glm5x_status glm5x_moe_load_expert_nvfp4_device(glm5x_moe* m, int32_t expert,
   return load_nvfp4_common(m, expert, gate, up, down, true);
 }
 
+// MXFP4 expert admission (GLM5XMXFP4 sidecars / .k3x MXFP4 records,
+// reference/k3x_ref/mxfp4.py:31-107 layout): packed [rows, cols/2] and
+// row-major E8M0 scales [rows, cols/32]. Scales go to the 128x4 blocked
+// layout the block-scaled MMA reads; gate/up rows are interleaved like the
+// NVFP4 path. A 0xFF scale byte (NaN in E8M0) is rejected, as the reference's
+// decode_mxfp4 does (runtime/src/ops.cpp:40-63, mxfp4.py:110-144).
+static glm5x_status admit_mxfp4(glm5x_moe* m, int slot, const glm5x_mxfp4_matrix* gate,
+                                const glm5x_mxfp4_matrix* up, const glm5x_mxfp4_matrix* down,
+                                bool device_ptrs) {
+  const int H = m->H(), I = m->I();
+  const size_t g_pb = (size_t)I * H / 2, g_rm = (size_t)I * H / 32, g_sb = m->sf_bytes(I, H);
+  const size_t d_pb = m->w2_packed_bytes(), d_rm = (size_t)H * I / 32;
+  cudaStream_t st = m->stream;
+  const size_t need = 2 * (g_pb + g_rm + g_sb) + d_rm + 16;
+  if (m->stage_w_bytes < need) {
+    if (m->stage_w) cudaFree(m->stage_w);
+    m->stage_w = nullptr;
+    m->stage_w_bytes = 0;
+    G5_CHECK(m, cudaMalloc(&m->stage_w, need), "weight staging");
+    m->stage_w_bytes = need;
+  }
+  uint8_t* s = m->stage_w;
+  uint8_t *gp = s, *grm = gp + g_pb, *gsb = grm + g_rm;
+  uint8_t *upk = gsb + g_sb, *urm = upk + g_pb, *usb = urm + g_rm;
+  uint8_t* drm = usb + g_sb;
+  uint32_t* bad = reinterpret_cast<uint32_t*>(drm + d_rm);
+  const cudaMemcpyKind kind = device_ptrs ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+  G5_CHECK(m, cudaMemcpyAsync(gp, gate->packed, g_pb, kind, st), "gate upload");
+  G5_CHECK(m, cudaMemcpyAsync(grm, gate->scales, g_rm, kind, st), "gate scales");
+  G5_CHECK(m, cudaMemcpyAsync(upk, up->packed, g_pb, kind, st), "up upload");
+  G5_CHECK(m, cudaMemcpyAsync(urm, up->scales, g_rm, kind, st), "up scales");
+  G5_CHECK(m, cudaMemcpyAsync(drm, down->scales, d_rm, kind, st), "down scales");
+  G5_CHECK(m, cudaMemsetAsync(bad, 0, sizeof(uint32_t), st), "scale check");
+  G5_CHECK(m, launch_find_byte(grm, g_rm, 0xFF, bad, st), "scale check");
+  G5_CHECK(m, launch_find_byte(urm, g_rm, 0xFF, bad, st), "scale check");
+  G5_CHECK(m, launch_find_byte(drm, d_rm, 0xFF, bad, st), "scale check");
+  uint32_t found = 0;
+  G5_CHECK(m, cudaMemcpyAsync(&found, bad, sizeof found, cudaMemcpyDeviceToHost, st), "scale check");
+  G5_CHECK(m, cudaStreamSynchronize(st), "scale check");
+  if (found) return m->fail(GLM5X_INVALID_MXFP4, "E8M0 scale 0xff is reserved");
+  G5_CHECK(m, cudaMemsetAsync(gsb, 0, g_sb, st), "scales");
+  G5_CHECK(m, cudaMemsetAsync(usb, 0, g_sb, st), "scales");
+  G5_CHECK(m, launch_scales_to_blocked(grm, I, H / 32, gsb, st), "gate scales");
+  G5_CHECK(m, launch_scales_to_blocked(urm, I, H / 32, usb, st), "up scales");
+  G5_CHECK(m, launch_interleave_gate_up(gp, gsb, upk, usb, I, H, 32,
+                                        m->w13_packed + (size_t)slot * m->w13_packed_bytes(),
+                                        m->w13_sf + (size_t)slot * m->w13_sf_bytes(), st),
+           "gate/up interleave");
+  G5_CHECK(m, cudaMemcpyAsync(m->w2_packed + (size_t)slot * d_pb, down->packed, d_pb, kind, st),
+           "down");
+  G5_CHECK(m, launch_scales_to_blocked(drm, H, I / 32,
+                                       m->w2_sf + (size_t)slot * m->w2_sf_bytes(), st),
+           "down scales");
+  G5_CHECK(m, cudaStreamSynchronize(st), "expert admission");
+  if (!m->loaded[slot]) {
+    m->loaded[slot] = 1;
+    m->stats.loaded_experts++;
+    m->stats.resident_weight_bytes +=
+        m->w13_packed_bytes() + m->w13_sf_bytes() + d_pb + m->w2_sf_bytes();
+  }
+  return GLM5X_OK;
+}
+
+static glm5x_status load_mxfp4_common(glm5x_moe* m, int32_t expert,
+                                      const glm5x_mxfp4_matrix* gate,
+                                      const glm5x_mxfp4_matrix* up,
+                                      const glm5x_mxfp4_matrix* down, bool dev) {
+  if (!m) return fail_global(GLM5X_INVALID_STATE, "null engine");
+  if (!m->mx()) return m->fail(GLM5X_INVALID_STATE, "engine precision is not MXFP4");
+  const int slot = slot_of(m, expert);
+  if (slot < 0) return m->fail(GLM5X_INVALID_EXTENT, "expert %d is not held by this engine", expert);
+  const glm5x_mxfp4_matrix* mats[3] = {gate, up, down};
+  const int64_t shape[3][2] = {{m->I(), m->H()}, {m->I(), m->H()}, {m->H(), m->I()}};
+  const char* role[3] = {"gate", "up", "down"};
+  for (int r = 0; r < 3; ++r) {
+    const glm5x_mxfp4_matrix* w = mats[r];
+    if (!w || !w->packed || !w->scales)
+      return m->fail(GLM5X_INVALID_EXTENT, "%s: null matrix", role[r]);
+    if (w->rows != shape[r][0] || w->cols != shape[r][1])
+      return m->fail(GLM5X_INVALID_EXTENT, "%s: shape [%lld, %lld], expected [%lld, %lld]",
+                     role[r], (long long)w->rows, (long long)w->cols, (long long)shape[r][0],
+                     (long long)shape[r][1]);
+    if (w->group_size != 32)
+      return m->fail(GLM5X_INVALID_EXTENT, "%s: MXFP4 group size must be 32", role[r]);
+  }
+  cudaSetDevice(m->device);
+  return admit_mxfp4(m, slot, gate, up, down, dev);
+}
+
 glm5x_status glm5x_moe_load_expert_mxfp4(glm5x_moe* m, int32_t expert,
                                          const glm5x_mxfp4_matrix* gate,
                                          const glm5x_mxfp4_matrix* up,
                                          const glm5x_mxfp4_matrix* down) {
-  if (!m) return fail_global(GLM5X_INVALID_STATE, "null engine");
-  (void)expert;
-  (void)gate;
-  (void)up;
-  (void)down;
-  return m->fail(GLM5X_BACKEND_UNAVAILABLE, "MXFP4 experts are not admitted by this build yet");
+  return load_mxfp4_common(m, expert, gate, up, down, false);
+}
+
+glm5x_status glm5x_moe_load_expert_mxfp4_device(glm5x_moe* m, int32_t expert,
+                                                const glm5x_mxfp4_matrix* gate,
+                                                const glm5x_mxfp4_matrix* up,
+                                                const glm5x_mxfp4_matrix* down) {
+  return load_mxfp4_common(m, expert, gate, up, down, true);
 }
 
 glm5x_status glm5x_moe_load_sidecar(glm5x_moe* m, int32_t expert, const char* path) {
@@ -562,8 +668,6 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
   if (T64 <= 0 || T64 > m->cfg.max_tokens)
     return m->fail(GLM5X_INVALID_EXTENT, "tokens %lld outside [1, %d]", (long long)T64,
                    m->cfg.max_tokens);
-  if (m->cfg.precision != GLM5X_PRECISION_NVFP4)
-    return m->fail(GLM5X_BACKEND_UNAVAILABLE, "MXFP4 forward is not built yet");
   if (m->E_loc != m->cfg.num_experts)
     return m->fail(GLM5X_INVALID_STATE, "expert-parallel engines forward through the EP API");
   for (int s = 0; s < m->nseg; ++s)
@@ -575,7 +679,9 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
   int bn = pick_bn(m, T);
   // tiles narrower than 128 rows each take a 128-row block: make sure the
   // worst case still fits the workspace, else use 128-row tiles
-  if (bn < 128 && (int64_t)(128 / bn) * T * m->kk() + (int64_t)m->nseg * 128 > m->rows_cap) {
+  const bool mx = m->mx();
+  if (bn < 128 && (int64_t)(128 / bn) * T * m->kk() * m->terms() + (int64_t)m->nseg * 128 >
+                      m->rows_cap) {
     if (m->force_bn) return m->fail(GLM5X_INVALID_EXTENT, "token tile %d too narrow for %d tokens", bn, T);
     bn = 128;
   }
@@ -606,15 +712,26 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
   }
   mark(2);
   mark(3);
-  G5_CHECK(m, launch_permute(ids, wts, m->token_amax, T, k, E, hs, bn, m->pb, m->err, st),
+  G5_CHECK(m, launch_permute(ids, wts, m->token_amax, T, k, E, hs, bn, m->pb, m->err, st,
+                             m->terms()),
            "permute");
   launches += 3;
   const int64_t max_rows = (int64_t)T * m->kk() + (int64_t)m->nseg * 8;
   mark(4);
-  G5_CHECK(m, launch_nvfp4_quantize_segments(x, H, m->pb.row_token, m->pb.seg_start,
-                                             m->pb.seg_count, m->pb.qprefix, m->nseg, bn,
-                                             m->pb.seg_amax, max_rows, m->act_packed, m->act_sf,
-                                             m->act_global, st), "activation quantize");
+  if (mx) {
+    // MXFP4 experts take full-precision activations in the reference; the
+    // tensor cores get four MXFP4 residual terms per activation row
+    G5_CHECK(m, launch_mxfp4_terms_segments(x, H, m->pb.row_token, m->pb.seg_start,
+                                            m->pb.seg_count, m->pb.qprefix, m->nseg, bn, max_rows,
+                                            m->act_packed, m->act_sf, st),
+             "activation terms");
+  } else {
+    G5_CHECK(m, launch_nvfp4_quantize_segments(x, H, m->pb.row_token, m->pb.seg_start,
+                                               m->pb.seg_count, m->pb.qprefix, m->nseg, bn,
+                                               m->pb.seg_amax, max_rows, m->act_packed,
+                                               m->act_sf, m->act_global, st),
+             "activation quantize");
+  }
   GemmParams g1{};
   g1.a_packed = m->w13_packed;
   g1.b_packed = m->act_packed;
@@ -623,8 +740,8 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
   g1.seg_count = m->pb.seg_count;
   g1.seg_start = m->pb.seg_start;
   g1.ntile_prefix = m->pb.ntile_prefix;
-  g1.a_global = m->w13_global;
-  g1.b_global = m->act_global;
+  g1.a_global = mx ? m->ones : m->w13_global;
+  g1.b_global = mx ? m->ones : m->act_global;
   g1.out = m->h_bf16;
   g1.h_amax = m->pb.h_amax;
   g1.err = m->err;
@@ -632,24 +749,33 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
   g1.M_per = 2 * I;
   g1.nseg = m->nseg;
   mark(5);
-  const bool pair = bn == 256 && m->use_pair && m->pair_grid >= 2;
+  const bool pair = !mx && bn == 256 && m->use_pair && m->pair_grid >= 2;
   G5_CHECK(m,
            pair ? launch_nvfp4_pair_gemm(0, &m->tm_w13, m->tm_act, &m->tm_w13_sf, &m->tm_act_sf,
                                          g1, m->pair_grid, st)
-                : launch_nvfp4_grouped_gemm(bn, 0, &m->tm_w13, m->tm_act, g1, m->num_sms, st),
+                : launch_nvfp4_grouped_gemm(bn, 0, &m->tm_w13, m->tm_act, g1, m->num_sms, st,
+                                            mx ? 1 : 0),
            "gate/up GEMM");
   mark(6);
-  G5_CHECK(m, launch_nvfp4_quantize_segments(m->h_bf16, I, nullptr, m->pb.seg_start,
-                                             m->pb.seg_count, m->pb.qprefix, m->nseg, bn,
-                                             m->pb.h_amax, max_rows, m->h_packed, m->h_sf,
-                                             m->h_global, st), "h quantize");
+  if (mx) {
+    G5_CHECK(m, launch_mxfp4_terms_segments(m->h_bf16, I, nullptr, m->pb.seg_start,
+                                            m->pb.seg_count, m->pb.qprefix, m->nseg, bn, max_rows,
+                                            m->h_packed, m->h_sf, st),
+             "h terms");
+  } else {
+    G5_CHECK(m, launch_nvfp4_quantize_segments(m->h_bf16, I, nullptr, m->pb.seg_start,
+                                               m->pb.seg_count, m->pb.qprefix, m->nseg, bn,
+                                               m->pb.h_amax, max_rows, m->h_packed, m->h_sf,
+                                               m->h_global, st),
+             "h quantize");
+  }
   GemmParams g2 = g1;
   g2.a_packed = m->w2_packed;
   g2.b_packed = m->h_packed;
   g2.sfa = m->w2_sf;
   g2.sfb = m->h_sf;
-  g2.a_global = m->w2_global;
-  g2.b_global = m->h_global;
+  g2.a_global = mx ? m->ones : m->w2_global;
+  g2.b_global = mx ? m->ones : m->h_global;
   g2.row_weight = m->pb.row_weight;
   g2.out = m->y_bf16;
   g2.h_amax = nullptr;
@@ -659,7 +785,8 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
   G5_CHECK(m,
            pair ? launch_nvfp4_pair_gemm(1, &m->tm_w2, m->tm_h, &m->tm_w2_sf, &m->tm_h_sf, g2,
                                          m->pair_grid, st)
-                : launch_nvfp4_grouped_gemm(bn, 1, &m->tm_w2, m->tm_h, g2, m->num_sms, st),
+                : launch_nvfp4_grouped_gemm(bn, 1, &m->tm_w2, m->tm_h, g2, m->num_sms, st,
+                                            mx ? 1 : 0),
            "down GEMM");
   mark(8);
   G5_CHECK(m, launch_combine(m->y_bf16, m->pb.pos, T, m->kk(), H, out, st), "combine");

@@ -13,6 +13,7 @@
 // runtime/cuda/moe_layer.cu:25-44; shared add moe_layer.cu:64-70): every
 // token gathers its k routed rows plus its shared-expert row (already
 // weighted in the down-projection epilogue) in FP32.
+#include <algorithm>
 #include <cstdint>
 
 #include "fp4_codec.h"
@@ -100,6 +101,23 @@ cudaError_t launch_scales_to_blocked(const uint8_t* rm, int64_t rows, int64_t sf
   if (n == 0) return cudaSuccess;
   scales_to_blocked_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(rm, rows, sf_cols,
                                                                         blocked);
+  return cudaGetLastError();
+}
+
+__global__ void find_byte_kernel(const uint8_t* __restrict__ p, int64_t n, uint32_t value,
+                                 uint32_t* __restrict__ found) {
+  bool hit = false;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    hit |= p[i] == value;
+  if (__any_sync(0xffffffffu, hit) && (threadIdx.x & 31) == 0) atomicOr(found, 1u);
+}
+
+cudaError_t launch_find_byte(const uint8_t* p, int64_t n, uint32_t value, uint32_t* found,
+                             cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  const int64_t blocks = std::min<int64_t>((n + 255) / 256, 1184);
+  find_byte_kernel<<<(unsigned)blocks, 256, 0, st>>>(p, n, value, found);
   return cudaGetLastError();
 }
 

@@ -6,16 +6,17 @@ exists.
 """
 from __future__ import annotations
 
-__all__ = ["GLM5XMoELayer", "NVFP4Expert", "GLM5XNVFP4Weight", "quantize_nvfp4_weight",
+__all__ = ["GLM5XMoELayer", "NVFP4Expert", "MXFP4Expert", "GLM5XNVFP4Weight",
+           "GLM5XMXFP4Weight", "quantize_nvfp4_weight", "quantize_mxfp4_weight",
            "dequantize_nvfp4", "encode_mxfp4", "decode_mxfp4"]
 
 
 def __getattr__(name):
-    if name in ("GLM5XMoELayer", "NVFP4Expert", "GLM5XMoEForward"):
+    if name in ("GLM5XMoELayer", "NVFP4Expert", "MXFP4Expert", "GLM5XMoEForward"):
         from . import layer
         return getattr(layer, name)
-    if name in ("GLM5XNVFP4Weight", "quantize_nvfp4_weight", "dequantize_nvfp4",
-                "encode_mxfp4", "decode_mxfp4"):
+    if name in ("GLM5XNVFP4Weight", "GLM5XMXFP4Weight", "quantize_nvfp4_weight",
+                "quantize_mxfp4_weight", "dequantize_nvfp4", "encode_mxfp4", "decode_mxfp4"):
         from . import nvfp4
         return getattr(nvfp4, name)
     raise AttributeError(name)

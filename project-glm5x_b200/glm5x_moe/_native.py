@@ -91,6 +91,9 @@ SIGNATURES = {
                                            ctypes.POINTER(Nvfp4Matrix)],
     "glm5x_moe_load_expert_mxfp4": [_P, _I32, ctypes.POINTER(Mxfp4Matrix),
                                     ctypes.POINTER(Mxfp4Matrix), ctypes.POINTER(Mxfp4Matrix)],
+    "glm5x_moe_load_expert_mxfp4_device": [_P, _I32, ctypes.POINTER(Mxfp4Matrix),
+                                           ctypes.POINTER(Mxfp4Matrix),
+                                           ctypes.POINTER(Mxfp4Matrix)],
     "glm5x_moe_load_sidecar": [_P, _I32, ctypes.c_char_p],
     "glm5x_moe_forward": [_P, _P, _I64, _P, _P],
     "glm5x_moe_forward_host": [_P, _P, _I64, _P],

@@ -16,7 +16,7 @@ from typing import Mapping
 import torch
 
 from . import _native as N
-from .nvfp4 import GLM5XNVFP4Weight
+from .nvfp4 import GLM5XMXFP4Weight, GLM5XNVFP4Weight
 
 
 @dataclass(frozen=True)
@@ -36,6 +36,15 @@ class NVFP4Expert:
     gate_proj: GLM5XNVFP4Weight
     up_proj: GLM5XNVFP4Weight
     down_proj: GLM5XNVFP4Weight
+
+
+@dataclass(frozen=True)
+class MXFP4Expert:
+    """gate/up [I, H] and down [H, I] MXFP4 projections of one expert."""
+
+    gate_proj: GLM5XMXFP4Weight
+    up_proj: GLM5XMXFP4Weight
+    down_proj: GLM5XMXFP4Weight
 
 
 def _stream() -> ctypes.c_void_p:
@@ -93,13 +102,16 @@ class GLM5XMoELayer:
             raise ValueError("GLM5X_ROUTER_BIAS_SHAPE")
         N.check(N.lib().glm5x_moe_set_router(self._h, w.data_ptr(), b.data_ptr()), self._h)
 
-    def load_expert(self, expert_id: int, expert: NVFP4Expert) -> None:
-        """Admit one NVFP4 expert held in device tensors (expert_id -1 = shared)."""
+    def load_expert(self, expert_id: int, expert: NVFP4Expert | MXFP4Expert) -> None:
+        """Admit one NVFP4 or MXFP4 expert held in device tensors (expert_id -1
+        = shared); the format must match the layer's precision."""
         g, u, d = expert.gate_proj.matrix(), expert.up_proj.matrix(), expert.down_proj.matrix()
+        fn = (N.lib().glm5x_moe_load_expert_mxfp4_device if isinstance(expert, MXFP4Expert)
+              else N.lib().glm5x_moe_load_expert_nvfp4_device)
         with torch.cuda.device(self.device):
             torch.cuda.current_stream().synchronize()
-            N.check(N.lib().glm5x_moe_load_expert_nvfp4_device(
-                self._h, expert_id, ctypes.byref(g), ctypes.byref(u), ctypes.byref(d)), self._h)
+            N.check(fn(self._h, expert_id, ctypes.byref(g), ctypes.byref(u), ctypes.byref(d)),
+                    self._h)
 
     def load_sidecar(self, expert_id: int, path: str) -> None:
         N.check(N.lib().glm5x_moe_load_sidecar(self._h, expert_id, str(path).encode()), self._h)

@@ -175,3 +175,33 @@ def decode_mxfp4(packed: torch.Tensor, scales: torch.Tensor, rows: int, cols: in
         raise ValueError("E8M0 scale 0xff is reserved")
     N.check(st)
     return out
+
+
+@dataclass(frozen=True)
+class GLM5XMXFP4Weight:
+    """One MXFP4 matrix on the device: packed E2M1 codes [rows * cols / 2]
+    (low nibble first) and row-major E8M0 scales [rows * cols / 32], the
+    layout of encode_mxfp4 (k3x_ref/mxfp4.py:31-107) and of .pm4 sidecars."""
+
+    packed: torch.Tensor
+    scales: torch.Tensor
+    shape: tuple[int, int]
+
+    def __post_init__(self) -> None:
+        rows, cols = self.shape
+        if self.packed.numel() != rows * cols // 2 or self.scales.numel() != rows * cols // 32:
+            raise ValueError("GLM5X_MXFP4_WEIGHT_SHAPE")
+        if self.packed.dtype != torch.uint8 or self.scales.dtype != torch.uint8:
+            raise ValueError("GLM5X_MXFP4_WEIGHT_DTYPE")
+
+    def matrix(self) -> N.Mxfp4Matrix:
+        rows, cols = self.shape
+        return N.Mxfp4Matrix(self.packed.data_ptr(), self.scales.data_ptr(), rows, cols, 32)
+
+
+def quantize_mxfp4_weight(weight: torch.Tensor, *, scale_mode: str = "max_abs"
+                          ) -> GLM5XMXFP4Weight:
+    """Encode a [rows, cols] CUDA matrix to MXFP4 (group 32) on the GPU."""
+    packed, scales = encode_mxfp4(weight, 32, scale_mode=scale_mode)
+    return GLM5XMXFP4Weight(packed.contiguous(), scales.contiguous(),
+                            (int(weight.shape[0]), int(weight.shape[1])))

@@ -31,10 +31,28 @@ def make_expert(H: int, I: int, seed: int, device="cuda"):
     return NVFP4Expert(*mats), tuple(deq)
 
 
+def make_expert_mxfp4(H: int, I: int, seed: int, device="cuda"):
+    """Returns (MXFP4Expert on device, (gate_deq, up_deq, down_deq) FP32 host),
+    encoded by the library's GPU MXFP4 encoder (max_abs, group 32) and
+    decoded by the oracle."""
+    from glm5x_moe.layer import MXFP4Expert
+    from glm5x_moe.nvfp4 import quantize_mxfp4_weight
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    mats, deq = [], []
+    for shape in ((I, H), (I, H), (H, I)):
+        w = (torch.randn(shape, generator=g) * 0.02).to(torch.bfloat16).to(device)
+        q = quantize_mxfp4_weight(w)
+        mats.append(q)
+        deq.append(O.mxfp4_decode(q.packed.cpu().numpy(), q.scales.cpu().numpy(), *shape))
+    return MXFP4Expert(*mats), tuple(deq)
+
+
 def oracle_forward(hidden: np.ndarray, ids: np.ndarray, weights: np.ndarray,
-                   experts_deq: dict, shared_deq=None) -> tuple[np.ndarray, dict]:
+                   experts_deq: dict, shared_deq=None, expert_fn=None) -> tuple[np.ndarray, dict]:
     """hidden [T, H] (BF16 values as FP32); ids/weights [T, k]. Returns the
-    layer output [T, H] and the per-(token, slot) expert outputs."""
+    layer output [T, H] and the per-(token, slot) expert outputs. expert_fn
+    defaults to the NVFP4 per-slab oracle."""
+    expert_fn = expert_fn or O.nvfp4_expert_dequant_oracle
     T, H = hidden.shape
     out = np.zeros((T, H), dtype=np.float64)
     per = {}
@@ -43,11 +61,11 @@ def oracle_forward(hidden: np.ndarray, ids: np.ndarray, weights: np.ndarray,
         order = np.argsort(tok, kind="stable")
         tok, slot = tok[order], slot[order]
         gd, ud, dd = experts_deq[e]
-        y = O.nvfp4_expert_dequant_oracle(hidden[tok], (gd, ud), dd)
+        y = expert_fn(hidden[tok], (gd, ud), dd)
         for i, (t, s) in enumerate(zip(tok, slot)):
             per[(int(t), int(s))] = y[i]
             out[t] += np.float64(weights[t, s]) * y[i]
     if shared_deq is not None:
         gd, ud, dd = shared_deq
-        out += O.nvfp4_expert_dequant_oracle(hidden, (gd, ud), dd)
+        out += expert_fn(hidden, (gd, ud), dd)
     return out.astype(np.float32), per
