@@ -229,6 +229,78 @@ def build_layer(T: int, device_index: int, seed: int = 0, experts: int = E):
     return layer
 
 
+MXFP4_EXPERT_BYTES = 3 * (H * I // 2 + H * I // 32)   # 20,054,016 (E2M1 + E8M0/32)
+
+
+def zipf_bias(experts: int, seed: int):
+    """C3 router bias U(-0.1, 0.1) plus the Zipf(1.1) skew of config 4:
+    bias_e += 0.5 * (pi(e) + 1)^-1.1 for a seeded permutation pi."""
+    import torch
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    bias = torch.rand(experts, generator=g) * 0.2 - 0.1
+    perm = torch.randperm(experts, generator=g)
+    return bias + 0.5 * (perm.to(torch.float64) + 1.0).pow(-1.1).to(torch.float32)
+
+
+def run_decode_c4(device_index: int, steps: int, warmup: int, T: int = 64) -> dict:
+    """Config 4 on one GPU: the full MXFP4 layer (256 experts + shared,
+    GLM-5 shapes) at decode batch 64 with the Zipf-skewed router. HBM-bound:
+    algorithmic bytes = (distinct experts touched + 1 shared) x 20,054,016 B of
+    MXFP4 weights + the 3.1 MB router + 64 x 6144 BF16 in + FP32 out."""
+    import torch
+    from glm5x_moe.layer import GLM5XMoELayer, MXFP4Expert
+    from glm5x_moe.nvfp4 import quantize_mxfp4_weight
+    dev = torch.device("cuda", device_index)
+    layer = GLM5XMoELayer(hidden_size=H, intermediate_size=I, num_experts=E, top_k=K_TOP,
+                          routed_scaling_factor=SCALE, has_shared=True, max_tokens=T,
+                          device=device_index, precision="mxfp4")
+    g = torch.Generator(device=dev).manual_seed(4)
+    for e in list(range(E)) + [-1]:
+        mats = [quantize_mxfp4_weight((torch.randn(shape, generator=g, device=dev) * 0.02)
+                                      .to(torch.bfloat16))
+                for shape in ((I, H), (I, H), (H, I))]
+        layer.load_expert(e, MXFP4Expert(*mats))
+        del mats
+    gc = torch.Generator(device="cpu").manual_seed(5)
+    router = (torch.randn(E, H, generator=gc) * 0.02).to(torch.bfloat16)
+    layer.set_router(router, zipf_bias(E, 6))
+    hidden = torch.randn(T, H, generator=gc).to(torch.bfloat16).to(dev)
+    res = layer(hidden)
+    touched = int(torch.unique(res.topk_indices).numel())
+    for _ in range(warmup):
+        layer(hidden, want_routing=False)
+    layer.set_profiling(True)
+    layer.phase_times()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        layer(hidden, want_routing=False)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    layer.check()
+    ms = e0.elapsed_time(e1) / steps
+    phases, n = layer.phase_times()
+    phases = {k: v / max(n, 1) for k, v in phases.items()}
+    layer.close()
+    weight_bytes = (touched + 1) * MXFP4_EXPERT_BYTES
+    alg = weight_bytes + E * H * 2 + E * 4 + T * H * 2 + T * H * 4
+    hbm = peaks()["hbm_gbs"]
+    gu_bytes = (touched + 1) * 2 * (H * I // 2 + H * I // 32)
+    dn_bytes = (touched + 1) * (H * I // 2 + H * I // 32)
+    return {
+        "workload": "c4: GLM-5 MoE layer, MXFP4 experts (E2M1 + E8M0/32), decode batch 64, "
+                    "256 experts + shared, Zipf(1.1)-skewed router bias, 1 GPU",
+        "tokens_per_s": T / (ms / 1000.0), "ms_per_step": ms, "experts_touched": touched,
+        "phases_ms": phases,
+        "roofline": {"bound": "hbm", "kernel": "whole layer step", "achieved": alg / (ms / 1000.0) / 1e9,
+                     "peak": hbm, "unit": "GB/s", "frac": alg / (ms / 1000.0) / 1e9 / hbm,
+                     "algorithmic_bytes": alg,
+                     "gate_up_gemm_frac": gu_bytes / (phases["gate_up_gemm"] / 1000.0) / 1e9 / hbm,
+                     "down_gemm_frac": dn_bytes / (phases["down_gemm"] / 1000.0) / 1e9 / hbm},
+    }
+
+
 # ---------------------------------------------------------------- CPU reference
 def cpu_reference_sample(seconds: float = 12.0, threads: int | None = None) -> dict:
     """Times the reference's CPU expert path (oracle/_ref/libk3x_ref.so,
@@ -432,6 +504,10 @@ def run_ours(args) -> None:
             "e2e": {"value": e2e_value, "unit": "tokens/s",
                     "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 4},
         }
+        if not args.no_decode and not custom:
+            layer.close()
+            torch.cuda.empty_cache()
+            line["decode"] = run_decode_c4(local, max(args.steps, 20), args.warmup)
         if not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_reference_sample(seconds=12.0)
         print(json.dumps(line), flush=True)
@@ -449,6 +525,8 @@ def main() -> None:
     ap.add_argument("--workload", default="c5", choices=["c5", "c3"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode", action="store_true",
+                    help="skip the config-4 MXFP4 decode (HBM roofline) measurement")
     ap.add_argument("--no-library-gemm", action="store_true",
                     help="skip the cuBLASLt NVFP4 reference GEMM of the roofline")
     ap.add_argument("--tokens", type=int, default=0, help="override tokens (profiling only)")
