@@ -73,10 +73,12 @@ G5_HD float bits_f(uint32_t b) {
 #endif
 }
 
-// E2M1 magnitude table in the reference's code order (codes 8..15 negate).
+// E2M1 value of a code in the reference's code order (codes 8..15 negate):
+// magnitudes 0, 0.5, 1, 1.5, 2, 3, 4, 6 = half of the 4-bit table
+// 0, 1, 2, 3, 4, 6, 8, 12 held in one register (no indexed local array).
 G5_HD float e2m1_value(uint32_t code) {
-  const float mag[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
-  const float m = mag[code & 7u];
+  const uint32_t twice = (0xC8643210u >> (4u * (code & 7u))) & 0xFu;
+  const float m = static_cast<float>(twice) * 0.5f;
   return (code & 8u) ? -m : m;
 }
 

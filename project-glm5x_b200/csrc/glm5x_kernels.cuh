@@ -39,12 +39,13 @@ cudaError_t launch_nvfp4_quantize_segments(const uint16_t* src, int K, const int
                                            const float* seg_amax, int64_t max_rows,
                                            uint8_t* packed, uint8_t* scales_blocked,
                                            float* seg_global, cudaStream_t st);
-// Four-term MXFP4 expansion of expert-major rows (4 operand rows per token).
+// Four-term MXFP4 expansion of expert-major rows (4 operand rows per token);
+// records kErrNonFinite in *err for Inf / NaN inputs.
 cudaError_t launch_mxfp4_terms_segments(const uint16_t* src, int K, const int32_t* row_token,
                                         const int32_t* seg_start, const int32_t* seg_count,
                                         const int32_t* qprefix, int nseg, int bn,
                                         int64_t max_slots, uint8_t* packed,
-                                        uint8_t* scales_blocked, cudaStream_t st);
+                                        uint8_t* scales_blocked, uint32_t* err, cudaStream_t st);
 cudaError_t launch_nvfp4_dequantize(const uint8_t* packed, const uint8_t* scales_blocked,
                                     float g, int64_t rows, int64_t cols, float* out,
                                     cudaStream_t st);
@@ -81,11 +82,17 @@ cudaError_t launch_permute(const int32_t* ids, const float* weights, const float
 // ------------------------------------------------------------ router_tc.cu
 // BF16 router logits on tcgen05 + sigmoid/bias/top-k epilogue. tmap_x: hidden
 // [T, H] BF16, box {64, 128}; tmap_w: router weight [E, H] BF16, box {64, E}.
+// When the 128-token tiles would leave SMs idle and `partials` is given
+// (router_partials_floats() floats), the contraction is split along K over
+// several CTAs per tile and a second kernel sums the partial logits in a
+// fixed order before the top-k. Returns the launches issued in *launches.
 bool router_tc_supported(int E, int H, int k);
+size_t router_partials_floats(int num_sms, int E);
 cudaError_t launch_router_tc(const CUtensorMap* tmap_x, const CUtensorMap* tmap_w,
                              const float* bias, int T, int H, int E, int k, float routed_scale,
                              float* logits, int32_t* ids, float* weights, uint32_t* err,
-                             cudaStream_t st);
+                             cudaStream_t st, float* partials = nullptr, int num_sms = 0,
+                             int* launches = nullptr);
 
 // ------------------------------------------------------------ gemm_nvfp4.cu
 // Grouped block-scaled FP4 GEMM over expert segments, weights as the M side:

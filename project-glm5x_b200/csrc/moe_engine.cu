@@ -151,6 +151,7 @@ struct glm5x_moe {
   uint8_t *act_packed = nullptr, *act_sf = nullptr, *h_packed = nullptr, *h_sf = nullptr;
   float *act_global = nullptr, *h_global = nullptr;
   float* ones = nullptr;  // unit global scales (MXFP4 has none)
+  float* router_partials = nullptr;  // split-K router partial logits
   uint16_t *h_bf16 = nullptr, *y_bf16 = nullptr;
   uint16_t* stage_in = nullptr;  // host-API staging
   float* stage_out = nullptr;
@@ -370,6 +371,7 @@ glm5x_status glm5x_moe_create(const glm5x_moe_config* cfg, int device, glm5x_moe
   ok &= m->alloc(&m->h_packed, (size_t)R * I / 2);
   ok &= m->alloc(&m->h_sf, m->sf_bytes(rb * 128, I));
   ok &= m->alloc(&m->ones, (size_t)2 * nseg);
+  ok &= m->alloc(&m->router_partials, router_partials_floats(m->num_sms, E));
   ok &= m->alloc(&m->h_global, (size_t)nseg);
   ok &= m->alloc(&m->y_bf16, (size_t)R * H);
   ok &= m->alloc(&m->stage_in, (size_t)T * H);
@@ -692,9 +694,13 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
     if (m->profiling) cudaEventRecord(m->ev[pslot][phase], st);
   };
   mark(0);
-  G5_CHECK(m, launch_row_amax_bf16(x, T, H, m->token_amax, m->err, st), "row amax");
+  if (!mx) {
+    // per-token amax for the NVFP4 slab global scales (MXFP4 has none; its
+    // term kernel checks for non-finite inputs itself)
+    G5_CHECK(m, launch_row_amax_bf16(x, T, H, m->token_amax, m->err, st), "row amax");
+    ++launches;
+  }
   mark(1);
-  ++launches;
   const int32_t* ids = ids_in;
   const float* wts = w_in;
   if (!ids_in) {
@@ -703,10 +709,11 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
     CUtensorMap tm_x;
     if (!make_tmap_bf16(&tm_x, x, H, T, 128))
       return m->fail(GLM5X_BACKEND_UNAVAILABLE, "hidden tensor map");
+    int rl = 0;
     G5_CHECK(m, launch_router_tc(&tm_x, &m->tm_router, m->router_bias, T, H, E, k,
                                  m->cfg.routed_scaling, m->logits, m->topk_ids, m->topk_w, m->err,
-                                 st), "router");
-    launches += 1;
+                                 st, m->router_partials, m->num_sms, &rl), "router");
+    launches += rl;
     ids = m->topk_ids;
     wts = m->topk_w;
   }
@@ -723,7 +730,7 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
     // tensor cores get four MXFP4 residual terms per activation row
     G5_CHECK(m, launch_mxfp4_terms_segments(x, H, m->pb.row_token, m->pb.seg_start,
                                             m->pb.seg_count, m->pb.qprefix, m->nseg, bn, max_rows,
-                                            m->act_packed, m->act_sf, st),
+                                            m->act_packed, m->act_sf, m->err, st),
              "activation terms");
   } else {
     G5_CHECK(m, launch_nvfp4_quantize_segments(x, H, m->pb.row_token, m->pb.seg_start,
@@ -760,7 +767,7 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
   if (mx) {
     G5_CHECK(m, launch_mxfp4_terms_segments(m->h_bf16, I, nullptr, m->pb.seg_start,
                                             m->pb.seg_count, m->pb.qprefix, m->nseg, bn, max_rows,
-                                            m->h_packed, m->h_sf, st),
+                                            m->h_packed, m->h_sf, m->err, st),
              "h terms");
   } else {
     G5_CHECK(m, launch_nvfp4_quantize_segments(m->h_bf16, I, nullptr, m->pb.seg_start,

@@ -11,6 +11,7 @@
 //    reference/k3x_ref/mxfp4.py:110-144, runtime/src/ops.cpp:40-63).
 //  * mxfp4_encode: encode_mxfp4 (mxfp4.py:31-107, both scale modes).
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cstdint>
 
 #include "fp4_codec.h"
@@ -297,9 +298,14 @@ __global__ void mxfp4_terms_segments_kernel(
     const uint16_t* __restrict__ src, int K, const int32_t* __restrict__ row_token,
     const int32_t* __restrict__ seg_start, const int32_t* __restrict__ seg_count,
     const int32_t* __restrict__ qprefix, int nseg, int bn, uint8_t* __restrict__ packed,
-    uint8_t* __restrict__ scales_blocked) {
+    uint8_t* __restrict__ scales_blocked, uint32_t* __restrict__ err) {
+  // one warp per (token slot, 1024-element chunk of the row); lane = group
   const int warps = blockDim.x / 32;
-  const int64_t f = blockIdx.x * (int64_t)warps + threadIdx.x / 32;
+  const int ng = K / 32;
+  const int nchunk = (ng + 31) / 32;
+  const int64_t wid = blockIdx.x * (int64_t)warps + threadIdx.x / 32;
+  const int64_t f = wid / nchunk;
+  const int g = static_cast<int>(wid % nchunk) * 32 + lane_id();
   if (f >= qprefix[nseg]) return;
   int lo = 0, hi = nseg;
   while (hi - lo > 1) {
@@ -308,61 +314,85 @@ __global__ void mxfp4_terms_segments_kernel(
   }
   const int s = lo;
   const int r = static_cast<int>(f - qprefix[s]);  // token slot in the segment
-  const int ng = K / 32;
   int64_t rows[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) rows[j] = seg_start[s] + segment_row(4 * r + j, bn);
+  if (g >= ng) return;
   if (4 * r >= seg_count[s]) {
-    for (int g = lane_id(); g < ng; g += 32)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        *reinterpret_cast<uint4*>(packed + rows[j] * (K / 2) + g * 16) = make_uint4(0, 0, 0, 0);
-        scales_blocked[blocked_sf_offset(rows[j], g, ng)] = 0;
-      }
+    for (int j = 0; j < 4; ++j) {
+      *reinterpret_cast<uint4*>(packed + rows[j] * (K / 2) + g * 16) = make_uint4(0, 0, 0, 0);
+      scales_blocked[blocked_sf_offset(rows[j], g, ng)] = 0;
+    }
     return;
   }
   const int64_t t = row_token ? row_token[rows[0]] : rows[0];
-  const uint16_t* xrow = src + t * (int64_t)K;
-  for (int g = lane_id(); g < ng; g += 32) {
-    const uint4* qv = reinterpret_cast<const uint4*>(xrow + g * 32);
-    float res[32];
+  const uint4* qv = reinterpret_cast<const uint4*>(src + t * (int64_t)K + g * 32);
+  float res[32];
+  bool bad = false;
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const uint4 v = __ldg(qv + u);
-      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  for (int u = 0; u < 4; ++u) {
+    const uint4 v = __ldg(qv + u);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      res[8 * u + 2 * i] = __uint_as_float(w[i] << 16);
+      res[8 * u + 2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+      // BF16 Inf / NaN: all exponent bits set in either half
+      bad |= (w[i] & 0x7f80u) == 0x7f80u || (w[i] & 0x7f800000u) == 0x7f800000u;
+    }
+  }
+  if (bad) atomicOr(err, kErrNonFinite);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float m = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) m = fmaxf(m, fabsf(res[i]));
+    // smallest e with m <= 6 * 2^e: e = ceil(log2(m / 6)) from the bits
+    int e = -127;
+    if (m > 0.0f) {
+      const uint32_t qb = __float_as_uint(m / 6.0f);
+      const int ex = (int)(qb >> 23) - 127;
+      e = ex + ((qb & 0x7fffffu) != 0u ? 1 : 0);
+      if (ex == -127) e = -126;  // subnormal quotient
+      e = e < -127 ? -127 : (e > 127 ? 127 : e);
+    }
+    const float scale = pow2f(e);
+    const float inv = e == -127 ? 0.0f : pow2f(-e);
+    // Any rounding of the codes is valid here (the residual is taken from the
+    // codes actually chosen): the hardware converter encodes 8 values and
+    // decodes them back to FP16 pairs for the residual update.
+    uint32_t word[4];
+#pragma unroll
+    for (int w8 = 0; w8 < 4; ++w8) {
+      float q[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) q[i] = __fmul_rn(res[8 * w8 + i], inv);
+      uint32_t h[4];
+      asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+          "cvt.rn.satfinite.e2m1x2.f32 b0, %6, %5;\n\t"
+          "cvt.rn.satfinite.e2m1x2.f32 b1, %8, %7;\n\t"
+          "cvt.rn.satfinite.e2m1x2.f32 b2, %10, %9;\n\t"
+          "cvt.rn.satfinite.e2m1x2.f32 b3, %12, %11;\n\t"
+          "mov.b32 %0, {b0, b1, b2, b3};\n\t"
+          "cvt.rn.f16x2.e2m1x2 %1, b0;\n\t"
+          "cvt.rn.f16x2.e2m1x2 %2, b1;\n\t"
+          "cvt.rn.f16x2.e2m1x2 %3, b2;\n\t"
+          "cvt.rn.f16x2.e2m1x2 %4, b3;\n\t}"
+          : "=r"(word[w8]), "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3])
+          : "f"(q[0]), "f"(q[1]), "f"(q[2]), "f"(q[3]), "f"(q[4]), "f"(q[5]), "f"(q[6]),
+            "f"(q[7]));
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        res[8 * u + 2 * i] = __uint_as_float(w[i] << 16);
-        res[8 * u + 2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+        // low half = the low nibble's value (element 2i), high half element 2i + 1
+        const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&h[i]));
+        res[8 * w8 + 2 * i] = fmaf(-v.x, scale, res[8 * w8 + 2 * i]);
+        res[8 * w8 + 2 * i + 1] = fmaf(-v.y, scale, res[8 * w8 + 2 * i + 1]);
       }
     }
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float m = 0.0f;
-#pragma unroll
-      for (int i = 0; i < 32; ++i) m = fmaxf(m, fabsf(res[i]));
-      // smallest e with m <= 6 * 2^e: e = ceil(log2(m / 6)) from the bits
-      int e = -127;
-      if (m > 0.0f) {
-        const uint32_t qb = __float_as_uint(m / 6.0f);
-        const int ex = (int)(qb >> 23) - 127;
-        e = ex + ((qb & 0x7fffffu) != 0u ? 1 : 0);
-        if (ex == -127) e = -126;  // subnormal quotient
-        e = e < -127 ? -127 : (e > 127 ? 127 : e);
-      }
-      const float scale = pow2f(e);
-      const float inv = e == -127 ? 0.0f : pow2f(-e);
-      uint32_t word[4] = {0, 0, 0, 0};
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const uint32_t c = e == -127 ? 0u : e2m1_encode(res[i] * inv);
-        word[i / 8] |= c << (4 * (i % 8));
-        res[i] -= e2m1_value(c) * scale;
-      }
-      *reinterpret_cast<uint4*>(packed + rows[j] * (K / 2) + g * 16) =
-          make_uint4(word[0], word[1], word[2], word[3]);
-      scales_blocked[blocked_sf_offset(rows[j], g, ng)] = static_cast<uint8_t>(e + 127);
-    }
+    *reinterpret_cast<uint4*>(packed + rows[j] * (K / 2) + g * 16) =
+        make_uint4(word[0], word[1], word[2], word[3]);
+    scales_blocked[blocked_sf_offset(rows[j], g, ng)] = static_cast<uint8_t>(e + 127);
   }
 }
 
@@ -499,11 +529,13 @@ cudaError_t launch_mxfp4_terms_segments(const uint16_t* src, int K, const int32_
                                         const int32_t* seg_start, const int32_t* seg_count,
                                         const int32_t* qprefix, int nseg, int bn,
                                         int64_t max_slots, uint8_t* packed,
-                                        uint8_t* scales_blocked, cudaStream_t st) {
+                                        uint8_t* scales_blocked, uint32_t* err, cudaStream_t st) {
   if (max_slots <= 0) return cudaSuccess;
+  if (K % 32) return cudaErrorInvalidValue;
   const int warps = 8;
-  mxfp4_terms_segments_kernel<<<(unsigned)((max_slots + warps - 1) / warps), warps * 32, 0, st>>>(
-      src, K, row_token, seg_start, seg_count, qprefix, nseg, bn, packed, scales_blocked);
+  const int64_t nwarps = max_slots * ((K / 32 + 31) / 32);
+  mxfp4_terms_segments_kernel<<<(unsigned)((nwarps + warps - 1) / warps), warps * 32, 0, st>>>(
+      src, K, row_token, seg_start, seg_count, qprefix, nseg, bn, packed, scales_blocked, err);
   return cudaGetLastError();
 }
 

@@ -11,7 +11,11 @@
 // One CTA per 128-token tile: the 128 x 256 FP32 logit tile lives in TMEM
 // (kind::f16, BF16 inputs, K = 16 per MMA); each epilogue thread owns one
 // token (one TMEM lane) and reads its 256 logits 32 columns at a time.
+// Split mode (gridDim.y > 1, small batches): CTA (tile, y) contracts K-steps
+// [y * ks_per, (y + 1) * ks_per) and writes its partial logits to plane y of
+// `partials`; topk_kernel sums the planes in order and selects.
 #include <cuda.h>
+#include <algorithm>
 #include <cstdint>
 
 #include "fp4_codec.h"
@@ -37,7 +41,8 @@ __global__ void __launch_bounds__(192, 1)
                      const __grid_constant__ CUtensorMap tmap_w, const float* __restrict__ bias,
                      int T, int H, int E, int k, uint32_t tmem_cols, float routed_scale,
                      float* __restrict__ logits, int32_t* __restrict__ ids,
-                     float* __restrict__ weights, uint32_t* err) {
+                     float* __restrict__ weights, uint32_t* err, int ks_per,
+                     float* __restrict__ partials) {
   constexpr int kMaxK = KL;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -50,7 +55,9 @@ __global__ void __launch_bounds__(192, 1)
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int t0 = blockIdx.x * kTok;
-  const int ksteps = H / kKStage;
+  const bool split = gridDim.y > 1;
+  const int ks_begin = split ? (int)blockIdx.y * ks_per : 0;
+  const int ks_end = split ? min(H / kKStage, ks_begin + ks_per) : H / kKStage;
   for (int i = threadIdx.x; i < kMaxExp; i += blockDim.x) s_bias[i] = i < E ? bias[i] : 0.0f;
   const uint32_t b_bytes = (uint32_t)E * 128;
   if (threadIdx.x == 0) {
@@ -76,7 +83,7 @@ __global__ void __launch_bounds__(192, 1)
       tma_prefetch_desc(&tmap_x);
       tma_prefetch_desc(&tmap_w);
       uint32_t phase = 0;
-      for (int ks = 0, stage = 0; ks < ksteps; ++ks) {
+      for (int ks = ks_begin, stage = 0; ks < ks_end; ++ks) {
         if (!mbar_wait(&empty[stage], phase ^ 1u, err)) break;
         uint8_t* sa = smem + stage * kStageBytes;
         mbar_arrive_expect_tx(&full[stage], kABytes + b_bytes);
@@ -94,7 +101,7 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t idesc = idesc_bf16(kTok, (uint32_t)E);
       uint32_t phase = 0;
       bool ok = true;
-      for (int ks = 0, stage = 0; ks < ksteps; ++ks) {
+      for (int ks = ks_begin, stage = 0; ks < ks_end; ++ks) {
         if (!mbar_wait(&full[stage], phase, err)) {
           ok = false;
           break;
@@ -105,7 +112,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
         for (int c = 0; c < 4; ++c)
           mma_bf16(tmem, desc_kmajor_sw128(a + 32 * c), desc_kmajor_sw128(b + 32 * c), idesc,
-                   (ks | c) != 0 ? 1u : 0u);
+                   (ks != ks_begin || c != 0) ? 1u : 0u);
         tc_commit(&empty[stage]);
         if (++stage == kStages) {
           stage = 0;
@@ -119,7 +126,25 @@ __global__ void __launch_bounds__(192, 1)
   } else {
     const int q = warp & 3;
     const int t = t0 + 32 * q + lane;
-    if (mbar_wait(done, 0, err)) {
+    if (split) {
+      if (mbar_wait(done, 0, err)) {
+        tc_fence_after();
+        float* dst = partials + (int64_t)blockIdx.y * T * E + (int64_t)t * E;
+        for (int c0 = 0; c0 < E; c0 += 32) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(tmem + ((uint32_t)(32 * q) << 16) + c0, v);
+          tmem_ld_wait(v);
+          if (t < T) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+              if (c0 + i < E)
+                *reinterpret_cast<float4*>(dst + c0 + i) =
+                    make_float4(__uint_as_float(v[i]), __uint_as_float(v[i + 1]),
+                                __uint_as_float(v[i + 2]), __uint_as_float(v[i + 3]));
+          }
+        }
+      }
+    } else if (mbar_wait(done, 0, err)) {
       tc_fence_after();
       float top_v[kMaxK], top_s[kMaxK];
       int top_i[kMaxK];
@@ -192,14 +217,15 @@ __global__ void __launch_bounds__(192, 1)
 template <int KL>
 cudaError_t launch_kl(const CUtensorMap* tx, const CUtensorMap* tw, const float* bias, int T,
                       int H, int E, int k, float scale, float* logits, int32_t* ids,
-                      float* weights, uint32_t* err, cudaStream_t st) {
+                      float* weights, uint32_t* err, cudaStream_t st, int nsplit, int ks_per,
+                      float* partials) {
   uint32_t cols = 32;
   while (cols < (uint32_t)E) cols <<= 1;
   cudaError_t e = cudaFuncSetAttribute(router_tc_kernel<KL>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem);
   if (e != cudaSuccess) return e;
-  router_tc_kernel<KL><<<(T + kTok - 1) / kTok, 192, kSmem, st>>>(
-      *tx, *tw, bias, T, H, E, k, cols, scale, logits, ids, weights, err);
+  router_tc_kernel<KL><<<dim3((T + kTok - 1) / kTok, nsplit), 192, kSmem, st>>>(
+      *tx, *tw, bias, T, H, E, k, cols, scale, logits, ids, weights, err, ks_per, partials);
   return cudaGetLastError();
 }
 
@@ -210,17 +236,51 @@ bool router_tc_supported(int E, int H, int k) {
          k <= E;
 }
 
+// logits[i] = sum of the nsplit partial planes at i, added in plane order.
+__global__ void sum_partials_kernel(const float* __restrict__ partials, int nsplit, int64_t n,
+                                    float* __restrict__ logits) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float v = partials[i];
+#pragma unroll 8
+  for (int p = 1; p < nsplit; ++p) v = f_add(v, partials[(int64_t)p * n + i]);
+  logits[i] = v;
+}
+
+size_t router_partials_floats(int num_sms, int E) {
+  // nsplit * T <= (num_sms / tiles) * tiles * 128
+  return (size_t)(num_sms + 1) * kTok * E;
+}
+
 cudaError_t launch_router_tc(const CUtensorMap* tmap_x, const CUtensorMap* tmap_w,
                              const float* bias, int T, int H, int E, int k, float routed_scale,
                              float* logits, int32_t* ids, float* weights, uint32_t* err,
-                             cudaStream_t st) {
+                             cudaStream_t st, float* partials, int num_sms, int* launches) {
   if (!router_tc_supported(E, H, k)) return cudaErrorInvalidValue;
+  if (launches) *launches = 0;
   if (T == 0) return cudaSuccess;
-  if (k <= 8)
-    return launch_kl<8>(tmap_x, tmap_w, bias, T, H, E, k, routed_scale, logits, ids, weights,
-                        err, st);
-  return launch_kl<16>(tmap_x, tmap_w, bias, T, H, E, k, routed_scale, logits, ids, weights,
-                       err, st);
+  const int tiles = (T + kTok - 1) / kTok;
+  const int ksteps = H / kKStage;
+  // K-split count: fill the SMs, at least 4 K-steps per CTA
+  int nsplit = partials && num_sms > 0 ? num_sms / tiles : 1;
+  nsplit = std::max(1, std::min(nsplit, ksteps / 4));
+  const int ks_per = (ksteps + nsplit - 1) / nsplit;
+  nsplit = (ksteps + ks_per - 1) / ks_per;
+  cudaError_t e =
+      k <= 8 ? launch_kl<8>(tmap_x, tmap_w, bias, T, H, E, k, routed_scale, logits, ids, weights,
+                            err, st, nsplit, ks_per, partials)
+             : launch_kl<16>(tmap_x, tmap_w, bias, T, H, E, k, routed_scale, logits, ids,
+                             weights, err, st, nsplit, ks_per, partials);
+  if (e != cudaSuccess) return e;
+  if (launches) *launches = 1;
+  if (nsplit == 1) return cudaSuccess;
+  if (launches) *launches = 3;
+  if (!logits) return cudaErrorInvalidValue;
+  const int64_t n = (int64_t)T * E;
+  sum_partials_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(partials, nsplit, n, logits);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  return launch_topk(logits, 0, bias, T, E, k, routed_scale, ids, weights, err, st);
 }
 
 }  // namespace glm5x
