@@ -178,6 +178,25 @@ glm5x_status glm5x_moe_forward_host(glm5x_moe* moe, const uint16_t* hidden_bf16,
 glm5x_status glm5x_moe_forward_routed(glm5x_moe* moe, const void* hidden_bf16, int64_t tokens,
                                       const int32_t* ids, const float* weights, float* out,
                                       void* stream);
+/* Expert-parallel building blocks (experts sharded across
+ * ranks by config.expert_begin / expert_count, tokens exchanged by the
+ * caller's all-to-all). The reference has no expert-parallel API; these
+ * replace the per-rank halves of its single-process expert path
+ * (layer10_moe.py:760-847 + 954-961).
+ *
+ * glm5x_moe_route: router only (logits, sigmoid + bias, top-k, renormalize,
+ * x routed_scaling) over `tokens` BF16 rows on the device; ids/weights
+ * [tokens, top_k], logits [tokens, num_experts] (NULL: internal buffer). */
+glm5x_status glm5x_moe_route(glm5x_moe* moe, const void* hidden_bf16, int64_t tokens,
+                             int32_t* ids, float* weights, float* logits, void* stream);
+/* glm5x_moe_forward_expert_rows: rows [R, hidden] BF16 dispatched to this
+ * engine, ids [R, top_k] GLOBAL expert ids (slots whose expert this engine
+ * does not hold, or -1, are skipped), weights [R, top_k]. out[r] = sum over
+ * the held slots of weight * expert(row r), plus the shared expert for rows
+ * r < shared_rows. FP32 out [R, hidden]. */
+glm5x_status glm5x_moe_forward_expert_rows(glm5x_moe* moe, const void* rows_bf16, int64_t rows,
+                                           const int32_t* ids, const float* weights,
+                                           int64_t shared_rows, float* out, void* stream);
 /* Routing of the last forward (synchronizes): ids/weights [T, top_k] in
  * descending choice order, logits [T, num_experts] (may be NULL). */
 glm5x_status glm5x_moe_last_routing(glm5x_moe* moe, int32_t* ids, float* weights,

@@ -75,9 +75,13 @@ cudaError_t launch_topk(const float* in, int values_are_scores, const float* bia
                         cudaStream_t st);
 // rows_per: operand rows per (token, slot) -- 1 for NVFP4, 4 for the MXFP4
 // four-term activation expansion (pos and row_token refer to the first).
+// ids in [begin, begin + count) -> id - begin, others -> -1.
+cudaError_t launch_map_local_ids(const int32_t* ids, int64_t n, int begin, int count,
+                                 int32_t* out, cudaStream_t st);
 cudaError_t launch_permute(const int32_t* ids, const float* weights, const float* token_amax,
                            int T, int k, int E, int has_shared, int bn, PermuteBuffers b,
-                           uint32_t* err, cudaStream_t st, int rows_per = 1);
+                           uint32_t* err, cudaStream_t st, int rows_per = 1,
+                           int skip_invalid = 0, int shared_rows = -1);
 
 // ------------------------------------------------------------ router_tc.cu
 // BF16 router logits on tcgen05 + sigmoid/bias/top-k epilogue. tmap_x: hidden

@@ -147,6 +147,7 @@ struct glm5x_moe {
   uint32_t* err = nullptr;
   float *token_amax = nullptr, *logits = nullptr, *topk_w = nullptr;
   int32_t* topk_ids = nullptr;
+  int32_t* ids_local = nullptr;  // expert-parallel rows: global -> local expert ids
   PermuteBuffers pb{};
   uint8_t *act_packed = nullptr, *act_sf = nullptr, *h_packed = nullptr, *h_sf = nullptr;
   float *act_global = nullptr, *h_global = nullptr;
@@ -353,6 +354,7 @@ glm5x_status glm5x_moe_create(const glm5x_moe_config* cfg, int device, glm5x_moe
   ok &= m->alloc(&m->logits, (size_t)T * E);
   ok &= m->alloc(&m->topk_w, (size_t)T * k);
   ok &= m->alloc(&m->topk_ids, (size_t)T * k);
+  ok &= m->alloc(&m->ids_local, (size_t)T * k);
   ok &= m->alloc(&m->pb.chunk_count, (size_t)((T + 255) / 256) * E);
   ok &= m->alloc(&m->pb.rank, (size_t)T * k);
   ok &= m->alloc(&m->pb.seg_count, (size_t)nseg + 1);
@@ -664,19 +666,25 @@ glm5x_status glm5x_moe_load_sidecar(glm5x_moe* m, int32_t expert, const char* pa
   return glm5x_moe_load_expert_mxfp4(m, expert, &mats[0], &mats[1], &mats[2]);
 }
 
+// ep_rows: the rows are tokens dispatched to this engine by expert-parallel
+// ranks; ids_in holds global expert ids, slots of experts held elsewhere are
+// skipped, and only rows < shared_rows take the shared expert.
 static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
                                 const int32_t* ids_in, const float* w_in, float* out,
-                                cudaStream_t st) {
+                                cudaStream_t st, bool ep_rows = false, int64_t shared_rows = -1) {
   if (T64 <= 0 || T64 > m->cfg.max_tokens)
     return m->fail(GLM5X_INVALID_EXTENT, "tokens %lld outside [1, %d]", (long long)T64,
                    m->cfg.max_tokens);
-  if (m->E_loc != m->cfg.num_experts)
-    return m->fail(GLM5X_INVALID_STATE, "expert-parallel engines forward through the EP API");
+  if (!ep_rows && m->E_loc != m->cfg.num_experts)
+    return m->fail(GLM5X_INVALID_STATE,
+                   "expert-parallel engines run glm5x_moe_forward_expert_rows");
+  if (ep_rows && !ids_in) return m->fail(GLM5X_INVALID_STATE, "expert rows need ids");
   for (int s = 0; s < m->nseg; ++s)
     if (!m->loaded[s]) return m->fail(GLM5X_INVALID_STATE, "expert slot %d not loaded", s);
   if (!ids_in && !m->router_set) return m->fail(GLM5X_INVALID_STATE, "router not set");
   const int T = static_cast<int>(T64);
   const int H = m->H(), I = m->I(), E = m->cfg.num_experts, k = m->K();
+  const int E_perm = ep_rows ? m->E_loc : E;  // segments the permutation builds
   const int hs = m->cfg.has_shared ? 1 : 0;
   int bn = pick_bn(m, T);
   // tiles narrower than 128 rows each take a 128-row block: make sure the
@@ -719,8 +727,16 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
   }
   mark(2);
   mark(3);
-  G5_CHECK(m, launch_permute(ids, wts, m->token_amax, T, k, E, hs, bn, m->pb, m->err, st,
-                             m->terms()),
+  if (ep_rows) {
+    G5_CHECK(m, launch_map_local_ids(ids_in, (int64_t)T * k, m->cfg.expert_begin, m->E_loc,
+                                     m->ids_local, st),
+             "local ids");
+    ids = m->ids_local;
+    ++launches;
+  }
+  G5_CHECK(m, launch_permute(ids, wts, m->token_amax, T, k, E_perm, hs, bn, m->pb, m->err, st,
+                             m->terms(), ep_rows ? 1 : 0,
+                             shared_rows < 0 ? -1 : (int)std::min<int64_t>(shared_rows, T)),
            "permute");
   launches += 3;
   const int64_t max_rows = (int64_t)T * m->kk() + (int64_t)m->nseg * 8;
@@ -827,6 +843,45 @@ glm5x_status glm5x_moe_forward_routed(glm5x_moe* m, const void* hidden, int64_t 
   cudaSetDevice(m->device);
   cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : m->stream;
   return run_forward(m, static_cast<const uint16_t*>(hidden), T, ids, weights, out, st);
+}
+
+glm5x_status glm5x_moe_forward_expert_rows(glm5x_moe* m, const void* rows, int64_t R,
+                                           const int32_t* ids, const float* weights,
+                                           int64_t shared_rows, float* out, void* stream) {
+  if (!m || !rows || !out || !ids || !weights)
+    return fail_global(GLM5X_INVALID_STATE, "null argument");
+  if (shared_rows < 0 || shared_rows > R)
+    return m->fail(GLM5X_INVALID_EXTENT, "shared_rows outside [0, rows]");
+  if (shared_rows > 0 && !m->cfg.has_shared)
+    return m->fail(GLM5X_INVALID_STATE, "engine has no shared expert");
+  cudaSetDevice(m->device);
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : m->stream;
+  return run_forward(m, static_cast<const uint16_t*>(rows), R, ids, weights, out, st, true,
+                     shared_rows);
+}
+
+glm5x_status glm5x_moe_route(glm5x_moe* m, const void* hidden, int64_t T, int32_t* ids,
+                             float* weights, float* logits, void* stream) {
+  if (!m || !hidden || !ids || !weights) return fail_global(GLM5X_INVALID_STATE, "null argument");
+  if (!m->router_set) return m->fail(GLM5X_INVALID_STATE, "router not set");
+  if (T <= 0 || T > m->cfg.max_tokens)
+    return m->fail(GLM5X_INVALID_EXTENT, "tokens %lld outside [1, %d]", (long long)T,
+                   m->cfg.max_tokens);
+  if (reinterpret_cast<uintptr_t>(hidden) % 16)
+    return m->fail(GLM5X_INVALID_EXTENT, "hidden must be 16-byte aligned");
+  cudaSetDevice(m->device);
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : m->stream;
+  CUtensorMap tm_x;
+  if (!make_tmap_bf16(&tm_x, hidden, m->H(), T, 128))
+    return m->fail(GLM5X_BACKEND_UNAVAILABLE, "hidden tensor map");
+  int rl = 0;
+  G5_CHECK(m, launch_router_tc(&tm_x, &m->tm_router, m->router_bias, (int)T, m->H(),
+                               m->cfg.num_experts, m->K(), m->cfg.routed_scaling,
+                               logits ? logits : m->logits, ids, weights, m->err, st,
+                               m->router_partials, m->num_sms, &rl),
+           "router");
+  m->stats.kernel_launches += rl;
+  return GLM5X_OK;
 }
 
 glm5x_status glm5x_moe_forward_host(glm5x_moe* m, const uint16_t* hidden, int64_t T,

@@ -111,10 +111,13 @@ __global__ void topk_kernel(const float* __restrict__ in, int values_are_scores,
 constexpr int kChunk = 256;  // tokens per counting chunk
 
 // Per 256-token chunk: per-expert counts and each (token, slot)'s rank among
-// the chunk's tokens routed to the same expert (stable). E <= 256.
+// the chunk's tokens routed to the same expert (stable). E <= 256. With
+// skip_invalid, an id outside [0, E) marks a slot with no expert here (the
+// expert-parallel engines receive rows whose other slots live on other
+// ranks); otherwise it is an error.
 __global__ void __launch_bounds__(kChunk) permute_count_kernel(
-    const int32_t* __restrict__ ids, int T, int k, int E, int32_t* __restrict__ chunk_count,
-    int32_t* __restrict__ rank, uint32_t* err) {
+    const int32_t* __restrict__ ids, int T, int k, int E, int skip_invalid,
+    int32_t* __restrict__ chunk_count, int32_t* __restrict__ rank, uint32_t* err) {
   __shared__ uint32_t bits[256][kChunk / 32];
   const int c = blockIdx.x;
   for (int i = threadIdx.x; i < 256 * (kChunk / 32); i += blockDim.x) (&bits[0][0])[i] = 0;
@@ -126,6 +129,10 @@ __global__ void __launch_bounds__(kChunk) permute_count_kernel(
     for (int s = 0; s < k; ++s) {
       int e = ids[(int64_t)t * k + s];
       if (e < 0 || e >= E) {
+        if (skip_invalid) {
+          my[s] = -1;
+          continue;
+        }
         atomicOr(err, kErrBounds);
         e = 0;
       }
@@ -143,6 +150,10 @@ __global__ void __launch_bounds__(kChunk) permute_count_kernel(
   if (t < T) {
     for (int s = 0; s < k; ++s) {
       const int e = my[s];
+      if (e < 0) {
+        rank[(int64_t)t * k + s] = -1;
+        continue;
+      }
       int r = __popc(bits[e][word] & ((1u << bit) - 1u));
       for (int w = 0; w < word; ++w) r += __popc(bits[e][w]);
       rank[(int64_t)t * k + s] = r;
@@ -172,7 +183,7 @@ __device__ int block_exclusive_scan(int v, int* buf, int* total) {
 // quantizer row prefix (counts rounded up to 8) and the GEMM N-tile prefix,
 // and clears the per-segment amax accumulators.
 __global__ void permute_scan_kernel(int32_t* __restrict__ chunk_count, int nchunks, int T, int E,
-                                    int has_shared, int bn, int rows_per,
+                                    int has_shared, int shared_rows, int bn, int rows_per,
                                     int32_t* __restrict__ seg_count,
                                     int32_t* __restrict__ seg_start,
                                     int32_t* __restrict__ qprefix,
@@ -189,7 +200,7 @@ __global__ void permute_scan_kernel(int32_t* __restrict__ chunk_count, int nchun
       count += v;
     }
   } else if (e == E && has_shared) {
-    count = T;
+    count = shared_rows;  // tokens 0 .. shared_rows - 1 take the shared expert
   }
   const bool valid = e < nseg;
   // every (token, slot) takes rows_per operand rows (4 for the MXFP4 term
@@ -220,9 +231,11 @@ __global__ void permute_scan_kernel(int32_t* __restrict__ chunk_count, int nchun
 }
 
 // One thread per (token, slot) pair, plus one per token for the shared expert.
+// Slots without an expert here (rank -1) and shared slots of tokens past
+// shared_rows get pos = -1.
 __global__ void permute_scatter_kernel(const int32_t* __restrict__ ids,
                                        const float* __restrict__ weights, int T, int k, int E,
-                                       int has_shared, int bn, int rows_per,
+                                       int has_shared, int shared_rows, int bn, int rows_per,
                                        const int32_t* __restrict__ chunk_base,
                                        const int32_t* __restrict__ rank,
                                        const int32_t* __restrict__ seg_start,
@@ -237,13 +250,21 @@ __global__ void permute_scatter_kernel(const int32_t* __restrict__ ids,
   int p, e;
   float w;
   if (s < k) {
+    const int r = rank[(int64_t)t * k + s];
+    if (r < 0) {
+      pos[idx] = -1;
+      return;
+    }
     e = ids[(int64_t)t * k + s];
     e = e < 0 || e >= E ? 0 : e;
-    p = seg_start[e] + segment_row(rows_per * (chunk_base[(int64_t)(t / kChunk) * E + e] +
-                                               rank[(int64_t)t * k + s]),
+    p = seg_start[e] + segment_row(rows_per * (chunk_base[(int64_t)(t / kChunk) * E + e] + r),
                                    bn);
     w = weights[(int64_t)t * k + s];
   } else {
+    if (t >= shared_rows) {
+      pos[idx] = -1;
+      return;
+    }
     e = E;
     p = seg_start[E] + segment_row(rows_per * t, bn);
     w = 1.0f;
@@ -252,6 +273,23 @@ __global__ void permute_scatter_kernel(const int32_t* __restrict__ ids,
   row_token[p] = t;
   row_weight[p] = w;
   atomicMax(reinterpret_cast<unsigned int*>(seg_amax + e), __float_as_uint(token_amax[t]));
+}
+
+// Global expert ids -> this engine's local ids (begin .. begin + count - 1
+// -> 0 .. count - 1), -1 for experts held elsewhere.
+__global__ void map_local_ids_kernel(const int32_t* __restrict__ ids, int64_t n, int begin,
+                                     int count, int32_t* __restrict__ out) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int e = ids[i];
+  out[i] = (e >= begin && e < begin + count) ? e - begin : -1;
+}
+
+cudaError_t launch_map_local_ids(const int32_t* ids, int64_t n, int begin, int count,
+                                 int32_t* out, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  map_local_ids_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(ids, n, begin, count, out);
+  return cudaGetLastError();
 }
 
 // ------------------------------------------------------------------ launchers
@@ -267,21 +305,25 @@ cudaError_t launch_topk(const float* in, int values_are_scores, const float* bia
 
 cudaError_t launch_permute(const int32_t* ids, const float* weights, const float* token_amax,
                            int T, int k, int E, int has_shared, int bn, PermuteBuffers b,
-                           uint32_t* err, cudaStream_t st, int rows_per) {
+                           uint32_t* err, cudaStream_t st, int rows_per, int skip_invalid,
+                           int shared_rows) {
   const int nchunks = (T + kChunk - 1) / kChunk;
+  if (shared_rows < 0 || shared_rows > T) shared_rows = T;
   if (T > 0) {
-    permute_count_kernel<<<nchunks, kChunk, 0, st>>>(ids, T, k, E, b.chunk_count, b.rank, err);
+    permute_count_kernel<<<nchunks, kChunk, 0, st>>>(ids, T, k, E, skip_invalid, b.chunk_count,
+                                                     b.rank, err);
   }
   const int nseg = E + has_shared;
   int threads = 32;
   while (threads < nseg + 1) threads <<= 1;
   permute_scan_kernel<<<1, threads, threads * sizeof(int), st>>>(
-      b.chunk_count, nchunks, T, E, has_shared, bn, rows_per, b.seg_count, b.seg_start, b.qprefix,
-      b.ntile_prefix, b.seg_amax, b.h_amax);
+      b.chunk_count, nchunks, T, E, has_shared, shared_rows, bn, rows_per, b.seg_count,
+      b.seg_start, b.qprefix, b.ntile_prefix, b.seg_amax, b.h_amax);
   const int64_t n = (int64_t)T * (k + has_shared);
   if (n > 0) {
     permute_scatter_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(
-        ids, weights, T, k, E, has_shared, bn, rows_per, b.chunk_count, b.rank, b.seg_start,
+        ids, weights, T, k, E, has_shared, shared_rows, bn, rows_per, b.chunk_count, b.rank,
+        b.seg_start,
         token_amax, b.pos,
         b.row_token, b.row_weight, b.seg_amax);
   }

@@ -69,6 +69,7 @@ __global__ void combine_kernel(const uint16_t* __restrict__ y, const int32_t* __
   for (int v = threadIdx.x; v < H / 8; v += blockDim.x) {
     float acc[8] = {};
     for (int s = 0; s < kk; ++s) {
+      if (rows[s] < 0) continue;  // slot with no expert on this engine
       const uint4 q = __ldg(reinterpret_cast<const uint4*>(y + (int64_t)rows[s] * H) + v);
       const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll

@@ -162,6 +162,37 @@ class GLM5XMoELayer:
                                                      _stream()), self._h)
         return out
 
+    def route(self, hidden: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """Router only: (ids [T, k] int32, weights [T, k] fp32) on the device."""
+        flat = hidden.reshape(-1, self.hidden_size).to(torch.bfloat16).contiguous()
+        T = flat.shape[0]
+        ids = torch.empty((T, self.top_k), dtype=torch.int32, device=self.device)
+        w = torch.empty((T, self.top_k), dtype=torch.float32, device=self.device)
+        with torch.cuda.device(self.device):
+            N.check(N.lib().glm5x_moe_route(self._h, flat.data_ptr(), T, ids.data_ptr(),
+                                            w.data_ptr(), None, _stream()), self._h)
+        return ids, w
+
+    def forward_expert_rows(self, rows: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
+                            shared_rows: int = 0) -> torch.Tensor:
+        """Experts held by this engine over dispatched rows: ids are global
+        expert ids (others / -1 skipped); rows < shared_rows also take the
+        shared expert. Returns FP32 [R, H]."""
+        flat = rows.reshape(-1, self.hidden_size).to(torch.bfloat16).contiguous()
+        R = flat.shape[0]
+        out = torch.empty((R, self.hidden_size), dtype=torch.float32, device=self.device)
+        if R == 0:
+            return out
+        ids = ids.to(device=self.device, dtype=torch.int32).contiguous()
+        weights = weights.to(device=self.device, dtype=torch.float32).contiguous()
+        if tuple(ids.shape) != (R, self.top_k) or tuple(weights.shape) != (R, self.top_k):
+            raise ValueError("GLM5X_ROUTING_SHAPE")
+        with torch.cuda.device(self.device):
+            N.check(N.lib().glm5x_moe_forward_expert_rows(
+                self._h, flat.data_ptr(), R, ids.data_ptr(), weights.data_ptr(), shared_rows,
+                out.data_ptr(), _stream()), self._h)
+        return out
+
     def forward_host(self, hidden_bf16_host: torch.Tensor, out_host: torch.Tensor) -> None:
         """Host buffers in/out: H2D copy, forward, D2H copy, synchronize."""
         T = hidden_bf16_host.shape[0]

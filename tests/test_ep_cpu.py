@@ -1,0 +1,104 @@
+"""Expert-parallel dispatch / combine (glm5x_moe.ep) on CPU ranks over gloo.
+
+The engine is a CPU stand-in with the same two calls as the GPU engine
+(route, forward_expert_rows): every expert is a fixed linear map, so the
+expert-parallel result must equal the single-process sum
+out[t] = shared(x_t) + sum_s w[t,s] * expert_{ids[t,s]}(x_t) up to FP32 summation
+order. Covers worlds 2 and 4, ranks that receive no rows, tokens whose
+experts all live on one rank, and uneven token counts per rank.
+"""
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+H, E, K = 32, 16, 4
+
+
+class FakeEngine:
+    def __init__(self, begin: int, count: int, seed: int = 0) -> None:
+        g = torch.Generator().manual_seed(seed)
+        self.router = torch.randn(H, E, generator=g)
+        self.experts = torch.randn(E, H, H, generator=g) * 0.1
+        self.shared = torch.randn(H, H, generator=g) * 0.1
+        self.bias = torch.zeros(E)
+        self.begin, self.count = begin, count
+
+    def route(self, x: torch.Tensor):
+        logits = x.float() @ self.router + self.bias
+        # stable: descending score, ties to the lower expert id
+        order = torch.sort(-logits, dim=1, stable=True).indices[:, :K]
+        w = torch.softmax(torch.gather(logits, 1, order), dim=1)
+        return order.to(torch.int32), w
+
+    def forward_expert_rows(self, rows, ids, w, shared_rows=0):
+        xf = rows.float()
+        out = torch.zeros((rows.shape[0], H))
+        for r in range(rows.shape[0]):
+            for s in range(K):
+                e = int(ids[r, s])
+                if self.begin <= e < self.begin + self.count:
+                    out[r] += float(w[r, s]) * (xf[r] @ self.experts[e])
+            if r < shared_rows:
+                out[r] += xf[r] @ self.shared
+        return out
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank: int, world: int, port: int, tokens: list[int], skew: bool, q) -> None:
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from glm5x_moe.ep import ExpertParallelMoE, expert_range
+        begin, count = expert_range(rank, world, E)
+        eng = FakeEngine(begin, count)
+        if skew:
+            # every token prefers experts 0..3 (all on rank 0)
+            eng.bias[:4] = 50.0
+        ep = ExpertParallelMoE(eng, rank=rank, world=world, num_experts=E, top_k=K,
+                               hidden_size=H)
+        g = torch.Generator().manual_seed(100 + rank)
+        x = torch.randn(tokens[rank], H, generator=g).to(torch.bfloat16)
+        out = ep(x)
+        ref_eng = FakeEngine(0, E)
+        if skew:
+            ref_eng.bias[:4] = 50.0
+        ids, w = ref_eng.route(x)
+        want = ref_eng.forward_expert_rows(x, ids, w, shared_rows=x.shape[0])
+        err = float((out - want).abs().max() / want.abs().max())
+        q.put((rank, err, ep.last_counts))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,tokens,skew", [(2, [7, 5], False), (4, [6, 1, 9, 3], False),
+                                               (2, [8, 4], True)])
+def test_expert_parallel_matches_single_process(world, tokens, skew):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, tokens, skew, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    res = sorted(q.get(timeout=10) for _ in range(world))
+    for rank, err, counts in res:
+        assert err < 1e-5, (rank, err)
+    if skew:
+        # with all top experts on rank 0, rank 1 receives nothing
+        sent, recv = res[1][2]
+        assert sum(recv) == 0 and sent[0] == tokens[1]
