@@ -275,6 +275,14 @@ glm5x_status glm5x_mxfp4_decode(const uint8_t* packed, const uint8_t* scales, in
 glm5x_status glm5x_select_routing(const float* scores, const float* bias, int64_t tokens,
                                   int32_t num_experts, int32_t top_k, float routed_scale,
                                   int32_t* ids, float* weights, void* stream);
+/* out[t] (+)= sum over s < slots of rows[pos[t, s]] (BF16 rows, FP32 sums in
+ * slot order; pos < 0 = absent), device buffers: the weighted scatter of
+ * scatter_expert_major_outputs (runtime/src/expert_major.cpp:148-196) /
+ * index_add_ (layer10_moe.py:843-846) in gather form with a fixed order. The
+ * expert-parallel layer adds each token's per-rank partial sums with it. */
+glm5x_status glm5x_combine_rows(const void* rows_bf16, const int32_t* pos, int64_t tokens,
+                                int32_t slots, int64_t hidden, float* out, int32_t accumulate,
+                                void* stream);
 /* The device expert-major permutation (build_expert_major_plan,
  * runtime/src/expert_major.cpp:12-98): ids [T,k] -> seg_count [E],
  * seg_start [E+1] (128-aligned), pos [T,k], row_token [rows]. */

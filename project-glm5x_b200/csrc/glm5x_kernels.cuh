@@ -144,9 +144,10 @@ cudaError_t launch_nvfp4_pair_gemm(int epi, const CUtensorMap* tmap_a, const CUt
                                    const GemmParams& p, int grid, cudaStream_t st);
 
 // ------------------------------------------------------------ combine.cu
-// out[t, :] = sum_{s < kk} y[pos[t, s], :] (FP32 accumulation of BF16 rows).
+// out[t, :] (+)= sum_{s < kk} y[pos[t, s], :] in slot order (FP32
+// accumulation of BF16 rows); pos < 0 marks an absent slot. kk <= 32.
 cudaError_t launch_combine(const uint16_t* y, const int32_t* pos, int T, int kk, int H,
-                           float* out, cudaStream_t st);
+                           float* out, cudaStream_t st, int accumulate = 0);
 
 // ------------------------------------------------------------ weights.cu
 // Interleave gate [I, K] and up [I, K] (packed NVFP4 + blocked scales) into

@@ -1176,6 +1176,18 @@ glm5x_status glm5x_select_routing(const float* scores, const float* bias, int64_
   return sync_error(st, err, 0, "select routing");
 }
 
+glm5x_status glm5x_combine_rows(const void* rows_bf16, const int32_t* pos, int64_t T,
+                                int32_t slots, int64_t hidden, float* out, int32_t accumulate,
+                                void* stream) {
+  if (!rows_bf16 || !pos || !out || T <= 0 || slots <= 0 || slots > 32 || hidden <= 0 ||
+      hidden % 8)
+    return fail_global(GLM5X_INVALID_EXTENT, "combine_rows: bad extents or null pointer");
+  if (launch_combine(static_cast<const uint16_t*>(rows_bf16), pos, (int)T, slots, (int)hidden,
+                     out, as_stream(stream), accumulate ? 1 : 0) != cudaSuccess)
+    return fail_global(GLM5X_DEVICE_ERROR, "combine_rows launch");
+  return GLM5X_OK;
+}
+
 glm5x_status glm5x_expert_major_plan(const int32_t* ids, int64_t T, int32_t k, int32_t E,
                                      int32_t* seg_count, int32_t* seg_start, int32_t* pos,
                                      int32_t* row_token, void* stream) {

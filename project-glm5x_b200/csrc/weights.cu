@@ -59,9 +59,10 @@ __global__ void scales_to_blocked_kernel(const uint8_t* __restrict__ rm, int64_t
   blocked[blocked_sf_offset(r, c, sf_cols)] = rm[idx];
 }
 
-// One block per token; 8 BF16 (16 bytes) per vector.
+// One block per token; 8 BF16 (16 bytes) per vector. accumulate: add the
+// sum to out instead of storing it.
 __global__ void combine_kernel(const uint16_t* __restrict__ y, const int32_t* __restrict__ pos,
-                               int kk, int H, float* __restrict__ out) {
+                               int kk, int H, float* __restrict__ out, int accumulate) {
   const int t = blockIdx.x;
   __shared__ int32_t rows[32];
   if (threadIdx.x < kk) rows[threadIdx.x] = pos[(int64_t)t * kk + threadIdx.x];
@@ -79,8 +80,14 @@ __global__ void combine_kernel(const uint16_t* __restrict__ y, const int32_t* __
       }
     }
     float4* o = reinterpret_cast<float4*>(out + (int64_t)t * H) + 2 * v;
-    o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-    o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    if (accumulate) {
+      const float4 a = o[0], b = o[1];
+      o[0] = make_float4(a.x + acc[0], a.y + acc[1], a.z + acc[2], a.w + acc[3]);
+      o[1] = make_float4(b.x + acc[4], b.y + acc[5], b.z + acc[6], b.w + acc[7]);
+    } else {
+      o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    }
   }
 }
 
@@ -123,9 +130,10 @@ cudaError_t launch_find_byte(const uint8_t* p, int64_t n, uint32_t value, uint32
 }
 
 cudaError_t launch_combine(const uint16_t* y, const int32_t* pos, int T, int kk, int H,
-                           float* out, cudaStream_t st) {
+                           float* out, cudaStream_t st, int accumulate) {
   if (T == 0) return cudaSuccess;
-  combine_kernel<<<T, 256, 0, st>>>(y, pos, kk, H, out);
+  if (kk > 32 || H % 8) return cudaErrorInvalidValue;
+  combine_kernel<<<T, 256, 0, st>>>(y, pos, kk, H, out, accumulate);
   return cudaGetLastError();
 }
 

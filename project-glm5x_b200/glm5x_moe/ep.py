@@ -10,14 +10,14 @@ expert and the full router. A forward on rank r:
 2. dispatch: every (token, destination rank) pair whose token has at least
    one expert on that rank sends the token's BF16 row once, with its top-k
    global ids masked to that rank's experts (-1 elsewhere) and its weights;
-   counts go first (all-to-all of int64), then rows, ids and weights
-   (all-to-all-v);
+   counts go first (all-to-all of int64), then the rows and the id/weight
+   words (all-to-all-v);
 3. runs its experts over [local tokens; received rows] in one engine call:
    the local tokens take only the shared expert, the received rows only the
    held routed experts;
 4. combine: each received row's weighted sum returns to its source
-   (all-to-all-v of FP32 rows), where the partial sums of a token are added
-   in destination-rank order onto its shared-expert output.
+   (all-to-all-v of BF16 rows), where the partial sums of a token are added
+   in FP32, in destination-rank order, onto its shared-expert output.
 
 Everything runs on the caller's current stream; torch.distributed (NCCL on
 GPUs) moves the bytes. The engine is any object with route(hidden) ->
@@ -44,6 +44,36 @@ class ExpertParallelMoE:
         self.hidden_size = hidden_size
         self.group = group
         self.last_counts: tuple[list[int], list[int]] | None = None
+        self.last_local_assignments = 0
+        self._timing = False
+        self._stage_ms = [0.0, 0.0, 0.0, 0.0]
+        self._pending: list = []
+        self._timed = 0
+
+    STAGES = ("route", "dispatch", "experts", "combine")
+
+    def set_timing(self, enable: bool) -> None:
+        """Record CUDA events on the current stream at the stage boundaries."""
+        self._timing = enable
+
+    def stage_times(self) -> tuple[dict, int]:
+        """(milliseconds per stage summed since the last call, forwards)."""
+        for evs in self._pending:
+            evs[-1].synchronize()
+            for i in range(4):
+                self._stage_ms[i] += evs[i].elapsed_time(evs[i + 1])
+            self._timed += 1
+        self._pending = []
+        out = (dict(zip(self.STAGES, self._stage_ms)), self._timed)
+        self._stage_ms = [0.0, 0.0, 0.0, 0.0]
+        self._timed = 0
+        return out
+
+    def _mark(self, evs) -> None:
+        if evs is not None:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            evs.append(e)
 
     def plan(self, ids: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
         """(dest [n], token [n], counts [W]) of the dispatch pairs, ordered by
@@ -59,11 +89,16 @@ class ExpertParallelMoE:
         H = self.hidden_size
         x = hidden.reshape(-1, H).to(torch.bfloat16).contiguous()
         T = x.shape[0]
+        evs = [] if self._timing else None
+        self._mark(evs)
         ids, w = self.engine.route(x)
+        self._mark(evs)
         d_idx, t_idx, send_counts = self.plan(ids)
-        send_ids = torch.where(ids[t_idx].long() // self.per == d_idx[:, None], ids[t_idx],
-                               torch.full_like(ids[t_idx], -1)).contiguous()
-        send_w = w[t_idx].contiguous()
+        # per pair: k masked ids and k weights (as raw 32-bit words) in one row
+        sel = ids[t_idx]
+        meta = torch.cat([torch.where(sel.long() // self.per == d_idx[:, None], sel,
+                                      torch.full_like(sel, -1)),
+                          w[t_idx].view(torch.int32)], dim=1).contiguous()
         send_rows = x[t_idx].contiguous()
         recv_counts = torch.empty_like(send_counts)
         dist.all_to_all_single(recv_counts, send_counts.contiguous(), group=self.group)
@@ -75,23 +110,49 @@ class ExpertParallelMoE:
         rows = torch.empty((T + R, H), dtype=torch.bfloat16, device=x.device)
         rows[:T] = x
         dist.all_to_all_single(rows[T:], send_rows, rc, sc, group=self.group)
-        rids = torch.full((T + R, self.top_k), -1, dtype=torch.int32, device=x.device)
-        rw = torch.zeros((T + R, self.top_k), dtype=torch.float32, device=x.device)
-        dist.all_to_all_single(rids[T:], send_ids, rc, sc, group=self.group)
-        dist.all_to_all_single(rw[T:], send_w, rc, sc, group=self.group)
+        rmeta = torch.empty((T + R, 2 * self.top_k), dtype=torch.int32, device=x.device)
+        rmeta[:T, :self.top_k] = -1
+        rmeta[:T, self.top_k:] = 0
+        dist.all_to_all_single(rmeta[T:], meta, rc, sc, group=self.group)
+        rids = rmeta[:, :self.top_k]
+        rw = rmeta[:, self.top_k:].view(torch.float32)
+        self._mark(evs)
         y = self.engine.forward_expert_rows(rows, rids, rw, shared_rows=T)
-        back = torch.empty((t_idx.numel(), H), dtype=torch.float32, device=x.device)
-        dist.all_to_all_single(back, y[T:].contiguous(), sc, rc, group=self.group)
+        self._mark(evs)
+        # partial sums travel back as BF16 (each is a sum of BF16 expert
+        # outputs already; rounding it once more costs 2^-9 relative)
+        back = torch.empty((t_idx.numel(), H), dtype=torch.bfloat16, device=x.device)
+        dist.all_to_all_single(back, y[T:].to(torch.bfloat16), sc, rc, group=self.group)
         out = y[:T]
-        off = 0
-        for d in range(self.world):
-            n = sc[d]
-            if n:
-                # one row per token per destination: no index repeats within
-                # a call, so the sum order is fixed (destination order)
-                out.index_add_(0, t_idx[off:off + n], back[off:off + n])
-            off += n
+        # pos[t, d] = row of pair (t, d) in `back`, -1 if the token sent nothing
+        # to rank d; partial sums are added in destination order
+        pos = torch.full((T, self.world), -1, dtype=torch.int32, device=x.device)
+        pos[t_idx, d_idx] = torch.arange(t_idx.numel(), dtype=torch.int32, device=x.device)
+        self.combine(back, pos, out)
+        self._mark(evs)
+        if evs is not None:
+            self._pending.append(evs)
         return out.reshape(*hidden.shape[:-1], H)
+
+    @staticmethod
+    def combine(rows: torch.Tensor, pos: torch.Tensor, out: torch.Tensor) -> None:
+        """out[t] += sum_d rows[pos[t, d]] (pos < 0 skipped), FP32, fixed order.
+        Device tensors go through glm5x_combine_rows; the host loop serves
+        engines that return host tensors (the CPU stand-in of the gloo tests),
+        it is never a substitute for the device kernel."""
+        if out.is_cuda:
+            from . import _native as N
+            N.check(N.lib().glm5x_combine_rows(
+                rows.data_ptr(), pos.data_ptr(), out.shape[0], pos.shape[1], out.shape[1],
+                out.data_ptr(), 1, N.stream_arg(torch.cuda.current_stream().cuda_stream)))
+            return
+        for d in range(pos.shape[1]):
+            sel = pos[:, d] >= 0
+            out[sel] += rows[pos[sel, d].long()].float()
+
+    def count_local_assignments(self, rows_ids: torch.Tensor, begin: int) -> int:
+        """Held (row, slot) assignments among dispatched rows (synchronizes)."""
+        return int(((rows_ids >= begin) & (rows_ids < begin + self.per)).sum().item())
 
 
 def expert_range(rank: int, world: int, num_experts: int) -> tuple[int, int]:

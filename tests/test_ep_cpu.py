@@ -3,8 +3,9 @@
 The engine is a CPU stand-in with the same two calls as the GPU engine
 (route, forward_expert_rows): every expert is a fixed linear map, so the
 expert-parallel result must equal the single-process sum
-out[t] = shared(x_t) + sum_s w[t,s] * expert_{ids[t,s]}(x_t) up to FP32 summation
-order. Covers worlds 2 and 4, ranks that receive no rows, tokens whose
+out[t] = shared(x_t) + sum_s w[t,s] * expert_{ids[t,s]}(x_t) up to the BF16
+rounding of the per-destination partial sums on their way back (2^-9
+relative each) and FP32 summation order. Covers worlds 2 and 4, ranks that receive no rows, tokens whose
 experts all live on one rank, and uneven token counts per rank.
 """
 from __future__ import annotations
@@ -97,7 +98,7 @@ def test_expert_parallel_matches_single_process(world, tokens, skew):
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     res = sorted(q.get(timeout=10) for _ in range(world))
     for rank, err, counts in res:
-        assert err < 1e-5, (rank, err)
+        assert err < 5e-3, (rank, err)
     if skew:
         # with all top experts on rank 0, rank 1 receives nothing
         sent, recv = res[1][2]
