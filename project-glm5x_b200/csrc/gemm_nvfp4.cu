@@ -89,8 +89,8 @@ struct Cfg {
   static constexpr int kStageSfCols = kSfaCols + kSfbCols;
   static constexpr int kTmemCols = 512;
   static_assert(kSfBase + kStages * kStageSfCols <= kTmemCols, "TMEM budget");
-  static constexpr size_t kSmem = (size_t)kStages * kStageBytes + 1024 + 256;
-  static_assert((3 * kStages + 2 * kAcc + 1) * 8 + 4 <= 256, "barrier area");
+  static constexpr size_t kSmem = (size_t)kStages * kStageBytes + 1024 + 512;
+  static_assert((4 * kStages + 2 * kAcc + 1) * 8 + 4 <= 512, "barrier area");
   static_assert(kSmem + 3 * 4 * (kMaxSeg + 1) <= 232448, "shared memory budget");
 };
 
@@ -139,7 +139,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
   uint64_t* empty = full + C::kStages;
   uint64_t* sf_ready = empty + C::kStages;
-  uint64_t* tfull = sf_ready + C::kStages;
+  uint64_t* full_sf = sf_ready + C::kStages;  // a stage's scale chunks landed
+  uint64_t* tfull = full_sf + C::kStages;
   uint64_t* tempty = tfull + C::kAcc;
   uint64_t* drained = tempty + C::kAcc;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drained + 1);
@@ -161,6 +162,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
       mbar_init(&sf_ready[s], 4);
+      mbar_init(&full_sf[s], 1);
     }
     for (int a = 0; a < C::kAcc; ++a) {
       mbar_init(&tfull[a], 1);
@@ -226,8 +228,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int box1 = rows1 <= 0 ? 0 : (rows1 <= 32 ? 32 : (rows1 <= 64 ? 64 : 128));
         const CUtensorMap* m0 = box0 == 32 ? &tmap_b32 : (box0 == 64 ? &tmap_b64 : &tmap_b128);
         const CUtensorMap* m1 = box1 == 32 ? &tmap_b32 : (box1 == 64 ? &tmap_b64 : &tmap_b128);
-        const uint32_t bytes = C::kABytes + (box0 + box1) * kBKBytes + C::kSfaBytes +
-                               sfb_ch * C::kCh * kChunkBytes;
+        const uint32_t bytes = C::kABytes + (box0 + box1) * kBKBytes;
+        const uint32_t sf_bytes = C::kSfaBytes + sfb_ch * C::kCh * kChunkBytes;
         for (int ks = 0; ks < ks_count; ++ks) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, p.err)) {
             ok = false;
@@ -237,16 +239,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sb = sa + C::kABytes;
           uint8_t* ssfa = sb + C::kBBytes;
           uint8_t* ssfb = ssfa + C::kSfaBytes;
+          // scale chunks first, on their own barrier: the staging warps move
+          // them into TMEM while the operand tiles are still landing
+          mbar_arrive_expect_tx(&full_sf[stage], sf_bytes);
+          bulk_load(ssfa, sfa + (size_t)ks * C::kCh * kChunkBytes, C::kSfaBytes, &full_sf[stage]);
+          for (int h = 0; h < sfb_ch; ++h)
+            bulk_load(ssfb + h * C::kCh * kChunkBytes,
+                      sfb + ((size_t)h * kc_per_rb + ks * C::kCh) * kChunkBytes,
+                      C::kCh * kChunkBytes, &full_sf[stage]);
           mbar_arrive_expect_tx(&full[stage], bytes);
           tma_load_2d(sa, &tmap_a, &full[stage], ks * kBKBytes, a_row);
           tma_load_2d(sb, m0, &full[stage], ks * kBKBytes, ti.row_start);
           if (box1) tma_load_2d(sb + 128 * kBKBytes, m1, &full[stage], ks * kBKBytes,
                                 ti.row_start + 128);
-          bulk_load(ssfa, sfa + (size_t)ks * C::kCh * kChunkBytes, C::kSfaBytes, &full[stage]);
-          for (int h = 0; h < sfb_ch; ++h)
-            bulk_load(ssfb + h * C::kCh * kChunkBytes,
-                      sfb + ((size_t)h * kc_per_rb + ks * C::kCh) * kChunkBytes,
-                      C::kCh * kChunkBytes, &full[stage]);
           if (++stage == C::kStages) {
             stage = 0;
             phase ^= 1u;
@@ -333,7 +338,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!decode_tile(tile, m_tiles, p.nseg, BN, s_ntp, s_cnt, s_start, ti)) continue;
       const bool two_blocks = ti.n_valid > 128;
       for (int ks = 0; ks < ks_count; ++ks) {
-        if (!mbar_wait(&full[stage], phase, p.err)) {
+        if (!mbar_wait(&full_sf[stage], phase, p.err)) {
           ok = false;
           break;
         }

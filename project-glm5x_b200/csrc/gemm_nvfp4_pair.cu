@@ -10,12 +10,17 @@
 // scale chunks and all N rows' scale chunks (the MMA reads every column's
 // scales from each CTA's own TMEM).
 //
-// Roles (per CTA, 320 threads): warp 0 issues this CTA's TMA loads, all
-// counted on the leader CTA's full barrier; warp 1 of the leader copies the
-// scale chunks into both TMEMs and issues the pair MMAs (the peer's warp 1
-// only shares the TMEM allocation); warps 2-9 of both CTAs drain their own
-// TMEM and signal the leader when done. The leader's commits arrive on both
-// CTAs' barriers.
+// Roles (per CTA, 512 threads, four warpgroups):
+//   warp 0     this CTA's TMA loads of its weight rows and token rows,
+//              counted on the leader CTA's full barrier, plus its scale
+//              chunks (bulk copies on its own full_sf barrier);
+//   warp 1     TMEM (pair allocation); in the leader it issues the pair MMAs
+//              once both CTAs' operands have landed and both CTAs' scales are
+//              in TMEM, and its commits arrive on both CTAs' barriers;
+//   warps 2-5  scale staging into this CTA's TMEM with tcgen05.st (one warp
+//              per lane quadrant), then an arrive on the leader's sf_ready;
+//   warps 8-15 epilogue: drain this CTA's accumulator half to registers,
+//              signal the leader, then SwiGLU / routing weight and stores.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cstdint>
@@ -31,7 +36,11 @@ constexpr int kBN = 256;           // token rows per pair tile (up to 128 per CT
 constexpr int kBK = 128;           // K bytes per stage (256 FP4)
 constexpr int kChunk = 512;        // one 128-row x 4-scale chunk
 constexpr int kEpiWarps = 8;
-constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kEpiWarp0 = 8;
+constexpr int kThreads = 512;
+constexpr uint32_t kRegsLow = 80;
+constexpr uint32_t kRegsEpi = 176;
+static_assert(256 * kRegsLow + 256 * kRegsEpi <= 65536, "register split");
 constexpr int kStages = 5;
 constexpr int kABytes = 128 * kBK;           // this CTA's weight rows
 constexpr int kBBytes = 128 * kBK;           // this CTA's token rows
@@ -44,6 +53,7 @@ constexpr int kTmemCols = 512;
 static_assert(kSfBase + kStages * (kSfaCols + kSfbCols) <= kTmemCols, "TMEM budget");
 constexpr int kMaxSeg = 260;
 constexpr size_t kSmem = (size_t)kStages * kStageBytes + 1024 + 256;
+static_assert((4 * kStages + 3) * 8 + 4 <= 256, "barrier area");
 static_assert(kSmem + 3 * 4 * (kMaxSeg + 1) <= 232448, "shared memory budget");
 
 struct PairTile {
@@ -82,16 +92,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     nvfp4_pair_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                            const __grid_constant__ CUtensorMap tmap_b32,
                            const __grid_constant__ CUtensorMap tmap_b64,
-                           const __grid_constant__ CUtensorMap tmap_b128,
-                           const __grid_constant__ CUtensorMap tmap_sfa,
-                           const __grid_constant__ CUtensorMap tmap_sfb, const GemmParams p) {
+                           const __grid_constant__ CUtensorMap tmap_b128, const GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);  // leader's used
   uint64_t* empty = full + kStages;
-  uint64_t* tfull = empty + kStages;
-  uint64_t* tempty = tfull + 1;
+  uint64_t* full_sf = empty + kStages;
+  uint64_t* sf_ready = full_sf + kStages;  // leader's used
+  uint64_t* tfull = sf_ready + kStages;
+  uint64_t* tempty = tfull + 1;            // leader's used
   uint64_t* drained = tempty + 1;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drained + 1);
   __shared__ int32_t s_ntp[kMaxSeg + 1], s_cnt[kMaxSeg], s_start[kMaxSeg + 1];
@@ -113,6 +123,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
+      mbar_init(&full_sf[s], 1);
+      mbar_init(&sf_ready[s], 8);  // 4 staging warps in each CTA
     }
     mbar_init(tfull, 1);
     mbar_init(tempty, 2 * 32 * kEpiWarps);
@@ -131,12 +143,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = *tmem_holder;
   const int total_tiles = m2_tiles * s_ntp[p.nseg];
 
+  if (warp < kEpiWarp0) {
+  regs_dealloc<kRegsLow>();
   if (warp == 0) {
     // ------------------------------------------------------ TMA producer
     if (lane == 0) {
       tma_prefetch_desc(&tmap_a);
-      tma_prefetch_desc(&tmap_sfa);
-      tma_prefetch_desc(&tmap_sfb);
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -149,9 +161,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const CUtensorMap* mb = box == 32 ? &tmap_b32 : (box == 64 ? &tmap_b64 : &tmap_b128);
         const int sfb_ch = n_mma > 128 ? 2 : 1;
         const int a_row = ti.seg * p.M_per + ti.m2 * kPM + (int)rank * 128;
-        const int sfa_y = 2 * (a_row / 128) * kc_per_rb;          // 256-byte rows of the map
-        const int sfb_y = 2 * (ti.row_start / 128) * kc_per_rb;
-        const uint32_t cta_bytes = kABytes + box * kBK + kSfaBytes + sfb_ch * 4 * kChunk;
+        const uint8_t* sfa = p.sfa + (size_t)(a_row / 128) * kc_per_rb * kChunk;
+        const uint8_t* sfb = p.sfb + (size_t)(ti.row_start / 128) * kc_per_rb * kChunk;
+        const uint32_t cta_bytes = kABytes + box * kBK;
+        const uint32_t sf_bytes = kSfaBytes + sfb_ch * 4 * kChunk;
         for (int ks = 0; ks < ks_count; ++ks) {
           if (!mbar_wait_cluster(&empty[stage], phase ^ 1u, p.err)) {
             ok = false;
@@ -165,10 +178,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (leader) mbar_arrive_expect_tx(&full[stage], 2 * cta_bytes);
           tma_load_2d_pair(sa, &tmap_a, lead_full, ks * kBK, a_row);
           tma_load_2d_pair(sb, mb, lead_full, ks * kBK, ti.row_start + (int)rank * half);
-          tma_load_2d_pair(ssfa, &tmap_sfa, lead_full, 0, sfa_y + 8 * ks);
+          mbar_arrive_expect_tx(&full_sf[stage], sf_bytes);
+          bulk_load(ssfa, sfa + (size_t)ks * 4 * kChunk, kSfaBytes, &full_sf[stage]);
           for (int h = 0; h < sfb_ch; ++h)
-            tma_load_2d_pair(ssfb + h * 4 * kChunk, &tmap_sfb, lead_full, 0,
-                             sfb_y + 2 * h * kc_per_rb + 8 * ks);
+            bulk_load(ssfb + h * 4 * kChunk, sfb + ((size_t)h * kc_per_rb + ks * 4) * kChunk,
+                      4 * kChunk, &full_sf[stage]);
           if (++stage == kStages) {
             stage = 0;
             phase ^= 1u;
@@ -187,30 +201,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         PairTile ti;
         if (!decode_pair_tile(tile, m2_tiles, p.nseg, s_ntp, s_cnt, s_start, ti)) continue;
         const uint32_t n_mma = (uint32_t)((ti.n_valid + 15) & ~15);
-        const int sfb_ch = n_mma > 128 ? 2 : 1;
         const uint32_t idesc = idesc_fp4(kPM, n_mma, 0, 0, 0);
         if (!mbar_wait_cluster(tempty, acc_phase ^ 1u, p.err)) break;
         tc_fence_after();
         for (int ks = 0; ks < ks_count; ++ks) {
-          if (!mbar_wait_cluster(&full[stage], phase, p.err)) {
+          if (!mbar_wait_cluster(&full[stage], phase, p.err) ||
+              !mbar_wait_cluster(&sf_ready[stage], phase, p.err)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint8_t* sa = smem + stage * kStageBytes;
           const uint8_t* sb = sa + kABytes;
-          const uint8_t* ssfa = sb + kBBytes;
-          const uint8_t* ssfb = ssfa + kSfaBytes;
           const uint32_t sfa_col = tmem_base + kSfBase + stage * (kSfaCols + kSfbCols);
           const uint32_t sfb_col = sfa_col + kSfaCols;
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-            tmem_cp_sf_pair(sfa_col + 4 * c, desc_sf_chunk(smem_u32(ssfa + c * kChunk)));
-          for (int h = 0; h < sfb_ch; ++h)
-#pragma unroll
-            for (int c = 0; c < 4; ++c)
-              tmem_cp_sf_pair(sfb_col + 8 * c + 4 * h,
-                              desc_sf_chunk(smem_u32(ssfb + h * 4 * kChunk + c * kChunk)));
           const uint32_t a_addr = smem_u32(sa), b_addr = smem_u32(sb);
 #pragma unroll
           for (int c = 0; c < 4; ++c)
@@ -231,10 +235,64 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(drained, 0, p.err);
     }
     __syncwarp();
+  } else if (warp < 6) {
+    // ------------------------------------------------------ scale staging
+    // (both CTAs; the layout tcgen05.cp.32x128b.warpx4 writes)
+    const int q = warp & 3;
+    const uint32_t t_lane = tmem_base + ((uint32_t)(32 * q) << 16);
+    const uint32_t lead_ready0 = mapa_shared(smem_u32(&sf_ready[0]), 0);
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int tile = pair; tile < total_tiles && ok; tile += npairs) {
+      PairTile ti;
+      if (!decode_pair_tile(tile, m2_tiles, p.nseg, s_ntp, s_cnt, s_start, ti)) continue;
+      const bool two_blocks = ((ti.n_valid + 15) & ~15) > 128;
+      for (int ks = 0; ks < ks_count; ++ks) {
+        if (!mbar_wait(&full_sf[stage], phase, p.err)) {
+          ok = false;
+          break;
+        }
+        const uint8_t* ssfa = smem + stage * kStageBytes + kABytes + kBBytes;
+        const uint8_t* ssfb = ssfa + kSfaBytes;
+        const uint32_t sfa_col = kSfBase + stage * (kSfaCols + kSfbCols);
+        const uint32_t sfb_col = sfa_col + kSfaCols;
+        uint32_t r[kSfaCols];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const uint4 v = *reinterpret_cast<const uint4*>(ssfa + c * kChunk + lane * 16);
+          r[4 * c] = v.x; r[4 * c + 1] = v.y; r[4 * c + 2] = v.z; r[4 * c + 3] = v.w;
+        }
+#pragma unroll
+        for (int o = 0; o < kSfaCols; o += 8) tmem_st_32x32b_x8(t_lane + sfa_col + o, r + o);
+        // chunk c of 128-row block h -> columns 8c + 4h
+        uint32_t rb[kSfbCols];
+#pragma unroll
+        for (int g = 0; g < kSfbCols / 4; ++g) {
+          const int c = g / 2, h = g % 2;
+          uint4 v = make_uint4(0u, 0u, 0u, 0u);
+          if (h == 0 || two_blocks)
+            v = *reinterpret_cast<const uint4*>(ssfb + (h * 4 + c) * kChunk + lane * 16);
+          rb[4 * g] = v.x; rb[4 * g + 1] = v.y; rb[4 * g + 2] = v.z; rb[4 * g + 3] = v.w;
+        }
+#pragma unroll
+        for (int o = 0; o < kSfbCols; o += 8) tmem_st_32x32b_x8(t_lane + sfb_col + o, rb + o);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(lead_ready0 + stage * 8u);
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  }
   } else {
     // ------------------------------------------------------ epilogue (both CTAs)
+    regs_alloc<kRegsEpi>();
     const int q = warp & 3;
-    const int half_cols = (warp - 2) >> 2;
+    const int half_cols = (warp - kEpiWarp0) >> 2;
     const uint32_t lead_tempty = mapa_shared(smem_u32(tempty), 0);
     uint32_t acc_phase = 0;
     for (int tile = pair; tile < total_tiles; tile += npairs) {
@@ -243,6 +301,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait_cluster(tfull, acc_phase, p.err)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(32 * q) << 16);
+      // drain to registers and hand the accumulator back before the math
+      constexpr int kChunks = kBN / 64;
+      uint32_t v[kChunks][32];
+#pragma unroll
+      for (int i = 0; i < kChunks; ++i)
+        if (32 * half_cols + 64 * i < ti.n_valid)
+          tmem_ld_32x32b_x32(t_row + 32 * half_cols + 64 * i, v[i]);
+      tmem_ld_wait();
+#pragma unroll
+      for (int i = 0; i < kChunks; ++i) reg_fence(v[i]);
+      tc_fence_before();
+      mbar_arrive_cluster(lead_tempty);
+      acc_phase ^= 1u;
       const int m_tile = 2 * ti.m2 + (int)rank;  // this CTA's 128-row weight tile
       const float bscale = p.b_global[ti.seg];
       if (EPI == 0) {
@@ -252,16 +323,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int j = m_tile * 64 + 16 * q + (lane & 15);
         const int hcols = p.M_per / 2;
         float amax = 0.0f;
-        for (int c0 = 32 * half_cols; c0 < ti.n_valid; c0 += 64) {
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(t_row + c0, v);
-          tmem_ld_wait(v);
+#pragma unroll
+        for (int ch = 0; ch < kChunks; ++ch) {
+          const int c0 = 32 * half_cols + 64 * ch;
+          if (c0 >= ti.n_valid) break;
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const float send = __uint_as_float(lo ? v[i + 16] : v[i]);
+            const float send = __uint_as_float(lo ? v[ch][i + 16] : v[ch][i]);
             const float recv = __shfl_xor_sync(0xffffffffu, send, 16);
-            const float gate = lo ? __uint_as_float(v[i]) * s_gate : recv * s_gate;
-            const float up = lo ? recv * s_up : __uint_as_float(v[i + 16]) * s_up;
+            const float gate = lo ? __uint_as_float(v[ch][i]) * s_gate : recv * s_gate;
+            const float up = lo ? recv * s_up : __uint_as_float(v[ch][i + 16]) * s_up;
             const int col = c0 + i + (lo ? 0 : 16);
             if (col < ti.n_valid) {
               const float h = __fdividef(gate, 1.0f + __expf(-gate)) * up;
@@ -277,23 +348,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else {
         const float scale = bscale * p.a_global[ti.seg];
         const int o = m_tile * 128 + 32 * q + lane;
-        for (int c0 = 32 * half_cols; c0 < ti.n_valid; c0 += 64) {
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(t_row + c0, v);
+#pragma unroll
+        for (int ch = 0; ch < kChunks; ++ch) {
+          const int c0 = 32 * half_cols + 64 * ch;
+          if (c0 >= ti.n_valid) break;
           const float wmine =
               c0 + lane < ti.n_valid ? p.row_weight[ti.row_start + c0 + lane] * scale : 0.0f;
-          tmem_ld_wait(v);
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const float w = __shfl_sync(0xffffffffu, wmine, i);
             if (c0 + i < ti.n_valid)
-              p.out[(size_t)(ti.row_start + c0 + i) * p.M_per + o] = f2bf(__uint_as_float(v[i]) * w);
+              p.out[(size_t)(ti.row_start + c0 + i) * p.M_per + o] =
+                  f2bf(__uint_as_float(v[ch][i]) * w);
           }
         }
       }
-      tc_fence_before();
-      mbar_arrive_cluster(lead_tempty);
-      acc_phase ^= 1u;
     }
   }
 
@@ -324,7 +393,14 @@ cudaError_t launch_pair(const CUtensorMap* ta, const CUtensorMap* tb, const CUte
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, *ta, tb[0], tb[1], tb[2], *tsfa, *tsfb, p);
+  (void)tsfa;
+  (void)tsfb;
+  // setmaxnreg.inc waits until the block's launch registers cover the split
+  cudaFuncAttributes fa{};
+  e = cudaFuncGetAttributes(&fa, kern);
+  if (e != cudaSuccess) return e;
+  if ((size_t)fa.numRegs * kThreads < 256u * (kRegsLow + kRegsEpi)) return cudaErrorInvalidConfiguration;
+  return cudaLaunchKernelEx(&cfg, kern, *ta, tb[0], tb[1], tb[2], p);
 }
 
 }  // namespace
