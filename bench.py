@@ -542,6 +542,11 @@ def run_ours(args) -> None:
         layer.set_tile_n(args.tile_n)
     if args.pair_cta:
         layer.set_pair_mma(True)
+    if args.down_tiles:
+        mode = args.down_tiles
+        layer.set_token_major_down(mode == "tm")
+        if mode != "tm":
+            layer.set_down_tile_n(int(mode))
     hidden = make_hidden(T, seed=100 + rank, device=dev)
     # warm-up
     for _ in range(args.warmup):
@@ -659,6 +664,8 @@ def main() -> None:
     ap.add_argument("--tokens", type=int, default=0, help="override tokens (profiling only)")
     ap.add_argument("--tile-n", type=int, default=0, help="force the GEMM token tile (tuning)")
     ap.add_argument("--pair-cta", action="store_true", help="256-row tiles on CTA pairs (tuning)")
+    ap.add_argument("--down-tiles", default="", choices=["", "tm", "128", "256"],
+                    help="down projection tiles: token-major or weight-major width (tuning)")
     ap.add_argument("--experts", type=int, default=0, help="override experts (profiling only)")
     args = ap.parse_args()
     if args.warmup < 3:

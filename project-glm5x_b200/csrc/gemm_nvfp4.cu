@@ -126,7 +126,12 @@ __device__ __forceinline__ uint16_t f2bf(float x) {
   return __bfloat16_as_ushort(__float2bfloat16_rn(x));
 }
 
-template <int BN, int EPI, int MX>
+// TM = 1 (token-major, down projection of large batches, BN = 256): the MMA's
+// M side is 128 token rows and its N side 256 weight rows, so each epilogue
+// thread holds one token's consecutive output features and stores them in
+// 16-byte pieces; tiles enumerate 128-token tiles fastest within a 256-row
+// weight tile. A / SFA are the token rows, B / SFB the weights.
+template <int BN, int EPI, int MX, int TM>
 __global__ void __launch_bounds__(kThreads, 1)
     nvfp4_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                               const __grid_constant__ CUtensorMap tmap_b32,
@@ -147,15 +152,33 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
-  const int m_tiles = p.M_per / kBM;
+  static_assert(!TM || (BN == 256 && EPI == 1 && !MX), "token-major: down projection, BN 256");
+  const int m_tiles = TM ? p.M_per / 256 : p.M_per / kBM;
+  constexpr int kTileRows = TM ? 128 : BN;  // token rows per tile
   const int ks_count = p.K / 256;
   const int kc_per_rb = p.K / (MX ? 128 : 64);  // scale chunks per 128-row block
   __shared__ int32_t s_ntp[kMaxSeg + 1], s_cnt[kMaxSeg], s_start[kMaxSeg + 1];
 
+  // Token-tile prefix: from the permutation (tiles of its width), or, when
+  // this launch's tiles differ from it (TM, or a wider-than-128 width the
+  // permutation did not use; segments are contiguous 128-aligned rows then),
+  // counted here.
+  const bool own_prefix = TM || p.ntile_prefix == nullptr;
   for (int i = threadIdx.x; i <= p.nseg; i += blockDim.x) {
-    s_ntp[i] = p.ntile_prefix[i];
+    if (!own_prefix) s_ntp[i] = p.ntile_prefix[i];
     s_start[i] = p.seg_start[i];
     if (i < p.nseg) s_cnt[i] = p.seg_count[i];
+  }
+  if (own_prefix) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int acc = 0;
+      for (int i = 0; i < p.nseg; ++i) {
+        s_ntp[i] = acc;
+        acc += (s_cnt[i] + kTileRows - 1) / kTileRows;
+      }
+      s_ntp[p.nseg] = acc;
+    }
   }
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
@@ -201,7 +224,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto prefetch_tile = [&](int tile) {
         TileInfo tp;
         if (tile >= total_tiles ||
-            !decode_tile(tile, m_tiles, p.nseg, BN, s_ntp, s_cnt, s_start, tp))
+            !decode_tile(tile, m_tiles, p.nseg, kTileRows, s_ntp, s_cnt, s_start, tp))
           return;
         const size_t a_row = (size_t)tp.seg * p.M_per + (size_t)tp.m_tile * kBM;
         const uint8_t* a = p.a_packed + a_row * a_row_bytes;
@@ -214,16 +237,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
         TileInfo ti;
-        if (!decode_tile(tile, m_tiles, p.nseg, BN, s_ntp, s_cnt, s_start, ti)) continue;
+        if (!decode_tile(tile, m_tiles, p.nseg, kTileRows, s_ntp, s_cnt, s_start, ti)) continue;
         if (G5_GEMM_L2_PREFETCH) prefetch_tile(tile + gridDim.x);
-        const int a_row = ti.seg * p.M_per + ti.m_tile * kBM;
-        const int sfb_ch = ti.n_valid > 128 ? 2 : 1;
+        // TM: A = the 128 token rows, B = 256 weight rows
+        const int w_row = ti.seg * p.M_per + ti.m_tile * (TM ? 256 : kBM);
+        const int a_row = TM ? ti.row_start : w_row;
+        const int b_row = TM ? w_row : ti.row_start;
+        const int sfb_ch = TM ? 2 : (ti.n_valid > 128 ? 2 : 1);
         const uint8_t* sfa = p.sfa + (size_t)(a_row / 128) * kc_per_rb * kChunkBytes;
-        const uint8_t* sfb = p.sfb + (size_t)(ti.row_start / 128) * kc_per_rb * kChunkBytes;
+        const uint8_t* sfb = p.sfb + (size_t)(b_row / 128) * kc_per_rb * kChunkBytes;
         // activation rows in pieces: rows [0, 128) and [128, n), each rounded
         // up to 32 rows and loaded with the 32/64/128-row box that fits
-        const int rows0 = G5_GEMM_B_PIECES ? (ti.n_valid < 128 ? ti.n_valid : 128) : (BN < 128 ? BN : 128);
-        const int rows1 = G5_GEMM_B_PIECES ? ti.n_valid - rows0 : (BN > 128 ? BN - 128 : 0);
+        const int b_rows = TM ? 256 : ti.n_valid;
+        const int rows0 = G5_GEMM_B_PIECES ? (b_rows < 128 ? b_rows : 128) : (BN < 128 ? BN : 128);
+        const int rows1 = G5_GEMM_B_PIECES ? b_rows - rows0 : (BN > 128 ? BN - 128 : 0);
         const int box0 = rows0 <= 32 ? 32 : (rows0 <= 64 ? 64 : 128);
         const int box1 = rows1 <= 0 ? 0 : (rows1 <= 32 ? 32 : (rows1 <= 64 ? 64 : 128));
         const CUtensorMap* m0 = box0 == 32 ? &tmap_b32 : (box0 == 64 ? &tmap_b64 : &tmap_b128);
@@ -249,9 +276,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                       C::kCh * kChunkBytes, &full_sf[stage]);
           mbar_arrive_expect_tx(&full[stage], bytes);
           tma_load_2d(sa, &tmap_a, &full[stage], ks * kBKBytes, a_row);
-          tma_load_2d(sb, m0, &full[stage], ks * kBKBytes, ti.row_start);
+          tma_load_2d(sb, m0, &full[stage], ks * kBKBytes, b_row);
           if (box1) tma_load_2d(sb + 128 * kBKBytes, m1, &full[stage], ks * kBKBytes,
-                                ti.row_start + 128);
+                                b_row + 128);
           if (++stage == C::kStages) {
             stage = 0;
             phase ^= 1u;
@@ -268,8 +295,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
         TileInfo ti;
-        if (!decode_tile(tile, m_tiles, p.nseg, BN, s_ntp, s_cnt, s_start, ti)) continue;
-        const uint32_t n_mma = (uint32_t)((ti.n_valid + 7) / 8 * 8);
+        if (!decode_tile(tile, m_tiles, p.nseg, kTileRows, s_ntp, s_cnt, s_start, ti)) continue;
+        const uint32_t n_mma = TM ? 256u : (uint32_t)((ti.n_valid + 7) / 8 * 8);
         const uint32_t idesc = idesc_fp4(kBM, n_mma, 0, 0, 0);
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, p.err)) break;
         tc_fence_after();
@@ -335,8 +362,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
       TileInfo ti;
-      if (!decode_tile(tile, m_tiles, p.nseg, BN, s_ntp, s_cnt, s_start, ti)) continue;
-      const bool two_blocks = ti.n_valid > 128;
+      if (!decode_tile(tile, m_tiles, p.nseg, kTileRows, s_ntp, s_cnt, s_start, ti)) continue;
+      const bool two_blocks = TM || ti.n_valid > 128;
       for (int ks = 0; ks < ks_count; ++ks) {
         if (!mbar_wait(&full_sf[stage], phase, p.err)) {
           ok = false;
@@ -387,7 +414,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
       TileInfo ti;
-      if (!decode_tile(tile, m_tiles, p.nseg, BN, s_ntp, s_cnt, s_start, ti)) continue;
+      if (!decode_tile(tile, m_tiles, p.nseg, kTileRows, s_ntp, s_cnt, s_start, ti)) continue;
       if (!mbar_wait(&tfull[acc], acc_phase, p.err)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(32 * q) << 16) + acc * BN;
@@ -398,14 +425,38 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t v[kChunks][32];
 #pragma unroll
       for (int i = 0; i < kChunks; ++i)
-        if (32 * half + 64 * i < ti.n_valid) tmem_ld_32x32b_x32(t_row + 32 * half + 64 * i, v[i]);
+        if (TM || 32 * half + 64 * i < ti.n_valid)
+          tmem_ld_32x32b_x32(t_row + 32 * half + 64 * i, v[i]);
       tmem_ld_wait();
 #pragma unroll
       for (int i = 0; i < kChunks; ++i) reg_fence(v[i]);
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
       const float bscale = p.b_global[ti.seg];
-      if (MX && EPI == 0) {
+      if (TM) {
+        // lane = token row 32q + lane of the tile; a chunk = 32 consecutive
+        // output features of that token, stored as four 16-byte pieces
+        const int r = 32 * q + lane;
+        if (r < ti.n_valid) {
+          const float w = p.row_weight[ti.row_start + r] * (bscale * p.a_global[ti.seg]);
+          uint16_t* yrow = p.out + (size_t)(ti.row_start + r) * p.M_per + ti.m_tile * 256;
+#pragma unroll
+          for (int ch = 0; ch < kChunks; ++ch) {
+            const int c0 = 32 * half + 64 * ch;
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const __nv_bfloat162 b2 = __floats2bfloat162_rn(
+                  __uint_as_float(v[ch][2 * i]) * w, __uint_as_float(v[ch][2 * i + 1]) * w);
+              pk[i] = *reinterpret_cast<const uint32_t*>(&b2);
+            }
+            uint4* dst = reinterpret_cast<uint4*>(yrow + c0);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+          }
+        }
+      } else if (MX && EPI == 0) {
         // Columns 4r..4r+3 of a chunk are the four terms of the chunk's token
         // r (r = 0..7): their sum is the token's product. Lanes l < 16 hold
         // gate rows and compute h for tokens 0-3, lanes l + 16 the matching up
@@ -519,10 +570,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) tmem_dealloc(tmem_base, C::kTmemCols);
 }
 
-template <int BN, int EPI, int MX>
+template <int BN, int EPI, int MX, int TM = 0>
 cudaError_t launch_impl(const CUtensorMap* ta, const CUtensorMap* tb, const GemmParams& p,
                         int num_sms, cudaStream_t st) {
-  auto kern = nvfp4_grouped_gemm_kernel<BN, EPI, MX>;
+  auto kern = nvfp4_grouped_gemm_kernel<BN, EPI, MX, TM>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)Cfg<BN, MX>::kSmem);
   if (e != cudaSuccess) return e;
@@ -552,6 +603,12 @@ cudaError_t launch_nvfp4_grouped_gemm(int bn, int epi, const CUtensorMap* tmap_a
                                       const CUtensorMap* tmap_b, const GemmParams& p,
                                       int num_sms, cudaStream_t st, int mxfp4) {
   if (p.nseg > kMaxSeg || p.K % 256 || p.M_per % kBM) return cudaErrorInvalidValue;
+  if (epi == 2) {
+    // token-major down projection (tmap_a: token rows, box 128; tmap_b[2]:
+    // weight rows, box 128)
+    if (mxfp4 || p.M_per % 256) return cudaErrorInvalidValue;
+    return launch_impl<256, 1, 0, 1>(tmap_a, tmap_b, p, num_sms, st);
+  }
 #define G5_CASE(BN_)                                                                     \
   case BN_:                                                                              \
     if (mxfp4)                                                                           \

@@ -128,6 +128,9 @@ struct GemmParams {
 // mxfp4 = 1: MXFP4 operands (E8M0 scale per 32 in the blocked layout) and
 // four B rows per token (residual terms), summed in the epilogue; outputs and
 // routing weights live on each token's term-0 row.
+// epi = 2: token-major down projection (NVFP4, segments in 128-row tiles):
+// tmap_a / p.a_packed / p.sfa are the token rows (box 128), tmap_b[2] /
+// p.b_packed / p.sfb the weights; output and weighting as epi 1.
 cudaError_t launch_nvfp4_grouped_gemm(int bn, int epi, const CUtensorMap* tmap_a,
                                       const CUtensorMap* tmap_b, const GemmParams& p,
                                       int num_sms, cudaStream_t st, int mxfp4 = 0);

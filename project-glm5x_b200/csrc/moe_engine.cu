@@ -188,6 +188,8 @@ struct glm5x_moe {
   CUtensorMap tm_w13_sf{}, tm_w2_sf{}, tm_act_sf{}, tm_h_sf{};
   int pair_grid = 0;       // CTAs for the pair GEMM (0 = unavailable)
   bool use_pair = false;   // 256-row token tiles on CTA pairs (opt-in: slower than single CTAs)
+  bool token_major_down = false;  // token-major down projection (opt-in: not faster here)
+  int down_bn = 0;                // weight-major down projection tile width (0 = same)
   CUtensorMap tm_act[4]{}, tm_h[4]{};  // box rows 32, 64, 128, 256
 
   glm5x_status fail(glm5x_status st, const char* fmt, ...) {
@@ -805,12 +807,32 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
   g2.K = I;
   g2.M_per = H;
   mark(7);
-  G5_CHECK(m,
-           pair ? launch_nvfp4_pair_gemm(1, &m->tm_w2, m->tm_h, &m->tm_w2_sf, &m->tm_h_sf, g2,
-                                         m->pair_grid, st)
-                : launch_nvfp4_grouped_gemm(bn, 1, &m->tm_w2, m->tm_h, g2, m->num_sms, st,
-                                            mx ? 1 : 0),
-           "down GEMM");
+  // Large batches (token tiles >= 128 rows): token-major down projection,
+  // whose epilogue stores each token's output features contiguously.
+  const bool token_major = !mx && !pair && bn >= 128 && m->token_major_down && H % 256 == 0;
+  if (token_major) {
+    GemmParams g2t = g2;
+    g2t.a_packed = m->h_packed;
+    g2t.b_packed = m->w2_packed;
+    g2t.sfa = m->h_sf;
+    g2t.sfb = m->w2_sf;
+    const CUtensorMap tw[3] = {m->tm_w2, m->tm_w2, m->tm_w2};
+    G5_CHECK(m, launch_nvfp4_grouped_gemm(256, 2, &m->tm_h[2], tw, g2t, m->num_sms, st),
+             "down GEMM");
+  } else if (!mx && !pair && bn >= 128 && m->down_bn >= 128 && m->down_bn != bn) {
+    // another tile width >= 128 for the down projection (its own tile prefix)
+    GemmParams g2w = g2;
+    g2w.ntile_prefix = nullptr;
+    G5_CHECK(m, launch_nvfp4_grouped_gemm(m->down_bn, 1, &m->tm_w2, m->tm_h, g2w, m->num_sms, st),
+             "down GEMM");
+  } else {
+    G5_CHECK(m,
+             pair ? launch_nvfp4_pair_gemm(1, &m->tm_w2, m->tm_h, &m->tm_w2_sf, &m->tm_h_sf, g2,
+                                           m->pair_grid, st)
+                  : launch_nvfp4_grouped_gemm(bn, 1, &m->tm_w2, m->tm_h, g2, m->num_sms, st,
+                                              mx ? 1 : 0),
+             "down GEMM");
+  }
   mark(8);
   G5_CHECK(m, launch_combine(m->y_bf16, m->pb.pos, T, m->kk(), H, out, st), "combine");
   mark(9);
@@ -1001,6 +1023,20 @@ glm5x_status glm5x_moe_set_tile_n(glm5x_moe* m, int32_t bn) {
 glm5x_status glm5x_moe_set_pair_mma(glm5x_moe* m, int32_t enable) {
   if (!m) return fail_global(GLM5X_INVALID_STATE, "null engine");
   m->use_pair = enable != 0;
+  return GLM5X_OK;
+}
+
+glm5x_status glm5x_moe_set_token_major_down(glm5x_moe* m, int32_t enable) {
+  if (!m) return fail_global(GLM5X_INVALID_STATE, "null engine");
+  m->token_major_down = enable != 0;
+  return GLM5X_OK;
+}
+
+glm5x_status glm5x_moe_set_down_tile_n(glm5x_moe* m, int32_t bn) {
+  if (!m) return fail_global(GLM5X_INVALID_STATE, "null engine");
+  if (bn != 0 && bn != 128 && bn != 256)
+    return m->fail(GLM5X_INVALID_EXTENT, "down tile must be 0, 128 or 256");
+  m->down_bn = bn;
   return GLM5X_OK;
 }
 

@@ -224,8 +224,17 @@ class GLM5XMoELayer:
         N.check(N.lib().glm5x_moe_set_tile_n(self._h, bn), self._h)
 
     def set_pair_mma(self, enable: bool) -> None:
-        """256-row token tiles on CTA pairs (default) or single CTAs."""
+        """256-row token tiles on CTA pairs or single CTAs (default)."""
         N.check(N.lib().glm5x_moe_set_pair_mma(self._h, 1 if enable else 0), self._h)
+
+    def set_down_tile_n(self, bn: int) -> None:
+        """Weight-major down projection token tile (128/256, 0 = gate/up's)."""
+        N.check(N.lib().glm5x_moe_set_down_tile_n(self._h, bn), self._h)
+
+    def set_token_major_down(self, enable: bool) -> None:
+        """Token-major down projection for large batches, or weight-major
+        tiles (default)."""
+        N.check(N.lib().glm5x_moe_set_token_major_down(self._h, 1 if enable else 0), self._h)
 
     def set_profiling(self, enable: bool) -> None:
         N.check(N.lib().glm5x_moe_set_profiling(self._h, 1 if enable else 0), self._h)

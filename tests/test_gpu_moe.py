@@ -31,17 +31,23 @@ def _assert_close(got, want, what):
     assert max_rel <= MAX_REL and cos >= MIN_COS, (what, max_rel, l2, cos)
 
 
-@pytest.mark.parametrize("T,bn,pair", [(1, 0, True), (5, 0, True), (40, 0, True), (300, 0, True),
-                                       (40, 32, True), (100, 64, True), (300, 128, True),
-                                       (300, 256, True), (520, 256, True), (130, 32, True),
-                                       (300, 256, False), (520, 256, False), (7, 256, True)])
-def test_routed_expert_path_small_shapes(T, bn, pair):
+@pytest.mark.parametrize("T,bn,pair,tm", [(1, 0, True, True), (5, 0, True, True),
+                                          (40, 0, True, True), (300, 0, True, True),
+                                          (40, 32, True, True), (100, 64, True, True),
+                                          (300, 128, True, True), (300, 128, False, False),
+                                          (300, 256, True, True), (520, 256, True, True),
+                                          (130, 32, True, True), (300, 256, False, True),
+                                          (520, 256, False, True), (520, 256, False, False),
+                                          (7, 256, True, True), (7, 256, False, True)])
+def test_routed_expert_path_small_shapes(T, bn, pair, tm):
     """Every token-tile width (256-row tiles on CTA pairs and on single CTAs),
-    including segments that span several tiles and narrow tiles."""
+    the token-major and weight-major down projections, segments that span
+    several tiles and narrow tiles."""
     H, I, E, k = 512, 512, 8, 2
     layer = _layer(H, I, E, k, True, 600)
     layer.set_tile_n(bn)
     layer.set_pair_mma(pair)
+    layer.set_token_major_down(tm)
     experts, deq = {}, {}
     for e in list(range(E)) + [-1]:
         ex, dq = make_expert(H, I, 1000 + e)
@@ -55,7 +61,7 @@ def test_routed_expert_path_small_shapes(T, bn, pair):
     layer.check()
     shared = deq.pop(-1)
     want, _ = oracle_forward(bf16_to_np(hidden), ids, w, deq, shared)
-    _assert_close(out.cpu().numpy(), want, f"T={T} bn={bn} pair={pair}")
+    _assert_close(out.cpu().numpy(), want, f"T={T} bn={bn} pair={pair} tm={tm}")
     layer.close()
 
 
