@@ -276,11 +276,13 @@ def run_decode_c4(device_index: int, steps: int, warmup: int, T: int = 64) -> di
     layer.phase_times()
     torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("decode_timed")
     e0.record()
     for _ in range(steps):
         layer(hidden, want_routing=False)
     e1.record()
     torch.cuda.synchronize(dev)
+    torch.cuda.nvtx.range_pop()
     layer.check()
     ms = e0.elapsed_time(e1) / steps
     phases, n = layer.phase_times()
@@ -529,6 +531,9 @@ def run_ours(args) -> None:
     import torch
     world, rank, local = dist_setup()
     torch.cuda.set_device(local)
+    if args.decode_only:
+        print(json.dumps(run_decode_c4(local, args.steps, args.warmup)), flush=True)
+        return
     if world > 1:
         run_ours_ep(args, world, rank, local)
         return
@@ -659,6 +664,8 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true",
                     help="skip the config-4 MXFP4 decode (HBM roofline) measurement")
+    ap.add_argument("--decode-only", action="store_true",
+                    help="only the config-4 MXFP4 decode measurement (profiling)")
     ap.add_argument("--no-library-gemm", action="store_true",
                     help="skip the cuBLASLt NVFP4 reference GEMM of the roofline")
     ap.add_argument("--tokens", type=int, default=0, help="override tokens (profiling only)")
