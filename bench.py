@@ -545,8 +545,8 @@ def run_ours(args) -> None:
     layer = build_layer(T, local, seed=0, experts=experts)
     if args.tile_n:
         layer.set_tile_n(args.tile_n)
-    if args.pair_cta:
-        layer.set_pair_mma(True)
+    if args.single_cta:
+        layer.set_pair_mma(False)
     if args.down_tiles:
         mode = args.down_tiles
         layer.set_token_major_down(mode == "tm")
@@ -670,7 +670,8 @@ def main() -> None:
                     help="skip the cuBLASLt NVFP4 reference GEMM of the roofline")
     ap.add_argument("--tokens", type=int, default=0, help="override tokens (profiling only)")
     ap.add_argument("--tile-n", type=int, default=0, help="force the GEMM token tile (tuning)")
-    ap.add_argument("--pair-cta", action="store_true", help="256-row tiles on CTA pairs (tuning)")
+    ap.add_argument("--single-cta", action="store_true",
+                    help="256-row tiles on single CTAs instead of CTA pairs (tuning)")
     ap.add_argument("--down-tiles", default="", choices=["", "tm", "128", "256"],
                     help="down projection tiles: token-major or weight-major width (tuning)")
     ap.add_argument("--experts", type=int, default=0, help="override experts (profiling only)")

@@ -222,9 +222,9 @@ glm5x_status glm5x_moe_phase_times(glm5x_moe* moe, float* ms, int32_t* forwards)
 /* Token-tile width of the expert GEMMs: 32, 64, 128 or 256 rows, or 0 to
  * choose from the batch (the default). */
 glm5x_status glm5x_moe_set_tile_n(glm5x_moe* moe, int32_t bn);
-/* 256-row token tiles run on single CTAs (the default) or on CTA pairs
- * (tcgen05 cta_group::2, enable = 1); both give the same results to within
- * accumulation order. */
+/* 256-row token tiles run on CTA pairs (tcgen05 cta_group::2, enable = 1,
+ * the default) or on single CTAs (enable = 0); both give the same results to
+ * within accumulation order. */
 glm5x_status glm5x_moe_set_pair_mma(glm5x_moe* moe, int32_t enable);
 /* Down projection of batches with >= 128-row token tiles: token-major tiles
  * (enable = 1: each epilogue thread stores one token's output features) or

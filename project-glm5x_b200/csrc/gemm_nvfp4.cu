@@ -49,6 +49,12 @@
 #ifndef G5_GEMM_B_PIECES
 #define G5_GEMM_B_PIECES 1
 #endif
+// Threads issuing the stage loads: 1 = warp 0 issues scales, weights and
+// activations; 2 = warp 6 takes the activation rows; 3 = warp 6 the weight
+// rows and warp 7 the activation rows.
+#ifndef G5_GEMM_PRODUCERS
+#define G5_GEMM_PRODUCERS 2
+#endif
 
 namespace glm5x {
 
@@ -182,7 +188,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], G5_GEMM_PRODUCERS > 1 ? 2 : 1);
       mbar_init(&empty[s], 1);
       mbar_init(&sf_ready[s], 4);
       mbar_init(&full_sf[s], 1);
@@ -213,9 +219,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp < kEpiWarp0) {
   // the producer, MMA and staging warpgroups give registers back together
   regs_dealloc<kRegsLow>();
-  if (warp == 0) {
-    // ------------------------------------------------------ TMA producer
-    if (lane == 0) {
+  if (warp == 0 || warp == 6 || warp == 7) {
+    // ------------------------------------------------------ TMA producer(s)
+    const int role = warp == 0 ? 0 : warp - 5;
+    constexpr int kP = G5_GEMM_PRODUCERS;
+    const bool do_sf = role == 0;
+    const bool do_a = kP == 3 ? role == 1 : role == 0;
+    const bool do_b = kP == 1 ? role == 0 : role == kP - 1;
+    if (lane == 0 && (do_sf || do_a || do_b)) {
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -238,7 +249,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
         TileInfo ti;
         if (!decode_tile(tile, m_tiles, p.nseg, kTileRows, s_ntp, s_cnt, s_start, ti)) continue;
-        if (G5_GEMM_L2_PREFETCH) prefetch_tile(tile + gridDim.x);
+        if (G5_GEMM_L2_PREFETCH && role == 0) prefetch_tile(tile + gridDim.x);
         // TM: A = the 128 token rows, B = 256 weight rows
         const int w_row = ti.seg * p.M_per + ti.m_tile * (TM ? 256 : kBM);
         const int a_row = TM ? ti.row_start : w_row;
@@ -255,7 +266,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int box1 = rows1 <= 0 ? 0 : (rows1 <= 32 ? 32 : (rows1 <= 64 ? 64 : 128));
         const CUtensorMap* m0 = box0 == 32 ? &tmap_b32 : (box0 == 64 ? &tmap_b64 : &tmap_b128);
         const CUtensorMap* m1 = box1 == 32 ? &tmap_b32 : (box1 == 64 ? &tmap_b64 : &tmap_b128);
-        const uint32_t bytes = C::kABytes + (box0 + box1) * kBKBytes;
+        const uint32_t bytes =
+            (do_a ? (uint32_t)C::kABytes : 0u) + (do_b ? (uint32_t)(box0 + box1) * kBKBytes : 0u);
         const uint32_t sf_bytes = C::kSfaBytes + sfb_ch * C::kCh * kChunkBytes;
         for (int ks = 0; ks < ks_count; ++ks) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, p.err)) {
@@ -268,17 +280,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* ssfb = ssfa + C::kSfaBytes;
           // scale chunks first, on their own barrier: the staging warps move
           // them into TMEM while the operand tiles are still landing
-          mbar_arrive_expect_tx(&full_sf[stage], sf_bytes);
-          bulk_load(ssfa, sfa + (size_t)ks * C::kCh * kChunkBytes, C::kSfaBytes, &full_sf[stage]);
-          for (int h = 0; h < sfb_ch; ++h)
-            bulk_load(ssfb + h * C::kCh * kChunkBytes,
-                      sfb + ((size_t)h * kc_per_rb + ks * C::kCh) * kChunkBytes,
-                      C::kCh * kChunkBytes, &full_sf[stage]);
-          mbar_arrive_expect_tx(&full[stage], bytes);
-          tma_load_2d(sa, &tmap_a, &full[stage], ks * kBKBytes, a_row);
-          tma_load_2d(sb, m0, &full[stage], ks * kBKBytes, b_row);
-          if (box1) tma_load_2d(sb + 128 * kBKBytes, m1, &full[stage], ks * kBKBytes,
-                                b_row + 128);
+          if (do_sf) {
+            mbar_arrive_expect_tx(&full_sf[stage], sf_bytes);
+            bulk_load(ssfa, sfa + (size_t)ks * C::kCh * kChunkBytes, C::kSfaBytes,
+                      &full_sf[stage]);
+            for (int h = 0; h < sfb_ch; ++h)
+              bulk_load(ssfb + h * C::kCh * kChunkBytes,
+                        sfb + ((size_t)h * kc_per_rb + ks * C::kCh) * kChunkBytes,
+                        C::kCh * kChunkBytes, &full_sf[stage]);
+          }
+          if (bytes) mbar_arrive_expect_tx(&full[stage], bytes);
+          if (do_a) tma_load_2d(sa, &tmap_a, &full[stage], ks * kBKBytes, a_row);
+          if (do_b) {
+            tma_load_2d(sb, m0, &full[stage], ks * kBKBytes, b_row);
+            if (box1)
+              tma_load_2d(sb + 128 * kBKBytes, m1, &full[stage], ks * kBKBytes, b_row + 128);
+          }
           if (++stage == C::kStages) {
             stage = 0;
             phase ^= 1u;
@@ -397,7 +414,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sf_ready[stage]);
+        if (lane == 0) mbar_arrive_relaxed(&sf_ready[stage]);
         if (++stage == C::kStages) {
           stage = 0;
           phase ^= 1u;
@@ -431,7 +448,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int i = 0; i < kChunks; ++i) reg_fence(v[i]);
       tc_fence_before();
-      mbar_arrive(&tempty[acc]);
+      mbar_arrive_relaxed(&tempty[acc]);
       const float bscale = p.b_global[ti.seg];
       if (TM) {
         // lane = token row 32q + lane of the tile; a chunk = 32 consecutive

@@ -42,6 +42,12 @@ constexpr uint32_t kRegsLow = 80;
 constexpr uint32_t kRegsEpi = 176;
 static_assert(256 * kRegsLow + 256 * kRegsEpi <= 65536, "register split");
 constexpr int kStages = 5;
+// Threads issuing the stage loads in each CTA: 1 = warp 0 issues everything;
+// 2 = warp 6 takes the token rows (one issuing thread streams copies at a
+// lower rate than two).
+#ifndef G5_PAIR_PRODUCERS
+#define G5_PAIR_PRODUCERS 1
+#endif
 constexpr int kABytes = 128 * kBK;           // this CTA's weight rows
 constexpr int kBBytes = 128 * kBK;           // this CTA's token rows
 constexpr int kSfaBytes = 4 * kChunk;
@@ -121,7 +127,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], G5_PAIR_PRODUCERS);
       mbar_init(&empty[s], 1);
       mbar_init(&full_sf[s], 1);
       mbar_init(&sf_ready[s], 8);  // 4 staging warps in each CTA
@@ -145,9 +151,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp < kEpiWarp0) {
   regs_dealloc<kRegsLow>();
-  if (warp == 0) {
-    // ------------------------------------------------------ TMA producer
-    if (lane == 0) {
+  if (warp == 0 || warp == 6) {
+    // ------------------------------------------------------ TMA producer(s)
+    const bool do_a = warp == 0;
+    const bool do_b = G5_PAIR_PRODUCERS == 1 ? warp == 0 : warp == 6;
+    if (lane == 0 && (do_a || do_b)) {
       tma_prefetch_desc(&tmap_a);
       int stage = 0;
       uint32_t phase = 0;
@@ -163,7 +171,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int a_row = ti.seg * p.M_per + ti.m2 * kPM + (int)rank * 128;
         const uint8_t* sfa = p.sfa + (size_t)(a_row / 128) * kc_per_rb * kChunk;
         const uint8_t* sfb = p.sfb + (size_t)(ti.row_start / 128) * kc_per_rb * kChunk;
-        const uint32_t cta_bytes = kABytes + box * kBK;
+        const uint32_t cta_bytes = (do_a ? kABytes : 0) + (do_b ? box * kBK : 0);
         const uint32_t sf_bytes = kSfaBytes + sfb_ch * 4 * kChunk;
         for (int ks = 0; ks < ks_count; ++ks) {
           if (!mbar_wait_cluster(&empty[stage], phase ^ 1u, p.err)) {
@@ -176,13 +184,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* ssfb = ssfa + kSfaBytes;
           const uint32_t lead_full = mapa_shared(smem_u32(&full[stage]), 0);
           if (leader) mbar_arrive_expect_tx(&full[stage], 2 * cta_bytes);
-          tma_load_2d_pair(sa, &tmap_a, lead_full, ks * kBK, a_row);
-          tma_load_2d_pair(sb, mb, lead_full, ks * kBK, ti.row_start + (int)rank * half);
-          mbar_arrive_expect_tx(&full_sf[stage], sf_bytes);
-          bulk_load(ssfa, sfa + (size_t)ks * 4 * kChunk, kSfaBytes, &full_sf[stage]);
-          for (int h = 0; h < sfb_ch; ++h)
-            bulk_load(ssfb + h * 4 * kChunk, sfb + ((size_t)h * kc_per_rb + ks * 4) * kChunk,
-                      4 * kChunk, &full_sf[stage]);
+          if (do_a) tma_load_2d_pair(sa, &tmap_a, lead_full, ks * kBK, a_row);
+          if (do_b)
+            tma_load_2d_pair(sb, mb, lead_full, ks * kBK, ti.row_start + (int)rank * half);
+          if (do_a) {
+            mbar_arrive_expect_tx(&full_sf[stage], sf_bytes);
+            bulk_load(ssfa, sfa + (size_t)ks * 4 * kChunk, kSfaBytes, &full_sf[stage]);
+            for (int h = 0; h < sfb_ch; ++h)
+              bulk_load(ssfb + h * 4 * kChunk, sfb + ((size_t)h * kc_per_rb + ks * 4) * kChunk,
+                        4 * kChunk, &full_sf[stage]);
+          }
           if (++stage == kStages) {
             stage = 0;
             phase ^= 1u;
@@ -280,7 +291,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(lead_ready0 + stage * 8u);
+        if (lane == 0) mbar_arrive_cluster_relaxed(lead_ready0 + stage * 8u);
         if (++stage == kStages) {
           stage = 0;
           phase ^= 1u;
@@ -312,7 +323,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int i = 0; i < kChunks; ++i) reg_fence(v[i]);
       tc_fence_before();
-      mbar_arrive_cluster(lead_tempty);
+      mbar_arrive_cluster_relaxed(lead_tempty);
       acc_phase ^= 1u;
       const int m_tile = 2 * ti.m2 + (int)rank;  // this CTA's 128-row weight tile
       const float bscale = p.b_global[ti.seg];

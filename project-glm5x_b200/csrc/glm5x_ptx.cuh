@@ -56,6 +56,16 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// Arrive without release semantics. For barriers that only hand TMEM between
+// the tensor pipe and threads: the arriving thread has waited for its own
+// tcgen05.st / tcgen05.ld and issued tcgen05.fence::before_thread_sync, and no
+// generic-proxy data is passed through the barrier. (A release arrive would
+// also wait for the thread's unrelated memory traffic to drain.)
+__device__ __forceinline__ void mbar_arrive_relaxed(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.relaxed.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -405,6 +415,15 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
 // peer CTA).
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+
+// Cluster-scope arrive without release semantics, for the same TMEM hand-offs
+// as mbar_arrive_relaxed. A release at cluster scope costs on the order of a
+// thousand cycles per call here, which serialises a per-stage hand-off.
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(
+                   cluster_addr)
                : "memory");
 }
 

@@ -187,7 +187,7 @@ struct glm5x_moe {
   CUtensorMap tm_router{};
   CUtensorMap tm_w13_sf{}, tm_w2_sf{}, tm_act_sf{}, tm_h_sf{};
   int pair_grid = 0;       // CTAs for the pair GEMM (0 = unavailable)
-  bool use_pair = false;   // 256-row token tiles on CTA pairs (opt-in: slower than single CTAs)
+  bool use_pair = true;    // 256-row token tiles on CTA pairs (cta_group::2)
   bool token_major_down = false;  // token-major down projection (opt-in: not faster here)
   int down_bn = 0;                // weight-major down projection tile width (0 = same)
   CUtensorMap tm_act[4]{}, tm_h[4]{};  // box rows 32, 64, 128, 256

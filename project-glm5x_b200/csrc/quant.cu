@@ -154,63 +154,128 @@ __device__ __forceinline__ float rcp_approx(float d) {
   return r;
 }
 
-// One 16-element NVFP4 block with max_abs scaling against global scale g
-// (six_g = 6 * g, rcp_six_g = rcp.approx(six_g)): writes the 8 packed bytes
-// as two words and returns the E4M3 scale byte. Bit-identical to
+// float -> E4M3 byte by the hardware converter (round to nearest even,
+// saturating), for values already clamped to [2^-6, 448]: the same bits as
+// e4m3_encode on that range.
+__device__ __forceinline__ uint32_t e4m3_rn_hw(float v) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(0.0f), "f"(v));
+  return r & 0xffu;
+}
+
+// E2M1 code of x / d (d > 0) when RN(x / d) is known to round to magnitude k
+// or k + 1 (k <= 6): decides which side of the threshold t_k between them the
+// quotient falls. RN(x / d) lands above t_k exactly when |x| / d > t_k +
+// ulp(t_k) / 2 (every threshold has an even significand, so the midpoint
+// itself rounds down to t_k), and (t_k + ulp(t_k) / 2) * d has at most
+// 25 + 24 significant bits, so the comparison is exact in double precision.
+// The code is the argmin's: ties toward the smaller magnitude, the sign from
+// x, and +0 for a zero magnitude.
+__device__ __forceinline__ uint32_t e2m1_code_across(float x, double d, uint32_t k) {
+  // t_k = (v_k + v_(k+1)) / 2 for the E2M1 magnitudes v = 0, 0.5, 1, ..., 6
+  // (their doubles 0, 1, 2, 3, 4, 6, 8, 12 one nibble each)
+  const uint32_t twice = 0xC8643210u;
+  const float t = (float)(((twice >> (4 * k)) & 0xfu) + ((twice >> (4 * k + 4)) & 0xfu)) * 0.25f;
+  const uint32_t tb = f_bits(t);
+  const double t_mid = (double)t + (double)__uint_as_float((tb & 0x7f800000u) - (24u << 23));
+  const uint32_t mag = k + (fabs((double)x) > t_mid * d ? 1u : 0u);
+  return mag == 0u ? 0u : (mag | (x < 0.0f ? 8u : 0u));
+}
+
+// max of two BF16 pairs, NaN-propagating
+__device__ __forceinline__ uint32_t bf16x2_max_nan(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+// Bit 4j of the result is set when nibble j of v is nonzero.
+__device__ __forceinline__ uint64_t nibbles_nonzero(uint64_t v) {
+  v |= v >> 2;
+  v |= v >> 1;
+  return v & 0x1111111111111111ull;
+}
+
+// One 16-element NVFP4 block of BF16 values (w = the block's eight packed
+// pairs, xb = the same 16 values in memory) with max_abs scaling against
+// global scale g (six_g = 6 * g, rcp_six_g = rcp.approx(six_g)): writes the 8
+// packed bytes as two words and returns the E4M3 scale byte. Bit-identical to
 // nvfp4_quantize_block(..., mse = false), i.e. to the reference's
 // scale = E4M3(clamp(bmax / (6 g))), code = argmin |RN(x / (scale * g)) - c|.
 //
-// Every quotient is first taken as RN(x * rcp.approx(divisor)), within 3 ulps
-// of the IEEE quotient. A rounding decision can only differ between the two
-// when the quotient lies within a few ulps of a decision boundary, and every
-// boundary has a run of zero low mantissa bits: E4M3 rounding midpoints (low
-// 20 bits 0x80000) for the scale, and for the codes the thresholds 0.25,
-// 0.75, 1.25, 1.75, 2.5, 3.5 and 5 (low 21 bits zero). Quotients within 8 bit
-// steps of such a pattern are recomputed with IEEE division; BF16 data puts
-// about 0.5% of the codes there (exact ties are common). The other codes come
-// from the hardware E2M1 converter (nearest, saturating at 6), which agrees
-// with the argmin away from ties; its -0 is mapped to +0 (code 0) like the
-// argmin. Exact zeros and non-finite values also take the IEEE path (the
-// caller's bmax must propagate NaN).
-__device__ __forceinline__ uint32_t quantize_block16(const float (&x)[16], float bmax, float g,
-                                                     float six_g, float rcp_six_g,
-                                                     uint32_t& lo32, uint32_t& hi32) {
+// The scale's quotient is taken as RN(bmax * rcp.approx(6 g)), within 3 ulps
+// of the IEEE quotient; when that lies within 8 bit steps of an E4M3 rounding
+// midpoint (low 20 bits 0x80000) the IEEE quotient is computed instead.
+// Codes: with r = rcp.approx(d) (relative error below 2^-22 together with the
+// products' roundings), x * r * (1 - 2^-19) and x * r * (1 + 2^-19) bracket
+// the exact quotient x / d strictly, so when the hardware converter (nearest,
+// saturating at 6, its -0 mapped to +0 like the argmin) gives both the same
+// code, no decision threshold lies between them and that code is the
+// argmin's. Otherwise the two codes are neighbours around one threshold and
+// e2m1_code_across decides exactly; BF16 data sends a fraction of a percent
+// of the codes there (exact ties are common). Blocks with a non-finite value
+// take IEEE division for every code.
+__device__ __forceinline__ uint32_t quantize_block16_bf16(const uint32_t (&w)[8],
+                                                          const uint16_t* __restrict__ xb,
+                                                          float g, float six_g, float rcp_six_g,
+                                                          uint32_t& lo32, uint32_t& hi32) {
+  uint32_t m = w[0] & 0x7fff7fffu;
+#pragma unroll
+  for (int j = 1; j < 8; ++j) m = bf16x2_max_nan(m, w[j] & 0x7fff7fffu);
+  const float bmax = fmax_nan(__uint_as_float(m << 16), __uint_as_float(m & 0xffff0000u));
   float base = __fmul_rn(bmax, rcp_six_g);
   if (((f_bits(base) + 8u - 0x80000u) & 0xfffffu) <= 16u || !(base <= 3.0e38f))
     base = f_div(bmax, six_g);
   base = fminf(fmaxf(base, kE4M3Tiny), kE4M3Max);
-  const uint32_t sb = e4m3_encode(base);
+  const uint32_t sb = e4m3_rn_hw(base);
   const float denom = f_mul(e4m3_decode(sb), g);
-  const float ra = rcp_approx(denom);
-  float q[16];
-  bool any_near = !(bmax <= 3.0e38f);  // bmax is NaN-propagating: NaN / Inf input
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    q[i] = __fmul_rn(x[i], ra);
-    any_near |= ((f_bits(q[i]) + 8u) & 0x1fffffu) <= 16u;  // the sign bit does not matter
-  }
-  lo32 = clear_negative_zero(e2m1x8_rn(q));
-  hi32 = clear_negative_zero(e2m1x8_rn(q + 8));
-  if (!any_near) return sb;
-  uint32_t near = 0;
   if (!(bmax <= 3.0e38f)) {
-    near = 0xffffu;
-  } else {
+    // NaN / Inf in the block: every code by IEEE division and the argmin
+    lo32 = hi32 = 0u;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) near |= (((f_bits(q[i]) + 8u) & 0x1fffffu) <= 16u ? 1u : 0u) << i;
+    for (int i = 0; i < 16; ++i) {
+      const uint32_t xw = w[i >> 1];
+      const float xi = __uint_as_float((i & 1) ? (xw & 0xffff0000u) : (xw << 16));
+      const uint32_t code = e2m1_encode(f_div(xi, denom));
+      if (i < 8) lo32 |= code << (4 * i); else hi32 |= code << (4 * (i - 8));
+    }
+    return sb;
   }
-  while (near) {
-    const int i = __ffs(near) - 1;
-    near &= near - 1;
-    float xi = x[0];  // x[i] without dynamic indexing (keeps x in registers)
+  const float ra = rcp_approx(denom);
+  const float ra_lo = __fmul_rn(ra, 1.0f - 0x1p-19f);
+  const float ra_hi = __fmul_rn(ra, 1.0f + 0x1p-19f);
+  uint32_t ca[2], cb[2];
 #pragma unroll
-    for (int k = 1; k < 16; ++k) xi = k == i ? x[k] : xi;
-    const uint32_t code = e2m1_encode(f_div(xi, denom));
-    if (i < 8)
-      lo32 = (lo32 & ~(0xfu << (4 * i))) | (code << (4 * i));
-    else
-      hi32 = (hi32 & ~(0xfu << (4 * (i - 8)))) | (code << (4 * (i - 8)));
+  for (int h = 0; h < 2; ++h) {
+    float qa[8], qb[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t xw = w[4 * h + j];
+      const float x0 = __uint_as_float(xw << 16), x1 = __uint_as_float(xw & 0xffff0000u);
+      qa[2 * j] = __fmul_rn(x0, ra_lo);
+      qa[2 * j + 1] = __fmul_rn(x1, ra_lo);
+      qb[2 * j] = __fmul_rn(x0, ra_hi);
+      qb[2 * j + 1] = __fmul_rn(x1, ra_hi);
+    }
+    ca[h] = clear_negative_zero(e2m1x8_rn(qa));
+    cb[h] = clear_negative_zero(e2m1x8_rn(qb));
   }
+  lo32 = ca[0];
+  hi32 = ca[1];
+  if (((ca[0] ^ cb[0]) | (ca[1] ^ cb[1])) == 0u) return sb;
+  uint64_t codes = ((uint64_t)ca[1] << 32) | ca[0];
+  const uint64_t other = ((uint64_t)cb[1] << 32) | cb[0];
+  uint64_t todo = nibbles_nonzero(codes ^ other);
+  const double dd = (double)denom;
+  while (todo) {
+    const int bit = __ffsll((long long)todo) - 1;
+    todo &= todo - 1;
+    const float xi = __uint_as_float((uint32_t)__ldg(xb + (bit >> 2)) << 16);
+    const uint32_t k = min((uint32_t)(codes >> bit) & 7u, (uint32_t)(other >> bit) & 7u);
+    codes = (codes & ~(0xfull << bit)) | ((uint64_t)e2m1_code_across(xi, dd, k) << bit);
+  }
+  lo32 = (uint32_t)codes;
+  hi32 = (uint32_t)(codes >> 32);
   return sb;
 }
 
@@ -253,19 +318,12 @@ __global__ void nvfp4_quantize_segments_kernel(
   const bool word_scales =
       (nb & 31) == 0 && (reinterpret_cast<uintptr_t>(scales_blocked) & 3) == 0;
   for (int b = lane_id(); b < nb; b += 32) {
-    const uint4* q = reinterpret_cast<const uint4*>(xrow + b * 16);
+    const uint16_t* xb = xrow + b * 16;
+    const uint4* q = reinterpret_cast<const uint4*>(xb);
     const uint4 v0 = __ldg(q), v1 = __ldg(q + 1);
     const uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-    float x[16];
-    float bmax = 0.0f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      x[2 * j] = __uint_as_float(w[j] << 16);
-      x[2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
-      bmax = fmax_nan(bmax, fmax_nan(fabsf(x[2 * j]), fabsf(x[2 * j + 1])));
-    }
     uint32_t lo32, hi32;
-    const uint32_t sb = quantize_block16(x, bmax, g, six_g, rcp_six_g, lo32, hi32);
+    const uint32_t sb = quantize_block16_bf16(w, xb, g, six_g, rcp_six_g, lo32, hi32);
     *reinterpret_cast<uint2*>(prow + b * 8) = make_uint2(lo32, hi32);
     if (word_scales) {
       uint32_t sw = sb << (8 * (b & 3));

@@ -224,7 +224,7 @@ class GLM5XMoELayer:
         N.check(N.lib().glm5x_moe_set_tile_n(self._h, bn), self._h)
 
     def set_pair_mma(self, enable: bool) -> None:
-        """256-row token tiles on CTA pairs or single CTAs (default)."""
+        """256-row token tiles on CTA pairs (default) or single CTAs."""
         N.check(N.lib().glm5x_moe_set_pair_mma(self._h, 1 if enable else 0), self._h)
 
     def set_down_tile_n(self, bn: int) -> None:
