@@ -182,6 +182,31 @@ __device__ __forceinline__ uint32_t e2m1_code_across(float x, double d, uint32_t
   return mag == 0u ? 0u : (mag | (x < 0.0f ? 8u : 0u));
 }
 
+// E2M1 codes of eight BF16 values (four packed pairs w[0..3], low half
+// first) times r_lo and times r_hi: two code words from the hardware
+// converter (nearest, saturating at 6), the products as packed f32x2.
+__device__ __forceinline__ void e2m1x8_bracket(const uint32_t* w, float r_lo, float r_hi,
+                                               uint32_t& ca, uint32_t& cb) {
+  asm("{\n\t.reg .b32 x0, x1;\n\t.reg .b64 ra, rb, xx, qa, qb;\n\t"
+      ".reg .f32 a0, a1, b0, b1;\n\t.reg .b8 p0, p1, p2, p3, q0, q1, q2, q3;\n\t"
+      "mov.b64 ra, {%6, %6};\n\tmov.b64 rb, {%7, %7};\n\t"
+#define G5_BRACKET_PAIR(W, P, Q)                                              \
+      "shl.b32 x0, " W ", 16;\n\tand.b32 x1, " W ", 0xffff0000;\n\t"            \
+      "mov.b64 xx, {x0, x1};\n\t"                                             \
+      "mul.rn.f32x2 qa, xx, ra;\n\tmul.rn.f32x2 qb, xx, rb;\n\t"               \
+      "mov.b64 {a0, a1}, qa;\n\tmov.b64 {b0, b1}, qb;\n\t"                     \
+      "cvt.rn.satfinite.e2m1x2.f32 " P ", a1, a0;\n\t"                          \
+      "cvt.rn.satfinite.e2m1x2.f32 " Q ", b1, b0;\n\t"
+      G5_BRACKET_PAIR("%2", "p0", "q0")
+      G5_BRACKET_PAIR("%3", "p1", "q1")
+      G5_BRACKET_PAIR("%4", "p2", "q2")
+      G5_BRACKET_PAIR("%5", "p3", "q3")
+#undef G5_BRACKET_PAIR
+      "mov.b32 %0, {p0, p1, p2, p3};\n\tmov.b32 %1, {q0, q1, q2, q3};\n\t}"
+      : "=r"(ca), "=r"(cb)
+      : "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3]), "f"(r_lo), "f"(r_hi));
+}
+
 // max of two BF16 pairs, NaN-propagating
 __device__ __forceinline__ uint32_t bf16x2_max_nan(uint32_t a, uint32_t b) {
   uint32_t r;
@@ -245,27 +270,17 @@ __device__ __forceinline__ uint32_t quantize_block16_bf16(const uint32_t (&w)[8]
   const float ra_lo = __fmul_rn(ra, 1.0f - 0x1p-19f);
   const float ra_hi = __fmul_rn(ra, 1.0f + 0x1p-19f);
   uint32_t ca[2], cb[2];
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    float qa[8], qb[8];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const uint32_t xw = w[4 * h + j];
-      const float x0 = __uint_as_float(xw << 16), x1 = __uint_as_float(xw & 0xffff0000u);
-      qa[2 * j] = __fmul_rn(x0, ra_lo);
-      qa[2 * j + 1] = __fmul_rn(x1, ra_lo);
-      qb[2 * j] = __fmul_rn(x0, ra_hi);
-      qb[2 * j + 1] = __fmul_rn(x1, ra_hi);
-    }
-    ca[h] = clear_negative_zero(e2m1x8_rn(qa));
-    cb[h] = clear_negative_zero(e2m1x8_rn(qb));
-  }
-  lo32 = ca[0];
-  hi32 = ca[1];
+  e2m1x8_bracket(w, ra_lo, ra_hi, ca[0], cb[0]);
+  e2m1x8_bracket(w + 4, ra_lo, ra_hi, ca[1], cb[1]);
+  // -0 (code 8) only comes with magnitude 0 on both sides, so comparing the
+  // raw words finds exactly the codes whose magnitudes differ
+  lo32 = clear_negative_zero(ca[0]);
+  hi32 = clear_negative_zero(ca[1]);
   if (((ca[0] ^ cb[0]) | (ca[1] ^ cb[1])) == 0u) return sb;
-  uint64_t codes = ((uint64_t)ca[1] << 32) | ca[0];
+  uint64_t codes = ((uint64_t)hi32 << 32) | lo32;
   const uint64_t other = ((uint64_t)cb[1] << 32) | cb[0];
-  uint64_t todo = nibbles_nonzero(codes ^ other);
+  const uint64_t raw = ((uint64_t)ca[1] << 32) | ca[0];
+  uint64_t todo = nibbles_nonzero(raw ^ other);
   const double dd = (double)denom;
   while (todo) {
     const int bit = __ffsll((long long)todo) - 1;
@@ -279,6 +294,20 @@ __device__ __forceinline__ uint32_t quantize_block16_bf16(const uint32_t (&w)[8]
   return sb;
 }
 
+// 32 bytes (16 BF16 values) from global memory with an L2 cache policy
+__device__ __forceinline__ void ld32_policy(const void* p, uint64_t pol, uint32_t (&w)[8]) {
+  asm volatile("ld.global.nc.L2::cache_hint.v8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8], %9;"
+               : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]), "=r"(w[4]), "=r"(w[5]),
+                 "=r"(w[6]), "=r"(w[7])
+               : "l"(p), "l"(pol));
+}
+
+// Expert-major rows gathered from token rows (GATHER) read each source row
+// once per routed slot: the loads ask the L2 to keep the source rows (evict
+// last) and the packed output, written once and read by the next GEMM, to go
+// first. Without a gather the source is read once and goes first. WIDE: the
+// source is 32-byte aligned and each lane's block is one 256-bit load.
+template <bool GATHER, bool WIDE>
 __global__ void nvfp4_quantize_segments_kernel(
     const uint16_t* __restrict__ src, int K, const int32_t* __restrict__ row_token,
     const int32_t* __restrict__ seg_start, const int32_t* __restrict__ seg_count,
@@ -300,40 +329,48 @@ __global__ void nvfp4_quantize_segments_kernel(
   const int64_t row = seg_start[s] + segment_row(r, bn);
   const float g = nvfp4_global_scale(seg_amax[s]);
   if (r == 0 && lane_id() == 0) seg_global[s] = g;
-  const int nb = K / 16;
-  uint8_t* prow = packed + row * (K / 2);
+  const int nb = K / 16;  // a multiple of 32: every lane runs every iteration
+  const int lane = lane_id();
+  uint8_t* prow = packed + row * (K / 2) + lane * 8;
+  // blocked scale layout: block b = lane + 32 i sits 4096 i bytes after b = lane
+  uint8_t* psf = scales_blocked + blocked_sf_offset(row, lane, nb);
   if (r >= seg_count[s]) {
-    for (int b = lane_id(); b < nb; b += 32) {
-      *reinterpret_cast<uint2*>(prow + b * 8) = make_uint2(0, 0);
-      scales_blocked[blocked_sf_offset(row, b, nb)] = 0;
+    for (int b = lane; b < nb; b += 32, prow += 256, psf += 4096) {
+      *reinterpret_cast<uint2*>(prow) = make_uint2(0, 0);
+      *psf = 0;
     }
     return;
   }
-  const int64_t t = row_token ? row_token[row] : row;
-  const uint16_t* xrow = src + t * (int64_t)K;
+  const int64_t t = GATHER ? row_token[row] : row;
+  const uint16_t* xrow = src + t * (int64_t)K + lane * 16;
   const float six_g = f_mul(kFp4Max, g);
   const float rcp_six_g = rcp_approx(six_g);
-  // nb a multiple of 32: every lane runs every iteration, and lanes 4j..4j+3
-  // hold the four scales of one 32-bit word of the blocked layout
-  const bool word_scales =
-      (nb & 31) == 0 && (reinterpret_cast<uintptr_t>(scales_blocked) & 3) == 0;
-  for (int b = lane_id(); b < nb; b += 32) {
-    const uint16_t* xb = xrow + b * 16;
-    const uint4* q = reinterpret_cast<const uint4*>(xb);
-    const uint4 v0 = __ldg(q), v1 = __ldg(q + 1);
-    const uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-    uint32_t lo32, hi32;
-    const uint32_t sb = quantize_block16_bf16(w, xb, g, six_g, rcp_six_g, lo32, hi32);
-    *reinterpret_cast<uint2*>(prow + b * 8) = make_uint2(lo32, hi32);
-    if (word_scales) {
-      uint32_t sw = sb << (8 * (b & 3));
-      sw |= __shfl_xor_sync(0xffffffffu, sw, 1);
-      sw |= __shfl_xor_sync(0xffffffffu, sw, 2);
-      if ((b & 3) == 0)
-        *reinterpret_cast<uint32_t*>(scales_blocked + blocked_sf_offset(row, b, nb)) = sw;
+  uint64_t pol_src, pol_out;
+  if (GATHER) {
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol_src));
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol_out));
+  } else {
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol_src));
+  }
+  for (int b = lane; b < nb; b += 32, xrow += 512, prow += 256, psf += 4096) {
+    uint32_t w[8];
+    if (WIDE) {
+      ld32_policy(xrow, pol_src, w);
     } else {
-      scales_blocked[blocked_sf_offset(row, b, nb)] = static_cast<uint8_t>(sb);
+      const uint4* q = reinterpret_cast<const uint4*>(xrow);
+      const uint4 v0 = __ldg(q), v1 = __ldg(q + 1);
+      w[0] = v0.x; w[1] = v0.y; w[2] = v0.z; w[3] = v0.w;
+      w[4] = v1.x; w[5] = v1.y; w[6] = v1.z; w[7] = v1.w;
     }
+    uint32_t lo32, hi32;
+    const uint32_t sb = quantize_block16_bf16(w, xrow, g, six_g, rcp_six_g, lo32, hi32);
+    if (GATHER)
+      asm volatile("st.global.L2::cache_hint.v2.u32 [%0], {%1, %2}, %3;" ::"l"(prow), "r"(lo32),
+                   "r"(hi32), "l"(pol_out)
+                   : "memory");
+    else
+      *reinterpret_cast<uint2*>(prow) = make_uint2(lo32, hi32);
+    *psf = static_cast<uint8_t>(sb);
   }
 }
 
@@ -576,10 +613,16 @@ cudaError_t launch_nvfp4_quantize_segments(const uint16_t* src, int K, const int
                                            uint8_t* packed, uint8_t* scales_blocked,
                                            float* seg_global, cudaStream_t st) {
   if (max_rows <= 0) return cudaSuccess;
+  if (K % 512) return cudaErrorInvalidValue;
   const int warps = 8;
-  nvfp4_quantize_segments_kernel<<<(unsigned)((max_rows + warps - 1) / warps), warps * 32, 0,
-                                   st>>>(src, K, row_token, seg_start, seg_count, qprefix, nseg,
-                                         bn, seg_amax, packed, scales_blocked, seg_global);
+  const bool wide = (reinterpret_cast<uintptr_t>(src) & 31) == 0;
+  const dim3 grid((unsigned)((max_rows + warps - 1) / warps)), block(warps * 32);
+  auto kernel = row_token ? (wide ? nvfp4_quantize_segments_kernel<true, true>
+                                  : nvfp4_quantize_segments_kernel<true, false>)
+                          : (wide ? nvfp4_quantize_segments_kernel<false, true>
+                                  : nvfp4_quantize_segments_kernel<false, false>);
+  kernel<<<grid, block, 0, st>>>(src, K, row_token, seg_start, seg_count, qprefix, nseg, bn,
+                                 seg_amax, packed, scales_blocked, seg_global);
   return cudaGetLastError();
 }
 
