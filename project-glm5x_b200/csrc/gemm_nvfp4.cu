@@ -51,7 +51,7 @@
 #endif
 // Threads issuing the stage loads: 1 = warp 0 issues scales, weights and
 // activations; 2 = warp 6 takes the activation rows; 3 = warp 6 the weight
-// rows and warp 7 the activation rows.
+// rows and warp 7 the activation rows; 4 = warp 6 takes the scale chunks.
 #ifndef G5_GEMM_PRODUCERS
 #define G5_GEMM_PRODUCERS 2
 #endif
@@ -188,7 +188,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
-      mbar_init(&full[s], G5_GEMM_PRODUCERS > 1 ? 2 : 1);
+      mbar_init(&full[s], (G5_GEMM_PRODUCERS == 2 || G5_GEMM_PRODUCERS == 3) ? 2 : 1);
       mbar_init(&empty[s], 1);
       mbar_init(&sf_ready[s], 4);
       mbar_init(&full_sf[s], 1);
@@ -223,9 +223,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------ TMA producer(s)
     const int role = warp == 0 ? 0 : warp - 5;
     constexpr int kP = G5_GEMM_PRODUCERS;
-    const bool do_sf = role == 0;
+    const bool do_sf = kP == 4 ? role == 1 : role == 0;
     const bool do_a = kP == 3 ? role == 1 : role == 0;
-    const bool do_b = kP == 1 ? role == 0 : role == kP - 1;
+    const bool do_b = (kP == 1 || kP == 4) ? role == 0 : role == kP - 1;
     if (lane == 0 && (do_sf || do_a || do_b)) {
       int stage = 0;
       uint32_t phase = 0;

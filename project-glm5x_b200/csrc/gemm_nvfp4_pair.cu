@@ -42,11 +42,11 @@ constexpr uint32_t kRegsLow = 80;
 constexpr uint32_t kRegsEpi = 176;
 static_assert(256 * kRegsLow + 256 * kRegsEpi <= 65536, "register split");
 constexpr int kStages = 5;
-// Threads issuing the stage loads in each CTA: 1 = warp 0 issues everything;
-// 2 = warp 6 takes the token rows (one issuing thread streams copies at a
-// lower rate than two).
-#ifndef G5_PAIR_PRODUCERS
-#define G5_PAIR_PRODUCERS 1
+// Stage loads in each CTA: 0 = warp 0 issues everything; 1 = warp 6 takes
+// the token rows; 2 = warp 6 takes the scale chunks (one issuing thread
+// streams copies at a lower rate than two).
+#ifndef G5_PAIR_SPLIT
+#define G5_PAIR_SPLIT 0
 #endif
 constexpr int kABytes = 128 * kBK;           // this CTA's weight rows
 constexpr int kBBytes = 128 * kBK;           // this CTA's token rows
@@ -127,7 +127,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full[s], G5_PAIR_PRODUCERS);
+      mbar_init(&full[s], G5_PAIR_SPLIT == 1 ? 2 : 1);
       mbar_init(&empty[s], 1);
       mbar_init(&full_sf[s], 1);
       mbar_init(&sf_ready[s], 8);  // 4 staging warps in each CTA
@@ -154,8 +154,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 || warp == 6) {
     // ------------------------------------------------------ TMA producer(s)
     const bool do_a = warp == 0;
-    const bool do_b = G5_PAIR_PRODUCERS == 1 ? warp == 0 : warp == 6;
-    if (lane == 0 && (do_a || do_b)) {
+    const bool do_b = G5_PAIR_SPLIT == 1 ? warp == 6 : warp == 0;
+    const bool do_sf = G5_PAIR_SPLIT == 2 ? warp == 6 : warp == 0;
+    if (lane == 0 && (do_a || do_b || do_sf)) {
       tma_prefetch_desc(&tmap_a);
       int stage = 0;
       uint32_t phase = 0;
@@ -183,17 +184,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* ssfa = sb + kBBytes;
           uint8_t* ssfb = ssfa + kSfaBytes;
           const uint32_t lead_full = mapa_shared(smem_u32(&full[stage]), 0);
-          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * cta_bytes);
-          if (do_a) tma_load_2d_pair(sa, &tmap_a, lead_full, ks * kBK, a_row);
-          if (do_b)
-            tma_load_2d_pair(sb, mb, lead_full, ks * kBK, ti.row_start + (int)rank * half);
-          if (do_a) {
+          if (do_sf) {
             mbar_arrive_expect_tx(&full_sf[stage], sf_bytes);
             bulk_load(ssfa, sfa + (size_t)ks * 4 * kChunk, kSfaBytes, &full_sf[stage]);
             for (int h = 0; h < sfb_ch; ++h)
               bulk_load(ssfb + h * 4 * kChunk, sfb + ((size_t)h * kc_per_rb + ks * 4) * kChunk,
                         4 * kChunk, &full_sf[stage]);
           }
+          if (leader && cta_bytes) mbar_arrive_expect_tx(&full[stage], 2 * cta_bytes);
+          if (do_a) tma_load_2d_pair(sa, &tmap_a, lead_full, ks * kBK, a_row);
+          if (do_b)
+            tma_load_2d_pair(sb, mb, lead_full, ks * kBK, ti.row_start + (int)rank * half);
           if (++stage == kStages) {
             stage = 0;
             phase ^= 1u;
