@@ -195,7 +195,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < C::kAcc; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 32 * kEpiWarps);
+      mbar_init(&tempty[a], kEpiWarps);  // one arrive per epilogue warp
     }
     mbar_init(drained, 1);
     fence_barrier_init();
@@ -448,7 +448,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int i = 0; i < kChunks; ++i) reg_fence(v[i]);
       tc_fence_before();
-      mbar_arrive_relaxed(&tempty[acc]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive_relaxed(&tempty[acc]);
       const float bscale = p.b_global[ti.seg];
       if (TM) {
         // lane = token row 32q + lane of the tile; a chunk = 32 consecutive

@@ -133,7 +133,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&sf_ready[s], 8);  // 4 staging warps in each CTA
     }
     mbar_init(tfull, 1);
-    mbar_init(tempty, 2 * 32 * kEpiWarps);
+    mbar_init(tempty, 2 * kEpiWarps);  // one arrive per epilogue warp of each CTA
     mbar_init(drained, 1);
     fence_barrier_init();
     fence_proxy_async_smem();
@@ -324,7 +324,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int i = 0; i < kChunks; ++i) reg_fence(v[i]);
       tc_fence_before();
-      mbar_arrive_cluster_relaxed(lead_tempty);
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster_relaxed(lead_tempty);
       acc_phase ^= 1u;
       const int m_tile = 2 * ti.m2 + (int)rank;  // this CTA's 128-row weight tile
       const float bscale = p.b_global[ti.seg];
