@@ -284,6 +284,67 @@ glm5x_status glm5x_mxfp4_decode(const uint8_t* packed, const uint8_t* scales, in
 glm5x_status glm5x_select_routing(const float* scores, const float* bias, int64_t tokens,
                                   int32_t num_experts, int32_t top_k, float routed_scale,
                                   int32_t* ids, float* weights, void* stream);
+/* ---------------------------------------------------------------- routing policy */
+
+/* k3x::RoutingMode / RoutingPolicyConfig (runtime/include/k3x/
+ * routing_policy.hpp:11-19). fixed: fixed_k of the ladder 4/6/8/12/16 (<= the
+ * natural top-k); adaptive (natural top-k 16): the smallest ladder K whose
+ * natural probability mass reaches mass_target, that covers the entropy's
+ * effective support and whose boundary gap reaches minimum_boundary_gap
+ * (routing_policy.cpp:111-135); quality_floor_k raises fixed / adaptive K.
+ * Slots past a token's selected K hold id -1 and weight 0, and the selected
+ * weights are renormalized over the selected scores. collect_diagnostics keeps
+ * the per-token decision scalars in natural mode as well (the other modes
+ * always keep them). */
+typedef enum glm5x_routing_mode {
+  GLM5X_ROUTING_NATURAL = 0,
+  GLM5X_ROUTING_FIXED = 1,
+  GLM5X_ROUTING_ADAPTIVE = 2,
+} glm5x_routing_mode;
+
+typedef struct glm5x_routing_policy {
+  int32_t mode;                 /* glm5x_routing_mode */
+  int32_t fixed_k;
+  float mass_target;            /* (0, 1]; the reference's default is 0.9 */
+  float minimum_boundary_gap;   /* [0, 1] */
+  int32_t quality_floor_k;      /* 0 or a ladder K */
+  int32_t collect_diagnostics;
+} glm5x_routing_policy;
+
+/* Routing counters of the last router pass with diagnostics, as the
+ * reference's session exports them (runtime/src/model.cpp:102-113). */
+typedef struct glm5x_routing_stats {
+  uint64_t decisions;
+  uint64_t selected_experts;
+  uint64_t quality_escalated_decisions;
+  double normalized_entropy_sum;
+  double selected_mass_sum;
+  double boundary_confidence_sum;
+} glm5x_routing_stats;
+
+/* Validates like select_routing (GLM5X_INVALID_STATE with the reference's
+ * message for an invalid threshold, floor, fixed K or adaptive without a
+ * natural Top-16) and applies to later forwards and glm5x_moe_route. */
+glm5x_status glm5x_moe_set_routing_policy(glm5x_moe* moe, const glm5x_routing_policy* policy);
+/* Sums of the last router pass's per-token decisions (synchronizes). */
+glm5x_status glm5x_moe_routing_stats(glm5x_moe* moe, glm5x_routing_stats* out);
+/* Per-token decisions of the last router pass over `tokens` tokens, host
+ * buffers (either may be NULL): sel [tokens, 2] = selected K, quality-floor
+ * escalated; diag [tokens, 4] = normalized entropy, entropy effective support,
+ * selected cumulative mass, boundary confidence. Synchronizes. */
+glm5x_status glm5x_moe_routing_decisions(glm5x_moe* moe, int64_t tokens, int32_t* sel,
+                                         float* diag);
+/* select_routing with a policy over given sigmoid scores for T tokens at once
+ * (device buffers): ids / weights [T, natural_top_k] (weights times
+ * routed_scale), sel [T, 2] and diag [T, 4] as above (either may be NULL).
+ * Synchronizes; invalid scores (outside [0, 1] or non-finite) and a zero
+ * selected mass are GLM5X_INVALID_STATE as in the reference. */
+glm5x_status glm5x_select_routing_policy(const float* scores, const float* bias, int64_t tokens,
+                                         int32_t num_experts, int32_t natural_top_k,
+                                         const glm5x_routing_policy* policy, float routed_scale,
+                                         int32_t* ids, float* weights, int32_t* sel,
+                                         float* diag, void* stream);
+
 /* out[t] (+)= sum over s < slots of rows[pos[t, s]] (BF16 rows, FP32 sums in
  * slot order; pos < 0 = absent), device buffers: the weighted scatter of
  * scatter_expert_major_outputs (runtime/src/expert_major.cpp:148-196) /

@@ -394,6 +394,100 @@ int orc_route_tokens(const float* hidden, const float* router, const float* bias
   return 0;
 }
 
+/* select_routing with a Top-K policy (runtime/src/routing_policy.cpp:31-159):
+ * mode 0 natural, 1 fixed (fixed_k), 2 adaptive (k must be 16), floor_k the
+ * quality floor. Validation as routing_policy.cpp:41-70; the decision
+ * scalars in the reference's FP32 operation order (:89-150). Outputs:
+ * ids[k] / weights[k] in natural order with -1 / 0 past the selected K,
+ * sel[2] = (selected K, quality floor escalated), diag[4] = (normalized
+ * entropy, entropy effective support, selected cumulative mass, boundary
+ * confidence). Returns 0, or -1 where the reference fails. */
+static int orc_in_ladder(int k) { return k == 4 || k == 6 || k == 8 || k == 12 || k == 16; }
+
+static float orc_boundary_confidence(const float* p, int k, int selected) {
+  if (selected >= k) return 1.0f;
+  float gap = p[selected - 1] - p[selected];
+  if (gap < 0.0f) gap = 0.0f;
+  const float top = p[0] > 1.17549435e-38f ? p[0] : 1.17549435e-38f;
+  return gap / top;
+}
+
+static int orc_choose_adaptive(const float* p, int k, int floor_k, float support,
+                               float mass_target, float min_gap) {
+  const float eps = 1.0e-5f;
+  float cumulative = 0.0f;
+  for (int slot = 0; slot < k; ++slot) {
+    cumulative += p[slot];
+    const int candidate = slot + 1;
+    if (!orc_in_ladder(candidate) || candidate < floor_k) continue;
+    const float confidence = orc_boundary_confidence(p, k, candidate);
+    if (cumulative + eps >= mass_target && (float)candidate + eps >= support &&
+        confidence + eps >= min_gap)
+      return candidate;
+  }
+  return k;
+}
+
+int orc_select_routing_policy(const float* scores, const float* bias, int n, int k, int mode,
+                              int fixed_k, float mass_target, float min_gap, int floor_k,
+                              int32_t* ids, float* weights, int32_t* sel, float* diag) {
+  if (n <= 0 || k <= 0 || k > n || k > 16) return -1;
+  if (!isfinite(mass_target) || mass_target <= 0.0f || mass_target > 1.0f ||
+      !isfinite(min_gap) || min_gap < 0.0f || min_gap > 1.0f)
+    return -1;
+  if (floor_k != 0 && (!orc_in_ladder(floor_k) || (mode != 0 && floor_k > k))) return -1;
+  if (mode == 1 && (!orc_in_ladder(fixed_k) || fixed_k > k)) return -1;
+  if (mode == 2 && k != 16) return -1;
+  if (mode < 0 || mode > 2) return -1;
+  int32_t order[16];
+  float top[16];
+  int32_t nat[16];
+  float nat_w[16];
+  /* the natural order and weights of the natural Top-k */
+  if (orc_select_routing(scores, bias, n, k, nat, nat_w)) return -1;
+  for (int s = 0; s < k; ++s) {
+    order[s] = nat[s];
+    top[s] = scores[nat[s]];
+  }
+  float denom = 0.0f;
+  for (int s = 0; s < k; ++s) denom += top[s];
+  float p[16];
+  float entropy = 0.0f;
+  for (int s = 0; s < k; ++s) {
+    p[s] = top[s] / denom;
+    if (p[s] > 0.0f) entropy -= p[s] * logf(p[s]);
+  }
+  const float support = expf(entropy);
+  int selected = k, unfloored = k;
+  if (mode == 1) {
+    unfloored = fixed_k;
+    selected = fixed_k > floor_k ? fixed_k : floor_k;
+  } else if (mode == 2) {
+    unfloored = orc_choose_adaptive(p, k, 0, support, mass_target, min_gap);
+    selected = orc_choose_adaptive(p, k, floor_k, support, mass_target, min_gap);
+  }
+  float sdenom = 0.0f;
+  for (int s = 0; s < selected; ++s) sdenom += top[s];
+  if (!isfinite(sdenom) || sdenom <= 0.0f) return -1;
+  for (int s = 0; s < k; ++s) {
+    ids[s] = s < selected ? order[s] : -1;
+    weights[s] = s < selected ? top[s] / sdenom : 0.0f;
+  }
+  if (sel) {
+    sel[0] = selected;
+    sel[1] = selected > unfloored;
+  }
+  if (diag) {
+    float mass = 0.0f;
+    for (int s = 0; s < selected; ++s) mass += p[s];
+    diag[0] = k == 1 ? 0.0f : entropy / logf((float)k);
+    diag[1] = support;
+    diag[2] = mass;
+    diag[3] = orc_boundary_confidence(p, k, selected);
+  }
+  return 0;
+}
+
 /* ---------------------------------------------------------------------- */
 /* Dense SwiGLU expert (CPU reference path)                                */
 /* ---------------------------------------------------------------------- */

@@ -31,6 +31,8 @@ _f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
 _u8p = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
 _i32p = np.ctypeslib.ndpointer(dtype=np.int32, flags="C_CONTIGUOUS")
 _i64 = ctypes.c_int64
+_POLICY_ARGS = [_f32p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                ctypes.c_float, ctypes.c_float, ctypes.c_int, _i32p, _f32p, _i32p, _f32p]
 
 
 def lib() -> ctypes.CDLL:
@@ -64,6 +66,8 @@ def lib() -> ctypes.CDLL:
         L.orc_mxfp4_decode.argtypes = [_u8p, _u8p, _i64, _i64, ctypes.c_int, _f32p]
         L.orc_select_routing.restype = ctypes.c_int
         L.orc_select_routing.argtypes = [_f32p, _f32p, ctypes.c_int, ctypes.c_int, _i32p, _f32p]
+        L.orc_select_routing_policy.restype = ctypes.c_int
+        L.orc_select_routing_policy.argtypes = _POLICY_ARGS
         L.orc_route_tokens.restype = ctypes.c_int
         L.orc_route_tokens.argtypes = [_f32p, _f32p, _f32p, _i64, _i64, ctypes.c_int,
                                        ctypes.c_int, ctypes.c_float, ctypes.c_void_p, _i32p, _f32p]
@@ -85,6 +89,8 @@ def ref_lib() -> ctypes.CDLL | None:
         R = _REF
         R.ref_select_routing.restype = ctypes.c_int
         R.ref_select_routing.argtypes = [_f32p, _f32p, ctypes.c_int, ctypes.c_int, _i32p, _f32p]
+        R.ref_select_routing_policy.restype = ctypes.c_int
+        R.ref_select_routing_policy.argtypes = _POLICY_ARGS
         R.ref_decode_mxfp4.restype = ctypes.c_int
         R.ref_decode_mxfp4.argtypes = [_u8p, _u8p, _i64, _i64, _i64, _f32p]
         R.ref_dense_silu_mlp.restype = ctypes.c_int
@@ -192,6 +198,32 @@ def select_routing(scores, bias, k: int):
     if lib().orc_select_routing(s, b, s.size, k, ids, w):
         raise ValueError("invalid routing")
     return ids, w
+
+
+ROUTING_MODES = {"natural": 0, "fixed": 1, "adaptive": 2}
+
+
+def select_routing_policy(scores, bias, k: int, mode: str = "natural", fixed_k: int = 0,
+                          mass_target: float = 0.9, minimum_boundary_gap: float = 0.0,
+                          quality_floor_k: int = 0, use_reference: bool = False):
+    """select_routing with a policy for one token (routing_policy.cpp:31-159):
+    (ids [k] with -1 past the selected K, weights [k], selected_k, escalated,
+    diag [4] = normalized entropy, effective support, selected mass, boundary
+    confidence). `use_reference` runs the reference's own C++ (oracle/_ref)
+    instead of the C restatement. Raises ValueError where the reference fails."""
+    s, b = _f32(scores), _f32(bias)
+    ids = np.zeros(k, dtype=np.int32)
+    w = np.zeros(k, dtype=np.float32)
+    sel = np.zeros(2, dtype=np.int32)
+    diag = np.zeros(4, dtype=np.float32)
+    L = ref_lib() if use_reference else lib()
+    if L is None:
+        raise RuntimeError("oracle/_ref is not built")
+    fn = L.ref_select_routing_policy if use_reference else L.orc_select_routing_policy
+    if fn(s, b, s.size, k, ROUTING_MODES[mode], fixed_k, float(mass_target),
+          float(minimum_boundary_gap), quality_floor_k, ids, w, sel, diag):
+        raise ValueError("invalid routing")
+    return ids, w, int(sel[0]), bool(sel[1]), diag
 
 
 def route_tokens(hidden, router, bias, k: int = 8, routed_scale: float = 2.5,

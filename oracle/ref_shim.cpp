@@ -41,6 +41,37 @@ int ref_select_routing(const float* scores, const float* bias, int n, int k, int
   return 0;
 }
 
+// k3x::select_routing with a policy (runtime/src/routing_policy.cpp:31-159):
+// ids / weights [k] (-1 / 0 past the selected K), sel [2], diag [4] as
+// orc_select_routing_policy.
+int ref_select_routing_policy(const float* scores, const float* bias, int n, int k, int mode,
+                              int fixed_k, float mass_target, float min_gap, int floor_k,
+                              int32_t* ids, float* weights, int32_t* sel, float* diag) {
+  k3x::RoutingPolicyConfig cfg{};
+  cfg.mode = mode == 1 ? k3x::RoutingMode::fixed
+                       : (mode == 2 ? k3x::RoutingMode::adaptive : k3x::RoutingMode::natural);
+  cfg.fixed_k = static_cast<std::size_t>(fixed_k);
+  cfg.mass_target = mass_target;
+  cfg.minimum_boundary_gap = min_gap;
+  cfg.quality_floor_k = static_cast<std::size_t>(floor_k);
+  auto r = k3x::select_routing(std::span<const float>(scores, n), std::span<const float>(bias, n),
+                               static_cast<std::size_t>(k), cfg);
+  if (!r) return -1;
+  const auto& d = r.value();
+  for (int s = 0; s < k; ++s) {
+    const bool on = static_cast<std::size_t>(s) < d.selected_k;
+    ids[s] = on ? static_cast<int32_t>(d.expert_ids[s]) : -1;
+    weights[s] = on ? d.normalized_weights[s] : 0.0f;
+  }
+  sel[0] = static_cast<int32_t>(d.selected_k);
+  sel[1] = d.quality_floor_escalated ? 1 : 0;
+  diag[0] = d.normalized_entropy;
+  diag[1] = d.entropy_effective_support;
+  diag[2] = d.selected_cumulative_mass;
+  diag[3] = d.boundary_confidence;
+  return 0;
+}
+
 // k3x::decode_mxfp4 (runtime/src/ops.cpp:40-63).
 int ref_decode_mxfp4(const uint8_t* packed, const uint8_t* scales, int64_t rows, int64_t cols,
                      int64_t group, float* out) {

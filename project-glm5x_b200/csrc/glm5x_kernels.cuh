@@ -70,9 +70,28 @@ struct PermuteBuffers {
   float* row_weight;      // [rows], routing weight of each segment row
 };
 
+// Top-K policy of k3x::select_routing (runtime/include/k3x/routing_policy.hpp:
+// 11-19): mode 0 natural, 1 fixed (fixed_k of the ladder 4/6/8/12/16), 2
+// adaptive (natural Top-16; the smallest ladder K meeting the mass, entropy
+// support and boundary-gap tests), quality_floor_k raising fixed/adaptive K.
+struct RoutingPolicy {
+  int32_t mode = 0;
+  int32_t fixed_k = 0;
+  float mass_target = 0.9f;
+  float minimum_boundary_gap = 0.0f;
+  int32_t quality_floor_k = 0;
+};
+
+// One warp per token: sigmoid scores (or given scores), natural top-k by
+// score + bias, the policy's selected K <= k. Slots past the selected K get id
+// -1 and weight 0; the selected weights are score / sum(selected scores) *
+// routed_scale. Optional per-token outputs: sel [T, 2] = (selected K,
+// quality-floor escalated) and diag [T, 4] = (normalized entropy, entropy
+// effective support, selected cumulative mass, boundary confidence).
 cudaError_t launch_topk(const float* in, int values_are_scores, const float* bias, int T, int E,
                         int k, float routed_scale, int32_t* ids, float* weights, uint32_t* err,
-                        cudaStream_t st);
+                        cudaStream_t st, const RoutingPolicy& policy = RoutingPolicy(),
+                        int32_t* sel = nullptr, float* diag = nullptr);
 // rows_per: operand rows per (token, slot) -- 1 for NVFP4, 4 for the MXFP4
 // four-term activation expansion (pos and row_token refer to the first).
 // ids in [begin, begin + count) -> id - begin, others -> -1.
@@ -89,14 +108,18 @@ cudaError_t launch_permute(const int32_t* ids, const float* weights, const float
 // When the 128-token tiles would leave SMs idle and `partials` is given
 // (router_partials_floats() floats), the contraction is split along K over
 // several CTAs per tile and a second kernel sums the partial logits in a
-// fixed order before the top-k. Returns the launches issued in *launches.
+// fixed order before the top-k. A non-natural policy or requested sel/diag
+// outputs re-run the top-k over the logits with that policy (logits must be
+// given). Returns the launches issued in *launches.
 bool router_tc_supported(int E, int H, int k);
 size_t router_partials_floats(int num_sms, int E);
 cudaError_t launch_router_tc(const CUtensorMap* tmap_x, const CUtensorMap* tmap_w,
                              const float* bias, int T, int H, int E, int k, float routed_scale,
                              float* logits, int32_t* ids, float* weights, uint32_t* err,
                              cudaStream_t st, float* partials = nullptr, int num_sms = 0,
-                             int* launches = nullptr);
+                             int* launches = nullptr,
+                             const RoutingPolicy& policy = RoutingPolicy(),
+                             int32_t* sel = nullptr, float* diag = nullptr);
 
 // ------------------------------------------------------------ gemm_nvfp4.cu
 // Grouped block-scaled FP4 GEMM over expert segments, weights as the M side:

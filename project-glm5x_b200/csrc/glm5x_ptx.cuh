@@ -16,6 +16,7 @@ enum DeviceError : uint32_t {
   kErrNonFinite = 1u << 1,
   kErrBadScale = 1u << 2,
   kErrBounds = 1u << 3,
+  kErrRoutingMass = 1u << 4,  // a token's selected routing scores sum to zero
 };
 
 // Wall-clock budget of one bounded wait before it gives up (ns).

@@ -12,6 +12,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -120,6 +121,37 @@ namespace glm5x {
 void set_last_error(const char* msg) { g_last_error = msg; }
 }  // namespace glm5x
 
+// select_routing's configuration checks (routing_policy.cpp:50-70), message
+// for message.
+static const char* routing_policy_error(const glm5x_routing_policy& p, int natural_k) {
+  auto ladder = [](int k) { return k == 4 || k == 6 || k == 8 || k == 12 || k == 16; };
+  if (p.mode < GLM5X_ROUTING_NATURAL || p.mode > GLM5X_ROUTING_ADAPTIVE)
+    return "invalid routing mode";
+  if (!std::isfinite(p.mass_target) || p.mass_target <= 0.0f || p.mass_target > 1.0f ||
+      !std::isfinite(p.minimum_boundary_gap) || p.minimum_boundary_gap < 0.0f ||
+      p.minimum_boundary_gap > 1.0f)
+    return "invalid adaptive routing threshold";
+  if (p.quality_floor_k != 0 &&
+      (!ladder(p.quality_floor_k) ||
+       (p.mode != GLM5X_ROUTING_NATURAL && p.quality_floor_k > natural_k)))
+    return "invalid routing quality floor";
+  if (p.mode == GLM5X_ROUTING_FIXED && (!ladder(p.fixed_k) || p.fixed_k > natural_k))
+    return "invalid fixed routing K";
+  if (p.mode == GLM5X_ROUTING_ADAPTIVE && natural_k != 16)
+    return "adaptive routing requires natural Top-16";
+  return nullptr;
+}
+
+static RoutingPolicy to_device_policy(const glm5x_routing_policy& p) {
+  RoutingPolicy d;
+  d.mode = p.mode;
+  d.fixed_k = p.fixed_k;
+  d.mass_target = p.mass_target;
+  d.minimum_boundary_gap = p.minimum_boundary_gap;
+  d.quality_floor_k = p.quality_floor_k;
+  return d;
+}
+
 struct glm5x_moe {
   glm5x_moe_config cfg{};
   int device = 0;
@@ -148,6 +180,11 @@ struct glm5x_moe {
   float *token_amax = nullptr, *logits = nullptr, *topk_w = nullptr;
   int32_t* topk_ids = nullptr;
   int32_t* ids_local = nullptr;  // expert-parallel rows: global -> local expert ids
+  RoutingPolicy policy{};        // select_routing mode of the router
+  bool routing_diag = false;     // keep per-token routing diagnostics
+  int32_t* route_sel = nullptr;  // [max_tokens, 2] selected K, escalated
+  float* route_diag = nullptr;   // [max_tokens, 4] entropy, support, mass, confidence
+  int64_t route_T = 0;           // tokens of the last router pass with diagnostics
   PermuteBuffers pb{};
   uint8_t *act_packed = nullptr, *act_sf = nullptr, *h_packed = nullptr, *h_sf = nullptr;
   float *act_global = nullptr, *h_global = nullptr;
@@ -357,6 +394,8 @@ glm5x_status glm5x_moe_create(const glm5x_moe_config* cfg, int device, glm5x_moe
   ok &= m->alloc(&m->topk_w, (size_t)T * k);
   ok &= m->alloc(&m->topk_ids, (size_t)T * k);
   ok &= m->alloc(&m->ids_local, (size_t)T * k);
+  ok &= m->alloc(&m->route_sel, (size_t)T * 2);
+  ok &= m->alloc(&m->route_diag, (size_t)T * 4);
   ok &= m->alloc(&m->pb.chunk_count, (size_t)((T + 255) / 256) * E);
   ok &= m->alloc(&m->pb.rank, (size_t)T * k);
   ok &= m->alloc(&m->pb.seg_count, (size_t)nseg + 1);
@@ -720,9 +759,13 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
     if (!make_tmap_bf16(&tm_x, x, H, T, 128))
       return m->fail(GLM5X_BACKEND_UNAVAILABLE, "hidden tensor map");
     int rl = 0;
+    const bool diag = m->policy.mode != 0 || m->routing_diag;
     G5_CHECK(m, launch_router_tc(&tm_x, &m->tm_router, m->router_bias, T, H, E, k,
                                  m->cfg.routed_scaling, m->logits, m->topk_ids, m->topk_w, m->err,
-                                 st, m->router_partials, m->num_sms, &rl), "router");
+                                 st, m->router_partials, m->num_sms, &rl, m->policy,
+                                 diag ? m->route_sel : nullptr, diag ? m->route_diag : nullptr),
+             "router");
+    m->route_T = diag ? T : 0;
     launches += rl;
     ids = m->topk_ids;
     wts = m->topk_w;
@@ -737,7 +780,7 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
     ++launches;
   }
   G5_CHECK(m, launch_permute(ids, wts, m->token_amax, T, k, E_perm, hs, bn, m->pb, m->err, st,
-                             m->terms(), ep_rows ? 1 : 0,
+                             m->terms(), ep_rows ? 1 : 2,
                              shared_rows < 0 ? -1 : (int)std::min<int64_t>(shared_rows, T)),
            "permute");
   launches += 3;
@@ -897,11 +940,14 @@ glm5x_status glm5x_moe_route(glm5x_moe* m, const void* hidden, int64_t T, int32_
   if (!make_tmap_bf16(&tm_x, hidden, m->H(), T, 128))
     return m->fail(GLM5X_BACKEND_UNAVAILABLE, "hidden tensor map");
   int rl = 0;
+  const bool diag = m->policy.mode != 0 || m->routing_diag;
   G5_CHECK(m, launch_router_tc(&tm_x, &m->tm_router, m->router_bias, (int)T, m->H(),
                                m->cfg.num_experts, m->K(), m->cfg.routed_scaling,
                                logits ? logits : m->logits, ids, weights, m->err, st,
-                               m->router_partials, m->num_sms, &rl),
+                               m->router_partials, m->num_sms, &rl, m->policy,
+                               diag ? m->route_sel : nullptr, diag ? m->route_diag : nullptr),
            "router");
+  m->route_T = diag ? T : 0;
   m->stats.kernel_launches += rl;
   return GLM5X_OK;
 }
@@ -937,6 +983,7 @@ glm5x_status glm5x_moe_check(glm5x_moe* m) {
     if (e & kErrWaitTimeout) return m->fail(GLM5X_WAIT_TIMEOUT, "device wait timed out (0x%x)", e);
     if (e & kErrNonFinite) return m->fail(GLM5X_INVALID_STATE, "non-finite input (0x%x)", e);
     if (e & kErrBounds) return m->fail(GLM5X_INVALID_EXTENT, "routing ids invalid (0x%x)", e);
+    if (e & kErrRoutingMass) return m->fail(GLM5X_INVALID_STATE, "zero routing mass (0x%x)", e);
     return m->fail(GLM5X_DEVICE_ERROR, "device error word 0x%x", e);
   }
   return GLM5X_OK;
@@ -955,6 +1002,51 @@ glm5x_status glm5x_moe_last_routing(glm5x_moe* m, int32_t* ids, float* weights, 
   if (logits)
     G5_CHECK(m, cudaMemcpy(logits, m->logits, sizeof(float) * T * m->cfg.num_experts,
                            cudaMemcpyDeviceToHost), "logits");
+  return GLM5X_OK;
+}
+
+glm5x_status glm5x_moe_set_routing_policy(glm5x_moe* m, const glm5x_routing_policy* p) {
+  if (!m || !p) return fail_global(GLM5X_INVALID_STATE, "null argument");
+  if (const char* why = routing_policy_error(*p, m->K())) return m->fail(GLM5X_INVALID_STATE, "%s", why);
+  m->policy = to_device_policy(*p);
+  m->routing_diag = p->collect_diagnostics != 0;
+  return GLM5X_OK;
+}
+
+glm5x_status glm5x_moe_routing_decisions(glm5x_moe* m, int64_t T, int32_t* sel, float* diag) {
+  if (!m) return fail_global(GLM5X_INVALID_STATE, "null engine");
+  if (m->route_T <= 0 || T != m->route_T)
+    return m->fail(GLM5X_INVALID_STATE, "no router pass with diagnostics over %lld tokens",
+                   (long long)T);
+  cudaSetDevice(m->device);
+  G5_CHECK(m, cudaDeviceSynchronize(), "sync");
+  if (sel)
+    G5_CHECK(m, cudaMemcpy(sel, m->route_sel, sizeof(int32_t) * 2 * T, cudaMemcpyDeviceToHost),
+             "routing decisions");
+  if (diag)
+    G5_CHECK(m, cudaMemcpy(diag, m->route_diag, sizeof(float) * 4 * T, cudaMemcpyDeviceToHost),
+             "routing diagnostics");
+  return GLM5X_OK;
+}
+
+glm5x_status glm5x_moe_routing_stats(glm5x_moe* m, glm5x_routing_stats* out) {
+  if (!m || !out) return fail_global(GLM5X_INVALID_STATE, "null argument");
+  const int64_t T = m->route_T;
+  if (T <= 0) return m->fail(GLM5X_INVALID_STATE, "no router pass with diagnostics");
+  std::vector<int32_t> sel(2 * T);
+  std::vector<float> diag(4 * T);
+  glm5x_status st = glm5x_moe_routing_decisions(m, T, sel.data(), diag.data());
+  if (st != GLM5X_OK) return st;
+  glm5x_routing_stats r{};
+  r.decisions = (uint64_t)T;
+  for (int64_t t = 0; t < T; ++t) {
+    r.selected_experts += (uint64_t)sel[2 * t];
+    r.quality_escalated_decisions += sel[2 * t + 1] ? 1u : 0u;
+    r.normalized_entropy_sum += diag[4 * t];
+    r.selected_mass_sum += diag[4 * t + 2];
+    r.boundary_confidence_sum += diag[4 * t + 3];
+  }
+  *out = r;
   return GLM5X_OK;
 }
 
@@ -1062,6 +1154,7 @@ glm5x_status glm5x_moe_debug_copy(glm5x_moe* m, int32_t which, void* dst, size_t
 }  // extern "C"
 
 static cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
 
 static glm5x_status sync_error(cudaStream_t st, uint32_t* err_dev, uint32_t mask_invalid,
                                const char* what) {
@@ -1209,6 +1302,23 @@ glm5x_status glm5x_select_routing(const float* scores, const float* bias, int64_
   cudaStream_t st = as_stream(stream);
   cudaMemsetAsync(err, 0, 4, st);
   launch_topk(scores, 1, bias, (int)T, E, k, scale, ids, weights, err, st);
+  return sync_error(st, err, 0, "select routing");
+}
+
+glm5x_status glm5x_select_routing_policy(const float* scores, const float* bias, int64_t T,
+                                         int32_t E, int32_t k, const glm5x_routing_policy* p,
+                                         float scale, int32_t* ids, float* weights,
+                                         int32_t* sel, float* diag, void* stream) {
+  if (!scores || !bias || !ids || !weights || !p || T <= 0 || E <= 0 || E > 512 || k <= 0 ||
+      k > 16 || k > E)
+    return fail_global(GLM5X_INVALID_STATE, "invalid routing dimensions");
+  if (const char* why = routing_policy_error(*p, k)) return fail_global(GLM5X_INVALID_STATE, "%s", why);
+  uint32_t* err = nullptr;
+  if (cudaMalloc(&err, 4) != cudaSuccess) return fail_global(GLM5X_OUT_OF_MEMORY, "scratch");
+  cudaStream_t st = as_stream(stream);
+  cudaMemsetAsync(err, 0, 4, st);
+  launch_topk(scores, 1, bias, (int)T, E, k, scale, ids, weights, err, st, to_device_policy(*p),
+              sel, diag);
   return sync_error(st, err, 0, "select routing");
 }
 

@@ -1,7 +1,7 @@
 // route.cu -- router top-k and the expert-major token permutation.
 //
-// Routing follows the reference's C++ natural-mode policy
-// (runtime/src/routing_policy.cpp:31-159, called from
+// Routing follows the reference's C++ policy (natural, fixed and adaptive
+// Top-K of runtime/src/routing_policy.cpp:31-159, natural mode called from
 // runtime/src/cuda_glm5x_real_expert_bench.cpp:287-328) and the Python router
 // (reference/glm5x_ref/layer10_moe.py:760-789): score = sigmoid(logit),
 // choice = score + bias, top-k by choice with ties to the lower expert index
@@ -26,10 +26,45 @@ namespace glm5x {
 // One warp per token. Lane l owns experts l, l+32, ... (E <= 32 * 16).
 // `values_are_scores` = 1 means `in` already holds sigmoid scores (the
 // select_routing parity entry point), else logits.
+// select_routing's K ladder (routing_policy.cpp:13)
+__device__ __forceinline__ bool k_in_ladder(int k) {
+  return k == 4 || k == 6 || k == 8 || k == 12 || k == 16;
+}
+
+// boundary_confidence (routing_policy.cpp:21-29): the probability gap at the
+// selected K relative to the largest natural probability, 1 at K = k.
+__device__ float boundary_confidence(const float* p, int k, int selected) {
+  if (selected >= k) return 1.0f;
+  const float gap = fmaxf(0.0f, f_sub(p[selected - 1], p[selected]));
+  return f_div(gap, fmaxf(p[0], 1.17549435e-38f));
+}
+
+// choose_adaptive (routing_policy.cpp:115-133): the first ladder K >= floor
+// whose cumulative natural probability reaches mass_target, that covers the
+// entropy's effective support and whose boundary gap reaches
+// minimum_boundary_gap, each test with the 1e-5 slack; k when none does.
+__device__ int choose_adaptive(const float* p, int k, int floor_k, float support,
+                               const RoutingPolicy& pol) {
+  constexpr float kEps = 1.0e-5f;
+  float cumulative = 0.0f;
+  for (int slot = 0; slot < k; ++slot) {
+    cumulative = f_add(cumulative, p[slot]);
+    const int candidate = slot + 1;
+    if (!k_in_ladder(candidate) || candidate < floor_k) continue;
+    const float confidence = boundary_confidence(p, k, candidate);
+    if (f_add(cumulative, kEps) >= pol.mass_target &&
+        f_add(static_cast<float>(candidate), kEps) >= support &&
+        f_add(confidence, kEps) >= pol.minimum_boundary_gap)
+      return candidate;
+  }
+  return k;
+}
+
 __global__ void topk_kernel(const float* __restrict__ in, int values_are_scores,
                             const float* __restrict__ bias, int T, int E, int k,
                             float routed_scale, int32_t* __restrict__ ids,
-                            float* __restrict__ weights, uint32_t* err) {
+                            float* __restrict__ weights, uint32_t* err, RoutingPolicy pol,
+                            int32_t* __restrict__ sel_out, float* __restrict__ diag) {
   const int warps = blockDim.x / 32;
   const int t = blockIdx.x * warps + threadIdx.x / 32;
   if (t >= T) return;
@@ -99,11 +134,52 @@ __global__ void topk_kernel(const float* __restrict__ in, int values_are_scores,
     sel_id[s] = best_e;
     denom = f_add(denom, sc);
   }
-  if (lane == 0) {
+  if (lane != 0) return;
+  // natural probabilities, entropy and the policy's K (routing_policy.cpp:
+  // 89-134), in the reference's FP32 operation order
+  if (!(denom > 0.0f) || !isfinite(denom)) atomicOr(err, kErrRoutingMass);
+  int selected = k;
+  if (pol.mode != 0 || sel_out || diag) {
+    float p[16];
+    float entropy = 0.0f;
     for (int s = 0; s < k; ++s) {
-      ids[(int64_t)t * k + s] = sel_id[s];
-      weights[(int64_t)t * k + s] = f_mul(f_div(sel_score[s], denom), routed_scale);
+      p[s] = f_div(sel_score[s], denom);
+      if (p[s] > 0.0f) entropy = f_sub(entropy, f_mul(p[s], logf(p[s])));
     }
+    const float support = expf(entropy);
+    int unfloored = k;
+    if (pol.mode == 1) {
+      unfloored = pol.fixed_k;
+      selected = max(pol.fixed_k, pol.quality_floor_k);
+    } else if (pol.mode == 2) {
+      unfloored = choose_adaptive(p, k, 0, support, pol);
+      selected = choose_adaptive(p, k, pol.quality_floor_k, support, pol);
+    }
+    if (sel_out) {
+      sel_out[2 * (int64_t)t] = selected;
+      sel_out[2 * (int64_t)t + 1] = selected > unfloored ? 1 : 0;
+    }
+    if (diag) {
+      float mass = 0.0f;
+      for (int s = 0; s < selected; ++s) mass = f_add(mass, p[s]);
+      float4 d;
+      d.x = k == 1 ? 0.0f : f_div(entropy, logf(static_cast<float>(k)));
+      d.y = support;
+      d.z = mass;
+      d.w = boundary_confidence(p, k, selected);
+      reinterpret_cast<float4*>(diag)[t] = d;
+    }
+  }
+  float sdenom = denom;
+  if (selected < k) {
+    sdenom = 0.0f;
+    for (int s = 0; s < selected; ++s) sdenom = f_add(sdenom, sel_score[s]);
+    if (!(sdenom > 0.0f) || !isfinite(sdenom)) atomicOr(err, kErrRoutingMass);
+  }
+  for (int s = 0; s < k; ++s) {
+    const bool on = s < selected;
+    ids[(int64_t)t * k + s] = on ? sel_id[s] : -1;
+    weights[(int64_t)t * k + s] = on ? f_mul(f_div(sel_score[s], sdenom), routed_scale) : 0.0f;
   }
 }
 
@@ -111,10 +187,11 @@ __global__ void topk_kernel(const float* __restrict__ in, int values_are_scores,
 constexpr int kChunk = 256;  // tokens per counting chunk
 
 // Per 256-token chunk: per-expert counts and each (token, slot)'s rank among
-// the chunk's tokens routed to the same expert (stable). E <= 256. With
-// skip_invalid, an id outside [0, E) marks a slot with no expert here (the
+// the chunk's tokens routed to the same expert (stable). E <= 256.
+// skip_invalid = 1: an id outside [0, E) marks a slot with no expert here (the
 // expert-parallel engines receive rows whose other slots live on other
-// ranks); otherwise it is an error.
+// ranks); 2: only -1 does (a slot a fixed / adaptive routing policy left
+// empty); 0, and other ids under 2: an error.
 __global__ void __launch_bounds__(kChunk) permute_count_kernel(
     const int32_t* __restrict__ ids, int T, int k, int E, int skip_invalid,
     int32_t* __restrict__ chunk_count, int32_t* __restrict__ rank, uint32_t* err) {
@@ -129,7 +206,7 @@ __global__ void __launch_bounds__(kChunk) permute_count_kernel(
     for (int s = 0; s < k; ++s) {
       int e = ids[(int64_t)t * k + s];
       if (e < 0 || e >= E) {
-        if (skip_invalid) {
+        if (skip_invalid == 1 || (skip_invalid == 2 && e == -1)) {
           my[s] = -1;
           continue;
         }
@@ -295,11 +372,12 @@ cudaError_t launch_map_local_ids(const int32_t* ids, int64_t n, int begin, int c
 // ------------------------------------------------------------------ launchers
 cudaError_t launch_topk(const float* in, int values_are_scores, const float* bias, int T, int E,
                         int k, float routed_scale, int32_t* ids, float* weights, uint32_t* err,
-                        cudaStream_t st) {
+                        cudaStream_t st, const RoutingPolicy& policy, int32_t* sel,
+                        float* diag) {
   if (T == 0) return cudaSuccess;
   const int warps = 8;
-  topk_kernel<<<(T + warps - 1) / warps, warps * 32, 0, st>>>(in, values_are_scores, bias, T, E,
-                                                               k, routed_scale, ids, weights, err);
+  topk_kernel<<<(T + warps - 1) / warps, warps * 32, 0, st>>>(
+      in, values_are_scores, bias, T, E, k, routed_scale, ids, weights, err, policy, sel, diag);
   return cudaGetLastError();
 }
 

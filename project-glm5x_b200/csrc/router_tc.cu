@@ -255,7 +255,8 @@ size_t router_partials_floats(int num_sms, int E) {
 cudaError_t launch_router_tc(const CUtensorMap* tmap_x, const CUtensorMap* tmap_w,
                              const float* bias, int T, int H, int E, int k, float routed_scale,
                              float* logits, int32_t* ids, float* weights, uint32_t* err,
-                             cudaStream_t st, float* partials, int num_sms, int* launches) {
+                             cudaStream_t st, float* partials, int num_sms, int* launches,
+                             const RoutingPolicy& policy, int32_t* sel, float* diag) {
   if (!router_tc_supported(E, H, k)) return cudaErrorInvalidValue;
   if (launches) *launches = 0;
   if (T == 0) return cudaSuccess;
@@ -272,15 +273,23 @@ cudaError_t launch_router_tc(const CUtensorMap* tmap_x, const CUtensorMap* tmap_
              : launch_kl<16>(tmap_x, tmap_w, bias, T, H, E, k, routed_scale, logits, ids,
                              weights, err, st, nsplit, ks_per, partials);
   if (e != cudaSuccess) return e;
+  const bool policy_pass = policy.mode != 0 || sel || diag;
   if (launches) *launches = 1;
-  if (nsplit == 1) return cudaSuccess;
+  if (nsplit == 1) {
+    if (!policy_pass) return cudaSuccess;
+    if (!logits) return cudaErrorInvalidValue;
+    if (launches) *launches = 2;
+    return launch_topk(logits, 0, bias, T, E, k, routed_scale, ids, weights, err, st, policy,
+                       sel, diag);
+  }
   if (launches) *launches = 3;
   if (!logits) return cudaErrorInvalidValue;
   const int64_t n = (int64_t)T * E;
   sum_partials_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(partials, nsplit, n, logits);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  return launch_topk(logits, 0, bias, T, E, k, routed_scale, ids, weights, err, st);
+  return launch_topk(logits, 0, bias, T, E, k, routed_scale, ids, weights, err, st, policy, sel,
+                     diag);
 }
 
 }  // namespace glm5x

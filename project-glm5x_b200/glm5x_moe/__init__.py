@@ -8,7 +8,8 @@ from __future__ import annotations
 
 __all__ = ["GLM5XMoELayer", "NVFP4Expert", "MXFP4Expert", "GLM5XNVFP4Weight",
            "GLM5XMXFP4Weight", "quantize_nvfp4_weight", "quantize_mxfp4_weight",
-           "dequantize_nvfp4", "encode_mxfp4", "decode_mxfp4"]
+           "dequantize_nvfp4", "encode_mxfp4", "decode_mxfp4", "RoutingMode",
+           "RoutingPolicyConfig", "select_routing"]
 
 
 def __getattr__(name):
@@ -19,4 +20,7 @@ def __getattr__(name):
                 "quantize_mxfp4_weight", "dequantize_nvfp4", "encode_mxfp4", "decode_mxfp4"):
         from . import nvfp4
         return getattr(nvfp4, name)
+    if name in ("RoutingMode", "RoutingPolicyConfig", "select_routing", "RoutingDecisions"):
+        from . import routing
+        return getattr(routing, name)
     raise AttributeError(name)

@@ -72,6 +72,23 @@ class MoeStats(ctypes.Structure):
         "loaded_experts")]
 
 
+class RoutingPolicy(ctypes.Structure):
+    _fields_ = [
+        ("mode", ctypes.c_int32), ("fixed_k", ctypes.c_int32), ("mass_target", ctypes.c_float),
+        ("minimum_boundary_gap", ctypes.c_float), ("quality_floor_k", ctypes.c_int32),
+        ("collect_diagnostics", ctypes.c_int32),
+    ]
+
+
+class RoutingStats(ctypes.Structure):
+    _fields_ = [
+        ("decisions", ctypes.c_uint64), ("selected_experts", ctypes.c_uint64),
+        ("quality_escalated_decisions", ctypes.c_uint64),
+        ("normalized_entropy_sum", ctypes.c_double), ("selected_mass_sum", ctypes.c_double),
+        ("boundary_confidence_sum", ctypes.c_double),
+    ]
+
+
 _P = ctypes.c_void_p
 _I32 = ctypes.c_int32
 _I64 = ctypes.c_int64
@@ -120,6 +137,11 @@ SIGNATURES = {
     "glm5x_mxfp4_encode_f32": [_P, _I64, _I64, _I64, _I32, _P, _P, _P],
     "glm5x_mxfp4_decode": [_P, _P, _I64, _I64, _I64, _P, _P],
     "glm5x_select_routing": [_P, _P, _I64, _I32, _I32, _F, _P, _P, _P],
+    "glm5x_select_routing_policy": [_P, _P, _I64, _I32, _I32, ctypes.POINTER(RoutingPolicy), _F,
+                                    _P, _P, _P, _P, _P],
+    "glm5x_moe_set_routing_policy": [_P, ctypes.POINTER(RoutingPolicy)],
+    "glm5x_moe_routing_stats": [_P, ctypes.POINTER(RoutingStats)],
+    "glm5x_moe_routing_decisions": [_P, _I64, _P, _P],
     "glm5x_expert_major_plan": [_P, _I64, _I32, _I32, _P, _P, _P, _P, _P],
     "glm5x_expert_major_plan_noalloc": [_P, _I64, _I32, _I32, _P, _P, _P, _P, _P],
 }

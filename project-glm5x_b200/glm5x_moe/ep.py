@@ -77,11 +77,14 @@ class ExpertParallelMoE:
 
     def plan(self, ids: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
         """(dest [n], token [n], counts [W]) of the dispatch pairs, ordered by
-        destination rank, tokens ascending within a destination."""
+        destination rank, tokens ascending within a destination. Slots with id
+        -1 (left empty by a fixed / adaptive routing policy) go nowhere."""
         T = ids.shape[0]
-        dest = ids.long() // self.per
-        mask = torch.zeros((T, self.world), dtype=torch.bool, device=ids.device)
-        mask.scatter_(1, dest, True)
+        valid = ids >= 0
+        dest = torch.where(valid, ids.long() // self.per, 0)
+        hits = torch.zeros((T, self.world), dtype=torch.int32, device=ids.device)
+        hits.scatter_add_(1, dest, valid.to(torch.int32))
+        mask = hits > 0
         d_idx, t_idx = mask.t().nonzero(as_tuple=True)
         return d_idx, t_idx, mask.sum(dim=0)
 

@@ -227,6 +227,33 @@ class GLM5XMoELayer:
         """256-row token tiles on CTA pairs (default) or single CTAs."""
         N.check(N.lib().glm5x_moe_set_pair_mma(self._h, 1 if enable else 0), self._h)
 
+    def set_routing_policy(self, config, collect_diagnostics: bool = False) -> None:
+        """select_routing policy of the router (a routing.RoutingPolicyConfig:
+        natural, fixed or adaptive Top-K with a quality floor). Fixed and
+        adaptive leave id -1 / weight 0 in the slots past each token's K;
+        ``collect_diagnostics`` keeps the per-token decision scalars in
+        natural mode too."""
+        pol = config.to_c(collect_diagnostics)
+        N.check(N.lib().glm5x_moe_set_routing_policy(self._h, ctypes.byref(pol)), self._h)
+
+    def routing_stats(self) -> dict:
+        """Counters of the last router pass with diagnostics (the reference
+        session's routing_* fields): decisions, selected_experts,
+        quality_escalated_decisions and the entropy / mass / confidence sums."""
+        st = N.RoutingStats()
+        N.check(N.lib().glm5x_moe_routing_stats(self._h, ctypes.byref(st)), self._h)
+        return {name: getattr(st, name) for name, _ in N.RoutingStats._fields_}
+
+    def routing_decisions(self, tokens: int):
+        """Per-token decisions of the last router pass over ``tokens`` tokens
+        (CPU tensors): (sel [T, 2] int32 = selected K, escalated; diag [T, 4]
+        = normalized entropy, effective support, selected mass, confidence)."""
+        sel = torch.empty((tokens, 2), dtype=torch.int32)
+        diag = torch.empty((tokens, 4), dtype=torch.float32)
+        N.check(N.lib().glm5x_moe_routing_decisions(self._h, tokens, sel.data_ptr(),
+                                                    diag.data_ptr()), self._h)
+        return sel, diag
+
     def set_down_tile_n(self, bn: int) -> None:
         """Weight-major down projection token tile (128/256, 0 = gate/up's)."""
         N.check(N.lib().glm5x_moe_set_down_tile_n(self._h, bn), self._h)

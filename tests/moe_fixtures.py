@@ -49,14 +49,15 @@ def make_expert_mxfp4(H: int, I: int, seed: int, device="cuda"):
 
 def oracle_forward(hidden: np.ndarray, ids: np.ndarray, weights: np.ndarray,
                    experts_deq: dict, shared_deq=None, expert_fn=None) -> tuple[np.ndarray, dict]:
-    """hidden [T, H] (BF16 values as FP32); ids/weights [T, k]. Returns the
+    """hidden [T, H] (BF16 values as FP32); ids/weights [T, k] (id -1 = an
+    empty slot, as a fixed / adaptive routing policy leaves). Returns the
     layer output [T, H] and the per-(token, slot) expert outputs. expert_fn
     defaults to the NVFP4 per-slab oracle."""
     expert_fn = expert_fn or O.nvfp4_expert_dequant_oracle
     T, H = hidden.shape
     out = np.zeros((T, H), dtype=np.float64)
     per = {}
-    for e in sorted(set(int(v) for v in ids.reshape(-1))):
+    for e in sorted(set(int(v) for v in ids.reshape(-1) if v >= 0)):  # -1 = empty slot
         tok, slot = np.nonzero(ids == e)
         order = np.argsort(tok, kind="stable")
         tok, slot = tok[order], slot[order]

@@ -6,7 +6,8 @@ expert-parallel result must equal the single-process sum
 out[t] = shared(x_t) + sum_s w[t,s] * expert_{ids[t,s]}(x_t) up to the BF16
 rounding of the per-destination partial sums on their way back (2^-9
 relative each) and FP32 summation order. Covers worlds 2 and 4, ranks that receive no rows, tokens whose
-experts all live on one rank, and uneven token counts per rank.
+experts all live on one rank, uneven token counts per rank, and routes
+with empty slots (id -1, as a fixed-K routing policy leaves them).
 """
 from __future__ import annotations
 
@@ -22,19 +23,23 @@ H, E, K = 32, 16, 4
 
 
 class FakeEngine:
-    def __init__(self, begin: int, count: int, seed: int = 0) -> None:
+    def __init__(self, begin: int, count: int, seed: int = 0, keep: int = K) -> None:
         g = torch.Generator().manual_seed(seed)
         self.router = torch.randn(H, E, generator=g)
         self.experts = torch.randn(E, H, H, generator=g) * 0.1
         self.shared = torch.randn(H, H, generator=g) * 0.1
         self.bias = torch.zeros(E)
         self.begin, self.count = begin, count
+        self.keep = keep  # slots past `keep` left empty (id -1), as a fixed-K policy does
 
     def route(self, x: torch.Tensor):
         logits = x.float() @ self.router + self.bias
         # stable: descending score, ties to the lower expert id
         order = torch.sort(-logits, dim=1, stable=True).indices[:, :K]
         w = torch.softmax(torch.gather(logits, 1, order), dim=1)
+        if self.keep < K:
+            order[:, self.keep:] = -1
+            w[:, self.keep:] = 0.0
         return order.to(torch.int32), w
 
     def forward_expert_rows(self, rows, ids, w, shared_rows=0):
@@ -43,7 +48,7 @@ class FakeEngine:
         for r in range(rows.shape[0]):
             for s in range(K):
                 e = int(ids[r, s])
-                if self.begin <= e < self.begin + self.count:
+                if e >= 0 and self.begin <= e < self.begin + self.count:
                     out[r] += float(w[r, s]) * (xf[r] @ self.experts[e])
             if r < shared_rows:
                 out[r] += xf[r] @ self.shared
@@ -56,14 +61,15 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank: int, world: int, port: int, tokens: list[int], skew: bool, q) -> None:
+def _worker(rank: int, world: int, port: int, tokens: list[int], skew: bool, q,
+            keep: int = K) -> None:
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         from glm5x_moe.ep import ExpertParallelMoE, expert_range
         begin, count = expert_range(rank, world, E)
-        eng = FakeEngine(begin, count)
+        eng = FakeEngine(begin, count, keep=keep)
         if skew:
             # every token prefers experts 0..3 (all on rank 0)
             eng.bias[:4] = 50.0
@@ -72,7 +78,7 @@ def _worker(rank: int, world: int, port: int, tokens: list[int], skew: bool, q) 
         g = torch.Generator().manual_seed(100 + rank)
         x = torch.randn(tokens[rank], H, generator=g).to(torch.bfloat16)
         out = ep(x)
-        ref_eng = FakeEngine(0, E)
+        ref_eng = FakeEngine(0, E, keep=keep)
         if skew:
             ref_eng.bias[:4] = 50.0
         ids, w = ref_eng.route(x)
@@ -83,13 +89,15 @@ def _worker(rank: int, world: int, port: int, tokens: list[int], skew: bool, q) 
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,tokens,skew", [(2, [7, 5], False), (4, [6, 1, 9, 3], False),
-                                               (2, [8, 4], True)])
-def test_expert_parallel_matches_single_process(world, tokens, skew):
+@pytest.mark.parametrize("world,tokens,skew,keep", [(2, [7, 5], False, K),
+                                                    (4, [6, 1, 9, 3], False, K),
+                                                    (2, [8, 4], True, K),
+                                                    (4, [5, 8, 2, 7], False, 2)])
+def test_expert_parallel_matches_single_process(world, tokens, skew, keep):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, tokens, skew, q))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, tokens, skew, q, keep))
              for r in range(world)]
     for p in procs:
         p.start()
