@@ -284,6 +284,27 @@ glm5x_status glm5x_mxfp4_decode(const uint8_t* packed, const uint8_t* scales, in
 glm5x_status glm5x_select_routing(const float* scores, const float* bias, int64_t tokens,
                                   int32_t num_experts, int32_t top_k, float routed_scale,
                                   int32_t* ids, float* weights, void* stream);
+/* ---------------------------------------------------------------- activation files */
+
+/* GLM5XACT BF16 activation batches, the reference's hidden-state hand-off
+ * between its Python layer and C++ runtime (load_glm5x_bf16_activation,
+ * runtime/src/glm5x_activation.cpp:53-109; write_bf16_activation,
+ * converter/glm5x_converter/activation.py:21-57): a 40-byte header
+ * "<8sIIIIHHQI" = ("GLM5XACT", 1, 40, tokens, hidden, 3 = BF16, 0, payload
+ * bytes, CRC32C) then BF16 [tokens, hidden]. Reading with out = NULL checks
+ * the header and file size and returns the extents; with a buffer of
+ * out_elems >= tokens * hidden values it also reads the payload and checks
+ * its CRC. Non-zero expected_* must match. Status codes are the reference's:
+ * IO_ERROR, TRUNCATED_FILE, BAD_MAGIC, UNSUPPORTED_VERSION, INVALID_EXTENT,
+ * DATA_CRC_MISMATCH. Host memory only. */
+glm5x_status glm5x_read_bf16_activation(const char* path, uint32_t expected_tokens,
+                                        uint32_t expected_hidden, uint32_t* tokens,
+                                        uint32_t* hidden, uint16_t* out, uint64_t out_elems);
+/* Writes [tokens, hidden] BF16 values as a GLM5XACT file (beside the path,
+ * then renamed over it). */
+glm5x_status glm5x_write_bf16_activation(const char* path, const uint16_t* data,
+                                         uint32_t tokens, uint32_t hidden);
+
 /* ---------------------------------------------------------------- routing policy */
 
 /* k3x::RoutingMode / RoutingPolicyConfig (runtime/include/k3x/

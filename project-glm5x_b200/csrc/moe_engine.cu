@@ -24,6 +24,7 @@
 #include "fp4_codec.h"
 #include "glm5x_kernels.cuh"
 #include "glm5x_ptx.cuh"
+#include "activation_file.h"
 #include "sidecar.h"
 
 using namespace glm5x;
@@ -1303,6 +1304,30 @@ glm5x_status glm5x_select_routing(const float* scores, const float* bias, int64_
   cudaMemsetAsync(err, 0, 4, st);
   launch_topk(scores, 1, bias, (int)T, E, k, scale, ids, weights, err, st);
   return sync_error(st, err, 0, "select routing");
+}
+
+glm5x_status glm5x_read_bf16_activation(const char* path, uint32_t expected_tokens,
+                                        uint32_t expected_hidden, uint32_t* tokens,
+                                        uint32_t* hidden, uint16_t* out, uint64_t out_elems) {
+  if (!path) return fail_global(GLM5X_INVALID_STATE, "null path");
+  ActivationHeader hdr;
+  std::string msg;
+  const int rc = out ? read_activation(path, expected_tokens, expected_hidden, &hdr, out,
+                                       out_elems, &msg)
+                     : read_activation_header(path, expected_tokens, expected_hidden, &hdr, &msg);
+  if (rc != 0) return fail_global(static_cast<glm5x_status>(rc), "%s", msg.c_str());
+  if (tokens) *tokens = hdr.tokens;
+  if (hidden) *hidden = hdr.hidden;
+  return GLM5X_OK;
+}
+
+glm5x_status glm5x_write_bf16_activation(const char* path, const uint16_t* data,
+                                         uint32_t tokens, uint32_t hidden) {
+  if (!path || !data) return fail_global(GLM5X_INVALID_STATE, "null argument");
+  std::string msg;
+  const int rc = write_activation(path, data, tokens, hidden, &msg);
+  if (rc != 0) return fail_global(static_cast<glm5x_status>(rc), "%s", msg.c_str());
+  return GLM5X_OK;
 }
 
 glm5x_status glm5x_select_routing_policy(const float* scores, const float* bias, int64_t T,

@@ -140,6 +140,10 @@ SIGNATURES = {
     "glm5x_select_routing_policy": [_P, _P, _I64, _I32, _I32, ctypes.POINTER(RoutingPolicy), _F,
                                     _P, _P, _P, _P, _P],
     "glm5x_moe_set_routing_policy": [_P, ctypes.POINTER(RoutingPolicy)],
+    "glm5x_read_bf16_activation": [ctypes.c_char_p, ctypes.c_uint32, ctypes.c_uint32,
+                                   ctypes.POINTER(ctypes.c_uint32),
+                                   ctypes.POINTER(ctypes.c_uint32), _P, ctypes.c_uint64],
+    "glm5x_write_bf16_activation": [ctypes.c_char_p, _P, ctypes.c_uint32, ctypes.c_uint32],
     "glm5x_moe_routing_stats": [_P, ctypes.POINTER(RoutingStats)],
     "glm5x_moe_routing_decisions": [_P, _I64, _P, _P],
     "glm5x_expert_major_plan": [_P, _I64, _I32, _I32, _P, _P, _P, _P, _P],

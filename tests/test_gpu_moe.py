@@ -149,3 +149,30 @@ def test_router_and_layer_glm_shape():
     want, _ = oracle_forward(x, ids_g, w_g, deq, shared)
     _assert_close(res.output.cpu().numpy(), want, "layer")
     layer.close()
+
+
+def test_activation_file_handoff(tmp_path):
+    """The reference bench's hand-off (--input-bf16 / --expected-bf16): the
+    MoE input read from a GLM5XACT file, the output written as one and read
+    back, against the expert oracle."""
+    from glm5x_moe.activation import load_bf16_activation, write_bf16_activation
+    H, I, E, k, T = 512, 512, 8, 2, 24
+    layer = _layer(H, I, E, k, True, T)
+    deq = {}
+    for e in list(range(E)) + [-1]:
+        ex, dq = make_expert(H, I, 400 + e)
+        layer.load_expert(e, ex)
+        deq[e] = dq
+    g = torch.Generator().manual_seed(8)
+    layer.set_router((torch.randn(E, H, generator=g) * 0.05).to(torch.bfloat16),
+                     torch.rand(E, generator=g) * 0.2 - 0.1)
+    write_bf16_activation(tmp_path / "in.glm5xact", torch.randn(T, H, generator=g))
+    hidden = load_bf16_activation(tmp_path / "in.glm5xact", T, H)
+    res = layer(hidden.cuda())
+    write_bf16_activation(tmp_path / "out.glm5xact", res.output)
+    out = load_bf16_activation(tmp_path / "out.glm5xact", T, H).float().numpy()
+    shared = deq.pop(-1)
+    want, _ = oracle_forward(bf16_to_np(hidden), res.topk_indices.numpy(),
+                             res.topk_weights.numpy(), deq, shared)
+    _assert_close(out, want, "activation hand-off")
+    layer.close()
