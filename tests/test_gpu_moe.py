@@ -156,7 +156,7 @@ def test_activation_file_handoff(tmp_path):
     MoE input read from a GLM5XACT file, the output written as one and read
     back, against the expert oracle."""
     from glm5x_moe.activation import load_bf16_activation, write_bf16_activation
-    H, I, E, k, T = 512, 512, 8, 2, 24
+    H, I, E, k, T = 512, 512, 16, 2, 24
     layer = _layer(H, I, E, k, True, T)
     deq = {}
     for e in list(range(E)) + [-1]:
