@@ -100,7 +100,7 @@ cudaError_t launch_map_local_ids(const int32_t* ids, int64_t n, int begin, int c
 cudaError_t launch_permute(const int32_t* ids, const float* weights, const float* token_amax,
                            int T, int k, int E, int has_shared, int bn, PermuteBuffers b,
                            uint32_t* err, cudaStream_t st, int rows_per = 1,
-                           int skip_invalid = 0, int shared_rows = -1);
+                           int skip_invalid = 0, int shared_rows = -1, int* launches = nullptr);
 
 // ------------------------------------------------------------ router_tc.cu
 // BF16 router logits on tcgen05 + sigmoid/bias/top-k epilogue. tmap_x: hidden

@@ -780,11 +780,13 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
     ids = m->ids_local;
     ++launches;
   }
+  int pl = 0;
   G5_CHECK(m, launch_permute(ids, wts, m->token_amax, T, k, E_perm, hs, bn, m->pb, m->err, st,
                              m->terms(), ep_rows ? 1 : 2,
-                             shared_rows < 0 ? -1 : (int)std::min<int64_t>(shared_rows, T)),
+                             shared_rows < 0 ? -1 : (int)std::min<int64_t>(shared_rows, T),
+                             &pl),
            "permute");
-  launches += 3;
+  launches += pl;
   const int64_t max_rows = (int64_t)T * m->kk() + (int64_t)m->nseg * 8;
   mark(4);
   if (mx) {

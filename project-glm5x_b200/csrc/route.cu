@@ -369,6 +369,105 @@ cudaError_t launch_map_local_ids(const int32_t* ids, int64_t n, int begin, int c
   return cudaGetLastError();
 }
 
+// Batches of at most one 256-token chunk (decode): the count, scan and
+// scatter above in one block, so the three dependent launches become one.
+// Same outputs as the three kernels (chunk bases are 0 with one chunk; the
+// per-(token, slot) ranks are recomputed from the shared bitmaps).
+// blockDim = a power of two >= max(256, E + has_shared + 1).
+__global__ void permute_small_kernel(const int32_t* __restrict__ ids,
+                                     const float* __restrict__ weights,
+                                     const float* __restrict__ token_amax, int T, int k, int E,
+                                     int has_shared, int shared_rows, int bn, int rows_per,
+                                     int skip_invalid, PermuteBuffers b, uint32_t* err) {
+  __shared__ uint32_t bits[256][kChunk / 32];
+  extern __shared__ int scan_buf[];
+  for (int i = threadIdx.x; i < 256 * (kChunk / 32); i += blockDim.x) (&bits[0][0])[i] = 0;
+  __syncthreads();
+  auto skipped = [&](int e) {
+    return (e < 0 || e >= E) && (skip_invalid == 1 || (skip_invalid == 2 && e == -1));
+  };
+  {
+    const int t = threadIdx.x;
+    const int word = t / 32, bit = t % 32;
+    if (t < T) {
+      for (int s = 0; s < k; ++s) {
+        int e = ids[(int64_t)t * k + s];
+        if (skipped(e)) continue;
+        if (e < 0 || e >= E) {
+          atomicOr(err, kErrBounds);
+          e = 0;
+        }
+        const uint32_t prev = atomicOr(&bits[e][word], 1u << bit);
+        if (prev & (1u << bit)) atomicOr(err, kErrBounds);  // duplicate expert in one token
+      }
+    }
+  }
+  __syncthreads();
+  // segment counts, starts, quantizer prefix, tile prefix (permute_scan_kernel)
+  const int e = threadIdx.x;
+  const int nseg = E + has_shared;
+  int count = 0;
+  if (e < E) {
+    for (int w = 0; w < kChunk / 32; ++w) count += __popc(bits[e][w]);
+  } else if (e == E && has_shared) {
+    count = shared_rows;
+  }
+  const bool valid = e < nseg;
+  const int rows = count * rows_per;
+  int tot;
+  const int start = block_exclusive_scan(valid ? segment_rows(rows, bn) : 0, scan_buf, &tot);
+  const int q = block_exclusive_scan(valid ? (rows + 7) / 8 * 8 / rows_per : 0, scan_buf, &tot);
+  const int qt = tot;
+  const int nt = valid ? (rows + bn - 1) / bn : 0;
+  const int tp = block_exclusive_scan(nt, scan_buf, &tot);
+  if (valid) {
+    b.seg_count[e] = rows;
+    b.seg_start[e] = start;
+    b.qprefix[e] = q;
+    b.ntile_prefix[e] = tp;
+    b.seg_amax[e] = 0.0f;
+    b.h_amax[e] = 0.0f;
+  }
+  if (e == 0) {
+    b.qprefix[nseg] = qt;
+    b.ntile_prefix[nseg] = tot;
+  }
+  if (e == nseg - 1) b.seg_start[nseg] = start + segment_rows(rows, bn);
+  __syncthreads();
+  // scatter (permute_scatter_kernel with chunk base 0)
+  const int kk = k + has_shared;
+  for (int idx = threadIdx.x; idx < T * kk; idx += blockDim.x) {
+    const int t = idx / kk, s = idx % kk;
+    int p, ex;
+    float w;
+    if (s < k) {
+      ex = ids[(int64_t)t * k + s];
+      if (skipped(ex)) {
+        b.pos[idx] = -1;
+        continue;
+      }
+      ex = ex < 0 || ex >= E ? 0 : ex;
+      const int word = t / 32, bit = t % 32;
+      int r = __popc(bits[ex][word] & ((1u << bit) - 1u));
+      for (int wd = 0; wd < word; ++wd) r += __popc(bits[ex][wd]);
+      p = b.seg_start[ex] + segment_row(rows_per * r, bn);
+      w = weights[(int64_t)t * k + s];
+    } else {
+      if (t >= shared_rows) {
+        b.pos[idx] = -1;
+        continue;
+      }
+      ex = E;
+      p = b.seg_start[E] + segment_row(rows_per * t, bn);
+      w = 1.0f;
+    }
+    b.pos[idx] = p;
+    b.row_token[p] = t;
+    b.row_weight[p] = w;
+    atomicMax(reinterpret_cast<unsigned int*>(b.seg_amax + ex), __float_as_uint(token_amax[t]));
+  }
+}
+
 // ------------------------------------------------------------------ launchers
 cudaError_t launch_topk(const float* in, int values_are_scores, const float* bias, int T, int E,
                         int k, float routed_scale, int32_t* ids, float* weights, uint32_t* err,
@@ -384,9 +483,19 @@ cudaError_t launch_topk(const float* in, int values_are_scores, const float* bia
 cudaError_t launch_permute(const int32_t* ids, const float* weights, const float* token_amax,
                            int T, int k, int E, int has_shared, int bn, PermuteBuffers b,
                            uint32_t* err, cudaStream_t st, int rows_per, int skip_invalid,
-                           int shared_rows) {
+                           int shared_rows, int* launches) {
   const int nchunks = (T + kChunk - 1) / kChunk;
   if (shared_rows < 0 || shared_rows > T) shared_rows = T;
+  if (nchunks == 1 && E <= 256) {
+    int threads = 256;
+    while (threads < E + has_shared + 1) threads <<= 1;
+    permute_small_kernel<<<1, threads, threads * sizeof(int), st>>>(
+        ids, weights, token_amax, T, k, E, has_shared, shared_rows, bn, rows_per, skip_invalid,
+        b, err);
+    if (launches) *launches = 1;
+    return cudaGetLastError();
+  }
+  if (launches) *launches = 3;
   if (T > 0) {
     permute_count_kernel<<<nchunks, kChunk, 0, st>>>(ids, T, k, E, skip_invalid, b.chunk_count,
                                                      b.rank, err);

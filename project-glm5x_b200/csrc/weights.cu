@@ -63,11 +63,14 @@ __global__ void scales_to_blocked_kernel(const uint8_t* __restrict__ rm, int64_t
 // sum to out instead of storing it.
 __global__ void combine_kernel(const uint16_t* __restrict__ y, const int32_t* __restrict__ pos,
                                int kk, int H, float* __restrict__ out, int accumulate) {
+  // block (t, y) sums 8-element groups y * per .. (y + 1) * per - 1 of token t
   const int t = blockIdx.x;
+  const int per = (H / 8 + gridDim.y - 1) / gridDim.y;
+  const int v_end = min(H / 8, ((int)blockIdx.y + 1) * per);
   __shared__ int32_t rows[32];
   if (threadIdx.x < kk) rows[threadIdx.x] = pos[(int64_t)t * kk + threadIdx.x];
   __syncthreads();
-  for (int v = threadIdx.x; v < H / 8; v += blockDim.x) {
+  for (int v = blockIdx.y * per + threadIdx.x; v < v_end; v += blockDim.x) {
     float acc[8] = {};
     for (int s = 0; s < kk; ++s) {
       if (rows[s] < 0) continue;  // slot with no expert on this engine
@@ -133,7 +136,9 @@ cudaError_t launch_combine(const uint16_t* y, const int32_t* pos, int T, int kk,
                            float* out, cudaStream_t st, int accumulate) {
   if (T == 0) return cudaSuccess;
   if (kk > 32 || H % 8) return cudaErrorInvalidValue;
-  combine_kernel<<<T, 256, 0, st>>>(y, pos, kk, H, out, accumulate);
+  // small batches split each token's row over several blocks to fill the SMs
+  const int split = std::max(1, std::min(H / 8 / 256, 296 / T));
+  combine_kernel<<<dim3(T, split), 256, 0, st>>>(y, pos, kk, H, out, accumulate);
   return cudaGetLastError();
 }
 

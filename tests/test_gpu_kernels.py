@@ -115,7 +115,8 @@ def test_gpu_select_routing_bit_exact():
             assert np.array_equal(w_h[t], (wo * np.float32(scale)).astype(np.float32)), t
 
 
-@pytest.mark.parametrize("T,E,k", [(1, 8, 2), (300, 256, 8), (1000, 64, 4)])
+@pytest.mark.parametrize("T,E,k", [(1, 8, 2), (64, 256, 8), (256, 256, 8), (300, 256, 8),
+                                   (1000, 64, 4)])
 def test_gpu_expert_major_plan(T, E, k):
     from glm5x_moe import _native as N
     rng = np.random.default_rng(T)
