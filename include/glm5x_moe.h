@@ -35,10 +35,15 @@ typedef enum glm5x_status {
   GLM5X_IO_ERROR = 1,
   GLM5X_BAD_MAGIC = 2,
   GLM5X_UNSUPPORTED_VERSION = 3,
+  GLM5X_UNSUPPORTED_REQUIRED_FEATURE = 4,
+  GLM5X_SUPERBLOCK_CRC_MISMATCH = 6,
   GLM5X_TRUNCATED_FILE = 7,
+  GLM5X_INVALID_DIRECTORY = 8,
   GLM5X_INVALID_EXTENT = 9,
   GLM5X_DATA_CRC_MISMATCH = 10,
   GLM5X_AUXILIARY_CRC_MISMATCH = 11,
+  GLM5X_DIRECTORY_SHA256_MISMATCH = 12,
+  GLM5X_ROOT_SHA256_MISMATCH = 13,
   GLM5X_TENSOR_NOT_FOUND = 14,
   GLM5X_INVALID_MXFP4 = 15,
   GLM5X_INVALID_STATE = 16,
@@ -158,6 +163,54 @@ glm5x_status glm5x_moe_load_expert_mxfp4_device(glm5x_moe* moe, int32_t expert,
  * "<8sII" ("GLM5XPI4", 1, json_len), sorted compact JSON, payload; CRC32C of
  * every section is verified. */
 glm5x_status glm5x_moe_load_sidecar(glm5x_moe* moe, int32_t expert, const char* path);
+
+/* ---------------------------------------------------------------- .k3x containers */
+
+/* An open K3X v1 checkpoint container (.k3x), the reference runtime's weight
+ * file: opened with the checks of k3x::Reader::open (runtime/src/reader.cpp:
+ * 420-702) and its status codes (BAD_MAGIC, UNSUPPORTED_VERSION,
+ * SUPERBLOCK_CRC_MISMATCH, TRUNCATED_FILE, INVALID_DIRECTORY, INVALID_EXTENT,
+ * ...). verify_checksums = 1 is the reader's checksums mode: every extent's
+ * CRC32C and the directory and root SHA-256 (a pass over the whole file);
+ * 0 checks the metadata only. Host memory only. */
+typedef struct glm5x_k3x glm5x_k3x;
+
+/* One tensor record (converter/k3x_converter/format.py:155-210): dtype 1 FP32,
+ * 2 UINT8, 3 BF16; quantization 1 = MXFP4 (UINT8 packed E2M1 data, E8M0
+ * auxiliary extent); dimensions[0..rank) = the logical shape. */
+typedef struct glm5x_k3x_tensor_info {
+  uint64_t tensor_id; /* FNV-1a 64 of the tensor name */
+  int32_t dtype;
+  int32_t quantization;
+  int32_t rank;
+  int32_t layer_id;   /* -1 = none */
+  int32_t expert_id;  /* -1 = none */
+  int32_t reserved;
+  uint64_t dimensions[4];
+  uint64_t data_length;
+  uint64_t logical_length;
+  uint64_t auxiliary_length;
+} glm5x_k3x_tensor_info;
+
+glm5x_status glm5x_k3x_open(const char* path, int32_t verify_checksums, glm5x_k3x** out);
+void glm5x_k3x_close(glm5x_k3x* file);
+/* The record of tensor `name` (looked up by FNV-1a 64 of the name, as
+ * runtime/src/model.cpp:538-551 does); TENSOR_NOT_FOUND if absent. */
+glm5x_status glm5x_k3x_tensor(const glm5x_k3x* file, const char* name,
+                              glm5x_k3x_tensor_info* info);
+/* Reads tensor `name`'s data (and auxiliary extent, when it has one and
+ * `auxiliary` is not NULL) into host buffers of at least their lengths
+ * (Reader::read_tensor / read_auxiliary, runtime/src/reader.cpp:749-778). */
+glm5x_status glm5x_k3x_read(const glm5x_k3x* file, const char* name, void* data,
+                            uint64_t data_capacity, void* auxiliary, uint64_t auxiliary_capacity);
+/* Admits expert slot `expert` (-1 = shared) from the three MXFP4 records
+ * `<prefix>.gate`, `<prefix>.up`, `<prefix>.down` of an open container (the
+ * names runtime/src/model.cpp:538-551 builds, e.g.
+ * "model.layers.1.feed_forward.experts.3"), through
+ * glm5x_moe_load_expert_mxfp4: row-major E8M0 scales are reordered into the
+ * MMA's blocked layout, 0xFF scales rejected. The engine must be MXFP4. */
+glm5x_status glm5x_moe_load_expert_k3x(glm5x_moe* moe, int32_t expert, const glm5x_k3x* file,
+                                       const char* prefix);
 
 /* Full sublayer on device buffers: hidden [T, hidden] BF16 -> out [T, hidden]
  * FP32 = sum over top-k of weight * expert(x) + shared(x). Asynchronous on

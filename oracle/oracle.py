@@ -91,6 +91,12 @@ def ref_lib() -> ctypes.CDLL | None:
         R.ref_select_routing.argtypes = [_f32p, _f32p, ctypes.c_int, ctypes.c_int, _i32p, _f32p]
         R.ref_select_routing_policy.restype = ctypes.c_int
         R.ref_select_routing_policy.argtypes = _POLICY_ARGS
+        R.ref_k3x_open.restype = ctypes.c_int
+        R.ref_k3x_open.argtypes = [ctypes.c_char_p, ctypes.c_int]
+        R.ref_k3x_read.restype = ctypes.c_int
+        R.ref_k3x_read.argtypes = [ctypes.c_char_p, ctypes.c_uint64, _u8p, ctypes.c_uint64, _u8p,
+                                   ctypes.c_uint64, ctypes.POINTER(ctypes.c_uint64),
+                                   ctypes.POINTER(ctypes.c_uint64)]
         R.ref_decode_mxfp4.restype = ctypes.c_int
         R.ref_decode_mxfp4.argtypes = [_u8p, _u8p, _i64, _i64, _i64, _f32p]
         R.ref_dense_silu_mlp.restype = ctypes.c_int
@@ -224,6 +230,22 @@ def select_routing_policy(scores, bias, k: int, mode: str = "natural", fixed_k: 
           float(minimum_boundary_gap), quality_floor_k, ids, w, sel, diag):
         raise ValueError("invalid routing")
     return ids, w, int(sel[0]), bool(sel[1]), diag
+
+
+def ref_k3x_open(path, verify: bool = True) -> int:
+    """k3x::Reader::open of the reference's C++ (oracle/_ref): its ErrorCode."""
+    return int(ref_lib().ref_k3x_open(str(path).encode(), 1 if verify else 0))
+
+
+def ref_k3x_read(path, tensor_id: int, capacity: int = 1 << 24):
+    """(status, data bytes, auxiliary bytes) of Reader::read_tensor /
+    read_auxiliary in the reference's C++ (oracle/_ref)."""
+    data = np.zeros(capacity, dtype=np.uint8)
+    aux = np.zeros(capacity, dtype=np.uint8)
+    dl, al = ctypes.c_uint64(), ctypes.c_uint64()
+    rc = ref_lib().ref_k3x_read(str(path).encode(), tensor_id, data, capacity, aux, capacity,
+                                ctypes.byref(dl), ctypes.byref(al))
+    return int(rc), data[:dl.value].copy(), aux[:al.value].copy()
 
 
 def route_tokens(hidden, router, bias, k: int = 8, routed_scale: float = 2.5,

@@ -10,6 +10,7 @@
 #include "k3x/expert_major.hpp"
 #include "k3x/ops.hpp"
 #include "k3x/routing_policy.hpp"
+#include "k3x/reader.hpp"
 
 #include <cstddef>
 #include <cstdint>
@@ -69,6 +70,37 @@ int ref_select_routing_policy(const float* scores, const float* bias, int n, int
   diag[1] = d.entropy_effective_support;
   diag[2] = d.selected_cumulative_mass;
   diag[3] = d.boundary_confidence;
+  return 0;
+}
+
+// k3x::Reader::open (runtime/src/reader.cpp:420-702): the ErrorCode value,
+// verify = the checksums mode.
+int ref_k3x_open(const char* path, int verify) {
+  auto r = k3x::Reader::open(path, verify ? k3x::VerifyMode::checksums
+                                          : k3x::VerifyMode::metadata_only);
+  return r ? 0 : static_cast<int>(r.error());
+}
+
+// Reader::read_tensor / read_auxiliary (runtime/src/reader.cpp:749-778) of the
+// tensor with the given id, metadata-only open; lengths in *data_len / *aux_len.
+int ref_k3x_read(const char* path, uint64_t tensor_id, uint8_t* data, uint64_t data_cap,
+                 uint8_t* aux, uint64_t aux_cap, uint64_t* data_len, uint64_t* aux_len) {
+  auto r = k3x::Reader::open(path, k3x::VerifyMode::metadata_only);
+  if (!r) return static_cast<int>(r.error());
+  auto d = r.value().read_tensor(tensor_id);
+  if (!d) return static_cast<int>(d.error());
+  *data_len = d.value().size();
+  if (*data_len > data_cap) return -1;
+  std::memcpy(data, d.value().data(), *data_len);
+  *aux_len = 0;
+  for (const auto& t : r.value().tensors()) {
+    if (t.tensor_id != tensor_id || !t.auxiliary_length) continue;
+    auto a = r.value().read_auxiliary(tensor_id);
+    if (!a) return static_cast<int>(a.error());
+    *aux_len = a.value().size();
+    if (*aux_len > aux_cap) return -1;
+    std::memcpy(aux, a.value().data(), *aux_len);
+  }
   return 0;
 }
 

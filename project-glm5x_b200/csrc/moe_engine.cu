@@ -25,6 +25,7 @@
 #include "glm5x_kernels.cuh"
 #include "glm5x_ptx.cuh"
 #include "activation_file.h"
+#include "k3x_reader.h"
 #include "sidecar.h"
 
 using namespace glm5x;
@@ -676,6 +677,96 @@ glm5x_status glm5x_moe_load_expert_mxfp4_device(glm5x_moe* m, int32_t expert,
                                                 const glm5x_mxfp4_matrix* up,
                                                 const glm5x_mxfp4_matrix* down) {
   return load_mxfp4_common(m, expert, gate, up, down, true);
+}
+
+struct glm5x_k3x {
+  K3xFile file;
+};
+
+glm5x_status glm5x_k3x_open(const char* path, int32_t verify, glm5x_k3x** out) {
+  if (!path || !out) return fail_global(GLM5X_INVALID_STATE, "null argument");
+  *out = nullptr;
+  auto* h = new glm5x_k3x;
+  std::string msg;
+  const int rc = k3x_open(path, verify != 0, &h->file, &msg);
+  if (rc != 0) {
+    delete h;
+    return fail_global(static_cast<glm5x_status>(rc), "%s: %s", path, msg.c_str());
+  }
+  *out = h;
+  return GLM5X_OK;
+}
+
+void glm5x_k3x_close(glm5x_k3x* h) { delete h; }
+
+static const K3xTensor* k3x_lookup(const glm5x_k3x* h, const char* name) {
+  return (h && name) ? k3x_find(h->file, fnv1a64(name)) : nullptr;
+}
+
+glm5x_status glm5x_k3x_tensor(const glm5x_k3x* h, const char* name, glm5x_k3x_tensor_info* info) {
+  if (!h || !name || !info) return fail_global(GLM5X_INVALID_STATE, "null argument");
+  const K3xTensor* t = k3x_lookup(h, name);
+  if (!t) return fail_global(GLM5X_TENSOR_NOT_FOUND, "%s", name);
+  glm5x_k3x_tensor_info r{};
+  r.tensor_id = t->tensor_id;
+  r.dtype = t->dtype;
+  r.quantization = t->quantization;
+  r.rank = t->rank;
+  r.layer_id = t->layer_id;
+  r.expert_id = t->expert_id;
+  for (int d = 0; d < 4; ++d) r.dimensions[d] = t->dims[d];
+  r.data_length = t->data_length;
+  r.logical_length = t->logical_length;
+  r.auxiliary_length = t->auxiliary_length;
+  *info = r;
+  return GLM5X_OK;
+}
+
+glm5x_status glm5x_k3x_read(const glm5x_k3x* h, const char* name, void* data, uint64_t data_cap,
+                            void* aux, uint64_t aux_cap) {
+  if (!h || !name || !data) return fail_global(GLM5X_INVALID_STATE, "null argument");
+  const K3xTensor* t = k3x_lookup(h, name);
+  if (!t) return fail_global(GLM5X_TENSOR_NOT_FOUND, "%s", name);
+  if (data_cap < t->data_length || (aux && t->auxiliary_length && aux_cap < t->auxiliary_length))
+    return fail_global(GLM5X_INVALID_EXTENT, "%s: buffer smaller than the extent", name);
+  std::string msg;
+  int rc = k3x_read_extent(h->file, t->data_offset, t->data_length,
+                           static_cast<uint8_t*>(data), &msg);
+  if (rc == 0 && aux && t->auxiliary_length)
+    rc = k3x_read_extent(h->file, t->auxiliary_offset, t->auxiliary_length,
+                         static_cast<uint8_t*>(aux), &msg);
+  if (rc != 0) return fail_global(static_cast<glm5x_status>(rc), "%s: %s", name, msg.c_str());
+  return GLM5X_OK;
+}
+
+glm5x_status glm5x_moe_load_expert_k3x(glm5x_moe* m, int32_t expert, const glm5x_k3x* h,
+                                       const char* prefix) {
+  if (!m || !h || !prefix) return fail_global(GLM5X_INVALID_STATE, "null argument");
+  static const char* roles[3] = {"gate", "up", "down"};
+  std::vector<uint8_t> packed[3], scales[3];
+  glm5x_mxfp4_matrix mats[3];
+  for (int r = 0; r < 3; ++r) {
+    const std::string name = std::string(prefix) + "." + roles[r];
+    const K3xTensor* t = k3x_lookup(h, name.c_str());
+    if (!t) return m->fail(GLM5X_TENSOR_NOT_FOUND, "%s", name.c_str());
+    if (t->dtype != 2 || t->quantization != 1 || t->rank != 2)
+      return m->fail(GLM5X_INVALID_MXFP4, "%s is not a rank-2 MXFP4 record", name.c_str());
+    const uint64_t rows = t->dims[0], cols = t->dims[1];
+    if (cols % 32 || t->data_length != rows * cols / 2 || t->auxiliary_length != rows * cols / 32)
+      return m->fail(GLM5X_INVALID_EXTENT, "%s: extents do not match [%llu, %llu]", name.c_str(),
+                     (unsigned long long)rows, (unsigned long long)cols);
+    packed[r].resize(t->data_length);
+    scales[r].resize(t->auxiliary_length);
+    std::string msg;
+    int rc = k3x_read_extent(h->file, t->data_offset, t->data_length, packed[r].data(), &msg);
+    if (rc == 0)
+      rc = k3x_read_extent(h->file, t->auxiliary_offset, t->auxiliary_length, scales[r].data(),
+                           &msg);
+    if (rc != 0) return m->fail(static_cast<glm5x_status>(rc), "%s: %s", name.c_str(), msg.c_str());
+    mats[r] = glm5x_mxfp4_matrix{packed[r].data(), scales[r].data(), (int64_t)rows,
+                                 (int64_t)cols, 32};
+  }
+  return glm5x_moe_load_expert_mxfp4(m, expert, &mats[0], &mats[1], &mats[2]);
 }
 
 glm5x_status glm5x_moe_load_sidecar(glm5x_moe* m, int32_t expert, const char* path) {

@@ -15,8 +15,10 @@ LIB_PATH = Path(os.environ.get("GLM5X_LIBRARY") or
                 Path(__file__).resolve().parent / "libglm5x_moe.so")
 
 STATUS_NAMES = {
-    0: "OK", 1: "IO_ERROR", 2: "BAD_MAGIC", 3: "UNSUPPORTED_VERSION", 7: "TRUNCATED_FILE",
-    9: "INVALID_EXTENT", 10: "DATA_CRC_MISMATCH", 11: "AUXILIARY_CRC_MISMATCH",
+    0: "OK", 1: "IO_ERROR", 2: "BAD_MAGIC", 3: "UNSUPPORTED_VERSION",
+    4: "UNSUPPORTED_REQUIRED_FEATURE", 6: "SUPERBLOCK_CRC_MISMATCH", 7: "TRUNCATED_FILE",
+    8: "INVALID_DIRECTORY", 9: "INVALID_EXTENT", 10: "DATA_CRC_MISMATCH",
+    11: "AUXILIARY_CRC_MISMATCH", 12: "DIRECTORY_SHA256_MISMATCH", 13: "ROOT_SHA256_MISMATCH",
     14: "TENSOR_NOT_FOUND", 15: "INVALID_MXFP4", 16: "INVALID_STATE",
     17: "BACKEND_UNAVAILABLE", 19: "UNSUPPORTED_ARCHITECTURE", 100: "DEVICE_ERROR",
     101: "OUT_OF_MEMORY", 102: "WAIT_TIMEOUT",
@@ -89,6 +91,16 @@ class RoutingStats(ctypes.Structure):
     ]
 
 
+class K3xTensorInfo(ctypes.Structure):
+    _fields_ = [
+        ("tensor_id", ctypes.c_uint64), ("dtype", ctypes.c_int32),
+        ("quantization", ctypes.c_int32), ("rank", ctypes.c_int32), ("layer_id", ctypes.c_int32),
+        ("expert_id", ctypes.c_int32), ("reserved", ctypes.c_int32),
+        ("dimensions", ctypes.c_uint64 * 4), ("data_length", ctypes.c_uint64),
+        ("logical_length", ctypes.c_uint64), ("auxiliary_length", ctypes.c_uint64),
+    ]
+
+
 _P = ctypes.c_void_p
 _I32 = ctypes.c_int32
 _I64 = ctypes.c_int64
@@ -112,6 +124,11 @@ SIGNATURES = {
                                            ctypes.POINTER(Mxfp4Matrix),
                                            ctypes.POINTER(Mxfp4Matrix)],
     "glm5x_moe_load_sidecar": [_P, _I32, ctypes.c_char_p],
+    "glm5x_k3x_open": [ctypes.c_char_p, _I32, ctypes.POINTER(_P)],
+    "glm5x_k3x_close": [_P],
+    "glm5x_k3x_tensor": [_P, ctypes.c_char_p, ctypes.POINTER(K3xTensorInfo)],
+    "glm5x_k3x_read": [_P, ctypes.c_char_p, _P, ctypes.c_uint64, _P, ctypes.c_uint64],
+    "glm5x_moe_load_expert_k3x": [_P, _I32, _P, ctypes.c_char_p],
     "glm5x_moe_forward": [_P, _P, _I64, _P, _P],
     "glm5x_moe_forward_host": [_P, _P, _I64, _P],
     "glm5x_moe_forward_routed": [_P, _P, _I64, _P, _P, _P, _P],
@@ -151,6 +168,7 @@ SIGNATURES = {
 }
 _RESTYPE = {
     "glm5x_moe_destroy": None,
+    "glm5x_k3x_close": None,
     "glm5x_moe_error_message": ctypes.c_char_p,
     "glm5x_last_error_message": ctypes.c_char_p,
 }

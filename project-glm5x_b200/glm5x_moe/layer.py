@@ -113,6 +113,13 @@ class GLM5XMoELayer:
             N.check(fn(self._h, expert_id, ctypes.byref(g), ctypes.byref(u), ctypes.byref(d)),
                     self._h)
 
+    def load_expert_k3x(self, expert_id: int, k3x_file, prefix: str) -> None:
+        """Admit expert ``expert_id`` (-1 = shared) from the MXFP4 records
+        ``<prefix>.gate / .up / .down`` of an open ``k3x.K3xFile`` (e.g.
+        prefix "model.layers.1.feed_forward.experts.3"); MXFP4 layers only."""
+        N.check(N.lib().glm5x_moe_load_expert_k3x(self._h, expert_id, k3x_file.handle,
+                                                  prefix.encode()), self._h)
+
     def load_sidecar(self, expert_id: int, path: str) -> None:
         N.check(N.lib().glm5x_moe_load_sidecar(self._h, expert_id, str(path).encode()), self._h)
 
