@@ -419,6 +419,26 @@ glm5x_status glm5x_select_routing_policy(const float* scores, const float* bias,
                                          int32_t* ids, float* weights, int32_t* sel,
                                          float* diag, void* stream);
 
+/* Greedy verification of speculative draft blocks for S sequences at once
+ * (verify_greedy_target_block, runtime/src/speculative.cpp:75-113): sequence
+ * s proposed draft_counts[s] <= max_draft_tokens candidates after
+ * anchors[s], and targets[s, 0 .. n] are the target's argmax tokens after the
+ * anchor and after each candidate (one expert-major block per sequence, as
+ * runtime/src/model.cpp:1640-1690 runs them). Outputs: accepted[s] = the
+ * length of the matching prefix, committed[s, 0 .. accepted[s]] = the
+ * accepted candidates then the first mismatching (or bonus) target token,
+ * status[s] = 0, GLM5X_INVALID_EXTENT (anchor or candidate outside the
+ * vocabulary, n outside [0, max]) or GLM5X_INVALID_STATE (a target token
+ * outside the vocabulary), as the reference returns them per sequence.
+ * Device buffers: candidates [S, max], targets / committed [S, max + 1].
+ * Asynchronous on `stream`. */
+glm5x_status glm5x_verify_greedy_target_blocks(const uint32_t* anchors, const uint32_t* candidates,
+                                               const int32_t* draft_counts,
+                                               const uint32_t* targets, int64_t sequences,
+                                               int32_t max_draft_tokens, uint32_t vocabulary_size,
+                                               int32_t* accepted, uint32_t* committed,
+                                               int32_t* status, void* stream);
+
 /* out[t] (+)= sum over s < slots of rows[pos[t, s]] (BF16 rows, FP32 sums in
  * slot order; pos < 0 = absent), device buffers: the weighted scatter of
  * scatter_expert_major_outputs (runtime/src/expert_major.cpp:148-196) /

@@ -488,6 +488,28 @@ int orc_select_routing_policy(const float* scores, const float* bias, int n, int
   return 0;
 }
 
+/* verify_greedy_target_block (runtime/src/speculative.cpp:8-21, 75-113):
+ * candidates[n] after `anchor`, targets[n_targets]. Returns 0 (committed[0 ..
+ * *accepted] filled), 9 (invalid extent) or 16 (invalid state). */
+int orc_verify_greedy_target_block(uint32_t anchor, const uint32_t* candidates, int n,
+                                   int max_draft, uint32_t vocab, const uint32_t* targets,
+                                   int n_targets, int* accepted, uint32_t* committed) {
+  if (vocab == 0 || anchor >= vocab || n > max_draft) return 9;
+  for (int i = 0; i < n; ++i)
+    if (candidates[i] >= vocab) return 9;
+  if (n_targets == 0 || n_targets - 1 != n) return 9;
+  for (int i = 0; i < n_targets; ++i)
+    if (targets[i] >= vocab) return 16;
+  int a = 0;
+  for (; a < n; ++a) {
+    if (candidates[a] != targets[a]) break;
+    committed[a] = candidates[a];
+  }
+  committed[a] = a < n ? targets[a] : targets[n_targets - 1];
+  *accepted = a;
+  return 0;
+}
+
 /* ---------------------------------------------------------------------- */
 /* Dense SwiGLU expert (CPU reference path)                                */
 /* ---------------------------------------------------------------------- */

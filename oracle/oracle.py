@@ -31,6 +31,9 @@ _f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
 _u8p = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
 _i32p = np.ctypeslib.ndpointer(dtype=np.int32, flags="C_CONTIGUOUS")
 _i64 = ctypes.c_int64
+_u32p = np.ctypeslib.ndpointer(dtype=np.uint32, flags="C_CONTIGUOUS")
+_VERIFY_ARGS = [ctypes.c_uint32, _u32p, ctypes.c_int, ctypes.c_int, ctypes.c_uint32, _u32p,
+                ctypes.c_int, ctypes.POINTER(ctypes.c_int), _u32p]
 _POLICY_ARGS = [_f32p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                 ctypes.c_float, ctypes.c_float, ctypes.c_int, _i32p, _f32p, _i32p, _f32p]
 
@@ -68,6 +71,8 @@ def lib() -> ctypes.CDLL:
         L.orc_select_routing.argtypes = [_f32p, _f32p, ctypes.c_int, ctypes.c_int, _i32p, _f32p]
         L.orc_select_routing_policy.restype = ctypes.c_int
         L.orc_select_routing_policy.argtypes = _POLICY_ARGS
+        L.orc_verify_greedy_target_block.restype = ctypes.c_int
+        L.orc_verify_greedy_target_block.argtypes = _VERIFY_ARGS
         L.orc_route_tokens.restype = ctypes.c_int
         L.orc_route_tokens.argtypes = [_f32p, _f32p, _f32p, _i64, _i64, ctypes.c_int,
                                        ctypes.c_int, ctypes.c_float, ctypes.c_void_p, _i32p, _f32p]
@@ -91,6 +96,8 @@ def ref_lib() -> ctypes.CDLL | None:
         R.ref_select_routing.argtypes = [_f32p, _f32p, ctypes.c_int, ctypes.c_int, _i32p, _f32p]
         R.ref_select_routing_policy.restype = ctypes.c_int
         R.ref_select_routing_policy.argtypes = _POLICY_ARGS
+        R.ref_verify_greedy_target_block.restype = ctypes.c_int
+        R.ref_verify_greedy_target_block.argtypes = _VERIFY_ARGS
         R.ref_k3x_open.restype = ctypes.c_int
         R.ref_k3x_open.argtypes = [ctypes.c_char_p, ctypes.c_int]
         R.ref_k3x_read.restype = ctypes.c_int
@@ -246,6 +253,21 @@ def ref_k3x_read(path, tensor_id: int, capacity: int = 1 << 24):
     rc = ref_lib().ref_k3x_read(str(path).encode(), tensor_id, data, capacity, aux, capacity,
                                 ctypes.byref(dl), ctypes.byref(al))
     return int(rc), data[:dl.value].copy(), aux[:al.value].copy()
+
+
+def verify_greedy_target_block(anchor: int, candidates, max_draft: int, vocab: int, targets,
+                               use_reference: bool = False):
+    """(status, accepted, committed tokens) of verify_greedy_target_block;
+    `use_reference` runs the reference's own C++ (oracle/_ref)."""
+    c = np.ascontiguousarray(np.asarray(candidates, dtype=np.uint32).reshape(-1))
+    t = np.ascontiguousarray(np.asarray(targets, dtype=np.uint32).reshape(-1))
+    out = np.zeros(c.size + 2, dtype=np.uint32)
+    acc = ctypes.c_int(0)
+    fn = (ref_lib().ref_verify_greedy_target_block if use_reference
+          else lib().orc_verify_greedy_target_block)
+    rc = fn(int(anchor), c if c.size else np.zeros(1, np.uint32), c.size, int(max_draft),
+            int(vocab), t if t.size else np.zeros(1, np.uint32), t.size, ctypes.byref(acc), out)
+    return int(rc), (acc.value if rc == 0 else 0), (out[:acc.value + 1].copy() if rc == 0 else None)
 
 
 def route_tokens(hidden, router, bias, k: int = 8, routed_scale: float = 2.5,

@@ -11,6 +11,7 @@
 #include "k3x/ops.hpp"
 #include "k3x/routing_policy.hpp"
 #include "k3x/reader.hpp"
+#include "k3x/speculative.hpp"
 
 #include <cstddef>
 #include <cstdint>
@@ -101,6 +102,24 @@ int ref_k3x_read(const char* path, uint64_t tensor_id, uint8_t* data, uint64_t d
     if (*aux_len > aux_cap) return -1;
     std::memcpy(aux, a.value().data(), *aux_len);
   }
+  return 0;
+}
+
+// k3x::verify_greedy_target_block (runtime/src/speculative.cpp:75-113):
+// 0 (committed / accepted filled) or the ErrorCode value.
+int ref_verify_greedy_target_block(uint32_t anchor, const uint32_t* candidates, int n,
+                                   int max_draft, uint32_t vocab, const uint32_t* targets,
+                                   int n_targets, int* accepted, uint32_t* committed) {
+  k3x::DraftProposal p;
+  p.anchor_token = anchor;
+  p.candidate_tokens.assign(candidates, candidates + n);
+  auto r = k3x::verify_greedy_target_block(
+      p, static_cast<std::size_t>(max_draft), vocab,
+      std::span<const std::uint32_t>(targets, static_cast<std::size_t>(n_targets)));
+  if (!r) return static_cast<int>(r.error());
+  *accepted = static_cast<int>(r.value().accepted_draft_tokens);
+  for (std::size_t i = 0; i < r.value().committed_tokens.size(); ++i)
+    committed[i] = r.value().committed_tokens[i];
   return 0;
 }
 

@@ -102,6 +102,15 @@ cudaError_t launch_permute(const int32_t* ids, const float* weights, const float
                            uint32_t* err, cudaStream_t st, int rows_per = 1,
                            int skip_invalid = 0, int shared_rows = -1, int* launches = nullptr);
 
+// ------------------------------------------------------------ speculative.cu
+// verify_greedy_target_block for S sequences (one thread each): status[s] 0,
+// 9 (invalid extent) or 16 (invalid state); committed[s, 0 .. accepted[s]].
+cudaError_t launch_verify_greedy_blocks(const uint32_t* anchors, const uint32_t* candidates,
+                                        const int32_t* draft_counts, const uint32_t* targets,
+                                        int64_t S, int max_draft, uint32_t vocab,
+                                        int32_t* accepted, uint32_t* committed, int32_t* status,
+                                        cudaStream_t st);
+
 // ------------------------------------------------------------ router_tc.cu
 // BF16 router logits on tcgen05 + sigmoid/bias/top-k epilogue. tmap_x: hidden
 // [T, H] BF16, box {64, 128}; tmap_w: router weight [E, H] BF16, box {64, E}.

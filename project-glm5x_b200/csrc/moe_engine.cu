@@ -1440,6 +1440,22 @@ glm5x_status glm5x_select_routing_policy(const float* scores, const float* bias,
   return sync_error(st, err, 0, "select routing");
 }
 
+glm5x_status glm5x_verify_greedy_target_blocks(const uint32_t* anchors, const uint32_t* candidates,
+                                               const int32_t* draft_counts,
+                                               const uint32_t* targets, int64_t S,
+                                               int32_t max_draft, uint32_t vocab,
+                                               int32_t* accepted, uint32_t* committed,
+                                               int32_t* status, void* stream) {
+  if (!anchors || !draft_counts || !targets || !accepted || !committed || !status || S <= 0 ||
+      max_draft < 0 || (max_draft > 0 && !candidates))
+    return fail_global(GLM5X_INVALID_STATE, "verify: null buffer or bad sizes");
+  if (vocab == 0) return fail_global(GLM5X_INVALID_EXTENT, "verify: empty vocabulary");
+  if (launch_verify_greedy_blocks(anchors, candidates, draft_counts, targets, S, max_draft, vocab,
+                                  accepted, committed, status, as_stream(stream)) != cudaSuccess)
+    return fail_global(GLM5X_DEVICE_ERROR, "verify launch");
+  return GLM5X_OK;
+}
+
 glm5x_status glm5x_combine_rows(const void* rows_bf16, const int32_t* pos, int64_t T,
                                 int32_t slots, int64_t hidden, float* out, int32_t accumulate,
                                 void* stream) {

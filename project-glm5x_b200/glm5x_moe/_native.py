@@ -135,6 +135,8 @@ SIGNATURES = {
     "glm5x_moe_forward_expert_rows": [_P, _P, _I64, _P, _P, _I64, _P, _P],
     "glm5x_moe_route": [_P, _P, _I64, _P, _P, _P, _P],
     "glm5x_combine_rows": [_P, _P, _I64, _I32, _I64, _P, _I32, _P],
+    "glm5x_verify_greedy_target_blocks": [_P, _P, _P, _P, _I64, _I32, ctypes.c_uint32, _P, _P,
+                                          _P, _P],
     "glm5x_moe_last_routing": [_P, _P, _P, _P, _I64],
     "glm5x_moe_check": [_P],
     "glm5x_moe_get_stats": [_P, ctypes.POINTER(MoeStats)],
