@@ -387,7 +387,8 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
-def build_ep_layer(T: int, local: int, rank: int, world: int, experts: int = E):
+def build_ep_layer(T: int, local: int, rank: int, world: int, experts: int = E,
+                   fp4_dispatch: bool = False):
     """This rank's engine of the expert-parallel layer: experts
     [rank * E/W, (rank + 1) * E/W) + the shared expert, the full router.
     Expert e's weights are drawn from its own seed, so every rank holds the
@@ -400,7 +401,11 @@ def build_ep_layer(T: int, local: int, rank: int, world: int, experts: int = E):
     begin, count = expert_range(rank, world, experts)
     layer = GLM5XMoELayer(hidden_size=H, intermediate_size=I, num_experts=experts, top_k=K_TOP,
                           routed_scaling_factor=SCALE, has_shared=True,
-                          max_tokens=T * (world + 1), device=local, expert_begin=begin,
+                          # local tokens + received rows: one per (token, rank) with
+                          # BF16 dispatch, one per (token, expert) with FP4 dispatch
+                          # (room for twice the average with FP4)
+                          max_tokens=T * (2 * K_TOP + 1 if fp4_dispatch else world + 1),
+                          device=local, expert_begin=begin,
                           expert_count=count)
     for e in list(range(begin, begin + count)) + [-1]:
         g = torch.Generator(device=dev).manual_seed(7000 + e)
@@ -429,11 +434,12 @@ def run_ours_ep(args, world: int, rank: int, local: int) -> None:
     experts = args.experts or E
     stream = torch.cuda.Stream(device=dev)
     torch.cuda.set_stream(stream)
-    layer = build_ep_layer(T, local, rank, world, experts)
+    fp4 = args.dispatch == "fp4"
+    layer = build_ep_layer(T, local, rank, world, experts, fp4_dispatch=fp4)
     if args.tile_n:
         layer.set_tile_n(args.tile_n)
     ep = ExpertParallelMoE(layer, rank=rank, world=world, num_experts=experts, top_k=K_TOP,
-                           hidden_size=H)
+                           hidden_size=H, fp4_dispatch=fp4)
     hidden = make_hidden(T, seed=100 + rank, device=dev)
     for _ in range(args.warmup):
         ep(hidden)
@@ -508,7 +514,8 @@ def run_ours_ep(args, world: int, rank: int, local: int) -> None:
                                    f"experts top-8 + 1 shared, expert parallel: {experts // world}"
                                    " experts per GPU",
                        "global_batch": world * T, "tokens_per_rank": T,
-                       "parallelism": f"ep{world} (NCCL all-to-all dispatch / combine)",
+                       "parallelism": f"ep{world} (NCCL all-to-all dispatch / combine, "
+                                      f"{'NVFP4' if fp4 else 'BF16'} dispatch)",
                        "l2": "inputs larger than L2"},
             "phases_ms": phases, "ep_stages_ms": stages,
             "roofline": {"bound": "tensor", "kernel": "gate_up_gemm (rank 0)",
@@ -675,6 +682,8 @@ def main() -> None:
     ap.add_argument("--down-tiles", default="", choices=["", "tm", "128", "256"],
                     help="down projection tiles: token-major or weight-major width (tuning)")
     ap.add_argument("--experts", type=int, default=0, help="override experts (profiling only)")
+    ap.add_argument("--dispatch", default="bf16", choices=["bf16", "fp4"],
+                    help="expert-parallel token rows as BF16 or as sender-quantized NVFP4")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

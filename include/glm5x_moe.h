@@ -250,6 +250,38 @@ glm5x_status glm5x_moe_route(glm5x_moe* moe, const void* hidden_bf16, int64_t to
 glm5x_status glm5x_moe_forward_expert_rows(glm5x_moe* moe, const void* rows_bf16, int64_t rows,
                                            const int32_t* ids, const float* weights,
                                            int64_t shared_rows, float* out, void* stream);
+
+/* Expert-parallel FP4 dispatch (no counterpart in the reference, which runs
+ * every expert in one process). The slab of a routed expert is every rank's
+ * tokens routed to it, as one GPU would see the concatenated batch; its NVFP4
+ * global scale needs the slab's max |x| over all ranks. So:
+ *  1. glm5x_moe_slab_amax: amax[e] (device, num_experts floats) = max |x| of
+ *     this rank's tokens routed to e (ids [T, top_k] global ids, -1 skipped);
+ *     the caller reduces it with MAX over the ranks;
+ *  2. glm5x_moe_quantize_rows: NVFP4 codes (packed [n, H/2]) and row-major
+ *     E4M3 scales ([n, H/16]) of token row_token[r] for expert row_expert[r]
+ *     with that expert's reduced slab scale: the bits the single-GPU segment
+ *     quantizer gives the row; these rows travel instead of BF16 rows;
+ *  3. glm5x_moe_forward_quantized_rows on the rank holding the experts: the
+ *     T local tokens take the shared expert (out_local [T, H] FP32, their own
+ *     slab) and the R received rows their expert (row_expert global ids held
+ *     here, row_weight the routing weights); out_groups[g] (FP32 [groups, H])
+ *     = the sum, in listed order, of the weighted expert rows of received rows
+ *     group_rows[g, 0 .. slots) (-1 = none), e.g. one group per source token.
+ * T + R must not exceed max_tokens. NVFP4 engines only. */
+glm5x_status glm5x_moe_slab_amax(glm5x_moe* moe, const void* hidden_bf16, int64_t tokens,
+                                 const int32_t* ids, float* amax, void* stream);
+glm5x_status glm5x_moe_quantize_rows(glm5x_moe* moe, const void* hidden_bf16, int64_t tokens,
+                                     const int32_t* row_token, const int32_t* row_expert,
+                                     int64_t rows, const float* amax, void* packed,
+                                     void* scales, void* stream);
+glm5x_status glm5x_moe_forward_quantized_rows(glm5x_moe* moe, const void* hidden_bf16,
+                                              int64_t tokens, const void* packed,
+                                              const void* scales, const int32_t* row_expert,
+                                              const float* row_weight, int64_t rows,
+                                              const float* amax, float* out_local,
+                                              const int32_t* group_rows, int64_t groups,
+                                              int32_t slots, float* out_groups, void* stream);
 /* Routing of the last forward (synchronizes): ids/weights [T, top_k] in
  * descending choice order, logits [T, num_experts] (may be NULL). */
 glm5x_status glm5x_moe_last_routing(glm5x_moe* moe, int32_t* ids, float* weights,

@@ -38,7 +38,23 @@ cudaError_t launch_nvfp4_quantize_segments(const uint16_t* src, int K, const int
                                            const int32_t* qprefix, int nseg, int bn,
                                            const float* seg_amax, int64_t max_rows,
                                            uint8_t* packed, uint8_t* scales_blocked,
-                                           float* seg_global, cudaStream_t st);
+                                           float* seg_global, cudaStream_t st,
+                                           int first_seg = 0);
+// Expert-parallel FP4 dispatch: the sender's quantization of (token, expert)
+// rows with the reduced slab scale of each row's expert (row-major E4M3
+// scales), and the receiver's placement of such rows into the routed
+// segments [0, nseg_routed) (blocked scales, padded rows zeroed, each
+// segment's global scale from amax[expert_begin + s]).
+cudaError_t launch_nvfp4_quantize_rows(const uint16_t* src, int K, const int32_t* row_token,
+                                       const int32_t* row_expert, int64_t n, const float* amax,
+                                       uint8_t* packed, uint8_t* scales, cudaStream_t st);
+cudaError_t launch_place_nvfp4_rows(const uint8_t* packed_in, const uint8_t* scales_in, int K,
+                                    const int32_t* row_token, int row_base,
+                                    const int32_t* seg_start, const int32_t* seg_count,
+                                    const int32_t* qprefix, int nseg_routed, int bn,
+                                    const float* amax, int expert_begin, int64_t max_rows,
+                                    uint8_t* packed, uint8_t* scales_blocked, float* seg_global,
+                                    cudaStream_t st);
 // Four-term MXFP4 expansion of expert-major rows (4 operand rows per token);
 // records kErrNonFinite in *err for Inf / NaN inputs.
 cudaError_t launch_mxfp4_terms_segments(const uint16_t* src, int K, const int32_t* row_token,
@@ -69,6 +85,14 @@ struct PermuteBuffers {
   int32_t* row_token;     // [rows], token of each segment row
   float* row_weight;      // [rows], routing weight of each segment row
 };
+
+// Expert-parallel FP4 dispatch: per-expert slab amax from token amax and
+// global ids [T, k] (amax [E] zeroed here), and the expert-major rows of
+// received rows listed per group (see route.cu).
+cudaError_t launch_slab_amax(const float* token_amax, const int32_t* ids, int T, int k, int E,
+                             float* amax, cudaStream_t st);
+cudaError_t launch_map_group_pos(const int32_t* group_rows, int64_t n, const int32_t* pos,
+                                 int kk, int row_base, int32_t* out, cudaStream_t st);
 
 // Top-K policy of k3x::select_routing (runtime/include/k3x/routing_policy.hpp:
 // 11-19): mode 0 natural, 1 fixed (fixed_k of the ladder 4/6/8/12/16), 2

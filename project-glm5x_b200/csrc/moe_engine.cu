@@ -802,28 +802,52 @@ glm5x_status glm5x_moe_load_sidecar(glm5x_moe* m, int32_t expert, const char* pa
 // ep_rows: the rows are tokens dispatched to this engine by expert-parallel
 // ranks; ids_in holds global expert ids, slots of experts held elsewhere are
 // skipped, and only rows < shared_rows take the shared expert.
+// Rows quantized by their senders (expert-parallel FP4 dispatch): R rows of
+// one held expert each, placed after the T local tokens (which take only the
+// shared expert); outputs the local tokens' shared-expert rows and, per
+// group of received rows (one source token), the sum of their weighted
+// expert rows.
+struct PrequantRows {
+  const uint8_t* packed;      // [R, H/2] E2M1 codes
+  const uint8_t* scales;      // [R, H/16] E4M3, row-major
+  const int32_t* row_expert;  // [R] global expert ids (held by this engine)
+  const float* row_weight;    // [R]
+  int64_t R;
+  const float* amax;          // [num_experts] slab amax reduced over all ranks
+  const int32_t* group_rows;  // [groups, slots] received row indices, -1 = none
+  int64_t groups;
+  int slots;
+  float* out_groups;          // [groups, H]
+};
+
 static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
                                 const int32_t* ids_in, const float* w_in, float* out,
-                                cudaStream_t st, bool ep_rows = false, int64_t shared_rows = -1) {
+                                cudaStream_t st, bool ep_rows = false, int64_t shared_rows = -1,
+                                const PrequantRows* pq = nullptr) {
+  if (pq && (pq->R < 0 || T64 + pq->R > m->cfg.max_tokens || m->mx()))
+    return m->fail(GLM5X_INVALID_EXTENT, "local tokens + received rows exceed max_tokens (or MXFP4)");
   if (T64 <= 0 || T64 > m->cfg.max_tokens)
     return m->fail(GLM5X_INVALID_EXTENT, "tokens %lld outside [1, %d]", (long long)T64,
                    m->cfg.max_tokens);
   if (!ep_rows && m->E_loc != m->cfg.num_experts)
     return m->fail(GLM5X_INVALID_STATE,
                    "expert-parallel engines run glm5x_moe_forward_expert_rows");
-  if (ep_rows && !ids_in) return m->fail(GLM5X_INVALID_STATE, "expert rows need ids");
+  if (ep_rows && !ids_in && !pq) return m->fail(GLM5X_INVALID_STATE, "expert rows need ids");
   for (int s = 0; s < m->nseg; ++s)
     if (!m->loaded[s]) return m->fail(GLM5X_INVALID_STATE, "expert slot %d not loaded", s);
-  if (!ids_in && !m->router_set) return m->fail(GLM5X_INVALID_STATE, "router not set");
+  if (!ids_in && !pq && !m->router_set) return m->fail(GLM5X_INVALID_STATE, "router not set");
   const int T = static_cast<int>(T64);
-  const int H = m->H(), I = m->I(), E = m->cfg.num_experts, k = m->K();
+  const int H = m->H(), I = m->I(), E = m->cfg.num_experts;
+  // with sender-quantized rows: T + R one-slot rows (local tokens' slot empty)
+  const int k = pq ? 1 : m->K();
+  const int N = pq ? T + static_cast<int>(pq->R) : T;
   const int E_perm = ep_rows ? m->E_loc : E;  // segments the permutation builds
   const int hs = m->cfg.has_shared ? 1 : 0;
-  int bn = pick_bn(m, T);
+  int bn = pick_bn(m, N);
   // tiles narrower than 128 rows each take a 128-row block: make sure the
   // worst case still fits the workspace, else use 128-row tiles
   const bool mx = m->mx();
-  if (bn < 128 && (int64_t)(128 / bn) * T * m->kk() * m->terms() + (int64_t)m->nseg * 128 >
+  if (bn < 128 && (int64_t)(128 / bn) * N * m->kk() * m->terms() + (int64_t)m->nseg * 128 >
                       m->rows_cap) {
     if (m->force_bn) return m->fail(GLM5X_INVALID_EXTENT, "token tile %d too narrow for %d tokens", bn, T);
     bn = 128;
@@ -840,11 +864,13 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
     // term kernel checks for non-finite inputs itself)
     G5_CHECK(m, launch_row_amax_bf16(x, T, H, m->token_amax, m->err, st), "row amax");
     ++launches;
+    if (pq && pq->R > 0)  // received rows carry no amax here: their slabs' scales are given
+      G5_CHECK(m, cudaMemsetAsync(m->token_amax + T, 0, sizeof(float) * pq->R, st), "row amax");
   }
   mark(1);
   const int32_t* ids = ids_in;
   const float* wts = w_in;
-  if (!ids_in) {
+  if (!ids_in && !pq) {
     if (reinterpret_cast<uintptr_t>(x) % 16)
       return m->fail(GLM5X_INVALID_EXTENT, "hidden must be 16-byte aligned");
     CUtensorMap tm_x;
@@ -864,7 +890,21 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
   }
   mark(2);
   mark(3);
-  if (ep_rows) {
+  if (pq) {
+    // rows [0, T): local tokens, no routed slot; rows [T, N): one held expert
+    G5_CHECK(m, cudaMemsetAsync(m->ids_local, 0xFF, sizeof(int32_t) * T, st), "local ids");
+    G5_CHECK(m, launch_map_local_ids(pq->row_expert, pq->R, m->cfg.expert_begin, m->E_loc,
+                                     m->ids_local + T, st),
+             "local ids");
+    G5_CHECK(m, cudaMemsetAsync(m->topk_w, 0, sizeof(float) * T, st), "row weights");
+    if (pq->R > 0)
+      G5_CHECK(m, cudaMemcpyAsync(m->topk_w + T, pq->row_weight, sizeof(float) * pq->R,
+                                  cudaMemcpyDeviceToDevice, st),
+               "row weights");
+    ids = m->ids_local;
+    wts = m->topk_w;
+    ++launches;
+  } else if (ep_rows) {
     G5_CHECK(m, launch_map_local_ids(ids_in, (int64_t)T * k, m->cfg.expert_begin, m->E_loc,
                                      m->ids_local, st),
              "local ids");
@@ -872,13 +912,13 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
     ++launches;
   }
   int pl = 0;
-  G5_CHECK(m, launch_permute(ids, wts, m->token_amax, T, k, E_perm, hs, bn, m->pb, m->err, st,
+  G5_CHECK(m, launch_permute(ids, wts, m->token_amax, N, k, E_perm, hs, bn, m->pb, m->err, st,
                              m->terms(), ep_rows ? 1 : 2,
-                             shared_rows < 0 ? -1 : (int)std::min<int64_t>(shared_rows, T),
+                             pq ? T : (shared_rows < 0 ? -1 : (int)std::min<int64_t>(shared_rows, T)),
                              &pl),
            "permute");
   launches += pl;
-  const int64_t max_rows = (int64_t)T * m->kk() + (int64_t)m->nseg * 8;
+  const int64_t max_rows = (int64_t)N * m->kk() + (int64_t)m->nseg * 8;
   mark(4);
   if (mx) {
     // MXFP4 experts take full-precision activations in the reference; the
@@ -887,6 +927,20 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
                                             m->pb.seg_count, m->pb.qprefix, m->nseg, bn, max_rows,
                                             m->act_packed, m->act_sf, m->err, st),
              "activation terms");
+  } else if (pq) {
+    // the shared expert's slab from the local tokens, the routed slabs from
+    // the senders' rows
+    G5_CHECK(m, launch_nvfp4_quantize_segments(x, H, m->pb.row_token, m->pb.seg_start,
+                                               m->pb.seg_count, m->pb.qprefix, m->nseg, bn,
+                                               m->pb.seg_amax, max_rows, m->act_packed,
+                                               m->act_sf, m->act_global, st, m->E_loc),
+             "activation quantize");
+    G5_CHECK(m, launch_place_nvfp4_rows(pq->packed, pq->scales, H, m->pb.row_token, T,
+                                        m->pb.seg_start, m->pb.seg_count, m->pb.qprefix,
+                                        m->E_loc, bn, pq->amax, m->cfg.expert_begin, max_rows,
+                                        m->act_packed, m->act_sf, m->act_global, st),
+             "received rows");
+    ++launches;
   } else {
     G5_CHECK(m, launch_nvfp4_quantize_segments(x, H, m->pb.row_token, m->pb.seg_start,
                                                m->pb.seg_count, m->pb.qprefix, m->nseg, bn,
@@ -971,7 +1025,20 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
              "down GEMM");
   }
   mark(8);
-  G5_CHECK(m, launch_combine(m->y_bf16, m->pb.pos, T, m->kk(), H, out, st), "combine");
+  if (pq) {
+    // local tokens: their shared-expert rows; received rows: per group
+    G5_CHECK(m, launch_combine(m->y_bf16, m->pb.pos, T, 1 + hs, H, out, st), "combine");
+    const int64_t n = pq->groups * pq->slots;
+    G5_CHECK(m, launch_map_group_pos(pq->group_rows, n, m->pb.pos, 1 + hs, T, m->ids_local, st),
+             "group rows");
+    if (pq->groups > 0)
+      G5_CHECK(m, launch_combine(m->y_bf16, m->ids_local, (int)pq->groups, pq->slots, H,
+                                 pq->out_groups, st),
+               "group combine");
+    launches += 2;
+  } else {
+    G5_CHECK(m, launch_combine(m->y_bf16, m->pb.pos, T, m->kk(), H, out, st), "combine");
+  }
   mark(9);
   if (m->profiling) {
     m->prof_pending[pslot] = true;
@@ -982,7 +1049,7 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
   m->stats.kernel_launches += launches;
   m->last_T = T;
   m->last_bn = bn;
-  m->routed_last = ids_in == nullptr;
+  m->routed_last = ids_in == nullptr && !pq;
   return GLM5X_OK;
 }
 
@@ -1017,6 +1084,64 @@ glm5x_status glm5x_moe_forward_expert_rows(glm5x_moe* m, const void* rows, int64
   cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : m->stream;
   return run_forward(m, static_cast<const uint16_t*>(rows), R, ids, weights, out, st, true,
                      shared_rows);
+}
+
+glm5x_status glm5x_moe_slab_amax(glm5x_moe* m, const void* hidden, int64_t T, const int32_t* ids,
+                                 float* amax, void* stream) {
+  if (!m || !hidden || !ids || !amax) return fail_global(GLM5X_INVALID_STATE, "null argument");
+  if (m->mx()) return m->fail(GLM5X_INVALID_STATE, "slab amax: NVFP4 engines only");
+  if (reinterpret_cast<uintptr_t>(hidden) % 16)
+    return m->fail(GLM5X_INVALID_EXTENT, "hidden must be 16-byte aligned");
+  if (T <= 0 || T > m->cfg.max_tokens)
+    return m->fail(GLM5X_INVALID_EXTENT, "tokens %lld outside [1, %d]", (long long)T,
+                   m->cfg.max_tokens);
+  cudaSetDevice(m->device);
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : m->stream;
+  G5_CHECK(m, launch_row_amax_bf16(static_cast<const uint16_t*>(hidden), T, m->H(), m->token_amax,
+                                   m->err, st),
+           "row amax");
+  G5_CHECK(m, launch_slab_amax(m->token_amax, ids, (int)T, m->K(), m->cfg.num_experts, amax, st),
+           "slab amax");
+  m->stats.kernel_launches += 2;
+  return GLM5X_OK;
+}
+
+glm5x_status glm5x_moe_quantize_rows(glm5x_moe* m, const void* hidden, int64_t T,
+                                     const int32_t* row_token, const int32_t* row_expert,
+                                     int64_t n, const float* amax, void* packed, void* scales,
+                                     void* stream) {
+  if (!m || !hidden || !amax || (n > 0 && (!row_token || !row_expert || !packed || !scales)))
+    return fail_global(GLM5X_INVALID_STATE, "null argument");
+  if (m->mx()) return m->fail(GLM5X_INVALID_STATE, "row quantization: NVFP4 engines only");
+  if (T <= 0 || n < 0 || reinterpret_cast<uintptr_t>(hidden) % 16)
+    return m->fail(GLM5X_INVALID_EXTENT, "bad row quantization extents");
+  cudaSetDevice(m->device);
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : m->stream;
+  G5_CHECK(m, launch_nvfp4_quantize_rows(static_cast<const uint16_t*>(hidden), m->H(), row_token,
+                                         row_expert, n, amax, static_cast<uint8_t*>(packed),
+                                         static_cast<uint8_t*>(scales), st),
+           "row quantize");
+  m->stats.kernel_launches += n > 0 ? 1 : 0;
+  return GLM5X_OK;
+}
+
+glm5x_status glm5x_moe_forward_quantized_rows(
+    glm5x_moe* m, const void* hidden, int64_t T, const void* packed, const void* scales,
+    const int32_t* row_expert, const float* row_weight, int64_t R, const float* amax,
+    float* out_local, const int32_t* group_rows, int64_t groups, int32_t slots,
+    float* out_groups, void* stream) {
+  if (!m || !hidden || !amax || !out_local ||
+      (R > 0 && (!packed || !scales || !row_expert || !row_weight)) ||
+      (groups > 0 && (!group_rows || !out_groups)))
+    return fail_global(GLM5X_INVALID_STATE, "null argument");
+  if (R < 0 || groups < 0 || groups > R || slots <= 0 || slots > 32)
+    return m->fail(GLM5X_INVALID_EXTENT, "bad received-row extents");
+  cudaSetDevice(m->device);
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : m->stream;
+  PrequantRows pq{static_cast<const uint8_t*>(packed), static_cast<const uint8_t*>(scales),
+                  row_expert, row_weight, R, amax, group_rows, groups, slots, out_groups};
+  return run_forward(m, static_cast<const uint16_t*>(hidden), T, nullptr, nullptr, out_local, st,
+                     true, T, &pq);
 }
 
 glm5x_status glm5x_moe_route(glm5x_moe* m, const void* hidden, int64_t T, int32_t* ids,

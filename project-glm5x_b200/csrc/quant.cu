@@ -313,11 +313,11 @@ __global__ void nvfp4_quantize_segments_kernel(
     const int32_t* __restrict__ seg_start, const int32_t* __restrict__ seg_count,
     const int32_t* __restrict__ qprefix, int nseg, int bn, const float* __restrict__ seg_amax,
     uint8_t* __restrict__ packed, uint8_t* __restrict__ scales_blocked,
-    float* __restrict__ seg_global) {
+    float* __restrict__ seg_global, int first_seg) {
   const int warps = blockDim.x / 32;
   const int64_t f = blockIdx.x * (int64_t)warps + threadIdx.x / 32;
   const int total = qprefix[nseg];
-  if (f >= total) return;
+  if (f >= total || f < qprefix[first_seg]) return;  // segments before first_seg are filled elsewhere
   // upper_bound over qprefix[0..nseg]
   int lo = 0, hi = nseg;
   while (hi - lo > 1) {
@@ -372,6 +372,108 @@ __global__ void nvfp4_quantize_segments_kernel(
       *reinterpret_cast<uint2*>(prow) = make_uint2(lo32, hi32);
     *psf = static_cast<uint8_t>(sb);
   }
+}
+
+// ------------------------------------------------------------------ NVFP4 rows for dispatch
+// Expert-parallel FP4 dispatch. The sender quantizes each (token, expert)
+// row it sends with the expert's slab global scale, taken from the slab
+// amax reduced over all ranks, so every row's codes and block scales are the
+// ones the single-GPU segment quantizer gives the same row in that expert's
+// slab. Rows: row r is token row_token[r] of src for expert row_expert[r];
+// packed [n, K/2], scales [n, K/16] row-major E4M3. One warp per row.
+__global__ void nvfp4_quantize_rows_kernel(const uint16_t* __restrict__ src, int K,
+                                           const int32_t* __restrict__ row_token,
+                                           const int32_t* __restrict__ row_expert, int64_t n,
+                                           const float* __restrict__ amax,
+                                           uint8_t* __restrict__ packed,
+                                           uint8_t* __restrict__ scales) {
+  const int64_t r = blockIdx.x * (int64_t)(blockDim.x / 32) + threadIdx.x / 32;
+  if (r >= n) return;
+  const int lane = lane_id();
+  const int nb = K / 16;
+  const float g = nvfp4_global_scale(amax[row_expert[r]]);
+  const float six_g = f_mul(kFp4Max, g);
+  const float rcp_six_g = rcp_approx(six_g);
+  const uint16_t* xrow = src + (int64_t)row_token[r] * K;
+  for (int b = lane; b < nb; b += 32) {
+    const uint16_t* xb = xrow + b * 16;
+    const uint4* q = reinterpret_cast<const uint4*>(xb);
+    const uint4 v0 = __ldg(q), v1 = __ldg(q + 1);
+    const uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    uint32_t lo32, hi32;
+    const uint32_t sb = quantize_block16_bf16(w, xb, g, six_g, rcp_six_g, lo32, hi32);
+    *reinterpret_cast<uint2*>(packed + r * (K / 2) + b * 8) = make_uint2(lo32, hi32);
+    scales[r * nb + b] = static_cast<uint8_t>(sb);
+  }
+}
+
+// The receiver's side: rows quantized by their senders go into the routed
+// segments [0, nseg_routed) of the expert-major layout (codes copied, scales
+// into the blocked layout, rows past a segment's count zero-filled as the
+// segment quantizer does); segment s's global scale comes from the reduced
+// slab amax of global expert expert_begin + s. row_token[row] - row_base is
+// the received row index.
+__global__ void place_nvfp4_rows_kernel(const uint8_t* __restrict__ packed_in,
+                                        const uint8_t* __restrict__ scales_in, int K,
+                                        const int32_t* __restrict__ row_token, int row_base,
+                                        const int32_t* __restrict__ seg_start,
+                                        const int32_t* __restrict__ seg_count,
+                                        const int32_t* __restrict__ qprefix, int nseg_routed,
+                                        int bn, const float* __restrict__ amax, int expert_begin,
+                                        uint8_t* __restrict__ packed,
+                                        uint8_t* __restrict__ scales_blocked,
+                                        float* __restrict__ seg_global) {
+  const int64_t f = blockIdx.x * (int64_t)(blockDim.x / 32) + threadIdx.x / 32;
+  if (f >= qprefix[nseg_routed]) return;
+  int lo = 0, hi = nseg_routed;
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (qprefix[mid] <= f) lo = mid; else hi = mid;
+  }
+  const int s = lo;
+  const int r = static_cast<int>(f - qprefix[s]);
+  const int64_t row = seg_start[s] + segment_row(r, bn);
+  const int lane = lane_id();
+  if (r == 0 && lane == 0) seg_global[s] = nvfp4_global_scale(amax[expert_begin + s]);
+  const int nb = K / 16;
+  uint4* prow = reinterpret_cast<uint4*>(packed + row * (K / 2));
+  if (r >= seg_count[s]) {
+    for (int v = lane; v < K / 32; v += 32) prow[v] = make_uint4(0, 0, 0, 0);
+    for (int b = lane; b < nb; b += 32) scales_blocked[blocked_sf_offset(row, b, nb)] = 0;
+    return;
+  }
+  const int64_t i = row_token[row] - row_base;
+  const uint4* src = reinterpret_cast<const uint4*>(packed_in + i * (K / 2));
+  for (int v = lane; v < K / 32; v += 32) prow[v] = __ldg(src + v);
+  for (int b = lane; b < nb; b += 32)
+    scales_blocked[blocked_sf_offset(row, b, nb)] = scales_in[i * nb + b];
+}
+
+cudaError_t launch_nvfp4_quantize_rows(const uint16_t* src, int K, const int32_t* row_token,
+                                       const int32_t* row_expert, int64_t n, const float* amax,
+                                       uint8_t* packed, uint8_t* scales, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  if (K % 512 || (reinterpret_cast<uintptr_t>(src) & 15)) return cudaErrorInvalidValue;
+  const int warps = 8;
+  nvfp4_quantize_rows_kernel<<<(unsigned)((n + warps - 1) / warps), warps * 32, 0, st>>>(
+      src, K, row_token, row_expert, n, amax, packed, scales);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_place_nvfp4_rows(const uint8_t* packed_in, const uint8_t* scales_in, int K,
+                                    const int32_t* row_token, int row_base,
+                                    const int32_t* seg_start, const int32_t* seg_count,
+                                    const int32_t* qprefix, int nseg_routed, int bn,
+                                    const float* amax, int expert_begin, int64_t max_rows,
+                                    uint8_t* packed, uint8_t* scales_blocked, float* seg_global,
+                                    cudaStream_t st) {
+  if (max_rows <= 0) return cudaSuccess;
+  if (K % 512) return cudaErrorInvalidValue;
+  const int warps = 8;
+  place_nvfp4_rows_kernel<<<(unsigned)((max_rows + warps - 1) / warps), warps * 32, 0, st>>>(
+      packed_in, scales_in, K, row_token, row_base, seg_start, seg_count, qprefix, nseg_routed,
+      bn, amax, expert_begin, packed, scales_blocked, seg_global);
+  return cudaGetLastError();
 }
 
 // ------------------------------------------------------------------ MXFP4 terms
@@ -611,7 +713,7 @@ cudaError_t launch_nvfp4_quantize_segments(const uint16_t* src, int K, const int
                                            const int32_t* qprefix, int nseg, int bn,
                                            const float* seg_amax, int64_t max_rows,
                                            uint8_t* packed, uint8_t* scales_blocked,
-                                           float* seg_global, cudaStream_t st) {
+                                           float* seg_global, cudaStream_t st, int first_seg) {
   if (max_rows <= 0) return cudaSuccess;
   if (K % 512) return cudaErrorInvalidValue;
   const int warps = 8;
@@ -622,7 +724,7 @@ cudaError_t launch_nvfp4_quantize_segments(const uint16_t* src, int K, const int
                           : (wide ? nvfp4_quantize_segments_kernel<false, true>
                                   : nvfp4_quantize_segments_kernel<false, false>);
   kernel<<<grid, block, 0, st>>>(src, K, row_token, seg_start, seg_count, qprefix, nseg, bn,
-                                 seg_amax, packed, scales_blocked, seg_global);
+                                 seg_amax, packed, scales_blocked, seg_global, first_seg);
   return cudaGetLastError();
 }
 

@@ -468,6 +468,47 @@ __global__ void permute_small_kernel(const int32_t* __restrict__ ids,
   }
 }
 
+// Expert-parallel FP4 dispatch helpers. slab amax: amax[e] = max over the
+// (token, slot) pairs routed to e of the token's max |x| (the slab amax the
+// permutation scatter accumulates per segment), amax zeroed by the caller.
+// group positions: out[i] = the expert-major row of received row
+// group_rows[i] (its only routed slot, slot 0 of row row_base + g), -1 kept.
+__global__ void slab_amax_kernel(const float* __restrict__ token_amax,
+                                 const int32_t* __restrict__ ids, int64_t n, int k, int E,
+                                 float* __restrict__ amax) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int e = ids[i];
+  if (e >= 0 && e < E)
+    atomicMax(reinterpret_cast<unsigned int*>(amax + e), __float_as_uint(token_amax[i / k]));
+}
+
+__global__ void map_group_pos_kernel(const int32_t* __restrict__ group_rows, int64_t n,
+                                     const int32_t* __restrict__ pos, int kk, int row_base,
+                                     int32_t* __restrict__ out) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int g = group_rows[i];
+  out[i] = g < 0 ? -1 : pos[(int64_t)(row_base + g) * kk];
+}
+
+cudaError_t launch_slab_amax(const float* token_amax, const int32_t* ids, int T, int k, int E,
+                             float* amax, cudaStream_t st) {
+  cudaError_t e = cudaMemsetAsync(amax, 0, sizeof(float) * E, st);
+  if (e != cudaSuccess || T <= 0) return e;
+  const int64_t n = (int64_t)T * k;
+  slab_amax_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(token_amax, ids, n, k, E, amax);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_map_group_pos(const int32_t* group_rows, int64_t n, const int32_t* pos,
+                                 int kk, int row_base, int32_t* out, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  map_group_pos_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(group_rows, n, pos, kk,
+                                                                    row_base, out);
+  return cudaGetLastError();
+}
+
 // ------------------------------------------------------------------ launchers
 cudaError_t launch_topk(const float* in, int values_are_scores, const float* bias, int T, int E,
                         int k, float routed_scale, int32_t* ids, float* weights, uint32_t* err,

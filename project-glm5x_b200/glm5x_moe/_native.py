@@ -133,6 +133,10 @@ SIGNATURES = {
     "glm5x_moe_forward_host": [_P, _P, _I64, _P],
     "glm5x_moe_forward_routed": [_P, _P, _I64, _P, _P, _P, _P],
     "glm5x_moe_forward_expert_rows": [_P, _P, _I64, _P, _P, _I64, _P, _P],
+    "glm5x_moe_slab_amax": [_P, _P, _I64, _P, _P, _P],
+    "glm5x_moe_quantize_rows": [_P, _P, _I64, _P, _P, _I64, _P, _P, _P, _P],
+    "glm5x_moe_forward_quantized_rows": [_P, _P, _I64, _P, _P, _P, _P, _I64, _P, _P, _P, _I64,
+                                         _I32, _P, _P],
     "glm5x_moe_route": [_P, _P, _I64, _P, _P, _P, _P],
     "glm5x_combine_rows": [_P, _P, _I64, _I32, _I64, _P, _I32, _P],
     "glm5x_verify_greedy_target_blocks": [_P, _P, _P, _P, _I64, _I32, ctypes.c_uint32, _P, _P,

@@ -19,9 +19,20 @@ expert and the full router. A forward on rank r:
    (all-to-all-v of BF16 rows), where the partial sums of a token are added
    in FP32, in destination-rank order, onto its shared-expert output.
 
+With fp4_dispatch, step 2 sends NVFP4 rows instead: every rank computes the
+per-expert max |x| of its tokens (slab_amax) and the ranks reduce it with MAX,
+which gives each routed expert's slab scale exactly as one GPU computes it
+for the concatenated batch; every (token, expert) pair then travels as that
+expert's NVFP4 row (H/2 code bytes + H/16 scale bytes + 12 bytes of expert
+id, weight and token instead of 2H bytes per (token, rank)), the receiver
+runs its experts on the rows as they are (forward_quantized_rows) and sums
+each source token's rows before the return. The result is bit-identical to
+the BF16 dispatch.
+
 Everything runs on the caller's current stream; torch.distributed (NCCL on
 GPUs) moves the bytes. The engine is any object with route(hidden) ->
-(ids, weights) and forward_expert_rows(rows, ids, weights, shared_rows).
+(ids, weights) and forward_expert_rows(rows, ids, weights, shared_rows), plus
+slab_amax, quantize_rows and forward_quantized_rows for fp4_dispatch.
 """
 from __future__ import annotations
 
@@ -33,7 +44,7 @@ class ExpertParallelMoE:
     """Dispatch / expert / combine around one rank's engine."""
 
     def __init__(self, engine, *, rank: int, world: int, num_experts: int, top_k: int,
-                 hidden_size: int, group=None) -> None:
+                 hidden_size: int, group=None, fp4_dispatch: bool = False) -> None:
         if num_experts % world:
             raise ValueError("GLM5X_EP_EXPERTS_NOT_DIVISIBLE")
         self.engine = engine
@@ -43,6 +54,7 @@ class ExpertParallelMoE:
         self.top_k = top_k
         self.hidden_size = hidden_size
         self.group = group
+        self.fp4_dispatch = fp4_dispatch
         self.last_counts: tuple[list[int], list[int]] | None = None
         self.last_local_assignments = 0
         self._timing = False
@@ -96,6 +108,9 @@ class ExpertParallelMoE:
         self._mark(evs)
         ids, w = self.engine.route(x)
         self._mark(evs)
+        if self.fp4_dispatch:
+            out = self._forward_fp4(x, ids, w, evs)
+            return out.reshape(*hidden.shape[:-1], H)
         d_idx, t_idx, send_counts = self.plan(ids)
         # per pair: k masked ids and k weights (as raw 32-bit words) in one row
         sel = ids[t_idx]
@@ -136,6 +151,67 @@ class ExpertParallelMoE:
         if evs is not None:
             self._pending.append(evs)
         return out.reshape(*hidden.shape[:-1], H)
+
+    def _forward_fp4(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, evs):
+        T, H, k, W = x.shape[0], self.hidden_size, self.top_k, self.world
+        dev = x.device
+        amax = self.engine.slab_amax(x, ids)
+        dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=self.group)
+        # (token, slot) pairs with an expert, by destination rank, then token, then slot
+        flat_ids = ids.reshape(-1).long()
+        valid = flat_ids >= 0
+        dest = torch.where(valid, flat_ids // self.per, torch.full_like(flat_ids, W))
+        n_flat = flat_ids.numel()
+        order = torch.argsort(dest * n_flat + torch.arange(n_flat, device=dev))
+        order = order[: int(valid.sum().item())]
+        pair_tok = (order // k).to(torch.int32)
+        pair_exp = flat_ids[order].to(torch.int32)
+        pair_w = w.reshape(-1)[order].float()
+        send_counts = torch.bincount(dest[order], minlength=W)
+        packed, scales = self.engine.quantize_rows(x, pair_tok, pair_exp, amax)
+        meta = torch.stack([pair_exp, pair_w.view(torch.int32), pair_tok], dim=1).contiguous()
+        recv_counts = torch.empty_like(send_counts)
+        dist.all_to_all_single(recv_counts, send_counts.contiguous(), group=self.group)
+        sc, rc = send_counts.tolist(), recv_counts.tolist()
+        R = sum(rc)
+        rpacked = torch.empty((R, H // 2), dtype=torch.uint8, device=dev)
+        rscales = torch.empty((R, H // 16), dtype=torch.uint8, device=dev)
+        rmeta = torch.empty((R, 3), dtype=torch.int32, device=dev)
+        dist.all_to_all_single(rpacked, packed, rc, sc, group=self.group)
+        dist.all_to_all_single(rscales, scales, rc, sc, group=self.group)
+        dist.all_to_all_single(rmeta, meta, rc, sc, group=self.group)
+        # groups: consecutive received rows of one source token (source rank order)
+        src = torch.repeat_interleave(torch.arange(W, device=dev),
+                                      torch.tensor(rc, device=dev))
+        tok = rmeta[:, 2]
+        new = torch.ones(R, dtype=torch.bool, device=dev)
+        if R > 1:
+            new[1:] = (src[1:] != src[:-1]) | (tok[1:] != tok[:-1])
+        gid = torch.cumsum(new.long(), 0) - 1
+        first = torch.nonzero(new).reshape(-1)
+        G = first.numel()
+        group_rows = torch.full((G, k), -1, dtype=torch.int32, device=dev)
+        if R:
+            slot = torch.arange(R, device=dev) - first[gid]
+            group_rows[gid, slot] = torch.arange(R, dtype=torch.int32, device=dev)
+        gcount = torch.bincount(src[first], minlength=W).tolist() if R else [0] * W
+        self.last_counts = (sc, rc)
+        self._mark(evs)
+        out, out_groups = self.engine.forward_quantized_rows(
+            x, rpacked, rscales, rmeta[:, 0], rmeta[:, 1].view(torch.float32), amax, group_rows)
+        self._mark(evs)
+        # one partial sum per (token, destination) returns, as in the BF16 dispatch
+        d_idx, t_idx, tok_counts = self.plan(ids)
+        back = torch.empty((t_idx.numel(), H), dtype=torch.bfloat16, device=dev)
+        dist.all_to_all_single(back, out_groups.to(torch.bfloat16), tok_counts.tolist(), gcount,
+                               group=self.group)
+        pos = torch.full((T, W), -1, dtype=torch.int32, device=dev)
+        pos[t_idx, d_idx] = torch.arange(t_idx.numel(), dtype=torch.int32, device=dev)
+        self.combine(back, pos, out)
+        self._mark(evs)
+        if evs is not None:
+            self._pending.append(evs)
+        return out
 
     @staticmethod
     def combine(rows: torch.Tensor, pos: torch.Tensor, out: torch.Tensor) -> None:

@@ -234,6 +234,63 @@ class GLM5XMoELayer:
         """256-row token tiles on CTA pairs (default) or single CTAs."""
         N.check(N.lib().glm5x_moe_set_pair_mma(self._h, 1 if enable else 0), self._h)
 
+    # ---------------------------------------------- expert-parallel FP4 dispatch
+    def slab_amax(self, hidden: torch.Tensor, ids: torch.Tensor) -> torch.Tensor:
+        """Per-expert max |x| of this rank's tokens routed to each expert
+        (FP32 [num_experts], device); reduce it with MAX over the ranks."""
+        flat = hidden.reshape(-1, self.hidden_size).to(torch.bfloat16).contiguous()
+        ids = ids.to(device=self.device, dtype=torch.int32).contiguous()
+        amax = torch.empty(self.num_experts, dtype=torch.float32, device=self.device)
+        with torch.cuda.device(self.device):
+            N.check(N.lib().glm5x_moe_slab_amax(self._h, flat.data_ptr(), flat.shape[0],
+                                                ids.data_ptr(), amax.data_ptr(), _stream()),
+                    self._h)
+        return amax
+
+    def quantize_rows(self, hidden: torch.Tensor, row_token: torch.Tensor,
+                      row_expert: torch.Tensor, amax: torch.Tensor):
+        """NVFP4 rows to send: token row_token[r] quantized for expert
+        row_expert[r] with that expert's reduced slab scale. Returns
+        (packed uint8 [n, H/2], scales uint8 [n, H/16] row-major E4M3)."""
+        flat = hidden.reshape(-1, self.hidden_size).to(torch.bfloat16).contiguous()
+        tok = row_token.to(device=self.device, dtype=torch.int32).contiguous()
+        exp = row_expert.to(device=self.device, dtype=torch.int32).contiguous()
+        n = tok.numel()
+        H = self.hidden_size
+        packed = torch.empty((n, H // 2), dtype=torch.uint8, device=self.device)
+        scales = torch.empty((n, H // 16), dtype=torch.uint8, device=self.device)
+        with torch.cuda.device(self.device):
+            N.check(N.lib().glm5x_moe_quantize_rows(
+                self._h, flat.data_ptr(), flat.shape[0], tok.data_ptr(), exp.data_ptr(), n,
+                amax.data_ptr(), packed.data_ptr(), scales.data_ptr(), _stream()), self._h)
+        return packed, scales
+
+    def forward_quantized_rows(self, hidden: torch.Tensor, packed: torch.Tensor,
+                               scales: torch.Tensor, row_expert: torch.Tensor,
+                               row_weight: torch.Tensor, amax: torch.Tensor,
+                               group_rows: torch.Tensor):
+        """The local tokens through the shared expert and the received NVFP4
+        rows through their held experts. Returns (out_local FP32 [T, H],
+        out_groups FP32 [G, H]) with out_groups[g] = the sum of the weighted
+        expert rows of received rows group_rows[g, :] (-1 = none)."""
+        flat = hidden.reshape(-1, self.hidden_size).to(torch.bfloat16).contiguous()
+        T, H = flat.shape[0], self.hidden_size
+        exp = row_expert.to(device=self.device, dtype=torch.int32).contiguous()
+        wts = row_weight.to(device=self.device, dtype=torch.float32).contiguous()
+        grp = group_rows.to(device=self.device, dtype=torch.int32).contiguous()
+        R = exp.numel()
+        G, slots = grp.shape
+        out_local = torch.empty((T, H), dtype=torch.float32, device=self.device)
+        out_groups = torch.empty((G, H), dtype=torch.float32, device=self.device)
+        with torch.cuda.device(self.device):
+            N.check(N.lib().glm5x_moe_forward_quantized_rows(
+                self._h, flat.data_ptr(), T, packed.data_ptr() if R else None,
+                scales.data_ptr() if R else None, exp.data_ptr() if R else None,
+                wts.data_ptr() if R else None, R, amax.data_ptr(), out_local.data_ptr(),
+                grp.data_ptr() if G else None, G, max(slots, 1),
+                out_groups.data_ptr() if G else None, _stream()), self._h)
+        return out_local, out_groups
+
     def set_routing_policy(self, config, collect_diagnostics: bool = False) -> None:
         """select_routing policy of the router (a routing.RoutingPolicyConfig:
         natural, fixed or adaptive Top-K with a quality floor). Fixed and

@@ -7,7 +7,10 @@ out[t] = shared(x_t) + sum_s w[t,s] * expert_{ids[t,s]}(x_t) up to the BF16
 rounding of the per-destination partial sums on their way back (2^-9
 relative each) and FP32 summation order. Covers worlds 2 and 4, ranks that receive no rows, tokens whose
 experts all live on one rank, uneven token counts per rank, and routes
-with empty slots (id -1, as a fixed-K routing policy leaves them).
+with empty slots (id -1, as a fixed-K routing policy leaves them), and the
+FP4 dispatch (rows quantized by their senders against the slab scales reduced
+over the ranks; here with a 4-bit stand-in code and the single-process
+result built with the concatenated batch's slab scales).
 """
 from __future__ import annotations
 
@@ -54,6 +57,53 @@ class FakeEngine:
                 out[r] += xf[r] @ self.shared
         return out
 
+    # FP4 dispatch stand-ins: a 4-bit code per value (two per byte) against
+    # the expert's slab amax, so the rows' bytes and sizes travel as NVFP4
+    # rows do and the result depends on the reduced slab scale
+    def slab_amax(self, x, ids):
+        amax = torch.zeros(E)
+        xa = x.float().abs().amax(dim=1)
+        for t in range(x.shape[0]):
+            for s in range(K):
+                e = int(ids[t, s])
+                if e >= 0:
+                    amax[e] = max(float(amax[e]), float(xa[t]))
+        return amax
+
+    @staticmethod
+    def fake_codes(v, amax):
+        return torch.clamp(torch.round(v / max(amax, 1e-30) * 7.0), -7, 7)
+
+    def quantize_rows(self, x, row_token, row_expert, amax):
+        n = row_token.numel()
+        packed = torch.zeros((n, H // 2), dtype=torch.uint8)
+        for r in range(n):
+            q = (self.fake_codes(x[int(row_token[r])].float(), float(amax[int(row_expert[r])]))
+                 + 8).to(torch.uint8)
+            packed[r] = q[0::2] | (q[1::2] << 4)
+        return packed, torch.zeros((n, H // 16), dtype=torch.uint8)
+
+    @staticmethod
+    def fake_decode(packed_row, amax):
+        lo, hi = (packed_row & 15).float() - 8, (packed_row >> 4).float() - 8
+        v = torch.stack([lo, hi], dim=1).reshape(-1)
+        return v * max(amax, 1e-30) / 7.0
+
+    def forward_quantized_rows(self, x, packed, scales, row_expert, row_weight, amax, group_rows):
+        out_local = x.float() @ self.shared
+        rows = torch.zeros((packed.shape[0], H))
+        for r in range(packed.shape[0]):
+            e = int(row_expert[r])
+            assert self.begin <= e < self.begin + self.count
+            rows[r] = float(row_weight[r]) * (self.fake_decode(packed[r], float(amax[e]))
+                                              @ self.experts[e])
+        out_groups = torch.zeros((group_rows.shape[0], H))
+        for g in range(group_rows.shape[0]):
+            for j in range(group_rows.shape[1]):
+                if int(group_rows[g, j]) >= 0:
+                    out_groups[g] += rows[int(group_rows[g, j])]
+        return out_local, out_groups
+
 
 def _free_port() -> int:
     with socket.socket() as s:
@@ -62,7 +112,7 @@ def _free_port() -> int:
 
 
 def _worker(rank: int, world: int, port: int, tokens: list[int], skew: bool, q,
-            keep: int = K) -> None:
+            keep: int = K, fp4: bool = False) -> None:
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -74,30 +124,46 @@ def _worker(rank: int, world: int, port: int, tokens: list[int], skew: bool, q,
             # every token prefers experts 0..3 (all on rank 0)
             eng.bias[:4] = 50.0
         ep = ExpertParallelMoE(eng, rank=rank, world=world, num_experts=E, top_k=K,
-                               hidden_size=H)
-        g = torch.Generator().manual_seed(100 + rank)
-        x = torch.randn(tokens[rank], H, generator=g).to(torch.bfloat16)
+                               hidden_size=H, fp4_dispatch=fp4)
+        xs = [torch.randn(tokens[r], H, generator=torch.Generator().manual_seed(100 + r))
+              .to(torch.bfloat16) for r in range(world)]
+        x = xs[rank]
         out = ep(x)
         ref_eng = FakeEngine(0, E, keep=keep)
         if skew:
             ref_eng.bias[:4] = 50.0
         ids, w = ref_eng.route(x)
-        want = ref_eng.forward_expert_rows(x, ids, w, shared_rows=x.shape[0])
+        if fp4:
+            # one process, the concatenated batch's slab scales
+            amax = torch.zeros(E)
+            for xr in xs:
+                amax = torch.maximum(amax, ref_eng.slab_amax(xr, ref_eng.route(xr)[0]))
+            want = x.float() @ ref_eng.shared
+            for t in range(x.shape[0]):
+                for s in range(K):
+                    e = int(ids[t, s])
+                    if e >= 0:
+                        v = ref_eng.fake_codes(x[t].float(), float(amax[e])) * float(amax[e]) / 7.0
+                        want[t] += float(w[t, s]) * (v @ ref_eng.experts[e])
+        else:
+            want = ref_eng.forward_expert_rows(x, ids, w, shared_rows=x.shape[0])
         err = float((out - want).abs().max() / want.abs().max())
         q.put((rank, err, ep.last_counts))
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,tokens,skew,keep", [(2, [7, 5], False, K),
-                                                    (4, [6, 1, 9, 3], False, K),
-                                                    (2, [8, 4], True, K),
-                                                    (4, [5, 8, 2, 7], False, 2)])
-def test_expert_parallel_matches_single_process(world, tokens, skew, keep):
+@pytest.mark.parametrize("world,tokens,skew,keep,fp4", [(2, [7, 5], False, K, False),
+                                                        (4, [6, 1, 9, 3], False, K, False),
+                                                        (2, [8, 4], True, K, False),
+                                                        (4, [5, 8, 2, 7], False, 2, False),
+                                                        (2, [7, 5], False, K, True),
+                                                        (4, [6, 1, 9, 3], False, 3, True)])
+def test_expert_parallel_matches_single_process(world, tokens, skew, keep, fp4):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, tokens, skew, q, keep))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, tokens, skew, q, keep, fp4))
              for r in range(world)]
     for p in procs:
         p.start()

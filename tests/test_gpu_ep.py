@@ -7,7 +7,9 @@ the shared expert only on the leading rows; checked against the oracle.
 test_expert_parallel_two_gpus: two ranks (one process per GPU, NCCL) each
 hold half the experts, exchange tokens with glm5x_moe.ep, and must match the
 oracle of the same layer (routed-expert slabs across ranks, shared-expert
-slab per rank) within the north-star tolerance (needs 2 GPUs).
+slab per rank) within the north-star tolerance (needs 2 GPUs); the FP4
+dispatch must give the same bits as the BF16 dispatch (one GPU: the same
+with a single rank).
 """
 from __future__ import annotations
 
@@ -89,8 +91,10 @@ def _ep_worker(rank, world, port, q):
         tokens = [48 + 16 * r for r in range(world)]
         T = tokens[rank]
         begin, count = expert_range(rank, world, E)
+        # room for the local tokens plus every received row: BF16 dispatch
+        # sends a token once per rank, FP4 dispatch once per (token, expert)
         ep_layer = GLM5XMoELayer(hidden_size=H, intermediate_size=I, num_experts=E, top_k=k,
-                                 has_shared=True, max_tokens=T + sum(tokens), device=rank,
+                                 has_shared=True, max_tokens=T + k * sum(tokens), device=rank,
                                  expert_begin=begin, expert_count=count)
         full = GLM5XMoELayer(hidden_size=H, intermediate_size=I, num_experts=E, top_k=k,
                              has_shared=True, max_tokens=sum(tokens), device=rank)
@@ -113,6 +117,13 @@ def _ep_worker(rank, world, port, q):
         got = ep(x).cpu().numpy()
         torch.cuda.synchronize(rank)
         ep_layer.check()
+        # FP4 dispatch: the same slabs, so the same bits
+        ep4 = ExpertParallelMoE(ep_layer, rank=rank, world=world, num_experts=E, top_k=k,
+                                hidden_size=H, fp4_dispatch=True)
+        got4 = ep4(x).cpu().numpy()
+        torch.cuda.synchronize(rank)
+        ep_layer.check()
+        fp4_equal = bool(np.array_equal(got, got4))
         # Oracle with the parallel layer's slabs: a routed expert's slab holds
         # every rank's tokens routed to it (the same slab as one GPU running
         # the concatenated batch); the shared expert's slab is the rank's own
@@ -128,26 +139,37 @@ def _ep_worker(rank, world, port, q):
         want = routed[off:off + T] + O.nvfp4_expert_dequant_oracle(bf16_to_np(xs[rank]),
                                                                    shared[:2], shared[2])
         max_rel, l2, cos = O.relative_error(got, want)
-        q.put((rank, max_rel, cos, ep.last_counts))
+        q.put((rank, max_rel, cos, ep.last_counts, fp4_equal, ep4.last_counts))
         full.close()
         ep_layer.close()
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_expert_parallel_two_gpus():
+def _run_ep(world):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_ep_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_ep_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
         p.join(timeout=300)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
-    for _ in range(2):
-        rank, max_rel, cos, counts = q.get(timeout=10)
+    for _ in range(world):
+        rank, max_rel, cos, counts, fp4_equal, counts4 = q.get(timeout=10)
         assert max_rel <= MAX_REL and cos >= MIN_COS, (rank, max_rel, cos, counts)
-        assert sum(counts[1]) > 0, counts
+        assert sum(counts[1]) > 0 and sum(counts4[1]) > 0, (counts, counts4)
+        assert fp4_equal, rank
+
+
+def test_expert_parallel_fp4_dispatch_one_gpu():
+    """The expert-parallel module with one rank: BF16 and FP4 dispatch give
+    the same bits, and both match the oracle."""
+    _run_ep(1)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_expert_parallel_two_gpus():
+    _run_ep(2)
