@@ -223,6 +223,23 @@ glm5x_status glm5x_moe_forward(glm5x_moe* moe, const void* hidden_bf16, int64_t 
  * ComputeBackend convention of host spans in and host vectors out. */
 glm5x_status glm5x_moe_forward_host(glm5x_moe* moe, const uint16_t* hidden_bf16,
                                     int64_t tokens, float* out);
+/* Pipelined form of glm5x_moe_forward_host for callers with a stream of
+ * batches (no reference counterpart: ComputeBackend calls are synchronous).
+ * Enqueues the upload of `hidden_bf16`, the forward and the download into
+ * `out` and returns a ticket without waiting. The upload runs on a copy
+ * stream, the forward on the engine's stream and the download on a second
+ * copy stream, ordered by events over two staging slots, so the upload of one
+ * batch, the forward of the previous one and the download of the one before
+ * overlap. Both host buffers must stay valid and unchanged until
+ * glm5x_moe_wait_host(ticket) returns; page-locked buffers let the copies
+ * run asynchronously. Results equal glm5x_moe_forward_host's. */
+glm5x_status glm5x_moe_submit_host(glm5x_moe* moe, const uint16_t* hidden_bf16, int64_t tokens,
+                                   float* out, int64_t* ticket);
+/* Blocks until the download of `ticket` is done and returns the status of its
+ * forward's device checks (the error words glm5x_moe_check reports).
+ * GLM5X_INVALID_STATE for a ticket not yet submitted or older than the last
+ * 64 submissions. */
+glm5x_status glm5x_moe_wait_host(glm5x_moe* moe, int64_t ticket);
 /* Expert path only, with caller-supplied routing (device buffers): ids
  * [T, top_k] int32 global expert ids, weights [T, top_k] FP32 (the
  * contribution of each slot, already scaled). Replaces

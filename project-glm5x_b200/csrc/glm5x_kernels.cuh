@@ -205,6 +205,7 @@ cudaError_t launch_nvfp4_pair_gemm(int epi, const CUtensorMap* tmap_a, const CUt
 // ------------------------------------------------------------ combine.cu
 // out[t, :] (+)= sum_{s < kk} y[pos[t, s], :] in slot order (FP32
 // accumulation of BF16 rows); pos < 0 marks an absent slot. kk <= 32.
+cudaError_t launch_error_snapshot(uint32_t* err, uint32_t* snap, cudaStream_t st);
 cudaError_t launch_combine(const uint16_t* y, const int32_t* pos, int T, int kk, int H,
                            float* out, cudaStream_t st, int accumulate = 0);
 

@@ -195,6 +195,19 @@ struct glm5x_moe {
   uint16_t *h_bf16 = nullptr, *y_bf16 = nullptr;
   uint16_t* stage_in = nullptr;  // host-API staging
   float* stage_out = nullptr;
+  // Pipelined host API (glm5x_moe_submit_host / glm5x_moe_wait_host): two
+  // staging slots, an upload and a download stream beside the compute
+  // stream, and per-ticket events and error words in a ring.
+  static constexpr int kTicketRing = 64;
+  bool pipe_ready = false;
+  cudaStream_t up_stream = nullptr, down_stream = nullptr;
+  uint16_t* pipe_in[2]{};
+  float* pipe_out[2]{};
+  cudaEvent_t up_done[kTicketRing]{}, comp_done[kTicketRing]{}, down_done[kTicketRing]{};
+  uint32_t* err_snap = nullptr;  // device: error word of each ticket's forward
+  uint32_t* err_host = nullptr;  // page-locked copy of err_snap
+  int64_t ticket_of[kTicketRing]{};
+  int64_t next_ticket = 0;
   uint8_t* stage_w = nullptr;    // weight admission staging
   size_t stage_w_bytes = 0;
   float* scratch_f = nullptr;
@@ -467,10 +480,16 @@ glm5x_status glm5x_moe_create(const glm5x_moe_config* cfg, int device, glm5x_moe
 void glm5x_moe_destroy(glm5x_moe* m) {
   if (!m) return;
   cudaSetDevice(m->device);
-  if (m->stream) cudaStreamSynchronize(m->stream);
+  for (cudaStream_t s : {m->stream, m->up_stream, m->down_stream})
+    if (s) cudaStreamSynchronize(s);
   for (void* p : m->allocations) cudaFree(p);
   if (m->stage_w) cudaFree(m->stage_w);
-  if (m->stream) cudaStreamDestroy(m->stream);
+  for (cudaStream_t s : {m->stream, m->up_stream, m->down_stream})
+    if (s) cudaStreamDestroy(s);
+  for (int i = 0; i < glm5x_moe::kTicketRing; ++i)
+    for (cudaEvent_t e : {m->up_done[i], m->comp_done[i], m->down_done[i]})
+      if (e) cudaEventDestroy(e);
+  if (m->err_host) cudaFreeHost(m->err_host);
   for (auto& row : m->ev)
     for (auto& e : row)
       if (e) cudaEventDestroy(e);
@@ -1191,21 +1210,118 @@ glm5x_status glm5x_moe_forward_host(glm5x_moe* m, const uint16_t* hidden, int64_
   return glm5x_moe_check(m);
 }
 
+static glm5x_status error_word_status(glm5x_moe* m, uint32_t e) {
+  if (!e) return GLM5X_OK;
+  if (e & kErrWaitTimeout) return m->fail(GLM5X_WAIT_TIMEOUT, "device wait timed out (0x%x)", e);
+  if (e & kErrNonFinite) return m->fail(GLM5X_INVALID_STATE, "non-finite input (0x%x)", e);
+  if (e & kErrBounds) return m->fail(GLM5X_INVALID_EXTENT, "routing ids invalid (0x%x)", e);
+  if (e & kErrRoutingMass) return m->fail(GLM5X_INVALID_STATE, "zero routing mass (0x%x)", e);
+  return m->fail(GLM5X_DEVICE_ERROR, "device error word 0x%x", e);
+}
+
 glm5x_status glm5x_moe_check(glm5x_moe* m) {
   if (!m) return fail_global(GLM5X_INVALID_STATE, "null engine");
   cudaSetDevice(m->device);
   G5_CHECK(m, cudaDeviceSynchronize(), "device synchronize");
   uint32_t e = 0;
   G5_CHECK(m, cudaMemcpy(&e, m->err, sizeof e, cudaMemcpyDeviceToHost), "error word");
-  if (e) {
-    cudaMemset(m->err, 0, sizeof(uint32_t));
-    if (e & kErrWaitTimeout) return m->fail(GLM5X_WAIT_TIMEOUT, "device wait timed out (0x%x)", e);
-    if (e & kErrNonFinite) return m->fail(GLM5X_INVALID_STATE, "non-finite input (0x%x)", e);
-    if (e & kErrBounds) return m->fail(GLM5X_INVALID_EXTENT, "routing ids invalid (0x%x)", e);
-    if (e & kErrRoutingMass) return m->fail(GLM5X_INVALID_STATE, "zero routing mass (0x%x)", e);
-    return m->fail(GLM5X_DEVICE_ERROR, "device error word 0x%x", e);
+  if (e) cudaMemset(m->err, 0, sizeof(uint32_t));
+  return error_word_status(m, e);
+}
+
+// Staging slots, streams and events of the pipelined host API, made on its
+// first use so engines that never call it hold none of them.
+static glm5x_status pipe_init(glm5x_moe* m) {
+  if (m->pipe_ready) return GLM5X_OK;
+  const size_t n = (size_t)m->cfg.max_tokens * m->H();
+  bool ok = true;
+  for (int b = 0; b < 2; ++b) {
+    if (!m->pipe_in[b]) ok = ok && m->alloc(&m->pipe_in[b], n);
+    if (!m->pipe_out[b]) ok = ok && m->alloc(&m->pipe_out[b], n);
   }
+  if (!m->err_snap) ok = ok && m->alloc(&m->err_snap, glm5x_moe::kTicketRing);
+  if (!ok) return m->fail(GLM5X_OUT_OF_MEMORY, "pipelined staging buffers");
+  if (!m->err_host)
+    G5_CHECK(m, cudaHostAlloc(&m->err_host, sizeof(uint32_t) * glm5x_moe::kTicketRing,
+                              cudaHostAllocDefault),
+             "page-locked error words");
+  for (cudaStream_t* s : {&m->up_stream, &m->down_stream})
+    if (!*s) G5_CHECK(m, cudaStreamCreateWithFlags(s, cudaStreamNonBlocking), "copy stream");
+  for (int i = 0; i < glm5x_moe::kTicketRing; ++i) {
+    for (cudaEvent_t* e : {&m->up_done[i], &m->comp_done[i], &m->down_done[i]})
+      if (!*e) G5_CHECK(m, cudaEventCreateWithFlags(e, cudaEventDisableTiming), "event create");
+    m->ticket_of[i] = -1;
+  }
+  m->pipe_ready = true;
   return GLM5X_OK;
+}
+
+// Ticket t uses staging slot t % 2 and ring entry t % kTicketRing. Its upload
+// waits until the forward of ticket t - 2 has read the slot's input, its
+// forward until the download of ticket t - 2 has read the slot's output, and
+// its download until its own forward is done, so the upload of one batch, the
+// forward of the previous one and the download of the one before can run at
+// the same time. The error word is copied and cleared after each forward so
+// every ticket reports the device errors of its own kernels.
+glm5x_status glm5x_moe_submit_host(glm5x_moe* m, const uint16_t* hidden, int64_t T, float* out,
+                                   int64_t* ticket) {
+  if (!m || !hidden || !out || !ticket) return fail_global(GLM5X_INVALID_STATE, "null argument");
+  if (T <= 0 || T > m->cfg.max_tokens)
+    return m->fail(GLM5X_INVALID_EXTENT, "tokens outside [1, max_tokens]");
+  cudaSetDevice(m->device);
+  glm5x_status s = pipe_init(m);
+  if (s != GLM5X_OK) return s;
+  const int64_t t = m->next_ticket;
+  const int b = (int)(t & 1), r = (int)(t % glm5x_moe::kTicketRing);
+  const int rp = (int)((t + glm5x_moe::kTicketRing - 2) % glm5x_moe::kTicketRing);
+  const size_t in_bytes = sizeof(uint16_t) * T * m->H(), out_bytes = sizeof(float) * T * m->H();
+  if (t >= 2) G5_CHECK(m, cudaStreamWaitEvent(m->up_stream, m->comp_done[rp], 0), "upload order");
+  G5_CHECK(m, cudaMemcpyAsync(m->pipe_in[b], hidden, in_bytes, cudaMemcpyHostToDevice,
+                              m->up_stream),
+           "hidden upload");
+  G5_CHECK(m, cudaEventRecord(m->up_done[r], m->up_stream), "event record");
+  G5_CHECK(m, cudaStreamWaitEvent(m->stream, m->up_done[r], 0), "forward order");
+  if (t >= 2) G5_CHECK(m, cudaStreamWaitEvent(m->stream, m->down_done[rp], 0), "forward order");
+  s = run_forward(m, m->pipe_in[b], T, nullptr, nullptr, m->pipe_out[b], m->stream);
+  if (s == GLM5X_OK) {
+    const cudaError_t ce = launch_error_snapshot(m->err, m->err_snap + r, m->stream);
+    if (ce != cudaSuccess) s = cuda_fail(m, ce, "error word snapshot");
+    m->stats.kernel_launches += 1;
+  }
+  // the events are recorded on failure too, so the next submission of this
+  // ticket number orders itself after whatever this one launched
+  G5_CHECK(m, cudaEventRecord(m->comp_done[r], m->stream), "event record");
+  G5_CHECK(m, cudaStreamWaitEvent(m->down_stream, m->comp_done[r], 0), "download order");
+  if (s == GLM5X_OK) {
+    G5_CHECK(m, cudaMemcpyAsync(out, m->pipe_out[b], out_bytes, cudaMemcpyDeviceToHost,
+                                m->down_stream),
+             "output download");
+    G5_CHECK(m, cudaMemcpyAsync(m->err_host + r, m->err_snap + r, sizeof(uint32_t),
+                                cudaMemcpyDeviceToHost, m->down_stream),
+             "error word download");
+  }
+  G5_CHECK(m, cudaEventRecord(m->down_done[r], m->down_stream), "event record");
+  if (s != GLM5X_OK) return s;
+  m->ticket_of[r] = t;
+  m->next_ticket = t + 1;
+  m->stats.activation_h2d_bytes += in_bytes;
+  m->stats.device_to_host_bytes += out_bytes;
+  *ticket = t;
+  return GLM5X_OK;
+}
+
+glm5x_status glm5x_moe_wait_host(glm5x_moe* m, int64_t t) {
+  if (!m) return fail_global(GLM5X_INVALID_STATE, "null engine");
+  if (!m->pipe_ready || t < 0 || t >= m->next_ticket)
+    return m->fail(GLM5X_INVALID_STATE, "ticket %lld was not submitted", (long long)t);
+  const int r = (int)(t % glm5x_moe::kTicketRing);
+  if (m->ticket_of[r] != t)
+    return m->fail(GLM5X_INVALID_STATE, "ticket %lld is older than the last %d submissions",
+                   (long long)t, glm5x_moe::kTicketRing);
+  cudaSetDevice(m->device);
+  G5_CHECK(m, cudaEventSynchronize(m->down_done[r]), "pipelined forward");
+  m->stats.stream_synchronization_count++;
+  return error_word_status(m, m->err_host[r]);
 }
 
 glm5x_status glm5x_moe_last_routing(glm5x_moe* m, int32_t* ids, float* weights, float* logits,

@@ -142,4 +142,16 @@ cudaError_t launch_combine(const uint16_t* y, const int32_t* pos, int T, int kk,
   return cudaGetLastError();
 }
 
+// Moves the engine's error word into a per-forward slot and clears it, in
+// stream order after the forward's kernels.
+__global__ void error_snapshot_kernel(uint32_t* err, uint32_t* snap) {
+  *snap = *err;
+  *err = 0u;
+}
+
+cudaError_t launch_error_snapshot(uint32_t* err, uint32_t* snap, cudaStream_t st) {
+  error_snapshot_kernel<<<1, 1, 0, st>>>(err, snap);
+  return cudaGetLastError();
+}
+
 }  // namespace glm5x

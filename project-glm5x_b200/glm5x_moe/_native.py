@@ -131,6 +131,8 @@ SIGNATURES = {
     "glm5x_moe_load_expert_k3x": [_P, _I32, _P, ctypes.c_char_p],
     "glm5x_moe_forward": [_P, _P, _I64, _P, _P],
     "glm5x_moe_forward_host": [_P, _P, _I64, _P],
+    "glm5x_moe_submit_host": [_P, _P, _I64, _P, _P],
+    "glm5x_moe_wait_host": [_P, _I64],
     "glm5x_moe_forward_routed": [_P, _P, _I64, _P, _P, _P, _P],
     "glm5x_moe_forward_expert_rows": [_P, _P, _I64, _P, _P, _I64, _P, _P],
     "glm5x_moe_slab_amax": [_P, _P, _I64, _P, _P, _P],

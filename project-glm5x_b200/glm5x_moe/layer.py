@@ -80,11 +80,14 @@ class GLM5XMoELayer:
         self.top_k = top_k
         self.has_shared = has_shared
         self.max_tokens = max_tokens
+        self._in_flight: dict[int, tuple[torch.Tensor, torch.Tensor]] = {}
 
     def close(self) -> None:
         if getattr(self, "_h", None):
+            # destroy synchronizes every stream before the host buffers go
             N.lib().glm5x_moe_destroy(self._h)
             self._h = None
+            self._in_flight = {}
 
     def __del__(self) -> None:  # pragma: no cover - interpreter shutdown order
         try:
@@ -205,6 +208,30 @@ class GLM5XMoELayer:
         T = hidden_bf16_host.shape[0]
         N.check(N.lib().glm5x_moe_forward_host(self._h, hidden_bf16_host.data_ptr(), T,
                                                out_host.data_ptr()), self._h)
+
+    def submit_host(self, hidden_bf16_host: torch.Tensor, out_host: torch.Tensor) -> int:
+        """Pipelined host forward: enqueues upload, forward and download and
+        returns a ticket for wait_host(). Both tensors are held until then."""
+        T = hidden_bf16_host.shape[0]
+        if (hidden_bf16_host.device.type != "cpu" or out_host.device.type != "cpu"
+                or hidden_bf16_host.dtype != torch.bfloat16 or out_host.dtype != torch.float32
+                or not hidden_bf16_host.is_contiguous() or not out_host.is_contiguous()
+                or tuple(hidden_bf16_host.shape) != (T, self.hidden_size)
+                or tuple(out_host.shape) != (T, self.hidden_size)):
+            raise ValueError("GLM5X_HOST_BUFFERS")
+        ticket = ctypes.c_int64()
+        N.check(N.lib().glm5x_moe_submit_host(self._h, hidden_bf16_host.data_ptr(), T,
+                                              out_host.data_ptr(), ctypes.byref(ticket)),
+                self._h)
+        self._in_flight[ticket.value] = (hidden_bf16_host, out_host)
+        return ticket.value
+
+    def wait_host(self, ticket: int) -> None:
+        """Waits for a submit_host() ticket; raises its forward's device error."""
+        try:
+            N.check(N.lib().glm5x_moe_wait_host(self._h, ticket), self._h)
+        finally:
+            self._in_flight.pop(ticket, None)
 
     def check(self) -> None:
         N.check(N.lib().glm5x_moe_check(self._h), self._h)
