@@ -245,6 +245,27 @@ def zipf_bias(experts: int, seed: int):
     return bias + 0.5 * (perm.to(torch.float64) + 1.0).pow(-1.1).to(torch.float32)
 
 
+def profiled_phases(fwd, hidden, steps: int, engine=None) -> tuple[dict, int]:
+    """Per-phase milliseconds of `steps` further forwards with phase events on.
+    The events sit between the forward's kernels on its stream and each adds
+    about 2.5 us to a step, so the timed steps run without them and the phase
+    split comes from these forwards. `fwd` is the layer, or the
+    expert-parallel wrapper around `engine`."""
+    import torch
+    engine = engine or fwd
+    engine.set_profiling(True)
+    engine.phase_times()
+    for _ in range(steps):
+        if engine is fwd:
+            fwd(hidden, want_routing=False)
+        else:
+            fwd(hidden)
+    torch.cuda.synchronize()
+    phases, n = engine.phase_times()
+    engine.set_profiling(False)
+    return {k: v / max(n, 1) for k, v in phases.items()}, n
+
+
 def run_decode_c4(device_index: int, steps: int, warmup: int, T: int = 64) -> dict:
     """Config 4 on one GPU: the full MXFP4 layer (256 experts + shared,
     GLM-5 shapes) at decode batch 64 with the Zipf-skewed router. HBM-bound:
@@ -272,8 +293,6 @@ def run_decode_c4(device_index: int, steps: int, warmup: int, T: int = 64) -> di
     touched = int(torch.unique(res.topk_indices).numel())
     for _ in range(warmup):
         layer(hidden, want_routing=False)
-    layer.set_profiling(True)
-    layer.phase_times()
     torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.nvtx.range_push("decode_timed")
@@ -285,8 +304,7 @@ def run_decode_c4(device_index: int, steps: int, warmup: int, T: int = 64) -> di
     torch.cuda.nvtx.range_pop()
     layer.check()
     ms = e0.elapsed_time(e1) / steps
-    phases, n = layer.phase_times()
-    phases = {k: v / max(n, 1) for k, v in phases.items()}
+    phases, _ = profiled_phases(layer, hidden, steps)
     layer.close()
     weight_bytes = (touched + 1) * MXFP4_EXPERT_BYTES
     alg = weight_bytes + E * H * 2 + E * 4 + T * H * 2 + T * H * 4
@@ -451,10 +469,6 @@ def run_ours_ep(args, world: int, rank: int, local: int) -> None:
     dist.all_reduce(per_dest)
     local_assign = int(per_dest[rank].item())
     stats0 = layer.stats()
-    layer.set_profiling(True)
-    layer.phase_times()
-    ep.set_timing(True)
-    ep.stage_times()
     dist.barrier()
     torch.cuda.synchronize()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -469,9 +483,11 @@ def run_ours_ep(args, world: int, rank: int, local: int) -> None:
     layer.check()
     ms_total = start.elapsed_time(stop)
     launches = layer.stats()["kernel_launches"] - stats0["kernel_launches"]
-    phases, nprof = layer.phase_times()
-    layer.set_profiling(False)
-    phases = {k: v / max(nprof, 1) for k, v in phases.items()}
+    # phase and stage split from further steps with the events on (they add
+    # about 2.5 us each, so the timed steps ran without them)
+    ep.set_timing(True)
+    ep.stage_times()
+    phases, nprof = profiled_phases(ep, hidden, args.steps, engine=layer)
     stages, nst = ep.stage_times()
     ep.set_timing(False)
     stages = {k: v / max(nst, 1) for k, v in stages.items()}
@@ -480,17 +496,42 @@ def run_ours_ep(args, world: int, rank: int, local: int) -> None:
     ms_total = float(t.item())
     ms_step = ms_total / args.steps
     value = world * T * args.steps / (ms_total / 1000.0)
-    # end to end: pinned host hidden -> device, forward, FP32 output -> host
-    hid_host = hidden.cpu().pin_memory()
-    out_host = torch.empty((T, H), dtype=torch.float32).pin_memory()
-    dev_in = torch.empty_like(hidden)
+    # end to end: pinned host hidden -> device, forward, FP32 output -> host.
+    # The upload of step i+1 and the download of step i-1 run on their own
+    # streams beside the forward of step i; two device input buffers and two
+    # pinned output buffers alternate so no copy touches another step's data.
+    hid_pp = [hidden.cpu().pin_memory(), hidden.cpu().pin_memory()]
+    out_pp = [torch.empty((T, H), dtype=torch.float32).pin_memory() for _ in range(2)]
+    dev_in = [torch.empty_like(hidden), torch.empty_like(hidden)]
+    up, down = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    in_ready = [torch.cuda.Event(), torch.cuda.Event()]
+    in_free = [torch.cuda.Event(), torch.cuda.Event()]
+
+    def upload(i):
+        b = i % 2
+        if i >= 2:
+            up.wait_event(in_free[b])
+        with torch.cuda.stream(up):
+            dev_in[b].copy_(hid_pp[b], non_blocking=True)
+        in_ready[b].record(up)
+
     dist.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(args.steps):
-        dev_in.copy_(hid_host, non_blocking=True)
-        out_host.copy_(ep(dev_in), non_blocking=True)
+    upload(0)
+    for i in range(args.steps):
+        b = i % 2
+        if i + 1 < args.steps:
+            upload(i + 1)
+        stream.wait_event(in_ready[b])
+        y = ep(dev_in[b])
+        in_free[b].record(stream)
+        down.wait_event(in_free[b])
+        with torch.cuda.stream(down):
+            out_pp[b].copy_(y, non_blocking=True)
+        y.record_stream(down)
+    stream.wait_stream(down)
     e1.record(stream)
     torch.cuda.synchronize()
     t = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev)
@@ -526,7 +567,11 @@ def run_ours_ep(args, world: int, rank: int, local: int) -> None:
             "gpu_launches": int(launches),
             "clocks": clocks.summary(),
             "e2e": {"value": world * T / (e2e_ms / 1000.0), "unit": "tokens/s",
-                    "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 4},
+                    "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 4,
+                    "ms_per_step": e2e_ms,
+                    "api": "ExpertParallelMoE on each rank; pinned host BF16 in, FP32 out, "
+                           "upload / forward / download of consecutive steps on three "
+                           "streams"},
         }
         print(json.dumps(line), flush=True)
     layer.close()
@@ -565,11 +610,6 @@ def run_ours(args) -> None:
         layer(hidden, want_routing=False)
     torch.cuda.synchronize()
     stats0 = layer.stats()
-    # phase events (CUDA events on the forward's own stream between its
-    # kernels) are recorded during the timed steps themselves
-    layer.set_profiling(True)
-    layer.phase_times()  # drop warm-up samples
-    torch.cuda.synchronize()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
         torch.cuda.nvtx.range_push("bench_timed")
@@ -582,9 +622,7 @@ def run_ours(args) -> None:
     layer.check()
     ms_total = start.elapsed_time(stop)
     launches = layer.stats()["kernel_launches"] - stats0["kernel_launches"]
-    phases, nprof = layer.phase_times()
-    layer.set_profiling(False)
-    phases = {k: v / max(nprof, 1) for k, v in phases.items()}
+    phases, nprof = profiled_phases(layer, hidden, args.steps)
     ms_step = ms_total / args.steps
     value = world * T * args.steps / (ms_total / 1000.0)
 

@@ -235,6 +235,14 @@ glm5x_status glm5x_moe_forward_host(glm5x_moe* moe, const uint16_t* hidden_bf16,
  * run asynchronously. Results equal glm5x_moe_forward_host's. */
 glm5x_status glm5x_moe_submit_host(glm5x_moe* moe, const uint16_t* hidden_bf16, int64_t tokens,
                                    float* out, int64_t* ticket);
+/* Copies n <= 4096 int64 words from device memory to `dst` (host) after the
+ * work already on `stream` (NULL = the engine's stream), through page-locked
+ * mapped memory the device writes with ordinary stores, then synchronizes
+ * `stream`. A read-back of a few counts this way uses no copy engine, so it
+ * does not wait behind a large download running on another stream (the
+ * expert-parallel dispatch reads its all-to-all counts with it). */
+glm5x_status glm5x_moe_read_ints(glm5x_moe* moe, const int64_t* src, int64_t n, int64_t* dst,
+                                 void* stream);
 /* Blocks until the download of `ticket` is done and returns the status of its
  * forward's device checks (the error words glm5x_moe_check reports).
  * GLM5X_INVALID_STATE for a ticket not yet submitted or older than the last

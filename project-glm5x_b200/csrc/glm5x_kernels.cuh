@@ -206,6 +206,8 @@ cudaError_t launch_nvfp4_pair_gemm(int epi, const CUtensorMap* tmap_a, const CUt
 // out[t, :] (+)= sum_{s < kk} y[pos[t, s], :] in slot order (FP32
 // accumulation of BF16 rows); pos < 0 marks an absent slot. kk <= 32.
 cudaError_t launch_error_snapshot(uint32_t* err, uint32_t* snap, cudaStream_t st);
+cudaError_t launch_store_ints_to_host(const int64_t* src, int64_t n, int64_t* dst_mapped,
+                                      cudaStream_t st);
 cudaError_t launch_combine(const uint16_t* y, const int32_t* pos, int T, int kk, int H,
                            float* out, cudaStream_t st, int accumulate = 0);
 

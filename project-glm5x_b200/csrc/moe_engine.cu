@@ -208,6 +208,10 @@ struct glm5x_moe {
   uint32_t* err_host = nullptr;  // page-locked copy of err_snap
   int64_t ticket_of[kTicketRing]{};
   int64_t next_ticket = 0;
+  // glm5x_moe_read_ints: page-locked words the device writes with stores
+  static constexpr int64_t kHostInts = 4096;
+  int64_t* host_ints = nullptr;
+  int64_t* host_ints_dev = nullptr;  // device address of host_ints
   uint8_t* stage_w = nullptr;    // weight admission staging
   size_t stage_w_bytes = 0;
   float* scratch_f = nullptr;
@@ -490,6 +494,7 @@ void glm5x_moe_destroy(glm5x_moe* m) {
     for (cudaEvent_t e : {m->up_done[i], m->comp_done[i], m->down_done[i]})
       if (e) cudaEventDestroy(e);
   if (m->err_host) cudaFreeHost(m->err_host);
+  if (m->host_ints) cudaFreeHost(m->host_ints);
   for (auto& row : m->ev)
     for (auto& e : row)
       if (e) cudaEventDestroy(e);
@@ -1307,6 +1312,31 @@ glm5x_status glm5x_moe_submit_host(glm5x_moe* m, const uint16_t* hidden, int64_t
   m->stats.activation_h2d_bytes += in_bytes;
   m->stats.device_to_host_bytes += out_bytes;
   *ticket = t;
+  return GLM5X_OK;
+}
+
+glm5x_status glm5x_moe_read_ints(glm5x_moe* m, const int64_t* src, int64_t n, int64_t* dst,
+                                 void* stream) {
+  if (!m || (n > 0 && (!src || !dst))) return fail_global(GLM5X_INVALID_STATE, "null argument");
+  if (n < 0 || n > glm5x_moe::kHostInts)
+    return m->fail(GLM5X_INVALID_EXTENT, "read_ints: n outside [0, %lld]",
+                   (long long)glm5x_moe::kHostInts);
+  if (n == 0) return GLM5X_OK;
+  cudaSetDevice(m->device);
+  if (!m->host_ints) {
+    G5_CHECK(m, cudaHostAlloc(&m->host_ints, sizeof(int64_t) * glm5x_moe::kHostInts,
+                              cudaHostAllocMapped),
+             "mapped host words");
+    void* d = nullptr;
+    G5_CHECK(m, cudaHostGetDevicePointer(&d, m->host_ints, 0), "mapped host words");
+    m->host_ints_dev = static_cast<int64_t*>(d);
+  }
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : m->stream;
+  G5_CHECK(m, launch_store_ints_to_host(src, n, m->host_ints_dev, st), "read_ints");
+  m->stats.kernel_launches += 1;
+  G5_CHECK(m, cudaStreamSynchronize(st), "read_ints");
+  m->stats.stream_synchronization_count++;
+  std::memcpy(dst, m->host_ints, sizeof(int64_t) * n);
   return GLM5X_OK;
 }
 

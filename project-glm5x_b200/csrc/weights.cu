@@ -149,6 +149,22 @@ __global__ void error_snapshot_kernel(uint32_t* err, uint32_t* snap) {
   *err = 0u;
 }
 
+// Stores device words into mapped page-locked host memory from the SMs, so a
+// small read-back needs no copy engine (and does not queue behind a large
+// download another stream has on one).
+__global__ void store_ints_to_host_kernel(const int64_t* __restrict__ src, int64_t n,
+                                          volatile int64_t* dst) {
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
+  __threadfence_system();
+}
+
+cudaError_t launch_store_ints_to_host(const int64_t* src, int64_t n, int64_t* dst_mapped,
+                                      cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  store_ints_to_host_kernel<<<1, 256, 0, st>>>(src, n, dst_mapped);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_error_snapshot(uint32_t* err, uint32_t* snap, cudaStream_t st) {
   error_snapshot_kernel<<<1, 1, 0, st>>>(err, snap);
   return cudaGetLastError();

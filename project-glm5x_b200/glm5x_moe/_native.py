@@ -133,6 +133,7 @@ SIGNATURES = {
     "glm5x_moe_forward_host": [_P, _P, _I64, _P],
     "glm5x_moe_submit_host": [_P, _P, _I64, _P, _P],
     "glm5x_moe_wait_host": [_P, _I64],
+    "glm5x_moe_read_ints": [_P, _P, _I64, _P, _P],
     "glm5x_moe_forward_routed": [_P, _P, _I64, _P, _P, _P, _P],
     "glm5x_moe_forward_expert_rows": [_P, _P, _I64, _P, _P, _I64, _P, _P],
     "glm5x_moe_slab_amax": [_P, _P, _I64, _P, _P, _P],

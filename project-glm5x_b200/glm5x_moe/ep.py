@@ -100,6 +100,34 @@ class ExpertParallelMoE:
         d_idx, t_idx = mask.t().nonzero(as_tuple=True)
         return d_idx, t_idx, mask.sum(dim=0)
 
+    def _dest_mask(self, ids: torch.Tensor) -> torch.Tensor:
+        """[T, W] bool: token t has at least one expert on rank d."""
+        valid = ids >= 0
+        dest = torch.where(valid, ids.long() // self.per, 0)
+        hits = torch.zeros((ids.shape[0], self.world), dtype=torch.int32, device=ids.device)
+        hits.scatter_add_(1, dest, valid.to(torch.int32))
+        return hits > 0
+
+    @staticmethod
+    def _pairs(mask: torch.Tensor, n_pairs: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """The (dest, token) pairs of plan() for a known pair count, found by a
+        prefix sum and a scatter instead of nonzero (which reads its size back
+        to the host)."""
+        T = mask.shape[0]
+        flat = mask.t().reshape(-1)
+        pos = torch.cumsum(flat, 0) - 1
+        pos = torch.where(flat, pos, torch.full_like(pos, n_pairs))  # unused slot
+        lin = torch.empty(n_pairs + 1, dtype=torch.int64, device=mask.device)
+        lin.scatter_(0, pos, torch.arange(flat.numel(), device=mask.device))
+        lin = lin[:n_pairs]
+        return lin // T, lin % T
+
+    def _host_ints(self, t: torch.Tensor) -> list[int]:
+        # engines with read_ints bring counts back without a copy engine, so
+        # the read does not wait behind a download on another stream
+        reader = getattr(self.engine, "read_ints", None)
+        return reader(t) if reader is not None else t.tolist()
+
     def __call__(self, hidden: torch.Tensor) -> torch.Tensor:
         H = self.hidden_size
         x = hidden.reshape(-1, H).to(torch.bfloat16).contiguous()
@@ -111,22 +139,26 @@ class ExpertParallelMoE:
         if self.fp4_dispatch:
             out = self._forward_fp4(x, ids, w, evs)
             return out.reshape(*hidden.shape[:-1], H)
-        d_idx, t_idx, send_counts = self.plan(ids)
+        # counts first: one host read for both directions (the split sizes)
+        mask = self._dest_mask(ids)
+        send_counts = mask.sum(dim=0)
+        recv_counts = torch.empty_like(send_counts)
+        dist.all_to_all_single(recv_counts, send_counts.contiguous(), group=self.group)
+        counts = self._host_ints(torch.cat([send_counts, recv_counts]))
+        sc, rc = counts[:self.world], counts[self.world:]
+        self.last_counts = (sc, rc)
+        R = sum(rc)
+        d_idx, t_idx = self._pairs(mask, sum(sc))
         # per pair: k masked ids and k weights (as raw 32-bit words) in one row
         sel = ids[t_idx]
         meta = torch.cat([torch.where(sel.long() // self.per == d_idx[:, None], sel,
                                       torch.full_like(sel, -1)),
                           w[t_idx].view(torch.int32)], dim=1).contiguous()
         send_rows = x[t_idx].contiguous()
-        recv_counts = torch.empty_like(send_counts)
-        dist.all_to_all_single(recv_counts, send_counts.contiguous(), group=self.group)
-        sc = send_counts.tolist()
-        rc = recv_counts.tolist()
-        self.last_counts = (sc, rc)
-        R = sum(rc)
-        # local tokens first (shared expert), then the received rows
+        # local tokens first (shared expert), then the received rows; the
+        # local rows are copied by a kernel (x * 1 is exact), not a copy engine
         rows = torch.empty((T + R, H), dtype=torch.bfloat16, device=x.device)
-        rows[:T] = x
+        torch.mul(x, 1, out=rows[:T])
         dist.all_to_all_single(rows[T:], send_rows, rc, sc, group=self.group)
         rmeta = torch.empty((T + R, 2 * self.top_k), dtype=torch.int32, device=x.device)
         rmeta[:T, :self.top_k] = -1

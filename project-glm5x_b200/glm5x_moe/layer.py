@@ -233,6 +233,19 @@ class GLM5XMoELayer:
         finally:
             self._in_flight.pop(ticket, None)
 
+    def read_ints(self, t: torch.Tensor) -> list[int]:
+        """A small device int64 tensor's values on the host, after the work on
+        the current stream, without a copy-engine transfer."""
+        src = t.reshape(-1).to(dtype=torch.int64).contiguous()
+        if src.device.type != "cuda":
+            return src.tolist()
+        n = src.numel()
+        out = (ctypes.c_int64 * max(n, 1))()
+        with torch.cuda.device(self.device):
+            N.check(N.lib().glm5x_moe_read_ints(self._h, src.data_ptr(), n,
+                                                ctypes.addressof(out), _stream()), self._h)
+        return list(out[:n])
+
     def check(self) -> None:
         N.check(N.lib().glm5x_moe_check(self._h), self._h)
 

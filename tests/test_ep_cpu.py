@@ -177,3 +177,26 @@ def test_expert_parallel_matches_single_process(world, tokens, skew, keep, fp4):
         # with all top experts on rank 0, rank 1 receives nothing
         sent, recv = res[1][2]
         assert sum(recv) == 0 and sent[0] == tokens[1]
+
+
+@pytest.mark.parametrize("T,W,seed", [(1, 2, 0), (37, 4, 1), (64, 8, 2), (5, 4, 3)])
+def test_sync_free_pairs_match_plan(T, W, seed):
+    """The dispatch pairs built from a known count (prefix sum + scatter)
+    equal plan()'s nonzero order: by destination rank, tokens ascending,
+    including tokens that reach no rank (all slots empty) and ranks that
+    receive nothing."""
+    from glm5x_moe.ep import ExpertParallelMoE
+    g = torch.Generator().manual_seed(seed)
+    ep = ExpertParallelMoE(FakeEngine(0, E), rank=0, world=W, num_experts=E, top_k=K,
+                           hidden_size=H)
+    ids = torch.randint(0, E // 2, (T, K), generator=g).to(torch.int32)  # upper ranks idle
+    ids[::3, 1:] = -1
+    if T > 2:
+        ids[2, :] = -1
+    d_ref, t_ref, c_ref = ep.plan(ids)
+    mask = ep._dest_mask(ids)
+    assert torch.equal(mask.sum(dim=0), c_ref)
+    counts = ep._host_ints(torch.cat([c_ref, c_ref]))
+    assert counts[:W] == c_ref.tolist()
+    d, t = ep._pairs(mask, sum(counts[:W]))
+    assert torch.equal(d, d_ref) and torch.equal(t, t_ref)

@@ -115,3 +115,21 @@ def test_pipelined_host_forward_errors():
     layer.forward_host(x, want)
     assert torch.equal(o, want)
     layer.close()
+
+
+def test_read_ints_through_mapped_memory():
+    """glm5x_moe_read_ints: device int64 words on the host after the current
+    stream's work, written by device stores into mapped page-locked memory."""
+    from glm5x_moe._native import Glm5xError
+    layer, _ = _layer()
+    vals = torch.arange(-5, 3000, 7, dtype=torch.int64, device="cuda") * 1_000_003
+    assert layer.read_ints(vals) == vals.cpu().tolist()
+    # the read follows work queued before it on the stream
+    x = torch.zeros(4096, dtype=torch.int64, device="cuda")
+    x += torch.arange(4096, device="cuda")
+    assert layer.read_ints(x) == list(range(4096))
+    assert layer.read_ints(torch.empty(0, dtype=torch.int64, device="cuda")) == []
+    with pytest.raises(Glm5xError) as ei:
+        layer.read_ints(torch.zeros(4097, dtype=torch.int64, device="cuda"))
+    assert ei.value.code == 9
+    layer.close()
