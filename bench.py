@@ -266,7 +266,8 @@ def profiled_phases(fwd, hidden, steps: int, engine=None) -> tuple[dict, int]:
     return {k: v / max(n, 1) for k, v in phases.items()}, n
 
 
-def run_decode_c4(device_index: int, steps: int, warmup: int, T: int = 64) -> dict:
+def run_decode_c4(device_index: int, steps: int, warmup: int, T: int = 64,
+                  experts: int = 0) -> dict:
     """Config 4 on one GPU: the full MXFP4 layer (256 experts + shared,
     GLM-5 shapes) at decode batch 64 with the Zipf-skewed router. HBM-bound:
     algorithmic bytes = (distinct experts touched + 1 shared) x 20,054,016 B of
@@ -275,19 +276,20 @@ def run_decode_c4(device_index: int, steps: int, warmup: int, T: int = 64) -> di
     from glm5x_moe.layer import GLM5XMoELayer, MXFP4Expert
     from glm5x_moe.nvfp4 import quantize_mxfp4_weight
     dev = torch.device("cuda", device_index)
-    layer = GLM5XMoELayer(hidden_size=H, intermediate_size=I, num_experts=E, top_k=K_TOP,
+    E_ = experts or E  # fewer experts only for small profiling captures
+    layer = GLM5XMoELayer(hidden_size=H, intermediate_size=I, num_experts=E_, top_k=K_TOP,
                           routed_scaling_factor=SCALE, has_shared=True, max_tokens=T,
                           device=device_index, precision="mxfp4")
     g = torch.Generator(device=dev).manual_seed(4)
-    for e in list(range(E)) + [-1]:
+    for e in list(range(E_)) + [-1]:
         mats = [quantize_mxfp4_weight((torch.randn(shape, generator=g, device=dev) * 0.02)
                                       .to(torch.bfloat16))
                 for shape in ((I, H), (I, H), (H, I))]
         layer.load_expert(e, MXFP4Expert(*mats))
         del mats
     gc = torch.Generator(device="cpu").manual_seed(5)
-    router = (torch.randn(E, H, generator=gc) * 0.02).to(torch.bfloat16)
-    layer.set_router(router, zipf_bias(E, 6))
+    router = (torch.randn(E_, H, generator=gc) * 0.02).to(torch.bfloat16)
+    layer.set_router(router, zipf_bias(E_, 6))
     hidden = torch.randn(T, H, generator=gc).to(torch.bfloat16).to(dev)
     res = layer(hidden)
     touched = int(torch.unique(res.topk_indices).numel())
@@ -307,13 +309,14 @@ def run_decode_c4(device_index: int, steps: int, warmup: int, T: int = 64) -> di
     phases, _ = profiled_phases(layer, hidden, steps)
     layer.close()
     weight_bytes = (touched + 1) * MXFP4_EXPERT_BYTES
-    alg = weight_bytes + E * H * 2 + E * 4 + T * H * 2 + T * H * 4
+    alg = weight_bytes + E_ * H * 2 + E_ * 4 + T * H * 2 + T * H * 4
     hbm = peaks()["hbm_gbs"]
     gu_bytes = (touched + 1) * 2 * (H * I // 2 + H * I // 32)
     dn_bytes = (touched + 1) * (H * I // 2 + H * I // 32)
     return {
-        "workload": "c4: GLM-5 MoE layer, MXFP4 experts (E2M1 + E8M0/32), decode batch 64, "
-                    "256 experts + shared, Zipf(1.1)-skewed router bias, 1 GPU",
+        "workload": (f"c4: GLM-5 MoE layer, MXFP4 experts (E2M1 + E8M0/32), decode batch {T}, "
+                     f"{E_} experts + shared, Zipf(1.1)-skewed router bias, 1 GPU"
+                     + ("" if E_ == E else " (reduced expert count: profiling case)")),
         "tokens_per_s": T / (ms / 1000.0), "ms_per_step": ms, "experts_touched": touched,
         "phases_ms": phases,
         "roofline": {"bound": "hbm", "kernel": "whole layer step", "achieved": alg / (ms / 1000.0) / 1e9,
@@ -584,7 +587,8 @@ def run_ours(args) -> None:
     world, rank, local = dist_setup()
     torch.cuda.set_device(local)
     if args.decode_only:
-        print(json.dumps(run_decode_c4(local, args.steps, args.warmup)), flush=True)
+        print(json.dumps(run_decode_c4(local, args.steps, args.warmup,
+                                       experts=args.decode_experts)), flush=True)
         return
     if world > 1:
         run_ours_ep(args, world, rank, local)
@@ -753,6 +757,8 @@ def main() -> None:
     ap.add_argument("--down-tiles", default="", choices=["", "tm", "128", "256"],
                     help="down projection tiles: token-major or weight-major width (tuning)")
     ap.add_argument("--experts", type=int, default=0, help="override experts (profiling only)")
+    ap.add_argument("--decode-experts", type=int, default=0,
+                    help="with --decode-only: fewer experts (small profiling captures only)")
     ap.add_argument("--dispatch", default="bf16", choices=["bf16", "fp4"],
                     help="expert-parallel token rows as BF16 or as sender-quantized NVFP4")
     args = ap.parse_args()
