@@ -195,47 +195,56 @@ class ExpertParallelMoE:
         dest = torch.where(valid, flat_ids // self.per, torch.full_like(flat_ids, W))
         n_flat = flat_ids.numel()
         order = torch.argsort(dest * n_flat + torch.arange(n_flat, device=dev))
-        order = order[: int(valid.sum().item())]
+        # per destination: rows (token, expert pairs) and distinct tokens; the
+        # receiver's rows and row groups per source come back in one exchange
+        mask = self._dest_mask(ids)
+        # (a scatter-add count: CUDA bincount reads its input's maximum back)
+        rows_per = torch.zeros(W + 1, dtype=torch.int64, device=dev)
+        rows_per.scatter_add_(0, dest, torch.ones_like(dest))
+        send = torch.stack([rows_per[:W], mask.sum(dim=0)], dim=1)
+        recv = torch.empty_like(send)
+        dist.all_to_all_single(recv, send.contiguous(), group=self.group)
+        counts = self._host_ints(torch.cat([send.t().reshape(-1), recv.t().reshape(-1)]))
+        sc, tc, rc, gcount = (counts[0:W], counts[W:2 * W], counts[2 * W:3 * W],
+                              counts[3 * W:4 * W])
+        n_pairs, R, G = sum(sc), sum(rc), sum(gcount)
+        order = order[:n_pairs]
         pair_tok = (order // k).to(torch.int32)
         pair_exp = flat_ids[order].to(torch.int32)
         pair_w = w.reshape(-1)[order].float()
-        send_counts = torch.bincount(dest[order], minlength=W)
         packed, scales = self.engine.quantize_rows(x, pair_tok, pair_exp, amax)
         meta = torch.stack([pair_exp, pair_w.view(torch.int32), pair_tok], dim=1).contiguous()
-        recv_counts = torch.empty_like(send_counts)
-        dist.all_to_all_single(recv_counts, send_counts.contiguous(), group=self.group)
-        sc, rc = send_counts.tolist(), recv_counts.tolist()
-        R = sum(rc)
         rpacked = torch.empty((R, H // 2), dtype=torch.uint8, device=dev)
         rscales = torch.empty((R, H // 16), dtype=torch.uint8, device=dev)
         rmeta = torch.empty((R, 3), dtype=torch.int32, device=dev)
         dist.all_to_all_single(rpacked, packed, rc, sc, group=self.group)
         dist.all_to_all_single(rscales, scales, rc, sc, group=self.group)
         dist.all_to_all_single(rmeta, meta, rc, sc, group=self.group)
-        # groups: consecutive received rows of one source token (source rank order)
-        src = torch.repeat_interleave(torch.arange(W, device=dev),
-                                      torch.tensor(rc, device=dev))
+        # groups: consecutive received rows of one source token (source rank
+        # order); G, known from the exchange, sizes them without a read-back
+        src = torch.repeat_interleave(torch.arange(W, device=dev), recv[:, 0], output_size=R)
         tok = rmeta[:, 2]
         new = torch.ones(R, dtype=torch.bool, device=dev)
         if R > 1:
             new[1:] = (src[1:] != src[:-1]) | (tok[1:] != tok[:-1])
         gid = torch.cumsum(new.long(), 0) - 1
-        first = torch.nonzero(new).reshape(-1)
-        G = first.numel()
+        first = torch.empty(G + 1, dtype=torch.int64, device=dev)
+        first.scatter_(0, torch.where(new, gid, torch.full_like(gid, G)),
+                       torch.arange(R, device=dev))
+        first = first[:G]
         group_rows = torch.full((G, k), -1, dtype=torch.int32, device=dev)
         if R:
             slot = torch.arange(R, device=dev) - first[gid]
             group_rows[gid, slot] = torch.arange(R, dtype=torch.int32, device=dev)
-        gcount = torch.bincount(src[first], minlength=W).tolist() if R else [0] * W
         self.last_counts = (sc, rc)
         self._mark(evs)
         out, out_groups = self.engine.forward_quantized_rows(
             x, rpacked, rscales, rmeta[:, 0], rmeta[:, 1].view(torch.float32), amax, group_rows)
         self._mark(evs)
         # one partial sum per (token, destination) returns, as in the BF16 dispatch
-        d_idx, t_idx, tok_counts = self.plan(ids)
+        d_idx, t_idx = self._pairs(mask, sum(tc))
         back = torch.empty((t_idx.numel(), H), dtype=torch.bfloat16, device=dev)
-        dist.all_to_all_single(back, out_groups.to(torch.bfloat16), tok_counts.tolist(), gcount,
+        dist.all_to_all_single(back, out_groups.to(torch.bfloat16), tc, gcount,
                                group=self.group)
         pos = torch.full((T, W), -1, dtype=torch.int32, device=dev)
         pos[t_idx, d_idx] = torch.arange(t_idx.numel(), dtype=torch.int32, device=dev)
