@@ -105,6 +105,76 @@ class FakeEngine:
         return out_local, out_groups
 
 
+class CountingEngine(FakeEngine):
+    """FakeEngine with the engine's read_ints, counting the reads."""
+
+    reads = 0
+
+    def read_ints(self, t):
+        CountingEngine.reads += 1
+        return t.reshape(-1).tolist()
+
+
+def _audit_worker(rank: int, world: int, port: int, fp4: bool, q) -> None:
+    """One forward with every other host read-back entry point counted: the
+    dispatch must take its split sizes through exactly one read_ints and
+    never through tolist / item / nonzero / bincount (each of which reads
+    back to the host on a GPU)."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from glm5x_moe.ep import ExpertParallelMoE, expert_range
+        begin, count = expert_range(rank, world, E)
+        eng = CountingEngine(begin, count)
+        ep = ExpertParallelMoE(eng, rank=rank, world=world, num_experts=E, top_k=K,
+                               hidden_size=H, fp4_dispatch=fp4)
+        x = torch.randn(6 + rank, H, generator=torch.Generator().manual_seed(7 + rank))
+        x = x.to(torch.bfloat16)
+        ids, w = eng.route(x)  # the engine's own calls are not audited
+        eng.route = lambda _x, _r=(ids, w): _r
+        calls = {"tolist": 0, "item": 0, "nonzero": 0, "bincount": 0}
+        saved = (torch.Tensor.tolist, torch.Tensor.item, torch.nonzero, torch.Tensor.nonzero,
+                 torch.bincount)
+
+        def wrap(name, fn):
+            def f(*a, **kw):
+                calls[name] += 1
+                return fn(*a, **kw)
+            return f
+
+        in_read = [False]
+        orig_read = eng.read_ints
+
+        def read(t):
+            in_read[0] = True
+            try:
+                return orig_read(t)
+            finally:
+                in_read[0] = False
+        eng.read_ints = read
+        tolist = saved[0]
+
+        def counted_tolist(self_t):
+            if not in_read[0]:
+                calls["tolist"] += 1
+            return tolist(self_t)
+        torch.Tensor.tolist = counted_tolist
+        torch.Tensor.item = wrap("item", saved[1])
+        torch.nonzero = wrap("nonzero", saved[2])
+        torch.Tensor.nonzero = wrap("nonzero", saved[3])
+        torch.bincount = wrap("bincount", saved[4])
+        try:
+            CountingEngine.reads = 0
+            ep(x)
+        finally:
+            (torch.Tensor.tolist, torch.Tensor.item, torch.nonzero, torch.Tensor.nonzero,
+             torch.bincount) = saved
+        q.put((rank, CountingEngine.reads, calls))
+    finally:
+        dist.destroy_process_group()
+
+
 def _free_port() -> int:
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -200,3 +270,19 @@ def test_sync_free_pairs_match_plan(T, W, seed):
     assert counts[:W] == c_ref.tolist()
     d, t = ep._pairs(mask, sum(counts[:W]))
     assert torch.equal(d, d_ref) and torch.equal(t, t_ref)
+
+
+@pytest.mark.parametrize("fp4", [False, True])
+def test_dispatch_reads_counts_once(fp4):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_audit_worker, args=(r, 2, port, fp4, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    for rank, reads, calls in sorted(q.get(timeout=10) for _ in range(2)):
+        assert reads == 1, (rank, reads)
+        assert all(v == 0 for v in calls.values()), (rank, calls)
