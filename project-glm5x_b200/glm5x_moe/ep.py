@@ -132,6 +132,10 @@ class ExpertParallelMoE:
         H = self.hidden_size
         x = hidden.reshape(-1, H).to(torch.bfloat16).contiguous()
         T = x.shape[0]
+        if self.fp4_dispatch and T == 0:
+            # raised before this rank's first collective; the other ranks'
+            # collectives then end with the process group's timeout
+            raise ValueError("GLM5X_FP4_DISPATCH_NEEDS_LOCAL_TOKENS")
         evs = [] if self._timing else None
         self._mark(evs)
         ids, w = self.engine.route(x)
@@ -260,6 +264,8 @@ class ExpertParallelMoE:
         Device tensors go through glm5x_combine_rows; the host loop serves
         engines that return host tensors (the CPU stand-in of the gloo tests),
         it is never a substitute for the device kernel."""
+        if out.shape[0] == 0:  # a rank with no local tokens has nothing to add
+            return
         if out.is_cuda:
             from . import _native as N
             N.check(N.lib().glm5x_combine_rows(

@@ -178,6 +178,8 @@ class GLM5XMoELayer:
         T = flat.shape[0]
         ids = torch.empty((T, self.top_k), dtype=torch.int32, device=self.device)
         w = torch.empty((T, self.top_k), dtype=torch.float32, device=self.device)
+        if T == 0:  # an expert-parallel rank with no local tokens this step
+            return ids, w
         with torch.cuda.device(self.device):
             N.check(N.lib().glm5x_moe_route(self._h, flat.data_ptr(), T, ids.data_ptr(),
                                             w.data_ptr(), None, _stream()), self._h)

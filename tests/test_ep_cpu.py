@@ -5,7 +5,8 @@ The engine is a CPU stand-in with the same two calls as the GPU engine
 expert-parallel result must equal the single-process sum
 out[t] = shared(x_t) + sum_s w[t,s] * expert_{ids[t,s]}(x_t) up to the BF16
 rounding of the per-destination partial sums on their way back (2^-9
-relative each) and FP32 summation order. Covers worlds 2 and 4, ranks that receive no rows, tokens whose
+relative each) and FP32 summation order. Covers worlds 2 and 4, ranks that receive no rows, ranks with no local
+tokens (BF16 dispatch; the FP4 dispatch refuses them), tokens whose
 experts all live on one rank, uneven token counts per rank, and routes
 with empty slots (id -1, as a fixed-K routing policy leaves them), and the
 FP4 dispatch (rows quantized by their senders against the slab scales reduced
@@ -217,7 +218,11 @@ def _worker(rank: int, world: int, port: int, tokens: list[int], skew: bool, q,
                         want[t] += float(w[t, s]) * (v @ ref_eng.experts[e])
         else:
             want = ref_eng.forward_expert_rows(x, ids, w, shared_rows=x.shape[0])
-        err = float((out - want).abs().max() / want.abs().max())
+        if x.shape[0] == 0:  # a rank with no local tokens still serves the others
+            assert tuple(out.shape) == (0, H)
+            err = 0.0
+        else:
+            err = float((out - want).abs().max() / want.abs().max())
         q.put((rank, err, ep.last_counts))
     finally:
         dist.destroy_process_group()
@@ -227,6 +232,8 @@ def _worker(rank: int, world: int, port: int, tokens: list[int], skew: bool, q,
                                                         (4, [6, 1, 9, 3], False, K, False),
                                                         (2, [8, 4], True, K, False),
                                                         (4, [5, 8, 2, 7], False, 2, False),
+                                                        (2, [0, 5], False, K, False),
+                                                        (4, [4, 0, 3, 2], False, K, False),
                                                         (2, [7, 5], False, K, True),
                                                         (4, [6, 1, 9, 3], False, 3, True)])
 def test_expert_parallel_matches_single_process(world, tokens, skew, keep, fp4):
@@ -286,3 +293,13 @@ def test_dispatch_reads_counts_once(fp4):
     for rank, reads, calls in sorted(q.get(timeout=10) for _ in range(2)):
         assert reads == 1, (rank, reads)
         assert all(v == 0 for v in calls.values()), (rank, calls)
+
+
+def test_fp4_dispatch_refuses_a_rank_without_tokens():
+    """Raised on the empty rank before any collective or engine call."""
+    from glm5x_moe.ep import ExpertParallelMoE
+    ep = ExpertParallelMoE(FakeEngine(0, E), rank=0, world=2, num_experts=E, top_k=K,
+                           hidden_size=H, fp4_dispatch=True)
+    with pytest.raises(ValueError, match="NEEDS_LOCAL_TOKENS"):
+        ep(torch.zeros((0, H), dtype=torch.bfloat16))
+
