@@ -34,7 +34,9 @@ def _assert_close(got, want, what):
     assert max_rel <= MAX_REL and cos >= MIN_COS, (what, max_rel, l2, cos)
 
 
-def test_expert_rows_single_gpu():
+@pytest.mark.parametrize("shared_rows", [30, 0])
+def test_expert_rows_single_gpu(shared_rows):
+    """shared_rows = 0: only received rows, as on a rank without local tokens."""
     from glm5x_moe.layer import GLM5XMoELayer
     H, I, E, k, R = 512, 512, 8, 2, 70
     layer = GLM5XMoELayer(hidden_size=H, intermediate_size=I, num_experts=E, top_k=k,
@@ -49,7 +51,6 @@ def test_expert_rows_single_gpu():
     ids[::7, 1] = -1
     w = rng.random((R, k)).astype(np.float32) + 0.25
     rows = torch.randn(R, H, generator=torch.Generator().manual_seed(5)).to(torch.bfloat16)
-    shared_rows = 30
     out = layer.forward_expert_rows(rows.cuda(), torch.from_numpy(ids), torch.from_numpy(w),
                                     shared_rows=shared_rows).cpu().numpy()
     layer.check()
@@ -64,7 +65,9 @@ def test_expert_rows_single_gpu():
             y = O.nvfp4_expert_dequant_oracle(x[tok], deq[e][:2], deq[e][2])
             for i, (t, s) in enumerate(zip(tok, slot)):
                 want[t] += w[t, s] * y[i]
-    want[:shared_rows] += O.nvfp4_expert_dequant_oracle(x[:shared_rows], shared[:2], shared[2])
+    if shared_rows:
+        want[:shared_rows] += O.nvfp4_expert_dequant_oracle(x[:shared_rows], shared[:2],
+                                                            shared[2])
     _assert_close(out, want, "expert rows")
     layer.close()
 
