@@ -29,6 +29,13 @@ runs its experts on the rows as they are (forward_quantized_rows) and sums
 each source token's rows before the return. The result is bit-identical to
 the BF16 dispatch.
 
+Every rank takes the same collectives in the same order in every forward,
+including ranks without local tokens (both dispatches) and forwards that fail:
+the received-row count is checked against the engine's capacity
+(`max_rows`, the engine's max_tokens) on every rank, the verdict is reduced
+with MAX over the ranks together with the counts, and all ranks raise
+together before any row is exchanged.
+
 Everything runs on the caller's current stream; torch.distributed (NCCL on
 GPUs) moves the bytes. The engine is any object with route(hidden) ->
 (ids, weights) and forward_expert_rows(rows, ids, weights, shared_rows), plus
@@ -44,10 +51,15 @@ class ExpertParallelMoE:
     """Dispatch / expert / combine around one rank's engine."""
 
     def __init__(self, engine, *, rank: int, world: int, num_experts: int, top_k: int,
-                 hidden_size: int, group=None, fp4_dispatch: bool = False) -> None:
+                 hidden_size: int, group=None, fp4_dispatch: bool = False,
+                 max_rows: int | None = None) -> None:
         if num_experts % world:
             raise ValueError("GLM5X_EP_EXPERTS_NOT_DIVISIBLE")
         self.engine = engine
+        self.num_experts = num_experts
+        # local tokens + received rows one engine call takes (the engine's
+        # max_tokens); None = unbounded (host stand-in engines)
+        self.max_rows = max_rows if max_rows is not None else getattr(engine, "max_tokens", None)
         self.rank = rank
         self.world = world
         self.per = num_experts // world
@@ -128,14 +140,25 @@ class ExpertParallelMoE:
         reader = getattr(self.engine, "read_ints", None)
         return reader(t) if reader is not None else t.tolist()
 
+    def _over_capacity(self, T: int, recv_rows: torch.Tensor) -> torch.Tensor:
+        """[1] int64 on the device: 1 when some rank's local tokens plus
+        received rows exceed its engine's capacity (MAX over the ranks, so
+        every rank reads the same verdict with its counts)."""
+        limit = self.max_rows if self.max_rows is not None else 1 << 62
+        flag = (recv_rows.sum() + T > limit).to(torch.int64).reshape(1)
+        dist.all_reduce(flag, op=dist.ReduceOp.MAX, group=self.group)
+        return flag
+
+    @staticmethod
+    def _raise_over_capacity(flag: int) -> None:
+        if flag:
+            # every rank raises here, after the same collectives
+            raise ValueError("GLM5X_EP_ROWS_EXCEED_MAX_TOKENS")
+
     def __call__(self, hidden: torch.Tensor) -> torch.Tensor:
         H = self.hidden_size
         x = hidden.reshape(-1, H).to(torch.bfloat16).contiguous()
         T = x.shape[0]
-        if self.fp4_dispatch and T == 0:
-            # raised before this rank's first collective; the other ranks'
-            # collectives then end with the process group's timeout
-            raise ValueError("GLM5X_FP4_DISPATCH_NEEDS_LOCAL_TOKENS")
         evs = [] if self._timing else None
         self._mark(evs)
         ids, w = self.engine.route(x)
@@ -148,8 +171,10 @@ class ExpertParallelMoE:
         send_counts = mask.sum(dim=0)
         recv_counts = torch.empty_like(send_counts)
         dist.all_to_all_single(recv_counts, send_counts.contiguous(), group=self.group)
-        counts = self._host_ints(torch.cat([send_counts, recv_counts]))
-        sc, rc = counts[:self.world], counts[self.world:]
+        over = self._over_capacity(T, recv_counts)
+        counts = self._host_ints(torch.cat([send_counts, recv_counts, over]))
+        self._raise_over_capacity(counts[2 * self.world])
+        sc, rc = counts[:self.world], counts[self.world:2 * self.world]
         self.last_counts = (sc, rc)
         R = sum(rc)
         d_idx, t_idx = self._pairs(mask, sum(sc))
@@ -191,7 +216,10 @@ class ExpertParallelMoE:
     def _forward_fp4(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, evs):
         T, H, k, W = x.shape[0], self.hidden_size, self.top_k, self.world
         dev = x.device
-        amax = self.engine.slab_amax(x, ids)
+        if T:
+            amax = self.engine.slab_amax(x, ids)
+        else:  # no local tokens: nothing of this rank's in any slab
+            amax = torch.zeros(self.num_experts, dtype=torch.float32, device=dev)
         dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=self.group)
         # (token, slot) pairs with an expert, by destination rank, then token, then slot
         flat_ids = ids.reshape(-1).long()
@@ -208,7 +236,9 @@ class ExpertParallelMoE:
         send = torch.stack([rows_per[:W], mask.sum(dim=0)], dim=1)
         recv = torch.empty_like(send)
         dist.all_to_all_single(recv, send.contiguous(), group=self.group)
-        counts = self._host_ints(torch.cat([send.t().reshape(-1), recv.t().reshape(-1)]))
+        over = self._over_capacity(T, recv[:, 0])
+        counts = self._host_ints(torch.cat([send.t().reshape(-1), recv.t().reshape(-1), over]))
+        self._raise_over_capacity(counts[4 * W])
         sc, tc, rc, gcount = (counts[0:W], counts[W:2 * W], counts[2 * W:3 * W],
                               counts[3 * W:4 * W])
         n_pairs, R, G = sum(sc), sum(rc), sum(gcount)
@@ -216,7 +246,11 @@ class ExpertParallelMoE:
         pair_tok = (order // k).to(torch.int32)
         pair_exp = flat_ids[order].to(torch.int32)
         pair_w = w.reshape(-1)[order].float()
-        packed, scales = self.engine.quantize_rows(x, pair_tok, pair_exp, amax)
+        if n_pairs:
+            packed, scales = self.engine.quantize_rows(x, pair_tok, pair_exp, amax)
+        else:
+            packed = torch.empty((0, H // 2), dtype=torch.uint8, device=dev)
+            scales = torch.empty((0, H // 16), dtype=torch.uint8, device=dev)
         meta = torch.stack([pair_exp, pair_w.view(torch.int32), pair_tok], dim=1).contiguous()
         rpacked = torch.empty((R, H // 2), dtype=torch.uint8, device=dev)
         rscales = torch.empty((R, H // 16), dtype=torch.uint8, device=dev)
@@ -242,8 +276,13 @@ class ExpertParallelMoE:
             group_rows[gid, slot] = torch.arange(R, dtype=torch.int32, device=dev)
         self.last_counts = (sc, rc)
         self._mark(evs)
-        out, out_groups = self.engine.forward_quantized_rows(
-            x, rpacked, rscales, rmeta[:, 0], rmeta[:, 1].view(torch.float32), amax, group_rows)
+        if T or R:
+            out, out_groups = self.engine.forward_quantized_rows(
+                x, rpacked, rscales, rmeta[:, 0], rmeta[:, 1].view(torch.float32), amax,
+                group_rows)
+        else:  # nothing local, nothing received: no engine work this step
+            out = torch.empty((0, H), dtype=torch.float32, device=dev)
+            out_groups = torch.empty((0, H), dtype=torch.float32, device=dev)
         self._mark(evs)
         # one partial sum per (token, destination) returns, as in the BF16 dispatch
         d_idx, t_idx = self._pairs(mask, sum(tc))

@@ -326,9 +326,10 @@ class GLM5XMoELayer:
         out_groups = torch.empty((G, H), dtype=torch.float32, device=self.device)
         with torch.cuda.device(self.device):
             N.check(N.lib().glm5x_moe_forward_quantized_rows(
-                self._h, flat.data_ptr(), T, packed.data_ptr() if R else None,
+                self._h, flat.data_ptr() if T else None, T, packed.data_ptr() if R else None,
                 scales.data_ptr() if R else None, exp.data_ptr() if R else None,
-                wts.data_ptr() if R else None, R, amax.data_ptr(), out_local.data_ptr(),
+                wts.data_ptr() if R else None, R, amax.data_ptr(),
+                out_local.data_ptr() if T else None,
                 grp.data_ptr() if G else None, G, max(slots, 1),
                 out_groups.data_ptr() if G else None, _stream()), self._h)
         return out_local, out_groups

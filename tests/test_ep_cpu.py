@@ -6,12 +6,14 @@ expert-parallel result must equal the single-process sum
 out[t] = shared(x_t) + sum_s w[t,s] * expert_{ids[t,s]}(x_t) up to the BF16
 rounding of the per-destination partial sums on their way back (2^-9
 relative each) and FP32 summation order. Covers worlds 2 and 4, ranks that receive no rows, ranks with no local
-tokens (BF16 dispatch; the FP4 dispatch refuses them), tokens whose
+tokens (both dispatches), tokens whose
 experts all live on one rank, uneven token counts per rank, and routes
 with empty slots (id -1, as a fixed-K routing policy leaves them), and the
 FP4 dispatch (rows quantized by their senders against the slab scales reduced
 over the ranks; here with a 4-bit stand-in code and the single-process
-result built with the concatenated batch's slab scales).
+result built with the concatenated batch's slab scales), and a forward whose
+received rows exceed one rank's capacity, which every rank refuses together
+after the same collectives.
 """
 from __future__ import annotations
 
@@ -235,7 +237,9 @@ def _worker(rank: int, world: int, port: int, tokens: list[int], skew: bool, q,
                                                         (2, [0, 5], False, K, False),
                                                         (4, [4, 0, 3, 2], False, K, False),
                                                         (2, [7, 5], False, K, True),
-                                                        (4, [6, 1, 9, 3], False, 3, True)])
+                                                        (4, [6, 1, 9, 3], False, 3, True),
+                                                        (2, [0, 5], False, K, True),
+                                                        (4, [4, 0, 3, 0], False, K, True)])
 def test_expert_parallel_matches_single_process(world, tokens, skew, keep, fp4):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
@@ -295,11 +299,49 @@ def test_dispatch_reads_counts_once(fp4):
         assert all(v == 0 for v in calls.values()), (rank, calls)
 
 
-def test_fp4_dispatch_refuses_a_rank_without_tokens():
-    """Raised on the empty rank before any collective or engine call."""
-    from glm5x_moe.ep import ExpertParallelMoE
-    ep = ExpertParallelMoE(FakeEngine(0, E), rank=0, world=2, num_experts=E, top_k=K,
-                           hidden_size=H, fp4_dispatch=True)
-    with pytest.raises(ValueError, match="NEEDS_LOCAL_TOKENS"):
-        ep(torch.zeros((0, H), dtype=torch.bfloat16))
+def _capacity_worker(rank: int, world: int, port: int, fp4: bool, q) -> None:
+    """Rank 1's engine takes at most 10 rows per call; rank 0 has 12 tokens
+    with all their experts on rank 1. Every rank must raise the capacity
+    error (none may block in a collective the others skipped), and a
+    forward within capacity must still work afterwards."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from glm5x_moe.ep import ExpertParallelMoE, expert_range
+        begin, count = expert_range(rank, world, E)
+        eng = FakeEngine(begin, count)
+        eng.bias[E // 2:E // 2 + K] = 50.0  # every token's top-k on rank 1
+        ep = ExpertParallelMoE(eng, rank=rank, world=world, num_experts=E, top_k=K,
+                               hidden_size=H, fp4_dispatch=fp4,
+                               max_rows=1000 if rank == 0 else 10)
+        x = torch.randn(12 if rank == 0 else 0, H,
+                        generator=torch.Generator().manual_seed(rank)).to(torch.bfloat16)
+        raised = ""
+        try:
+            ep(x)
+        except ValueError as e:
+            raised = str(e)
+        small = torch.randn(2 if rank == 0 else 0, H,
+                            generator=torch.Generator().manual_seed(9)).to(torch.bfloat16)
+        out = ep(small)
+        q.put((rank, raised, tuple(out.shape)))
+    finally:
+        dist.destroy_process_group()
 
+
+@pytest.mark.parametrize("fp4", [False, True])
+def test_capacity_overflow_raises_on_every_rank(fp4):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_capacity_worker, args=(r, 2, port, fp4, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    res = sorted(q.get(timeout=10) for _ in range(2))
+    for rank, raised, shape in res:
+        assert "EXCEED_MAX_TOKENS" in raised, (rank, raised)
+    assert res[0][2] == (2, H) and res[1][2] == (0, H)
