@@ -29,6 +29,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <cstdio>
 #include <mutex>
 
 #include "../../include/glm5x_moe.h"
@@ -128,17 +129,23 @@ extern "C" glm5x_status glm5x_expert_major_plan_noalloc(const int32_t* ids, int6
   uint32_t* err = scratch + kOffErr;
   // weights and token amax are read but do not affect the plan; clear them
   // (with the error word) so no call reads what an earlier call left behind
-  if (cudaMemsetAsync(scratch + kOffWeights, 0, sizeof(uint32_t) * (size_t)T * k, st) !=
-          cudaSuccess ||
-      cudaMemsetAsync(scratch + kOffTokAmax, 0, sizeof(uint32_t) * (size_t)T, st) != cudaSuccess ||
-      cudaMemsetAsync(err, 0, sizeof(uint32_t), st) != cudaSuccess)
+  auto device_fail = [](const char* step, cudaError_t e) {
+    char buf[256];
+    std::snprintf(buf, sizeof buf, "expert_major_plan_noalloc: %s: %s", step,
+                  cudaGetErrorString(e));
+    set_last_error(buf);
     return GLM5X_DEVICE_ERROR;
-  if (launch_permute(ids, weights, tok_amax, (int)T, k, E, 0, 256, b, err, st) != cudaSuccess)
-    return GLM5X_DEVICE_ERROR;
+  };
+  cudaError_t e = cudaMemsetAsync(scratch + kOffWeights, 0, sizeof(uint32_t) * (size_t)T * k, st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(scratch + kOffTokAmax, 0, sizeof(uint32_t) * (size_t)T, st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(err, 0, sizeof(uint32_t), st);
+  if (e != cudaSuccess) return device_fail("clearing the scratch", e);
+  e = launch_permute(ids, weights, tok_amax, (int)T, k, E, 0, 256, b, err, st);
+  if (e != cudaSuccess) return device_fail("permutation launch", e);
   uint32_t word = 0;
-  if (cudaMemcpyAsync(&word, err, sizeof word, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
-      cudaStreamSynchronize(st) != cudaSuccess)
-    return GLM5X_DEVICE_ERROR;
+  e = cudaMemcpyAsync(&word, err, sizeof word, cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return device_fail("reading the error word", e);
   if (word) {
     set_last_error("expert_major_plan_noalloc: expert id out of range or repeated in a token");
     return GLM5X_INVALID_EXTENT;

@@ -44,6 +44,21 @@ def test_noalloc_plan_matches_allocating_plan_twice():
             assert np.array_equal(w, g)
 
 
+def test_noalloc_plan_at_its_limits_then_smaller():
+    """The advertised maxima (8192 tokens, 65536 (token, slot) pairs: the
+    whole chunk-count, rank and row-weight regions of the scratch array),
+    then a smaller multi-chunk plan that must not read the larger call's
+    leftover chunk counts."""
+    rng = np.random.default_rng(31)
+    cases = [(8192, 256, 8), (300, 256, 8)]
+    for T, E, k in cases:
+        ids = np.stack([rng.permutation(E)[:k] for _ in range(T)]).astype(np.int32)
+        want = _plan("glm5x_expert_major_plan", ids, E)
+        got = _plan("glm5x_expert_major_plan_noalloc", ids, E)
+        for w, g in zip(want, got):
+            assert np.array_equal(w, g)
+
+
 def test_noalloc_plan_rejects_oversize():
     from glm5x_moe import _native as N
     ids = torch.zeros((9000, 8), dtype=torch.int32, device="cuda")
