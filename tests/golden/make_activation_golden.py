@@ -11,6 +11,7 @@ put on sys.path for that.
 """
 from __future__ import annotations
 
+import os
 import sys
 from pathlib import Path
 
@@ -31,4 +32,7 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("GLM5X_REFERENCE_ROOT")
+    if not root:
+        sys.exit("usage: %s <reference project root> (or set GLM5X_REFERENCE_ROOT)" % sys.argv[0])
+    main(root)

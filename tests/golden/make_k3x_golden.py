@@ -13,6 +13,7 @@ tests/golden/_shims is put on sys.path for that.
 from __future__ import annotations
 
 import shutil
+import os
 import sys
 import tempfile
 from pathlib import Path
@@ -36,4 +37,7 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("GLM5X_REFERENCE_ROOT")
+    if not root:
+        sys.exit("usage: %s <reference project root> (or set GLM5X_REFERENCE_ROOT)" % sys.argv[0])
+    main(root)
