@@ -158,11 +158,62 @@ glm5x_status glm5x_moe_load_expert_mxfp4_device(glm5x_moe* moe, int32_t expert,
                                                 const glm5x_mxfp4_matrix* gate,
                                                 const glm5x_mxfp4_matrix* up,
                                                 const glm5x_mxfp4_matrix* down);
-/* Parse and admit a .pn4 / .pm4 packed sidecar
- * (GLM5XPackedExpertCache._decode_role, packed_cache.py:407-504): header
- * "<8sII" ("GLM5XPI4", 1, json_len), sorted compact JSON, payload; CRC32C of
- * every section is verified. */
+/* Parse and admit a .pn4 / .pm4 packed sidecar of the engine's precision
+ * (GLM5XPackedExpertCache.get / _decode_role, packed_cache.py:506-617,
+ * 407-504): glm5x_sidecar_open(path, engine precision, NULL) then
+ * glm5x_moe_load_expert_sidecar. */
 glm5x_status glm5x_moe_load_sidecar(glm5x_moe* moe, int32_t expert, const char* path);
+
+/* ---------------------------------------------------------------- packed sidecars */
+
+/* An open, fully checked packed expert sidecar (host memory only; no device
+ * work). Layout of GLM5XPackedExpertCache.put (packed_cache.py:327-404):
+ * header "<8sII" = ("GLM5XPI4", 1, json_len), compact sorted-key JSON
+ * {format "glm5x-<nvfp4|mxfp4>-expert-v1", source_digest, roles [gate, up,
+ * down], payload_bytes}, then the payload (per role: packed E2M1 bytes, then
+ * qparams = blocked E4M3 scales + FP32 global for NVFP4, row-major E8M0 for
+ * MXFP4). The checks run in the order of the reference's get / _decode_role
+ * (packed_cache.py:518-545, 407-423, 476-479), and the message of a failure
+ * (glm5x_last_error_message) starts with the reference's error code:
+ *   GLM5X_PACKED_CACHE_HEADER       TRUNCATED_FILE    file shorter than 16 bytes
+ *   GLM5X_PACKED_CACHE_FORMAT       BAD_MAGIC / UNSUPPORTED_VERSION / INVALID_STATE
+ *                                   (magic, version, format string vs `precision`)
+ *   GLM5X_PACKED_CACHE_METADATA     INVALID_DIRECTORY metadata not a JSON object
+ *   GLM5X_PACKED_CACHE_SOURCE_MISMATCH INVALID_STATE  source_digest differs
+ *   GLM5X_PACKED_CACHE_ROLES        INVALID_DIRECTORY roles not three complete records
+ *   GLM5X_PACKED_CACHE_PAYLOAD_EXTENT INVALID_EXTENT  payload size / a section outside it
+ *   GLM5X_PACKED_CACHE_PACKED_CRC   DATA_CRC_MISMATCH
+ *   GLM5X_PACKED_CACHE_QPARAM_CRC   AUXILIARY_CRC_MISMATCH
+ *   GLM5X_PACKED_CACHE_NVFP4_QPARAM_EXTENT INVALID_EXTENT scale + global bytes != qparams
+ * precision: GLM5X_PRECISION_NVFP4 / _MXFP4, or -1 to take the file's;
+ * source_digest: the digest get() is given, or NULL to skip that check. */
+typedef struct glm5x_sidecar glm5x_sidecar;
+
+typedef struct glm5x_sidecar_role {
+  int32_t precision;       /* glm5x_precision of the file */
+  int32_t reserved;
+  int64_t rows, cols, group_size;
+  const uint8_t* packed;   /* rows * cols / 2 bytes, inside the reader */
+  int64_t packed_bytes;
+  const uint8_t* scales;   /* NVFP4: blocked E4M3; MXFP4: row-major E8M0 */
+  int64_t scale_bytes;
+  float global_scale;      /* NVFP4; 1 for MXFP4 */
+} glm5x_sidecar_role;
+
+glm5x_status glm5x_sidecar_open(const char* path, int32_t precision, const char* source_digest,
+                                glm5x_sidecar** out);
+void glm5x_sidecar_close(glm5x_sidecar* sidecar);
+/* role 0 gate, 1 up, 2 down; the pointers stay valid until close. */
+glm5x_status glm5x_sidecar_get_role(const glm5x_sidecar* sidecar, int32_t role,
+                                    glm5x_sidecar_role* out);
+/* "<root>/layer-LLLL-expert-EEEE.<pn4|pm4>" (GLM5XPackedExpertCache._path,
+ * packed_cache.py:198-214); GLM5X_INVALID_STATE for a negative key. */
+glm5x_status glm5x_sidecar_path(const char* root, int32_t layer, int32_t expert,
+                                int32_t precision, char* buf, size_t capacity);
+/* Admits expert slot `expert` (-1 = shared) from an open sidecar of the
+ * engine's precision through glm5x_moe_load_expert_nvfp4 / _mxfp4. */
+glm5x_status glm5x_moe_load_expert_sidecar(glm5x_moe* moe, int32_t expert,
+                                           const glm5x_sidecar* sidecar);
 
 /* ---------------------------------------------------------------- .k3x containers */
 

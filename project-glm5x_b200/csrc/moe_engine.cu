@@ -793,34 +793,46 @@ glm5x_status glm5x_moe_load_expert_k3x(glm5x_moe* m, int32_t expert, const glm5x
   return glm5x_moe_load_expert_mxfp4(m, expert, &mats[0], &mats[1], &mats[2]);
 }
 
-glm5x_status glm5x_moe_load_sidecar(glm5x_moe* m, int32_t expert, const char* path) {
-  if (!m || !path) return fail_global(GLM5X_INVALID_STATE, "null argument");
-  Sidecar sc;
-  std::string msg;
-  const int rc = read_sidecar(path, &sc, &msg);
-  if (rc != 0) return m->fail(static_cast<glm5x_status>(rc), "%s", msg.c_str());
-  if (sc.precision == 0) {
+glm5x_status glm5x_moe_load_expert_sidecar(glm5x_moe* m, int32_t expert,
+                                           const glm5x_sidecar* sc) {
+  if (!m || !sc) return fail_global(GLM5X_INVALID_STATE, "null argument");
+  glm5x_sidecar_role ro[3];
+  for (int r = 0; r < 3; ++r)
+    if (glm5x_sidecar_get_role(sc, r, &ro[r]) != GLM5X_OK)
+      return m->fail(GLM5X_INVALID_STATE, "sidecar role %d unreadable", r);
+  if (ro[0].precision != m->cfg.precision)
+    return m->fail(GLM5X_INVALID_STATE, "GLM5X_PACKED_CACHE_FORMAT: sidecar is %s, engine is %s",
+                   ro[0].precision == 0 ? "NVFP4" : "MXFP4", m->mx() ? "MXFP4" : "NVFP4");
+  if (ro[0].precision == GLM5X_PRECISION_NVFP4) {
     glm5x_nvfp4_matrix mats[3];
     for (int r = 0; r < 3; ++r) {
-      const SidecarRole& ro = sc.roles[r];
-      if (ro.group_size != 16) return m->fail(GLM5X_INVALID_EXTENT, "NVFP4 group size must be 16");
-      const int64_t expect = ((ro.rows + 127) / 128) * ((ro.cols / 16 + 3) / 4) * 512;
-      if (ro.scale_bytes != expect)
+      if (ro[r].group_size != 16) return m->fail(GLM5X_INVALID_EXTENT, "NVFP4 group size must be 16");
+      const int64_t expect = ((ro[r].rows + 127) / 128) * ((ro[r].cols / 16 + 3) / 4) * 512;
+      if (ro[r].scale_bytes != expect)
         return m->fail(GLM5X_INVALID_EXTENT, "NVFP4 blocked scale size mismatch");
-      mats[r] = glm5x_nvfp4_matrix{sc.payload.data() + ro.packed_offset,
-                                   sc.payload.data() + ro.scale_offset, ro.global_scale, ro.rows,
-                                   ro.cols};
+      mats[r] = glm5x_nvfp4_matrix{ro[r].packed, ro[r].scales, ro[r].global_scale, ro[r].rows,
+                                   ro[r].cols};
     }
     return glm5x_moe_load_expert_nvfp4(m, expert, &mats[0], &mats[1], &mats[2]);
   }
   glm5x_mxfp4_matrix mats[3];
   for (int r = 0; r < 3; ++r) {
-    const SidecarRole& ro = sc.roles[r];
-    mats[r] = glm5x_mxfp4_matrix{sc.payload.data() + ro.packed_offset,
-                                 sc.payload.data() + ro.scale_offset, ro.rows, ro.cols,
-                                 ro.group_size};
+    if (ro[r].group_size <= 0 || ro[r].scale_bytes != ro[r].rows * ro[r].cols / ro[r].group_size)
+      return m->fail(GLM5X_INVALID_EXTENT, "MXFP4 scale size mismatch");
+    mats[r] = glm5x_mxfp4_matrix{ro[r].packed, ro[r].scales, ro[r].rows, ro[r].cols,
+                                 ro[r].group_size};
   }
   return glm5x_moe_load_expert_mxfp4(m, expert, &mats[0], &mats[1], &mats[2]);
+}
+
+glm5x_status glm5x_moe_load_sidecar(glm5x_moe* m, int32_t expert, const char* path) {
+  if (!m || !path) return fail_global(GLM5X_INVALID_STATE, "null argument");
+  glm5x_sidecar* sc = nullptr;
+  const glm5x_status rc = glm5x_sidecar_open(path, m->cfg.precision, nullptr, &sc);
+  if (rc != GLM5X_OK) return m->fail(rc, "%s", glm5x_last_error_message());
+  const glm5x_status st = glm5x_moe_load_expert_sidecar(m, expert, sc);
+  glm5x_sidecar_close(sc);
+  return st;
 }
 
 // ep_rows: the rows are tokens dispatched to this engine by expert-parallel
@@ -850,7 +862,9 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
                                 const PrequantRows* pq = nullptr) {
   if (pq && (pq->R < 0 || T64 + pq->R > m->cfg.max_tokens || m->mx()))
     return m->fail(GLM5X_INVALID_EXTENT, "local tokens + received rows exceed max_tokens (or MXFP4)");
-  if (T64 <= 0 || T64 > m->cfg.max_tokens)
+  // an expert-parallel rank without local tokens still runs the rows it received
+  const bool rows_only = pq && T64 == 0 && pq->R > 0;
+  if ((T64 <= 0 && !rows_only) || T64 > m->cfg.max_tokens)
     return m->fail(GLM5X_INVALID_EXTENT, "tokens %lld outside [1, %d]", (long long)T64,
                    m->cfg.max_tokens);
   if (!ep_rows && m->E_loc != m->cfg.num_experts)
@@ -1154,7 +1168,7 @@ glm5x_status glm5x_moe_forward_quantized_rows(
     const int32_t* row_expert, const float* row_weight, int64_t R, const float* amax,
     float* out_local, const int32_t* group_rows, int64_t groups, int32_t slots,
     float* out_groups, void* stream) {
-  if (!m || !hidden || !amax || !out_local ||
+  if (!m || (T > 0 && (!hidden || !out_local)) || !amax ||
       (R > 0 && (!packed || !scales || !row_expert || !row_weight)) ||
       (groups > 0 && (!group_rows || !out_groups)))
     return fail_global(GLM5X_INVALID_STATE, "null argument");

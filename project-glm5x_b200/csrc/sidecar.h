@@ -13,9 +13,11 @@ enum SidecarStatus {
   kSidecarMagic = 2,
   kSidecarVersion = 3,
   kSidecarTruncated = 7,
+  kSidecarDirectory = 8,
   kSidecarExtent = 9,
   kSidecarDataCrc = 10,
   kSidecarAuxCrc = 11,
+  kSidecarState = 16,
 };
 
 struct SidecarRole {
@@ -27,6 +29,7 @@ struct SidecarRole {
 
 struct Sidecar {
   int precision = 0;  // 0 NVFP4, 1 MXFP4
+  std::string source_digest;
   SidecarRole roles[3];  // gate, up, down
   std::vector<uint8_t> payload;
 };
@@ -34,7 +37,11 @@ struct Sidecar {
 // CRC-32C (Castagnoli), the checksum google_crc32c computes.
 uint32_t crc32c(const uint8_t* data, size_t n);
 
-// Returns a SidecarStatus (values equal k3x::ErrorCode / glm5x_status).
-int read_sidecar(const char* path, Sidecar* out, std::string* msg);
+// Reads and checks one sidecar. precision: 0 NVFP4, 1 MXFP4, -1 either (the
+// file's format string decides); source_digest: the expected source_digest,
+// or NULL for none. Returns a SidecarStatus (values equal k3x::ErrorCode /
+// glm5x_status) and, on failure, a message led by the reference's error code.
+int read_sidecar(const char* path, int precision, const char* source_digest, Sidecar* out,
+                 std::string* msg);
 
 }  // namespace glm5x

@@ -101,6 +101,16 @@ class K3xTensorInfo(ctypes.Structure):
     ]
 
 
+class SidecarRole(ctypes.Structure):
+    _fields_ = [
+        ("precision", ctypes.c_int32), ("reserved", ctypes.c_int32),
+        ("rows", ctypes.c_int64), ("cols", ctypes.c_int64), ("group_size", ctypes.c_int64),
+        ("packed", ctypes.c_void_p), ("packed_bytes", ctypes.c_int64),
+        ("scales", ctypes.c_void_p), ("scale_bytes", ctypes.c_int64),
+        ("global_scale", ctypes.c_float),
+    ]
+
+
 _P = ctypes.c_void_p
 _I32 = ctypes.c_int32
 _I64 = ctypes.c_int64
@@ -124,6 +134,11 @@ SIGNATURES = {
                                            ctypes.POINTER(Mxfp4Matrix),
                                            ctypes.POINTER(Mxfp4Matrix)],
     "glm5x_moe_load_sidecar": [_P, _I32, ctypes.c_char_p],
+    "glm5x_moe_load_expert_sidecar": [_P, _I32, _P],
+    "glm5x_sidecar_open": [ctypes.c_char_p, _I32, ctypes.c_char_p, ctypes.POINTER(_P)],
+    "glm5x_sidecar_close": [_P],
+    "glm5x_sidecar_get_role": [_P, _I32, ctypes.POINTER(SidecarRole)],
+    "glm5x_sidecar_path": [ctypes.c_char_p, _I32, _I32, _I32, ctypes.c_char_p, ctypes.c_size_t],
     "glm5x_k3x_open": [ctypes.c_char_p, _I32, ctypes.POINTER(_P)],
     "glm5x_k3x_close": [_P],
     "glm5x_k3x_tensor": [_P, ctypes.c_char_p, ctypes.POINTER(K3xTensorInfo)],
@@ -178,6 +193,7 @@ SIGNATURES = {
 _RESTYPE = {
     "glm5x_moe_destroy": None,
     "glm5x_k3x_close": None,
+    "glm5x_sidecar_close": None,
     "glm5x_moe_error_message": ctypes.c_char_p,
     "glm5x_last_error_message": ctypes.c_char_p,
 }

@@ -1,7 +1,6 @@
 """CPU tests: the C-ABI library loads, exports every declared entry point,
-rejects bad arguments before touching a device, and its host-side sidecar
-reader agrees with the reference's sidecar layout (packed_cache.py:327-404).
-No GPU compute is called here.
+and rejects bad arguments before touching a device (the sidecar reader has
+its own tests in test_sidecar.py). No GPU compute is called here.
 """
 from __future__ import annotations
 
@@ -65,41 +64,3 @@ def test_argument_validation_precedes_device_work():
     assert L.glm5x_moe_create(ctypes.byref(cfg), 0, ctypes.byref(h)) == 9
     assert L.glm5x_mxfp4_decode(None, None, 1, 30, 32, None, None) == 15
     assert L.glm5x_select_routing(None, None, 1, 256, 8, 1.0, None, None, None) == 16
-
-
-def _write_sidecar(path: Path, precision: str, roles: list[tuple[bytes, bytes, tuple[int, int]]],
-                   crc) -> None:
-    records, payload = [], bytearray()
-    for packed, qparams, shape in roles:
-        rec = {"shape": list(shape), "group_size": 16 if precision == "nvfp4" else 32,
-               "inner_k_tiles": 0, "packed_shape": [shape[0], shape[1] // 2],
-               "qparams_shape": [len(qparams)], "qparams_dtype": "uint8",
-               "packed_bytes": len(packed), "qparams_bytes": len(qparams),
-               "packed_crc32c": crc(packed), "qparams_crc32c": crc(qparams)}
-        if precision == "nvfp4":
-            rec["scale_bytes"] = len(qparams) - 4
-            rec["global_scale_bytes"] = 4
-        rec["packed_offset"] = len(payload)
-        payload.extend(packed)
-        rec["qparams_offset"] = len(payload)
-        payload.extend(qparams)
-        records.append(rec)
-    meta = {"format": f"glm5x-{precision}-expert-v1", "source_digest": "0" * 16,
-            "roles": records, "payload_bytes": len(payload)}
-    enc = json.dumps(meta, sort_keys=True, separators=(",", ":")).encode()
-    path.write_bytes(struct.pack("<8sII", b"GLM5XPI4", 1, len(enc)) + enc + bytes(payload))
-
-
-def test_sidecar_reader_rejects_corruption(tmp_path):
-    """The engine's sidecar parser runs on the host before any device work:
-    without an engine it cannot be called, so exercise the CRC path through
-    the checksum the reference uses (CRC-32C) and the reader's magic check
-    via a bad file handed to a null engine (INVALID_STATE first)."""
-    import sys
-    sys.path.insert(0, str(REPO / "tests" / "golden" / "_shims"))
-    import google_crc32c
-    assert google_crc32c.value(b"123456789") == 0xE3069283
-    from glm5x_moe import _native as N
-    p = tmp_path / "layer-0000-expert-0000.pn4"
-    _write_sidecar(p, "nvfp4", [(bytes(8), bytes(516), (1, 16))] * 3, google_crc32c.value)
-    assert N.lib().glm5x_moe_load_sidecar(None, 0, str(p).encode()) == 16
