@@ -37,6 +37,40 @@ def _scores(T, E, seed):
     return scores, bias
 
 
+LADDER = (4, 6, 8, 12, 16)
+EPS = 1e-5  # routing_policy.cpp:13 comparison_epsilon
+
+
+def _near_tie(scores, bias, natural_k, cfg, k_gpu, k_orc, tol=1e-5):
+    """True when the decision of select_routing (routing_policy.cpp:31-159)
+    for these scores sits within `tol` of a boundary, computed in double:
+    two choice scores adjacent in the natural order up to position
+    natural_k + 1 within `tol`, or, for a ladder K between the two selected
+    K, a mass / effective-support / boundary-gap test within `tol` of its
+    threshold. Only such tokens may decide differently on the device."""
+    s = np.asarray(scores, dtype=np.float64)
+    c = s + np.asarray(bias, dtype=np.float64)
+    order = np.argsort(-c, kind="stable")
+    cs = c[order[:natural_k + 1]]
+    if np.any(cs[:-1] - cs[1:] <= tol):
+        return True
+    if k_gpu == k_orc:
+        return False
+    p = s[order[:natural_k]] / s[order[:natural_k]].sum()
+    ent = -np.sum(p[p > 0] * np.log(p[p > 0]))
+    support = np.exp(ent)
+    lo, hi = min(k_gpu, k_orc), max(k_gpu, k_orc)
+    for K in LADDER:
+        if not lo <= K <= hi or K > natural_k:
+            continue
+        mass = p[:K].sum()
+        gap = 1.0 if K >= natural_k else max(p[K - 1] - p[K], 0.0) / p[0]
+        if (abs(mass + EPS - cfg.mass_target) <= tol or abs(K + EPS - support) <= tol
+                or abs(gap + EPS - cfg.minimum_boundary_gap) <= tol):
+            return True
+    return False
+
+
 @pytest.mark.parametrize("mode,kw,k", CONFIGS)
 def test_batched_select_routing(mode, kw, k):
     from glm5x_moe.routing import RoutingMode, RoutingPolicyConfig, select_routing
@@ -86,11 +120,8 @@ def test_engine_policy_routes_and_outputs():
         ids, w = res.topk_indices.numpy(), res.topk_weights.numpy()
         logits = res.router_logits.numpy()
         sel, diag = layer.routing_decisions(T)
-        agree = 0
         for t in range(T):
             s = (1.0 / (1.0 + np.exp(-logits[t].astype(np.float64)))).astype(np.float32)
-            # the device's sigmoid may differ from this host one by an ulp: compare
-            # the decision where both see the same scores
             oi, ow, ok, _, _ = O.select_routing_policy(s, bias.numpy(), k, cfg.mode.value,
                                                        fixed_k=cfg.fixed_k,
                                                        mass_target=cfg.mass_target)
@@ -98,8 +129,10 @@ def test_engine_policy_routes_and_outputs():
             assert (ids[t, kk:] == -1).all() and (w[t, kk:] == 0).all(), t
             if ok == kk and np.array_equal(oi[:kk], ids[t, :kk]):
                 assert np.allclose(ow[:kk] * 2.5, w[t, :kk], rtol=1e-5), t
-                agree += 1
-        assert agree >= 0.95 * T, (cfg, agree)
+            else:
+                # the device's sigmoid may differ from this host one by an ulp,
+                # which may only flip a decision that sits on a near-tie
+                assert _near_tie(s, bias.numpy(), k, cfg, kk, ok), (cfg, t, kk, ok)
         stats = layer.routing_stats()
         assert stats["decisions"] == T and stats["selected_experts"] == int(sel[:, 0].sum())
         if cfg.mode is RoutingMode.FIXED:
