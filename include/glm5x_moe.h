@@ -158,6 +158,22 @@ glm5x_status glm5x_moe_load_expert_mxfp4_device(glm5x_moe* moe, int32_t expert,
                                                 const glm5x_mxfp4_matrix* gate,
                                                 const glm5x_mxfp4_matrix* up,
                                                 const glm5x_mxfp4_matrix* down);
+/* BF16 expert (load_glm5x_bf16_expert's roles, runtime/include/k3x/
+ * glm5x_bundle.hpp:15-26; RawBf16MlpView, backend.hpp:129-140): gate/up [I, H]
+ * and down [H, I] BF16 row-major, host pointers, packed on the device at
+ * admission. NVFP4 engines pack each projection with quantize_nvfp4_weight
+ * (the reference's NVFP4 mode does this when it loads float experts,
+ * _quantize_expert_nvfp4, layer10_moe.py:603-619; GLM5X_SCALE_MSE is its
+ * default), bit-identical to the reference's packer; MXFP4 engines encode
+ * with encode_mxfp4, group 32 (k3x_ref/mxfp4.py:31-107). The packed bytes are
+ * then admitted as by glm5x_moe_load_expert_nvfp4 / _mxfp4. Synchronizes. */
+glm5x_status glm5x_moe_load_expert_bf16(glm5x_moe* moe, int32_t expert, const uint16_t* gate,
+                                        const uint16_t* up, const uint16_t* down,
+                                        int32_t scale_mode);
+/* Same, with the BF16 projections already in device memory. */
+glm5x_status glm5x_moe_load_expert_bf16_device(glm5x_moe* moe, int32_t expert,
+                                               const uint16_t* gate, const uint16_t* up,
+                                               const uint16_t* down, int32_t scale_mode);
 /* Parse and admit a .pn4 / .pm4 packed sidecar of the engine's precision
  * (GLM5XPackedExpertCache.get / _decode_role, packed_cache.py:506-617,
  * 407-504): glm5x_sidecar_open(path, engine precision, NULL) then
@@ -326,6 +342,62 @@ glm5x_status glm5x_moe_route(glm5x_moe* moe, const void* hidden_bf16, int64_t to
 glm5x_status glm5x_moe_forward_expert_rows(glm5x_moe* moe, const void* rows_bf16, int64_t rows,
                                            const int32_t* ids, const float* weights,
                                            int64_t shared_rows, float* out, void* stream);
+
+/* ---------------------------------------------------------------- expert parallelism */
+
+/* Expert-parallel MoE sublayer over the GPUs of one node (no counterpart in
+ * the reference, which runs every expert in one process; this is the
+ * multi-GPU form of layer10_moe.py:791-847 + 954-961, the drop-in's EP entry
+ * glm5x_moe_create_ep). One object per rank, one process per GPU: rank r of
+ * `world` holds experts [r * E/world, (r + 1) * E/world) plus a replica of the
+ * shared expert and the router (load them through glm5x_moe_ep_engine with
+ * GLOBAL expert ids). Tokens are exchanged by the library's own kernels over
+ * NVLink peer memory, mapped through CUDA IPC: each rank stores every token
+ * row once into each destination rank that holds one of its experts, and
+ * pulls each destination's weighted partial sum back (see ep_peer.cu); no
+ * host synchronization inside a forward. The result equals the NCCL
+ * all-to-all form (glm5x_moe/ep.py) bit for bit.
+ *
+ * Every rank must call glm5x_moe_ep_forward the same number of times (T may
+ * differ per rank, and may be 0); its waits on peers are bounded, and a peer
+ * that does not take part makes glm5x_moe_ep_check report
+ * GLM5X_WAIT_TIMEOUT. All ranks must have finished their last forward (e.g.
+ * a barrier) before any rank calls glm5x_moe_ep_destroy. */
+typedef struct glm5x_moe_ep glm5x_moe_ep;
+#define GLM5X_EP_HANDLE_BYTES 64
+
+/* Creates rank `rank` of `world` (<= 16) with room for max_local_tokens
+ * local tokens per forward (the receive area holds world times that). The
+ * config is the whole layer's (num_experts = all experts; expert_begin /
+ * expert_count / max_tokens are set here). Not usable until connected. */
+glm5x_status glm5x_moe_ep_create(const glm5x_moe_config* config, int device, int32_t rank,
+                                 int32_t world, int64_t max_local_tokens, glm5x_moe_ep** out);
+/* This rank's GLM5X_EP_HANDLE_BYTES-byte memory handle, for the caller to
+ * gather from every rank (any transport). */
+glm5x_status glm5x_moe_ep_handle(glm5x_moe_ep* ep, void* handle);
+/* Maps every peer's memory: handles = world * GLM5X_EP_HANDLE_BYTES bytes in
+ * rank order (this rank's own entry is not used). */
+glm5x_status glm5x_moe_ep_connect(glm5x_moe_ep* ep, const void* handles);
+/* glm5x_moe_ep_create + handle exchange over the caller's NCCL communicator
+ * (an ncclComm_t of exactly these `world` ranks, this process being `rank`;
+ * one ncclAllGather of the handles) + glm5x_moe_ep_connect. NCCL is taken
+ * from the process (the library that made `nccl_comm`), else libnccl.so.2. */
+glm5x_status glm5x_moe_create_ep(const glm5x_moe_config* config, int device, void* nccl_comm,
+                                 int32_t rank, int32_t world, int64_t max_local_tokens,
+                                 glm5x_moe_ep** out);
+/* The rank's engine (owned by the EP object): glm5x_moe_set_router,
+ * glm5x_moe_load_expert_* (global ids of the held experts, -1 = shared). */
+glm5x_moe* glm5x_moe_ep_engine(glm5x_moe_ep* ep);
+/* hidden [T, H] BF16 (device) -> out [T, H] FP32 (device) = sum over top-k
+ * of weight * expert(x) + shared(x), experts on whichever rank holds them.
+ * Asynchronous on `stream` (NULL = the EP object's stream). */
+glm5x_status glm5x_moe_ep_forward(glm5x_moe_ep* ep, const void* hidden_bf16, int64_t tokens,
+                                  float* out, void* stream);
+/* Synchronizes the device and reports the engine's and the exchange's error
+ * words (GLM5X_WAIT_TIMEOUT when a peer did not answer in time). */
+glm5x_status glm5x_moe_ep_check(glm5x_moe_ep* ep);
+const char* glm5x_moe_ep_error_message(const glm5x_moe_ep* ep);
+void glm5x_moe_ep_destroy(glm5x_moe_ep* ep);
 
 /* Expert-parallel FP4 dispatch (no counterpart in the reference, which runs
  * every expert in one process). The slab of a routed expert is every rank's

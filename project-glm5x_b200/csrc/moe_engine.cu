@@ -703,6 +703,112 @@ glm5x_status glm5x_moe_load_expert_mxfp4_device(glm5x_moe* m, int32_t expert,
   return load_mxfp4_common(m, expert, gate, up, down, true);
 }
 
+// BF16 experts packed on the device at admission. NVFP4 engines: each
+// projection through quantize_nvfp4_weight (the reference's NVFP4 mode packs
+// float experts when it loads them, _quantize_expert_nvfp4,
+// reference/glm5x_ref/layer10_moe.py:603-619; scale_mode "mse" is its
+// default, nvfp4.py:180-198). MXFP4 engines: encode_mxfp4 with group 32, as
+// GLM5XPackedExpertCache.put encodes .pm4 sidecars (packed_cache.py:256-266,
+// max_abs there). The packed bytes then take the NVFP4 / MXFP4 admission
+// path, so the resident weights are those of loading the packed expert.
+static glm5x_status load_bf16_common(glm5x_moe* m, int32_t expert, const uint16_t* gate,
+                                     const uint16_t* up, const uint16_t* down, int32_t scale_mode,
+                                     bool dev) {
+  if (!m) return fail_global(GLM5X_INVALID_STATE, "null engine");
+  if (!gate || !up || !down) return m->fail(GLM5X_INVALID_STATE, "null projection");
+  if (scale_mode != GLM5X_SCALE_MAX_ABS && scale_mode != GLM5X_SCALE_MSE)
+    return m->fail(GLM5X_INVALID_STATE, "scale_mode must be GLM5X_SCALE_MAX_ABS or _MSE");
+  const int slot = slot_of(m, expert);
+  if (slot < 0) return m->fail(GLM5X_INVALID_EXTENT, "expert %d is not held by this engine", expert);
+  cudaSetDevice(m->device);
+  const int64_t H = m->H(), I = m->I();
+  const int64_t n = I * H;  // elements of each projection
+  const uint16_t* src[3] = {gate, up, down};
+  const int64_t rows[3] = {I, I, H}, cols[3] = {H, H, I};
+  const bool mx = m->mx();
+  size_t sb[3];
+  for (int r = 0; r < 3; ++r)
+    sb[r] = mx ? (size_t)(n / 32) : (size_t)((rows[r] + 127) / 128) * ((cols[r] / 16 + 3) / 4) * 512;
+  // one scratch block: BF16 sources (host input only), packed, scales, FP32
+  // amax / globals and the error word
+  const size_t in_bytes = dev ? 0 : (size_t)3 * n * 2;
+  const size_t total = in_bytes + (size_t)3 * n / 2 + sb[0] + sb[1] + sb[2] + 256;
+  uint8_t* buf = nullptr;
+  G5_CHECK(m, cudaMalloc(&buf, total), "BF16 admission scratch");
+  struct Free {
+    uint8_t* p;
+    ~Free() { cudaFree(p); }
+  } free_buf{buf};
+  cudaStream_t st = m->stream;
+  uint8_t* cur = buf;
+  const __nv_bfloat16* d_src[3];
+  for (int r = 0; r < 3; ++r) {
+    if (dev) {
+      d_src[r] = reinterpret_cast<const __nv_bfloat16*>(src[r]);
+    } else {
+      G5_CHECK(m, cudaMemcpyAsync(cur, src[r], (size_t)n * 2, cudaMemcpyHostToDevice, st),
+               "BF16 upload");
+      d_src[r] = reinterpret_cast<const __nv_bfloat16*>(cur);
+      cur += (size_t)n * 2;
+    }
+  }
+  uint8_t* packed[3];
+  uint8_t* scales[3];
+  for (int r = 0; r < 3; ++r) {
+    packed[r] = cur;
+    cur += n / 2;
+  }
+  for (int r = 0; r < 3; ++r) {
+    scales[r] = cur;
+    cur += sb[r];
+  }
+  cur = buf + (total - 256);
+  float* amax = reinterpret_cast<float*>(cur);
+  float* globals = amax + 4;
+  uint32_t* err = reinterpret_cast<uint32_t*>(globals + 4);
+  G5_CHECK(m, cudaMemsetAsync(err, 0, 4, st), "BF16 admission");
+  for (int r = 0; r < 3; ++r) {
+    if (mx)
+      G5_CHECK(m, launch_mxfp4_encode<__nv_bfloat16>(d_src[r], n, 32, scale_mode, packed[r],
+                                                     scales[r], err, st),
+               "MXFP4 encode");
+    else
+      G5_CHECK(m, launch_nvfp4_quantize_matrix<__nv_bfloat16>(d_src[r], rows[r], cols[r],
+                                                              scale_mode, amax + r, packed[r],
+                                                              scales[r], globals + r, err, st),
+               "NVFP4 quantize");
+  }
+  float g[3] = {1.0f, 1.0f, 1.0f};
+  uint32_t word = 0;
+  G5_CHECK(m, cudaMemcpyAsync(g, globals, sizeof g, cudaMemcpyDeviceToHost, st), "globals");
+  G5_CHECK(m, cudaMemcpyAsync(&word, err, 4, cudaMemcpyDeviceToHost, st), "error word");
+  G5_CHECK(m, cudaStreamSynchronize(st), "BF16 admission");
+  if (word & (kErrBadScale | kErrNonFinite))
+    return m->fail(mx ? GLM5X_INVALID_MXFP4 : GLM5X_INVALID_STATE,
+                   "BF16 expert: non-finite weights or a scale out of range (0x%x)", word);
+  if (word) return m->fail(GLM5X_DEVICE_ERROR, "BF16 expert: device error 0x%x", word);
+  if (mx) {
+    glm5x_mxfp4_matrix mats[3];
+    for (int r = 0; r < 3; ++r) mats[r] = glm5x_mxfp4_matrix{packed[r], scales[r], rows[r], cols[r], 32};
+    return admit_mxfp4(m, slot, &mats[0], &mats[1], &mats[2], true);
+  }
+  glm5x_nvfp4_matrix mats[3];
+  for (int r = 0; r < 3; ++r) mats[r] = glm5x_nvfp4_matrix{packed[r], scales[r], g[r], rows[r], cols[r]};
+  return admit_nvfp4(m, slot, &mats[0], &mats[1], &mats[2], true);
+}
+
+glm5x_status glm5x_moe_load_expert_bf16(glm5x_moe* m, int32_t expert, const uint16_t* gate,
+                                        const uint16_t* up, const uint16_t* down,
+                                        int32_t scale_mode) {
+  return load_bf16_common(m, expert, gate, up, down, scale_mode, false);
+}
+
+glm5x_status glm5x_moe_load_expert_bf16_device(glm5x_moe* m, int32_t expert, const uint16_t* gate,
+                                               const uint16_t* up, const uint16_t* down,
+                                               int32_t scale_mode) {
+  return load_bf16_common(m, expert, gate, up, down, scale_mode, true);
+}
+
 struct glm5x_k3x {
   K3xFile file;
 };
@@ -843,6 +949,21 @@ glm5x_status glm5x_moe_load_sidecar(glm5x_moe* m, int32_t expert, const char* pa
 // shared expert); outputs the local tokens' shared-expert rows and, per
 // group of received rows (one source token), the sum of their weighted
 // expert rows.
+// Rows written into this engine's input by expert-parallel peers
+// (glm5x_moe_ep_forward): the input holds local_cap local-token rows (the
+// first local_tokens of them valid; they take the shared expert) and then
+// the received rows, whose count the device knows (recv_count) but the host
+// does not; ids of rows past it are -1. Outputs: the local tokens' rows
+// (FP32, `out`) and each received row's weighted expert sum as BF16 in
+// `partial` [rows - local_cap, H]; rows' max |x| come from their senders.
+struct PeerRows {
+  int64_t local_cap;
+  int64_t local_tokens;
+  const float* row_amax;      // [rows] (NVFP4 engines)
+  const int32_t* recv_count;  // device: received rows
+  uint16_t* partial;          // [rows - local_cap, H] BF16
+};
+
 struct PrequantRows {
   const uint8_t* packed;      // [R, H/2] E2M1 codes
   const uint8_t* scales;      // [R, H/16] E4M3, row-major
@@ -859,7 +980,8 @@ struct PrequantRows {
 static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
                                 const int32_t* ids_in, const float* w_in, float* out,
                                 cudaStream_t st, bool ep_rows = false, int64_t shared_rows = -1,
-                                const PrequantRows* pq = nullptr) {
+                                const PrequantRows* pq = nullptr,
+                                const PeerRows* peer = nullptr) {
   if (pq && (pq->R < 0 || T64 + pq->R > m->cfg.max_tokens || m->mx()))
     return m->fail(GLM5X_INVALID_EXTENT, "local tokens + received rows exceed max_tokens (or MXFP4)");
   // an expert-parallel rank without local tokens still runs the rows it received
@@ -897,7 +1019,10 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
     if (m->profiling) cudaEventRecord(m->ev[pslot][phase], st);
   };
   mark(0);
-  if (!mx) {
+  const float* row_amax = m->token_amax;
+  if (!mx && peer && peer->row_amax) {
+    row_amax = peer->row_amax;  // computed by the senders while they sent the rows
+  } else if (!mx) {
     // per-token amax for the NVFP4 slab global scales (MXFP4 has none; its
     // term kernel checks for non-finite inputs itself)
     G5_CHECK(m, launch_row_amax_bf16(x, T, H, m->token_amax, m->err, st), "row amax");
@@ -950,7 +1075,7 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
     ++launches;
   }
   int pl = 0;
-  G5_CHECK(m, launch_permute(ids, wts, m->token_amax, N, k, E_perm, hs, bn, m->pb, m->err, st,
+  G5_CHECK(m, launch_permute(ids, wts, row_amax, N, k, E_perm, hs, bn, m->pb, m->err, st,
                              m->terms(), ep_rows ? 1 : 2,
                              pq ? T : (shared_rows < 0 ? -1 : (int)std::min<int64_t>(shared_rows, T)),
                              &pl),
@@ -1063,7 +1188,17 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
              "down GEMM");
   }
   mark(8);
-  if (pq) {
+  if (peer) {
+    // local tokens: their shared-expert rows (FP32); received rows: their
+    // weighted expert sums, BF16, for the senders to pull back
+    G5_CHECK(m, launch_combine(m->y_bf16, m->pb.pos, (int)peer->local_tokens, m->kk(), H, out, st),
+             "combine");
+    G5_CHECK(m, launch_combine_rows_bf16(m->y_bf16, m->pb.pos + peer->local_cap * m->kk(),
+                                         N - peer->local_cap, peer->recv_count, m->kk(), H,
+                                         peer->partial, st),
+             "partial sums");
+    ++launches;
+  } else if (pq) {
     // local tokens: their shared-expert rows; received rows: per group
     G5_CHECK(m, launch_combine(m->y_bf16, m->pb.pos, T, 1 + hs, H, out, st), "combine");
     const int64_t n = pq->groups * pq->slots;
@@ -1090,6 +1225,33 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
   m->routed_last = ids_in == nullptr && !pq;
   return GLM5X_OK;
 }
+
+
+extern "C++" {
+namespace glm5x {
+// Expert forward over rows peers wrote into this engine's input (see
+// PeerRows); used by the expert-parallel engine in ep_peer.cu.
+glm5x_status engine_forward_peer_rows(glm5x_moe* m, const uint16_t* rows, int64_t local_cap,
+                                      int64_t local_tokens, int64_t recv_cap,
+                                      const int32_t* ids, const float* weights,
+                                      const float* row_amax, const int32_t* recv_count,
+                                      float* out_local, uint16_t* partial, cudaStream_t st) {
+  if (local_tokens < 0 || local_tokens > local_cap || recv_cap < 0)
+    return m->fail(GLM5X_INVALID_EXTENT, "peer rows: bad extents");
+  cudaSetDevice(m->device);
+  PeerRows pr{local_cap, local_tokens, row_amax, recv_count, partial};
+  return run_forward(m, rows, local_cap + recv_cap, ids, weights, out_local, st, true,
+                     local_tokens, nullptr, &pr);
+}
+
+glm5x_status engine_fail(glm5x_moe* m, glm5x_status st, const char* msg) {
+  return m->fail(st, "%s", msg);
+}
+
+int engine_device(const glm5x_moe* m) { return m->device; }
+int engine_num_sms(const glm5x_moe* m) { return m->num_sms; }
+}  // namespace glm5x
+}  // extern "C++"
 
 glm5x_status glm5x_moe_forward(glm5x_moe* m, const void* hidden, int64_t T, float* out,
                                void* stream) {

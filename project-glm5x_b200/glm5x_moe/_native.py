@@ -28,6 +28,8 @@ NUM_PHASES = 9
 PHASE_NAMES = ["row_amax", "router_logits", "topk", "permute", "act_quantize", "gate_up_gemm",
                "h_quantize", "down_gemm", "combine"]
 
+EP_HANDLE_BYTES = 64
+
 PRECISION_NVFP4 = 0
 PRECISION_MXFP4 = 1
 SCALE_MAX_ABS = 0
@@ -134,6 +136,8 @@ SIGNATURES = {
                                            ctypes.POINTER(Mxfp4Matrix),
                                            ctypes.POINTER(Mxfp4Matrix)],
     "glm5x_moe_load_sidecar": [_P, _I32, ctypes.c_char_p],
+    "glm5x_moe_load_expert_bf16": [_P, _I32, _P, _P, _P, _I32],
+    "glm5x_moe_load_expert_bf16_device": [_P, _I32, _P, _P, _P, _I32],
     "glm5x_moe_load_expert_sidecar": [_P, _I32, _P],
     "glm5x_sidecar_open": [ctypes.c_char_p, _I32, ctypes.c_char_p, ctypes.POINTER(_P)],
     "glm5x_sidecar_close": [_P],
@@ -160,6 +164,17 @@ SIGNATURES = {
     "glm5x_verify_greedy_target_blocks": [_P, _P, _P, _P, _I64, _I32, ctypes.c_uint32, _P, _P,
                                           _P, _P],
     "glm5x_moe_last_routing": [_P, _P, _P, _P, _I64],
+    "glm5x_moe_ep_create": [ctypes.POINTER(MoeConfig), ctypes.c_int, _I32, _I32, _I64,
+                            ctypes.POINTER(_P)],
+    "glm5x_moe_ep_handle": [_P, _P],
+    "glm5x_moe_ep_connect": [_P, _P],
+    "glm5x_moe_create_ep": [ctypes.POINTER(MoeConfig), ctypes.c_int, _P, _I32, _I32, _I64,
+                            ctypes.POINTER(_P)],
+    "glm5x_moe_ep_engine": [_P],
+    "glm5x_moe_ep_forward": [_P, _P, _I64, _P, _P],
+    "glm5x_moe_ep_check": [_P],
+    "glm5x_moe_ep_error_message": [_P],
+    "glm5x_moe_ep_destroy": [_P],
     "glm5x_moe_check": [_P],
     "glm5x_moe_get_stats": [_P, ctypes.POINTER(MoeStats)],
     "glm5x_moe_debug_buffer": [_P, _I32, ctypes.POINTER(_P), ctypes.POINTER(ctypes.c_size_t)],
@@ -194,6 +209,9 @@ _RESTYPE = {
     "glm5x_moe_destroy": None,
     "glm5x_k3x_close": None,
     "glm5x_sidecar_close": None,
+    "glm5x_moe_ep_destroy": None,
+    "glm5x_moe_ep_engine": ctypes.c_void_p,
+    "glm5x_moe_ep_error_message": ctypes.c_char_p,
     "glm5x_moe_error_message": ctypes.c_char_p,
     "glm5x_last_error_message": ctypes.c_char_p,
 }

@@ -82,7 +82,29 @@ class GLM5XMoELayer:
         self.max_tokens = max_tokens
         self._in_flight: dict[int, tuple[torch.Tensor, torch.Tensor]] = {}
 
+    @classmethod
+    def _borrow(cls, handle: int, *, hidden_size: int, intermediate_size: int, num_experts: int,
+                top_k: int, has_shared: bool, max_tokens: int, device: int) -> "GLM5XMoELayer":
+        """A view of an engine another object owns (the engine of an
+        expert-parallel rank): weights and router go through it; close()
+        leaves the engine to its owner."""
+        self = cls.__new__(cls)
+        self._h = ctypes.c_void_p(handle)
+        self._owned = False
+        self.device = torch.device("cuda", device)
+        self.hidden_size = hidden_size
+        self.intermediate_size = intermediate_size
+        self.num_experts = num_experts
+        self.top_k = top_k
+        self.has_shared = has_shared
+        self.max_tokens = max_tokens
+        self._in_flight = {}
+        return self
+
     def close(self) -> None:
+        if getattr(self, "_h", None) and not getattr(self, "_owned", True):
+            self._h = None
+            return
         if getattr(self, "_h", None):
             # destroy synchronizes every stream before the host buffers go
             N.lib().glm5x_moe_destroy(self._h)
@@ -115,6 +137,31 @@ class GLM5XMoELayer:
             torch.cuda.current_stream().synchronize()
             N.check(fn(self._h, expert_id, ctypes.byref(g), ctypes.byref(u), ctypes.byref(d)),
                     self._h)
+
+    def load_expert_bf16(self, expert_id: int, gate_proj: torch.Tensor, up_proj: torch.Tensor,
+                         down_proj: torch.Tensor, *, scale_mode: str = "mse") -> None:
+        """Admit a float expert (gate/up [I, H], down [H, I]) packed on the
+        device at admission: NVFP4 layers pack each projection with the
+        reference's quantize_nvfp4_weight semantics (_quantize_expert_nvfp4,
+        layer10_moe.py:603-619), MXFP4 layers with encode_mxfp4 (group 32)."""
+        mode = {"max_abs": N.SCALE_MAX_ABS, "mse": N.SCALE_MSE}[scale_mode]
+        mats = [t.detach().to(dtype=torch.bfloat16).contiguous()
+                for t in (gate_proj, up_proj, down_proj)]
+        I, H = self.intermediate_size, self.hidden_size
+        if (tuple(mats[0].shape) != (I, H) or tuple(mats[1].shape) != (I, H)
+                or tuple(mats[2].shape) != (H, I)):
+            raise ValueError("GLM5X_EXPERT_WEIGHT_SHAPE_MISMATCH")
+        on_device = all(m.is_cuda for m in mats)
+        if on_device:
+            mats = [m.to(self.device) for m in mats]
+        else:
+            mats = [m.cpu() for m in mats]
+        fn = (N.lib().glm5x_moe_load_expert_bf16_device if on_device
+              else N.lib().glm5x_moe_load_expert_bf16)
+        with torch.cuda.device(self.device):
+            torch.cuda.current_stream().synchronize()
+            N.check(fn(self._h, expert_id, mats[0].data_ptr(), mats[1].data_ptr(),
+                       mats[2].data_ptr(), mode), self._h)
 
     def load_expert_k3x(self, expert_id: int, k3x_file, prefix: str) -> None:
         """Admit expert ``expert_id`` (-1 = shared) from the MXFP4 records
