@@ -428,6 +428,19 @@ def build_ep_layer(T: int, local: int, rank: int, world: int, experts: int = E,
                           max_tokens=T * (2 * K_TOP + 1 if fp4_dispatch else world + 1),
                           device=local, expert_begin=begin,
                           expert_count=count)
+    load_ep_weights(layer, rank, world, experts, dev)
+    return layer
+
+
+def load_ep_weights(layer, rank: int, world: int, experts: int, dev) -> None:
+    """Experts [rank * E/W, (rank + 1) * E/W) + the shared expert and the full
+    router into this rank's engine; expert e's weights come from its own seed,
+    so every rank holds the same model."""
+    import torch
+    from glm5x_moe.ep import expert_range
+    from glm5x_moe.layer import NVFP4Expert
+    from glm5x_moe.nvfp4 import quantize_nvfp4_weight
+    begin, count = expert_range(rank, world, experts)
     for e in list(range(begin, begin + count)) + [-1]:
         g = torch.Generator(device=dev).manual_seed(7000 + e)
         mats = [quantize_nvfp4_weight((torch.randn(shape, generator=g, device=dev) * 0.02)
@@ -440,7 +453,6 @@ def build_ep_layer(T: int, local: int, rank: int, world: int, experts: int = E,
     bias = torch.rand(experts, generator=gc) * 0.2 - 0.1
     layer.set_router(router, bias)
     torch.cuda.synchronize(dev)
-    return layer
 
 
 def run_ours_ep(args, world: int, rank: int, local: int) -> None:
@@ -456,11 +468,21 @@ def run_ours_ep(args, world: int, rank: int, local: int) -> None:
     stream = torch.cuda.Stream(device=dev)
     torch.cuda.set_stream(stream)
     fp4 = args.dispatch == "fp4"
-    layer = build_ep_layer(T, local, rank, world, experts, fp4_dispatch=fp4)
+    peer = args.dispatch == "peer"
+    if peer:
+        # the token exchange in the library's kernels over NVLink peer memory
+        from glm5x_moe.ep_peer import PeerExpertParallelMoE
+        ep = PeerExpertParallelMoE(rank=rank, world=world, max_local_tokens=T, hidden_size=H,
+                                   intermediate_size=I, num_experts=experts, top_k=K_TOP,
+                                   routed_scaling_factor=SCALE, device=local)
+        layer = ep.engine
+        load_ep_weights(layer, rank, world, experts, dev)
+    else:
+        layer = build_ep_layer(T, local, rank, world, experts, fp4_dispatch=fp4)
+        ep = ExpertParallelMoE(layer, rank=rank, world=world, num_experts=experts, top_k=K_TOP,
+                               hidden_size=H, fp4_dispatch=fp4)
     if args.tile_n:
         layer.set_tile_n(args.tile_n)
-    ep = ExpertParallelMoE(layer, rank=rank, world=world, num_experts=experts, top_k=K_TOP,
-                           hidden_size=H, fp4_dispatch=fp4)
     hidden = make_hidden(T, seed=100 + rank, device=dev)
     for _ in range(args.warmup):
         ep(hidden)
@@ -484,16 +506,23 @@ def run_ours_ep(args, world: int, rank: int, local: int) -> None:
         torch.cuda.synchronize()
         torch.cuda.nvtx.range_pop()
     layer.check()
+    if peer:
+        ep.check()
     ms_total = start.elapsed_time(stop)
     launches = layer.stats()["kernel_launches"] - stats0["kernel_launches"]
+    if peer:
+        launches += 7 * args.steps  # plan, exchange, tail clear, dispatch, wait, ready, combine
     # phase and stage split from further steps with the events on (they add
     # about 2.5 us each, so the timed steps ran without them)
-    ep.set_timing(True)
-    ep.stage_times()
+    if not peer:
+        ep.set_timing(True)
+        ep.stage_times()
     phases, nprof = profiled_phases(ep, hidden, args.steps, engine=layer)
-    stages, nst = ep.stage_times()
-    ep.set_timing(False)
-    stages = {k: v / max(nst, 1) for k, v in stages.items()}
+    stages = None
+    if not peer:
+        stages, nst = ep.stage_times()
+        ep.set_timing(False)
+        stages = {k: v / max(nst, 1) for k, v in stages.items()}
     t = torch.tensor([ms_total], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_total = float(t.item())
@@ -558,8 +587,11 @@ def run_ours_ep(args, world: int, rank: int, local: int) -> None:
                                    f"experts top-8 + 1 shared, expert parallel: {experts // world}"
                                    " experts per GPU",
                        "global_batch": world * T, "tokens_per_rank": T,
-                       "parallelism": f"ep{world} (NCCL all-to-all dispatch / combine, "
-                                      f"{'NVFP4' if fp4 else 'BF16'} dispatch)",
+                       "parallelism": (f"ep{world} (token rows stored into and partial sums "
+                                       "loaded from peers' memory over NVLink by the library's "
+                                       "kernels, BF16)") if peer else
+                                      (f"ep{world} (NCCL all-to-all dispatch / combine, "
+                                       f"{'NVFP4' if fp4 else 'BF16'} dispatch)"),
                        "l2": "inputs larger than L2"},
             "phases_ms": phases, "ep_stages_ms": stages,
             "roofline": {"bound": "tensor", "kernel": "gate_up_gemm (rank 0)",
@@ -572,12 +604,17 @@ def run_ours_ep(args, world: int, rank: int, local: int) -> None:
             "e2e": {"value": world * T / (e2e_ms / 1000.0), "unit": "tokens/s",
                     "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 4,
                     "ms_per_step": e2e_ms,
-                    "api": "ExpertParallelMoE on each rank; pinned host BF16 in, FP32 out, "
-                           "upload / forward / download of consecutive steps on three "
+                    "api": f"{type(ep).__name__} on each rank; pinned host BF16 in, FP32 "
+                           "out, upload / forward / download of consecutive steps on three "
                            "streams"},
         }
         print(json.dumps(line), flush=True)
-    layer.close()
+    dist.barrier()
+    torch.cuda.synchronize()
+    if peer:
+        ep.close()  # after the barrier: no peer still writes into this rank's memory
+    else:
+        layer.close()
     dist.barrier()
     dist.destroy_process_group()
 
@@ -759,8 +796,9 @@ def main() -> None:
     ap.add_argument("--experts", type=int, default=0, help="override experts (profiling only)")
     ap.add_argument("--decode-experts", type=int, default=0,
                     help="with --decode-only: fewer experts (small profiling captures only)")
-    ap.add_argument("--dispatch", default="bf16", choices=["bf16", "fp4"],
-                    help="expert-parallel token rows as BF16 or as sender-quantized NVFP4")
+    ap.add_argument("--dispatch", default="bf16", choices=["bf16", "fp4", "peer"],
+                    help="expert-parallel exchange: NCCL all-to-all of BF16 or of "
+                         "sender-quantized NVFP4 rows, or the library's peer-memory kernels")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

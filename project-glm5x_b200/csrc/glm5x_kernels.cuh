@@ -211,6 +211,12 @@ cudaError_t launch_store_ints_to_host(const int64_t* src, int64_t n, int64_t* ds
 cudaError_t launch_combine(const uint16_t* y, const int32_t* pos, int T, int kk, int H,
                            float* out, cudaStream_t st, int accumulate = 0);
 
+// Expert-parallel received rows: out[r] = BF16 of the slot sum (as
+// launch_combine) for r < *count (device), r < cap; grid-stride.
+cudaError_t launch_combine_rows_bf16(const uint16_t* y, const int32_t* pos, int64_t cap,
+                                     const int32_t* count, int kk, int H, uint16_t* out,
+                                     cudaStream_t st);
+
 // ------------------------------------------------------------ weights.cu
 // Interleave gate [I, K] and up [I, K] (packed NVFP4 + blocked scales) into
 // the stacked gate/up weight slot: 16 gate rows then 16 up rows per 32.

@@ -94,6 +94,54 @@ __global__ void combine_kernel(const uint16_t* __restrict__ y, const int32_t* __
   }
 }
 
+// Received rows of an expert-parallel engine: partial[r] = BF16(sum over the
+// row's slots of y[pos[r, s]]) for r < *count (a device value), FP32 sums in
+// slot order then one round to nearest even. Grid-stride over rows, so the
+// launch is sized by the capacity and the count is read on the device.
+__global__ void combine_rows_bf16_kernel(const uint16_t* __restrict__ y,
+                                         const int32_t* __restrict__ pos, int64_t cap,
+                                         const int32_t* __restrict__ count, int kk, int H,
+                                         uint16_t* __restrict__ out) {
+  const int64_t n = cap < (int64_t)*count ? cap : (int64_t)*count;
+  __shared__ int32_t rows[32];
+  for (int64_t r = blockIdx.x; r < n; r += gridDim.x) {
+    __syncthreads();
+    if (threadIdx.x < kk) rows[threadIdx.x] = pos[r * kk + threadIdx.x];
+    __syncthreads();
+    for (int v = threadIdx.x; v < H / 8; v += blockDim.x) {
+      float acc[8] = {};
+      for (int s = 0; s < kk; ++s) {
+        if (rows[s] < 0) continue;
+        const uint4 q = __ldg(reinterpret_cast<const uint4*>(y + (int64_t)rows[s] * H) + v);
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          acc[2 * i] += __uint_as_float(w[i] << 16);
+          acc[2 * i + 1] += __uint_as_float(w[i] & 0xffff0000u);
+        }
+      }
+      uint32_t o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t lo = __bfloat16_as_ushort(__float2bfloat16_rn(acc[2 * i]));
+        const uint32_t hi = __bfloat16_as_ushort(__float2bfloat16_rn(acc[2 * i + 1]));
+        o[i] = lo | (hi << 16);
+      }
+      reinterpret_cast<uint4*>(out + r * H)[v] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
+cudaError_t launch_combine_rows_bf16(const uint16_t* y, const int32_t* pos, int64_t cap,
+                                     const int32_t* count, int kk, int H, uint16_t* out,
+                                     cudaStream_t st) {
+  if (cap <= 0) return cudaSuccess;
+  if (kk > 32 || H % 8) return cudaErrorInvalidValue;
+  const unsigned blocks = (unsigned)std::min<int64_t>(cap, 148 * 8);
+  combine_rows_bf16_kernel<<<blocks, 256, 0, st>>>(y, pos, cap, count, kk, H, out);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_interleave_gate_up(const uint8_t* gate_packed, const uint8_t* gate_sf,
                                       const uint8_t* up_packed, const uint8_t* up_sf, int I,
                                       int K, int group, uint8_t* dst_packed, uint8_t* dst_sf,

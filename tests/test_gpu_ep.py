@@ -8,8 +8,11 @@ test_expert_parallel_two_gpus: two ranks (one process per GPU, NCCL) each
 hold half the experts, exchange tokens with glm5x_moe.ep, and must match the
 oracle of the same layer (routed-expert slabs across ranks, shared-expert
 slab per rank) within the north-star tolerance (needs 2 GPUs); the FP4
-dispatch must give the same bits as the BF16 dispatch (one GPU: the same
-with a single rank).
+dispatch and the peer-memory layer (glm5x_moe_ep_*, PeerExpertParallelMoE:
+rows stored into and partial sums pulled from the peers' memory by the
+library's kernels) must give the same bits as the BF16 all-to-all dispatch,
+over several forwards (both buffer parities) and with a rank that has no
+local tokens (one GPU: the same with a single rank).
 """
 from __future__ import annotations
 
@@ -127,6 +130,25 @@ def _ep_worker(rank, world, port, q):
         torch.cuda.synchronize(rank)
         ep_layer.check()
         fp4_equal = bool(np.array_equal(got, got4))
+        # the peer-memory layer: same experts, same router, same bits, on
+        # three forwards (parities 1, 0, 1), the middle one with rank 0 empty
+        from glm5x_moe.ep_peer import PeerExpertParallelMoE
+        peer = PeerExpertParallelMoE(rank=rank, world=world, max_local_tokens=max(tokens),
+                                     hidden_size=H, intermediate_size=I, num_experts=E,
+                                     top_k=k, device=rank)
+        for e in list(range(begin, begin + count)) + [-1]:
+            ex, _ = make_expert(H, I, 5000 + e, device=f"cuda:{rank}")
+            peer.engine.load_expert(e, ex)
+        peer.engine.set_router(router, bias)
+        x_b = x[:0] if rank == 0 else x
+        want_b = ep(x_b).cpu().numpy()
+        peer_equal = []
+        for xi, ref in ((x, got), (x_b, want_b), (x, got)):
+            out_p = peer(xi).cpu().numpy()
+            peer.check()
+            peer_equal.append(bool(np.array_equal(out_p, ref)))
+        dist.barrier()
+        peer.close()
         # Oracle with the parallel layer's slabs: a routed expert's slab holds
         # every rank's tokens routed to it (the same slab as one GPU running
         # the concatenated batch); the shared expert's slab is the rank's own
@@ -142,7 +164,7 @@ def _ep_worker(rank, world, port, q):
         want = routed[off:off + T] + O.nvfp4_expert_dequant_oracle(bf16_to_np(xs[rank]),
                                                                    shared[:2], shared[2])
         max_rel, l2, cos = O.relative_error(got, want)
-        q.put((rank, max_rel, cos, ep.last_counts, fp4_equal, ep4.last_counts))
+        q.put((rank, max_rel, cos, ep.last_counts, fp4_equal, ep4.last_counts, peer_equal))
         full.close()
         ep_layer.close()
     finally:
@@ -161,10 +183,11 @@ def _run_ep(world):
         p.join(timeout=300)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     for _ in range(world):
-        rank, max_rel, cos, counts, fp4_equal, counts4 = q.get(timeout=10)
+        rank, max_rel, cos, counts, fp4_equal, counts4, peer_equal = q.get(timeout=10)
         assert max_rel <= MAX_REL and cos >= MIN_COS, (rank, max_rel, cos, counts)
         assert sum(counts[1]) > 0 and sum(counts4[1]) > 0, (counts, counts4)
         assert fp4_equal, rank
+        assert all(peer_equal), (rank, peer_equal)
 
 
 def test_expert_parallel_fp4_dispatch_one_gpu():

@@ -163,7 +163,7 @@ def test_c3_full_layer_256_experts():
     x = bf16_to_np(hidden)
     ids_g, w_g = res.topk_indices.numpy(), res.topk_weights.numpy()
     _check_routes(x, router, bias, ids_g, w_g, res.router_logits.numpy())
-    assert len(np.unique(ids_g)) > 200  # the grid really spans the experts
+    assert len(np.unique(ids_g)) > 150  # the grid really spans the experts
     deq = _LazyDequant(experts, "nvfp4")
     want, _ = oracle_forward(x, ids_g, w_g, deq, deq[-1])
     _assert_close(res.output.cpu().numpy(), want, "c3 layer")

@@ -16,7 +16,7 @@ from sidecar_fixture import mxfp4_role, nvfp4_role, write_sidecar
 
 pytestmark = pytest.mark.gpu
 
-H, I, E, K, T = 512, 512, 8, 2, 40
+H, I, E, K, T = 512, 512, 16, 2, 40
 DIGEST = "glm5x-b200-gpu-sidecar-test"
 
 
