@@ -569,6 +569,7 @@ def run_ours_ep(args, world: int, rank: int, local: int) -> None:
     t = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_ms = float(t.item())
+    host_link = measure_host_link(T * H * 4, world, rank, dev)
     # per-rank gate/up GEMM rate: its routed assignments + the shared rows
     g1 = torch.tensor([phases["gate_up_gemm"]], device=dev)
     gemm1_flop = 2.0 * (local_assign + T) * (2 * I) * H
@@ -606,17 +607,138 @@ def run_ours_ep(args, world: int, rank: int, local: int) -> None:
                     "ms_per_step": e2e_ms,
                     "api": f"{type(ep).__name__} on each rank; pinned host BF16 in, FP32 "
                            "out, upload / forward / download of consecutive steps on three "
-                           "streams"},
+                           "streams",
+                    "host_link": host_link},
         }
-        print(json.dumps(line), flush=True)
     dist.barrier()
     torch.cuda.synchronize()
     if peer:
         ep.close()  # after the barrier: no peer still writes into this rank's memory
     else:
         layer.close()
+    torch.cuda.empty_cache()
+    dist.barrier()
+    decode = None
+    if not args.no_decode:
+        decode = run_decode_c4_ep(args, world, rank, local)
+    if rank == 0:
+        if decode is not None:
+            line["decode"] = decode
+        print(json.dumps(line), flush=True)
     dist.barrier()
     dist.destroy_process_group()
+
+
+def measure_host_link(nbytes: int, world: int, rank: int, dev) -> dict:
+    """Pinned device-to-host copy rate of one step's FP32 output, each rank
+    alone (the others wait at a barrier) and all ranks at once: the bound of
+    the end-to-end figure, which downloads this much per rank per step."""
+    import torch
+    import torch.distributed as dist
+    src = torch.empty(nbytes // 4, dtype=torch.float32, device=dev)
+    dst = torch.empty(nbytes // 4, dtype=torch.float32).pin_memory()
+    st = torch.cuda.Stream(device=dev)
+
+    def timed(reps: int = 3) -> float:
+        with torch.cuda.stream(st):
+            dst.copy_(src, non_blocking=True)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            for _ in range(reps):
+                dst.copy_(src, non_blocking=True)
+            e1.record(st)
+        e1.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    mine_alone = 0.0
+    for r in range(world):
+        dist.barrier()
+        if r == rank:
+            mine_alone = timed()
+    dist.barrier()
+    together = timed()
+    t = torch.tensor([together, mine_alone], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return {"d2h_bytes": nbytes, "alone_gbs": nbytes / (float(t[1]) / 1e3) / 1e9,
+            "all_ranks_gbs_per_rank": nbytes / (float(t[0]) / 1e3) / 1e9,
+            "note": "pinned D2H of one step's FP32 output per rank; alone = slowest rank "
+                    "copying with the others idle, all_ranks = slowest rank with every rank "
+                    "copying at once"}
+
+
+def run_decode_c4_ep(args, world: int, rank: int, local: int) -> dict | None:
+    """Config 4 under expert parallelism: the MXFP4 layer (256 experts +
+    shared, Zipf-skewed router) at a decode batch of 64 tokens split over the
+    ranks (64 / W each; strong scaling of the step), experts sharded E / W per
+    GPU, tokens exchanged by the peer-memory kernels. HBM-bound: a rank
+    streams its touched local experts + the shared expert."""
+    import torch
+    import torch.distributed as dist
+    from glm5x_moe.ep import expert_range
+    from glm5x_moe.ep_peer import PeerExpertParallelMoE
+    from glm5x_moe.layer import MXFP4Expert
+    from glm5x_moe.nvfp4 import quantize_mxfp4_weight
+    dev = torch.device("cuda", local)
+    Tall = 64
+    Tr = Tall // world
+    experts = E
+    ep = PeerExpertParallelMoE(rank=rank, world=world, max_local_tokens=Tr, hidden_size=H,
+                               intermediate_size=I, num_experts=experts, top_k=K_TOP,
+                               routed_scaling_factor=SCALE, precision="mxfp4", device=local)
+    begin, count = expert_range(rank, world, experts)
+    for e in list(range(begin, begin + count)) + [-1]:
+        g = torch.Generator(device=dev).manual_seed(9000 + e)
+        mats = [quantize_mxfp4_weight((torch.randn(shape, generator=g, device=dev) * 0.02)
+                                      .to(torch.bfloat16))
+                for shape in ((I, H), (I, H), (H, I))]
+        ep.engine.load_expert(e, MXFP4Expert(*mats))
+        del mats
+    gc = torch.Generator(device="cpu").manual_seed(5)
+    router = (torch.randn(experts, H, generator=gc) * 0.02).to(torch.bfloat16)
+    ep.engine.set_router(router, zipf_bias(experts, 6))
+    hidden_all = torch.randn(Tall, H, generator=gc).to(torch.bfloat16).to(dev)
+    hidden = hidden_all[rank * Tr:(rank + 1) * Tr].contiguous()
+    ids, _ = ep.engine.route(hidden_all)
+    touched = torch.unique(ids)
+    held = int(((touched >= begin) & (touched < begin + count)).sum().item())
+    for _ in range(args.warmup):
+        ep(hidden)
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    steps = max(args.steps, 20)
+    e0.record()
+    for _ in range(steps):
+        ep(hidden)
+    e1.record()
+    torch.cuda.synchronize()
+    ep.check()
+    ms = e0.elapsed_time(e1) / steps
+    bytes_rank = (held + 1) * MXFP4_EXPERT_BYTES + experts * H * 2 + Tr * H * 6
+    t = torch.tensor([ms, float(bytes_rank), float(held)], device=dev)
+    tmax = t.clone()
+    dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+    tsum = t.clone()
+    dist.all_reduce(tsum, op=dist.ReduceOp.SUM)
+    dist.barrier()
+    torch.cuda.synchronize()
+    ep.close()
+    torch.cuda.empty_cache()
+    ms_max, bytes_max = float(tmax[0]), float(tmax[1])
+    hbm = peaks()["hbm_gbs"]
+    return {
+        "workload": (f"c4: GLM-5 MoE layer, MXFP4 experts (E2M1 + E8M0/32), decode batch "
+                     f"{Tall} split {Tr} per rank, {experts} experts + shared, Zipf(1.1)-skewed "
+                     f"router bias, expert parallel over {world} GPUs ({count} experts each), "
+                     "peer-memory exchange"),
+        "tokens_per_s": Tall / (ms_max / 1000.0), "ms_per_step": ms_max,
+        "experts_touched": int(touched.numel()), "max_local_experts_touched": int(tmax[2]),
+        "roofline": {"bound": "hbm", "kernel": "whole layer step, busiest rank",
+                     "achieved": bytes_max / (ms_max / 1000.0) / 1e9, "peak": hbm,
+                     "unit": "GB/s", "frac": bytes_max / (ms_max / 1000.0) / 1e9 / hbm,
+                     "algorithmic_bytes_busiest_rank": bytes_max,
+                     "algorithmic_bytes_all_ranks": float(tsum[1])},
+    }
 
 
 def run_ours(args) -> None:

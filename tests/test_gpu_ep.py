@@ -123,6 +123,7 @@ def _ep_worker(rank, world, port, q):
         got = ep(x).cpu().numpy()
         torch.cuda.synchronize(rank)
         ep_layer.check()
+        counts = ep.last_counts
         # FP4 dispatch: the same slabs, so the same bits
         ep4 = ExpertParallelMoE(ep_layer, rank=rank, world=world, num_experts=E, top_k=k,
                                 hidden_size=H, fp4_dispatch=True)
@@ -164,7 +165,7 @@ def _ep_worker(rank, world, port, q):
         want = routed[off:off + T] + O.nvfp4_expert_dequant_oracle(bf16_to_np(xs[rank]),
                                                                    shared[:2], shared[2])
         max_rel, l2, cos = O.relative_error(got, want)
-        q.put((rank, max_rel, cos, ep.last_counts, fp4_equal, ep4.last_counts, peer_equal))
+        q.put((rank, max_rel, cos, counts, fp4_equal, ep4.last_counts, peer_equal))
         full.close()
         ep_layer.close()
     finally:

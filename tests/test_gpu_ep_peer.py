@@ -54,7 +54,7 @@ def test_peer_ep_single_rank_matches_oracle(precision):
 def test_peer_ep_rejects_bad_arguments():
     from glm5x_moe._native import Glm5xError
     from glm5x_moe.ep_peer import PeerExpertParallelMoE
-    with pytest.raises(Glm5xError, match="divisible"):
+    with pytest.raises(ValueError, match="DIVISIBLE"):
         PeerExpertParallelMoE(rank=0, world=3, max_local_tokens=8, hidden_size=H,
                               intermediate_size=I, num_experts=E, top_k=K)
     ep = PeerExpertParallelMoE(rank=0, world=1, max_local_tokens=8, hidden_size=H,
