@@ -575,7 +575,7 @@ def run_ours_ep(args, world: int, rank: int, local: int) -> None:
     gemm1_flop = 2.0 * (local_assign + T) * (2 * I) * H
     if rank == 0:
         pk = peaks()
-        fp4_peak = 4.0 * pk["bf16_sustained"]
+        fp4_peak = 4.0 * pk["bf16"]
         achieved = gemm1_flop / (phases["gate_up_gemm"] / 1000.0) / 1e12
         line = {
             "metric": "NVFP4 MoE-layer tokens/s", "value": value, "unit": "tokens/s",
@@ -598,7 +598,7 @@ def run_ours_ep(args, world: int, rank: int, local: int) -> None:
             "roofline": {"bound": "tensor", "kernel": "gate_up_gemm (rank 0)",
                          "achieved": achieved, "peak": fp4_peak, "unit": "TFLOP/s",
                          "frac": achieved / fp4_peak, "traffic": None,
-                         "peak_source": f"4 x bf16_tflops_sustained of {pk['source']} "
+                         "peak_source": f"4 x bf16_tflops (burst) of {pk['source']} "
                                         "MEASURED_PEAKS.json"},
             "gpu_launches": int(launches),
             "clocks": clocks.summary(),
@@ -831,7 +831,9 @@ def run_ours(args) -> None:
 
     if rank == 0:
         pk = peaks()
-        fp4_peak = 4.0 * pk["bf16_sustained"]  # dense FP4 : BF16 = 4 : 1 on B200
+        # dense FP4 : BF16 = 4 : 1 on B200; the GEMM is one 1-ms launch inside a
+        # 2.5-ms step, so the burst figure is its denominator
+        fp4_peak = 4.0 * pk["bf16"]
         assignments = T * (K_TOP + 1)
         custom = bool(args.tokens or args.experts)
         gemm1_flop = 2.0 * assignments * (2 * I) * H
@@ -865,8 +867,9 @@ def run_ours(args) -> None:
             "roofline": {"bound": "tensor", "kernel": "gate_up_gemm",
                          "achieved": achieved, "peak": fp4_peak, "unit": "TFLOP/s",
                          "frac": achieved / fp4_peak, "traffic": traffic,
-                         "peak_source": f"4 x bf16_tflops_sustained of {pk['source']} "
+                         "peak_source": f"4 x bf16_tflops (burst) of {pk['source']} "
                                         "MEASURED_PEAKS.json (dense FP4:BF16 rate 4:1)",
+                         "frac_of_sustained": achieved / (4.0 * pk["bf16_sustained"]),
                          "frac_of_nominal_9pf": achieved / 9000.0,
                          "library": {"kernel": f"cuBLASLt NVFP4 dense {assignments}x{2 * I}x{H} "
                                                "(torch._scaled_mm), same FLOPs, measured here",
