@@ -267,7 +267,7 @@ def profiled_phases(fwd, hidden, steps: int, engine=None) -> tuple[dict, int]:
 
 
 def run_decode_c4(device_index: int, steps: int, warmup: int, T: int = 64,
-                  experts: int = 0) -> dict:
+                  experts: int = 0, weight_rows: int = 0) -> dict:
     """Config 4 on one GPU: the full MXFP4 layer (256 experts + shared,
     GLM-5 shapes) at decode batch 64 with the Zipf-skewed router. HBM-bound:
     algorithmic bytes = (distinct experts touched + 1 shared) x 20,054,016 B of
@@ -290,6 +290,8 @@ def run_decode_c4(device_index: int, steps: int, warmup: int, T: int = 64,
     gc = torch.Generator(device="cpu").manual_seed(5)
     router = (torch.randn(E_, H, generator=gc) * 0.02).to(torch.bfloat16)
     layer.set_router(router, zipf_bias(E_, 6))
+    if weight_rows:
+        layer.set_weight_tile_rows(weight_rows)
     hidden = torch.randn(T, H, generator=gc).to(torch.bfloat16).to(dev)
     res = layer(hidden)
     touched = int(torch.unique(res.topk_indices).numel())
@@ -747,7 +749,8 @@ def run_ours(args) -> None:
     torch.cuda.set_device(local)
     if args.decode_only:
         print(json.dumps(run_decode_c4(local, args.steps, args.warmup,
-                                       experts=args.decode_experts)), flush=True)
+                                       experts=args.decode_experts,
+                                       weight_rows=args.weight_tile_rows)), flush=True)
         return
     if world > 1:
         run_ours_ep(args, world, rank, local)
@@ -919,6 +922,8 @@ def main() -> None:
     ap.add_argument("--down-tiles", default="", choices=["", "tm", "128", "256"],
                     help="down projection tiles: token-major or weight-major width (tuning)")
     ap.add_argument("--experts", type=int, default=0, help="override experts (profiling only)")
+    ap.add_argument("--weight-tile-rows", type=int, default=0, choices=[0, 128, 256],
+                    help="weight rows per narrow-token tile (tuning; 0 = the engine's default)")
     ap.add_argument("--decode-experts", type=int, default=0,
                     help="with --decode-only: fewer experts (small profiling captures only)")
     ap.add_argument("--dispatch", default="bf16", choices=["bf16", "fp4", "peer"],

@@ -468,6 +468,12 @@ glm5x_status glm5x_moe_set_token_major_down(glm5x_moe* moe, int32_t enable);
  * tile width 128 or 256 (0 = the gate/up GEMM's). Used when token-major tiles
  * are off. */
 glm5x_status glm5x_moe_set_down_tile_n(glm5x_moe* moe, int32_t bn);
+/* Weight rows per tile of the GEMMs for 32- and 64-row token tiles (small
+ * batches such as decode): 256 (the default: two 128-row halves with their
+ * own accumulators in one stage, so each stage hand-off streams twice the
+ * weight bytes) or 128 (one M = 128 MMA per K step). Both give the same
+ * results: every output element sums the same products in the same order. */
+glm5x_status glm5x_moe_set_weight_tile_rows(glm5x_moe* moe, int32_t rows);
 /* The engine's own stream (used by glm5x_moe_forward_host and by forwards
  * given a NULL stream), as a cudaStream_t. */
 glm5x_status glm5x_moe_get_stream(glm5x_moe* moe, void** stream);

@@ -77,21 +77,29 @@ constexpr int kMaxSeg = 260;      // segments (local experts + shared) per launc
 // chunk per K = 64 MMA). MX = 1: MXFP4 (E8M0 scale per 32, kind::mxf4 block32,
 // one chunk per two MMAs, which pick its scale bytes 0-1 or 2-3 by the scale
 // id) with four B rows per token (the residual terms of the activation).
-template <int BN, int MX>
+// MH = 2 (narrow token tiles): a tile covers 256 weight rows as two 128-row
+// halves, each with its own M = 128 MMAs and accumulator; one stage carries
+// both halves' weight rows against the same token rows, so every barrier
+// wait, stage hand-off and tile switch moves twice the weight bytes.
+template <int BN, int MX, int MH = 1>
 struct Cfg {
   static constexpr int kSfbCh = BN > 128 ? 2 : 1;  // 128-row scale blocks per tile
   static constexpr int kAcc = BN > 128 ? 1 : 2;    // TMEM accumulator buffers
-  static constexpr int kStages = BN > 128 ? 4 : (BN > 64 ? 5 : (BN > 32 ? 6 : 8));
   static constexpr int kCh = MX ? 2 : 4;           // scale chunks per 128 rows per stage
-  static constexpr int kABytes = kBM * kBKBytes;
+  static constexpr int kABytes = MH * kBM * kBKBytes;
   static constexpr int kBBytes = BN * kBKBytes;
-  static constexpr int kSfaBytes = kCh * kChunkBytes;
+  static constexpr int kSfaBytes = MH * kCh * kChunkBytes;
   static constexpr int kSfbBytes = kSfbCh * kCh * kChunkBytes;
   static constexpr int kStageBytes =
       ((kABytes + kBBytes + kSfaBytes + kSfbBytes + 1023) / 1024) * 1024;
-  static constexpr int kSfaCols = 4 * kCh;            // 4 columns per chunk
+  // two-half tiles: as many stages as fit (at most 5)
+  static constexpr int kStagesFit = (232448 - 1536 - 3 * 4 * (kMaxSeg + 1)) / kStageBytes;
+  static constexpr int kStages =
+      MH == 2 ? (kStagesFit < 5 ? kStagesFit : 5)
+              : (BN > 128 ? 4 : (BN > 64 ? 5 : (BN > 32 ? 6 : 8)));
+  static constexpr int kSfaCols = 4 * kCh * MH;       // half h's chunk c at 4 * kCh * h + 4c
   static constexpr int kSfbCols = 4 * kCh * kSfbCh;   // chunk c of block h at 4 * kSfbCh * c + 4 * h
-  static constexpr int kSfBase = kAcc * BN;
+  static constexpr int kSfBase = kAcc * MH * BN;
   static constexpr int kStageSfCols = kSfaCols + kSfbCols;
   static constexpr int kTmemCols = 512;
   static_assert(kSfBase + kStages * kStageSfCols <= kTmemCols, "TMEM budget");
@@ -137,13 +145,14 @@ __device__ __forceinline__ uint16_t f2bf(float x) {
 // thread holds one token's consecutive output features and stores them in
 // 16-byte pieces; tiles enumerate 128-token tiles fastest within a 256-row
 // weight tile. A / SFA are the token rows, B / SFB the weights.
-template <int BN, int EPI, int MX, int TM>
+template <int BN, int EPI, int MX, int TM, int MH>
 __global__ void __launch_bounds__(kThreads, 1)
     nvfp4_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                               const __grid_constant__ CUtensorMap tmap_b32,
                               const __grid_constant__ CUtensorMap tmap_b64,
                               const __grid_constant__ CUtensorMap tmap_b128, const GemmParams p) {
-  using C = Cfg<BN, MX>;
+  using C = Cfg<BN, MX, MH>;
+  static_assert(MH == 1 || (!TM && BN <= 64), "two weight halves: narrow token tiles only");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -159,7 +168,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   static_assert(!TM || (BN == 256 && EPI == 1 && !MX), "token-major: down projection, BN 256");
-  const int m_tiles = TM ? p.M_per / 256 : p.M_per / kBM;
+  const int m_tiles = TM ? p.M_per / 256 : p.M_per / (kBM * MH);
   constexpr int kTileRows = TM ? 128 : BN;  // token rows per tile
   const int ks_count = p.K / 256;
   const int kc_per_rb = p.K / (MX ? 128 : 64);  // scale chunks per 128-row block
@@ -251,7 +260,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!decode_tile(tile, m_tiles, p.nseg, kTileRows, s_ntp, s_cnt, s_start, ti)) continue;
         if (G5_GEMM_L2_PREFETCH && role == 0) prefetch_tile(tile + gridDim.x);
         // TM: A = the 128 token rows, B = 256 weight rows
-        const int w_row = ti.seg * p.M_per + ti.m_tile * (TM ? 256 : kBM);
+        const int w_row = ti.seg * p.M_per + ti.m_tile * (TM ? 256 : kBM * MH);
         const int a_row = TM ? ti.row_start : w_row;
         const int b_row = TM ? w_row : ti.row_start;
         const int sfb_ch = TM ? 2 : (ti.n_valid > 128 ? 2 : 1);
@@ -282,15 +291,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           // them into TMEM while the operand tiles are still landing
           if (do_sf) {
             mbar_arrive_expect_tx(&full_sf[stage], sf_bytes);
-            bulk_load(ssfa, sfa + (size_t)ks * C::kCh * kChunkBytes, C::kSfaBytes,
-                      &full_sf[stage]);
+#pragma unroll
+            for (int h = 0; h < MH; ++h)  // one 128-row scale block per weight half
+              bulk_load(ssfa + h * C::kCh * kChunkBytes,
+                        sfa + ((size_t)h * kc_per_rb + ks * C::kCh) * kChunkBytes,
+                        C::kCh * kChunkBytes, &full_sf[stage]);
             for (int h = 0; h < sfb_ch; ++h)
               bulk_load(ssfb + h * C::kCh * kChunkBytes,
                         sfb + ((size_t)h * kc_per_rb + ks * C::kCh) * kChunkBytes,
                         C::kCh * kChunkBytes, &full_sf[stage]);
           }
           if (bytes) mbar_arrive_expect_tx(&full[stage], bytes);
-          if (do_a) tma_load_2d(sa, &tmap_a, &full[stage], ks * kBKBytes, a_row);
+          if (do_a) {
+#pragma unroll
+            for (int h = 0; h < MH; ++h)
+              tma_load_2d(sa + h * kBM * kBKBytes, &tmap_a, &full[stage], ks * kBKBytes,
+                          a_row + h * kBM);
+          }
           if (do_b) {
             tma_load_2d(sb, m0, &full[stage], ks * kBKBytes, b_row);
             if (box1)
@@ -317,7 +334,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t idesc = idesc_fp4(kBM, n_mma, 0, 0, 0);
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, p.err)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * BN;
+        const uint32_t d_tmem = tmem_base + acc * MH * BN;
         for (int ks = 0; ks < ks_count; ++ks) {
           // operands landed (full) and this stage's scales are in TMEM
           if (!mbar_wait(&full[stage], phase, p.err) ||
@@ -333,19 +350,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t a_addr = smem_u32(sa), b_addr = smem_u32(sb);
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
-            if (MX) {
-              // chunk c / 2; scale bytes 0-1 (id 0) or 2-3 (id 2) of each column,
-              // given in the address's top bits and in the descriptor
-              const uint32_t id = (uint32_t)(c & 1) * 2u;
-              mma_mxfp4(d_tmem, desc_kmajor_sw128(a_addr + 32 * c),
-                        desc_kmajor_sw128(b_addr + 32 * c), idesc_fp4(kBM, n_mma, 1, id, id),
-                        (sfa_col + 4 * (c >> 1)) | (id << 30),
-                        (sfb_col + 4 * C::kSfbCh * (c >> 1)) | (id << 30),
-                        (ks | c) != 0 ? 1u : 0u);
-            } else {
-              mma_nvfp4(d_tmem, desc_kmajor_sw128(a_addr + 32 * c),
-                        desc_kmajor_sw128(b_addr + 32 * c), idesc, sfa_col + 4 * c,
-                        sfb_col + 4 * C::kSfbCh * c, (ks | c) != 0 ? 1u : 0u);
+#pragma unroll
+            for (int h = 0; h < MH; ++h) {
+              const uint32_t a_h = a_addr + h * kBM * kBKBytes;
+              const uint32_t sfa_h = sfa_col + 4 * C::kCh * h;
+              if (MX) {
+                // chunk c / 2; scale bytes 0-1 (id 0) or 2-3 (id 2) of each column,
+                // given in the address's top bits and in the descriptor
+                const uint32_t id = (uint32_t)(c & 1) * 2u;
+                mma_mxfp4(d_tmem + h * BN, desc_kmajor_sw128(a_h + 32 * c),
+                          desc_kmajor_sw128(b_addr + 32 * c), idesc_fp4(kBM, n_mma, 1, id, id),
+                          (sfa_h + 4 * (c >> 1)) | (id << 30),
+                          (sfb_col + 4 * C::kSfbCh * (c >> 1)) | (id << 30),
+                          (ks | c) != 0 ? 1u : 0u);
+              } else {
+                mma_nvfp4(d_tmem + h * BN, desc_kmajor_sw128(a_h + 32 * c),
+                          desc_kmajor_sw128(b_addr + 32 * c), idesc, sfa_h + 4 * c,
+                          sfb_col + 4 * C::kSfbCh * c, (ks | c) != 0 ? 1u : 0u);
+              }
             }
           }
           tc_commit(&empty[stage]);
@@ -390,10 +412,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint8_t* ssfb = ssfa + C::kSfaBytes;
         const uint32_t sfa_col = C::kSfBase + stage * C::kStageSfCols;
         const uint32_t sfb_col = sfa_col + C::kSfaCols;
-        // SFA: chunk c -> columns 4c..4c+3
+        // SFA: chunk c (of half c / kCh) -> columns 4c..4c+3
         uint32_t r[C::kSfaCols];
 #pragma unroll
-        for (int c = 0; c < C::kCh; ++c) {
+        for (int c = 0; c < C::kCh * MH; ++c) {
           const uint4 v = *reinterpret_cast<const uint4*>(ssfa + c * kChunkBytes + lane * 16);
           r[4 * c] = v.x; r[4 * c + 1] = v.y; r[4 * c + 2] = v.z; r[4 * c + 3] = v.w;
         }
@@ -434,144 +456,154 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!decode_tile(tile, m_tiles, p.nseg, kTileRows, s_ntp, s_cnt, s_start, ti)) continue;
       if (!mbar_wait(&tfull[acc], acc_phase, p.err)) break;
       tc_fence_after();
-      const uint32_t t_row = tmem_base + ((uint32_t)(32 * q) << 16) + acc * BN;
+      const uint32_t t_row = tmem_base + ((uint32_t)(32 * q) << 16) + acc * MH * BN;
       // Drain this warp's columns of the accumulator into registers and hand
       // the TMEM buffer back before any math or store, so the next tile's
       // MMAs overlap this tile's epilogue even with a single buffer.
       constexpr int kChunks = (BN + 63) / 64;
-      uint32_t v[kChunks][32];
+      uint32_t vv[MH][kChunks][32];
 #pragma unroll
-      for (int i = 0; i < kChunks; ++i)
-        if (TM || 32 * half + 64 * i < ti.n_valid)
-          tmem_ld_32x32b_x32(t_row + 32 * half + 64 * i, v[i]);
+      for (int h = 0; h < MH; ++h)
+#pragma unroll
+        for (int i = 0; i < kChunks; ++i)
+          if (TM || 32 * half + 64 * i < ti.n_valid)
+            tmem_ld_32x32b_x32(t_row + h * BN + 32 * half + 64 * i, vv[h][i]);
       tmem_ld_wait();
 #pragma unroll
-      for (int i = 0; i < kChunks; ++i) reg_fence(v[i]);
+      for (int h = 0; h < MH; ++h)
+#pragma unroll
+        for (int i = 0; i < kChunks; ++i) reg_fence(vv[h][i]);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_relaxed(&tempty[acc]);
-      const float bscale = p.b_global[ti.seg];
-      if (TM) {
-        // lane = token row 32q + lane of the tile; a chunk = 32 consecutive
-        // output features of that token, stored as four 16-byte pieces
-        const int r = 32 * q + lane;
-        if (r < ti.n_valid) {
-          const float w = p.row_weight[ti.row_start + r] * (bscale * p.a_global[ti.seg]);
-          uint16_t* yrow = p.out + (size_t)(ti.row_start + r) * p.M_per + ti.m_tile * 256;
 #pragma unroll
+      for (int h = 0; h < MH; ++h) {
+        // weight half h: 128-row m-tile mt of the expert
+        const int mt = ti.m_tile * MH + h;
+        auto& v = vv[h];
+        const float bscale = p.b_global[ti.seg];
+        if (TM) {
+          // lane = token row 32q + lane of the tile; a chunk = 32 consecutive
+          // output features of that token, stored as four 16-byte pieces
+          const int r = 32 * q + lane;
+          if (r < ti.n_valid) {
+            const float w = p.row_weight[ti.row_start + r] * (bscale * p.a_global[ti.seg]);
+            uint16_t* yrow = p.out + (size_t)(ti.row_start + r) * p.M_per + mt * 256;
+  #pragma unroll
+            for (int ch = 0; ch < kChunks; ++ch) {
+              const int c0 = 32 * half + 64 * ch;
+              uint32_t pk[16];
+  #pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const __nv_bfloat162 b2 = __floats2bfloat162_rn(
+                    __uint_as_float(v[ch][2 * i]) * w, __uint_as_float(v[ch][2 * i + 1]) * w);
+                pk[i] = *reinterpret_cast<const uint32_t*>(&b2);
+              }
+              uint4* dst = reinterpret_cast<uint4*>(yrow + c0);
+  #pragma unroll
+              for (int i = 0; i < 4; ++i)
+                dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+            }
+          }
+        } else if (MX && EPI == 0) {
+          // Columns 4r..4r+3 of a chunk are the four terms of the chunk's token
+          // r (r = 0..7): their sum is the token's product. Lanes l < 16 hold
+          // gate rows and compute h for tokens 0-3, lanes l + 16 the matching up
+          // rows and tokens 4-7; one swap per token pair. h goes to the token's
+          // term-0 row.
+          const float s_gate = bscale * p.a_global[2 * ti.seg];
+          const float s_up = bscale * p.a_global[2 * ti.seg + 1];
+          const bool lo = lane < 16;
+          const int j = mt * (kBM / 2) + 16 * q + (lane & 15);
+          const int hcols = p.M_per / 2;
+  #pragma unroll
           for (int ch = 0; ch < kChunks; ++ch) {
             const int c0 = 32 * half + 64 * ch;
-            uint32_t pk[16];
-#pragma unroll
+            if (c0 >= ti.n_valid) break;
+            float t[8];
+  #pragma unroll
+            for (int r = 0; r < 8; ++r)
+              t[r] = (__uint_as_float(v[ch][4 * r]) + __uint_as_float(v[ch][4 * r + 1])) +
+                     (__uint_as_float(v[ch][4 * r + 2]) + __uint_as_float(v[ch][4 * r + 3]));
+  #pragma unroll
+            for (int r = 0; r < 4; ++r) {
+              const float recv = __shfl_xor_sync(0xffffffffu, lo ? t[r + 4] : t[r], 16);
+              const float gate = (lo ? t[r] : recv) * s_gate;
+              const float up = (lo ? recv : t[r + 4]) * s_up;
+              const int col = c0 + 4 * (r + (lo ? 0 : 4));
+              if (col < ti.n_valid)
+                p.out[(size_t)(ti.row_start + col) * hcols + j] =
+                    f2bf(__fdividef(gate, 1.0f + __expf(-gate)) * up);
+            }
+          }
+        } else if (MX) {
+          // four term columns per token; routing weight of the term-0 row
+          const float scale = bscale * p.a_global[ti.seg];
+          const int o = mt * kBM + 32 * q + lane;
+  #pragma unroll
+          for (int ch = 0; ch < kChunks; ++ch) {
+            const int c0 = 32 * half + 64 * ch;
+            if (c0 >= ti.n_valid) break;
+            const float wmine = lane < 8 && c0 + 4 * lane < ti.n_valid
+                                    ? p.row_weight[ti.row_start + c0 + 4 * lane] * scale
+                                    : 0.0f;
+  #pragma unroll
+            for (int r = 0; r < 8; ++r) {
+              const float w = __shfl_sync(0xffffffffu, wmine, r);
+              const float t = (__uint_as_float(v[ch][4 * r]) + __uint_as_float(v[ch][4 * r + 1])) +
+                              (__uint_as_float(v[ch][4 * r + 2]) + __uint_as_float(v[ch][4 * r + 3]));
+              if (c0 + 4 * r < ti.n_valid)
+                p.out[(size_t)(ti.row_start + c0 + 4 * r) * p.M_per + o] = f2bf(t * w);
+            }
+          }
+        } else if (EPI == 0) {
+          // Rows 32q..32q+15 of the tile are gate rows, 32q+16..32q+31 the
+          // matching up rows. For columns (i, i+16) of a chunk, lanes l and
+          // l^16 swap one value so that every lane computes one h.
+          const float s_gate = bscale * p.a_global[2 * ti.seg];
+          const float s_up = bscale * p.a_global[2 * ti.seg + 1];
+          const bool lo = lane < 16;
+          const int j = mt * (kBM / 2) + 16 * q + (lane & 15);
+          const int hcols = p.M_per / 2;
+          float amax = 0.0f;
+  #pragma unroll
+          for (int ch = 0; ch < kChunks; ++ch) {
+            const int c0 = 32 * half + 64 * ch;
+            if (c0 >= ti.n_valid) break;
+  #pragma unroll
             for (int i = 0; i < 16; ++i) {
-              const __nv_bfloat162 b2 = __floats2bfloat162_rn(
-                  __uint_as_float(v[ch][2 * i]) * w, __uint_as_float(v[ch][2 * i + 1]) * w);
-              pk[i] = *reinterpret_cast<const uint32_t*>(&b2);
-            }
-            uint4* dst = reinterpret_cast<uint4*>(yrow + c0);
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-              dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
-          }
-        }
-      } else if (MX && EPI == 0) {
-        // Columns 4r..4r+3 of a chunk are the four terms of the chunk's token
-        // r (r = 0..7): their sum is the token's product. Lanes l < 16 hold
-        // gate rows and compute h for tokens 0-3, lanes l + 16 the matching up
-        // rows and tokens 4-7; one swap per token pair. h goes to the token's
-        // term-0 row.
-        const float s_gate = bscale * p.a_global[2 * ti.seg];
-        const float s_up = bscale * p.a_global[2 * ti.seg + 1];
-        const bool lo = lane < 16;
-        const int j = ti.m_tile * (kBM / 2) + 16 * q + (lane & 15);
-        const int hcols = p.M_per / 2;
-#pragma unroll
-        for (int ch = 0; ch < kChunks; ++ch) {
-          const int c0 = 32 * half + 64 * ch;
-          if (c0 >= ti.n_valid) break;
-          float t[8];
-#pragma unroll
-          for (int r = 0; r < 8; ++r)
-            t[r] = (__uint_as_float(v[ch][4 * r]) + __uint_as_float(v[ch][4 * r + 1])) +
-                   (__uint_as_float(v[ch][4 * r + 2]) + __uint_as_float(v[ch][4 * r + 3]));
-#pragma unroll
-          for (int r = 0; r < 4; ++r) {
-            const float recv = __shfl_xor_sync(0xffffffffu, lo ? t[r + 4] : t[r], 16);
-            const float gate = (lo ? t[r] : recv) * s_gate;
-            const float up = (lo ? recv : t[r + 4]) * s_up;
-            const int col = c0 + 4 * (r + (lo ? 0 : 4));
-            if (col < ti.n_valid)
-              p.out[(size_t)(ti.row_start + col) * hcols + j] =
-                  f2bf(__fdividef(gate, 1.0f + __expf(-gate)) * up);
-          }
-        }
-      } else if (MX) {
-        // four term columns per token; routing weight of the term-0 row
-        const float scale = bscale * p.a_global[ti.seg];
-        const int o = ti.m_tile * kBM + 32 * q + lane;
-#pragma unroll
-        for (int ch = 0; ch < kChunks; ++ch) {
-          const int c0 = 32 * half + 64 * ch;
-          if (c0 >= ti.n_valid) break;
-          const float wmine = lane < 8 && c0 + 4 * lane < ti.n_valid
-                                  ? p.row_weight[ti.row_start + c0 + 4 * lane] * scale
-                                  : 0.0f;
-#pragma unroll
-          for (int r = 0; r < 8; ++r) {
-            const float w = __shfl_sync(0xffffffffu, wmine, r);
-            const float t = (__uint_as_float(v[ch][4 * r]) + __uint_as_float(v[ch][4 * r + 1])) +
-                            (__uint_as_float(v[ch][4 * r + 2]) + __uint_as_float(v[ch][4 * r + 3]));
-            if (c0 + 4 * r < ti.n_valid)
-              p.out[(size_t)(ti.row_start + c0 + 4 * r) * p.M_per + o] = f2bf(t * w);
-          }
-        }
-      } else if (EPI == 0) {
-        // Rows 32q..32q+15 of the tile are gate rows, 32q+16..32q+31 the
-        // matching up rows. For columns (i, i+16) of a chunk, lanes l and
-        // l^16 swap one value so that every lane computes one h.
-        const float s_gate = bscale * p.a_global[2 * ti.seg];
-        const float s_up = bscale * p.a_global[2 * ti.seg + 1];
-        const bool lo = lane < 16;
-        const int j = ti.m_tile * (kBM / 2) + 16 * q + (lane & 15);
-        const int hcols = p.M_per / 2;
-        float amax = 0.0f;
-#pragma unroll
-        for (int ch = 0; ch < kChunks; ++ch) {
-          const int c0 = 32 * half + 64 * ch;
-          if (c0 >= ti.n_valid) break;
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float send = __uint_as_float(lo ? v[ch][i + 16] : v[ch][i]);
-            const float recv = __shfl_xor_sync(0xffffffffu, send, 16);
-            const float gate = lo ? __uint_as_float(v[ch][i]) * s_gate : recv * s_gate;
-            const float up = lo ? recv * s_up : __uint_as_float(v[ch][i + 16]) * s_up;
-            const int col = c0 + i + (lo ? 0 : 16);
-            if (col < ti.n_valid) {
-              const float h = __fdividef(gate, 1.0f + __expf(-gate)) * up;
-              const uint16_t hb = f2bf(h);
-              amax = fmaxf(amax, fabsf(__uint_as_float((uint32_t)hb << 16)));
-              p.out[(size_t)(ti.row_start + col) * hcols + j] = hb;
+              const float send = __uint_as_float(lo ? v[ch][i + 16] : v[ch][i]);
+              const float recv = __shfl_xor_sync(0xffffffffu, send, 16);
+              const float gate = lo ? __uint_as_float(v[ch][i]) * s_gate : recv * s_gate;
+              const float up = lo ? recv * s_up : __uint_as_float(v[ch][i + 16]) * s_up;
+              const int col = c0 + i + (lo ? 0 : 16);
+              if (col < ti.n_valid) {
+                const float h = __fdividef(gate, 1.0f + __expf(-gate)) * up;
+                const uint16_t hb = f2bf(h);
+                amax = fmaxf(amax, fabsf(__uint_as_float((uint32_t)hb << 16)));
+                p.out[(size_t)(ti.row_start + col) * hcols + j] = hb;
+              }
             }
           }
-        }
-        for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-        if (lane == 0 && amax > 0.0f)
-          atomicMax(reinterpret_cast<unsigned int*>(p.h_amax + ti.seg), __float_as_uint(amax));
-      } else {
-        const float scale = bscale * p.a_global[ti.seg];
-        const int o = ti.m_tile * kBM + 32 * q + lane;
-#pragma unroll
-        for (int ch = 0; ch < kChunks; ++ch) {
-          const int c0 = 32 * half + 64 * ch;
-          if (c0 >= ti.n_valid) break;
-          const float wmine =
-              c0 + lane < ti.n_valid ? p.row_weight[ti.row_start + c0 + lane] * scale : 0.0f;
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float w = __shfl_sync(0xffffffffu, wmine, i);
-            if (c0 + i < ti.n_valid)
-              p.out[(size_t)(ti.row_start + c0 + i) * p.M_per + o] =
-                  f2bf(__uint_as_float(v[ch][i]) * w);
+          for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+          if (lane == 0 && amax > 0.0f)
+            atomicMax(reinterpret_cast<unsigned int*>(p.h_amax + ti.seg), __float_as_uint(amax));
+        } else {
+          const float scale = bscale * p.a_global[ti.seg];
+          const int o = mt * kBM + 32 * q + lane;
+  #pragma unroll
+          for (int ch = 0; ch < kChunks; ++ch) {
+            const int c0 = 32 * half + 64 * ch;
+            if (c0 >= ti.n_valid) break;
+            const float wmine =
+                c0 + lane < ti.n_valid ? p.row_weight[ti.row_start + c0 + lane] * scale : 0.0f;
+  #pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const float w = __shfl_sync(0xffffffffu, wmine, i);
+              if (c0 + i < ti.n_valid)
+                p.out[(size_t)(ti.row_start + c0 + i) * p.M_per + o] =
+                    f2bf(__uint_as_float(v[ch][i]) * w);
+            }
           }
         }
       }
@@ -588,12 +620,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) tmem_dealloc(tmem_base, C::kTmemCols);
 }
 
-template <int BN, int EPI, int MX, int TM = 0>
+template <int BN, int EPI, int MX, int TM = 0, int MH = 1>
 cudaError_t launch_impl(const CUtensorMap* ta, const CUtensorMap* tb, const GemmParams& p,
                         int num_sms, cudaStream_t st) {
-  auto kern = nvfp4_grouped_gemm_kernel<BN, EPI, MX, TM>;
+  using C = Cfg<BN, MX, MH>;
+  auto kern = nvfp4_grouped_gemm_kernel<BN, EPI, MX, TM, MH>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)Cfg<BN, MX>::kSmem);
+                                       (int)C::kSmem);
   if (e != cudaSuccess) return e;
   // setmaxnreg.inc waits until the block's launch registers cover the split;
   // refuse a build whose launch register count could not.
@@ -601,7 +634,7 @@ cudaError_t launch_impl(const CUtensorMap* ta, const CUtensorMap* tb, const Gemm
   e = cudaFuncGetAttributes(&fa, kern);
   if (e != cudaSuccess) return e;
   if ((size_t)fa.numRegs * kThreads < 256u * (kRegsLow + kRegsEpi)) return cudaErrorInvalidConfiguration;
-  kern<<<num_sms, kThreads, Cfg<BN, MX>::kSmem, st>>>(*ta, tb[0], tb[1], tb[2], p);
+  kern<<<num_sms, kThreads, C::kSmem, st>>>(*ta, tb[0], tb[1], tb[2], p);
   return cudaGetLastError();
 }
 
@@ -619,13 +652,30 @@ size_t nvfp4_gemm_smem_bytes(int bn) {
 
 cudaError_t launch_nvfp4_grouped_gemm(int bn, int epi, const CUtensorMap* tmap_a,
                                       const CUtensorMap* tmap_b, const GemmParams& p,
-                                      int num_sms, cudaStream_t st, int mxfp4) {
+                                      int num_sms, cudaStream_t st, int mxfp4, int weight_rows) {
   if (p.nseg > kMaxSeg || p.K % 256 || p.M_per % kBM) return cudaErrorInvalidValue;
   if (epi == 2) {
     // token-major down projection (tmap_a: token rows, box 128; tmap_b[2]:
     // weight rows, box 128)
     if (mxfp4 || p.M_per % 256) return cudaErrorInvalidValue;
     return launch_impl<256, 1, 0, 1>(tmap_a, tmap_b, p, num_sms, st);
+  }
+  if (weight_rows == 256 && bn <= 64) {
+    // 256 weight rows per tile in two halves (narrow token tiles)
+    if (p.M_per % 256) return cudaErrorInvalidValue;
+#define G5_CASE2(BN_)                                                                   \
+  case BN_:                                                                             \
+    if (mxfp4)                                                                          \
+      return epi == 0 ? launch_impl<BN_, 0, 1, 0, 2>(tmap_a, tmap_b, p, num_sms, st)    \
+                      : launch_impl<BN_, 1, 1, 0, 2>(tmap_a, tmap_b, p, num_sms, st);   \
+    return epi == 0 ? launch_impl<BN_, 0, 0, 0, 2>(tmap_a, tmap_b, p, num_sms, st)      \
+                    : launch_impl<BN_, 1, 0, 0, 2>(tmap_a, tmap_b, p, num_sms, st);
+    switch (bn) {
+      G5_CASE2(32)
+      G5_CASE2(64)
+    }
+#undef G5_CASE2
+    return cudaErrorInvalidValue;
   }
 #define G5_CASE(BN_)                                                                     \
   case BN_:                                                                              \

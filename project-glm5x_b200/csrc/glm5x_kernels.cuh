@@ -187,9 +187,13 @@ struct GemmParams {
 // epi = 2: token-major down projection (NVFP4, segments in 128-row tiles):
 // tmap_a / p.a_packed / p.sfa are the token rows (box 128), tmap_b[2] /
 // p.b_packed / p.sfb the weights; output and weighting as epi 1.
+// weight_rows = 256 (token tiles of 32 or 64 rows only): each tile covers
+// 256 weight rows as two 128-row halves with their own MMAs and accumulators,
+// so one stage hand-off moves twice the weight bytes (M_per % 256 == 0).
 cudaError_t launch_nvfp4_grouped_gemm(int bn, int epi, const CUtensorMap* tmap_a,
                                       const CUtensorMap* tmap_b, const GemmParams& p,
-                                      int num_sms, cudaStream_t st, int mxfp4 = 0);
+                                      int num_sms, cudaStream_t st, int mxfp4 = 0,
+                                      int weight_rows = 128);
 size_t nvfp4_gemm_smem_bytes(int bn);
 
 // ------------------------------------------------------------ gemm_nvfp4_pair.cu

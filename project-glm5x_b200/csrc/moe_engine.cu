@@ -246,6 +246,10 @@ struct glm5x_moe {
   bool use_pair = true;    // 256-row token tiles on CTA pairs (cta_group::2)
   bool token_major_down = false;  // token-major down projection (opt-in: not faster here)
   int down_bn = 0;                // weight-major down projection tile width (0 = same)
+  // weight rows per tile of the single-CTA GEMMs for 32- and 64-row token
+  // tiles: 256 as two halves per stage (the default: config-4 decode 0.544 ->
+  // 0.467 ms, 0.67 -> 0.78 of HBM), or 128 (glm5x_moe_set_weight_tile_rows)
+  int weight_rows = 256;
   CUtensorMap tm_act[4]{}, tm_h[4]{};  // box rows 32, 64, 128, 256
 
   glm5x_status fail(glm5x_status st, const char* fmt, ...) {
@@ -1133,7 +1137,7 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
            pair ? launch_nvfp4_pair_gemm(0, &m->tm_w13, m->tm_act, &m->tm_w13_sf, &m->tm_act_sf,
                                          g1, m->pair_grid, st)
                 : launch_nvfp4_grouped_gemm(bn, 0, &m->tm_w13, m->tm_act, g1, m->num_sms, st,
-                                            mx ? 1 : 0),
+                                            mx ? 1 : 0, m->weight_rows),
            "gate/up GEMM");
   mark(6);
   if (mx) {
@@ -1184,7 +1188,7 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
              pair ? launch_nvfp4_pair_gemm(1, &m->tm_w2, m->tm_h, &m->tm_w2_sf, &m->tm_h_sf, g2,
                                            m->pair_grid, st)
                   : launch_nvfp4_grouped_gemm(bn, 1, &m->tm_w2, m->tm_h, g2, m->num_sms, st,
-                                              mx ? 1 : 0),
+                                              mx ? 1 : 0, m->weight_rows),
              "down GEMM");
   }
   mark(8);
@@ -1662,6 +1666,17 @@ glm5x_status glm5x_moe_set_pair_mma(glm5x_moe* m, int32_t enable) {
 glm5x_status glm5x_moe_set_token_major_down(glm5x_moe* m, int32_t enable) {
   if (!m) return fail_global(GLM5X_INVALID_STATE, "null engine");
   m->token_major_down = enable != 0;
+  return GLM5X_OK;
+}
+
+glm5x_status glm5x_moe_set_weight_tile_rows(glm5x_moe* m, int32_t rows) {
+  if (!m) return fail_global(GLM5X_INVALID_STATE, "null engine");
+  if (rows != 128 && rows != 256)
+    return m->fail(GLM5X_INVALID_EXTENT, "weight tile rows must be 128 or 256");
+  if (rows == 256 && (m->H() % 256 || (2 * m->I()) % 256))
+    return m->fail(GLM5X_INVALID_EXTENT, "256-row weight tiles need hidden and 2 x intermediate "
+                                         "multiples of 256");
+  m->weight_rows = rows;
   return GLM5X_OK;
 }
 

@@ -408,6 +408,11 @@ class GLM5XMoELayer:
                                                     diag.data_ptr()), self._h)
         return sel, diag
 
+    def set_weight_tile_rows(self, rows: int) -> None:
+        """Weight rows per tile for narrow token tiles: 128, or 256 as two
+        halves per stage (small batches)."""
+        N.check(N.lib().glm5x_moe_set_weight_tile_rows(self._h, rows), self._h)
+
     def set_down_tile_n(self, bn: int) -> None:
         """Weight-major down projection token tile (128/256, 0 = gate/up's)."""
         N.check(N.lib().glm5x_moe_set_down_tile_n(self._h, bn), self._h)

@@ -40,6 +40,17 @@ def _assert_close(got, want, what):
                                           (520, 256, False, True), (520, 256, False, False),
                                           (7, 256, True, True), (7, 256, False, True)])
 def test_routed_expert_path_small_shapes(T, bn, pair, tm):
+    _routed_path(T, bn, pair, tm, 128)
+
+
+@pytest.mark.parametrize("T,bn", [(1, 0), (5, 32), (40, 32), (100, 64), (130, 32), (7, 64)])
+def test_routed_expert_path_256_row_weight_tiles(T, bn):
+    """Narrow token tiles with 256 weight rows per tile (two 128-row halves
+    per stage): the same outputs as the oracle."""
+    _routed_path(T, bn, True, False, 256)
+
+
+def _routed_path(T, bn, pair, tm, weight_rows):
     """Every token-tile width (256-row tiles on CTA pairs and on single CTAs),
     the token-major and weight-major down projections, segments that span
     several tiles and narrow tiles."""
@@ -48,6 +59,7 @@ def test_routed_expert_path_small_shapes(T, bn, pair, tm):
     layer.set_tile_n(bn)
     layer.set_pair_mma(pair)
     layer.set_token_major_down(tm)
+    layer.set_weight_tile_rows(weight_rows)
     experts, deq = {}, {}
     for e in list(range(E)) + [-1]:
         ex, dq = make_expert(H, I, 1000 + e)
@@ -61,7 +73,7 @@ def test_routed_expert_path_small_shapes(T, bn, pair, tm):
     layer.check()
     shared = deq.pop(-1)
     want, _ = oracle_forward(bf16_to_np(hidden), ids, w, deq, shared)
-    _assert_close(out.cpu().numpy(), want, f"T={T} bn={bn} pair={pair} tm={tm}")
+    _assert_close(out.cpu().numpy(), want, f"T={T} bn={bn} pair={pair} tm={tm} w={weight_rows}")
     layer.close()
 
 

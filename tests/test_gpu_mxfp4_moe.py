@@ -34,14 +34,18 @@ def _assert_close(got, want, what):
     assert max_rel <= MAX_REL and cos >= MIN_COS, (what, max_rel, l2, cos)
 
 
-@pytest.mark.parametrize("T,bn", [(1, 0), (5, 0), (40, 0), (300, 0), (9, 32), (20, 64),
-                                  (40, 128), (150, 256), (300, 256)])
-def test_mxfp4_routed_expert_path(T, bn):
+@pytest.mark.parametrize("T,bn,weight_rows", [(1, 0, 128), (5, 0, 128), (40, 0, 128),
+                                              (300, 0, 128), (9, 32, 128), (20, 64, 128),
+                                              (40, 128, 128), (150, 256, 128),
+                                              (300, 256, 128), (1, 0, 256), (9, 32, 256),
+                                              (20, 64, 256), (40, 0, 256)])
+def test_mxfp4_routed_expert_path(T, bn, weight_rows):
     """Every token-tile width, segments spanning several tiles, the shared
     expert, and term rows padded inside a tile."""
     H, I, E, k = 512, 512, 8, 2
     layer = _layer(H, I, E, k, True, 320)
     layer.set_tile_n(bn)
+    layer.set_weight_tile_rows(weight_rows)
     deq = {}
     for e in list(range(E)) + [-1]:
         ex, dq = make_expert_mxfp4(H, I, 3000 + e)
@@ -56,7 +60,7 @@ def test_mxfp4_routed_expert_path(T, bn):
     shared = deq.pop(-1)
     want, _ = oracle_forward(bf16_to_np(hidden), ids, w, deq, shared,
                              expert_fn=O.mxfp4_expert_oracle)
-    _assert_close(out.cpu().numpy(), want, f"T={T} bn={bn}")
+    _assert_close(out.cpu().numpy(), want, f"T={T} bn={bn} w={weight_rows}")
     layer.close()
 
 
