@@ -516,15 +516,25 @@ def run_ours_ep(args, world: int, rank: int, local: int) -> None:
         launches += 7 * args.steps  # plan, exchange, tail clear, dispatch, wait, ready, combine
     # phase and stage split from further steps with the events on (they add
     # about 2.5 us each, so the timed steps ran without them)
-    if not peer:
-        ep.set_timing(True)
-        ep.stage_times()
+    ep.set_timing(True)
+    ep.stage_times()
     phases, nprof = profiled_phases(ep, hidden, args.steps, engine=layer)
-    stages = None
-    if not peer:
-        stages, nst = ep.stage_times()
-        ep.set_timing(False)
-        stages = {k: v / max(nst, 1) for k, v in stages.items()}
+    stages, nst = ep.stage_times()
+    ep.set_timing(False)
+    stages = {k: v / max(nst, 1) for k, v in stages.items()}
+    exchange = None
+    if peer:
+        # bytes this rank stored into other ranks (rows + ids + weights +
+        # amax) and pulled back from them (BF16 partial sums), per stage time
+        sent, _ = ep.last_counts()
+        out_rows = sum(c for d, c in enumerate(sent) if d != rank)
+        row_bytes = H * 2 + K_TOP * 8 + 4
+        exchange = {"rows_to_peers": out_rows,
+                    "dispatch_gbs": out_rows * row_bytes / (stages["dispatch"] / 1e3) / 1e9,
+                    "combine_gbs": out_rows * H * 2 / (stages["combine"] / 1e3) / 1e9,
+                    "note": "rank 0: bytes to / from other ranks over NVLink per stage time; "
+                            "the dispatch and combine stages include the wait for the "
+                            "slowest peer"}
     t = torch.tensor([ms_total], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_total = float(t.item())
@@ -596,7 +606,7 @@ def run_ours_ep(args, world: int, rank: int, local: int) -> None:
                                       (f"ep{world} (NCCL all-to-all dispatch / combine, "
                                        f"{'NVFP4' if fp4 else 'BF16'} dispatch)"),
                        "l2": "inputs larger than L2"},
-            "phases_ms": phases, "ep_stages_ms": stages,
+            "phases_ms": phases, "ep_stages_ms": stages, "ep_exchange": exchange,
             "roofline": {"bound": "tensor", "kernel": "gate_up_gemm (rank 0)",
                          "achieved": achieved, "peak": fp4_peak, "unit": "TFLOP/s",
                          "frac": achieved / fp4_peak, "traffic": None,
@@ -716,6 +726,13 @@ def run_decode_c4_ep(args, world: int, rank: int, local: int) -> dict | None:
     torch.cuda.synchronize()
     ep.check()
     ms = e0.elapsed_time(e1) / steps
+    ep.set_timing(True)
+    ep.stage_times()
+    for _ in range(steps):
+        ep(hidden)
+    stages, nst = ep.stage_times()
+    ep.set_timing(False)
+    stages = {k: v / max(nst, 1) for k, v in stages.items()}
     bytes_rank = (held + 1) * MXFP4_EXPERT_BYTES + experts * H * 2 + Tr * H * 6
     t = torch.tensor([ms, float(bytes_rank), float(held)], device=dev)
     tmax = t.clone()
@@ -735,6 +752,7 @@ def run_decode_c4_ep(args, world: int, rank: int, local: int) -> dict | None:
                      "peer-memory exchange"),
         "tokens_per_s": Tall / (ms_max / 1000.0), "ms_per_step": ms_max,
         "experts_touched": int(touched.numel()), "max_local_experts_touched": int(tmax[2]),
+        "ep_stages_ms_rank0": stages if rank == 0 else None,
         "roofline": {"bound": "hbm", "kernel": "whole layer step, busiest rank",
                      "achieved": bytes_max / (ms_max / 1000.0) / 1e9, "peak": hbm,
                      "unit": "GB/s", "frac": bytes_max / (ms_max / 1000.0) / 1e9 / hbm,
@@ -926,7 +944,7 @@ def main() -> None:
                     help="weight rows per narrow-token tile (tuning; 0 = the engine's default)")
     ap.add_argument("--decode-experts", type=int, default=0,
                     help="with --decode-only: fewer experts (small profiling captures only)")
-    ap.add_argument("--dispatch", default="bf16", choices=["bf16", "fp4", "peer"],
+    ap.add_argument("--dispatch", default="peer", choices=["bf16", "fp4", "peer"],
                     help="expert-parallel exchange: NCCL all-to-all of BF16 or of "
                          "sender-quantized NVFP4 rows, or the library's peer-memory kernels")
     args = ap.parse_args()

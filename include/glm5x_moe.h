@@ -397,6 +397,17 @@ glm5x_status glm5x_moe_ep_forward(glm5x_moe_ep* ep, const void* hidden_bf16, int
  * words (GLM5X_WAIT_TIMEOUT when a peer did not answer in time). */
 glm5x_status glm5x_moe_ep_check(glm5x_moe_ep* ep);
 const char* glm5x_moe_ep_error_message(const glm5x_moe_ep* ep);
+/* Stage times of later forwards, with CUDA events on the forward's stream
+ * (each event adds a few microseconds): 0 route, 1 plan + count exchange, 2
+ * dispatch + the wait for every source's rows, 3 experts, 4 ready + the
+ * partial-sum pull. glm5x_moe_ep_stage_times synchronizes and writes the
+ * milliseconds summed per stage since its last call and the forwards counted. */
+#define GLM5X_EP_STAGES 5
+glm5x_status glm5x_moe_ep_set_profiling(glm5x_moe_ep* ep, int32_t enable);
+glm5x_status glm5x_moe_ep_stage_times(glm5x_moe_ep* ep, float* ms, int32_t* forwards);
+/* Rows the last forward sent to each rank (sent[world]) and received in all
+ * (synchronizes the device). */
+glm5x_status glm5x_moe_ep_last_counts(glm5x_moe_ep* ep, int64_t* sent, int64_t* received);
 void glm5x_moe_ep_destroy(glm5x_moe_ep* ep);
 
 /* Expert-parallel FP4 dispatch (no counterpart in the reference, which runs

@@ -402,6 +402,12 @@ struct glm5x_moe_ep {
   uint32_t* err = nullptr;
   cudaStream_t stream = nullptr;
   std::string error;
+  // stage timing (glm5x_moe_ep_set_profiling): one set of events per profiled
+  // forward, read and released by glm5x_moe_ep_stage_times
+  bool profiling = false;
+  std::vector<std::vector<cudaEvent_t>> pending;
+  double stage_ms[GLM5X_EP_STAGES]{};
+  int profiled = 0;
 };
 
 namespace {
@@ -604,11 +610,22 @@ glm5x_status glm5x_moe_ep_forward(glm5x_moe_ep* ep, const void* hidden_bf16, int
     return ep_fail(ep, GLM5X_DEVICE_ERROR, std::string("ep forward: ") + what + ": " +
                                                cudaGetErrorString(cudaGetLastError()));
   };
+  std::vector<cudaEvent_t> evs;
+  auto mark = [&]() {
+    if (!ep->profiling) return;
+    cudaEvent_t e;
+    if (cudaEventCreate(&e) == cudaSuccess) {
+      cudaEventRecord(e, st);
+      evs.push_back(e);
+    }
+  };
+  mark();
   // route
   if (T > 0) {
     const glm5x_status rs = glm5x_moe_route(ep->engine, hidden_bf16, T, ep->ids, ep->wts, nullptr, st);
     if (rs != GLM5X_OK) return ep_fail(ep, rs, glm5x_moe_error_message(ep->engine));
   }
+  mark();
   // plan
   ep_plan_kernel<<<W, 1024, 0, st>>>(ep->ids, T, ep->k, ep->per, W, ep->pos, send_count);
   if (cudaGetLastError() != cudaSuccess) return cuda_fail("plan");
@@ -630,6 +647,7 @@ glm5x_status glm5x_moe_ep_forward(glm5x_moe_ep* ep, const void* hidden_bf16, int
                                             at<float>(ep->block, ep->L.wts[p]), ep->local_cap,
                                             ep->recv_cap, ep->k, recv_count);
   if (cudaGetLastError() != cudaSuccess) return cuda_fail("exchange");
+  mark();
   // dispatch
   DispatchArgs da{};
   da.peers = ep->peers;
@@ -656,6 +674,7 @@ glm5x_status glm5x_moe_ep_forward(glm5x_moe_ep* ep, const void* hidden_bf16, int
   ep_wait_arrivals_kernel<<<1, 32, 0, st>>>(at<uint64_t>(ep->block, ep->L.arrive),
                                             epoch * (uint64_t)W * kGrid, ep->err);
   if (cudaGetLastError() != cudaSuccess) return cuda_fail("dispatch");
+  mark();
   // experts over [local tokens | received rows]
   const glm5x_status es = engine_forward_peer_rows(
       ep->engine, at<uint16_t>(ep->block, ep->L.rows[p]), ep->local_cap, T, ep->recv_cap,
@@ -663,6 +682,7 @@ glm5x_status glm5x_moe_ep_forward(glm5x_moe_ep* ep, const void* hidden_bf16, int
       ep->mx ? nullptr : at<float>(ep->block, ep->L.amax[p]), recv_count, out,
       at<uint16_t>(ep->block, ep->L.partial[p]), st);
   if (es != GLM5X_OK) return ep_fail(ep, es, glm5x_moe_error_message(ep->engine));
+  mark();
   // ready, then pull the partial sums back
   ep_ready_kernel<<<1, 32, 0, st>>>(ep->peers, ep->L.ready[p], ep->rank, W, epoch);
   CombineArgs ca{};
@@ -681,6 +701,52 @@ glm5x_status glm5x_moe_ep_forward(glm5x_moe_ep* ep, const void* hidden_bf16, int
   ca.err = ep->err;
   ep_combine_kernel<<<kGrid, kThreads, 0, st>>>(ca);
   if (cudaGetLastError() != cudaSuccess) return cuda_fail("combine");
+  mark();
+  if (ep->profiling && evs.size() == GLM5X_EP_STAGES + 1) ep->pending.push_back(std::move(evs));
+  else
+    for (cudaEvent_t e : evs) cudaEventDestroy(e);
+  return GLM5X_OK;
+}
+
+glm5x_status glm5x_moe_ep_set_profiling(glm5x_moe_ep* ep, int32_t enable) {
+  if (!ep) return ep_fail(nullptr, GLM5X_INVALID_STATE, "ep profiling: null argument");
+  ep->profiling = enable != 0;
+  return GLM5X_OK;
+}
+
+glm5x_status glm5x_moe_ep_stage_times(glm5x_moe_ep* ep, float* ms, int32_t* forwards) {
+  if (!ep || !ms || !forwards)
+    return ep_fail(ep, GLM5X_INVALID_STATE, "ep stage times: null argument");
+  cudaSetDevice(ep->device);
+  for (auto& evs : ep->pending) {
+    cudaEventSynchronize(evs.back());
+    for (int i = 0; i < GLM5X_EP_STAGES; ++i) {
+      float t = 0.0f;
+      if (cudaEventElapsedTime(&t, evs[i], evs[i + 1]) == cudaSuccess) ep->stage_ms[i] += t;
+    }
+    for (cudaEvent_t e : evs) cudaEventDestroy(e);
+    ep->profiled++;
+  }
+  ep->pending.clear();
+  for (int i = 0; i < GLM5X_EP_STAGES; ++i) {
+    ms[i] = static_cast<float>(ep->stage_ms[i]);
+    ep->stage_ms[i] = 0.0;
+  }
+  *forwards = ep->profiled;
+  ep->profiled = 0;
+  return GLM5X_OK;
+}
+
+glm5x_status glm5x_moe_ep_last_counts(glm5x_moe_ep* ep, int64_t* sent, int64_t* received) {
+  if (!ep || !sent || !received)
+    return ep_fail(ep, GLM5X_INVALID_STATE, "ep counts: null argument");
+  cudaSetDevice(ep->device);
+  std::vector<int32_t> h(2 * ep->world + 1);
+  if (cudaDeviceSynchronize() != cudaSuccess ||
+      cudaMemcpy(h.data(), ep->small, h.size() * 4, cudaMemcpyDeviceToHost) != cudaSuccess)
+    return ep_fail(ep, GLM5X_DEVICE_ERROR, "ep counts: device error");
+  for (int d = 0; d < ep->world; ++d) sent[d] = h[d];
+  *received = h[2 * ep->world];
   return GLM5X_OK;
 }
 
@@ -710,6 +776,8 @@ void glm5x_moe_ep_destroy(glm5x_moe_ep* ep) {
                   static_cast<void*>(ep->wts), static_cast<void*>(ep->pos),
                   static_cast<void*>(ep->small), static_cast<void*>(ep->err)})
     if (q) cudaFree(q);
+  for (auto& evs : ep->pending)
+    for (cudaEvent_t e : evs) cudaEventDestroy(e);
   if (ep->stream) cudaStreamDestroy(ep->stream);
   if (ep->engine) glm5x_moe_destroy(ep->engine);
   delete ep;

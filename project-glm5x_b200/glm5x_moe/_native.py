@@ -174,6 +174,9 @@ SIGNATURES = {
     "glm5x_moe_ep_forward": [_P, _P, _I64, _P, _P],
     "glm5x_moe_ep_check": [_P],
     "glm5x_moe_ep_error_message": [_P],
+    "glm5x_moe_ep_set_profiling": [_P, _I32],
+    "glm5x_moe_ep_stage_times": [_P, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(_I32)],
+    "glm5x_moe_ep_last_counts": [_P, ctypes.POINTER(_I64), ctypes.POINTER(_I64)],
     "glm5x_moe_ep_destroy": [_P],
     "glm5x_moe_check": [_P],
     "glm5x_moe_get_stats": [_P, ctypes.POINTER(MoeStats)],

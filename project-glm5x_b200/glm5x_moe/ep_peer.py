@@ -89,6 +89,28 @@ class PeerExpertParallelMoE:
                 N.stream_arg(torch.cuda.current_stream().cuda_stream)))
         return out.reshape(*hidden.shape[:-1], self.hidden_size)
 
+    STAGES = ("route", "exchange", "dispatch", "experts", "combine")
+
+    def set_timing(self, enable: bool) -> None:
+        """CUDA events at the stage boundaries of later forwards."""
+        self._check(N.lib().glm5x_moe_ep_set_profiling(self._h, 1 if enable else 0))
+
+    def stage_times(self) -> tuple[dict, int]:
+        """(milliseconds per stage summed since the last call, forwards):
+        route, exchange (plan + counts), dispatch (rows out + wait for every
+        source's rows), experts, combine (ready + partial sums pulled back)."""
+        ms = (ctypes.c_float * len(self.STAGES))()
+        n = ctypes.c_int32()
+        self._check(N.lib().glm5x_moe_ep_stage_times(self._h, ms, ctypes.byref(n)))
+        return dict(zip(self.STAGES, (float(v) for v in ms))), int(n.value)
+
+    def last_counts(self) -> tuple[list[int], int]:
+        """(rows sent to each rank, rows received) of the last forward."""
+        sent = (ctypes.c_int64 * self.world)()
+        recv = ctypes.c_int64()
+        self._check(N.lib().glm5x_moe_ep_last_counts(self._h, sent, ctypes.byref(recv)))
+        return list(sent), int(recv.value)
+
     def check(self) -> None:
         """Synchronizes; raises GLM5X_WAIT_TIMEOUT if a peer did not answer."""
         self._check(N.lib().glm5x_moe_ep_check(self._h))
