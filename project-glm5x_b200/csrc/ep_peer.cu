@@ -18,8 +18,8 @@
 //   dispatch   each token's BF16 row, its top-k ids masked to d's experts,
 //              its weights and its max |x| are stored straight into d's
 //              receive area (NVLink stores), one warp per token reading the
-//              row once for all destinations; blocks then add to each
-//              destination's arrival counter;
+//              row once for all destinations; the grid's last block to
+//              finish then adds one to each destination's arrival counter;
 //   experts    after all arrivals: the engine over [local tokens | received
 //              rows] in one call; local tokens take the shared expert (FP32
 //              out), received rows their held experts, whose weighted sum
@@ -63,7 +63,7 @@ int engine_device(const glm5x_moe* m);
 namespace {
 
 constexpr int kMaxWorld = 16;
-constexpr int kGrid = 296;  // blocks of the dispatch / combine kernels (every rank the same)
+constexpr int kGrid = 296;  // most blocks of the dispatch / combine kernels
 constexpr int kThreads = 256;
 
 // Byte offsets inside one rank's block; identical on every rank.
@@ -214,6 +214,8 @@ __global__ void ep_clear_tail_kernel(int32_t* __restrict__ ids, float* __restric
 struct DispatchArgs {
   Peers peers;
   size_t rows_off, ids_off, wts_off, amax_off, arrive_off;
+  unsigned long long* done;       // local count of finished dispatch blocks (monotonic)
+  unsigned long long done_target; // its value once this forward's blocks have all finished
   const uint16_t* x;      // [T, H] local tokens
   const int32_t* ids;     // [T, k] global ids
   const float* w;         // [T, k]
@@ -278,9 +280,15 @@ __global__ void __launch_bounds__(kThreads) ep_dispatch_kernel(DispatchArgs a) {
     if (lane == 0) at<float>(own, a.amax_off)[t] = amax;
     if (my_row >= 0) at<float>(a.peers.base[lane], a.amax_off)[my_row] = amax;
   }
-  // every block adds one arrival at every destination once its stores are visible
+  // Every thread's stores become visible system-wide, then the block counts
+  // itself done; the last block of the grid adds one arrival at every
+  // destination (one per source rank and forward).
+  __threadfence_system();
   __syncthreads();
-  if ((int)threadIdx.x < a.W) {
+  __shared__ bool last;
+  if (threadIdx.x == 0) last = atomicAdd(a.done, 1ull) + 1ull == a.done_target;
+  __syncthreads();
+  if (last && (int)threadIdx.x < a.W) {
     __threadfence_system();
     red_add_release_sys(at<uint64_t>(a.peers.base[threadIdx.x], a.arrive_off), 1);
   }
@@ -399,6 +407,8 @@ struct glm5x_moe_ep {
   float* wts = nullptr;
   int32_t* pos = nullptr;     // [local_cap, W]
   int32_t* small = nullptr;   // send_count [W], send_off [W], recv_count [1]
+  unsigned long long* done = nullptr;  // finished dispatch blocks, all forwards
+  unsigned long long done_total = 0;
   uint32_t* err = nullptr;
   cudaStream_t stream = nullptr;
   std::string error;
@@ -486,10 +496,12 @@ glm5x_status glm5x_moe_ep_create(const glm5x_moe_config* cfg, int device, int32_
             cudaMalloc(&ep->pos, (size_t)ep->local_cap * W * 4) == cudaSuccess &&
             cudaMalloc(&ep->small, (2 * W + 1) * 4) == cudaSuccess &&
             cudaMalloc(&ep->err, 4) == cudaSuccess &&
+            cudaMalloc(&ep->done, 8) == cudaSuccess &&
             cudaStreamCreateWithFlags(&ep->stream, cudaStreamNonBlocking) == cudaSuccess;
   if (ok)
     ok = cudaMemsetAsync(ep->block, 0, ep->L.total, ep->stream) == cudaSuccess &&
-         cudaMemsetAsync(ep->err, 0, 4, ep->stream) == cudaSuccess;
+         cudaMemsetAsync(ep->err, 0, 4, ep->stream) == cudaSuccess &&
+         cudaMemsetAsync(ep->done, 0, 8, ep->stream) == cudaSuccess;
   if (ok) {
     // every id slot starts as -1: local rows never carry routed slots, and
     // received rows get theirs from their senders
@@ -670,9 +682,15 @@ glm5x_status glm5x_moe_ep_forward(glm5x_moe_ep* ep, const void* hidden_bf16, int
   da.local_cap = ep->local_cap;
   da.recv_cap = ep->recv_cap;
   da.err = ep->err;
-  ep_dispatch_kernel<<<kGrid, kThreads, 0, st>>>(da);
+  // one warp per token: as many blocks as the tokens need, at most kGrid
+  const int grid = std::max(1, std::min(kGrid, (T + kThreads / 32 - 1) / (kThreads / 32)));
+  ep->done_total += (unsigned long long)grid;
+  da.done = ep->done;
+  da.done_target = ep->done_total;
+  ep_dispatch_kernel<<<grid, kThreads, 0, st>>>(da);
+  // one arrival per source rank and forward
   ep_wait_arrivals_kernel<<<1, 32, 0, st>>>(at<uint64_t>(ep->block, ep->L.arrive),
-                                            epoch * (uint64_t)W * kGrid, ep->err);
+                                            epoch * (uint64_t)W, ep->err);
   if (cudaGetLastError() != cudaSuccess) return cuda_fail("dispatch");
   mark();
   // experts over [local tokens | received rows]
@@ -699,7 +717,7 @@ glm5x_status glm5x_moe_ep_forward(glm5x_moe_ep* ep, const void* hidden_bf16, int
   ca.recv_cap = ep->recv_cap;
   ca.epoch = epoch;
   ca.err = ep->err;
-  ep_combine_kernel<<<kGrid, kThreads, 0, st>>>(ca);
+  ep_combine_kernel<<<grid, kThreads, 0, st>>>(ca);
   if (cudaGetLastError() != cudaSuccess) return cuda_fail("combine");
   mark();
   if (ep->profiling && evs.size() == GLM5X_EP_STAGES + 1) ep->pending.push_back(std::move(evs));
@@ -774,7 +792,8 @@ void glm5x_moe_ep_destroy(glm5x_moe_ep* ep) {
     if (s != ep->rank && ep->peers.base[s]) cudaIpcCloseMemHandle(ep->peers.base[s]);
   for (void* q : {static_cast<void*>(ep->block), static_cast<void*>(ep->ids),
                   static_cast<void*>(ep->wts), static_cast<void*>(ep->pos),
-                  static_cast<void*>(ep->small), static_cast<void*>(ep->err)})
+                  static_cast<void*>(ep->small), static_cast<void*>(ep->err),
+                  static_cast<void*>(ep->done)})
     if (q) cudaFree(q);
   for (auto& evs : ep->pending)
     for (cudaEvent_t e : evs) cudaEventDestroy(e);
