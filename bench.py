@@ -783,6 +783,8 @@ def run_ours(args) -> None:
         layer.set_tile_n(args.tile_n)
     if args.single_cta:
         layer.set_pair_mma(False)
+    if args.pair_ring >= 0:
+        layer.set_pair_scale_ring(bool(args.pair_ring))
     if args.down_tiles:
         mode = args.down_tiles
         layer.set_token_major_down(mode == "tm")
@@ -940,6 +942,8 @@ def main() -> None:
     ap.add_argument("--down-tiles", default="", choices=["", "tm", "128", "256"],
                     help="down projection tiles: token-major or weight-major width (tuning)")
     ap.add_argument("--experts", type=int, default=0, help="override experts (profiling only)")
+    ap.add_argument("--pair-ring", type=int, default=-1, choices=[-1, 0, 1],
+                    help="CTA-pair GEMMs in the scale-ring form (tuning; -1 = engine default)")
     ap.add_argument("--weight-tile-rows", type=int, default=0, choices=[0, 128, 256],
                     help="weight rows per narrow-token tile (tuning; 0 = the engine's default)")
     ap.add_argument("--decode-experts", type=int, default=0,

@@ -479,6 +479,11 @@ glm5x_status glm5x_moe_set_token_major_down(glm5x_moe* moe, int32_t enable);
  * tile width 128 or 256 (0 = the gate/up GEMM's). Used when token-major tiles
  * are off. */
 glm5x_status glm5x_moe_set_down_tile_n(glm5x_moe* moe, int32_t bn);
+/* CTA-pair GEMMs (256-row token tiles) with their block scales fetched by
+ * the scale-staging warps (cp.async into a small ring) instead of the tile
+ * copies' producer, leaving the operand ring six stages of weight and token
+ * tiles (enable = 1), or the default form (0). Same results. */
+glm5x_status glm5x_moe_set_pair_scale_ring(glm5x_moe* moe, int32_t enable);
 /* Weight rows per tile of the GEMMs for 32- and 64-row token tiles (small
  * batches such as decode): 256 (the default: two 128-row halves with their
  * own accumulators in one stage, so each stage hand-off streams twice the

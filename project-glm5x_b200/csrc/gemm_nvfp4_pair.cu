@@ -93,6 +93,92 @@ __device__ __forceinline__ uint16_t f2bf(float x) {
   return __bfloat16_as_ushort(__float2bfloat16_rn(x));
 }
 
+// Epilogue warps 8-15 of both CTAs: drain this CTA's accumulator half to
+// registers, hand it back to the leader, then SwiGLU (EPI 0, BF16 h and the
+// slab amax) or the routing weight (EPI 1, BF16 y) and the stores.
+template <int EPI>
+__device__ __forceinline__ void pair_epilogue(const GemmParams& p, uint32_t tmem_base,
+                                              uint64_t* tfull, uint64_t* tempty, int pair,
+                                              int npairs, int m2_tiles, int total_tiles,
+                                              const int32_t* s_ntp, const int32_t* s_cnt,
+                                              const int32_t* s_start, uint32_t rank, int warp,
+                                              int lane) {
+    const int q = warp & 3;
+    const int half_cols = (warp - kEpiWarp0) >> 2;
+    const uint32_t lead_tempty = mapa_shared(smem_u32(tempty), 0);
+    uint32_t acc_phase = 0;
+    for (int tile = pair; tile < total_tiles; tile += npairs) {
+      PairTile ti;
+      if (!decode_pair_tile(tile, m2_tiles, p.nseg, s_ntp, s_cnt, s_start, ti)) continue;
+      if (!mbar_wait_cluster(tfull, acc_phase, p.err)) break;
+      tc_fence_after();
+      const uint32_t t_row = tmem_base + ((uint32_t)(32 * q) << 16);
+      // drain to registers and hand the accumulator back before the math
+      constexpr int kChunks = kBN / 64;
+      uint32_t v[kChunks][32];
+#pragma unroll
+      for (int i = 0; i < kChunks; ++i)
+        if (32 * half_cols + 64 * i < ti.n_valid)
+          tmem_ld_32x32b_x32(t_row + 32 * half_cols + 64 * i, v[i]);
+      tmem_ld_wait();
+#pragma unroll
+      for (int i = 0; i < kChunks; ++i) reg_fence(v[i]);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster_relaxed(lead_tempty);
+      acc_phase ^= 1u;
+      const int m_tile = 2 * ti.m2 + (int)rank;  // this CTA's 128-row weight tile
+      const float bscale = p.b_global[ti.seg];
+      if (EPI == 0) {
+        const float s_gate = bscale * p.a_global[2 * ti.seg];
+        const float s_up = bscale * p.a_global[2 * ti.seg + 1];
+        const bool lo = lane < 16;
+        const int j = m_tile * 64 + 16 * q + (lane & 15);
+        const int hcols = p.M_per / 2;
+        float amax = 0.0f;
+#pragma unroll
+        for (int ch = 0; ch < kChunks; ++ch) {
+          const int c0 = 32 * half_cols + 64 * ch;
+          if (c0 >= ti.n_valid) break;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float send = __uint_as_float(lo ? v[ch][i + 16] : v[ch][i]);
+            const float recv = __shfl_xor_sync(0xffffffffu, send, 16);
+            const float gate = lo ? __uint_as_float(v[ch][i]) * s_gate : recv * s_gate;
+            const float up = lo ? recv * s_up : __uint_as_float(v[ch][i + 16]) * s_up;
+            const int col = c0 + i + (lo ? 0 : 16);
+            if (col < ti.n_valid) {
+              const float h = __fdividef(gate, 1.0f + __expf(-gate)) * up;
+              const uint16_t hb = f2bf(h);
+              amax = fmaxf(amax, fabsf(__uint_as_float((uint32_t)hb << 16)));
+              p.out[(size_t)(ti.row_start + col) * hcols + j] = hb;
+            }
+          }
+        }
+        for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        if (lane == 0 && amax > 0.0f)
+          atomicMax(reinterpret_cast<unsigned int*>(p.h_amax + ti.seg), __float_as_uint(amax));
+      } else {
+        const float scale = bscale * p.a_global[ti.seg];
+        const int o = m_tile * 128 + 32 * q + lane;
+#pragma unroll
+        for (int ch = 0; ch < kChunks; ++ch) {
+          const int c0 = 32 * half_cols + 64 * ch;
+          if (c0 >= ti.n_valid) break;
+          const float wmine =
+              c0 + lane < ti.n_valid ? p.row_weight[ti.row_start + c0 + lane] * scale : 0.0f;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float w = __shfl_sync(0xffffffffu, wmine, i);
+            if (c0 + i < ti.n_valid)
+              p.out[(size_t)(ti.row_start + c0 + i) * p.M_per + o] =
+                  f2bf(__uint_as_float(v[ch][i]) * w);
+          }
+        }
+      }
+    }
+}
+
 template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     nvfp4_pair_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
@@ -303,80 +389,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------ epilogue (both CTAs)
     regs_alloc<kRegsEpi>();
-    const int q = warp & 3;
-    const int half_cols = (warp - kEpiWarp0) >> 2;
-    const uint32_t lead_tempty = mapa_shared(smem_u32(tempty), 0);
-    uint32_t acc_phase = 0;
-    for (int tile = pair; tile < total_tiles; tile += npairs) {
-      PairTile ti;
-      if (!decode_pair_tile(tile, m2_tiles, p.nseg, s_ntp, s_cnt, s_start, ti)) continue;
-      if (!mbar_wait_cluster(tfull, acc_phase, p.err)) break;
-      tc_fence_after();
-      const uint32_t t_row = tmem_base + ((uint32_t)(32 * q) << 16);
-      // drain to registers and hand the accumulator back before the math
-      constexpr int kChunks = kBN / 64;
-      uint32_t v[kChunks][32];
-#pragma unroll
-      for (int i = 0; i < kChunks; ++i)
-        if (32 * half_cols + 64 * i < ti.n_valid)
-          tmem_ld_32x32b_x32(t_row + 32 * half_cols + 64 * i, v[i]);
-      tmem_ld_wait();
-#pragma unroll
-      for (int i = 0; i < kChunks; ++i) reg_fence(v[i]);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster_relaxed(lead_tempty);
-      acc_phase ^= 1u;
-      const int m_tile = 2 * ti.m2 + (int)rank;  // this CTA's 128-row weight tile
-      const float bscale = p.b_global[ti.seg];
-      if (EPI == 0) {
-        const float s_gate = bscale * p.a_global[2 * ti.seg];
-        const float s_up = bscale * p.a_global[2 * ti.seg + 1];
-        const bool lo = lane < 16;
-        const int j = m_tile * 64 + 16 * q + (lane & 15);
-        const int hcols = p.M_per / 2;
-        float amax = 0.0f;
-#pragma unroll
-        for (int ch = 0; ch < kChunks; ++ch) {
-          const int c0 = 32 * half_cols + 64 * ch;
-          if (c0 >= ti.n_valid) break;
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float send = __uint_as_float(lo ? v[ch][i + 16] : v[ch][i]);
-            const float recv = __shfl_xor_sync(0xffffffffu, send, 16);
-            const float gate = lo ? __uint_as_float(v[ch][i]) * s_gate : recv * s_gate;
-            const float up = lo ? recv * s_up : __uint_as_float(v[ch][i + 16]) * s_up;
-            const int col = c0 + i + (lo ? 0 : 16);
-            if (col < ti.n_valid) {
-              const float h = __fdividef(gate, 1.0f + __expf(-gate)) * up;
-              const uint16_t hb = f2bf(h);
-              amax = fmaxf(amax, fabsf(__uint_as_float((uint32_t)hb << 16)));
-              p.out[(size_t)(ti.row_start + col) * hcols + j] = hb;
-            }
-          }
-        }
-        for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-        if (lane == 0 && amax > 0.0f)
-          atomicMax(reinterpret_cast<unsigned int*>(p.h_amax + ti.seg), __float_as_uint(amax));
-      } else {
-        const float scale = bscale * p.a_global[ti.seg];
-        const int o = m_tile * 128 + 32 * q + lane;
-#pragma unroll
-        for (int ch = 0; ch < kChunks; ++ch) {
-          const int c0 = 32 * half_cols + 64 * ch;
-          if (c0 >= ti.n_valid) break;
-          const float wmine =
-              c0 + lane < ti.n_valid ? p.row_weight[ti.row_start + c0 + lane] * scale : 0.0f;
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float w = __shfl_sync(0xffffffffu, wmine, i);
-            if (c0 + i < ti.n_valid)
-              p.out[(size_t)(ti.row_start + c0 + i) * p.M_per + o] =
-                  f2bf(__uint_as_float(v[ch][i]) * w);
-          }
-        }
-      }
-    }
+    pair_epilogue<EPI>(p, tmem_base, tfull, tempty, pair, npairs, m2_tiles, total_tiles, s_ntp,
+                       s_cnt, s_start, rank, warp, lane);
   }
 
   tc_fence_before();
@@ -386,18 +400,310 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) tmem_dealloc_pair(tmem_base, kTmemCols);
 }
 
+// ---------------------------------------------------------------------------
+// Scale-ring form (RING): the operand ring holds only the weight and token
+// tiles (32 KB a stage, six stages), so the producer issues two tensor copies
+// per stage; the scale chunks of a stage (this CTA's weight rows, 2 KB, and
+// the tile's token rows, up to 4 KB) are fetched by the four staging warps
+// themselves with 16-byte cp.async copies (load/store unit, not the TMA
+// engine) into a three-slot ring two stages ahead of their use, and go from
+// there into one of five TMEM scale slots, which the MMA thread hands back by
+// a commit on sf_free once the slot's MMAs are done.
+constexpr int kRStages = 6;
+constexpr int kRStageBytes = kABytes + kBBytes;          // 32 KB
+constexpr int kTSlots = 5;                               // TMEM scale slots
+constexpr int kRSlots = 3;                               // shared-memory scale ring
+constexpr int kRSlotBytes = kSfaBytes + kSfbBytes;       // 6 KB
+constexpr size_t kRSmem = (size_t)kRStages * kRStageBytes + kRSlots * kRSlotBytes + 1024 + 256;
+static_assert(kSfBase + kTSlots * (kSfaCols + kSfbCols) <= kTmemCols, "TMEM budget (ring)");
+static_assert((2 * kRStages + 2 * kTSlots + 3) * 8 + 4 <= 256, "barrier area (ring)");
+static_assert(kRSmem + 3 * 4 * (kMaxSeg + 1) <= 232448, "shared memory budget (ring)");
+
+// The stages of this pair's tiles in order, for the staging warps' lookahead.
+struct StageCursor {
+  int tile, ks;
+  PairTile ti;
+  bool valid;
+};
+
+__device__ __forceinline__ void cursor_seek(StageCursor& c, int tile, int npairs,
+                                            int total_tiles, int m2_tiles, int nseg,
+                                            const int32_t* ntp, const int32_t* cnt,
+                                            const int32_t* start) {
+  c.valid = false;
+  for (; tile < total_tiles; tile += npairs)
+    if (decode_pair_tile(tile, m2_tiles, nseg, ntp, cnt, start, c.ti)) {
+      c.tile = tile;
+      c.ks = 0;
+      c.valid = true;
+      return;
+    }
+}
+
+__device__ __forceinline__ void cursor_next(StageCursor& c, int ks_count, int npairs,
+                                            int total_tiles, int m2_tiles, int nseg,
+                                            const int32_t* ntp, const int32_t* cnt,
+                                            const int32_t* start) {
+  if (!c.valid) return;
+  if (++c.ks < ks_count) return;
+  cursor_seek(c, c.tile + npairs, npairs, total_tiles, m2_tiles, nseg, ntp, cnt, start);
+}
+
 template <int EPI>
-cudaError_t launch_pair(const CUtensorMap* ta, const CUtensorMap* tb, const CUtensorMap* tsfa,
-                        const CUtensorMap* tsfb, const GemmParams& p, int grid,
-                        cudaStream_t st) {
-  auto kern = nvfp4_pair_gemm_kernel<EPI>;
+__global__ void __launch_bounds__(kThreads, 1)
+    nvfp4_pair_gemm_ring_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                                const __grid_constant__ CUtensorMap tmap_b32,
+                                const __grid_constant__ CUtensorMap tmap_b64,
+                                const __grid_constant__ CUtensorMap tmap_b128,
+                                const GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* ring = smem + kRStages * kRStageBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + kRSlots * kRSlotBytes);  // leader's used
+  uint64_t* empty = full + kRStages;
+  uint64_t* sf_ready = empty + kRStages;   // leader's used
+  uint64_t* sf_free = sf_ready + kTSlots;
+  uint64_t* tfull = sf_free + kTSlots;
+  uint64_t* tempty = tfull + 1;            // leader's used
+  uint64_t* drained = tempty + 1;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drained + 1);
+  __shared__ int32_t s_ntp[kMaxSeg + 1], s_cnt[kMaxSeg], s_start[kMaxSeg + 1];
+  __shared__ bool s_staging_ok;
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int m2_tiles = p.M_per / kPM;
+  const int ks_count = p.K / 256;
+  const int kc_per_rb = p.K / 64;
+
+  for (int i = threadIdx.x; i <= p.nseg; i += blockDim.x) {
+    s_ntp[i] = p.ntile_prefix[i];
+    s_start[i] = p.seg_start[i];
+    if (i < p.nseg) s_cnt[i] = p.seg_count[i];
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kRStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int s = 0; s < kTSlots; ++s) {
+      mbar_init(&sf_ready[s], 8);  // 4 staging warps in each CTA
+      mbar_init(&sf_free[s], 1);
+    }
+    mbar_init(tfull, 1);
+    mbar_init(tempty, 2 * kEpiWarps);
+    mbar_init(drained, 1);
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_holder, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  const int total_tiles = m2_tiles * s_ntp[p.nseg];
+
+  if (warp < kEpiWarp0) {
+  regs_dealloc<kRegsLow>();
+  if (warp == 0) {
+    // ------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmap_a);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = pair; tile < total_tiles && ok; tile += npairs) {
+        PairTile ti;
+        if (!decode_pair_tile(tile, m2_tiles, p.nseg, s_ntp, s_cnt, s_start, ti)) continue;
+        const int n_mma = (ti.n_valid + 15) & ~15;
+        const int half = n_mma / 2;
+        const int box = half <= 32 ? 32 : (half <= 64 ? 64 : 128);
+        const CUtensorMap* mb = box == 32 ? &tmap_b32 : (box == 64 ? &tmap_b64 : &tmap_b128);
+        const int a_row = ti.seg * p.M_per + ti.m2 * kPM + (int)rank * 128;
+        const uint32_t cta_bytes = kABytes + box * kBK;
+        for (int ks = 0; ks < ks_count; ++ks) {
+          if (!mbar_wait_cluster(&empty[stage], phase ^ 1u, p.err)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + stage * kRStageBytes;
+          uint8_t* sb = sa + kABytes;
+          const uint32_t lead_full = mapa_shared(smem_u32(&full[stage]), 0);
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * cta_bytes);
+          tma_load_2d_pair(sa, &tmap_a, lead_full, ks * kBK, a_row);
+          tma_load_2d_pair(sb, mb, lead_full, ks * kBK, ti.row_start + (int)rank * half);
+          if (++stage == kRStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------ MMA (leader)
+    if (leader && lane == 0) {
+      int stage = 0, slot = 0;
+      uint32_t phase = 0, sphase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int tile = pair; tile < total_tiles && ok; tile += npairs) {
+        PairTile ti;
+        if (!decode_pair_tile(tile, m2_tiles, p.nseg, s_ntp, s_cnt, s_start, ti)) continue;
+        const uint32_t n_mma = (uint32_t)((ti.n_valid + 15) & ~15);
+        const uint32_t idesc = idesc_fp4(kPM, n_mma, 0, 0, 0);
+        if (!mbar_wait_cluster(tempty, acc_phase ^ 1u, p.err)) break;
+        tc_fence_after();
+        for (int ks = 0; ks < ks_count; ++ks) {
+          if (!mbar_wait_cluster(&full[stage], phase, p.err) ||
+              !mbar_wait_cluster(&sf_ready[slot], sphase, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint8_t* sa = smem + stage * kRStageBytes;
+          const uint8_t* sb = sa + kABytes;
+          const uint32_t sfa_col = tmem_base + kSfBase + slot * (kSfaCols + kSfbCols);
+          const uint32_t sfb_col = sfa_col + kSfaCols;
+          const uint32_t a_addr = smem_u32(sa), b_addr = smem_u32(sb);
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            mma_nvfp4_pair(tmem_base, desc_kmajor_sw128(a_addr + 32 * c),
+                           desc_kmajor_sw128(b_addr + 32 * c), idesc, sfa_col + 4 * c,
+                           sfb_col + 8 * c, (ks | c) != 0 ? 1u : 0u);
+          tc_commit_pair(&empty[stage], 0x3);
+          tc_commit_pair(&sf_free[slot], 0x3);
+          if (++stage == kRStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+          if (++slot == kTSlots) {
+            slot = 0;
+            sphase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit_pair(tfull, 0x3);
+        acc_phase ^= 1u;
+      }
+      tc_commit_pair(drained, 0x1);
+      mbar_wait(drained, 0, p.err);
+    }
+    __syncwarp();
+  } else if (warp < 6) {
+    // ------------------------------------------------------ scale fetch + staging
+    const int q = warp & 3;
+    const int tid = threadIdx.x - 64;  // 0..127 over the four staging warps
+    const uint32_t t_lane = tmem_base + ((uint32_t)(32 * q) << 16);
+    const uint32_t lead_ready0 = mapa_shared(smem_u32(&sf_ready[0]), 0);
+    // one stage's scale chunks into ring slot r: 384 pieces of 16 bytes
+    // (SFA 128, SFB block 0 128, SFB block 1 128 when the tile has one)
+    auto fetch = [&](const StageCursor& c, int r) {
+      if (c.valid) {
+        const int a_row = c.ti.seg * p.M_per + c.ti.m2 * kPM + (int)rank * 128;
+        const bool two = ((c.ti.n_valid + 15) & ~15) > 128;
+        const uint8_t* sfa = p.sfa + ((size_t)(a_row / 128) * kc_per_rb + c.ks * 4) * kChunk;
+        const uint8_t* sfb = p.sfb + ((size_t)(c.ti.row_start / 128) * kc_per_rb + c.ks * 4) * kChunk;
+        uint8_t* dst = ring + r * kRSlotBytes;
+        cp_async_16(dst + tid * 16, sfa + tid * 16);
+        cp_async_16(dst + kSfaBytes + tid * 16, sfb + tid * 16);
+        if (two)
+          cp_async_16(dst + kSfaBytes + 4 * kChunk + tid * 16,
+                      sfb + (size_t)kc_per_rb * kChunk + tid * 16);
+      }
+      cp_async_commit();  // an empty group when there is nothing left to fetch
+    };
+    StageCursor cur, ahead;
+    cursor_seek(cur, pair, npairs, total_tiles, m2_tiles, p.nseg, s_ntp, s_cnt, s_start);
+    ahead = cur;
+    fetch(ahead, 0);
+    cursor_next(ahead, ks_count, npairs, total_tiles, m2_tiles, p.nseg, s_ntp, s_cnt, s_start);
+    fetch(ahead, 1);
+    cursor_next(ahead, ks_count, npairs, total_tiles, m2_tiles, p.nseg, s_ntp, s_cnt, s_start);
+    int slot = 0, r = 0;
+    uint32_t sphase = 0;
+    while (cur.valid) {
+      // two stages ahead; slot (r + 2) % 3 was read by every staging warp in
+      // the previous iteration (named barrier 1 below)
+      fetch(ahead, r == 0 ? 2 : r - 1);
+      cursor_next(ahead, ks_count, npairs, total_tiles, m2_tiles, p.nseg, s_ntp, s_cnt, s_start);
+      cp_async_wait<2>();  // this stage's group has landed
+      // one thread waits until the TMEM slot's previous MMAs are done; the
+      // barrier then orders every staging thread after that wait and after
+      // every thread's copies, and all four warps leave together on a timeout
+      if (tid == 0) s_staging_ok = mbar_wait(&sf_free[slot], sphase ^ 1u, p.err);
+      named_barrier_sync(1, 128);
+      if (!s_staging_ok) break;
+      const uint8_t* ssfa = ring + r * kRSlotBytes;
+      const uint8_t* ssfb = ssfa + kSfaBytes;
+      const bool two_blocks = ((cur.ti.n_valid + 15) & ~15) > 128;
+      uint32_t ra[kSfaCols];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const uint4 v = *reinterpret_cast<const uint4*>(ssfa + c * kChunk + lane * 16);
+        ra[4 * c] = v.x; ra[4 * c + 1] = v.y; ra[4 * c + 2] = v.z; ra[4 * c + 3] = v.w;
+      }
+      uint32_t rb[kSfbCols];
+#pragma unroll
+      for (int g = 0; g < kSfbCols / 4; ++g) {
+        const int c = g / 2, h = g % 2;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (h == 0 || two_blocks)
+          v = *reinterpret_cast<const uint4*>(ssfb + (h * 4 + c) * kChunk + lane * 16);
+        rb[4 * g] = v.x; rb[4 * g + 1] = v.y; rb[4 * g + 2] = v.z; rb[4 * g + 3] = v.w;
+      }
+      named_barrier_sync(1, 128);  // slot r read by all: it may be refilled
+      tc_fence_after();
+      const uint32_t sfa_col = kSfBase + slot * (kSfaCols + kSfbCols);
+      const uint32_t sfb_col = sfa_col + kSfaCols;
+#pragma unroll
+      for (int o = 0; o < kSfaCols; o += 8) tmem_st_32x32b_x8(t_lane + sfa_col + o, ra + o);
+#pragma unroll
+      for (int o = 0; o < kSfbCols; o += 8) tmem_st_32x32b_x8(t_lane + sfb_col + o, rb + o);
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster_relaxed(lead_ready0 + slot * 8u);
+      if (++slot == kTSlots) {
+        slot = 0;
+        sphase ^= 1u;
+      }
+      r = r == 2 ? 0 : r + 1;
+      cursor_next(cur, ks_count, npairs, total_tiles, m2_tiles, p.nseg, s_ntp, s_cnt, s_start);
+    }
+    cp_async_wait<0>();
+  }
+  } else {
+    regs_alloc<kRegsEpi>();
+    pair_epilogue<EPI>(p, tmem_base, tfull, tempty, pair, npairs, m2_tiles, total_tiles, s_ntp,
+                       s_cnt, s_start, rank, warp, lane);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem_base, kTmemCols);
+}
+
+template <int EPI, int RING>
+cudaError_t launch_pair(const CUtensorMap* ta, const CUtensorMap* tb, const GemmParams& p,
+                        int grid, cudaStream_t st) {
+  auto kern = RING ? nvfp4_pair_gemm_ring_kernel<EPI> : nvfp4_pair_gemm_kernel<EPI>;
+  const size_t smem = RING ? kRSmem : kSmem;
   cudaError_t e =
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem);
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = kSmem;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -406,8 +712,6 @@ cudaError_t launch_pair(const CUtensorMap* ta, const CUtensorMap* tb, const CUte
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  (void)tsfa;
-  (void)tsfb;
   // setmaxnreg.inc waits until the block's launch registers cover the split
   cudaFuncAttributes fa{};
   e = cudaFuncGetAttributes(&fa, kern);
@@ -442,11 +746,16 @@ int nvfp4_pair_gemm_grid(int num_sms) {
 
 cudaError_t launch_nvfp4_pair_gemm(int epi, const CUtensorMap* tmap_a, const CUtensorMap* tmap_b,
                                    const CUtensorMap* tmap_sfa, const CUtensorMap* tmap_sfb,
-                                   const GemmParams& p, int grid, cudaStream_t st) {
+                                   const GemmParams& p, int grid, cudaStream_t st, int ring) {
+  (void)tmap_sfa;
+  (void)tmap_sfb;
   if (p.nseg > kMaxSeg || p.K % 256 || p.M_per % kPM || grid < 2 || grid % 2)
     return cudaErrorInvalidValue;
-  return epi == 0 ? launch_pair<0>(tmap_a, tmap_b, tmap_sfa, tmap_sfb, p, grid, st)
-                  : launch_pair<1>(tmap_a, tmap_b, tmap_sfa, tmap_sfb, p, grid, st);
+  if (ring)
+    return epi == 0 ? launch_pair<0, 1>(tmap_a, tmap_b, p, grid, st)
+                    : launch_pair<1, 1>(tmap_a, tmap_b, p, grid, st);
+  return epi == 0 ? launch_pair<0, 0>(tmap_a, tmap_b, p, grid, st)
+                  : launch_pair<1, 0>(tmap_a, tmap_b, p, grid, st);
 }
 
 }  // namespace glm5x

@@ -202,9 +202,12 @@ size_t nvfp4_gemm_smem_bytes(int bn);
 // uint8 tensors with a {256, 8} box (four 512-byte chunks). grid = an even
 // CTA count, at most nvfp4_pair_gemm_grid().
 int nvfp4_pair_gemm_grid(int num_sms);
+// ring = 1: the scale-ring form (operand ring of six 32 KB stages, scale
+// chunks fetched by the staging warps with cp.async into a three-slot ring,
+// five TMEM scale slots released by sf_free commits).
 cudaError_t launch_nvfp4_pair_gemm(int epi, const CUtensorMap* tmap_a, const CUtensorMap* tmap_b,
                                    const CUtensorMap* tmap_sfa, const CUtensorMap* tmap_sfb,
-                                   const GemmParams& p, int grid, cudaStream_t st);
+                                   const GemmParams& p, int grid, cudaStream_t st, int ring = 0);
 
 // ------------------------------------------------------------ combine.cu
 // out[t, :] (+)= sum_{s < kk} y[pos[t, s], :] in slot order (FP32

@@ -250,6 +250,8 @@ struct glm5x_moe {
   // tiles: 256 as two halves per stage (the default: config-4 decode 0.544 ->
   // 0.467 ms, 0.67 -> 0.78 of HBM), or 128 (glm5x_moe_set_weight_tile_rows)
   int weight_rows = 256;
+  // CTA-pair GEMMs in the scale-ring form (glm5x_moe_set_pair_scale_ring)
+  int pair_ring = 0;
   CUtensorMap tm_act[4]{}, tm_h[4]{};  // box rows 32, 64, 128, 256
 
   glm5x_status fail(glm5x_status st, const char* fmt, ...) {
@@ -1135,7 +1137,7 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
   const bool pair = !mx && bn == 256 && m->use_pair && m->pair_grid >= 2;
   G5_CHECK(m,
            pair ? launch_nvfp4_pair_gemm(0, &m->tm_w13, m->tm_act, &m->tm_w13_sf, &m->tm_act_sf,
-                                         g1, m->pair_grid, st)
+                                         g1, m->pair_grid, st, m->pair_ring)
                 : launch_nvfp4_grouped_gemm(bn, 0, &m->tm_w13, m->tm_act, g1, m->num_sms, st,
                                             mx ? 1 : 0, m->weight_rows),
            "gate/up GEMM");
@@ -1186,7 +1188,7 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
   } else {
     G5_CHECK(m,
              pair ? launch_nvfp4_pair_gemm(1, &m->tm_w2, m->tm_h, &m->tm_w2_sf, &m->tm_h_sf, g2,
-                                           m->pair_grid, st)
+                                           m->pair_grid, st, m->pair_ring)
                   : launch_nvfp4_grouped_gemm(bn, 1, &m->tm_w2, m->tm_h, g2, m->num_sms, st,
                                               mx ? 1 : 0, m->weight_rows),
              "down GEMM");
@@ -1666,6 +1668,12 @@ glm5x_status glm5x_moe_set_pair_mma(glm5x_moe* m, int32_t enable) {
 glm5x_status glm5x_moe_set_token_major_down(glm5x_moe* m, int32_t enable) {
   if (!m) return fail_global(GLM5X_INVALID_STATE, "null engine");
   m->token_major_down = enable != 0;
+  return GLM5X_OK;
+}
+
+glm5x_status glm5x_moe_set_pair_scale_ring(glm5x_moe* m, int32_t enable) {
+  if (!m) return fail_global(GLM5X_INVALID_STATE, "null engine");
+  m->pair_ring = enable ? 1 : 0;
   return GLM5X_OK;
 }
 

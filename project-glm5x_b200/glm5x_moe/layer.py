@@ -408,6 +408,10 @@ class GLM5XMoELayer:
                                                     diag.data_ptr()), self._h)
         return sel, diag
 
+    def set_pair_scale_ring(self, enable: bool) -> None:
+        """CTA-pair GEMMs with the staging warps fetching the block scales."""
+        N.check(N.lib().glm5x_moe_set_pair_scale_ring(self._h, 1 if enable else 0), self._h)
+
     def set_weight_tile_rows(self, rows: int) -> None:
         """Weight rows per tile for narrow token tiles: 128, or 256 as two
         halves per stage (small batches)."""

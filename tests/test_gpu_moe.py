@@ -43,6 +43,13 @@ def test_routed_expert_path_small_shapes(T, bn, pair, tm):
     _routed_path(T, bn, pair, tm, 128)
 
 
+@pytest.mark.parametrize("T", [7, 300, 520])
+def test_routed_expert_path_pair_scale_ring(T):
+    """256-row token tiles on CTA pairs with the block scales fetched by the
+    staging warps (scale-ring form): the same outputs as the oracle."""
+    _routed_path(T, 256, True, False, 128, ring=True)
+
+
 @pytest.mark.parametrize("T,bn", [(1, 0), (5, 32), (40, 32), (100, 64), (130, 32), (7, 64)])
 def test_routed_expert_path_256_row_weight_tiles(T, bn):
     """Narrow token tiles with 256 weight rows per tile (two 128-row halves
@@ -50,7 +57,7 @@ def test_routed_expert_path_256_row_weight_tiles(T, bn):
     _routed_path(T, bn, True, False, 256)
 
 
-def _routed_path(T, bn, pair, tm, weight_rows):
+def _routed_path(T, bn, pair, tm, weight_rows, ring=False):
     """Every token-tile width (256-row tiles on CTA pairs and on single CTAs),
     the token-major and weight-major down projections, segments that span
     several tiles and narrow tiles."""
@@ -60,6 +67,7 @@ def _routed_path(T, bn, pair, tm, weight_rows):
     layer.set_pair_mma(pair)
     layer.set_token_major_down(tm)
     layer.set_weight_tile_rows(weight_rows)
+    layer.set_pair_scale_ring(ring)
     experts, deq = {}, {}
     for e in list(range(E)) + [-1]:
         ex, dq = make_expert(H, I, 1000 + e)
@@ -77,14 +85,15 @@ def _routed_path(T, bn, pair, tm, weight_rows):
     layer.close()
 
 
-@pytest.mark.parametrize("pair", [True, False])
-def test_glm_shape_256_tiles(pair):
+@pytest.mark.parametrize("pair,ring", [(True, False), (False, False), (True, True)])
+def test_glm_shape_256_tiles(pair, ring):
     """GLM-shaped experts with 256-row token tiles (the prefill path), on CTA
-    pairs and on single CTAs."""
+    pairs (both forms) and on single CTAs."""
     H, I, E, k, T = 6144, 2048, 4, 4, 300
     layer = _layer(H, I, E, k, True, T)
     layer.set_tile_n(256)
     layer.set_pair_mma(pair)
+    layer.set_pair_scale_ring(ring)
     deq = {}
     for e in list(range(E)) + [-1]:
         ex, dq = make_expert(H, I, 900 + e)
@@ -98,7 +107,7 @@ def test_glm_shape_256_tiles(pair):
     layer.check()
     shared = deq.pop(-1)
     want, _ = oracle_forward(bf16_to_np(hidden), ids, w, deq, shared)
-    _assert_close(out.cpu().numpy(), want, f"pair={pair}")
+    _assert_close(out.cpu().numpy(), want, f"pair={pair} ring={ring}")
     layer.close()
 
 
