@@ -22,12 +22,13 @@
 //              finish then adds one to each destination's arrival counter;
 //   experts    after all arrivals: the engine over [local tokens | received
 //              rows] in one call; local tokens take the shared expert (FP32
-//              out), received rows their held experts, whose weighted sum
-//              per row is kept as BF16 in this rank's partial area;
-//   ready      a flag in every source's memory;
+//              out), received rows their held experts, and the engine's last
+//              kernel stores each received row's weighted sum as BF16 straight
+//              into its source's return area (NVLink stores), then raises a
+//              ready flag in every source;
 //   combine    after all W ready flags: each local token's partial sums are
-//              loaded from the destinations' partial areas (NVLink loads)
-//              and added in destination order onto its shared-expert row.
+//              read from this rank's own return area and added in
+//              destination order onto its shared-expert row.
 //
 // The received rows and their sums match ep.py's NCCL all-to-all path bit
 // for bit (same rows, same order, same BF16 rounding, same FP32 order).
@@ -57,7 +58,7 @@ glm5x_status engine_forward_peer_rows(glm5x_moe* m, const uint16_t* rows, int64_
                                       int64_t local_tokens, int64_t recv_cap,
                                       const int32_t* ids, const float* weights,
                                       const float* row_amax, const int32_t* recv_count,
-                                      float* out_local, uint16_t* partial, cudaStream_t st);
+                                      float* out_local, const RowReturn* ret, cudaStream_t st);
 int engine_device(const glm5x_moe* m);
 
 namespace {
@@ -72,7 +73,8 @@ struct Layout {
   size_t ids[2];      // [local_cap + recv_cap, k] int32 (global ids, -1 = none)
   size_t wts[2];      // [local_cap + recv_cap, k] FP32
   size_t amax[2];     // [local_cap + recv_cap] FP32
-  size_t partial[2];  // [recv_cap, H] BF16 weighted expert sums of received rows
+  size_t ret[2];      // [W, local_cap, H] BF16: the sums destination d returns for this
+                      // rank's rows sent to d, at row d * local_cap + position
   size_t counts[2];   // [W, W] int32: counts[s][d] = rows s sends to d
   size_t cnt_flag[2]; // [W] uint64: epoch when source s's count row arrived
   size_t ready[2];    // [W] uint64: epoch when destination d's partial sums are ready
@@ -163,6 +165,7 @@ struct ExchangeArgs {
   const int32_t* send_count;  // [W] local
   int32_t* recv_count;        // out: rows received this forward
   int32_t* send_off;          // out [W]: first row of this rank's rows in d's receive area
+  int32_t* recv_off;          // out [W]: first received row from each source
   uint32_t* err;
 };
 
@@ -188,6 +191,11 @@ __global__ void ep_exchange_kernel(ExchangeArgs a) {
       R = a.recv_cap;
     }
     *a.recv_count = (int32_t)R;
+    int64_t off_s = 0;
+    for (int s = 0; s < a.W; ++s) {
+      a.recv_off[s] = (int32_t)off_s;
+      off_s += c[s * a.W + a.rank];
+    }
     for (int d = 0; d < a.W; ++d) {
       int64_t off = 0;
       for (int s = 0; s < a.rank; ++s) off += c[s * a.W + d];
@@ -299,21 +307,14 @@ __global__ void ep_wait_arrivals_kernel(const uint64_t* arrive, uint64_t target,
 }
 
 // ------------------------------------------------------------------ ready / combine
-__global__ void ep_ready_kernel(Peers peers, size_t ready_off, int rank, int W, uint64_t epoch) {
-  if ((int)threadIdx.x < W) {
-    __threadfence_system();
-    st_release_sys(at<uint64_t>(peers.base[threadIdx.x], ready_off) + rank, epoch);
-  }
-}
-
+// ------------------------------------------------------------------ combine
 struct CombineArgs {
   Peers peers;
-  size_t partial_off, ready_off;
+  size_t ret_off, ready_off;
+  int64_t local_cap;
   float* out;           // [T, H] FP32 holding the shared-expert rows
   const int32_t* pos;   // [T, W]
-  const int32_t* send_off;
   int T, H, W, rank;
-  int64_t recv_cap;
   uint64_t epoch;
   uint32_t* err;
 };
@@ -325,25 +326,21 @@ __global__ void __launch_bounds__(kThreads) ep_combine_kernel(CombineArgs a) {
   const int lane = threadIdx.x & 31;
   const int warps = gridDim.x * (blockDim.x >> 5);
   const int vec = a.H / 8;
+  const uint4* ret = at<const uint4>(a.peers.base[a.rank], a.ret_off);
   for (int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < a.T; t += warps) {
     int64_t my_row = -1;
     if (lane < a.W) {
       const int p = a.pos[(int64_t)t * a.W + lane];
       if (p >= 0) {
-        my_row = a.send_off[lane] + p;
-        if (my_row >= a.recv_cap) {
-          atomicOr(a.err, kErrBounds);
-          my_row = -1;
-        }
+        if (p < a.local_cap) my_row = (int64_t)lane * a.local_cap + p;
+        else atomicOr(a.err, kErrBounds);
       }
     }
     const uint4* src[kMaxWorld];
 #pragma unroll
     for (int d = 0; d < kMaxWorld; ++d) {
       const int64_t row = __shfl_sync(0xffffffffu, my_row, d & 31);
-      src[d] = (d < a.W && row >= 0)
-                   ? at<const uint4>(a.peers.base[d], a.partial_off) + row * vec
-                   : nullptr;
+      src[d] = (d < a.W && row >= 0) ? ret + row * vec : nullptr;
     }
     float4* o = reinterpret_cast<float4*>(a.out + (int64_t)t * a.H);
     for (int v = lane; v < vec; v += 32) {
@@ -352,8 +349,8 @@ __global__ void __launch_bounds__(kThreads) ep_combine_kernel(CombineArgs a) {
 #pragma unroll
       for (int d = 0; d < kMaxWorld; ++d) {
         if (!src[d]) continue;
-        // written by another GPU this forward: load past the L1 (cache volatile)
-        const uint4 q = __ldcv(src[d] + v);
+        // stored by another GPU this forward: read past the L1
+        const uint4 q = __ldcg(src[d] + v);
         const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -406,9 +403,11 @@ struct glm5x_moe_ep {
   int32_t* ids = nullptr;     // [local_cap, k] routes of the local tokens
   float* wts = nullptr;
   int32_t* pos = nullptr;     // [local_cap, W]
-  int32_t* small = nullptr;   // send_count [W], send_off [W], recv_count [1]
+  int32_t* small = nullptr;   // send_count [W], send_off [W], recv_count [1], recv_off [W]
   unsigned long long* done = nullptr;  // finished dispatch blocks, all forwards
   unsigned long long done_total = 0;
+  unsigned long long* rdone = nullptr;  // finished return blocks, all forwards
+  unsigned long long rdone_total = 0;
   uint32_t* err = nullptr;
   cudaStream_t stream = nullptr;
   std::string error;
@@ -439,7 +438,7 @@ Layout make_layout(int64_t local_cap, int64_t recv_cap, int H, int k, int W) {
     L.ids[p] = off; off = align_up(off + (size_t)rows * k * 4);
     L.wts[p] = off; off = align_up(off + (size_t)rows * k * 4);
     L.amax[p] = off; off = align_up(off + (size_t)rows * 4);
-    L.partial[p] = off; off = align_up(off + (size_t)recv_cap * H * 2);
+    L.ret[p] = off; off = align_up(off + (size_t)W * local_cap * H * 2);
     L.counts[p] = off; off = align_up(off + (size_t)W * W * 4);
     L.cnt_flag[p] = off; off = align_up(off + (size_t)W * 8);
     L.ready[p] = off; off = align_up(off + (size_t)W * 8);
@@ -494,14 +493,16 @@ glm5x_status glm5x_moe_ep_create(const glm5x_moe_config* cfg, int device, int32_
             cudaMalloc(&ep->ids, (size_t)ep->local_cap * ep->k * 4) == cudaSuccess &&
             cudaMalloc(&ep->wts, (size_t)ep->local_cap * ep->k * 4) == cudaSuccess &&
             cudaMalloc(&ep->pos, (size_t)ep->local_cap * W * 4) == cudaSuccess &&
-            cudaMalloc(&ep->small, (2 * W + 1) * 4) == cudaSuccess &&
+            cudaMalloc(&ep->small, (3 * W + 1) * 4) == cudaSuccess &&
+            cudaMalloc(&ep->rdone, 8) == cudaSuccess &&
             cudaMalloc(&ep->err, 4) == cudaSuccess &&
             cudaMalloc(&ep->done, 8) == cudaSuccess &&
             cudaStreamCreateWithFlags(&ep->stream, cudaStreamNonBlocking) == cudaSuccess;
   if (ok)
     ok = cudaMemsetAsync(ep->block, 0, ep->L.total, ep->stream) == cudaSuccess &&
          cudaMemsetAsync(ep->err, 0, 4, ep->stream) == cudaSuccess &&
-         cudaMemsetAsync(ep->done, 0, 8, ep->stream) == cudaSuccess;
+         cudaMemsetAsync(ep->done, 0, 8, ep->stream) == cudaSuccess &&
+         cudaMemsetAsync(ep->rdone, 0, 8, ep->stream) == cudaSuccess;
   if (ok) {
     // every id slot starts as -1: local rows never carry routed slots, and
     // received rows get theirs from their senders
@@ -618,6 +619,7 @@ glm5x_status glm5x_moe_ep_forward(glm5x_moe_ep* ep, const void* hidden_bf16, int
   int32_t* send_count = ep->small;
   int32_t* send_off = ep->small + W;
   int32_t* recv_count = ep->small + 2 * W;
+  int32_t* recv_off = ep->small + 2 * W + 1;
   auto cuda_fail = [&](const char* what) {
     return ep_fail(ep, GLM5X_DEVICE_ERROR, std::string("ep forward: ") + what + ": " +
                                                cudaGetErrorString(cudaGetLastError()));
@@ -653,6 +655,7 @@ glm5x_status glm5x_moe_ep_forward(glm5x_moe_ep* ep, const void* hidden_bf16, int
   xa.send_count = send_count;
   xa.recv_count = recv_count;
   xa.send_off = send_off;
+  xa.recv_off = recv_off;
   xa.err = ep->err;
   ep_exchange_kernel<<<1, 64, 0, st>>>(xa);
   ep_clear_tail_kernel<<<592, 256, 0, st>>>(at<int32_t>(ep->block, ep->L.ids[p]),
@@ -693,28 +696,41 @@ glm5x_status glm5x_moe_ep_forward(glm5x_moe_ep* ep, const void* hidden_bf16, int
                                             epoch * (uint64_t)W, ep->err);
   if (cudaGetLastError() != cudaSuccess) return cuda_fail("dispatch");
   mark();
-  // experts over [local tokens | received rows]
+  // experts over [local tokens | received rows]; each received row's sum goes
+  // back into its source's return area, and the sources' ready flags rise
+  RowReturn rr{};
+  for (int s = 0; s < W; ++s) {
+    rr.base[s] = at<uint16_t>(ep->peers.base[s], ep->L.ret[p]) +
+                 (size_t)ep->rank * ep->local_cap * ep->H;
+    rr.flag[s] = at<uint64_t>(ep->peers.base[s], ep->L.ready[p]) + ep->rank;
+  }
+  rr.recv_off = recv_off;
+  rr.W = W;
+  rr.limit = ep->local_cap;
+  rr.epoch = epoch;
+  rr.grid = (int)std::max<int64_t>(1, std::min<int64_t>(592, ep->recv_cap));
+  ep->rdone_total += (unsigned long long)rr.grid;
+  rr.done = ep->rdone;
+  rr.done_target = ep->rdone_total;
+  rr.err = ep->err;
   const glm5x_status es = engine_forward_peer_rows(
       ep->engine, at<uint16_t>(ep->block, ep->L.rows[p]), ep->local_cap, T, ep->recv_cap,
       at<int32_t>(ep->block, ep->L.ids[p]), at<float>(ep->block, ep->L.wts[p]),
-      ep->mx ? nullptr : at<float>(ep->block, ep->L.amax[p]), recv_count, out,
-      at<uint16_t>(ep->block, ep->L.partial[p]), st);
+      ep->mx ? nullptr : at<float>(ep->block, ep->L.amax[p]), recv_count, out, &rr, st);
   if (es != GLM5X_OK) return ep_fail(ep, es, glm5x_moe_error_message(ep->engine));
   mark();
-  // ready, then pull the partial sums back
-  ep_ready_kernel<<<1, 32, 0, st>>>(ep->peers, ep->L.ready[p], ep->rank, W, epoch);
+  // the partial sums, returned into this rank's memory
   CombineArgs ca{};
   ca.peers = ep->peers;
-  ca.partial_off = ep->L.partial[p];
+  ca.ret_off = ep->L.ret[p];
+  ca.local_cap = ep->local_cap;
   ca.ready_off = ep->L.ready[p];
   ca.out = out;
   ca.pos = ep->pos;
-  ca.send_off = send_off;
   ca.T = T;
   ca.H = ep->H;
   ca.W = W;
   ca.rank = ep->rank;
-  ca.recv_cap = ep->recv_cap;
   ca.epoch = epoch;
   ca.err = ep->err;
   ep_combine_kernel<<<grid, kThreads, 0, st>>>(ca);
@@ -793,7 +809,7 @@ void glm5x_moe_ep_destroy(glm5x_moe_ep* ep) {
   for (void* q : {static_cast<void*>(ep->block), static_cast<void*>(ep->ids),
                   static_cast<void*>(ep->wts), static_cast<void*>(ep->pos),
                   static_cast<void*>(ep->small), static_cast<void*>(ep->err),
-                  static_cast<void*>(ep->done)})
+                  static_cast<void*>(ep->done), static_cast<void*>(ep->rdone)})
     if (q) cudaFree(q);
   for (auto& evs : ep->pending)
     for (cudaEvent_t e : evs) cudaEventDestroy(e);

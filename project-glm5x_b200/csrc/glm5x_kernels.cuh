@@ -224,6 +224,29 @@ cudaError_t launch_combine_rows_bf16(const uint16_t* y, const int32_t* pos, int6
                                      const int32_t* count, int kk, int H, uint16_t* out,
                                      cudaStream_t st);
 
+// The same sums stored straight into their sources' memory (expert
+// parallelism over peer memory): received row r (r < *count) came from source
+// s, the last s with recv_off[s] <= r, as that source's row p = r -
+// recv_off[s]; its BF16 sum goes to base[s] + p * H (p < limit). Every thread
+// then fences its stores at system scope and the grid's last block stores
+// `epoch` into flag[s] of every source with release semantics.
+constexpr int kMaxReturnRanks = 16;
+struct RowReturn {
+  uint16_t* base[kMaxReturnRanks];
+  uint64_t* flag[kMaxReturnRanks];
+  const int32_t* recv_off;  // [W] device
+  int W;
+  int64_t limit;            // rows each source's area holds
+  uint64_t epoch;
+  unsigned long long* done;        // finished blocks, all launches (monotonic)
+  unsigned long long done_target;  // its value after this launch
+  int grid;                        // blocks of this launch
+  uint32_t* err;
+};
+cudaError_t launch_combine_rows_return(const uint16_t* y, const int32_t* pos, int64_t cap,
+                                       const int32_t* count, int kk, int H,
+                                       const RowReturn& ret, cudaStream_t st);
+
 // ------------------------------------------------------------ weights.cu
 // Interleave gate [I, K] and up [I, K] (packed NVFP4 + blocked scales) into
 // the stacked gate/up weight slot: 16 gate rows then 16 up rows per 32.

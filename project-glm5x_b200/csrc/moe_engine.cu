@@ -960,14 +960,15 @@ glm5x_status glm5x_moe_load_sidecar(glm5x_moe* m, int32_t expert, const char* pa
 // first local_tokens of them valid; they take the shared expert) and then
 // the received rows, whose count the device knows (recv_count) but the host
 // does not; ids of rows past it are -1. Outputs: the local tokens' rows
-// (FP32, `out`) and each received row's weighted expert sum as BF16 in
-// `partial` [rows - local_cap, H]; rows' max |x| come from their senders.
+// (FP32, `out`) and each received row's weighted expert sum as BF16, stored
+// into its source's memory as `ret` describes (the last block then raises the
+// sources' flags); rows' max |x| come from their senders.
 struct PeerRows {
   int64_t local_cap;
   int64_t local_tokens;
   const float* row_amax;      // [rows] (NVFP4 engines)
   const int32_t* recv_count;  // device: received rows
-  uint16_t* partial;          // [rows - local_cap, H] BF16
+  const RowReturn* ret;
 };
 
 struct PrequantRows {
@@ -1199,9 +1200,9 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
     // weighted expert sums, BF16, for the senders to pull back
     G5_CHECK(m, launch_combine(m->y_bf16, m->pb.pos, (int)peer->local_tokens, m->kk(), H, out, st),
              "combine");
-    G5_CHECK(m, launch_combine_rows_bf16(m->y_bf16, m->pb.pos + peer->local_cap * m->kk(),
-                                         N - peer->local_cap, peer->recv_count, m->kk(), H,
-                                         peer->partial, st),
+    G5_CHECK(m, launch_combine_rows_return(m->y_bf16, m->pb.pos + peer->local_cap * m->kk(),
+                                           N - peer->local_cap, peer->recv_count, m->kk(), H,
+                                           *peer->ret, st),
              "partial sums");
     ++launches;
   } else if (pq) {
@@ -1241,11 +1242,11 @@ glm5x_status engine_forward_peer_rows(glm5x_moe* m, const uint16_t* rows, int64_
                                       int64_t local_tokens, int64_t recv_cap,
                                       const int32_t* ids, const float* weights,
                                       const float* row_amax, const int32_t* recv_count,
-                                      float* out_local, uint16_t* partial, cudaStream_t st) {
+                                      float* out_local, const RowReturn* ret, cudaStream_t st) {
   if (local_tokens < 0 || local_tokens > local_cap || recv_cap < 0)
     return m->fail(GLM5X_INVALID_EXTENT, "peer rows: bad extents");
   cudaSetDevice(m->device);
-  PeerRows pr{local_cap, local_tokens, row_amax, recv_count, partial};
+  PeerRows pr{local_cap, local_tokens, row_amax, recv_count, ret};
   return run_forward(m, rows, local_cap + recv_cap, ids, weights, out_local, st, true,
                      local_tokens, nullptr, &pr);
 }

@@ -142,6 +142,73 @@ cudaError_t launch_combine_rows_bf16(const uint16_t* y, const int32_t* pos, int6
   return cudaGetLastError();
 }
 
+__global__ void combine_rows_return_kernel(const uint16_t* __restrict__ y,
+                                           const int32_t* __restrict__ pos, int64_t cap,
+                                           const int32_t* __restrict__ count, int kk, int H,
+                                           RowReturn ret) {
+  const int64_t n = cap < (int64_t)*count ? cap : (int64_t)*count;
+  __shared__ int32_t rows[32];
+  __shared__ int32_t off[kMaxReturnRanks];
+  if ((int)threadIdx.x < ret.W) off[threadIdx.x] = ret.recv_off[threadIdx.x];
+  for (int64_t r = blockIdx.x; r < n; r += gridDim.x) {
+    __syncthreads();
+    if (threadIdx.x < kk) rows[threadIdx.x] = pos[r * kk + threadIdx.x];
+    __syncthreads();
+    int s = 0;
+    for (int i = 1; i < ret.W; ++i)
+      if (off[i] <= r) s = i;
+    const int64_t p = r - off[s];
+    if (p < 0 || p >= ret.limit) {
+      if (threadIdx.x == 0) atomicOr(ret.err, 1u << 3);  // kErrBounds
+      continue;
+    }
+    uint4* dst = reinterpret_cast<uint4*>(ret.base[s] + p * H);
+    for (int v = threadIdx.x; v < H / 8; v += blockDim.x) {
+      float acc[8] = {};
+      for (int j = 0; j < kk; ++j) {
+        if (rows[j] < 0) continue;
+        const uint4 q = __ldg(reinterpret_cast<const uint4*>(y + (int64_t)rows[j] * H) + v);
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          acc[2 * i] += __uint_as_float(w[i] << 16);
+          acc[2 * i + 1] += __uint_as_float(w[i] & 0xffff0000u);
+        }
+      }
+      uint32_t o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t lo = __bfloat16_as_ushort(__float2bfloat16_rn(acc[2 * i]));
+        const uint32_t hi = __bfloat16_as_ushort(__float2bfloat16_rn(acc[2 * i + 1]));
+        o[i] = lo | (hi << 16);
+      }
+      dst[v] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+  // every store visible system-wide, then the grid's last block raises the
+  // sources' flags
+  __threadfence_system();
+  __syncthreads();
+  __shared__ bool last;
+  if (threadIdx.x == 0) last = atomicAdd(ret.done, 1ull) + 1ull == ret.done_target;
+  __syncthreads();
+  if (last && (int)threadIdx.x < ret.W) {
+    __threadfence_system();
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(ret.flag[threadIdx.x]),
+                 "l"(ret.epoch)
+                 : "memory");
+  }
+}
+
+cudaError_t launch_combine_rows_return(const uint16_t* y, const int32_t* pos, int64_t cap,
+                                       const int32_t* count, int kk, int H,
+                                       const RowReturn& ret, cudaStream_t st) {
+  if (kk > 32 || H % 8 || ret.W > kMaxReturnRanks || ret.grid <= 0)
+    return cudaErrorInvalidValue;
+  combine_rows_return_kernel<<<ret.grid, 256, 0, st>>>(y, pos, cap, count, kk, H, ret);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_interleave_gate_up(const uint8_t* gate_packed, const uint8_t* gate_sf,
                                       const uint8_t* up_packed, const uint8_t* up_sf, int I,
                                       int K, int group, uint8_t* dst_packed, uint8_t* dst_sf,
