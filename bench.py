@@ -245,14 +245,26 @@ def zipf_bias(experts: int, seed: int):
     return bias + 0.5 * (perm.to(torch.float64) + 1.0).pow(-1.1).to(torch.float32)
 
 
-def profiled_phases(fwd, hidden, steps: int, engine=None) -> tuple[dict, int]:
+def profiled_phases(fwd, hidden, steps: int, engine=None, warmup: int = 0,
+                    idle_s: float = 0.0) -> tuple[dict, int]:
     """Per-phase milliseconds of `steps` further forwards with phase events on.
     The events sit between the forward's kernels on its stream and each adds
     about 2.5 us to a step, so the timed steps run without them and the phase
     split comes from these forwards. `fwd` is the layer, or the
-    expert-parallel wrapper around `engine`."""
+    expert-parallel wrapper around `engine`. With `idle_s` and `warmup` the
+    profiled forwards follow the same idle gap and warm-up as the timed ones:
+    the SM clock under the 1 kW power cap falls over a long run of GEMMs, so
+    forwards profiled straight after the timed ones would run slower."""
     import torch
     engine = engine or fwd
+    if idle_s:
+        torch.cuda.synchronize()
+        time.sleep(idle_s)
+    for _ in range(warmup):
+        if engine is fwd:
+            fwd(hidden, want_routing=False)
+        else:
+            fwd(hidden)
     engine.set_profiling(True)
     engine.phase_times()
     for _ in range(steps):
@@ -783,14 +795,18 @@ def run_ours(args) -> None:
         layer.set_tile_n(args.tile_n)
     if args.single_cta:
         layer.set_pair_mma(False)
-    if args.pair_ring >= 0:
-        layer.set_pair_scale_ring(bool(args.pair_ring))
+    if args.pair_wide >= 0:
+        layer.set_pair_wide_stages(bool(args.pair_wide))
     if args.down_tiles:
         mode = args.down_tiles
         layer.set_token_major_down(mode == "tm")
         if mode != "tm":
             layer.set_down_tile_n(int(mode))
     hidden = make_hidden(T, seed=100 + rank, device=dev)
+    # the timed steps and the profiled ones (below) both follow a 1 s idle
+    # gap and the warm-up, so they start from the same clock state
+    torch.cuda.synchronize()
+    time.sleep(1.0)
     # warm-up
     for _ in range(args.warmup):
         layer(hidden, want_routing=False)
@@ -808,7 +824,7 @@ def run_ours(args) -> None:
     layer.check()
     ms_total = start.elapsed_time(stop)
     launches = layer.stats()["kernel_launches"] - stats0["kernel_launches"]
-    phases, nprof = profiled_phases(layer, hidden, args.steps)
+    phases, nprof = profiled_phases(layer, hidden, args.steps, warmup=args.warmup, idle_s=1.0)
     ms_step = ms_total / args.steps
     value = world * T * args.steps / (ms_total / 1000.0)
 
@@ -942,8 +958,8 @@ def main() -> None:
     ap.add_argument("--down-tiles", default="", choices=["", "tm", "128", "256"],
                     help="down projection tiles: token-major or weight-major width (tuning)")
     ap.add_argument("--experts", type=int, default=0, help="override experts (profiling only)")
-    ap.add_argument("--pair-ring", type=int, default=-1, choices=[-1, 0, 1],
-                    help="CTA-pair GEMMs in the scale-ring form (tuning; -1 = engine default)")
+    ap.add_argument("--pair-wide", type=int, default=-1, choices=[-1, 0, 1],
+                    help="CTA-pair GEMMs with 512-K stages (tuning; -1 = engine default)")
     ap.add_argument("--weight-tile-rows", type=int, default=0, choices=[0, 128, 256],
                     help="weight rows per narrow-token tile (tuning; 0 = the engine's default)")
     ap.add_argument("--decode-experts", type=int, default=0,

@@ -479,17 +479,25 @@ glm5x_status glm5x_moe_set_token_major_down(glm5x_moe* moe, int32_t enable);
  * tile width 128 or 256 (0 = the gate/up GEMM's). Used when token-major tiles
  * are off. */
 glm5x_status glm5x_moe_set_down_tile_n(glm5x_moe* moe, int32_t bn);
-/* CTA-pair GEMMs (256-row token tiles) with their block scales fetched by
- * the scale-staging warps (cp.async into a small ring) instead of the tile
- * copies' producer, leaving the operand ring six stages of weight and token
- * tiles (enable = 1), or the default form (0). Same results. */
-glm5x_status glm5x_moe_set_pair_scale_ring(glm5x_moe* moe, int32_t enable);
+/* CTA-pair GEMMs (256-row token tiles) with pipeline stages of 512 of K
+ * (enable = 1, the default: one barrier wait and one commit of the
+ * MMA-issuing thread per eight MMAs, operand, token and scale copies from
+ * three threads) or of 256 (0). Same results: every output sums the same
+ * products in the same order. */
+glm5x_status glm5x_moe_set_pair_wide_stages(glm5x_moe* moe, int32_t enable);
 /* Weight rows per tile of the GEMMs for 32- and 64-row token tiles (small
  * batches such as decode): 256 (the default: two 128-row halves with their
  * own accumulators in one stage, so each stage hand-off streams twice the
  * weight bytes) or 128 (one M = 128 MMA per K step). Both give the same
  * results: every output element sums the same products in the same order. */
 glm5x_status glm5x_moe_set_weight_tile_rows(glm5x_moe* moe, int32_t rows);
+/* Tile order of the CTA-pair GEMMs (256-row token tiles), per GEMM: 0 runs
+ * a segment's weight tiles in turn; g > 0 cuts the segments into groups of
+ * about g token tiles and runs each group weight-tile-major (weight tile 0
+ * of every segment in the group, then tile 1, ...), so light and heavy
+ * experts share the GPU at every moment. Defaults: 8 (gate/up) and 16
+ * (down). Results do not depend on it: every tile computes the same sums. */
+glm5x_status glm5x_moe_set_pair_tile_order(glm5x_moe* moe, int32_t up_group, int32_t down_group);
 /* The engine's own stream (used by glm5x_moe_forward_host and by forwards
  * given a NULL stream), as a cudaStream_t. */
 glm5x_status glm5x_moe_get_stream(glm5x_moe* moe, void** stream);

@@ -18,7 +18,12 @@
 //              once both CTAs' operands have landed and both CTAs' scales are
 //              in TMEM, and its commits arrive on both CTAs' barriers;
 //   warps 2-5  scale staging into this CTA's TMEM with tcgen05.st (one warp
-//              per lane quadrant), then an arrive on the leader's sf_ready;
+//              per lane quadrant), then an arrive on the leader's full
+//              barrier: a stage's full barrier completes when the operand
+//              bytes of both CTAs have landed and all eight staging warps
+//              have arrived, so the MMA thread waits once per stage (each
+//              wait costs the single issuing thread ~70 cycles even when the
+//              barrier is already complete);
 //   warps 8-15 epilogue: drain this CTA's accumulator half to registers,
 //              signal the leader, then SwiGLU / routing weight and stores.
 #include <cuda.h>
@@ -59,34 +64,106 @@ constexpr int kTmemCols = 512;
 static_assert(kSfBase + kStages * (kSfaCols + kSfbCols) <= kTmemCols, "TMEM budget");
 constexpr int kMaxSeg = 260;
 constexpr size_t kSmem = (size_t)kStages * kStageBytes + 1024 + 256;
-static_assert((4 * kStages + 3) * 8 + 4 <= 256, "barrier area");
-static_assert(kSmem + 3 * 4 * (kMaxSeg + 1) <= 232448, "shared memory budget");
+static_assert((3 * kStages + 3) * 8 + 4 <= 256, "barrier area");
+static_assert(kSmem + sizeof(int32_t) * (4 * kMaxSeg + 4) + 16 <= 232448, "shared memory budget");
 
 struct PairTile {
   int seg, m2, row_start, n_valid;
 };
 
-__device__ __forceinline__ bool decode_pair_tile(int tile, int m2_tiles, int nseg,
-                                                 const int32_t* __restrict__ ntp,
-                                                 const int32_t* __restrict__ cnt,
-                                                 const int32_t* __restrict__ start,
-                                                 PairTile& ti) {
-  const int key = tile / m2_tiles;
-  int lo = 0, hi = nseg;
+// The tile list of one launch, held in shared memory: per segment its
+// token-tile prefix, row count and first row, and the group boundaries of
+// the tile order.
+//
+// Order. gt == 0: segment-major (a segment's weight tiles in turn, each
+// with its token tiles next to one another). gt > 0: the segments are cut
+// into groups by where their first token tile falls (group g holds the
+// segments whose tile prefix is in [g * gt, (g + 1) * gt)), and a group's
+// tiles run weight-tile-major: weight tile 0 of every segment in the group,
+// then weight tile 1, and so on. Routed loads are skewed (at config 5 an
+// expert gets 0 to ~900 rows), so in segment order the pairs running at
+// one time work on two or three experts: all light ones (their weights
+// streamed from HBM for a few rows, the tensor pipe idle) or all heavy ones
+// (weights reused from L2, HBM idle). In group order they run the same
+// weight tile of tens of experts, light and heavy together, and HBM and the
+// tensor pipe are busy at the same time; a group's token rows (gt tiles of
+// at most 256 rows) stay in L2 across its weight tiles, and each
+// (segment, weight tile) slab is still read once, by the pairs that run its
+// token tiles side by side.
+struct PairMap {
+  int32_t ntp[kMaxSeg + 1], cnt[kMaxSeg], start[kMaxSeg + 1], gseg[kMaxSeg + 2];
+  int nseg, m2_tiles, gt;
+};
+
+// largest s in [lo, hi) with ntp[s] <= key (ntp non-decreasing, ntp[lo] <= key)
+__device__ __forceinline__ int seg_search(const int32_t* __restrict__ ntp, int lo, int hi,
+                                          int key) {
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
     if (ntp[mid] <= key) lo = mid; else hi = mid;
   }
-  const int nt = ntp[lo + 1] - ntp[lo];
-  if (nt <= 0) return false;
-  const int local = tile - m2_tiles * ntp[lo];
-  ti.seg = lo;
-  ti.m2 = local / nt;
-  const int n = local % nt;
-  ti.row_start = start[lo] + n * kBN;
-  const int left = cnt[lo] - n * kBN;
+  return lo;
+}
+
+// Every thread of the CTA; ends with the map complete and visible.
+__device__ __forceinline__ void load_pair_map(PairMap& m, const GemmParams& p, int m2_tiles) {
+  for (int i = threadIdx.x; i <= p.nseg; i += blockDim.x) {
+    m.ntp[i] = p.ntile_prefix[i];
+    m.start[i] = p.seg_start[i];
+    if (i < p.nseg) m.cnt[i] = p.seg_count[i];
+  }
+  __syncthreads();
+  const int nt = m.ntp[p.nseg];
+  int gt = p.tile_group;
+  if (gt > nt) gt = nt > 0 ? nt : 1;  // one group: weight-tile-major over all segments
+  // at most kMaxSeg + 1 groups (their kMaxSeg + 2 boundaries fit gseg)
+  if (gt > 0 && (nt + gt - 1) / gt > kMaxSeg + 1) gt = (nt + kMaxSeg) / (kMaxSeg + 1);
+  if (gt > 0) {
+    const int groups = (nt + gt - 1) / gt;
+    for (int g = threadIdx.x; g <= groups; g += blockDim.x) {
+      // first segment whose tile prefix reaches g * gt (nseg if none)
+      int lo = 0, hi = p.nseg;
+      while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (m.ntp[mid] >= g * gt) hi = mid; else lo = mid + 1;
+      }
+      m.gseg[g] = lo;
+    }
+  }
+  if (threadIdx.x == 0) {
+    m.nseg = p.nseg;
+    m.m2_tiles = m2_tiles;
+    m.gt = gt;
+  }
+  __syncthreads();
+}
+
+__device__ __forceinline__ bool decode_pair_tile(int tile, const PairMap& m, PairTile& ti) {
+  const int key = tile / m.m2_tiles;
+  int s = seg_search(m.ntp, 0, m.nseg, key);
+  int n;
+  if (m.gt > 0) {
+    const int g = m.ntp[s] / m.gt;
+    const int gs = m.gseg[g], ge = m.gseg[g + 1];
+    const int base = m.ntp[gs], gnt = m.ntp[ge] - base;
+    if (gnt <= 0) return false;
+    const int local = tile - m.m2_tiles * base;
+    ti.m2 = local / gnt;
+    const int tt = base + local % gnt;
+    s = seg_search(m.ntp, gs, ge, tt);
+    n = tt - m.ntp[s];
+  } else {
+    const int nt = m.ntp[s + 1] - m.ntp[s];
+    if (nt <= 0) return false;
+    const int local = tile - m.m2_tiles * m.ntp[s];
+    ti.m2 = local / nt;
+    n = local % nt;
+  }
+  ti.seg = s;
+  ti.row_start = m.start[s] + n * kBN;
+  const int left = m.cnt[s] - n * kBN;
   ti.n_valid = left < kBN ? left : kBN;
-  return true;
+  return ti.n_valid > 0;
 }
 
 __device__ __forceinline__ uint16_t f2bf(float x) {
@@ -99,17 +176,15 @@ __device__ __forceinline__ uint16_t f2bf(float x) {
 template <int EPI>
 __device__ __forceinline__ void pair_epilogue(const GemmParams& p, uint32_t tmem_base,
                                               uint64_t* tfull, uint64_t* tempty, int pair,
-                                              int npairs, int m2_tiles, int total_tiles,
-                                              const int32_t* s_ntp, const int32_t* s_cnt,
-                                              const int32_t* s_start, uint32_t rank, int warp,
-                                              int lane) {
+                                              int npairs, int total_tiles, const PairMap& s_map,
+                                              uint32_t rank, int warp, int lane) {
     const int q = warp & 3;
     const int half_cols = (warp - kEpiWarp0) >> 2;
     const uint32_t lead_tempty = mapa_shared(smem_u32(tempty), 0);
     uint32_t acc_phase = 0;
     for (int tile = pair; tile < total_tiles; tile += npairs) {
       PairTile ti;
-      if (!decode_pair_tile(tile, m2_tiles, p.nseg, s_ntp, s_cnt, s_start, ti)) continue;
+      if (!decode_pair_tile(tile, s_map, ti)) continue;
       if (!mbar_wait_cluster(tfull, acc_phase, p.err)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(32 * q) << 16);
@@ -191,12 +266,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);  // leader's used
   uint64_t* empty = full + kStages;
   uint64_t* full_sf = empty + kStages;
-  uint64_t* sf_ready = full_sf + kStages;  // leader's used
-  uint64_t* tfull = sf_ready + kStages;
+  uint64_t* tfull = full_sf + kStages;
   uint64_t* tempty = tfull + 1;            // leader's used
   uint64_t* drained = tempty + 1;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drained + 1);
-  __shared__ int32_t s_ntp[kMaxSeg + 1], s_cnt[kMaxSeg], s_start[kMaxSeg + 1];
+  __shared__ PairMap s_map;
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const uint32_t rank = cluster_ctarank();
@@ -206,17 +280,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int ks_count = p.K / 256;
   const int kc_per_rb = p.K / 64;
 
-  for (int i = threadIdx.x; i <= p.nseg; i += blockDim.x) {
-    s_ntp[i] = p.ntile_prefix[i];
-    s_start[i] = p.seg_start[i];
-    if (i < p.nseg) s_cnt[i] = p.seg_count[i];
-  }
+  load_pair_map(s_map, p, m2_tiles);
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full[s], G5_PAIR_SPLIT == 1 ? 2 : 1);
+      // the leader producer(s)' expect-tx arrivals + 4 staging warps in each CTA
+      mbar_init(&full[s], (G5_PAIR_SPLIT == 1 ? 2 : 1) + 8);
       mbar_init(&empty[s], 1);
       mbar_init(&full_sf[s], 1);
-      mbar_init(&sf_ready[s], 8);  // 4 staging warps in each CTA
     }
     mbar_init(tfull, 1);
     mbar_init(tempty, 2 * kEpiWarps);  // one arrive per epilogue warp of each CTA
@@ -233,7 +303,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   cluster_sync();  // the peer's barriers exist before anyone signals them
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
-  const int total_tiles = m2_tiles * s_ntp[p.nseg];
+  const int total_tiles = m2_tiles * s_map.ntp[p.nseg];
 
   if (warp < kEpiWarp0) {
   regs_dealloc<kRegsLow>();
@@ -249,7 +319,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int tile = pair; tile < total_tiles && ok; tile += npairs) {
         PairTile ti;
-        if (!decode_pair_tile(tile, m2_tiles, p.nseg, s_ntp, s_cnt, s_start, ti)) continue;
+        if (!decode_pair_tile(tile, s_map, ti)) continue;
         const int n_mma = (ti.n_valid + 15) & ~15;
         const int half = n_mma / 2;  // token rows held by each CTA (multiple of 8)
         const int box = half <= 32 ? 32 : (half <= 64 ? 64 : 128);
@@ -297,14 +367,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int tile = pair; tile < total_tiles && ok; tile += npairs) {
         PairTile ti;
-        if (!decode_pair_tile(tile, m2_tiles, p.nseg, s_ntp, s_cnt, s_start, ti)) continue;
+        if (!decode_pair_tile(tile, s_map, ti)) continue;
         const uint32_t n_mma = (uint32_t)((ti.n_valid + 15) & ~15);
         const uint32_t idesc = idesc_fp4(kPM, n_mma, 0, 0, 0);
         if (!mbar_wait_cluster(tempty, acc_phase ^ 1u, p.err)) break;
         tc_fence_after();
         for (int ks = 0; ks < ks_count; ++ks) {
-          if (!mbar_wait_cluster(&full[stage], phase, p.err) ||
-              !mbar_wait_cluster(&sf_ready[stage], phase, p.err)) {
+          if (!mbar_wait_cluster(&full[stage], phase, p.err)) {
             ok = false;
             break;
           }
@@ -338,13 +407,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     // (both CTAs; the layout tcgen05.cp.32x128b.warpx4 writes)
     const int q = warp & 3;
     const uint32_t t_lane = tmem_base + ((uint32_t)(32 * q) << 16);
-    const uint32_t lead_ready0 = mapa_shared(smem_u32(&sf_ready[0]), 0);
+    const uint32_t lead_ready0 = mapa_shared(smem_u32(&full[0]), 0);
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
     for (int tile = pair; tile < total_tiles && ok; tile += npairs) {
       PairTile ti;
-      if (!decode_pair_tile(tile, m2_tiles, p.nseg, s_ntp, s_cnt, s_start, ti)) continue;
+      if (!decode_pair_tile(tile, s_map, ti)) continue;
       const bool two_blocks = ((ti.n_valid + 15) & ~15) > 128;
       for (int ks = 0; ks < ks_count; ++ks) {
         if (!mbar_wait(&full_sf[stage], phase, p.err)) {
@@ -389,8 +458,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------ epilogue (both CTAs)
     regs_alloc<kRegsEpi>();
-    pair_epilogue<EPI>(p, tmem_base, tfull, tempty, pair, npairs, m2_tiles, total_tiles, s_ntp,
-                       s_cnt, s_start, rank, warp, lane);
+    pair_epilogue<EPI>(p, tmem_base, tfull, tempty, pair, npairs, total_tiles, s_map, rank,
+                       warp, lane);
   }
 
   tc_fence_before();
@@ -401,57 +470,36 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
-// Scale-ring form (RING): the operand ring holds only the weight and token
-// tiles (32 KB a stage, six stages), so the producer issues two tensor copies
-// per stage; the scale chunks of a stage (this CTA's weight rows, 2 KB, and
-// the tile's token rows, up to 4 KB) are fetched by the four staging warps
-// themselves with 16-byte cp.async copies (load/store unit, not the TMA
-// engine) into a three-slot ring two stages ahead of their use, and go from
-// there into one of five TMEM scale slots, which the MMA thread hands back by
-// a commit on sf_free once the slot's MMAs are done.
-constexpr int kRStages = 6;
-constexpr int kRStageBytes = kABytes + kBBytes;          // 32 KB
-constexpr int kTSlots = 5;                               // TMEM scale slots
-constexpr int kRSlots = 3;                               // shared-memory scale ring
-constexpr int kRSlotBytes = kSfaBytes + kSfbBytes;       // 6 KB
-constexpr size_t kRSmem = (size_t)kRStages * kRStageBytes + kRSlots * kRSlotBytes + 1024 + 256;
-static_assert(kSfBase + kTSlots * (kSfaCols + kSfbCols) <= kTmemCols, "TMEM budget (ring)");
-static_assert((2 * kRStages + 2 * kTSlots + 3) * 8 + 4 <= 256, "barrier area (ring)");
-static_assert(kRSmem + 3 * 4 * (kMaxSeg + 1) <= 232448, "shared memory budget (ring)");
-
-// The stages of this pair's tiles in order, for the staging warps' lookahead.
-struct StageCursor {
-  int tile, ks;
-  PairTile ti;
-  bool valid;
-};
-
-__device__ __forceinline__ void cursor_seek(StageCursor& c, int tile, int npairs,
-                                            int total_tiles, int m2_tiles, int nseg,
-                                            const int32_t* ntp, const int32_t* cnt,
-                                            const int32_t* start) {
-  c.valid = false;
-  for (; tile < total_tiles; tile += npairs)
-    if (decode_pair_tile(tile, m2_tiles, nseg, ntp, cnt, start, c.ti)) {
-      c.tile = tile;
-      c.ks = 0;
-      c.valid = true;
-      return;
-    }
-}
-
-__device__ __forceinline__ void cursor_next(StageCursor& c, int ks_count, int npairs,
-                                            int total_tiles, int m2_tiles, int nseg,
-                                            const int32_t* ntp, const int32_t* cnt,
-                                            const int32_t* start) {
-  if (!c.valid) return;
-  if (++c.ks < ks_count) return;
-  cursor_seek(c, c.tile + npairs, npairs, total_tiles, m2_tiles, nseg, ntp, cnt, start);
-}
+// Wide-stage form (WIDE): a stage covers 512 of K (two 256-K chunks), so the
+// leader's MMA thread waits once, issues eight MMAs and commits once per
+// stage. Every tcgen05 instruction and every barrier wait costs that single
+// thread about 90 cycles, which holds the 256-K form at ~690 cycles a stage
+// against ~540 of tensor work for a full tile. Three operand stages of 64 KB
+// (both chunks' weight rows and token rows, no scales) fill the shared
+// memory; the block scales travel on their own two-slot ring (12 KB a slot)
+// into one of two TMEM scale slots (96 columns each). Copy threads per CTA:
+// warp 0 the weight rows, warp 6 the token rows, warp 7 the scale chunks (one
+// TMA-issuing thread streams about 50 bytes per SM cycle, two about 100).
+// The staging warps write a stage's scales once the MMAs of the stage two
+// back have finished (its commit), since those read the same TMEM slot.
+constexpr int kWChunks = 2;                                   // 256-K chunks per stage
+constexpr int kWStages = 3;
+constexpr int kWStageBytes = kWChunks * (kABytes + kBBytes);  // 64 KB
+constexpr int kWSfSlots = 2;
+constexpr int kWSfaBytes = kWChunks * kSfaBytes;              // [chunk][4 x 512 B]
+constexpr int kWSfbBytes = kWChunks * kSfbBytes;              // [block][chunk][4 x 512 B]
+constexpr int kWSfSlotBytes = kWSfaBytes + kWSfbBytes;        // 12 KB
+constexpr int kWChunkCols = kSfaCols + kSfbCols;              // 48 TMEM columns per chunk
+constexpr int kWSfCols = kWChunks * kWChunkCols;              // 96
+constexpr size_t kWSmem =
+    (size_t)kWStages * kWStageBytes + kWSfSlots * kWSfSlotBytes + 1024 + 256;
+static_assert(kSfBase + kWSfSlots * kWSfCols <= kTmemCols, "TMEM budget (wide)");
+static_assert((2 * kWStages + 2 * kWSfSlots + 3) * 8 + 4 <= 256, "barrier area (wide)");
+static_assert(kWSmem + sizeof(PairMap) + 16 <= 232448, "shared memory budget (wide)");
 
 template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
-    nvfp4_pair_gemm_ring_kernel(const __grid_constant__ CUtensorMap tmap_a,
+    nvfp4_pair_gemm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                 const __grid_constant__ CUtensorMap tmap_b32,
                                 const __grid_constant__ CUtensorMap tmap_b64,
                                 const __grid_constant__ CUtensorMap tmap_b128,
@@ -459,39 +507,37 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint8_t* ring = smem + kRStages * kRStageBytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(ring + kRSlots * kRSlotBytes);  // leader's used
-  uint64_t* empty = full + kRStages;
-  uint64_t* sf_ready = empty + kRStages;   // leader's used
-  uint64_t* sf_free = sf_ready + kTSlots;
-  uint64_t* tfull = sf_free + kTSlots;
-  uint64_t* tempty = tfull + 1;            // leader's used
+  uint8_t* sf_ring = smem + kWStages * kWStageBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sf_ring + kWSfSlots * kWSfSlotBytes);  // leader's
+  uint64_t* empty = full + kWStages;
+  uint64_t* full_sf = empty + kWStages;
+  uint64_t* sf_free = full_sf + kWSfSlots;
+  uint64_t* tfull = sf_free + kWSfSlots;
+  uint64_t* tempty = tfull + 1;  // leader's used
   uint64_t* drained = tempty + 1;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drained + 1);
-  __shared__ int32_t s_ntp[kMaxSeg + 1], s_cnt[kMaxSeg], s_start[kMaxSeg + 1];
-  __shared__ bool s_staging_ok;
+  __shared__ PairMap s_map;
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   const int m2_tiles = p.M_per / kPM;
-  const int ks_count = p.K / 256;
+  const int chunks = p.K / 256;
+  const int wstages = (chunks + kWChunks - 1) / kWChunks;
   const int kc_per_rb = p.K / 64;
 
-  for (int i = threadIdx.x; i <= p.nseg; i += blockDim.x) {
-    s_ntp[i] = p.ntile_prefix[i];
-    s_start[i] = p.seg_start[i];
-    if (i < p.nseg) s_cnt[i] = p.seg_count[i];
-  }
+  load_pair_map(s_map, p, m2_tiles);
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kRStages; ++s) {
-      mbar_init(&full[s], 1);
+    for (int s = 0; s < kWStages; ++s) {
+      // the leader's two operand copy threads' expect-tx arrivals + 4 staging
+      // warps in each CTA
+      mbar_init(&full[s], 2 + 8);
       mbar_init(&empty[s], 1);
     }
-    for (int s = 0; s < kTSlots; ++s) {
-      mbar_init(&sf_ready[s], 8);  // 4 staging warps in each CTA
-      mbar_init(&sf_free[s], 1);
+    for (int t = 0; t < kWSfSlots; ++t) {
+      mbar_init(&full_sf[t], 1);
+      mbar_init(&sf_free[t], 4);  // this CTA's staging warps
     }
     mbar_init(tfull, 1);
     mbar_init(tempty, 2 * kEpiWarps);
@@ -505,43 +551,89 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  cluster_sync();
+  cluster_sync();  // the peer's barriers exist before anyone signals them
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
-  const int total_tiles = m2_tiles * s_ntp[p.nseg];
+  const int total_tiles = m2_tiles * s_map.ntp[p.nseg];
 
   if (warp < kEpiWarp0) {
   regs_dealloc<kRegsLow>();
-  if (warp == 0) {
-    // ------------------------------------------------------ TMA producer
+  if (warp == 0 || warp == 6) {
+    // ------------------------------------------------------ operand copies
+    // (warp 0: this CTA's 128 weight rows; warp 6: its half of the token rows)
     if (lane == 0) {
-      tma_prefetch_desc(&tmap_a);
+      const bool do_a = warp == 0;
+      if (do_a) tma_prefetch_desc(&tmap_a);
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
       for (int tile = pair; tile < total_tiles && ok; tile += npairs) {
         PairTile ti;
-        if (!decode_pair_tile(tile, m2_tiles, p.nseg, s_ntp, s_cnt, s_start, ti)) continue;
+        if (!decode_pair_tile(tile, s_map, ti)) continue;
         const int n_mma = (ti.n_valid + 15) & ~15;
-        const int half = n_mma / 2;
+        const int half = n_mma / 2;  // token rows held by each CTA (multiple of 8)
         const int box = half <= 32 ? 32 : (half <= 64 ? 64 : 128);
         const CUtensorMap* mb = box == 32 ? &tmap_b32 : (box == 64 ? &tmap_b64 : &tmap_b128);
         const int a_row = ti.seg * p.M_per + ti.m2 * kPM + (int)rank * 128;
-        const uint32_t cta_bytes = kABytes + box * kBK;
-        for (int ks = 0; ks < ks_count; ++ks) {
+        const int b_row = ti.row_start + (int)rank * half;
+        const uint32_t chunk_bytes = do_a ? (uint32_t)kABytes : (uint32_t)(box * kBK);
+        for (int w = 0; w < wstages; ++w) {
+          const int c0 = w * kWChunks;
+          const int nc = chunks - c0 < kWChunks ? chunks - c0 : kWChunks;
           if (!mbar_wait_cluster(&empty[stage], phase ^ 1u, p.err)) {
             ok = false;
             break;
           }
-          uint8_t* sa = smem + stage * kRStageBytes;
-          uint8_t* sb = sa + kABytes;
+          uint8_t* dst = smem + stage * kWStageBytes + (do_a ? 0 : kWChunks * kABytes);
           const uint32_t lead_full = mapa_shared(smem_u32(&full[stage]), 0);
-          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * cta_bytes);
-          tma_load_2d_pair(sa, &tmap_a, lead_full, ks * kBK, a_row);
-          tma_load_2d_pair(sb, mb, lead_full, ks * kBK, ti.row_start + (int)rank * half);
-          if (++stage == kRStages) {
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2u * (uint32_t)nc * chunk_bytes);
+          for (int h = 0; h < nc; ++h) {
+            if (do_a)
+              tma_load_2d_pair(dst + h * kABytes, &tmap_a, lead_full, (c0 + h) * kBK, a_row);
+            else
+              tma_load_2d_pair(dst + h * kBBytes, mb, lead_full, (c0 + h) * kBK, b_row);
+          }
+          if (++stage == kWStages) {
             stage = 0;
             phase ^= 1u;
+          }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 7) {
+    // ------------------------------------------------------ scale copies
+    // (this CTA's weight rows' chunks and every token row's chunks)
+    if (lane == 0) {
+      int slot = 0;
+      uint32_t sphase = 0;
+      bool ok = true;
+      for (int tile = pair; tile < total_tiles && ok; tile += npairs) {
+        PairTile ti;
+        if (!decode_pair_tile(tile, s_map, ti)) continue;
+        const int n_mma = (ti.n_valid + 15) & ~15;
+        const int sfb_ch = n_mma > 128 ? 2 : 1;
+        const int a_row = ti.seg * p.M_per + ti.m2 * kPM + (int)rank * 128;
+        const uint8_t* sfa = p.sfa + (size_t)(a_row / 128) * kc_per_rb * kChunk;
+        const uint8_t* sfb = p.sfb + (size_t)(ti.row_start / 128) * kc_per_rb * kChunk;
+        for (int w = 0; w < wstages; ++w) {
+          const int c0 = w * kWChunks;
+          const int nc = chunks - c0 < kWChunks ? chunks - c0 : kWChunks;
+          if (!mbar_wait(&sf_free[slot], sphase ^ 1u, p.err)) {
+            ok = false;
+            break;
+          }
+          uint8_t* ssfa = sf_ring + slot * kWSfSlotBytes;
+          uint8_t* ssfb = ssfa + kWSfaBytes;
+          const uint32_t piece = (uint32_t)nc * 4u * kChunk;  // nc chunks of one 128-row block
+          mbar_arrive_expect_tx(&full_sf[slot], piece * (uint32_t)(1 + sfb_ch));
+          bulk_load(ssfa, sfa + (size_t)c0 * 4 * kChunk, piece, &full_sf[slot]);
+          for (int h = 0; h < sfb_ch; ++h)
+            bulk_load(ssfb + h * (kWSfbBytes / 2), sfb + ((size_t)h * kc_per_rb + c0 * 4) * kChunk,
+                      piece, &full_sf[slot]);
+          if (++slot == kWSfSlots) {
+            slot = 0;
+            sphase ^= 1u;
           }
         }
       }
@@ -551,42 +643,42 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------ MMA (leader)
     if (leader && lane == 0) {
       int stage = 0, slot = 0;
-      uint32_t phase = 0, sphase = 0, acc_phase = 0;
+      uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
       for (int tile = pair; tile < total_tiles && ok; tile += npairs) {
         PairTile ti;
-        if (!decode_pair_tile(tile, m2_tiles, p.nseg, s_ntp, s_cnt, s_start, ti)) continue;
+        if (!decode_pair_tile(tile, s_map, ti)) continue;
         const uint32_t n_mma = (uint32_t)((ti.n_valid + 15) & ~15);
         const uint32_t idesc = idesc_fp4(kPM, n_mma, 0, 0, 0);
         if (!mbar_wait_cluster(tempty, acc_phase ^ 1u, p.err)) break;
         tc_fence_after();
-        for (int ks = 0; ks < ks_count; ++ks) {
-          if (!mbar_wait_cluster(&full[stage], phase, p.err) ||
-              !mbar_wait_cluster(&sf_ready[slot], sphase, p.err)) {
+        for (int w = 0; w < wstages; ++w) {
+          const int nc = chunks - w * kWChunks < kWChunks ? chunks - w * kWChunks : kWChunks;
+          if (!mbar_wait_cluster(&full[stage], phase, p.err)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint8_t* sa = smem + stage * kRStageBytes;
-          const uint8_t* sb = sa + kABytes;
-          const uint32_t sfa_col = tmem_base + kSfBase + slot * (kSfaCols + kSfbCols);
-          const uint32_t sfb_col = sfa_col + kSfaCols;
-          const uint32_t a_addr = smem_u32(sa), b_addr = smem_u32(sb);
+          const uint32_t a_addr = smem_u32(smem + stage * kWStageBytes);
+          const uint32_t b_addr = a_addr + kWChunks * kABytes;
+          const uint32_t sf_col = tmem_base + kSfBase + slot * kWSfCols;
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
-            mma_nvfp4_pair(tmem_base, desc_kmajor_sw128(a_addr + 32 * c),
-                           desc_kmajor_sw128(b_addr + 32 * c), idesc, sfa_col + 4 * c,
-                           sfb_col + 8 * c, (ks | c) != 0 ? 1u : 0u);
+          for (int h = 0; h < kWChunks; ++h) {
+            if (h >= nc) break;
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+              mma_nvfp4_pair(tmem_base, desc_kmajor_sw128(a_addr + h * kABytes + 32 * c),
+                             desc_kmajor_sw128(b_addr + h * kBBytes + 32 * c), idesc,
+                             sf_col + h * kWChunkCols + 4 * c,
+                             sf_col + h * kWChunkCols + kSfaCols + 8 * c,
+                             (w | h | c) != 0 ? 1u : 0u);
+          }
           tc_commit_pair(&empty[stage], 0x3);
-          tc_commit_pair(&sf_free[slot], 0x3);
-          if (++stage == kRStages) {
+          if (++stage == kWStages) {
             stage = 0;
             phase ^= 1u;
           }
-          if (++slot == kTSlots) {
-            slot = 0;
-            sphase ^= 1u;
-          }
+          if (++slot == kWSfSlots) slot = 0;
         }
         if (!ok) break;
         tc_commit_pair(tfull, 0x3);
@@ -597,106 +689,91 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else if (warp < 6) {
-    // ------------------------------------------------------ scale fetch + staging
+    // ------------------------------------------------------ scale staging
+    // (both CTAs; the layout tcgen05.cp.32x128b.warpx4 writes)
     const int q = warp & 3;
-    const int tid = threadIdx.x - 64;  // 0..127 over the four staging warps
     const uint32_t t_lane = tmem_base + ((uint32_t)(32 * q) << 16);
-    const uint32_t lead_ready0 = mapa_shared(smem_u32(&sf_ready[0]), 0);
-    // one stage's scale chunks into ring slot r: 384 pieces of 16 bytes
-    // (SFA 128, SFB block 0 128, SFB block 1 128 when the tile has one)
-    auto fetch = [&](const StageCursor& c, int r) {
-      if (c.valid) {
-        const int a_row = c.ti.seg * p.M_per + c.ti.m2 * kPM + (int)rank * 128;
-        const bool two = ((c.ti.n_valid + 15) & ~15) > 128;
-        const uint8_t* sfa = p.sfa + ((size_t)(a_row / 128) * kc_per_rb + c.ks * 4) * kChunk;
-        const uint8_t* sfb = p.sfb + ((size_t)(c.ti.row_start / 128) * kc_per_rb + c.ks * 4) * kChunk;
-        uint8_t* dst = ring + r * kRSlotBytes;
-        cp_async_16(dst + tid * 16, sfa + tid * 16);
-        cp_async_16(dst + kSfaBytes + tid * 16, sfb + tid * 16);
-        if (two)
-          cp_async_16(dst + kSfaBytes + 4 * kChunk + tid * 16,
-                      sfb + (size_t)kc_per_rb * kChunk + tid * 16);
-      }
-      cp_async_commit();  // an empty group when there is nothing left to fetch
-    };
-    StageCursor cur, ahead;
-    cursor_seek(cur, pair, npairs, total_tiles, m2_tiles, p.nseg, s_ntp, s_cnt, s_start);
-    ahead = cur;
-    fetch(ahead, 0);
-    cursor_next(ahead, ks_count, npairs, total_tiles, m2_tiles, p.nseg, s_ntp, s_cnt, s_start);
-    fetch(ahead, 1);
-    cursor_next(ahead, ks_count, npairs, total_tiles, m2_tiles, p.nseg, s_ntp, s_cnt, s_start);
-    int slot = 0, r = 0;
+    const uint32_t lead_full0 = mapa_shared(smem_u32(&full[0]), 0);
+    int slot = 0, g = 0;
     uint32_t sphase = 0;
-    while (cur.valid) {
-      // two stages ahead; slot (r + 2) % 3 was read by every staging warp in
-      // the previous iteration (named barrier 1 below)
-      fetch(ahead, r == 0 ? 2 : r - 1);
-      cursor_next(ahead, ks_count, npairs, total_tiles, m2_tiles, p.nseg, s_ntp, s_cnt, s_start);
-      cp_async_wait<2>();  // this stage's group has landed
-      // one thread waits until the TMEM slot's previous MMAs are done; the
-      // barrier then orders every staging thread after that wait and after
-      // every thread's copies, and all four warps leave together on a timeout
-      if (tid == 0) s_staging_ok = mbar_wait(&sf_free[slot], sphase ^ 1u, p.err);
-      named_barrier_sync(1, 128);
-      if (!s_staging_ok) break;
-      const uint8_t* ssfa = ring + r * kRSlotBytes;
-      const uint8_t* ssfb = ssfa + kSfaBytes;
-      const bool two_blocks = ((cur.ti.n_valid + 15) & ~15) > 128;
-      uint32_t ra[kSfaCols];
+    bool ok = true;
+    for (int tile = pair; tile < total_tiles && ok; tile += npairs) {
+      PairTile ti;
+      if (!decode_pair_tile(tile, s_map, ti)) continue;
+      const bool two_blocks = ((ti.n_valid + 15) & ~15) > 128;
+      for (int w = 0; w < wstages; ++w, ++g) {
+        const int nc = chunks - w * kWChunks < kWChunks ? chunks - w * kWChunks : kWChunks;
+        if (!mbar_wait(&full_sf[slot], sphase, p.err)) {
+          ok = false;
+          break;
+        }
+        // the TMEM slot's previous stage (two back) has finished its MMAs
+        if (g >= kWSfSlots) {
+          const int gp = g - kWSfSlots;
+          if (!mbar_wait(&empty[gp % kWStages], (uint32_t)((gp / kWStages) & 1), p.err)) {
+            ok = false;
+            break;
+          }
+        }
+        const uint8_t* ssfa = sf_ring + slot * kWSfSlotBytes;
+        const uint8_t* ssfb = ssfa + kWSfaBytes;
+        const uint32_t col0 = kSfBase + slot * kWSfCols;
+        for (int h = 0; h < nc; ++h) {
+          uint32_t r[kSfaCols];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const uint4 v = *reinterpret_cast<const uint4*>(ssfa + c * kChunk + lane * 16);
-        ra[4 * c] = v.x; ra[4 * c + 1] = v.y; ra[4 * c + 2] = v.z; ra[4 * c + 3] = v.w;
+          for (int c = 0; c < 4; ++c) {
+            const uint4 v =
+                *reinterpret_cast<const uint4*>(ssfa + (h * 4 + c) * kChunk + lane * 16);
+            r[4 * c] = v.x; r[4 * c + 1] = v.y; r[4 * c + 2] = v.z; r[4 * c + 3] = v.w;
+          }
+#pragma unroll
+          for (int o = 0; o < kSfaCols; o += 8)
+            tmem_st_32x32b_x8(t_lane + col0 + h * kWChunkCols + o, r + o);
+          // chunk c of 128-row block hb -> columns 8c + 4hb
+          uint32_t rb[kSfbCols];
+#pragma unroll
+          for (int gg = 0; gg < kSfbCols / 4; ++gg) {
+            const int c = gg / 2, hb = gg % 2;
+            uint4 v = make_uint4(0u, 0u, 0u, 0u);
+            if (hb == 0 || two_blocks)
+              v = *reinterpret_cast<const uint4*>(ssfb + hb * (kWSfbBytes / 2) +
+                                                  (h * 4 + c) * kChunk + lane * 16);
+            rb[4 * gg] = v.x; rb[4 * gg + 1] = v.y; rb[4 * gg + 2] = v.z; rb[4 * gg + 3] = v.w;
+          }
+#pragma unroll
+          for (int o = 0; o < kSfbCols; o += 8)
+            tmem_st_32x32b_x8(t_lane + col0 + h * kWChunkCols + kSfaCols + o, rb + o);
+        }
+        tmem_st_wait();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sf_free[slot]);  // the ring slot may be refilled
+        tc_fence_before();
+        if (lane == 0) mbar_arrive_cluster_relaxed(lead_full0 + (g % kWStages) * 8u);
+        if (++slot == kWSfSlots) {
+          slot = 0;
+          sphase ^= 1u;
+        }
       }
-      uint32_t rb[kSfbCols];
-#pragma unroll
-      for (int g = 0; g < kSfbCols / 4; ++g) {
-        const int c = g / 2, h = g % 2;
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (h == 0 || two_blocks)
-          v = *reinterpret_cast<const uint4*>(ssfb + (h * 4 + c) * kChunk + lane * 16);
-        rb[4 * g] = v.x; rb[4 * g + 1] = v.y; rb[4 * g + 2] = v.z; rb[4 * g + 3] = v.w;
-      }
-      named_barrier_sync(1, 128);  // slot r read by all: it may be refilled
-      tc_fence_after();
-      const uint32_t sfa_col = kSfBase + slot * (kSfaCols + kSfbCols);
-      const uint32_t sfb_col = sfa_col + kSfaCols;
-#pragma unroll
-      for (int o = 0; o < kSfaCols; o += 8) tmem_st_32x32b_x8(t_lane + sfa_col + o, ra + o);
-#pragma unroll
-      for (int o = 0; o < kSfbCols; o += 8) tmem_st_32x32b_x8(t_lane + sfb_col + o, rb + o);
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster_relaxed(lead_ready0 + slot * 8u);
-      if (++slot == kTSlots) {
-        slot = 0;
-        sphase ^= 1u;
-      }
-      r = r == 2 ? 0 : r + 1;
-      cursor_next(cur, ks_count, npairs, total_tiles, m2_tiles, p.nseg, s_ntp, s_cnt, s_start);
     }
-    cp_async_wait<0>();
   }
   } else {
     regs_alloc<kRegsEpi>();
-    pair_epilogue<EPI>(p, tmem_base, tfull, tempty, pair, npairs, m2_tiles, total_tiles, s_ntp,
-                       s_cnt, s_start, rank, warp, lane);
+    pair_epilogue<EPI>(p, tmem_base, tfull, tempty, pair, npairs, total_tiles, s_map, rank,
+                       warp, lane);
   }
 
   tc_fence_before();
   __syncthreads();
-  cluster_sync();
+  cluster_sync();  // no CTA frees TMEM or exits while its peer may still signal it
   tc_fence_after();
   if (warp == 1) tmem_dealloc_pair(tmem_base, kTmemCols);
 }
 
-template <int EPI, int RING>
+template <int EPI, int WIDE>
 cudaError_t launch_pair(const CUtensorMap* ta, const CUtensorMap* tb, const GemmParams& p,
                         int grid, cudaStream_t st) {
-  auto kern = RING ? nvfp4_pair_gemm_ring_kernel<EPI> : nvfp4_pair_gemm_kernel<EPI>;
-  const size_t smem = RING ? kRSmem : kSmem;
+  auto kern = WIDE ? nvfp4_pair_gemm_wide_kernel<EPI> : nvfp4_pair_gemm_kernel<EPI>;
+  const size_t smem = WIDE ? kWSmem : kSmem;
   cudaError_t e =
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
@@ -746,12 +823,12 @@ int nvfp4_pair_gemm_grid(int num_sms) {
 
 cudaError_t launch_nvfp4_pair_gemm(int epi, const CUtensorMap* tmap_a, const CUtensorMap* tmap_b,
                                    const CUtensorMap* tmap_sfa, const CUtensorMap* tmap_sfb,
-                                   const GemmParams& p, int grid, cudaStream_t st, int ring) {
+                                   const GemmParams& p, int grid, cudaStream_t st, int wide) {
   (void)tmap_sfa;
   (void)tmap_sfb;
   if (p.nseg > kMaxSeg || p.K % 256 || p.M_per % kPM || grid < 2 || grid % 2)
     return cudaErrorInvalidValue;
-  if (ring)
+  if (wide)
     return epi == 0 ? launch_pair<0, 1>(tmap_a, tmap_b, p, grid, st)
                     : launch_pair<1, 1>(tmap_a, tmap_b, p, grid, st);
   return epi == 0 ? launch_pair<0, 0>(tmap_a, tmap_b, p, grid, st)

@@ -177,6 +177,8 @@ struct GemmParams {
   int K;                        // contraction length (elements)
   int M_per;                    // weight rows per expert
   int nseg;
+  int tile_group;               // CTA-pair GEMM tile order: 0 = segment-major, else
+                                // token tiles per weight-tile-major group
 };
 
 // tmap_b[i]: the activation rows with a box of (32 << i) rows, i = 0..2
@@ -202,12 +204,13 @@ size_t nvfp4_gemm_smem_bytes(int bn);
 // uint8 tensors with a {256, 8} box (four 512-byte chunks). grid = an even
 // CTA count, at most nvfp4_pair_gemm_grid().
 int nvfp4_pair_gemm_grid(int num_sms);
-// ring = 1: the scale-ring form (operand ring of six 32 KB stages, scale
-// chunks fetched by the staging warps with cp.async into a three-slot ring,
-// five TMEM scale slots released by sf_free commits).
+// wide = 1: stages of 512 K (three 64 KB operand stages, the block scales
+// on their own two-slot ring and two TMEM scale slots), one barrier wait and
+// one commit per eight MMAs; wide = 0: stages of 256 K (five 38 KB stages
+// holding operands and scales).
 cudaError_t launch_nvfp4_pair_gemm(int epi, const CUtensorMap* tmap_a, const CUtensorMap* tmap_b,
                                    const CUtensorMap* tmap_sfa, const CUtensorMap* tmap_sfb,
-                                   const GemmParams& p, int grid, cudaStream_t st, int ring = 0);
+                                   const GemmParams& p, int grid, cudaStream_t st, int wide = 0);
 
 // ------------------------------------------------------------ combine.cu
 // out[t, :] (+)= sum_{s < kk} y[pos[t, s], :] in slot order (FP32

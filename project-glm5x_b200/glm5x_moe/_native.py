@@ -190,7 +190,8 @@ SIGNATURES = {
     "glm5x_moe_set_token_major_down": [_P, _I32],
     "glm5x_moe_set_down_tile_n": [_P, _I32],
     "glm5x_moe_set_weight_tile_rows": [_P, _I32],
-    "glm5x_moe_set_pair_scale_ring": [_P, _I32],
+    "glm5x_moe_set_pair_wide_stages": [_P, _I32],
+    "glm5x_moe_set_pair_tile_order": [_P, _I32, _I32],
     "glm5x_nvfp4_quantize_f32": [_P, _I64, _I64, _I32, _P, _P, _P, _P],
     "glm5x_nvfp4_quantize_bf16": [_P, _I64, _I64, _I32, _P, _P, _P, _P],
     "glm5x_nvfp4_quantize_slabs_bf16": [_P, _I64, _P, _P, _P, _I32, _I64, _P, _P, _P, _P],

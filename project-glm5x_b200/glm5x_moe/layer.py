@@ -408,9 +408,15 @@ class GLM5XMoELayer:
                                                     diag.data_ptr()), self._h)
         return sel, diag
 
-    def set_pair_scale_ring(self, enable: bool) -> None:
-        """CTA-pair GEMMs with the staging warps fetching the block scales."""
-        N.check(N.lib().glm5x_moe_set_pair_scale_ring(self._h, 1 if enable else 0), self._h)
+    def set_pair_wide_stages(self, enable: bool) -> None:
+        """CTA-pair GEMMs with 512-K pipeline stages (or 256-K)."""
+        N.check(N.lib().glm5x_moe_set_pair_wide_stages(self._h, 1 if enable else 0), self._h)
+
+    def set_pair_tile_order(self, up_group: int, down_group: int) -> None:
+        """Tile order of the CTA-pair GEMMs: 0 = segment-major, g > 0 =
+        groups of about g token tiles, each run weight-tile-major."""
+        N.check(N.lib().glm5x_moe_set_pair_tile_order(self._h, int(up_group), int(down_group)),
+                self._h)
 
     def set_weight_tile_rows(self, rows: int) -> None:
         """Weight rows per tile for narrow token tiles: 128, or 256 as two

@@ -43,11 +43,11 @@ def test_routed_expert_path_small_shapes(T, bn, pair, tm):
     _routed_path(T, bn, pair, tm, 128)
 
 
-@pytest.mark.parametrize("T", [7, 300, 520])
-def test_routed_expert_path_pair_scale_ring(T):
-    """256-row token tiles on CTA pairs with the block scales fetched by the
-    staging warps (scale-ring form): the same outputs as the oracle."""
-    _routed_path(T, 256, True, False, 128, ring=True)
+@pytest.mark.parametrize("T,hi", [(7, 512), (300, 512), (520, 512), (300, 1024)])
+def test_routed_expert_path_pair_wide_stages(T, hi):
+    """256-row token tiles on CTA pairs with 512-K stages (one stage per tile
+    at K = 512, two at 1024): the same outputs as the oracle."""
+    _routed_path(T, 256, True, False, 128, wide=True, hi=hi)
 
 
 @pytest.mark.parametrize("T,bn", [(1, 0), (5, 32), (40, 32), (100, 64), (130, 32), (7, 64)])
@@ -57,17 +57,17 @@ def test_routed_expert_path_256_row_weight_tiles(T, bn):
     _routed_path(T, bn, True, False, 256)
 
 
-def _routed_path(T, bn, pair, tm, weight_rows, ring=False):
+def _routed_path(T, bn, pair, tm, weight_rows, wide=False, hi=512):
     """Every token-tile width (256-row tiles on CTA pairs and on single CTAs),
     the token-major and weight-major down projections, segments that span
     several tiles and narrow tiles."""
-    H, I, E, k = 512, 512, 8, 2
+    H, I, E, k = hi, hi, 8, 2
     layer = _layer(H, I, E, k, True, 600)
     layer.set_tile_n(bn)
     layer.set_pair_mma(pair)
     layer.set_token_major_down(tm)
     layer.set_weight_tile_rows(weight_rows)
-    layer.set_pair_scale_ring(ring)
+    layer.set_pair_wide_stages(wide)
     experts, deq = {}, {}
     for e in list(range(E)) + [-1]:
         ex, dq = make_expert(H, I, 1000 + e)
@@ -85,15 +85,15 @@ def _routed_path(T, bn, pair, tm, weight_rows, ring=False):
     layer.close()
 
 
-@pytest.mark.parametrize("pair,ring", [(True, False), (False, False), (True, True)])
-def test_glm_shape_256_tiles(pair, ring):
+@pytest.mark.parametrize("pair,wide", [(True, False), (False, False), (True, True)])
+def test_glm_shape_256_tiles(pair, wide):
     """GLM-shaped experts with 256-row token tiles (the prefill path), on CTA
     pairs (both forms) and on single CTAs."""
     H, I, E, k, T = 6144, 2048, 4, 4, 300
     layer = _layer(H, I, E, k, True, T)
     layer.set_tile_n(256)
     layer.set_pair_mma(pair)
-    layer.set_pair_scale_ring(ring)
+    layer.set_pair_wide_stages(wide)
     deq = {}
     for e in list(range(E)) + [-1]:
         ex, dq = make_expert(H, I, 900 + e)
@@ -107,7 +107,44 @@ def test_glm_shape_256_tiles(pair, ring):
     layer.check()
     shared = deq.pop(-1)
     want, _ = oracle_forward(bf16_to_np(hidden), ids, w, deq, shared)
-    _assert_close(out.cpu().numpy(), want, f"pair={pair} ring={ring}")
+    _assert_close(out.cpu().numpy(), want, f"pair={pair} wide={wide}")
+    layer.close()
+
+
+def test_pair_tile_order_bit_identical():
+    """The CTA-pair GEMMs' tile order (segment-major, or groups of g token
+    tiles run weight-tile-major) and stage width change only when each tile
+    runs: with a skewed routing (experts from 0 to several 256-row tiles) the
+    layer output is bit-identical across orders and forms, and matches the
+    oracle."""
+    H, I, E, k, T = 512, 512, 12, 3, 1500
+    layer = _layer(H, I, E, k, True, T)
+    layer.set_tile_n(256)
+    layer.set_pair_mma(True)
+    deq = {}
+    for e in list(range(E)) + [-1]:
+        ex, dq = make_expert(H, I, 700 + e)
+        layer.load_expert(e, ex)
+        deq[e] = dq
+    rng = np.random.default_rng(21)
+    pop = np.array([1.0 / (1 + e) ** 1.5 for e in range(E)])
+    ids = np.stack([rng.choice(E, size=k, replace=False, p=pop / pop.sum())
+                    for _ in range(T)]).astype(np.int32)
+    w = rng.random((T, k)).astype(np.float32) + 0.25
+    hidden = torch.randn(T, H, generator=torch.Generator().manual_seed(4)).to(torch.bfloat16)
+    outs = []
+    for up, down, wide in [(0, 0, False), (0, 0, True), (1, 1, True), (3, 5, True),
+                           (8, 16, True), (100000, 100000, True), (8, 16, False)]:
+        layer.set_pair_tile_order(up, down)
+        layer.set_pair_wide_stages(wide)
+        out = layer.forward_routed(hidden.cuda(), torch.from_numpy(ids), torch.from_numpy(w))
+        layer.check()
+        outs.append(out.cpu())
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+    shared = deq.pop(-1)
+    want, _ = oracle_forward(bf16_to_np(hidden), ids, w, deq, shared)
+    _assert_close(outs[0].numpy(), want, "tile order")
     layer.close()
 
 
