@@ -65,7 +65,6 @@ static_assert(kSfBase + kStages * (kSfaCols + kSfbCols) <= kTmemCols, "TMEM budg
 constexpr int kMaxSeg = 260;
 constexpr size_t kSmem = (size_t)kStages * kStageBytes + 1024 + 256;
 static_assert((3 * kStages + 3) * 8 + 4 <= 256, "barrier area");
-static_assert(kSmem + sizeof(int32_t) * (4 * kMaxSeg + 4) + 16 <= 232448, "shared memory budget");
 
 struct PairTile {
   int seg, m2, row_start, n_valid;
@@ -90,10 +89,19 @@ struct PairTile {
 // at most 256 rows) stay in L2 across its weight tiles, and each
 // (segment, weight tile) slab is still read once, by the pairs that run its
 // token tiles side by side.
+//
+// Decoding. A tile's segment comes from a table of every token tile's
+// segment (seg_tt, built at launch when the launch has at most kMaxTT token
+// tiles) instead of binary searches: one lookup against ~9 dependent
+// shared-memory loads per search, which the MMA-issuing thread otherwise
+// paid (~2000 cycles per tile with two searches) between tiles.
+constexpr int kMaxTT = 1536;
 struct PairMap {
   int32_t ntp[kMaxSeg + 1], cnt[kMaxSeg], start[kMaxSeg + 1], gseg[kMaxSeg + 2];
-  int nseg, m2_tiles, gt;
+  uint16_t seg_tt[kMaxTT];
+  int nseg, m2_tiles, gt, table;
 };
+static_assert(kSmem + sizeof(PairMap) + 16 <= 232448, "shared memory budget");
 
 // largest s in [lo, hi) with ntp[s] <= key (ntp non-decreasing, ntp[lo] <= key)
 __device__ __forceinline__ int seg_search(const int32_t* __restrict__ ntp, int lo, int hi,
@@ -130,17 +138,22 @@ __device__ __forceinline__ void load_pair_map(PairMap& m, const GemmParams& p, i
       m.gseg[g] = lo;
     }
   }
+  const bool table = nt <= kMaxTT;
+  if (table)
+    for (int sg = threadIdx.x; sg < p.nseg; sg += blockDim.x)
+      for (int tt = m.ntp[sg]; tt < m.ntp[sg + 1]; ++tt) m.seg_tt[tt] = (uint16_t)sg;
   if (threadIdx.x == 0) {
     m.nseg = p.nseg;
     m.m2_tiles = m2_tiles;
     m.gt = gt;
+    m.table = table ? 1 : 0;
   }
   __syncthreads();
 }
 
 __device__ __forceinline__ bool decode_pair_tile(int tile, const PairMap& m, PairTile& ti) {
   const int key = tile / m.m2_tiles;
-  int s = seg_search(m.ntp, 0, m.nseg, key);
+  int s = m.table ? (int)m.seg_tt[key] : seg_search(m.ntp, 0, m.nseg, key);
   int n;
   if (m.gt > 0) {
     const int g = m.ntp[s] / m.gt;
@@ -149,15 +162,15 @@ __device__ __forceinline__ bool decode_pair_tile(int tile, const PairMap& m, Pai
     if (gnt <= 0) return false;
     const int local = tile - m.m2_tiles * base;
     ti.m2 = local / gnt;
-    const int tt = base + local % gnt;
-    s = seg_search(m.ntp, gs, ge, tt);
+    const int tt = base + (local - ti.m2 * gnt);
+    s = m.table ? (int)m.seg_tt[tt] : seg_search(m.ntp, gs, ge, tt);
     n = tt - m.ntp[s];
   } else {
     const int nt = m.ntp[s + 1] - m.ntp[s];
     if (nt <= 0) return false;
     const int local = tile - m.m2_tiles * m.ntp[s];
     ti.m2 = local / nt;
-    n = local % nt;
+    n = local - ti.m2 * nt;
   }
   ti.seg = s;
   ti.row_start = m.start[s] + n * kBN;
@@ -517,6 +530,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* drained = tempty + 1;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drained + 1);
   __shared__ PairMap s_map;
+  // each tile's row count, from the leader's weight-copy thread (which decodes
+  // the tile anyway) to the MMA thread: written before the tile's first
+  // expect-tx arrival on the full barrier the MMA thread then waits on, read
+  // after that wait; eight tiles deep (the copy thread runs at most three
+  // stages ahead of the MMAs)
+  __shared__ int32_t s_tile_n[8];
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const uint32_t rank = cluster_ctarank();
@@ -564,12 +583,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       const bool do_a = warp == 0;
       if (do_a) tma_prefetch_desc(&tmap_a);
-      int stage = 0;
+      int stage = 0, k = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int tile = pair; tile < total_tiles && ok; tile += npairs) {
+      for (int tile = pair; tile < total_tiles && ok; tile += npairs, ++k) {
         PairTile ti;
-        if (!decode_pair_tile(tile, s_map, ti)) continue;
+        if (!decode_pair_tile(tile, s_map, ti)) ti.n_valid = 0;  // (every tile decodes)
+        if (do_a && leader) s_tile_n[k & 7] = ti.n_valid;
         const int n_mma = (ti.n_valid + 15) & ~15;
         const int half = n_mma / 2;  // token rows held by each CTA (multiple of 8)
         const int box = half <= 32 ? 32 : (half <= 64 ? 64 : 128);
@@ -642,21 +662,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------ MMA (leader)
     if (leader && lane == 0) {
-      int stage = 0, slot = 0;
+      int stage = 0, slot = 0, k = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
-      for (int tile = pair; tile < total_tiles && ok; tile += npairs) {
-        PairTile ti;
-        if (!decode_pair_tile(tile, s_map, ti)) continue;
-        const uint32_t n_mma = (uint32_t)((ti.n_valid + 15) & ~15);
-        const uint32_t idesc = idesc_fp4(kPM, n_mma, 0, 0, 0);
-        if (!mbar_wait_cluster(tempty, acc_phase ^ 1u, p.err)) break;
-        tc_fence_after();
+      // every tile index below total_tiles decodes to a tile, so the MMA
+      // thread only counts them and takes each tile's row count from the
+      // weight-copy thread (s_tile_n) after the tile's first full wait
+      for (int tile = pair; tile < total_tiles && ok; tile += npairs, ++k) {
+        uint32_t idesc = 0;
         for (int w = 0; w < wstages; ++w) {
           const int nc = chunks - w * kWChunks < kWChunks ? chunks - w * kWChunks : kWChunks;
           if (!mbar_wait_cluster(&full[stage], phase, p.err)) {
             ok = false;
             break;
+          }
+          if (w == 0) {
+            const uint32_t n_mma = (uint32_t)((s_tile_n[k & 7] + 15) & ~15);
+            idesc = idesc_fp4(kPM, n_mma, 0, 0, 0);
+            if (!mbar_wait_cluster(tempty, acc_phase ^ 1u, p.err)) {
+              ok = false;
+              break;
+            }
           }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(smem + stage * kWStageBytes);
