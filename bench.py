@@ -423,7 +423,7 @@ def run_reference(args) -> None:
 
 
 def build_ep_layer(T: int, local: int, rank: int, world: int, experts: int = E,
-                   fp4_dispatch: bool = False):
+                   fp4_dispatch: bool = False, placement: str = "contiguous"):
     """This rank's engine of the expert-parallel layer: experts
     [rank * E/W, (rank + 1) * E/W) + the shared expert, the full router.
     Expert e's weights are drawn from its own seed, so every rank holds the
@@ -442,30 +442,45 @@ def build_ep_layer(T: int, local: int, rank: int, world: int, experts: int = E,
                           max_tokens=T * (2 * K_TOP + 1 if fp4_dispatch else world + 1),
                           device=local, expert_begin=begin,
                           expert_count=count)
-    load_ep_weights(layer, rank, world, experts, dev)
+    load_ep_weights(layer, rank, world, experts, dev, placement)
     return layer
 
 
-def load_ep_weights(layer, rank: int, world: int, experts: int, dev) -> None:
-    """Experts [rank * E/W, (rank + 1) * E/W) + the shared expert and the full
-    router into this rank's engine; expert e's weights come from its own seed,
-    so every rank holds the same model."""
+def expert_order(bias, world: int, placement: str) -> list[int]:
+    """Renumbered expert j is original expert order[j] (section 6 of the
+    design notes): contiguous ranges of original ids, or the placement dealt
+    from the router's correction bias (`bias_balanced_order`)."""
+    from glm5x_moe.ep import bias_balanced_order
+    if placement == "bias" and world > 1:
+        return bias_balanced_order(bias, world)
+    return list(range(len(bias)))
+
+
+def load_ep_weights(layer, rank: int, world: int, experts: int, dev,
+                    placement: str = "contiguous") -> None:
+    """Experts [rank * E/W, (rank + 1) * E/W) of the renumbered order + the
+    shared expert and the full router (rows and bias in that order) into this
+    rank's engine; original expert e's weights come from its own seed, so
+    every rank holds the same model whatever the placement."""
     import torch
     from glm5x_moe.ep import expert_range
     from glm5x_moe.layer import NVFP4Expert
     from glm5x_moe.nvfp4 import quantize_nvfp4_weight
+    gc = torch.Generator(device="cpu").manual_seed(1)
+    router = (torch.randn(experts, H, generator=gc) * 0.02).to(torch.bfloat16)
+    bias = torch.rand(experts, generator=gc) * 0.2 - 0.1
+    order = expert_order(bias, world, placement)
     begin, count = expert_range(rank, world, experts)
-    for e in list(range(begin, begin + count)) + [-1]:
+    for j in list(range(begin, begin + count)) + [-1]:
+        e = order[j] if j >= 0 else -1
         g = torch.Generator(device=dev).manual_seed(7000 + e)
         mats = [quantize_nvfp4_weight((torch.randn(shape, generator=g, device=dev) * 0.02)
                                       .to(torch.bfloat16), scale_mode="mse")
                 for shape in ((I, H), (I, H), (H, I))]
-        layer.load_expert(e, NVFP4Expert(*mats))
+        layer.load_expert(j, NVFP4Expert(*mats))
         del mats
-    gc = torch.Generator(device="cpu").manual_seed(1)
-    router = (torch.randn(experts, H, generator=gc) * 0.02).to(torch.bfloat16)
-    bias = torch.rand(experts, generator=gc) * 0.2 - 0.1
-    layer.set_router(router, bias)
+    idx = torch.tensor(order, dtype=torch.long)
+    layer.set_router(router[idx].contiguous(), bias[idx].contiguous())
     torch.cuda.synchronize(dev)
 
 
@@ -490,9 +505,10 @@ def run_ours_ep(args, world: int, rank: int, local: int) -> None:
                                    intermediate_size=I, num_experts=experts, top_k=K_TOP,
                                    routed_scaling_factor=SCALE, device=local)
         layer = ep.engine
-        load_ep_weights(layer, rank, world, experts, dev)
+        load_ep_weights(layer, rank, world, experts, dev, args.placement)
     else:
-        layer = build_ep_layer(T, local, rank, world, experts, fp4_dispatch=fp4)
+        layer = build_ep_layer(T, local, rank, world, experts, fp4_dispatch=fp4,
+                               placement=args.placement)
         ep = ExpertParallelMoE(layer, rank=rank, world=world, num_experts=experts, top_k=K_TOP,
                                hidden_size=H, fp4_dispatch=fp4)
     if args.tile_n:
@@ -617,6 +633,9 @@ def run_ours_ep(args, world: int, rank: int, local: int) -> None:
                                        "kernels, BF16)") if peer else
                                       (f"ep{world} (NCCL all-to-all dispatch / combine, "
                                        f"{'NVFP4' if fp4 else 'BF16'} dispatch)"),
+                       "expert_placement": ("dealt from the router's correction bias "
+                                            "(bias_balanced_order)") if args.placement == "bias"
+                                           else "contiguous expert-id ranges",
                        "l2": "inputs larger than L2"},
             "phases_ms": phases, "ep_stages_ms": stages, "ep_exchange": exchange,
             "roofline": {"bound": "tensor", "kernel": "gate_up_gemm (rank 0)",
@@ -710,16 +729,20 @@ def run_decode_c4_ep(args, world: int, rank: int, local: int) -> dict | None:
                                intermediate_size=I, num_experts=experts, top_k=K_TOP,
                                routed_scaling_factor=SCALE, precision="mxfp4", device=local)
     begin, count = expert_range(rank, world, experts)
-    for e in list(range(begin, begin + count)) + [-1]:
+    gc = torch.Generator(device="cpu").manual_seed(5)
+    router = (torch.randn(experts, H, generator=gc) * 0.02).to(torch.bfloat16)
+    bias = zipf_bias(experts, 6)
+    order = expert_order(bias, world, args.placement)
+    for j in list(range(begin, begin + count)) + [-1]:
+        e = order[j] if j >= 0 else -1
         g = torch.Generator(device=dev).manual_seed(9000 + e)
         mats = [quantize_mxfp4_weight((torch.randn(shape, generator=g, device=dev) * 0.02)
                                       .to(torch.bfloat16))
                 for shape in ((I, H), (I, H), (H, I))]
-        ep.engine.load_expert(e, MXFP4Expert(*mats))
+        ep.engine.load_expert(j, MXFP4Expert(*mats))
         del mats
-    gc = torch.Generator(device="cpu").manual_seed(5)
-    router = (torch.randn(experts, H, generator=gc) * 0.02).to(torch.bfloat16)
-    ep.engine.set_router(router, zipf_bias(experts, 6))
+    idx = torch.tensor(order, dtype=torch.long)
+    ep.engine.set_router(router[idx].contiguous(), bias[idx].contiguous())
     hidden_all = torch.randn(Tall, H, generator=gc).to(torch.bfloat16).to(dev)
     hidden = hidden_all[rank * Tr:(rank + 1) * Tr].contiguous()
     ids, _ = ep.engine.route(hidden_all)
@@ -764,6 +787,9 @@ def run_decode_c4_ep(args, world: int, rank: int, local: int) -> dict | None:
                      "peer-memory exchange"),
         "tokens_per_s": Tall / (ms_max / 1000.0), "ms_per_step": ms_max,
         "experts_touched": int(touched.numel()), "max_local_experts_touched": int(tmax[2]),
+        "expert_placement": ("dealt from the router's correction bias (bias_balanced_order)"
+                             if args.placement == "bias" and world > 1
+                             else "contiguous expert-id ranges"),
         "ep_stages_ms_rank0": stages if rank == 0 else None,
         "roofline": {"bound": "hbm", "kernel": "whole layer step, busiest rank",
                      "achieved": bytes_max / (ms_max / 1000.0) / 1e9, "peak": hbm,
@@ -964,6 +990,9 @@ def main() -> None:
                     help="weight rows per narrow-token tile (tuning; 0 = the engine's default)")
     ap.add_argument("--decode-experts", type=int, default=0,
                     help="with --decode-only: fewer experts (small profiling captures only)")
+    ap.add_argument("--placement", default="bias", choices=["bias", "contiguous"],
+                    help="expert placement over N > 1 ranks: dealt from the router's correction "
+                         "bias (even loads) or contiguous ranges of expert ids")
     ap.add_argument("--dispatch", default="peer", choices=["bf16", "fp4", "peer"],
                     help="expert-parallel exchange: NCCL all-to-all of BF16 or of "
                          "sender-quantized NVFP4 rows, or the library's peer-memory kernels")

@@ -665,6 +665,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0, slot = 0, k = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
+      const uint64_t desc_a0 = desc_kmajor_sw128(smem_u32(smem));
       // every tile index below total_tiles decodes to a tile, so the MMA
       // thread only counts them and takes each tile's row count from the
       // weight-copy thread (s_tile_n) after the tile's first full wait
@@ -685,16 +686,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + stage * kWStageBytes);
-          const uint32_t b_addr = a_addr + kWChunks * kABytes;
+          // a descriptor's start address is in 16-byte units in its low bits
+          // (shared addresses stay below 256 KB, so adding never carries out)
+          const uint64_t da = desc_a0 + (uint64_t)(stage * (kWStageBytes >> 4));
+          const uint64_t db = da + (uint64_t)((kWChunks * kABytes) >> 4);
           const uint32_t sf_col = tmem_base + kSfBase + slot * kWSfCols;
 #pragma unroll
           for (int h = 0; h < kWChunks; ++h) {
             if (h >= nc) break;
 #pragma unroll
             for (int c = 0; c < 4; ++c)
-              mma_nvfp4_pair(tmem_base, desc_kmajor_sw128(a_addr + h * kABytes + 32 * c),
-                             desc_kmajor_sw128(b_addr + h * kBBytes + 32 * c), idesc,
+              mma_nvfp4_pair(tmem_base, da + (uint64_t)((h * kABytes + 32 * c) >> 4),
+                             db + (uint64_t)((h * kBBytes + 32 * c) >> 4), idesc,
                              sf_col + h * kWChunkCols + 4 * c,
                              sf_col + h * kWChunkCols + kSfaCols + 8 * c,
                              (w | h | c) != 0 ? 1u : 0u);

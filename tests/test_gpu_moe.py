@@ -148,6 +148,34 @@ def test_pair_tile_order_bit_identical():
     layer.close()
 
 
+def test_renumbered_experts_same_output():
+    """Expert placement renumbers the experts (original expert order[j] loaded
+    as expert j, router rows and bias permuted by order): the layer output is
+    bit-identical and the chosen ids map back through order."""
+    from glm5x_moe.ep import bias_balanced_order
+    H, I, E, k, T = 512, 512, 16, 4, 300
+    g = torch.Generator().manual_seed(31)
+    router = (torch.randn(E, H, generator=g) * 0.05).to(torch.bfloat16)
+    bias = torch.rand(E, generator=g) * 0.2 - 0.1
+    order = bias_balanced_order(bias, 4)
+    experts = {e: make_expert(H, I, 500 + e)[0] for e in list(range(E)) + [-1]}
+    hidden = torch.randn(T, H, generator=torch.Generator().manual_seed(5)).to(torch.bfloat16)
+    outs, ids = [], []
+    for perm in (list(range(E)), order):
+        layer = _layer(H, I, E, k, True, T)
+        for j in range(E):
+            layer.load_expert(j, experts[perm[j]])
+        layer.load_expert(-1, experts[-1])
+        idx = torch.tensor(perm, dtype=torch.long)
+        layer.set_router(router[idx].contiguous(), bias[idx].contiguous())
+        res = layer(hidden.cuda())
+        outs.append(res.output.cpu())
+        ids.append(torch.tensor(perm)[res.topk_indices.long()])
+        layer.close()
+    assert torch.equal(outs[0], outs[1])
+    assert torch.equal(ids[0], ids[1])
+
+
 def test_c2_eight_glm_experts_four_tokens():
     """Config 2: 8 GLM-shaped NVFP4 experts (6144 -> 2048) over the same 4
     tokens, each expert's output checked separately."""
