@@ -94,14 +94,21 @@ struct PairTile {
 // segment (seg_tt, built at launch when the launch has at most kMaxTT token
 // tiles) instead of binary searches: one lookup against ~9 dependent
 // shared-memory loads per search, which the MMA-issuing thread otherwise
-// paid (~2000 cycles per tile with two searches) between tiles.
-constexpr int kMaxTT = 1536;
+// paid (~2000 cycles per tile with two searches) between tiles. 768 entries
+// cover every launch of up to ~17k tokens per GPU at top-8 of 256 experts
+// (C5's 8192 tokens make ~450 token tiles); larger launches search.
+constexpr int kMaxTT = 768;
 struct PairMap {
   int32_t ntp[kMaxSeg + 1], cnt[kMaxSeg], start[kMaxSeg + 1], gseg[kMaxSeg + 2];
   uint16_t seg_tt[kMaxTT];
   int nseg, m2_tiles, gt, table;
 };
-static_assert(kSmem + sizeof(PairMap) + 16 <= 232448, "shared memory budget");
+// the down projection's epilogue stages 8 token rows x 32 features of BF16 y
+// per epilogue warp (512 bytes) to store them as 16-byte pieces
+template <int EPI>
+constexpr int kYStageBytes = EPI == 1 ? kEpiWarps * 512 : 16;
+static_assert(kSmem + sizeof(PairMap) + kYStageBytes<1> + 128 <= 232448,
+              "shared memory budget");
 
 // largest s in [lo, hi) with ntp[s] <= key (ntp non-decreasing, ntp[lo] <= key)
 __device__ __forceinline__ int seg_search(const int32_t* __restrict__ ntp, int lo, int hi,
@@ -183,6 +190,19 @@ __device__ __forceinline__ uint16_t f2bf(float x) {
   return __bfloat16_as_ushort(__float2bfloat16_rn(x));
 }
 
+__device__ __forceinline__ float shfl_idx_ordered(float v, int src) {
+  float r;
+  asm volatile("shfl.sync.idx.b32 %0, %1, %2, 0x1f, 0xffffffff;" : "=f"(r) : "f"(v), "r"(src));
+  return r;
+}
+
+// two floats rounded to BF16 (nearest even) in one word, lo in the low half
+__device__ __forceinline__ uint32_t bf16x2_rn(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
 // Epilogue warps 8-15 of both CTAs: drain this CTA's accumulator half to
 // registers, hand it back to the leader, then SwiGLU (EPI 0, BF16 h and the
 // slab amax) or the routing weight (EPI 1, BF16 y) and the stores.
@@ -190,7 +210,8 @@ template <int EPI>
 __device__ __forceinline__ void pair_epilogue(const GemmParams& p, uint32_t tmem_base,
                                               uint64_t* tfull, uint64_t* tempty, int pair,
                                               int npairs, int total_tiles, const PairMap& s_map,
-                                              uint32_t rank, int warp, int lane) {
+                                              uint32_t rank, int warp, int lane,
+                                              uint8_t* ystage) {
     const int q = warp & 3;
     const int half_cols = (warp - kEpiWarp0) >> 2;
     const uint32_t lead_tempty = mapa_shared(smem_u32(tempty), 0);
@@ -206,8 +227,14 @@ __device__ __forceinline__ void pair_epilogue(const GemmParams& p, uint32_t tmem
       uint32_t v[kChunks][32];
 #pragma unroll
       for (int i = 0; i < kChunks; ++i)
-        if (32 * half_cols + 64 * i < ti.n_valid)
-          tmem_ld_32x32b_x32(t_row + 32 * half_cols + 64 * i, v[i]);
+        if (32 * half_cols + 64 * i < ti.n_valid) {
+          if (EPI == 0) {
+            tmem_ld_32x32b_x32(t_row + 32 * half_cols + 64 * i, v[i]);
+          } else {
+            tmem_ld_16x256b_x4(t_row + 32 * half_cols + 64 * i, v[i]);
+            tmem_ld_16x256b_x4(t_row + (16u << 16) + 32 * half_cols + 64 * i, v[i] + 16);
+          }
+        }
       tmem_ld_wait();
 #pragma unroll
       for (int i = 0; i < kChunks; ++i) reg_fence(v[i]);
@@ -247,8 +274,21 @@ __device__ __forceinline__ void pair_epilogue(const GemmParams& p, uint32_t tmem
         if (lane == 0 && amax > 0.0f)
           atomicMax(reinterpret_cast<unsigned int*>(p.h_amax + ti.seg), __float_as_uint(amax));
       } else {
+        // v[ch] holds columns c0 .. c0 + 31 of this quadrant's 32 lanes as
+        // 16x8 fragments (lanes 0-15 in v[ch][0..15], lanes 16-31 in
+        // v[ch][16..31]): each thread has two neighbouring token columns of
+        // four output features. Eight tokens at a time go through the warp's
+        // 512-byte staging area (token row c: 32 features, 64 bytes, its
+        // 16-byte piece m in slot m ^ ((c >> 1) & 3), so neither the
+        // transposing stores nor the reads below meet a bank conflict), and
+        // each lane then stores 16 bytes (8 features of one token) of y.
         const float scale = bscale * p.a_global[ti.seg];
-        const int o = m_tile * 128 + 32 * q + lane;
+        const uint32_t sbuf = smem_u32(ystage) + (uint32_t)(warp - kEpiWarp0) * 512u;
+        const int sr = lane & 7, sm = lane >> 3;
+        const uint32_t st_addr = sbuf + sr * 64 + 16 * (sm ^ ((sr >> 1) & 3));
+        const int lr = lane >> 2;
+        const uint32_t ld_addr = sbuf + lr * 64 + 16 * ((lane & 3) ^ ((lr >> 1) & 3));
+        const int ycol = m_tile * 128 + 32 * q + 8 * (lane & 3);
 #pragma unroll
         for (int ch = 0; ch < kChunks; ++ch) {
           const int c0 = 32 * half_cols + 64 * ch;
@@ -256,11 +296,31 @@ __device__ __forceinline__ void pair_epilogue(const GemmParams& p, uint32_t tmem
           const float wmine =
               c0 + lane < ti.n_valid ? p.row_weight[ti.row_start + c0 + lane] * scale : 0.0f;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float w = __shfl_sync(0xffffffffu, wmine, i);
-            if (c0 + i < ti.n_valid)
-              p.out[(size_t)(ti.row_start + c0 + i) * p.M_per + o] =
-                  f2bf(__uint_as_float(v[ch][i]) * w);
+          for (int j = 0; j < 4; ++j) {
+            const int cj = c0 + 8 * j;
+            if (cj >= ti.n_valid) break;
+            // volatile: kept in order with the staging stores, so the
+            // compiler does not hoist every piece's weights at once (which
+            // spilled next to the 128 accumulator registers)
+            const float w0 = shfl_idx_ordered(wmine, 8 * j + 2 * (lane & 3));
+            const float w1 = shfl_idx_ordered(wmine, 8 * j + 2 * (lane & 3) + 1);
+            const uint32_t* a = v[ch] + 4 * j;
+            const uint32_t* b = v[ch] + 16 + 4 * j;
+            stmatrix_x4_trans(st_addr,
+                              bf16x2_rn(__uint_as_float(a[0]) * w0, __uint_as_float(a[1]) * w1),
+                              bf16x2_rn(__uint_as_float(a[2]) * w0, __uint_as_float(a[3]) * w1),
+                              bf16x2_rn(__uint_as_float(b[0]) * w0, __uint_as_float(b[1]) * w1),
+                              bf16x2_rn(__uint_as_float(b[2]) * w0, __uint_as_float(b[3]) * w1));
+            __syncwarp();
+            uint4 y;
+            asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(y.x), "=r"(y.y), "=r"(y.z), "=r"(y.w)
+                         : "r"(ld_addr)
+                         : "memory");
+            if (cj + lr < ti.n_valid)
+              *reinterpret_cast<uint4*>(p.out + (size_t)(ti.row_start + cj + lr) * p.M_per +
+                                        ycol) = y;
+            __syncwarp();
           }
         }
       }
@@ -284,6 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* drained = tempty + 1;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drained + 1);
   __shared__ PairMap s_map;
+  __shared__ __align__(128) uint8_t s_ystage[kYStageBytes<EPI>];
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const uint32_t rank = cluster_ctarank();
@@ -472,7 +533,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------ epilogue (both CTAs)
     regs_alloc<kRegsEpi>();
     pair_epilogue<EPI>(p, tmem_base, tfull, tempty, pair, npairs, total_tiles, s_map, rank,
-                       warp, lane);
+                       warp, lane, s_ystage);
   }
 
   tc_fence_before();
@@ -508,7 +569,9 @@ constexpr size_t kWSmem =
     (size_t)kWStages * kWStageBytes + kWSfSlots * kWSfSlotBytes + 1024 + 256;
 static_assert(kSfBase + kWSfSlots * kWSfCols <= kTmemCols, "TMEM budget (wide)");
 static_assert((2 * kWStages + 2 * kWSfSlots + 3) * 8 + 4 <= 256, "barrier area (wide)");
-static_assert(kWSmem + sizeof(PairMap) + 16 <= 232448, "shared memory budget (wide)");
+// PairMap, the tile row-count ring, the y staging area and its alignment
+static_assert(kWSmem + sizeof(PairMap) + 32 + kYStageBytes<1> + 128 <= 232448,
+              "shared memory budget (wide)");
 
 template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -530,6 +593,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* drained = tempty + 1;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drained + 1);
   __shared__ PairMap s_map;
+  __shared__ __align__(128) uint8_t s_ystage[kYStageBytes<EPI>];
   // each tile's row count, from the leader's weight-copy thread (which decodes
   // the tile anyway) to the MMA thread: written before the tile's first
   // expect-tx arrival on the full barrier the MMA thread then waits on, read
@@ -788,7 +852,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     regs_alloc<kRegsEpi>();
     pair_epilogue<EPI>(p, tmem_base, tfull, tempty, pair, npairs, total_tiles, s_map, rank,
-                       warp, lane);
+                       warp, lane, s_ystage);
   }
 
   tc_fence_before();

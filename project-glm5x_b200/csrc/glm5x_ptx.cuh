@@ -350,6 +350,33 @@ __device__ __forceinline__ void tmem_ld_32x32b_x8(uint32_t taddr, uint32_t (&r)[
       : "r"(taddr));
 }
 
+// 16 lanes x 32 consecutive columns as four 16x256b pieces: for piece j
+// (columns col + 8j ... + 7), thread i gets r[4j], r[4j+1] = lane (base +
+// i/4), columns 8j + 2(i%4) and 8j + 2(i%4) + 1, and r[4j+2], r[4j+3] = the
+// same columns of lane (base + 8 + i/4): the 16x8 accumulator fragment of an
+// mma.sync, one per piece.
+__device__ __forceinline__ void tmem_ld_16x256b_x4(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x256b.x4.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+// Four 8x8 matrices of 16-bit values stored transposed: register m of thread
+// i holds elements (row i/4, columns 2(i%4), 2(i%4) + 1) of matrix m (low
+// half first); column c of matrix m lands as 16 contiguous bytes at the
+// address thread 8m + c supplies.
+__device__ __forceinline__ void stmatrix_x4_trans(uint32_t saddr, uint32_t r0, uint32_t r1,
+                                                  uint32_t r2, uint32_t r3) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.trans.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(
+                   saddr),
+               "r"(r0), "r"(r1), "r"(r2), "r"(r3)
+               : "memory");
+}
+
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
