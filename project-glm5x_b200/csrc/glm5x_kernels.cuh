@@ -116,6 +116,14 @@ cudaError_t launch_topk(const float* in, int values_are_scores, const float* bia
                         int k, float routed_scale, int32_t* ids, float* weights, uint32_t* err,
                         cudaStream_t st, const RoutingPolicy& policy = RoutingPolicy(),
                         int32_t* sel = nullptr, float* diag = nullptr);
+// The same over the sum of nplanes planes of [T, E] values (plane p at
+// in + p * T * E, added in plane order: the K-split router's partial
+// logits), writing the sums to logits_out when it is given.
+cudaError_t launch_topk_planes(const float* in, int nplanes, float* logits_out,
+                               int values_are_scores, const float* bias, int T, int E, int k,
+                               float routed_scale, int32_t* ids, float* weights, uint32_t* err,
+                               cudaStream_t st, const RoutingPolicy& policy, int32_t* sel,
+                               float* diag);
 // rows_per: operand rows per (token, slot) -- 1 for NVFP4, 4 for the MXFP4
 // four-term activation expansion (pos and row_token refer to the first).
 // ids in [begin, begin + count) -> id - begin, others -> -1.

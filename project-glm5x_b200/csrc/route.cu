@@ -60,7 +60,12 @@ __device__ int choose_adaptive(const float* p, int k, int floor_k, float support
   return k;
 }
 
-__global__ void topk_kernel(const float* __restrict__ in, int values_are_scores,
+// in: nplanes planes of [T, E] (plane p at in + p * T * E) whose sum, taken
+// in plane order, is the value (the K-split router's partial logits; one
+// plane otherwise); logits_out, when given, receives that sum.
+template <int kMaxPer>
+__global__ void topk_kernel(const float* __restrict__ in, int nplanes,
+                            float* __restrict__ logits_out, int values_are_scores,
                             const float* __restrict__ bias, int T, int E, int k,
                             float routed_scale, int32_t* __restrict__ ids,
                             float* __restrict__ weights, uint32_t* err, RoutingPolicy pol,
@@ -69,15 +74,19 @@ __global__ void topk_kernel(const float* __restrict__ in, int values_are_scores,
   const int t = blockIdx.x * warps + threadIdx.x / 32;
   if (t >= T) return;
   const int lane = lane_id();
-  constexpr int kMaxPer = 16;
   float score[kMaxPer], choice[kMaxPer];
   const int per = (E + 31) / 32;
+  const int64_t plane = (int64_t)T * E;
   bool bad = false;
 #pragma unroll
   for (int j = 0; j < kMaxPer; ++j) {
     const int e = lane + 32 * j;
     if (j < per && e < E) {
-      const float v = in[(int64_t)t * E + e];
+      const int64_t i = (int64_t)t * E + e;
+      float v = in[i];
+#pragma unroll 4
+      for (int q = 1; q < nplanes; ++q) v = f_add(v, in[q * plane + i]);
+      if (logits_out) logits_out[i] = v;
       float s;
       if (values_are_scores) {
         s = v;
@@ -514,10 +523,27 @@ cudaError_t launch_topk(const float* in, int values_are_scores, const float* bia
                         int k, float routed_scale, int32_t* ids, float* weights, uint32_t* err,
                         cudaStream_t st, const RoutingPolicy& policy, int32_t* sel,
                         float* diag) {
+  return launch_topk_planes(in, 1, nullptr, values_are_scores, bias, T, E, k, routed_scale, ids,
+                            weights, err, st, policy, sel, diag);
+}
+
+cudaError_t launch_topk_planes(const float* in, int nplanes, float* logits_out,
+                               int values_are_scores, const float* bias, int T, int E, int k,
+                               float routed_scale, int32_t* ids, float* weights, uint32_t* err,
+                               cudaStream_t st, const RoutingPolicy& policy, int32_t* sel,
+                               float* diag) {
   if (T == 0) return cudaSuccess;
+  if (E > 512 || nplanes < 1) return cudaErrorInvalidValue;
   const int warps = 8;
-  topk_kernel<<<(T + warps - 1) / warps, warps * 32, 0, st>>>(
-      in, values_are_scores, bias, T, E, k, routed_scale, ids, weights, err, policy, sel, diag);
+  const dim3 grid((T + warps - 1) / warps), block(warps * 32);
+  if (E <= 256)
+    topk_kernel<8><<<grid, block, 0, st>>>(in, nplanes, logits_out, values_are_scores, bias, T,
+                                           E, k, routed_scale, ids, weights, err, policy, sel,
+                                           diag);
+  else
+    topk_kernel<16><<<grid, block, 0, st>>>(in, nplanes, logits_out, values_are_scores, bias, T,
+                                            E, k, routed_scale, ids, weights, err, policy, sel,
+                                            diag);
   return cudaGetLastError();
 }
 

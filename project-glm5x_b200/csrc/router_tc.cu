@@ -247,6 +247,9 @@ __global__ void sum_partials_kernel(const float* __restrict__ partials, int nspl
   logits[i] = v;
 }
 
+// K-split plane counts up to this are summed inside the selection kernel
+constexpr int kFusedPlanes = 4;
+
 size_t router_partials_floats(int num_sms, int E) {
   // nsplit * T <= (num_sms / tiles) * tiles * 128
   return (size_t)(num_sms + 1) * kTok * E;
@@ -282,8 +285,18 @@ cudaError_t launch_router_tc(const CUtensorMap* tmap_x, const CUtensorMap* tmap_
     return launch_topk(logits, 0, bias, T, E, k, routed_scale, ids, weights, err, st, policy,
                        sel, diag);
   }
-  if (launches) *launches = 3;
   if (!logits) return cudaErrorInvalidValue;
+  if (nsplit <= kFusedPlanes) {
+    // few planes (large batches): the selection kernel sums them in plane
+    // order as it reads them (and stores the logits), one launch and one
+    // pass over the planes
+    if (launches) *launches = 2;
+    return launch_topk_planes(partials, nsplit, logits, 0, bias, T, E, k, routed_scale, ids,
+                              weights, err, st, policy, sel, diag);
+  }
+  // many planes (small batches): one warp per token would add them up in a
+  // long chain of dependent loads, so a thread per logit sums them first
+  if (launches) *launches = 3;
   const int64_t n = (int64_t)T * E;
   sum_partials_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(partials, nsplit, n, logits);
   e = cudaGetLastError();
