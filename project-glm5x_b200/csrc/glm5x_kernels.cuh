@@ -148,8 +148,9 @@ cudaError_t launch_verify_greedy_blocks(const uint32_t* anchors, const uint32_t*
 // [T, H] BF16, box {64, 128}; tmap_w: router weight [E, H] BF16, box {64, E}.
 // When the 128-token tiles would leave SMs idle and `partials` is given
 // (router_partials_floats() floats), the contraction is split along K over
-// several CTAs per tile and a second kernel sums the partial logits in a
-// fixed order before the top-k. A non-natural policy or requested sel/diag
+// several CTAs per tile and the partial logits are summed in a fixed order
+// before the top-k (by the top-k kernel itself for up to four planes, else
+// by a separate kernel first). A non-natural policy or requested sel/diag
 // outputs re-run the top-k over the logits with that policy (logits must be
 // given). Returns the launches issued in *launches.
 bool router_tc_supported(int E, int H, int k);
@@ -160,7 +161,11 @@ cudaError_t launch_router_tc(const CUtensorMap* tmap_x, const CUtensorMap* tmap_
                              cudaStream_t st, float* partials = nullptr, int num_sms = 0,
                              int* launches = nullptr,
                              const RoutingPolicy& policy = RoutingPolicy(),
-                             int32_t* sel = nullptr, float* diag = nullptr);
+                             int32_t* sel = nullptr, float* diag = nullptr,
+                             float* row_amax = nullptr);
+// row_amax (optional, [T]): each token's max |x| over its row, NaN skipped
+// and any Inf / NaN flagged in err (launch_row_amax_bf16's values), taken
+// from the token tiles the router streams anyway.
 
 // ------------------------------------------------------------ gemm_nvfp4.cu
 // Grouped block-scaled FP4 GEMM over expert segments, weights as the M side:

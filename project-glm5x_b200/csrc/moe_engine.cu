@@ -1034,9 +1034,13 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
   };
   mark(0);
   const float* row_amax = m->token_amax;
+  // the tensor-core router reads every token row anyway: it takes the
+  // per-token amax on the way (no separate pass over the batch)
+  const bool router_runs = !ids_in && !pq;
+  const bool amax_in_router = !mx && !(peer && peer->row_amax) && router_runs;
   if (!mx && peer && peer->row_amax) {
     row_amax = peer->row_amax;  // computed by the senders while they sent the rows
-  } else if (!mx) {
+  } else if (!mx && !amax_in_router) {
     // per-token amax for the NVFP4 slab global scales (MXFP4 has none; its
     // term kernel checks for non-finite inputs itself)
     G5_CHECK(m, launch_row_amax_bf16(x, T, H, m->token_amax, m->err, st), "row amax");
@@ -1047,7 +1051,7 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
   mark(1);
   const int32_t* ids = ids_in;
   const float* wts = w_in;
-  if (!ids_in && !pq) {
+  if (router_runs) {
     if (reinterpret_cast<uintptr_t>(x) % 16)
       return m->fail(GLM5X_INVALID_EXTENT, "hidden must be 16-byte aligned");
     CUtensorMap tm_x;
@@ -1058,7 +1062,8 @@ static glm5x_status run_forward(glm5x_moe* m, const uint16_t* x, int64_t T64,
     G5_CHECK(m, launch_router_tc(&tm_x, &m->tm_router, m->router_bias, T, H, E, k,
                                  m->cfg.routed_scaling, m->logits, m->topk_ids, m->topk_w, m->err,
                                  st, m->router_partials, m->num_sms, &rl, m->policy,
-                                 diag ? m->route_sel : nullptr, diag ? m->route_diag : nullptr),
+                                 diag ? m->route_sel : nullptr, diag ? m->route_diag : nullptr,
+                                 amax_in_router ? m->token_amax : nullptr),
              "router");
     m->route_T = diag ? T : 0;
     launches += rl;

@@ -42,7 +42,7 @@ __global__ void __launch_bounds__(192, 1)
                      int T, int H, int E, int k, uint32_t tmem_cols, float routed_scale,
                      float* __restrict__ logits, int32_t* __restrict__ ids,
                      float* __restrict__ weights, uint32_t* err, int ks_per,
-                     float* __restrict__ partials) {
+                     float* __restrict__ partials, float* __restrict__ row_amax) {
   constexpr int kMaxK = KL;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -63,7 +63,8 @@ __global__ void __launch_bounds__(192, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+      // the MMA commit, and with row_amax the four epilogue warps' reads
+      mbar_init(&empty[s], row_amax ? 5 : 1);
     }
     mbar_init(done, 1);
     fence_barrier_init();
@@ -126,6 +127,56 @@ __global__ void __launch_bounds__(192, 1)
   } else {
     const int q = warp & 3;
     const int t = t0 + 32 * q + lane;
+    if (row_amax) {
+      // Per-token max |x| (the NVFP4 slab scales' input) from the token
+      // tiles the MMAs read: lane = token row 32q + lane of the tile, its
+      // 128-byte row read as eight 16-byte pieces in a lane-rotated order (the
+      // 128-byte swizzle only permutes pieces within a row, and the rotation
+      // spreads a warp's reads over all banks). NaN is skipped by the max and
+      // flagged, as the stand-alone row amax kernel does; rows past T are
+      // TMA zero fill.
+      const int r = 32 * q + lane;
+      uint32_t mx = 0u, mn = 0u;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int ks = ks_begin, stage = 0; ks < ks_end; ++ks) {
+        if (!mbar_wait(&full[stage], phase, err)) {
+          ok = false;
+          break;
+        }
+        const uint32_t row = smem_u32(smem + stage * kStageBytes) + r * 128;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          uint32_t w0, w1, w2, w3;
+          asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(w0), "=r"(w1), "=r"(w2), "=r"(w3)
+                       : "r"(row + 16 * ((i + r) & 7)));
+          const uint32_t wd[4] = {w0, w1, w2, w3};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t a = wd[j] & 0x7fff7fffu;
+            asm("max.bf16x2 %0, %0, %1;" : "+r"(mx) : "r"(a));
+            asm("max.NaN.bf16x2 %0, %0, %1;" : "+r"(mn) : "r"(a));
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[stage]);
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (ok && t < T) {
+        const float m = fmaxf(__uint_as_float(mx << 16), __uint_as_float(mx & 0xffff0000u));
+        // an Inf or NaN half of the NaN-propagating max: a non-finite input
+        if ((mn & 0x7f80u) == 0x7f80u || (mn & 0x7f800000u) == 0x7f800000u)
+          atomicOr(err, kErrNonFinite);
+        if (split)
+          atomicMax(reinterpret_cast<unsigned int*>(row_amax + t), __float_as_uint(m));
+        else
+          row_amax[t] = m;
+      }
+    }
     if (split) {
       if (mbar_wait(done, 0, err)) {
         tc_fence_after();
@@ -218,14 +269,15 @@ template <int KL>
 cudaError_t launch_kl(const CUtensorMap* tx, const CUtensorMap* tw, const float* bias, int T,
                       int H, int E, int k, float scale, float* logits, int32_t* ids,
                       float* weights, uint32_t* err, cudaStream_t st, int nsplit, int ks_per,
-                      float* partials) {
+                      float* partials, float* row_amax) {
   uint32_t cols = 32;
   while (cols < (uint32_t)E) cols <<= 1;
   cudaError_t e = cudaFuncSetAttribute(router_tc_kernel<KL>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem);
   if (e != cudaSuccess) return e;
   router_tc_kernel<KL><<<dim3((T + kTok - 1) / kTok, nsplit), 192, kSmem, st>>>(
-      *tx, *tw, bias, T, H, E, k, cols, scale, logits, ids, weights, err, ks_per, partials);
+      *tx, *tw, bias, T, H, E, k, cols, scale, logits, ids, weights, err, ks_per, partials,
+      row_amax);
   return cudaGetLastError();
 }
 
@@ -259,7 +311,8 @@ cudaError_t launch_router_tc(const CUtensorMap* tmap_x, const CUtensorMap* tmap_
                              const float* bias, int T, int H, int E, int k, float routed_scale,
                              float* logits, int32_t* ids, float* weights, uint32_t* err,
                              cudaStream_t st, float* partials, int num_sms, int* launches,
-                             const RoutingPolicy& policy, int32_t* sel, float* diag) {
+                             const RoutingPolicy& policy, int32_t* sel, float* diag,
+                             float* row_amax) {
   if (!router_tc_supported(E, H, k)) return cudaErrorInvalidValue;
   if (launches) *launches = 0;
   if (T == 0) return cudaSuccess;
@@ -270,11 +323,17 @@ cudaError_t launch_router_tc(const CUtensorMap* tmap_x, const CUtensorMap* tmap_
   nsplit = std::max(1, std::min(nsplit, ksteps / 4));
   const int ks_per = (ksteps + nsplit - 1) / nsplit;
   nsplit = (ksteps + ks_per - 1) / ks_per;
-  cudaError_t e =
-      k <= 8 ? launch_kl<8>(tmap_x, tmap_w, bias, T, H, E, k, routed_scale, logits, ids, weights,
-                            err, st, nsplit, ks_per, partials)
+  cudaError_t e = cudaSuccess;
+  if (row_amax && nsplit > 1) {
+    // the K planes' partial maxima meet in atomicMax (non-negative floats
+    // order as their bit patterns)
+    e = cudaMemsetAsync(row_amax, 0, sizeof(float) * (size_t)T, st);
+    if (e != cudaSuccess) return e;
+  }
+  e = k <= 8 ? launch_kl<8>(tmap_x, tmap_w, bias, T, H, E, k, routed_scale, logits, ids, weights,
+                            err, st, nsplit, ks_per, partials, row_amax)
              : launch_kl<16>(tmap_x, tmap_w, bias, T, H, E, k, routed_scale, logits, ids,
-                             weights, err, st, nsplit, ks_per, partials);
+                             weights, err, st, nsplit, ks_per, partials, row_amax);
   if (e != cudaSuccess) return e;
   const bool policy_pass = policy.mode != 0 || sel || diag;
   if (launches) *launches = 1;
