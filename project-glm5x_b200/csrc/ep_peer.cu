@@ -64,7 +64,10 @@ int engine_device(const glm5x_moe* m);
 namespace {
 
 constexpr int kMaxWorld = 16;
-constexpr int kGrid = 296;  // most blocks of the dispatch / combine kernels
+#ifndef G5_EP_GRID
+#define G5_EP_GRID 296
+#endif
+constexpr int kGrid = G5_EP_GRID;  // most blocks of the dispatch / combine kernels
 constexpr int kThreads = 256;
 
 // Byte offsets inside one rank's block; identical on every rank.
