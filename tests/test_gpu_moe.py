@@ -262,3 +262,29 @@ def test_activation_file_handoff(tmp_path):
                              res.topk_weights.numpy(), deq, shared)
     _assert_close(out, want, "activation hand-off")
     layer.close()
+
+
+def test_pair_tile_map_without_segment_table():
+    """A launch with more token tiles than the CTA-pair kernel's per-tile
+    segment table holds (here ~870 at 24576 tokens over 256 experts) finds
+    each tile's segment by binary search instead: its output agrees with the
+    single-CTA kernel on the same quantized activations (the two differ only
+    in accumulation order, far below the 1e-4 bound used here)."""
+    H, I, E, k, T = 512, 512, 256, 8, 24576
+    layer = _layer(H, I, E, k, True, T)
+    layer.set_tile_n(256)
+    for e in list(range(E)) + [-1]:
+        ex, _ = make_expert(H, I, 5000 + e)
+        layer.load_expert(e, ex)
+    g = torch.Generator().manual_seed(17)
+    ids = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)]).to(torch.int32)
+    w = torch.rand(T, k, generator=g) + 0.25
+    hidden = torch.randn(T, H, generator=g).to(torch.bfloat16).cuda()
+    outs = []
+    for pair in (True, False):
+        layer.set_pair_mma(pair)
+        outs.append(layer.forward_routed(hidden, ids, w).cpu())
+        layer.check()
+    ref = outs[1].abs().max().item()
+    assert (outs[0] - outs[1]).abs().max().item() <= 1e-4 * ref
+    layer.close()
