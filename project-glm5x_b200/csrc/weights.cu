@@ -94,6 +94,49 @@ __global__ void combine_kernel(const uint16_t* __restrict__ y, const int32_t* __
   }
 }
 
+// The same for a fixed slot count (the layer's top-8 + shared expert): every
+// slot's 16-byte piece is loaded before the sums, so a thread has all its
+// loads in flight at once; the sums still run in slot order, skipping empty
+// slots, so the result is combine_kernel's bit for bit.
+template <int KK>
+__global__ void combine_fixed_kernel(const uint16_t* __restrict__ y,
+                                     const int32_t* __restrict__ pos, int H,
+                                     float* __restrict__ out, int accumulate) {
+  const int t = blockIdx.x;
+  const int per = (H / 8 + gridDim.y - 1) / gridDim.y;
+  const int v_end = min(H / 8, ((int)blockIdx.y + 1) * per);
+  __shared__ int32_t rows[KK];
+  if (threadIdx.x < KK) rows[threadIdx.x] = pos[(int64_t)t * KK + threadIdx.x];
+  __syncthreads();
+  for (int v = blockIdx.y * per + threadIdx.x; v < v_end; v += blockDim.x) {
+    uint4 q[KK];
+#pragma unroll
+    for (int s = 0; s < KK; ++s)
+      q[s] = rows[s] >= 0 ? __ldg(reinterpret_cast<const uint4*>(y + (int64_t)rows[s] * H) + v)
+                          : make_uint4(0u, 0u, 0u, 0u);
+    float acc[8] = {};
+#pragma unroll
+    for (int s = 0; s < KK; ++s) {
+      if (rows[s] < 0) continue;  // slot with no expert on this engine
+      const uint32_t w[4] = {q[s].x, q[s].y, q[s].z, q[s].w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        acc[2 * i] += __uint_as_float(w[i] << 16);
+        acc[2 * i + 1] += __uint_as_float(w[i] & 0xffff0000u);
+      }
+    }
+    float4* o = reinterpret_cast<float4*>(out + (int64_t)t * H) + 2 * v;
+    if (accumulate) {
+      const float4 a = o[0], b = o[1];
+      o[0] = make_float4(a.x + acc[0], a.y + acc[1], a.z + acc[2], a.w + acc[3]);
+      o[1] = make_float4(b.x + acc[4], b.y + acc[5], b.z + acc[6], b.w + acc[7]);
+    } else {
+      o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    }
+  }
+}
+
 // Received rows of an expert-parallel engine: partial[r] = BF16(sum over the
 // row's slots of y[pos[r, s]]) for r < *count (a device value), FP32 sums in
 // slot order then one round to nearest even. Grid-stride over rows, so the
@@ -253,7 +296,10 @@ cudaError_t launch_combine(const uint16_t* y, const int32_t* pos, int T, int kk,
   if (kk > 32 || H % 8) return cudaErrorInvalidValue;
   // small batches split each token's row over several blocks to fill the SMs
   const int split = std::max(1, std::min(H / 8 / 256, 296 / T));
-  combine_kernel<<<dim3(T, split), 256, 0, st>>>(y, pos, kk, H, out, accumulate);
+  if (kk == 9)
+    combine_fixed_kernel<9><<<dim3(T, split), 256, 0, st>>>(y, pos, H, out, accumulate);
+  else
+    combine_kernel<<<dim3(T, split), 256, 0, st>>>(y, pos, kk, H, out, accumulate);
   return cudaGetLastError();
 }
 
