@@ -59,6 +59,46 @@ __global__ void scales_to_blocked_kernel(const uint8_t* __restrict__ rm, int64_t
   blocked[blocked_sf_offset(r, c, sf_cols)] = rm[idx];
 }
 
+// acc[0..7] += the 8 values of piece v (16 bytes) of y rows rows[0..KK), in
+// slot order, empty slots (-1) skipped; every slot's load is issued before
+// the first sum, so a thread has all of them in flight at once.
+template <int KK>
+__device__ __forceinline__ void sum_slot_pieces(const uint16_t* __restrict__ y,
+                                                const int32_t* rows, int v, int H,
+                                                float (&acc)[8]) {
+  uint4 q[KK];
+#pragma unroll
+  for (int s = 0; s < KK; ++s)
+    q[s] = rows[s] >= 0 ? __ldg(reinterpret_cast<const uint4*>(y + (int64_t)rows[s] * H) + v)
+                        : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+  for (int s = 0; s < KK; ++s) {
+    if (rows[s] < 0) continue;
+    const uint32_t w[4] = {q[s].x, q[s].y, q[s].z, q[s].w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      acc[2 * i] += __uint_as_float(w[i] << 16);
+      acc[2 * i + 1] += __uint_as_float(w[i] & 0xffff0000u);
+    }
+  }
+}
+
+// The same for any slot count, one slot's load at a time.
+__device__ __forceinline__ void sum_slot_pieces_any(const uint16_t* __restrict__ y,
+                                                    const int32_t* rows, int kk, int v, int H,
+                                                    float (&acc)[8]) {
+  for (int s = 0; s < kk; ++s) {
+    if (rows[s] < 0) continue;
+    const uint4 q = __ldg(reinterpret_cast<const uint4*>(y + (int64_t)rows[s] * H) + v);
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      acc[2 * i] += __uint_as_float(w[i] << 16);
+      acc[2 * i + 1] += __uint_as_float(w[i] & 0xffff0000u);
+    }
+  }
+}
+
 // One block per token; 8 BF16 (16 bytes) per vector. accumulate: add the
 // sum to out instead of storing it.
 __global__ void combine_kernel(const uint16_t* __restrict__ y, const int32_t* __restrict__ pos,
@@ -72,16 +112,7 @@ __global__ void combine_kernel(const uint16_t* __restrict__ y, const int32_t* __
   __syncthreads();
   for (int v = blockIdx.y * per + threadIdx.x; v < v_end; v += blockDim.x) {
     float acc[8] = {};
-    for (int s = 0; s < kk; ++s) {
-      if (rows[s] < 0) continue;  // slot with no expert on this engine
-      const uint4 q = __ldg(reinterpret_cast<const uint4*>(y + (int64_t)rows[s] * H) + v);
-      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        acc[2 * i] += __uint_as_float(w[i] << 16);
-        acc[2 * i + 1] += __uint_as_float(w[i] & 0xffff0000u);
-      }
-    }
+    sum_slot_pieces_any(y, rows, kk, v, H, acc);  // empty slots: no expert on this engine
     float4* o = reinterpret_cast<float4*>(out + (int64_t)t * H) + 2 * v;
     if (accumulate) {
       const float4 a = o[0], b = o[1];
@@ -94,10 +125,9 @@ __global__ void combine_kernel(const uint16_t* __restrict__ y, const int32_t* __
   }
 }
 
-// The same for a fixed slot count (the layer's top-8 + shared expert): every
-// slot's 16-byte piece is loaded before the sums, so a thread has all its
-// loads in flight at once; the sums still run in slot order, skipping empty
-// slots, so the result is combine_kernel's bit for bit.
+// combine_kernel for a fixed slot count (the layer's top-8 + shared expert),
+// all slot loads of a piece in flight at once; the sums still run in slot
+// order, skipping empty slots, so the result is combine_kernel's bit for bit.
 template <int KK>
 __global__ void combine_fixed_kernel(const uint16_t* __restrict__ y,
                                      const int32_t* __restrict__ pos, int H,
@@ -109,22 +139,8 @@ __global__ void combine_fixed_kernel(const uint16_t* __restrict__ y,
   if (threadIdx.x < KK) rows[threadIdx.x] = pos[(int64_t)t * KK + threadIdx.x];
   __syncthreads();
   for (int v = blockIdx.y * per + threadIdx.x; v < v_end; v += blockDim.x) {
-    uint4 q[KK];
-#pragma unroll
-    for (int s = 0; s < KK; ++s)
-      q[s] = rows[s] >= 0 ? __ldg(reinterpret_cast<const uint4*>(y + (int64_t)rows[s] * H) + v)
-                          : make_uint4(0u, 0u, 0u, 0u);
     float acc[8] = {};
-#pragma unroll
-    for (int s = 0; s < KK; ++s) {
-      if (rows[s] < 0) continue;  // slot with no expert on this engine
-      const uint32_t w[4] = {q[s].x, q[s].y, q[s].z, q[s].w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        acc[2 * i] += __uint_as_float(w[i] << 16);
-        acc[2 * i + 1] += __uint_as_float(w[i] & 0xffff0000u);
-      }
-    }
+    sum_slot_pieces<KK>(y, rows, v, H, acc);
     float4* o = reinterpret_cast<float4*>(out + (int64_t)t * H) + 2 * v;
     if (accumulate) {
       const float4 a = o[0], b = o[1];
@@ -153,16 +169,10 @@ __global__ void combine_rows_bf16_kernel(const uint16_t* __restrict__ y,
     __syncthreads();
     for (int v = threadIdx.x; v < H / 8; v += blockDim.x) {
       float acc[8] = {};
-      for (int s = 0; s < kk; ++s) {
-        if (rows[s] < 0) continue;
-        const uint4 q = __ldg(reinterpret_cast<const uint4*>(y + (int64_t)rows[s] * H) + v);
-        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          acc[2 * i] += __uint_as_float(w[i] << 16);
-          acc[2 * i + 1] += __uint_as_float(w[i] & 0xffff0000u);
-        }
-      }
+      if (kk == 9)
+        sum_slot_pieces<9>(y, rows, v, H, acc);
+      else
+        sum_slot_pieces_any(y, rows, kk, v, H, acc);
       uint32_t o[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -208,16 +218,10 @@ __global__ void combine_rows_return_kernel(const uint16_t* __restrict__ y,
     uint4* dst = reinterpret_cast<uint4*>(ret.base[s] + p * H);
     for (int v = threadIdx.x; v < H / 8; v += blockDim.x) {
       float acc[8] = {};
-      for (int j = 0; j < kk; ++j) {
-        if (rows[j] < 0) continue;
-        const uint4 q = __ldg(reinterpret_cast<const uint4*>(y + (int64_t)rows[j] * H) + v);
-        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          acc[2 * i] += __uint_as_float(w[i] << 16);
-          acc[2 * i + 1] += __uint_as_float(w[i] & 0xffff0000u);
-        }
-      }
+      if (kk == 9)
+        sum_slot_pieces<9>(y, rows, v, H, acc);
+      else
+        sum_slot_pieces_any(y, rows, kk, v, H, acc);
       uint32_t o[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
